@@ -1,0 +1,517 @@
+#!/usr/bin/env python
+"""bench.py -- picolm attention hot path on B200 (one JSON line on rank 0).
+
+Headline workload ("config 4"): batched decode,
+64 independent sequences per GPU, 2048 cached positions each, TinyLlama
+heads (32 query / 4 KV, head_dim 64), one new token per sequence per step;
+step i appends and attends at position 2048 + (i mod 64), i.e. the config's
+64 decode steps, cycled.  A step is one call of pl_attn_decode_batch_dev
+(one fused kernel: RoPE + FP16 append + split-KV attention + merge).
+
+  metric  decode-attn HBM GB/s = algorithmic bytes / device time, summed
+          over all ranks (KV rows read + q/k/v read + KV row and output
+          written; bytes per step in DESIGN.md)
+  e2e     the same metric through the host-buffer C entry point
+          pl_attn_decode_batch (pinned staging, H2D of q/k/v, D2H of out,
+          synchronous), i.e. what a C caller of the library sees
+  extra   prefill (config 3: causal prefill S=2048, 22 layers, TFLOPS),
+          long_ctx (config 5: 32768 cached, 16 layers, 32 steps, GB/s),
+          decode1 (config 1: one TinyLlama decode layer at pos 255, us/call)
+          -- single-GPU runs only.
+
+Multi-GPU: one process per GPU (torchrun); sequences are independent, so
+each rank runs its own 64 sequences with no collective on the data path
+(weak scaling); timing is the max over ranks of the device time.
+
+`--impl reference` times picolm's own CPU attention (oracle/_ref: the
+reference sources compiled in place; else the C restatement) on the same
+workload and prints the same line with "impl": "reference".
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+H, HK, HD = 32, 4, 64          # TinyLlama heads
+SEQS_PER_GPU = 64
+CTX = 2048
+NSTEP = 64                     # positions 2048 .. 2111
+KV_DIM = HK * HD
+Q_DIM = H * HD
+L2_FLUSH_BYTES = 256 << 20     # > 126 MB L2
+
+
+def step_bytes(pos: int, n_seq: int) -> int:
+    """Algorithmic bytes of one decode step for n_seq sequences at pos."""
+    rows = pos + 1
+    per_seq = (rows * KV_DIM * 2 * 2          # K and V rows read (FP16)
+               + Q_DIM * 4 + 2 * KV_DIM * 4   # q, k, v read (FP32)
+               + 2 * KV_DIM * 2               # appended K and V row (FP16)
+               + Q_DIM * 4)                   # output (FP32)
+    return per_seq * n_seq
+
+
+def load_peaks() -> dict:
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            d = json.load(f)
+        return {"hbm_gbs": d["hbm_gbs"], "bf16_tflops": d["bf16_tflops"],
+                "source": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "source": "fallback"}
+
+
+def profile_traffic(name: str):
+    """Per-launch DRAM bytes recorded in profiles/<name> ('traffic_bytes_per_launch: N')."""
+    p = os.path.join(ROOT, "profiles", name)
+    if not os.path.exists(p):
+        return None
+    for line in open(p):
+        if line.startswith("traffic_bytes_per_launch:"):
+            return float(line.split(":", 1)[1])
+    return None
+
+
+# ------------------------------------------------------------------ clocks
+class ClockSampler:
+    """NVML samples of SM clock and throttle reasons while a region runs."""
+    HW_SLOW, SW_THERM, HW_THERM, SW_POWER = 0x8, 0x20, 0x40, 0x4
+
+    def __init__(self, cuda_index: int):
+        self.samples, self.reasons, self.max_mhz = [], 0, None
+        self._stop = threading.Event()
+        self._h = None
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            import torch
+            bus = torch.cuda.get_device_properties(cuda_index).pci_bus_id
+            try:
+                self._h = pynvml.nvmlDeviceGetHandleByPciBusId(bus)
+            except Exception:
+                self._h = pynvml.nvmlDeviceGetHandleByIndex(cuda_index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self._h, pynvml.NVML_CLOCK_SM)
+            self._nv = pynvml
+        except Exception:
+            self._h = None
+
+    def _run(self):
+        nv = self._nv
+        while not self._stop.is_set():
+            try:
+                self.samples.append(nv.nvmlDeviceGetClockInfo(self._h, nv.NVML_CLOCK_SM))
+                self.reasons |= nv.nvmlDeviceGetCurrentClocksEventReasons(self._h)
+            except Exception:
+                pass
+            time.sleep(0.005)
+
+    def __enter__(self):
+        if self._h is not None:
+            self._t = threading.Thread(target=self._run, daemon=True)
+            self._t.start()
+        return self
+
+    def __exit__(self, *exc):
+        if self._h is not None:
+            self._stop.set()
+            self._t.join()
+
+    def summary(self) -> dict:
+        names = []
+        for bit, name in ((self.HW_SLOW, "hw_slowdown"), (self.SW_THERM, "sw_thermal_slowdown"),
+                          (self.HW_THERM, "hw_thermal_slowdown"), (self.SW_POWER, "sw_power_cap")):
+            if self.reasons & bit:
+                names.append(name)
+        return {"sm_mhz": float(np.median(self.samples)) if self.samples else None,
+                "sm_max_mhz": self.max_mhz, "reasons": names, "samples": len(self.samples)}
+
+
+# ------------------------------------------------------------ distributed
+def dist_setup():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    import torch
+    torch.cuda.set_device(local)
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    return rank, world, local
+
+
+def max_over_ranks(x: float, world: int) -> float:
+    if world == 1:
+        return x
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def barrier(world: int):
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+
+
+# ------------------------------------------------------------ workloads
+def make_cache_host(rng, n_rows: int, kv_dim: int) -> np.ndarray:
+    x = rng.standard_normal((n_rows, kv_dim), dtype=np.float32)
+    return x.astype(np.float16).view(np.uint16)
+
+
+def run_batched_decode(args, rank, world, local, peaks):
+    import torch
+    import picolm_b200 as pb
+    dev = torch.device("cuda", local)
+    at = pb.Attn(1, H, HK, CTX + NSTEP, n_seqs=SEQS_PER_GPU, device=local)
+    rng = np.random.default_rng(3 + 1000 * rank)
+    for s in range(SEQS_PER_GPU):
+        at.kv_upload(s, 0, 0, make_cache_host(rng, CTX, KV_DIM), make_cache_host(rng, CTX, KV_DIM))
+    gen = torch.Generator(device=dev).manual_seed(3 + rank)
+    q = torch.randn(NSTEP, SEQS_PER_GPU, Q_DIM, device=dev, generator=gen)
+    k = torch.randn(NSTEP, SEQS_PER_GPU, KV_DIM, device=dev, generator=gen)
+    v = torch.randn(NSTEP, SEQS_PER_GPU, KV_DIM, device=dev, generator=gen)
+    out = torch.empty(NSTEP, SEQS_PER_GPU, Q_DIM, device=dev)
+    seqs = torch.arange(SEQS_PER_GPU, dtype=torch.int32, device=dev)
+    pos = (CTX + torch.arange(NSTEP, dtype=torch.int32, device=dev))[:, None].repeat(
+        1, SEQS_PER_GPU).contiguous()
+    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
+    stream = torch.cuda.current_stream(dev)
+    sh = stream.cuda_stream
+
+    def step(i):
+        s = i % NSTEP
+        at.decode_batch_dev(0, SEQS_PER_GPU, seqs.data_ptr(), pos[s].data_ptr(),
+                            CTX + NSTEP - 1, q[s].data_ptr(), k[s].data_ptr(), v[s].data_ptr(),
+                            out[s].data_ptr(), sh)
+
+    for i in range(args.warmup):
+        flush.zero_()
+        step(i)
+    torch.cuda.synchronize()
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    total_bytes = 0
+    at.profile(True)
+    barrier(world)
+    torch.cuda.synchronize()
+    with ClockSampler(local) as clk:
+        for j in range(args.steps):
+            i = args.warmup + j
+            flush.zero_()                    # L2 flushed outside the timed pair
+            starts[j].record(stream)
+            step(i)
+            ends[j].record(stream)
+            total_bytes += step_bytes(CTX + i % NSTEP, SEQS_PER_GPU)
+        torch.cuda.synchronize()
+    barrier(world)
+    step_ms = [s.elapsed_time(e) for s, e in zip(starts, ends)]
+    kern_ms, n_attn, n_all = at.profile_read()
+    at.profile(False)
+    t_local = sum(step_ms) / 1e3
+    t_max = max_over_ranks(t_local, world)
+    value = total_bytes * world / t_max / 1e9
+    achieved = total_bytes / (kern_ms / 1e3) / 1e9    # per launch bytes / launch time
+    res = {
+        "value": value, "ms_per_step": t_max * 1e3 / args.steps,
+        "tok_per_s": SEQS_PER_GPU * world * args.steps / t_max,
+        "pct_peak": 100.0 * value / world / peaks["hbm_gbs"],
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"],
+                     "unit": "GB/s", "frac": achieved / peaks["hbm_gbs"],
+                     "peak_source": peaks["source"] + " (hbm_gbs, burst copy)",
+                     "traffic": profile_traffic("decode_kernel_config4.txt"),
+                     "kernel": "pl::decode_kernel<32,3> (fused RoPE+append+split-KV+merge)",
+                     "bytes_per_launch": total_bytes / args.steps},
+        "gpu_launches": n_all, "attn_launches": n_attn, "clocks": clk.summary(),
+    }
+    # ---- end to end through the host-buffer C entry point
+    qh = q.cpu().numpy()
+    kh = k.cpu().numpy()
+    vh = v.cpu().numpy()
+    seqs_h = np.arange(SEQS_PER_GPU, dtype=np.int32)
+    n_e2e = max(16, min(args.steps, 256))
+    for i in range(3):
+        at.decode_batch(0, seqs_h, np.full(SEQS_PER_GPU, CTX + i % NSTEP, np.int32), qh[i % NSTEP],
+                        kh[i % NSTEP], vh[i % NSTEP])
+    barrier(world)
+    e2e_bytes = 0
+    t0 = time.perf_counter()
+    for j in range(n_e2e):
+        s = j % NSTEP
+        at.decode_batch(0, seqs_h, np.full(SEQS_PER_GPU, CTX + s, np.int32), qh[s], kh[s], vh[s])
+        e2e_bytes += step_bytes(CTX + s, SEQS_PER_GPU)
+    t_e2e = max_over_ranks(time.perf_counter() - t0, world)
+    h2d = SEQS_PER_GPU * (Q_DIM + 2 * KV_DIM) * 4 + 2 * SEQS_PER_GPU * 4
+    d2h = SEQS_PER_GPU * Q_DIM * 4 + 4
+    res["e2e"] = {"value": e2e_bytes * world / t_e2e / 1e9, "unit": "GB/s",
+                  "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                  "ms_per_step": t_e2e * 1e3 / n_e2e, "steps": n_e2e,
+                  "api": "pl_attn_decode_batch (host buffers, synchronous)"}
+    at.close()
+    return res
+
+
+def cpu_decode_sample(max_seconds: float = 15.0, n_threads: int | None = None):
+    """picolm's CPU attention on the config-4 workload: full decode steps of
+    all 64 sequences (2048+ cached rows each), independent sequences spread
+    over the host's threads, until ~max_seconds of work."""
+    from oracle import oracle as O
+    use_ref = O.ref_available()
+    n_threads = n_threads or os.cpu_count() or 1
+    rng = np.random.default_rng(3)
+    ms = CTX + NSTEP
+    kc = np.zeros((SEQS_PER_GPU, ms, KV_DIM), np.uint16)
+    vc = np.zeros((SEQS_PER_GPU, ms, KV_DIM), np.uint16)
+    for s in range(SEQS_PER_GPU):
+        kc[s, :CTX] = make_cache_host(rng, CTX, KV_DIM)
+        vc[s, :CTX] = make_cache_host(rng, CTX, KV_DIM)
+    kf, vf = kc.reshape(-1), vc.reshape(-1)
+    c = O.cfg(H, HK, HD, ms)
+    tables = O.rope_tables(ms, HD, 10000.0)
+    total_bytes, steps = 0, 0
+    t0 = time.perf_counter()
+    while steps < NSTEP:
+        p = CTX + steps
+        q = rng.standard_normal(SEQS_PER_GPU * Q_DIM, dtype=np.float32)
+        k = rng.standard_normal(SEQS_PER_GPU * KV_DIM, dtype=np.float32)
+        v = rng.standard_normal(SEQS_PER_GPU * KV_DIM, dtype=np.float32)
+        O.attn_decode_seqs(c, kf, vf, ms * KV_DIM, np.full(SEQS_PER_GPU, p, np.int32), q, k, v,
+                           *tables, n_threads=n_threads, use_ref=use_ref)
+        total_bytes += step_bytes(p, SEQS_PER_GPU)
+        steps += 1
+        if time.perf_counter() - t0 > max_seconds:
+            break
+    dt = time.perf_counter() - t0
+    return {"value": total_bytes / dt / 1e9, "unit": "GB/s", "cores": n_threads,
+            "kind": "reference" if use_ref else "port",
+            "sample": f"{steps} full decode steps x {SEQS_PER_GPU} seqs at pos {CTX}..{CTX + steps - 1} "
+                      f"(config 4), {n_threads} threads, one sequence per thread at a time "
+                      f"(picolm's attention loop is single-threaded)",
+            "s_per_step": dt / steps}
+
+
+def run_prefill(args, local, peaks):
+    """Config 3: causal prefill, S=2048, 22 layers back to back."""
+    import torch
+    import picolm_b200 as pb
+    L, S = 22, 2048
+    dev = torch.device("cuda", local)
+    at = pb.Attn(L, H, HK, S, device=local)
+    gen = torch.Generator(device=dev).manual_seed(2)
+    # Q, K, V FP16-valued ~N(0,1), handed over as FP32 (model.c's q_batch etc.)
+    q = torch.randn(L, S, Q_DIM, device=dev, generator=gen).half().float()
+    k = torch.randn(L, S, KV_DIM, device=dev, generator=gen).half().float()
+    v = torch.randn(L, S, KV_DIM, device=dev, generator=gen).half().float()
+    out = torch.empty(L, S, Q_DIM, device=dev)
+    sh = torch.cuda.current_stream(dev).cuda_stream
+    flops_layer = 4.0 * H * HD * S * (S + 1) / 2
+
+    def run_all():
+        for l in range(L):
+            at.prefill_dev(0, l, 0, S, q[l].data_ptr(), k[l].data_ptr(), v[l].data_ptr(),
+                           out[l].data_ptr(), None, sh)
+
+    for _ in range(3):
+        run_all()
+    torch.cuda.synchronize()
+    at.profile(True)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    reps = 5
+    e0.record()
+    for _ in range(reps):
+        run_all()
+    e1.record()
+    torch.cuda.synchronize()
+    total_ms = e0.elapsed_time(e1)
+    kern_ms, n_attn, n_all = at.profile_read()
+    at.profile(False)
+    tflops_kernel = flops_layer * L * reps / (kern_ms / 1e3) / 1e12
+    res = {"metric": "prefill-attn TFLOPS (causal FLOPs / attention-kernel time)",
+           "value": tflops_kernel, "unit": "TFLOP/s",
+           "config": {"workload": "config3 causal prefill S=2048 x 22 layers, 32/4 heads, hd 64, "
+                                  "Q/K/V fp16-valued N(0,1) seed 2"},
+           "ms_per_22_layers": total_ms / reps,
+           "attn_kernel_ms_per_layer": kern_ms / (L * reps),
+           "tflops_whole_call": flops_layer * L * reps / (total_ms / 1e3) / 1e12,
+           "roofline": {"bound": "tensor", "achieved": tflops_kernel,
+                        "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
+                        "frac": tflops_kernel / peaks["bf16_tflops"],
+                        "peak_source": peaks["source"] + " (bf16 dense burst; fp16 taken equal)",
+                        "traffic": profile_traffic("prefill_kernel_config3.txt"),
+                        "kernel": "pl::prefill_attn_kernel (tcgen05, TMEM accumulators, TMA)",
+                        "flops_per_launch": flops_layer},
+           "gpu_launches": n_all}
+    # end to end through the host-buffer entry point, one layer
+    qh, kh, vh = q[0].cpu().numpy(), k[0].cpu().numpy(), v[0].cpu().numpy()
+    at.prefill(0, 0, 0, qh, kh, vh)
+    t0 = time.perf_counter()
+    n = 5
+    for _ in range(n):
+        at.prefill(0, 0, 0, qh, kh, vh)
+    dt = (time.perf_counter() - t0) / n
+    res["e2e"] = {"value": flops_layer / dt / 1e12, "unit": "TFLOP/s",
+                  "h2d_bytes_per_step": S * (Q_DIM + 2 * KV_DIM) * 4,
+                  "d2h_bytes_per_step": S * Q_DIM * 4 + 4, "ms_per_layer": dt * 1e3,
+                  "api": "pl_attn_prefill (host buffers)"}
+    at.close()
+    return res
+
+
+def run_long_ctx(args, local, peaks):
+    """Config 5 on one GPU: 16 layers, 32/8 heads, 32768 cached, 32 steps."""
+    import torch
+    import picolm_b200 as pb
+    L, HK5, CTX5, NS5 = 16, 8, 32768, 32
+    kv5 = HK5 * HD
+    dev = torch.device("cuda", local)
+    at = pb.Attn(L, H, HK5, CTX5 + NS5, rope_base=500000.0, device=local)
+    rng = np.random.default_rng(4)
+    for l in range(L):
+        at.kv_upload(0, l, 0, make_cache_host(rng, CTX5, kv5), make_cache_host(rng, CTX5, kv5))
+    gen = torch.Generator(device=dev).manual_seed(4)
+    q = torch.randn(NS5, L, Q_DIM, device=dev, generator=gen)
+    k = torch.randn(NS5, L, kv5, device=dev, generator=gen)
+    v = torch.randn(NS5, L, kv5, device=dev, generator=gen)
+    out = torch.empty(L, Q_DIM, device=dev)
+    seq0 = torch.zeros(1, dtype=torch.int32, device=dev)
+    posd = (CTX5 + torch.arange(NS5, dtype=torch.int32, device=dev)).contiguous()
+    sh = torch.cuda.current_stream(dev).cuda_stream
+
+    def step(s):
+        for l in range(L):
+            at.decode_batch_dev(l, 1, seq0.data_ptr(), posd[s:s + 1].data_ptr(), CTX5 + NS5 - 1,
+                                q[s, l].data_ptr(), k[s, l].data_ptr(), v[s, l].data_ptr(),
+                                out[l].data_ptr(), sh)
+
+    step(0)
+    torch.cuda.synchronize()
+    at.profile(True)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    nbytes = 0
+    for s in range(NS5):
+        step(s)
+        nbytes += L * ((CTX5 + s + 1) * kv5 * 4 + Q_DIM * 8 + kv5 * 12)
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1)
+    kern_ms, n_attn, n_all = at.profile_read()
+    at.profile(False)
+    at.close()
+    return {"metric": "long-context decode-attn HBM GB/s (config 5, 1 GPU)",
+            "value": nbytes / (ms / 1e3) / 1e9, "unit": "GB/s",
+            "pct_peak": 100.0 * nbytes / (ms / 1e3) / 1e9 / peaks["hbm_gbs"],
+            "tok_per_s": NS5 / (ms / 1e3), "ms_per_step_16_layers": ms / NS5,
+            "attn_kernel_gbs": nbytes / (kern_ms / 1e3) / 1e9, "gpu_launches": n_all,
+            "config": {"workload": "config5 16 layers, 32/8 heads, hd 64, theta 5e5, "
+                                   "32768 cached + 32 steps, KV N(0,1) seed 4"}}
+
+
+def run_decode1(local):
+    """Config 1: one TinyLlama decode layer at position 255 (latency)."""
+    import picolm_b200 as pb
+    rng = np.random.default_rng(0)
+    at = pb.Attn(1, H, HK, 256, device=local)
+    at.kv_upload(0, 0, 0, make_cache_host(rng, 255, KV_DIM), make_cache_host(rng, 255, KV_DIM))
+    q = rng.standard_normal(Q_DIM, dtype=np.float32)
+    k = rng.standard_normal(KV_DIM, dtype=np.float32)
+    v = rng.standard_normal(KV_DIM, dtype=np.float32)
+    for _ in range(20):
+        at.decode(0, 0, 255, q, k, v)
+    n = 500
+    t0 = time.perf_counter()
+    for _ in range(n):
+        at.decode(0, 0, 255, q, k, v)
+    dt = (time.perf_counter() - t0) / n
+    at.close()
+    return {"metric": "decode layer latency, config 1 (host buffers, synchronous)",
+            "us_per_call": dt * 1e6, "bytes_per_call": 281600}
+
+
+# ------------------------------------------------------------------ main
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=2000)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", choices=["all", "decode", "prefill", "long_ctx", "decode1"],
+                    default="all",
+                    help="all: headline + configs 1/3/5 + CPU baseline; decode: headline only; "
+                         "prefill / long_ctx / decode1: that workload alone (for profiling)")
+    args = ap.parse_args()
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    config = {"workload": "config4 batched decode: 64 seqs per GPU x 2048 cached positions, "
+                          "TinyLlama heads 32/4, hd 64, 64 decode steps (pos 2048..2111) cycled",
+              "seqs_per_gpu": SEQS_PER_GPU, "global_seqs": SEQS_PER_GPU * world,
+              "cached_positions": CTX, "parallelism": f"sequence shards x{world}, no collective",
+              "l2": "flushed (256 MB write) before every timed step, outside the timed pair"}
+    base = {"metric": "decode-attn HBM GB/s", "unit": "GB/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "fp16 KV, fp32 accumulate",
+            "data": "synthetic (seeded N(0,1) KV cache and q/k/v)", "config": config}
+
+    if args.impl == "reference":
+        if rank != 0:
+            return
+        r = cpu_decode_sample(max_seconds=20.0)
+        line = dict(base)
+        line.update({"impl": "reference", "value": r["value"],
+                     "ms_per_step": r["s_per_step"] * 1e3,
+                     "cpu_baseline": {k: r[k] for k in ("value", "unit", "cores", "kind",
+                                                        "sample")},
+                     "e2e": {"value": r["value"], "unit": "GB/s", "h2d_bytes_per_step": 0,
+                             "d2h_bytes_per_step": 0}})
+        line["steps"] = args.steps
+        print(json.dumps(line), flush=True)
+        return
+
+    rank, world, local = dist_setup()
+    from picolm_b200 import build
+    if rank == 0:
+        build.build()
+    barrier(world)
+    peaks = load_peaks()
+    if args.workload in ("prefill", "long_ctx", "decode1"):
+        if rank == 0:
+            fn = {"prefill": lambda: run_prefill(args, local, peaks),
+                  "long_ctx": lambda: run_long_ctx(args, local, peaks),
+                  "decode1": lambda: run_decode1(local)}[args.workload]
+            print(json.dumps(fn()), flush=True)
+        return
+    res = run_batched_decode(args, rank, world, local, peaks)
+    line = dict(base)
+    line.update({"impl": "ours", "value": res["value"], "ms_per_step": res["ms_per_step"],
+                 "tok_per_s": res["tok_per_s"], "pct_peak": res["pct_peak"],
+                 "roofline": res["roofline"], "e2e": res["e2e"],
+                 "gpu_launches": res["gpu_launches"], "clocks": res["clocks"]})
+    if world == 1 and args.workload == "all":
+        line["prefill"] = run_prefill(args, local, peaks)
+        line["long_ctx"] = run_long_ctx(args, local, peaks)
+        line["decode1"] = run_decode1(local)
+        cb = cpu_decode_sample(max_seconds=15.0)
+        line["cpu_baseline"] = {k: cb[k] for k in ("value", "unit", "cores", "kind", "sample")}
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,216 @@
+/*
+ * pl_attn.h -- C-ABI of the B200 attention module for picolm.
+ *
+ * picolm runs its attention block inline in model.c, twice:
+ *   decode  : model_forward_ex      picolm/model.c:802-892
+ *             (RoPE 820, FP16 KV append 822-826, GQA online softmax 848-892)
+ *   prefill : model_forward_prefill picolm/model.c:1019-1090
+ *             (per position: RoPE 1040-1041, append 1044-1051,
+ *              causal attention 1054-1089)
+ * and its only device backend, gpu.h, offloads matmuls alone
+ * (picolm/gpu.h:23-26).  This header adds the missing attention entry points
+ * in gpu.h's style: plain C, int status (0 = success, negative = failure),
+ * one module-global context, inline stubs when the backend is compiled out
+ * (picolm/gpu.h:33-42).  Unlike gpu_try_matmul there is NO CPU fallback:
+ * a failing call returns a negative code, pl_attn_strerror() names it, and
+ * the caller reports it and stops.
+ *
+ * KV cache.  It lives in device HBM, owned by the module, laid out as
+ * picolm's host cache (model.c:612-619, 802-805) with a sequence slot in
+ * front: [seq][layer][max_seq][n_kv_heads][head_dim] FP16 words.  Rows are
+ * written with picolm's own FP32->FP16 rounding (quant.c:41-78, ties away
+ * from zero), so the cache is bit-identical to the one model.c would hold.
+ *
+ * Threading.  One host thread drives the module.  Host-buffer calls are
+ * synchronous: caller buffers are read and written before return.
+ * Device-pointer calls (suffix _dev) are asynchronous on the given stream.
+ *
+ * Supported shapes: head_dim 64; n_kv_heads in {1, 2, 4, 8};
+ * n_heads / n_kv_heads in {1, 2, 4, 8}; LLaMA (pairwise) or Qwen (half-split)
+ * RoPE.  Other shapes are rejected with PL_EUNSUPPORTED at pl_attn_init.
+ */
+#ifndef PL_ATTN_H
+#define PL_ATTN_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- Status codes (0 = success, as gpu.h's int returns) ---- */
+#define PL_OK             0
+#define PL_EFAIL         -1   /* generic failure                              */
+#define PL_EARG          -2   /* argument out of range (seq, layer, pos, ...) */
+#define PL_ENOMEM        -3   /* device or pinned-host allocation failed      */
+#define PL_ECUDA         -4   /* CUDA runtime / driver error                  */
+#define PL_ETIMEOUT      -5   /* a bounded device-side wait gave up           */
+#define PL_ESTATE        -6   /* not initialised, or initialised twice        */
+#define PL_EDEVICE       -7   /* no usable sm_100 device                      */
+#define PL_EUNSUPPORTED  -8   /* shape not supported by the kernels           */
+
+#define PL_ROPE_LLAMA 0       /* pairs (2i, 2i+1)   -- tensor.c:558-601 */
+#define PL_ROPE_QWEN  1       /* pairs (i, i+hd/2)  -- tensor.c:537-557 */
+
+#ifndef PL_ATTN_DISABLED
+
+/* ---- Lifecycle (cf. gpu_init / gpu_available / gpu_shutdown,
+ *      picolm/gpu.h:9-29; called where picolm.c:186-193 and 312-314 call them) */
+
+/* Create the module context on CUDA device `device`: allocate the device KV
+ * cache for `n_seqs` independent sequences (slot 0 is the one model.c uses),
+ * zero it, and build the RoPE tables from rope_freq_base exactly as
+ * init_rope_tables does (model.c:545-556).  Replaces the KV calloc of
+ * allocate_run_state (model.c:612-619) for the attention path. */
+int  pl_attn_init(int n_layers, int n_heads, int n_kv_heads, int head_dim,
+                  int max_seq_len, float rope_freq_base, int rope_type,
+                  int n_seqs, int device);
+
+/* Replace the device RoPE tables with host tables [n_rows][half_dim]
+ * (model.c's s->rope_cos / s->rope_sin), copied once. */
+int  pl_attn_set_rope(const float *cos_tab, const float *sin_tab, int n_rows,
+                      int half_dim);
+
+/* 1 if pl_attn_init succeeded and the context is usable (gpu.h:20-21). */
+int  pl_attn_available(void);
+
+/* Release every device and host resource (gpu.h:28-29). */
+void pl_attn_shutdown(void);
+
+/* Static text for a status code. */
+const char *pl_attn_strerror(int rc);
+
+/* ---- Host-buffer entry points (the drop-in for model.c) ---- */
+
+/* Decode step for one sequence: replaces model.c:820-892.
+ * q [n_heads*head_dim] and k, v [n_kv_heads*head_dim] are the layer's FP32
+ * projections BEFORE RoPE (model.c's s->q, k_tmp, v_tmp); out
+ * [n_heads*head_dim] receives the attention output (model.c's s->xb).
+ * Rotates q and k by the RoPE of `pos`, appends k and v as FP16 at row pos
+ * of (seq, layer), attends rows [0, pos].  q, k, v are not modified. */
+int  pl_attn_decode(int seq, int layer, int pos, const float *q,
+                    const float *k, const float *v, float *out);
+
+/* n independent decode steps in one launch: sequence slot seqs[i] at
+ * position pos[i] with q + i*q_dim, k/v + i*kv_dim, out + i*q_dim.  Slots
+ * must be distinct. */
+int  pl_attn_decode_batch(int layer, int n, const int *seqs, const int *pos,
+                          const float *q, const float *k, const float *v,
+                          float *out);
+
+/* Causal prefill of n_tok positions start_pos .. start_pos+n_tok-1 for one
+ * sequence: replaces model.c:1039-1089.  q [n_tok][n_heads*head_dim],
+ * k, v [n_tok][n_kv_heads*head_dim] before RoPE; output row i is written at
+ * out + i*out_stride (model.c's xb_batch, out_stride = n_embd).  Position
+ * start_pos+i attends rows [0, start_pos+i], rows below start_pos being
+ * whatever the cache already holds (a loaded KV file, picolm.c:214-230). */
+int  pl_attn_prefill(int seq, int layer, int start_pos, int n_tok,
+                     const float *q, const float *k, const float *v,
+                     float *out, int out_stride);
+
+/* RoPE alone, in place on host buffers, bit-identical to rope()
+ * (tensor.c:533-603): q [n_tok][n_heads*head_dim], k [n_tok][kv_dim]
+ * (either may be NULL), position of row i = pos0 + i. */
+int  pl_attn_rope(int pos0, int n_tok, float *q, float *k);
+
+/* Copy FP16 cache rows [pos0, pos0+n_pos) of (seq, layer) out of / into
+ * device HBM; k and v are [n_pos][kv_dim] FP16 words.  With these,
+ * kvcache_save / kvcache_load (model.c:1158-1259) keep the KVCP file format
+ * while the cache lives on the device. */
+int  pl_kv_download(int seq, int layer, int pos0, int n_pos, uint16_t *k,
+                    uint16_t *v);
+int  pl_kv_upload(int seq, int layer, int pos0, int n_pos, const uint16_t *k,
+                  const uint16_t *v);
+
+/* ---- Device-pointer entry points (asynchronous on `stream`, a
+ *      cudaStream_t passed as void*; NULL = the module's own stream) ---- */
+
+/* pl_attn_decode_batch with every array already in device memory.
+ * max_pos must bound every d_pos[i] (it sizes the KV split). */
+int  pl_attn_decode_batch_dev(int layer, int n, const int *d_seqs,
+                              const int *d_pos, int max_pos, const float *d_q,
+                              const float *d_k, const float *d_v, float *d_out,
+                              void *stream);
+
+/* pl_attn_prefill with device arrays. */
+int  pl_attn_prefill_dev(int seq, int layer, int start_pos, int n_tok,
+                         const float *d_q, const float *d_k, const float *d_v,
+                         float *d_out, int out_stride, void *stream);
+
+/* One shard of a KV-split decode (a long sequence whose cache rows are
+ * spread over several devices).  This device holds global positions
+ * [row0, row0 + n_rows) of sequence slot `seq` in its local rows
+ * [0, n_rows).  q is rotated by the RoPE of global position `pos`; if
+ * `append` is nonzero, k is rotated too and k, v are appended at local row
+ * pos - row0 (which must be < n_rows).  Attends local rows [0, n_rows) and
+ * writes, per query head h, the partial triple
+ *   d_part[h*(head_dim+2) + 0]        m_h: running max, log2 domain
+ *   d_part[h*(head_dim+2) + 1]        l_h: sum of 2^(s - m_h)
+ *   d_part[h*(head_dim+2) + 2 + d]    o_h[d]: unnormalised sum of p * V
+ * with s = (q.k) * log2(e) / sqrt(head_dim).  Merge shards with
+ * pl_attn_combine_dev. */
+int  pl_attn_decode_partial_dev(int seq, int layer, int pos, int row0,
+                                int n_rows, int append, const float *d_q,
+                                const float *d_k, const float *d_v,
+                                float *d_part, void *stream);
+
+/* Log-sum-exp merge of n_part partial blocks laid out back to back
+ * (n_part * n_heads*(head_dim+2) floats) into out [n_heads*head_dim]:
+ *   M = max_g m_g, L = sum_g l_g 2^(m_g - M),
+ *   out = sum_g 2^(m_g - M) o_g / L. */
+int  pl_attn_combine_dev(int n_part, const float *d_parts, float *d_out,
+                         void *stream);
+
+/* Device address of the FP16 cache rows of (seq, layer): K at *d_k, V at
+ * *d_v, each [max_seq][kv_dim].  For engines that share the cache. */
+int  pl_attn_kv_ptr(int seq, int layer, uint16_t **d_k, uint16_t **d_v);
+
+/* ---- Profiling (cf. picolm's timing stats, picolm.c:285-302) ---- */
+
+/* Enable (1) or disable (0) device timing: every later call records CUDA
+ * events immediately before and after its attention kernel, on the stream
+ * that kernel runs on, and counts the module's kernel launches.  Enabling
+ * clears previous records. */
+int  pl_attn_profile(int enable);
+
+/* Total device time (ms) of the attention kernels recorded since the last
+ * read or enable, the number of those kernels, and the number of all module
+ * kernels launched (attention, prologue, combine, RoPE).  Waits for the
+ * recorded events; clears the records. */
+int  pl_attn_profile_read(double *attn_ms, long *attn_launches,
+                          long *all_launches);
+
+#else /* PL_ATTN_DISABLED: inline stubs, as gpu.h does without USE_VULKAN */
+
+static inline int  pl_attn_init(int a, int b, int c, int d, int e, float f,
+                                int g, int h, int i) {
+    (void)a; (void)b; (void)c; (void)d; (void)e; (void)f; (void)g; (void)h;
+    (void)i; return PL_EDEVICE;
+}
+static inline int  pl_attn_set_rope(const float *a, const float *b, int c, int d) {
+    (void)a; (void)b; (void)c; (void)d; return PL_ESTATE;
+}
+static inline int  pl_attn_available(void) { return 0; }
+static inline void pl_attn_shutdown(void) {}
+static inline const char *pl_attn_strerror(int rc) {
+    (void)rc; return "attention backend compiled out";
+}
+static inline int  pl_attn_decode(int a, int b, int c, const float *d,
+                                  const float *e, const float *f, float *g) {
+    (void)a; (void)b; (void)c; (void)d; (void)e; (void)f; (void)g;
+    return PL_ESTATE;
+}
+static inline int  pl_attn_prefill(int a, int b, int c, int d, const float *e,
+                                   const float *f, const float *g, float *h,
+                                   int i) {
+    (void)a; (void)b; (void)c; (void)d; (void)e; (void)f; (void)g; (void)h;
+    (void)i; return PL_ESTATE;
+}
+
+#endif /* PL_ATTN_DISABLED */
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* PL_ATTN_H */

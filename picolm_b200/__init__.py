@@ -1,0 +1,240 @@
+"""picolm_b200 -- B200 attention hot path for picolm, behind a C ABI.
+
+The product is the shared library ``libpl_attn.so`` built from
+``picolm_b200/csrc`` (see ``include/pl_attn.h`` for the C interface).  This
+module is a thin ctypes binding over that C ABI for Python callers, the test
+suite and the benchmark: every call goes straight into the CUDA library.
+There is no CPU path: if the library is missing, cannot be loaded, or has
+no usable sm_100 device, calls raise :class:`PlAttnError`.
+
+``Attn`` mirrors the C entry points one for one and keeps their argument
+meaning; host-buffer methods take numpy arrays, ``*_dev`` methods take raw
+device pointers (ints), e.g. ``torch.Tensor.data_ptr()``.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+import re
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "libpl_attn.so")
+HEADER = os.path.join(os.path.dirname(HERE), "include", "pl_attn.h")
+
+PL_OK = 0
+PL_EFAIL = -1
+PL_EARG = -2
+PL_ENOMEM = -3
+PL_ECUDA = -4
+PL_ETIMEOUT = -5
+PL_ESTATE = -6
+PL_EDEVICE = -7
+PL_EUNSUPPORTED = -8
+PL_ROPE_LLAMA = 0
+PL_ROPE_QWEN = 1
+HEAD_DIM = 64
+PART_STRIDE = HEAD_DIM + 2
+
+
+class PlAttnError(RuntimeError):
+    def __init__(self, rc: int, what: str):
+        self.rc = rc
+        super().__init__(f"{what}: {strerror(rc)} ({rc})")
+
+
+_f32p = np.ctypeslib.ndpointer(np.float32, flags="C_CONTIGUOUS")
+_u16p = np.ctypeslib.ndpointer(np.uint16, flags="C_CONTIGUOUS")
+_i32p = np.ctypeslib.ndpointer(np.int32, flags="C_CONTIGUOUS")
+_vp = C.c_void_p
+_lib = None
+
+
+def declared_symbols() -> list[str]:
+    """Names of the functions include/pl_attn.h declares (non-stub part)."""
+    text = open(HEADER).read()
+    text = text.split("#else /* PL_ATTN_DISABLED")[0]
+    return sorted(set(re.findall(r"\b(pl_[a-z0-9_]+)\s*\(", text)))
+
+
+def load(path: str = LIB_PATH) -> C.CDLL:
+    """Load libpl_attn.so and declare its signatures.  Raises if absent."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not os.path.exists(path):
+        raise PlAttnError(PL_EDEVICE, f"{path} is missing; run python -m picolm_b200.build")
+    lib = C.CDLL(path)
+    i = C.c_int
+    sig = {
+        "pl_attn_init": (i, [i, i, i, i, i, C.c_float, i, i, i]),
+        "pl_attn_set_rope": (i, [_f32p, _f32p, i, i]),
+        "pl_attn_available": (i, []),
+        "pl_attn_shutdown": (None, []),
+        "pl_attn_strerror": (C.c_char_p, [i]),
+        "pl_attn_decode": (i, [i, i, i, _f32p, _f32p, _f32p, _f32p]),
+        "pl_attn_decode_batch": (i, [i, i, _i32p, _i32p, _f32p, _f32p, _f32p, _f32p]),
+        "pl_attn_prefill": (i, [i, i, i, i, _f32p, _f32p, _f32p, _f32p, i]),
+        "pl_attn_rope": (i, [i, i, _vp, _vp]),
+        "pl_kv_download": (i, [i, i, i, i, _vp, _vp]),
+        "pl_kv_upload": (i, [i, i, i, i, _vp, _vp]),
+        "pl_attn_decode_batch_dev": (i, [i, i, _vp, _vp, i, _vp, _vp, _vp, _vp, _vp]),
+        "pl_attn_prefill_dev": (i, [i, i, i, i, _vp, _vp, _vp, _vp, i, _vp]),
+        "pl_attn_decode_partial_dev": (i, [i, i, i, i, i, i, _vp, _vp, _vp, _vp, _vp]),
+        "pl_attn_combine_dev": (i, [i, _vp, _vp, _vp]),
+        "pl_attn_kv_ptr": (i, [i, i, C.POINTER(_vp), C.POINTER(_vp)]),
+        "pl_attn_profile": (i, [i]),
+        "pl_attn_profile_read": (i, [C.POINTER(C.c_double), C.POINTER(C.c_long),
+                                     C.POINTER(C.c_long)]),
+    }
+    for name, (res, args) in sig.items():
+        fn = getattr(lib, name)
+        fn.restype = res
+        fn.argtypes = args
+    _lib = lib
+    return lib
+
+
+def strerror(rc: int) -> str:
+    try:
+        return load().pl_attn_strerror(rc).decode()
+    except Exception:  # library itself unavailable
+        return f"status {rc}"
+
+
+def _check(rc: int, what: str) -> None:
+    if rc != PL_OK:
+        raise PlAttnError(rc, what)
+
+
+def _ptr(a) -> int | None:
+    """numpy array -> host address (None passes NULL)."""
+    if a is None:
+        return None
+    return a.ctypes.data
+
+
+class Attn:
+    """The module context (one per process, like picolm's gpu.c state)."""
+
+    def __init__(self, n_layers: int, n_heads: int, n_kv_heads: int, max_seq: int,
+                 rope_base: float = 10000.0, rope_type: int = PL_ROPE_LLAMA,
+                 n_seqs: int = 1, device: int = 0, head_dim: int = HEAD_DIM):
+        self.lib = load()
+        self.n_layers, self.n_heads, self.n_kv_heads = n_layers, n_heads, n_kv_heads
+        self.head_dim, self.max_seq, self.n_seqs = head_dim, max_seq, n_seqs
+        self.q_dim = n_heads * head_dim
+        self.kv_dim = n_kv_heads * head_dim
+        _check(self.lib.pl_attn_init(n_layers, n_heads, n_kv_heads, head_dim, max_seq,
+                                     float(rope_base), rope_type, n_seqs, device),
+               "pl_attn_init")
+        self._open = True
+
+    # lifecycle ---------------------------------------------------------
+    def close(self) -> None:
+        if self._open:
+            self.lib.pl_attn_shutdown()
+            self._open = False
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+
+    def set_rope(self, cos_tab: np.ndarray, sin_tab: np.ndarray) -> None:
+        half = self.head_dim // 2
+        c = np.ascontiguousarray(cos_tab, np.float32).ravel()
+        s = np.ascontiguousarray(sin_tab, np.float32).ravel()
+        _check(self.lib.pl_attn_set_rope(c, s, c.size // half, half), "pl_attn_set_rope")
+
+    # host-buffer entry points -----------------------------------------
+    def decode(self, seq: int, layer: int, pos: int, q, k, v) -> np.ndarray:
+        out = np.empty(self.q_dim, np.float32)
+        _check(self.lib.pl_attn_decode(seq, layer, pos, _f32(q), _f32(k), _f32(v), out),
+               "pl_attn_decode")
+        return out
+
+    def decode_batch(self, layer: int, seqs, pos, q, k, v) -> np.ndarray:
+        seqs = np.ascontiguousarray(seqs, np.int32)
+        pos = np.ascontiguousarray(pos, np.int32)
+        n = seqs.size
+        out = np.empty(n * self.q_dim, np.float32)
+        _check(self.lib.pl_attn_decode_batch(layer, n, seqs, pos, _f32(q), _f32(k), _f32(v),
+                                             out), "pl_attn_decode_batch")
+        return out.reshape(n, self.q_dim)
+
+    def prefill(self, seq: int, layer: int, start_pos: int, q, k, v,
+                out_stride: int | None = None) -> np.ndarray:
+        q = _f32(q)
+        n_tok = q.size // self.q_dim
+        stride = self.q_dim if out_stride is None else out_stride
+        out = np.zeros(n_tok * stride, np.float32)
+        _check(self.lib.pl_attn_prefill(seq, layer, start_pos, n_tok, q, _f32(k), _f32(v),
+                                        out, stride), "pl_attn_prefill")
+        return out.reshape(n_tok, stride)
+
+    def rope(self, pos0: int, q=None, k=None):
+        qa = None if q is None else np.array(q, np.float32)
+        ka = None if k is None else np.array(k, np.float32)
+        n_tok = (qa.size // self.q_dim) if qa is not None else (ka.size // self.kv_dim)
+        _check(self.lib.pl_attn_rope(pos0, n_tok, _ptr(qa), _ptr(ka)), "pl_attn_rope")
+        return qa, ka
+
+    def kv_download(self, seq: int, layer: int, pos0: int, n_pos: int):
+        k = np.empty(n_pos * self.kv_dim, np.uint16)
+        v = np.empty(n_pos * self.kv_dim, np.uint16)
+        _check(self.lib.pl_kv_download(seq, layer, pos0, n_pos, _ptr(k), _ptr(v)),
+               "pl_kv_download")
+        return k.reshape(n_pos, self.kv_dim), v.reshape(n_pos, self.kv_dim)
+
+    def kv_upload(self, seq: int, layer: int, pos0: int, k, v) -> None:
+        k = np.ascontiguousarray(k, np.uint16)
+        v = np.ascontiguousarray(v, np.uint16)
+        n_pos = k.size // self.kv_dim
+        _check(self.lib.pl_kv_upload(seq, layer, pos0, n_pos, _ptr(k), _ptr(v)),
+               "pl_kv_upload")
+
+    # device-pointer entry points --------------------------------------
+    def decode_batch_dev(self, layer, n, d_seqs, d_pos, max_pos, d_q, d_k, d_v, d_out,
+                         stream=None) -> None:
+        _check(self.lib.pl_attn_decode_batch_dev(layer, n, d_seqs, d_pos, max_pos, d_q, d_k,
+                                                 d_v, d_out, stream),
+               "pl_attn_decode_batch_dev")
+
+    def prefill_dev(self, seq, layer, start_pos, n_tok, d_q, d_k, d_v, d_out,
+                    out_stride=None, stream=None) -> None:
+        stride = self.q_dim if out_stride is None else out_stride
+        _check(self.lib.pl_attn_prefill_dev(seq, layer, start_pos, n_tok, d_q, d_k, d_v, d_out,
+                                            stride, stream), "pl_attn_prefill_dev")
+
+    def decode_partial_dev(self, seq, layer, pos, row0, n_rows, append, d_q, d_k, d_v,
+                           d_part, stream=None) -> None:
+        _check(self.lib.pl_attn_decode_partial_dev(seq, layer, pos, row0, n_rows,
+                                                   1 if append else 0, d_q, d_k, d_v, d_part,
+                                                   stream), "pl_attn_decode_partial_dev")
+
+    def combine_dev(self, n_part, d_parts, d_out, stream=None) -> None:
+        _check(self.lib.pl_attn_combine_dev(n_part, d_parts, d_out, stream),
+               "pl_attn_combine_dev")
+
+    def profile(self, enable: bool = True) -> None:
+        _check(self.lib.pl_attn_profile(1 if enable else 0), "pl_attn_profile")
+
+    def profile_read(self):
+        """(attention-kernel ms, attention launches, all launches) since last read."""
+        ms, na, nl = C.c_double(), C.c_long(), C.c_long()
+        _check(self.lib.pl_attn_profile_read(C.byref(ms), C.byref(na), C.byref(nl)),
+               "pl_attn_profile_read")
+        return ms.value, na.value, nl.value
+
+    def kv_ptr(self, seq: int, layer: int):
+        k = _vp()
+        v = _vp()
+        _check(self.lib.pl_attn_kv_ptr(seq, layer, C.byref(k), C.byref(v)), "pl_attn_kv_ptr")
+        return k.value, v.value
+
+
+def _f32(a) -> np.ndarray:
+    return np.ascontiguousarray(a, np.float32).ravel()

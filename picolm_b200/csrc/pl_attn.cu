@@ -1,0 +1,755 @@
+// pl_attn.cu -- the module behind include/pl_attn.h: context, device KV
+// cache, RoPE tables, TMA descriptors, argument checks and kernel dispatch.
+//
+// One global context, as picolm's gpu.c keeps one (picolm/gpu.c:34-83).
+// Host-buffer calls stage their inputs through one pinned buffer and one
+// H2D copy, launch, and read the output and the device error word back with
+// one D2H copy.  There is no CPU fallback anywhere: every failure is a
+// negative status.
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <cmath>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <mutex>
+#include <vector>
+
+#include "../../include/pl_attn.h"
+#include "kern_decode.cuh"
+#include "kern_misc.cuh"
+#include "kern_prefill.cuh"
+
+namespace {
+
+using pl::kHD;
+using pl::kPartStride;
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                  const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                  const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                  CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+constexpr int kDecodeStages = 3;
+
+struct Ctx {
+  int device = -1;
+  int n_layers = 0, n_heads = 0, n_kv_heads = 0, max_seq = 0, n_seqs = 0, rope_type = 0;
+  int kv_dim = 0, q_dim = 0, kv_mul = 0;
+  int tp = 0;                 // decode tile rows (TP * n_kv_heads == 128)
+  int num_sms = 0, decode_slots = 0;
+  size_t layer_elems = 0;     // FP16 words per (seq, layer) slab
+  uint16_t* d_k = nullptr;    // [n_seqs][n_layers][max_seq][kv_dim]
+  uint16_t* d_v = nullptr;
+  float* d_cos = nullptr;     // [max_seq][32]
+  float* d_sin = nullptr;
+  // staging for host-buffer calls
+  uint8_t* d_stage = nullptr;
+  uint8_t* h_stage = nullptr;
+  size_t stage_cap = 0;
+  // split-KV partials
+  float* d_part = nullptr;
+  size_t part_cap = 0;        // floats
+  int* d_counters = nullptr;  // [n_seqs] per-sequence split counters (self-resetting)
+  // prefill FP16 q staging
+  uint16_t* d_q16 = nullptr;
+  size_t q16_cap = 0;         // elements
+  uint32_t* d_err = nullptr;  // device error word
+  cudaStream_t stream = nullptr;
+  CUtensorMap tm_k_dec, tm_v_dec;  // decode: box {64, tp, Hk, 1}
+  CUtensorMap tm_k_pf, tm_v_pf;    // prefill: box {64, 128 rows, 1, 1}
+  CUtensorMap tm_q16;              // prefill q staging: box {64, 1 head, 128 rows}
+  EncodeTiledFn encode = nullptr;
+  // profiling: event pairs around each attention kernel (see pl_attn_profile)
+  int profiling = 0;
+  std::vector<cudaEvent_t> ev_pool;  // even index: start, odd: end
+  size_t ev_used = 0;                // events recorded since the last read
+  long n_attn = 0, n_all = 0;        // attention launches / all launches
+};
+
+Ctx* g = nullptr;
+std::mutex g_mu;
+
+#define PL_CUDA(call)                                                     \
+  do {                                                                    \
+    cudaError_t e_ = (call);                                              \
+    if (e_ != cudaSuccess) {                                              \
+      std::fprintf(stderr, "pl_attn: %s failed: %s (%s:%d)\n", #call,      \
+                   cudaGetErrorString(e_), __FILE__, __LINE__);           \
+      return PL_ECUDA;                                                    \
+    }                                                                     \
+  } while (0)
+
+int make_map(EncodeTiledFn enc, CUtensorMap* m, uint16_t* base, int max_seq, int n_kv_heads,
+             int n_slabs, int box_rows, int box_heads) {
+  // dims, innermost first: head_dim, row, kv head, (seq, layer) slab
+  const cuuint64_t dims[4] = {static_cast<cuuint64_t>(kHD), static_cast<cuuint64_t>(max_seq),
+                              static_cast<cuuint64_t>(n_kv_heads),
+                              static_cast<cuuint64_t>(n_slabs)};
+  const cuuint64_t kv_bytes = static_cast<cuuint64_t>(n_kv_heads) * kHD * 2;
+  const cuuint64_t strides[3] = {kv_bytes, static_cast<cuuint64_t>(kHD) * 2,
+                                 kv_bytes * static_cast<cuuint64_t>(max_seq)};
+  const cuuint32_t box[4] = {static_cast<cuuint32_t>(kHD), static_cast<cuuint32_t>(box_rows),
+                             static_cast<cuuint32_t>(box_heads), 1u};
+  const cuuint32_t estr[4] = {1, 1, 1, 1};
+  CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4, base, dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    std::fprintf(stderr, "pl_attn: cuTensorMapEncodeTiled failed (%d)\n", static_cast<int>(r));
+    return PL_ECUDA;
+  }
+  return PL_OK;
+}
+
+void host_rope_tables(float* c, float* s, int max_seq, float base) {
+  // picolm/model.c:545-556, same libm calls in FP32
+  const int half = kHD / 2;
+  for (int p = 0; p < max_seq; ++p)
+    for (int i = 0; i < half; ++i) {
+      const float inv = powf(base, static_cast<float>(2 * i) / static_cast<float>(kHD));
+      const float theta = static_cast<float>(p) / inv;
+      c[static_cast<size_t>(p) * half + i] = cosf(theta);
+      s[static_cast<size_t>(p) * half + i] = sinf(theta);
+    }
+}
+
+int ensure_stage(size_t bytes) {
+  if (bytes <= g->stage_cap) return PL_OK;
+  size_t cap = g->stage_cap ? g->stage_cap : (1u << 20);
+  while (cap < bytes) cap *= 2;
+  if (g->d_stage) cudaFree(g->d_stage);
+  if (g->h_stage) cudaFreeHost(g->h_stage);
+  g->d_stage = nullptr;
+  g->h_stage = nullptr;
+  g->stage_cap = 0;
+  if (cudaMalloc(&g->d_stage, cap) != cudaSuccess) return PL_ENOMEM;
+  if (cudaMallocHost(&g->h_stage, cap) != cudaSuccess) return PL_ENOMEM;
+  g->stage_cap = cap;
+  return PL_OK;
+}
+
+int ensure_part(size_t floats) {
+  if (floats <= g->part_cap) return PL_OK;
+  if (g->d_part) cudaFree(g->d_part);
+  g->d_part = nullptr;
+  g->part_cap = 0;
+  if (cudaMalloc(&g->d_part, floats * sizeof(float)) != cudaSuccess) return PL_ENOMEM;
+  g->part_cap = floats;
+  return PL_OK;
+}
+
+// FP16 q staging for the prefill, [rows][n_heads][64], with its TMA map.
+// Rows past the current n_tok hold stale data; they only feed query rows
+// whose output is never stored.
+int ensure_q16(int n_tok) {
+  const size_t rows = static_cast<size_t>(n_tok);
+  if (rows * g->q_dim <= g->q16_cap) return PL_OK;
+  size_t cap_rows = 256;
+  while (cap_rows < rows) cap_rows *= 2;
+  if (g->d_q16) cudaFree(g->d_q16);
+  g->d_q16 = nullptr;
+  g->q16_cap = 0;
+  if (cudaMalloc(&g->d_q16, cap_rows * g->q_dim * sizeof(uint16_t)) != cudaSuccess)
+    return PL_ENOMEM;
+  if (cudaMemset(g->d_q16, 0, cap_rows * g->q_dim * sizeof(uint16_t)) != cudaSuccess)
+    return PL_ECUDA;
+  const cuuint64_t dims[3] = {static_cast<cuuint64_t>(kHD), static_cast<cuuint64_t>(g->n_heads),
+                              static_cast<cuuint64_t>(cap_rows)};
+  const cuuint64_t strides[2] = {static_cast<cuuint64_t>(kHD) * 2,
+                                 static_cast<cuuint64_t>(g->q_dim) * 2};
+  const cuuint32_t box[3] = {static_cast<cuuint32_t>(kHD), 1u,
+                             static_cast<cuuint32_t>(pl::kPfBlockM)};
+  const cuuint32_t estr[3] = {1, 1, 1};
+  if (g->encode(&g->tm_q16, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, g->d_q16, dims, strides, box, estr,
+                CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+    return PL_ECUDA;
+  g->q16_cap = cap_rows * g->q_dim;
+  return PL_OK;
+}
+
+// Profiling hooks: a start/end event pair around each attention kernel,
+// recorded on the kernel's own stream.
+cudaEvent_t prof_event() {
+  if (g->ev_used == g->ev_pool.size()) {
+    cudaEvent_t e;
+    if (cudaEventCreate(&e) != cudaSuccess) return nullptr;
+    g->ev_pool.push_back(e);
+  }
+  return g->ev_pool[g->ev_used++];
+}
+
+void prof_begin(cudaStream_t st) {
+  if (!g->profiling) return;
+  if (cudaEvent_t e = prof_event()) cudaEventRecord(e, st);
+}
+
+void prof_end(cudaStream_t st) {
+  if (!g->profiling) return;
+  if (cudaEvent_t e = prof_event()) cudaEventRecord(e, st);
+  ++g->n_attn;
+}
+
+void count_launch() {
+  if (g->profiling) ++g->n_all;
+}
+
+// Read (and clear) the device error word.
+int check_err_word(uint32_t w) {
+  if (w & (pl::ERR_TIMEOUT_FULL | pl::ERR_TIMEOUT_EMPTY | pl::ERR_TIMEOUT_MMA)) return PL_ETIMEOUT;
+  if (w) return PL_EFAIL;
+  return PL_OK;
+}
+
+int n_split_for(int n, int max_rows) {
+  const int tiles = (max_rows + g->tp - 1) / g->tp;
+  int ns = g->decode_slots / (n > 0 ? n : 1);
+  if (ns < 1) ns = 1;
+  if (ns > tiles) ns = tiles;
+  if (ns > 1024) ns = 1024;
+  return ns;
+}
+
+template <int TP>
+int launch_decode_tp(const pl::DecodeArgs& a, int n, cudaStream_t st) {
+  const int smem = kDecodeStages * 2 * TP * g->n_kv_heads * 128 + 1024 + 2 * kDecodeStages * 8;
+  auto kern = pl::decode_kernel<TP, kDecodeStages>;
+  static bool attr_done = false;
+  if (!attr_done) {
+    PL_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    attr_done = true;
+  }
+  dim3 grid(a.n_split, n);
+  dim3 block((g->n_kv_heads + 1) * 32);
+  prof_begin(st);
+  kern<<<grid, block, smem, st>>>(a, g->tm_k_dec, g->tm_v_dec);
+  PL_CUDA(cudaGetLastError());
+  prof_end(st);
+  count_launch();
+  return PL_OK;
+}
+
+// Launch the fused decode (+ combine when split).  All pointers are device
+// pointers.  mode/row0/n_rows/append as in DecodeArgs.  If part_out is not
+// null the merged partials are written there instead of out.
+int launch_decode(int layer, int n, const int* d_seqs, const int* d_pos, int max_rows,
+                  const float* d_q, const float* d_k, const float* d_v, float* d_out,
+                  int mode, int row0, int n_rows, int append, float* part_out,
+                  cudaStream_t st) {
+  int ns = n_split_for(n, max_rows);
+  if (mode == 1 && ns < 1) ns = 1;
+  const size_t need = static_cast<size_t>(n) * ns * g->n_heads * kPartStride;
+  int rc = ensure_part(need);
+  if (rc) return rc;
+  pl::DecodeArgs a;
+  a.n_layers = g->n_layers;
+  a.max_seq = g->max_seq;
+  a.n_heads = g->n_heads;
+  a.n_kv_heads = g->n_kv_heads;
+  a.kv_mul = g->kv_mul;
+  a.layer = layer;
+  a.n_slots = g->n_seqs;
+  a.rope_type = g->rope_type;
+  a.cos_tab = g->d_cos;
+  a.sin_tab = g->d_sin;
+  a.kc = g->d_k;
+  a.vc = g->d_v;
+  a.seqs = d_seqs;
+  a.pos = d_pos;
+  a.q = d_q;
+  a.k = d_k;
+  a.v = d_v;
+  a.out = d_out;
+  a.part = g->d_part;
+  a.part_out = part_out;
+  a.counters = g->d_counters;
+  a.n_split = ns;
+  a.merge_in_kernel = ns <= pl::kMaxInKernelMerge ? 1 : 0;
+  a.mode = mode;
+  a.row0 = row0;
+  a.n_rows = n_rows;
+  a.append = append;
+  a.score_scale = pl::kLog2e / sqrtf(static_cast<float>(kHD));
+  a.err = g->d_err;
+  switch (g->tp) {
+    case 16: rc = launch_decode_tp<16>(a, n, st); break;
+    case 32: rc = launch_decode_tp<32>(a, n, st); break;
+    case 64: rc = launch_decode_tp<64>(a, n, st); break;
+    case 128: rc = launch_decode_tp<128>(a, n, st); break;
+    default: return PL_EUNSUPPORTED;
+  }
+  if (rc) return rc;
+  if (!a.merge_in_kernel) {
+    pl::combine_kernel<<<dim3(g->n_heads, n), 64, 0, st>>>(ns, g->n_heads, g->d_part,
+                                                           mode == 1 ? nullptr : d_out, part_out);
+    PL_CUDA(cudaGetLastError());
+    count_launch();
+  }
+  return PL_OK;
+}
+
+cudaStream_t pick_stream(void* s) {
+  return s ? static_cast<cudaStream_t>(s) : g->stream;
+}
+
+int check_seq_layer(int seq, int layer) {
+  if (!g) return PL_ESTATE;
+  if (seq < 0 || seq >= g->n_seqs || layer < 0 || layer >= g->n_layers) return PL_EARG;
+  return PL_OK;
+}
+
+uint16_t* slab_k(int seq, int layer) {
+  return g->d_k + (static_cast<size_t>(seq) * g->n_layers + layer) * g->layer_elems;
+}
+uint16_t* slab_v(int seq, int layer) {
+  return g->d_v + (static_cast<size_t>(seq) * g->n_layers + layer) * g->layer_elems;
+}
+
+// Synchronise the module stream, fetch the error word (already copied to
+// the pinned area at `h_err`), clear it on the device if set.
+int finish_host_call(const uint32_t* h_err) {
+  PL_CUDA(cudaStreamSynchronize(g->stream));
+  const uint32_t w = *h_err;
+  if (w) {
+    cudaMemsetAsync(g->d_err, 0, sizeof(uint32_t), g->stream);
+    cudaStreamSynchronize(g->stream);
+  }
+  return check_err_word(w);
+}
+
+void free_ctx(Ctx* c) {
+  if (!c) return;
+  if (c->device >= 0) cudaSetDevice(c->device);
+  if (c->stream) cudaStreamSynchronize(c->stream);
+  cudaFree(c->d_k);
+  cudaFree(c->d_v);
+  cudaFree(c->d_cos);
+  cudaFree(c->d_sin);
+  cudaFree(c->d_stage);
+  cudaFreeHost(c->h_stage);
+  cudaFree(c->d_part);
+  cudaFree(c->d_counters);
+  cudaFree(c->d_q16);
+  cudaFree(c->d_err);
+  for (cudaEvent_t e : c->ev_pool) cudaEventDestroy(e);
+  if (c->stream) cudaStreamDestroy(c->stream);
+  delete c;
+}
+
+}  // namespace
+
+extern "C" {
+
+const char* pl_attn_strerror(int rc) {
+  switch (rc) {
+    case PL_OK: return "success";
+    case PL_EFAIL: return "failure";
+    case PL_EARG: return "argument out of range";
+    case PL_ENOMEM: return "out of device or pinned host memory";
+    case PL_ECUDA: return "CUDA error";
+    case PL_ETIMEOUT: return "a bounded device-side wait expired";
+    case PL_ESTATE: return "attention module not initialised (or initialised twice)";
+    case PL_EDEVICE: return "no usable sm_100 CUDA device";
+    case PL_EUNSUPPORTED: return "shape not supported by the B200 attention kernels";
+    default: return "unknown status";
+  }
+}
+
+int pl_attn_available(void) { return g != nullptr; }
+
+int pl_attn_init(int n_layers, int n_heads, int n_kv_heads, int head_dim, int max_seq_len,
+                 float rope_freq_base, int rope_type, int n_seqs, int device) {
+  std::lock_guard<std::mutex> lk(g_mu);
+  if (g) return PL_ESTATE;
+  if (n_layers <= 0 || n_heads <= 0 || n_kv_heads <= 0 || max_seq_len <= 0 || n_seqs <= 0 ||
+      device < 0 || !(rope_freq_base > 0.f))
+    return PL_EARG;
+  if (head_dim != kHD) return PL_EUNSUPPORTED;
+  if (n_heads % n_kv_heads) return PL_EUNSUPPORTED;
+  const int kv_mul = n_heads / n_kv_heads;
+  if (!(n_kv_heads == 1 || n_kv_heads == 2 || n_kv_heads == 4 || n_kv_heads == 8))
+    return PL_EUNSUPPORTED;
+  if (!(kv_mul == 1 || kv_mul == 2 || kv_mul == 4 || kv_mul == 8)) return PL_EUNSUPPORTED;
+  if (rope_type != PL_ROPE_LLAMA && rope_type != PL_ROPE_QWEN) return PL_EARG;
+
+  int ndev = 0;
+  if (cudaGetDeviceCount(&ndev) != cudaSuccess || device >= ndev) return PL_EDEVICE;
+  cudaDeviceProp prop;
+  if (cudaGetDeviceProperties(&prop, device) != cudaSuccess) return PL_EDEVICE;
+  if (prop.major != 10) return PL_EDEVICE;
+  if (cudaSetDevice(device) != cudaSuccess) return PL_EDEVICE;
+
+  Ctx* c = new Ctx();
+  c->device = device;
+  c->n_layers = n_layers;
+  c->n_heads = n_heads;
+  c->n_kv_heads = n_kv_heads;
+  c->max_seq = max_seq_len;
+  c->n_seqs = n_seqs;
+  c->rope_type = rope_type;
+  c->kv_dim = n_kv_heads * kHD;
+  c->q_dim = n_heads * kHD;
+  c->kv_mul = kv_mul;
+  c->tp = 128 / n_kv_heads;
+  c->num_sms = prop.multiProcessorCount;
+  c->layer_elems = static_cast<size_t>(max_seq_len) * c->kv_dim;
+  const size_t cache_elems = c->layer_elems * n_layers * n_seqs;
+
+  int rc = PL_OK;
+  void* fn = nullptr;
+  cudaDriverEntryPointQueryResult qres;
+  if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &qres) !=
+          cudaSuccess ||
+      qres != cudaDriverEntryPointSuccess || !fn) {
+    free_ctx(c);
+    return PL_ECUDA;
+  }
+  c->encode = reinterpret_cast<EncodeTiledFn>(fn);
+
+  if (cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking) != cudaSuccess ||
+      cudaMalloc(&c->d_k, cache_elems * 2) != cudaSuccess ||
+      cudaMalloc(&c->d_v, cache_elems * 2) != cudaSuccess ||
+      cudaMalloc(&c->d_cos, sizeof(float) * max_seq_len * (kHD / 2)) != cudaSuccess ||
+      cudaMalloc(&c->d_sin, sizeof(float) * max_seq_len * (kHD / 2)) != cudaSuccess ||
+      cudaMalloc(&c->d_err, 256) != cudaSuccess ||
+      cudaMalloc(&c->d_counters, sizeof(int) * (n_seqs + 1)) != cudaSuccess) {
+    free_ctx(c);
+    return PL_ENOMEM;
+  }
+  cudaMemsetAsync(c->d_k, 0, cache_elems * 2, c->stream);
+  cudaMemsetAsync(c->d_v, 0, cache_elems * 2, c->stream);
+  cudaMemsetAsync(c->d_err, 0, 256, c->stream);
+  cudaMemsetAsync(c->d_counters, 0, sizeof(int) * (n_seqs + 1), c->stream);
+  {
+    const size_t n = static_cast<size_t>(max_seq_len) * (kHD / 2);
+    float* hc = static_cast<float*>(std::malloc(n * sizeof(float)));
+    float* hs = static_cast<float*>(std::malloc(n * sizeof(float)));
+    if (!hc || !hs) {
+      std::free(hc);
+      std::free(hs);
+      free_ctx(c);
+      return PL_ENOMEM;
+    }
+    host_rope_tables(hc, hs, max_seq_len, rope_freq_base);
+    cudaMemcpy(c->d_cos, hc, n * sizeof(float), cudaMemcpyHostToDevice);
+    cudaMemcpy(c->d_sin, hs, n * sizeof(float), cudaMemcpyHostToDevice);
+    std::free(hc);
+    std::free(hs);
+  }
+  const int n_slabs = n_seqs * n_layers;
+  if ((rc = make_map(c->encode, &c->tm_k_dec, c->d_k, max_seq_len, n_kv_heads, n_slabs, c->tp,
+                     n_kv_heads)) ||
+      (rc = make_map(c->encode, &c->tm_v_dec, c->d_v, max_seq_len, n_kv_heads, n_slabs, c->tp,
+                     n_kv_heads)) ||
+      (rc = make_map(c->encode, &c->tm_k_pf, c->d_k, max_seq_len, n_kv_heads, n_slabs,
+                     pl::kPfBlockN, 1)) ||
+      (rc = make_map(c->encode, &c->tm_v_pf, c->d_v, max_seq_len, n_kv_heads, n_slabs,
+                     pl::kPfBlockN, 1))) {
+    free_ctx(c);
+    return rc;
+  }
+  // decode occupancy: concurrent CTAs the split heuristic aims to fill
+  {
+    const int smem = kDecodeStages * 2 * 128 * 128 + 1024 + 2 * kDecodeStages * 8;
+    const int per_sm = (227 * 1024) / smem;
+    c->decode_slots = c->num_sms * (per_sm > 0 ? per_sm : 1);
+  }
+  if (cudaStreamSynchronize(c->stream) != cudaSuccess) {
+    free_ctx(c);
+    return PL_ECUDA;
+  }
+  g = c;
+  return PL_OK;
+}
+
+void pl_attn_shutdown(void) {
+  std::lock_guard<std::mutex> lk(g_mu);
+  free_ctx(g);
+  g = nullptr;
+}
+
+int pl_attn_set_rope(const float* cos_tab, const float* sin_tab, int n_rows, int half_dim) {
+  if (!g) return PL_ESTATE;
+  if (!cos_tab || !sin_tab || half_dim != kHD / 2 || n_rows <= 0) return PL_EARG;
+  const int rows = n_rows < g->max_seq ? n_rows : g->max_seq;
+  const size_t bytes = static_cast<size_t>(rows) * half_dim * sizeof(float);
+  PL_CUDA(cudaMemcpyAsync(g->d_cos, cos_tab, bytes, cudaMemcpyHostToDevice, g->stream));
+  PL_CUDA(cudaMemcpyAsync(g->d_sin, sin_tab, bytes, cudaMemcpyHostToDevice, g->stream));
+  PL_CUDA(cudaStreamSynchronize(g->stream));
+  return PL_OK;
+}
+
+int pl_attn_decode_batch(int layer, int n, const int* seqs, const int* pos, const float* q,
+                         const float* k, const float* v, float* out) {
+  if (!g) return PL_ESTATE;
+  if (n <= 0 || n > g->n_seqs || !seqs || !pos || !q || !k || !v || !out) return PL_EARG;
+  if (layer < 0 || layer >= g->n_layers) return PL_EARG;
+  int max_pos = 0;
+  for (int i = 0; i < n; ++i) {
+    if (seqs[i] < 0 || seqs[i] >= g->n_seqs || pos[i] < 0 || pos[i] >= g->max_seq)
+      return PL_EARG;
+    for (int j = 0; j < i; ++j)
+      if (seqs[j] == seqs[i]) return PL_EARG;
+    if (pos[i] > max_pos) max_pos = pos[i];
+  }
+  if (cudaSetDevice(g->device) != cudaSuccess) return PL_ECUDA;
+  const size_t qb = static_cast<size_t>(n) * g->q_dim * sizeof(float);
+  const size_t kb = static_cast<size_t>(n) * g->kv_dim * sizeof(float);
+  const size_t ib = static_cast<size_t>(n) * sizeof(int);
+  const size_t in_bytes = qb + 2 * kb + 2 * ib;
+  const size_t out_off = (in_bytes + 255) & ~static_cast<size_t>(255);
+  const size_t total = out_off + qb + 256;
+  int rc = ensure_stage(total);
+  if (rc) return rc;
+  uint8_t* h = g->h_stage;
+  std::memcpy(h, q, qb);
+  std::memcpy(h + qb, k, kb);
+  std::memcpy(h + qb + kb, v, kb);
+  std::memcpy(h + qb + 2 * kb, seqs, ib);
+  std::memcpy(h + qb + 2 * kb + ib, pos, ib);
+  uint8_t* d = g->d_stage;
+  PL_CUDA(cudaMemcpyAsync(d, h, in_bytes, cudaMemcpyHostToDevice, g->stream));
+  float* d_out = reinterpret_cast<float*>(d + out_off);
+  rc = launch_decode(layer, n, reinterpret_cast<int*>(d + qb + 2 * kb),
+                     reinterpret_cast<int*>(d + qb + 2 * kb + ib), max_pos + 1,
+                     reinterpret_cast<float*>(d), reinterpret_cast<float*>(d + qb),
+                     reinterpret_cast<float*>(d + qb + kb), d_out, 0, 0, 0, 1, nullptr,
+                     g->stream);
+  if (rc) return rc;
+  // output and the error word in one read-back
+  PL_CUDA(cudaMemcpyAsync(d + out_off + qb, g->d_err, sizeof(uint32_t), cudaMemcpyDeviceToDevice,
+                          g->stream));
+  PL_CUDA(cudaMemcpyAsync(h + out_off, d + out_off, qb + sizeof(uint32_t), cudaMemcpyDeviceToHost,
+                          g->stream));
+  rc = finish_host_call(reinterpret_cast<uint32_t*>(h + out_off + qb));
+  if (rc) return rc;
+  std::memcpy(out, h + out_off, qb);
+  return PL_OK;
+}
+
+int pl_attn_decode(int seq, int layer, int pos, const float* q, const float* k, const float* v,
+                   float* out) {
+  return pl_attn_decode_batch(layer, 1, &seq, &pos, q, k, v, out);
+}
+
+int pl_attn_decode_batch_dev(int layer, int n, const int* d_seqs, const int* d_pos, int max_pos,
+                             const float* d_q, const float* d_k, const float* d_v, float* d_out,
+                             void* stream) {
+  if (!g) return PL_ESTATE;
+  if (n <= 0 || n > g->n_seqs || layer < 0 || layer >= g->n_layers || max_pos < 0 ||
+      max_pos >= g->max_seq)
+    return PL_EARG;
+  if (!d_seqs || !d_pos || !d_q || !d_k || !d_v || !d_out) return PL_EARG;
+  return launch_decode(layer, n, d_seqs, d_pos, max_pos + 1, d_q, d_k, d_v, d_out, 0, 0, 0, 1,
+                       nullptr, pick_stream(stream));
+}
+
+int pl_attn_decode_partial_dev(int seq, int layer, int pos, int row0, int n_rows, int append,
+                               const float* d_q, const float* d_k, const float* d_v,
+                               float* d_part, void* stream) {
+  int rc = check_seq_layer(seq, layer);
+  if (rc) return rc;
+  if (pos < 0 || row0 < 0 || n_rows < 0 || n_rows > g->max_seq || !d_q || !d_part) return PL_EARG;
+  if (append && (pos - row0 < 0 || pos - row0 >= n_rows || !d_k || !d_v)) return PL_EARG;
+  // the RoPE table must cover the global position
+  if (pos >= g->max_seq) return PL_EARG;
+  // seq and pos as one-element device arrays in the error-word page
+  int* d_ints = reinterpret_cast<int*>(g->d_err) + 16;
+  const int hv[2] = {seq, pos};
+  cudaStream_t st = pick_stream(stream);
+  PL_CUDA(cudaMemcpyAsync(d_ints, hv, sizeof hv, cudaMemcpyHostToDevice, st));
+  return launch_decode(layer, 1, d_ints, d_ints + 1, n_rows > 0 ? n_rows : 1, d_q,
+                       d_k ? d_k : d_q, d_v ? d_v : d_q, nullptr, 1, row0, n_rows,
+                       append ? 1 : 0, d_part, st);
+}
+
+int pl_attn_combine_dev(int n_part, const float* d_parts, float* d_out, void* stream) {
+  if (!g) return PL_ESTATE;
+  if (n_part <= 0 || !d_parts || !d_out) return PL_EARG;
+  cudaStream_t st = pick_stream(stream);
+  pl::combine_kernel<<<dim3(g->n_heads, 1), 64, 0, st>>>(n_part, g->n_heads, d_parts, d_out,
+                                                         nullptr);
+  PL_CUDA(cudaGetLastError());
+  count_launch();
+  return PL_OK;
+}
+
+int pl_attn_rope(int pos0, int n_tok, float* q, float* k) {
+  if (!g) return PL_ESTATE;
+  if (n_tok <= 0 || pos0 < 0 || pos0 + n_tok > g->max_seq || (!q && !k)) return PL_EARG;
+  const size_t qb = q ? static_cast<size_t>(n_tok) * g->q_dim * sizeof(float) : 0;
+  const size_t kb = k ? static_cast<size_t>(n_tok) * g->kv_dim * sizeof(float) : 0;
+  int rc = ensure_stage(qb + kb + 256);
+  if (rc) return rc;
+  if (q) std::memcpy(g->h_stage, q, qb);
+  if (k) std::memcpy(g->h_stage + qb, k, kb);
+  PL_CUDA(cudaMemcpyAsync(g->d_stage, g->h_stage, qb + kb, cudaMemcpyHostToDevice, g->stream));
+  float* dq = q ? reinterpret_cast<float*>(g->d_stage) : nullptr;
+  float* dk = k ? reinterpret_cast<float*>(g->d_stage + qb) : nullptr;
+  const dim3 rgrid(n_tok, (g->n_heads + g->n_kv_heads + 7) / 8);
+  pl::rope_inplace_kernel<<<rgrid, 256, 0, g->stream>>>(
+      dq, dk, g->n_heads, g->n_kv_heads, pos0, g->d_cos, g->d_sin, g->rope_type);
+  PL_CUDA(cudaGetLastError());
+  PL_CUDA(cudaMemcpyAsync(g->h_stage, g->d_stage, qb + kb, cudaMemcpyDeviceToHost, g->stream));
+  PL_CUDA(cudaStreamSynchronize(g->stream));
+  if (q) std::memcpy(q, g->h_stage, qb);
+  if (k) std::memcpy(k, g->h_stage + qb, kb);
+  return PL_OK;
+}
+
+int pl_kv_download(int seq, int layer, int pos0, int n_pos, uint16_t* k, uint16_t* v) {
+  int rc = check_seq_layer(seq, layer);
+  if (rc) return rc;
+  if (pos0 < 0 || n_pos < 0 || pos0 + n_pos > g->max_seq) return PL_EARG;
+  if (n_pos == 0) return PL_OK;
+  const size_t off = static_cast<size_t>(pos0) * g->kv_dim;
+  const size_t bytes = static_cast<size_t>(n_pos) * g->kv_dim * 2;
+  if (k) PL_CUDA(cudaMemcpyAsync(k, slab_k(seq, layer) + off, bytes, cudaMemcpyDeviceToHost,
+                                 g->stream));
+  if (v) PL_CUDA(cudaMemcpyAsync(v, slab_v(seq, layer) + off, bytes, cudaMemcpyDeviceToHost,
+                                 g->stream));
+  PL_CUDA(cudaStreamSynchronize(g->stream));
+  return PL_OK;
+}
+
+int pl_kv_upload(int seq, int layer, int pos0, int n_pos, const uint16_t* k, const uint16_t* v) {
+  int rc = check_seq_layer(seq, layer);
+  if (rc) return rc;
+  if (pos0 < 0 || n_pos < 0 || pos0 + n_pos > g->max_seq) return PL_EARG;
+  if (n_pos == 0) return PL_OK;
+  const size_t off = static_cast<size_t>(pos0) * g->kv_dim;
+  const size_t bytes = static_cast<size_t>(n_pos) * g->kv_dim * 2;
+  if (k) PL_CUDA(cudaMemcpyAsync(slab_k(seq, layer) + off, k, bytes, cudaMemcpyHostToDevice,
+                                 g->stream));
+  if (v) PL_CUDA(cudaMemcpyAsync(slab_v(seq, layer) + off, v, bytes, cudaMemcpyHostToDevice,
+                                 g->stream));
+  PL_CUDA(cudaStreamSynchronize(g->stream));
+  return PL_OK;
+}
+
+int pl_attn_kv_ptr(int seq, int layer, uint16_t** d_k, uint16_t** d_v) {
+  int rc = check_seq_layer(seq, layer);
+  if (rc) return rc;
+  if (d_k) *d_k = slab_k(seq, layer);
+  if (d_v) *d_v = slab_v(seq, layer);
+  return PL_OK;
+}
+
+// ---------------------------------------------------------------- prefill
+static int launch_prefill(int seq, int layer, int start_pos, int n_tok, const float* d_q,
+                          const float* d_k, const float* d_v, float* d_out, int out_stride,
+                          cudaStream_t st) {
+  int rc = ensure_q16(n_tok);
+  if (rc) return rc;
+  const size_t off = static_cast<size_t>(start_pos) * g->kv_dim;
+  const dim3 pgrid(n_tok, (g->n_heads + g->n_kv_heads + 7) / 8);
+  pl::prefill_prologue_kernel<<<pgrid, 256, 0, st>>>(
+      d_q, d_k, d_v, g->d_q16, slab_k(seq, layer) + off, slab_v(seq, layer) + off, g->n_heads,
+      g->n_kv_heads, start_pos, g->d_cos, g->d_sin, g->rope_type);
+  PL_CUDA(cudaGetLastError());
+  count_launch();
+  pl::PrefillArgs a;
+  a.q16 = g->d_q16;
+  a.out = d_out;
+  a.out_stride = out_stride;
+  a.n_tok = n_tok;
+  a.start_pos = start_pos;
+  a.n_heads = g->n_heads;
+  a.kv_mul = g->kv_mul;
+  a.slab = seq * g->n_layers + layer;
+  a.score_scale = pl::kLog2e / sqrtf(static_cast<float>(kHD));
+  a.err = g->d_err;
+  prof_begin(st);
+  if (pl::launch_prefill_attention(a, g->tm_q16, g->tm_k_pf, g->tm_v_pf, st) != 0)
+    return PL_ECUDA;
+  prof_end(st);
+  count_launch();
+  return PL_OK;
+}
+
+int pl_attn_prefill(int seq, int layer, int start_pos, int n_tok, const float* q, const float* k,
+                    const float* v, float* out, int out_stride) {
+  int rc = check_seq_layer(seq, layer);
+  if (rc) return rc;
+  if (n_tok <= 0 || start_pos < 0 || start_pos + n_tok > g->max_seq || !q || !k || !v || !out ||
+      out_stride < g->q_dim)
+    return PL_EARG;
+  if (cudaSetDevice(g->device) != cudaSuccess) return PL_ECUDA;
+  const size_t qb = static_cast<size_t>(n_tok) * g->q_dim * sizeof(float);
+  const size_t kb = static_cast<size_t>(n_tok) * g->kv_dim * sizeof(float);
+  const size_t in_bytes = qb + 2 * kb;
+  const size_t out_off = (in_bytes + 255) & ~static_cast<size_t>(255);
+  const size_t total = out_off + qb + 256;
+  rc = ensure_stage(total);
+  if (rc) return rc;
+  uint8_t* h = g->h_stage;
+  uint8_t* d = g->d_stage;
+  std::memcpy(h, q, qb);
+  std::memcpy(h + qb, k, kb);
+  std::memcpy(h + qb + kb, v, kb);
+  PL_CUDA(cudaMemcpyAsync(d, h, in_bytes, cudaMemcpyHostToDevice, g->stream));
+  float* d_out = reinterpret_cast<float*>(d + out_off);
+  rc = launch_prefill(seq, layer, start_pos, n_tok, reinterpret_cast<float*>(d),
+                      reinterpret_cast<float*>(d + qb), reinterpret_cast<float*>(d + qb + kb),
+                      d_out, g->q_dim, g->stream);
+  if (rc) return rc;
+  PL_CUDA(cudaMemcpyAsync(d + out_off + qb, g->d_err, sizeof(uint32_t), cudaMemcpyDeviceToDevice,
+                          g->stream));
+  PL_CUDA(cudaMemcpyAsync(h + out_off, d + out_off, qb + sizeof(uint32_t), cudaMemcpyDeviceToHost,
+                          g->stream));
+  rc = finish_host_call(reinterpret_cast<uint32_t*>(h + out_off + qb));
+  if (rc) return rc;
+  if (out_stride == g->q_dim) {
+    std::memcpy(out, h + out_off, qb);
+  } else {
+    for (int r = 0; r < n_tok; ++r)
+      std::memcpy(out + static_cast<size_t>(r) * out_stride,
+                  h + out_off + static_cast<size_t>(r) * g->q_dim * sizeof(float),
+                  g->q_dim * sizeof(float));
+  }
+  return PL_OK;
+}
+
+int pl_attn_prefill_dev(int seq, int layer, int start_pos, int n_tok, const float* d_q,
+                        const float* d_k, const float* d_v, float* d_out, int out_stride,
+                        void* stream) {
+  int rc = check_seq_layer(seq, layer);
+  if (rc) return rc;
+  if (n_tok <= 0 || start_pos < 0 || start_pos + n_tok > g->max_seq || !d_q || !d_k || !d_v ||
+      !d_out || out_stride < g->q_dim)
+    return PL_EARG;
+  return launch_prefill(seq, layer, start_pos, n_tok, d_q, d_k, d_v, d_out, out_stride,
+                        pick_stream(stream));
+}
+
+int pl_attn_profile(int enable) {
+  if (!g) return PL_ESTATE;
+  g->profiling = enable ? 1 : 0;
+  g->ev_used = 0;
+  g->n_attn = 0;
+  g->n_all = 0;
+  return PL_OK;
+}
+
+int pl_attn_profile_read(double* attn_ms, long* attn_launches, long* all_launches) {
+  if (!g) return PL_ESTATE;
+  double ms = 0.0;
+  for (size_t i = 0; i + 1 < g->ev_used; i += 2) {
+    PL_CUDA(cudaEventSynchronize(g->ev_pool[i + 1]));
+    float t = 0.f;
+    PL_CUDA(cudaEventElapsedTime(&t, g->ev_pool[i], g->ev_pool[i + 1]));
+    ms += t;
+  }
+  if (attn_ms) *attn_ms = ms;
+  if (attn_launches) *attn_launches = g->n_attn;
+  if (all_launches) *all_launches = g->n_all;
+  g->ev_used = 0;
+  g->n_attn = 0;
+  g->n_all = 0;
+  return PL_OK;
+}
+
+}  // extern "C"
