@@ -95,7 +95,10 @@ class ClockSampler:
             import pynvml
             pynvml.nvmlInit()
             import torch
-            bus = torch.cuda.get_device_properties(cuda_index).pci_bus_id
+            p = torch.cuda.get_device_properties(cuda_index)
+            # torch reports the PCI location as integers; NVML wants the
+            # "domain:bus:device.function" string
+            bus = f"{int(p.pci_domain_id):08X}:{int(p.pci_bus_id):02X}:{int(p.pci_device_id):02X}.0"
             try:
                 self._h = pynvml.nvmlDeviceGetHandleByPciBusId(bus)
             except Exception:
@@ -190,7 +193,15 @@ def run_batched_decode(args, rank, world, local, peaks):
     pos = (CTX + torch.arange(NSTEP, dtype=torch.int32, device=dev))[:, None].repeat(
         1, SEQS_PER_GPU).contiguous()
     flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
+    flush_rd = torch.ones(L2_FLUSH_BYTES // 4, dtype=torch.int32, device=dev)
     stream = torch.cuda.current_stream(dev)
+
+    def l2_flush():
+        # write a buffer larger than L2, then read another one, so that the
+        # L2 holds clean unrelated lines (no dirty write-back lands inside
+        # the timed step)
+        flush.zero_()
+        flush_rd.sum()
     sh = stream.cuda_stream
 
     def step(i):
@@ -200,7 +211,7 @@ def run_batched_decode(args, rank, world, local, peaks):
                             out[s].data_ptr(), sh)
 
     for i in range(args.warmup):
-        flush.zero_()
+        l2_flush()
         step(i)
     torch.cuda.synchronize()
     starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
@@ -212,7 +223,7 @@ def run_batched_decode(args, rank, world, local, peaks):
     with ClockSampler(local) as clk:
         for j in range(args.steps):
             i = args.warmup + j
-            flush.zero_()                    # L2 flushed outside the timed pair
+            l2_flush()                       # outside the timed event pair
             starts[j].record(stream)
             step(i)
             ends[j].record(stream)
@@ -460,7 +471,8 @@ def main():
                           "TinyLlama heads 32/4, hd 64, 64 decode steps (pos 2048..2111) cycled",
               "seqs_per_gpu": SEQS_PER_GPU, "global_seqs": SEQS_PER_GPU * world,
               "cached_positions": CTX, "parallelism": f"sequence shards x{world}, no collective",
-              "l2": "flushed (256 MB write) before every timed step, outside the timed pair"}
+              "l2": "flushed before every timed step, outside the timed pair: 256 MB write "
+                    "then 256 MB read of another buffer (L2 is 126 MB)"}
     base = {"metric": "decode-attn HBM GB/s", "unit": "GB/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "fp16 KV, fp32 accumulate",

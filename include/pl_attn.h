@@ -124,7 +124,7 @@ int  pl_kv_upload(int seq, int layer, int pos0, int n_pos, const uint16_t *k,
                   const uint16_t *v);
 
 /* ---- Device-pointer entry points (asynchronous on `stream`, a
- *      cudaStream_t passed as void*; NULL = the module's own stream) ---- */
+ *      cudaStream_t passed as void*; NULL = the CUDA default stream) ---- */
 
 /* pl_attn_decode_batch with every array already in device memory.
  * max_pos must bound every d_pos[i] (it sizes the KV split). */

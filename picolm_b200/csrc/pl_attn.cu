@@ -291,9 +291,9 @@ int launch_decode(int layer, int n, const int* d_seqs, const int* d_pos, int max
   return PL_OK;
 }
 
-cudaStream_t pick_stream(void* s) {
-  return s ? static_cast<cudaStream_t>(s) : g->stream;
-}
+// Device-pointer calls run on the caller's stream; NULL is the CUDA
+// default (legacy) stream, as everywhere in CUDA.
+cudaStream_t pick_stream(void* s) { return static_cast<cudaStream_t>(s); }
 
 int check_seq_layer(int seq, int layer) {
   if (!g) return PL_ESTATE;
