@@ -166,6 +166,30 @@ int  pl_attn_combine_dev(int n_part, const float *d_parts, float *d_out,
  * *d_v, each [max_seq][kv_dim].  For engines that share the cache. */
 int  pl_attn_kv_ptr(int seq, int layer, uint16_t **d_k, uint16_t **d_v);
 
+/* pl_attn_decode_batch_dev for callers that cannot allow the library to
+ * allocate device memory.  No counterpart in the reference: picolm's
+ * attention runs on the CPU and allocates nothing per step.
+ * pl_attn_decode_batch_dev may cudaMalloc a larger buffer for its split
+ * partials the first time a launch needs one; serving engines that reserve
+ * the whole device in their own pool, or latency-critical loops where an
+ * allocation's implicit device synchronisation would stall other streams,
+ * cannot accept that.  This entry point runs the same kernel with its
+ * scratch (split partials and merge counters) in one fixed file-scope device
+ * array of 4 MiB + 4 KiB, which every GPU that loads the library holds until
+ * the process exits; it calls no cudaMalloc, cudaFree or other allocating
+ * routine.  Limits: n <= 1024 sequences (larger n fails with PL_EARG and a
+ * message on stderr), and the KV split is capped so the partials fit in
+ * 4 MiB.  The first call on a device looks up the array's device address
+ * (cudaGetSymbolAddress); make that first call before any stream capture.
+ * All calls share the one array, so calls that overlap on the GPU (e.g. on
+ * two streams at once) race; the merge counters are cleared on the stream
+ * at the start of every call. */
+int  pl_attn_decode_batch_dev_noalloc(int layer, int n, const int *d_seqs,
+                                      const int *d_pos, int max_pos,
+                                      const float *d_q, const float *d_k,
+                                      const float *d_v, float *d_out,
+                                      void *stream);
+
 /* ---- Profiling (cf. picolm's timing stats, picolm.c:285-302) ---- */
 
 /* Enable (1) or disable (0) device timing: every later call records CUDA

@@ -84,6 +84,7 @@ def load(path: str = LIB_PATH) -> C.CDLL:
         "pl_attn_decode_partial_dev": (i, [i, i, i, i, i, i, _vp, _vp, _vp, _vp, _vp]),
         "pl_attn_combine_dev": (i, [i, _vp, _vp, _vp]),
         "pl_attn_kv_ptr": (i, [i, i, C.POINTER(_vp), C.POINTER(_vp)]),
+        "pl_attn_decode_batch_dev_noalloc": (i, [i, i, _vp, _vp, i, _vp, _vp, _vp, _vp, _vp]),
         "pl_attn_profile": (i, [i]),
         "pl_attn_profile_read": (i, [C.POINTER(C.c_double), C.POINTER(C.c_long),
                                      C.POINTER(C.c_long)]),
@@ -202,6 +203,15 @@ class Attn:
         _check(self.lib.pl_attn_decode_batch_dev(layer, n, d_seqs, d_pos, max_pos, d_q, d_k,
                                                  d_v, d_out, stream),
                "pl_attn_decode_batch_dev")
+
+    def decode_batch_dev_noalloc(self, layer, n, d_seqs, d_pos, max_pos, d_q, d_k, d_v,
+                                 d_out, stream=None) -> None:
+        """decode_batch_dev without any device allocation (fixed static scratch:
+        n <= 1024, split partials capped at 4 MiB; calls sharing it must not
+        overlap on the GPU)."""
+        _check(self.lib.pl_attn_decode_batch_dev_noalloc(layer, n, d_seqs, d_pos, max_pos, d_q,
+                                                         d_k, d_v, d_out, stream),
+               "pl_attn_decode_batch_dev_noalloc")
 
     def prefill_dev(self, seq, layer, start_pos, n_tok, d_q, d_k, d_v, d_out,
                     out_stride=None, stream=None) -> None:

@@ -753,3 +753,142 @@ int pl_attn_profile_read(double* attn_ms, long* attn_launches, long* all_launche
 }
 
 }  // extern "C"
+
+// =====================================================================
+// Decode that allocates nothing.
+//
+// pl_attn_decode_batch_dev may allocate device memory for its split-KV
+// partials the first time a launch needs more than it holds.  Some callers
+// cannot let a library allocate: serving engines that reserve the whole
+// device up front in their own pool (a late cudaMalloc can then fail, or
+// fragment that pool), and latency-critical decode loops, where cudaMalloc
+// and cudaFree may synchronise the device and stall every other stream.
+// pl_attn_decode_batch_dev_noalloc runs the same decode kernel with its
+// scratch in one file-scope __device__ array of fixed size instead.
+// =====================================================================
+namespace {
+
+constexpr int kNoAllocMaxSeqs = 1024;                       // merge counters
+constexpr size_t kNoAllocPartBytes = static_cast<size_t>(4) << 20;  // partials
+constexpr size_t kNoAllocCounterBytes = kNoAllocMaxSeqs * sizeof(int);
+constexpr size_t kNoAllocScratchBytes = kNoAllocCounterBytes + kNoAllocPartBytes;
+constexpr int kNoAllocMaxDevices = 64;
+
+// 4 MiB + 4 KiB, held by every GPU that loads this library until exit.  In
+// host code the name is only a host-side stand-in for the symbol: its
+// device address comes from cudaGetSymbolAddress, once per device.
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
+
+void* g_noalloc_addr[kNoAllocMaxDevices];
+std::mutex g_noalloc_mu;
+
+// Device address of g_noalloc_scratch on `device`, looked up on the first
+// call for that device with the device current.
+int noalloc_scratch(int device, uint8_t** addr) {
+  if (device < 0 || device >= kNoAllocMaxDevices) return PL_EDEVICE;
+  std::lock_guard<std::mutex> lk(g_noalloc_mu);
+  if (!g_noalloc_addr[device]) {
+    int cur = -1;
+    PL_CUDA(cudaGetDevice(&cur));
+    if (cur != device) PL_CUDA(cudaSetDevice(device));
+    void* p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (cur != device) cudaSetDevice(cur);
+    if (e != cudaSuccess || !p) {
+      std::fprintf(stderr, "pl_attn: cudaGetSymbolAddress(scratch) failed: %s\n",
+                   cudaGetErrorString(e));
+      return PL_ECUDA;
+    }
+    g_noalloc_addr[device] = p;
+  }
+  *addr = static_cast<uint8_t*>(g_noalloc_addr[device]);
+  return PL_OK;
+}
+
+template <int TP>
+int noalloc_launch_tp(const pl::DecodeArgs& a, int n, cudaStream_t st) {
+  const int smem = kDecodeStages * 2 * TP * g->n_kv_heads * 128 + 1024 + 2 * kDecodeStages * 8;
+  auto kern = pl::decode_kernel<TP, kDecodeStages>;
+  PL_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+  kern<<<dim3(a.n_split, n), dim3((g->n_kv_heads + 1) * 32), smem, st>>>(a, g->tm_k_dec,
+                                                                          g->tm_v_dec);
+  PL_CUDA(cudaGetLastError());
+  return PL_OK;
+}
+
+}  // namespace
+
+extern "C" int pl_attn_decode_batch_dev_noalloc(int layer, int n, const int* d_seqs,
+                                                const int* d_pos, int max_pos, const float* d_q,
+                                                const float* d_k, const float* d_v,
+                                                float* d_out, void* stream) {
+  if (!g) return PL_ESTATE;
+  if (n <= 0 || n > g->n_seqs || layer < 0 || layer >= g->n_layers || max_pos < 0 ||
+      max_pos >= g->max_seq)
+    return PL_EARG;
+  if (!d_seqs || !d_pos || !d_q || !d_k || !d_v || !d_out) return PL_EARG;
+  if (n > kNoAllocMaxSeqs) {
+    std::fprintf(stderr,
+                 "pl_attn_decode_batch_dev_noalloc: %d sequences exceed the fixed maximum of %d "
+                 "(its scratch is a static %zu-byte device array)\n",
+                 n, kNoAllocMaxSeqs, kNoAllocScratchBytes);
+    return PL_EARG;
+  }
+  uint8_t* scratch = nullptr;
+  int rc = noalloc_scratch(g->device, &scratch);
+  if (rc) return rc;
+  int* counters = reinterpret_cast<int*>(scratch);
+  float* part = reinterpret_cast<float*>(scratch + kNoAllocCounterBytes);
+  // as many splits as the decode heuristic wants, capped to what fits
+  int ns = n_split_for(n, max_pos + 1);
+  const size_t per_split = static_cast<size_t>(n) * g->n_heads * kPartStride * sizeof(float);
+  const int fit = static_cast<int>(kNoAllocPartBytes / per_split);
+  if (ns > fit) ns = fit > 1 ? fit : 1;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  // the array keeps the previous call's contents: the merge counters must
+  // start at zero
+  PL_CUDA(cudaMemsetAsync(counters, 0, sizeof(int) * n, st));
+  pl::DecodeArgs a;
+  a.n_layers = g->n_layers;
+  a.max_seq = g->max_seq;
+  a.n_heads = g->n_heads;
+  a.n_kv_heads = g->n_kv_heads;
+  a.kv_mul = g->kv_mul;
+  a.layer = layer;
+  a.n_slots = g->n_seqs;
+  a.rope_type = g->rope_type;
+  a.cos_tab = g->d_cos;
+  a.sin_tab = g->d_sin;
+  a.kc = g->d_k;
+  a.vc = g->d_v;
+  a.seqs = d_seqs;
+  a.pos = d_pos;
+  a.q = d_q;
+  a.k = d_k;
+  a.v = d_v;
+  a.out = d_out;
+  a.part = part;
+  a.part_out = nullptr;
+  a.counters = counters;
+  a.n_split = ns;
+  a.merge_in_kernel = ns <= pl::kMaxInKernelMerge ? 1 : 0;
+  a.mode = 0;
+  a.row0 = 0;
+  a.n_rows = 0;
+  a.append = 1;
+  a.score_scale = pl::kLog2e / sqrtf(static_cast<float>(kHD));
+  a.err = g->d_err;
+  switch (g->tp) {
+    case 16: rc = noalloc_launch_tp<16>(a, n, st); break;
+    case 32: rc = noalloc_launch_tp<32>(a, n, st); break;
+    case 64: rc = noalloc_launch_tp<64>(a, n, st); break;
+    case 128: rc = noalloc_launch_tp<128>(a, n, st); break;
+    default: return PL_EUNSUPPORTED;
+  }
+  if (rc) return rc;
+  if (!a.merge_in_kernel) {
+    pl::combine_kernel<<<dim3(g->n_heads, n), 64, 0, st>>>(ns, g->n_heads, part, d_out, nullptr);
+    PL_CUDA(cudaGetLastError());
+  }
+  return PL_OK;
+}
