@@ -144,19 +144,20 @@ int  pl_attn_prefill_dev(int seq, int layer, int start_pos, int n_tok,
  * [0, n_rows).  q is rotated by the RoPE of global position `pos`; if
  * `append` is nonzero, k is rotated too and k, v are appended at local row
  * pos - row0 (which must be < n_rows).  Attends local rows [0, n_rows) and
- * writes, per query head h, the partial triple
- *   d_part[h*(head_dim+2) + 0]        m_h: running max, log2 domain
- *   d_part[h*(head_dim+2) + 1]        l_h: sum of 2^(s - m_h)
- *   d_part[h*(head_dim+2) + 2 + d]    o_h[d]: unnormalised sum of p * V
- * with s = (q.k) * log2(e) / sqrt(head_dim).  Merge shards with
- * pl_attn_combine_dev. */
+ * writes, per query head h, the partial triple in a block of head_dim+4
+ * floats (16-byte aligned):
+ *   d_part[h*(head_dim+4) + 0]        m_h: running max, log2 domain
+ *   d_part[h*(head_dim+4) + 1]        l_h: sum of 2^(s - m_h)
+ *   d_part[h*(head_dim+4) + 4 + d]    o_h[d]: unnormalised sum of p * V
+ * with s = (q.k) * log2(e) / sqrt(head_dim).  An empty shard (n_rows = 0)
+ * writes m = -inf, l = 0, o = 0.  Merge shards with pl_attn_combine_dev. */
 int  pl_attn_decode_partial_dev(int seq, int layer, int pos, int row0,
                                 int n_rows, int append, const float *d_q,
                                 const float *d_k, const float *d_v,
                                 float *d_part, void *stream);
 
-/* Log-sum-exp merge of n_part partial blocks laid out back to back
- * (n_part * n_heads*(head_dim+2) floats) into out [n_heads*head_dim]:
+/* Log-sum-exp merge of n_part (1..16) partial blocks laid out back to back
+ * (n_part * n_heads*(head_dim+4) floats) into out [n_heads*head_dim]:
  *   M = max_g m_g, L = sum_g l_g 2^(m_g - M),
  *   out = sum_g 2^(m_g - M) o_g / L. */
 int  pl_attn_combine_dev(int n_part, const float *d_parts, float *d_out,
@@ -173,17 +174,19 @@ int  pl_attn_kv_ptr(int seq, int layer, uint16_t **d_k, uint16_t **d_v);
  * partials the first time a launch needs one; serving engines that reserve
  * the whole device in their own pool, or latency-critical loops where an
  * allocation's implicit device synchronisation would stall other streams,
- * cannot accept that.  This entry point runs the same kernel with its
- * scratch (split partials and merge counters) in one fixed file-scope device
- * array of 4 MiB + 4 KiB, which every GPU that loads the library holds until
- * the process exits; it calls no cudaMalloc, cudaFree or other allocating
- * routine.  Limits: n <= 1024 sequences (larger n fails with PL_EARG and a
- * message on stderr), and the KV split is capped so the partials fit in
- * 4 MiB.  The first call on a device looks up the array's device address
- * (cudaGetSymbolAddress); make that first call before any stream capture.
- * All calls share the one array, so calls that overlap on the GPU (e.g. on
- * two streams at once) race; the merge counters are cleared on the stream
- * at the start of every call. */
+ * cannot accept that.  This entry point runs the same kernels with their
+ * scratch (split partials and the per-sequence segment table) in one fixed
+ * file-scope device array of 4 MiB + 8 KiB, which every GPU that loads the
+ * library holds until the process exits; it calls no cudaMalloc, cudaFree
+ * or other allocating routine.  Limits: n <= 1024 sequences, and at most
+ * 4 MiB / (n_heads * 272 bytes) partial slots (one per CTA plus one per
+ * sequence: 481 for 32 query heads), so the KV split is capped to fit;
+ * larger n fails with PL_EARG and a message on stderr.  The first call on a
+ * device looks up the array's device address (cudaGetSymbolAddress); make
+ * that first call before any stream capture.  All calls share the one
+ * array, so calls that overlap on the GPU (e.g. on two streams at once)
+ * race; each call writes every scratch word it later reads, so nothing has
+ * to be cleared between calls. */
 int  pl_attn_decode_batch_dev_noalloc(int layer, int n, const int *d_seqs,
                                       const int *d_pos, int max_pos,
                                       const float *d_q, const float *d_k,

@@ -35,7 +35,7 @@ PL_EUNSUPPORTED = -8
 PL_ROPE_LLAMA = 0
 PL_ROPE_QWEN = 1
 HEAD_DIM = 64
-PART_STRIDE = HEAD_DIM + 2
+PART_STRIDE = HEAD_DIM + 4   # floats per partial: m, l, 2 pad, o[64]
 
 
 class PlAttnError(RuntimeError):

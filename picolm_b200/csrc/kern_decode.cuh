@@ -1,22 +1,29 @@
 // kern_decode.cuh -- fused decode step: RoPE(q, k) -> FP16 KV append ->
 // split-KV GQA attention (flash-decoding) -> split merge, for one or many
-// sequences in one launch.
+// sequences in ONE launch.
 //
-// Replaces picolm/model.c:820-892 (and its batched use).  One CTA handles
-// one sequence and one contiguous chunk of cache rows (a "split"):
+// Replaces picolm/model.c:820-892 (and its batched use).
 //
-//   warp Hk      (producer)  one lane streams K and V tiles of TP rows x all
-//                            KV heads into an NSTAGE-deep shared-memory ring
-//                            with 4-D TMA loads (128-byte swizzle), one
-//                            mbarrier pair per stage;
+// Work partition.  The cache rows to read form a flattened list of tiles
+// (TP rows x all KV heads each): sequence 0's tiles, then sequence 1's, ...
+// Every CTA computes the tile counts' prefix sum in shared memory and takes
+// an equal contiguous slice of that list, so all CTAs stream the same number
+// of bytes whatever the sequence lengths are.  A slice covers one or more
+// "segments" (the part of one sequence inside the slice); the TMA pipeline
+// runs on across segment boundaries.
+//
+// Inside a CTA:
+//   warp Hk      (producer)  one lane streams K and V tiles into an
+//                            NSTAGE-deep ring with 4-D TMA loads (128-byte
+//                            swizzle), one full/empty mbarrier pair a stage;
 //   warps 0..Hk-1 (consumers) warp w owns KV head w and its kv_mul query
 //                            heads.  Scores and P.V run on the tensor cores
 //                            (mma.sync m16n8k16, FP16 in / FP32 accumulate):
 //                            rows 0..7 of the A operand hold the high FP16
 //                            half of q (resp. p), rows 8..15 the residual
-//                            low half, so the FP16 operand costs no
-//                            precision (q ~ hi + lo to 2^-22).  Online
-//                            softmax in the log2 domain with quad shuffles.
+//                            low half, so the FP16 operand costs no precision
+//                            (q ~ hi + lo to 2^-22).  Online softmax in the
+//                            log2 domain with quad shuffles.
 //
 // Why tensor cores in a memory-bound kernel: with 8 query heads per KV head
 // each 256-byte K+V row feeds 2 x 8 x 64 multiply-adds, ~4.7 FP32-pipe
@@ -24,16 +31,20 @@
 // issue rate, so a CUDA-core dot product would cap the kernel below the HBM
 // roofline.  On the tensor pipe the same work costs a few percent.
 //
-// The row at `pos` is appended by the CTA whose chunk contains it: the warp
-// of each KV head rotates k (bit-exact picolm RoPE), encodes k and v with
+// The row at `pos` is appended by the segment that contains it: the warp of
+// each KV head rotates k (bit-exact picolm RoPE), encodes k and v with
 // picolm's FP16 rounding, stores them to HBM and patches them into the
 // shared-memory tile it reads (TMA may have fetched the row before the
 // store landed).
 //
-// Each split leaves a partial (m, l, o) in a scratch buffer.  With few
-// splits the last CTA of a sequence to finish merges them in the same
-// launch (a counter per sequence); with many splits (long single-sequence
-// contexts) a separate combine kernel with one CTA per head does it.
+// Merge.  A sequence covered by one segment is finished by that segment.
+// Otherwise each segment leaves a partial (m, l, o) in slot (cta + seq) of
+// a scratch buffer and CTA 0 records each sequence's (first slot, segment
+// count).  merge_kernel, launched right behind with programmatic dependent
+// launch (it is resident and waiting on griddepcontrol.wait when the decode
+// grid ends), merges them with 256 threads per 4 heads.  Merging inside the
+// decode grid instead puts a chain of L2 round trips at the end of the
+// slowest CTA; measured on B200 that tail cost 13 us of a 46 us step.
 #pragma once
 #include <cstdint>
 #include <cuda.h>
@@ -43,10 +54,16 @@
 
 namespace pl {
 
-constexpr int kHD = 64;               // head_dim supported by the kernels
-constexpr int kPartStride = kHD + 2;  // floats per (m, l, o[64]) partial
+constexpr int kHD = 64;                 // head_dim supported by the kernels
+constexpr int kPartStride = kHD + 4;    // floats per partial: m, l, 2 pad, o[64]
+constexpr int kPartO = 4;               // offset of o in a partial (16-byte aligned)
 constexpr float kLog2e = 1.4426950408889634f;
-constexpr int kMaxInKernelMerge = 32; // splits merged by the last CTA
+constexpr int kMaxLaunchSeqs = 1024;    // sequences per launch (prefix scan in smem)
+// merge_kernel shapes: HB heads per block x 16 float4 columns x LANES
+// segment lanes.  Many short merges: (4, 4) = 256 threads; few long merges
+// (a long single sequence split over every CTA): (2, 16) = 512 threads.
+constexpr int kMergeWideSegs = 32;      // use the wide shape above this many segments
+constexpr int kMaxCombineParts = 16;    // device partials merged by combine_kernel
 
 struct DecodeArgs {
   // cache geometry
@@ -55,18 +72,17 @@ struct DecodeArgs {
   const float* sin_tab;
   uint16_t* kc;          // [slots][n_layers][max_seq][kv_dim]
   uint16_t* vc;
-  // per-launch inputs, gridDim.y = number of sequences
+  // per-launch inputs
+  int n;                 // sequences in this launch (<= kMaxLaunchSeqs)
   const int* seqs;       // cache slot per sequence
   const int* pos;        // global position of the new token
   const float* q;        // [n][n_heads*64]   before RoPE
   const float* k;        // [n][kv_dim]       before RoPE
   const float* v;        // [n][kv_dim]
   float* out;            // [n][n_heads*64]   normalised output (mode 0)
-  float* part;           // [n][n_split][n_heads][66] per-split partials
-  float* part_out;       // mode 1: merged partial per sequence [n][n_heads][66]
-  int* counters;         // [n] finished-CTA counters, self-resetting
-  int n_split;
-  int merge_in_kernel;   // 1: last CTA per sequence merges; 0: combine kernel
+  float* part;           // [gridDim.x + n][n_heads][kPartStride] segment partials
+  float* part_out;       // mode 1: merged partial per sequence [n][n_heads][kPartStride]
+  int2* seg_info;        // [n] (first slot, segment count), written by CTA 0
   // mode 0: attend rows [0, pos], append at row pos.
   // mode 1: shard of a KV-split sequence: attend local rows [0, n_rows),
   //         append (if append) at local row pos - row0.
@@ -114,53 +130,129 @@ __device__ __forceinline__ uint32_t sw128(int r, int chunk) {
   return static_cast<uint32_t>(r * 128 + ((chunk ^ (r & 7)) << 4));
 }
 
-// Merge n_split partials of one sequence (part: [n_split][n_heads][66]).
-// Writes O/L to out, or the merged (M, L, O) to part_out.
-__device__ __forceinline__ void merge_partials(int n_split, int n_heads, const float* part,
-                                               float* out, float* part_out, int tid,
-                                               int nthreads) {
-  const size_t step = static_cast<size_t>(n_heads) * kPartStride;
-  for (int idx = tid; idx < n_heads * kHD; idx += nthreads) {
-    const int h = idx / kHD, d = idx % kHD;
-    const float* base = part + static_cast<size_t>(h) * kPartStride;
-    float M = -INFINITY;
-    for (int j = 0; j < n_split; ++j) M = fmaxf(M, __ldcg(base + j * step));
-    float L = 0.f, O = 0.f;
-    if (M != -INFINITY) {
-      for (int j = 0; j < n_split; ++j) {
-        const float* pj = base + j * step;
-        const float w = ex2(__ldcg(pj) - M);
-        L += w * __ldcg(pj + 1);
-        O += w * __ldcg(pj + 2 + d);
-      }
-    }
-    if (out) {
-      out[idx] = O / L;
-    } else {
-      float* dst = part_out + static_cast<size_t>(h) * kPartStride;
-      if (d == 0) {
-        dst[0] = M;
-        dst[1] = L;
-      }
-      dst[2 + d] = O;
-    }
+// ------------------------------------------------------------ partition
+struct Partition {
+  const int* prefix;  // [n+1] exclusive prefix sum of tile counts (shared memory)
+  long long T;        // total tiles
+  int G;              // CTAs that hold work (<= gridDim.x)
+  // CTA owning flattened tile x: the largest c with floor(c*T/G) <= x
+  __device__ __forceinline__ int cta_of(long long x) const {
+    return static_cast<int>(((x + 1) * G - 1) / T);
   }
+  __device__ __forceinline__ long long begin(int c) const { return c * T / G; }
+  __device__ __forceinline__ int n_seg(int i) const {
+    return cta_of(prefix[i + 1] - 1) - cta_of(prefix[i]) + 1;
+  }
+  // slot of sequence i's j-th segment (segments of i are CTAs cta_of(prefix[i]) + j)
+  __device__ __forceinline__ int slot(int i, int j) const { return cta_of(prefix[i]) + j + i; }
+};
+
+// Rows attended and the append row of sequence i.
+__device__ __forceinline__ void seq_rows(const DecodeArgs& a, int i, int& att_rows,
+                                         int& app_row) {
+  const int pos = a.pos[i];
+  att_rows = a.mode == 0 ? pos + 1 : a.n_rows;
+  app_row = a.mode == 0 ? pos : (a.append ? pos - a.row0 : -1);
 }
 
-// One consumer warp: KV head w of sequence i over tiles [t_begin, t_begin+ntiles).
+// -------------------------------------------------------------- merge
+// Log-sum-exp merge of `cnt` <= MAXC partials (slots src0 + j*slot_stride)
+// into either a normalised output out[n_heads*64] or a partial at dst
+// (which may be the first source slot).  Whole block.  The partials were
+// written by other CTAs moments ago, so the merge is bound by L2 latency,
+// not bandwidth: every thread issues all of its loads before using any.
+// smem_w >= 3 * MAXC * n_heads + 2 * n_heads floats.
+template <int MAXC>
+__device__ __forceinline__ void merge_slots(const float* src0, size_t slot_stride, int cnt,
+                                            int n_heads, float* out, float* dst, float* smem_w) {
+  const int tid = threadIdx.x, nthr = blockDim.x;
+  float* sm_m = smem_w;                  // [MAXC][n_heads]
+  float* sm_l = sm_m + MAXC * n_heads;   // [MAXC][n_heads]
+  float* sm_w = sm_l + MAXC * n_heads;   // [MAXC][n_heads] weights
+  float* sM = sm_w + MAXC * n_heads;     // [n_heads]
+  float* sL = sM + n_heads;              // [n_heads]
+  // (1) every (m, l) pair in one sweep
+  for (int t = tid; t < cnt * n_heads; t += nthr) {
+    const int j = t / n_heads, h = t - j * n_heads;
+    const float2 ml = __ldcg(reinterpret_cast<const float2*>(src0 + j * slot_stride +
+                                                             h * kPartStride));
+    sm_m[t] = ml.x;
+    sm_l[t] = ml.y;
+  }
+  __syncthreads();
+  // (2) per head: max, weights, sum
+  for (int h = tid; h < n_heads; h += nthr) {
+    float M = -INFINITY;
+    for (int j = 0; j < cnt; ++j) M = fmaxf(M, sm_m[j * n_heads + h]);
+    float L = 0.f;
+    for (int j = 0; j < cnt; ++j) {
+      const float w = M == -INFINITY ? 0.f : ex2(sm_m[j * n_heads + h] - M);
+      sm_w[j * n_heads + h] = w;
+      L += w * sm_l[j * n_heads + h];
+    }
+    sM[h] = M;
+    sL[h] = L;
+    if (out) {
+      const float inv = 1.0f / L;
+      for (int j = 0; j < cnt; ++j) sm_w[j * n_heads + h] *= inv;
+    }
+  }
+  __syncthreads();
+  // (3) the weighted sums, float4 at a time, all loads of an output issued together
+  for (int idx = tid; idx < n_heads * (kHD / 4); idx += nthr) {
+    const int h = idx / (kHD / 4), q4 = idx % (kHD / 4);
+    const float* base = src0 + h * kPartStride + kPartO + 4 * q4;
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int j0 = 0; j0 < cnt; j0 += 8) {  // 8 loads in flight per thread per round
+      float4 v[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j)
+        if (j0 + j < cnt) v[j] = __ldcg(reinterpret_cast<const float4*>(base + (j0 + j) * slot_stride));
+#pragma unroll
+      for (int j = 0; j < 8; ++j)
+        if (j0 + j < cnt) {
+          const float w = sm_w[(j0 + j) * n_heads + h];
+          acc.x += w * v[j].x;
+          acc.y += w * v[j].y;
+          acc.z += w * v[j].z;
+          acc.w += w * v[j].w;
+        }
+    }
+    if (out)
+      reinterpret_cast<float4*>(out + h * kHD)[q4] = acc;
+    else
+      reinterpret_cast<float4*>(dst + h * kPartStride + kPartO)[q4] = acc;
+  }
+  if (!out)
+    for (int h = tid; h < n_heads; h += nthr) {
+      dst[h * kPartStride] = sM[h];
+      dst[h * kPartStride + 1] = sL[h];
+    }
+  __syncthreads();
+}
+
+// ------------------------------------------------------------ consumer
+// KV head w of sequence i over local tiles [t_lo, t_hi); pipeline index of
+// tile t_lo is it0.  Writes the final result if the segment is the whole
+// sequence, else its partial to slot.
 template <int TP, int NSTAGE>
-__device__ __forceinline__ void decode_consumer(const DecodeArgs& a, int w, int lane, int i,
-                                                int split, int pos, int att_rows, int app_row,
-                                                int t_begin, int ntiles, int slab, bool appends,
-                                                const uint8_t* sK, const uint8_t* sV,
-                                                int tile_bytes, uint64_t* full, uint64_t* empty) {
+__device__ __forceinline__ void consume_segment(const DecodeArgs& a, int w, int lane, int i,
+                                                int t_lo, int t_hi, int it0, bool whole,
+                                                int slot, const uint8_t* sK, const uint8_t* sV,
+                                                int tile_bytes, uint64_t* full, uint64_t* empty,
+                                                bool& ok) {
   const int kv_dim = a.n_kv_heads * kHD;
   const int g = lane >> 2, c = lane & 3;
   const int kv_mul = a.kv_mul;
   const bool row_valid = g < kv_mul;
   const int qh = w * kv_mul + (row_valid ? g : 0);
+  const int pos = a.pos[i];
+  int att_rows, app_row;
+  seq_rows(a, i, att_rows, app_row);
+  const int slab = a.seqs[i] * a.n_layers + a.layer;
   const float* cs = a.cos_tab + static_cast<size_t>(pos) * (kHD / 2);
   const float* sn = a.sin_tab + static_cast<size_t>(pos) * (kHD / 2);
+  const bool appends = app_row >= t_lo * TP && app_row < t_hi * TP;
 
   // q fragments: this thread needs dims 16kk+2c, +1 and 16kk+8+2c, +1
   uint32_t qa[4][4];
@@ -203,15 +295,17 @@ __device__ __forceinline__ void decode_consumer(const DecodeArgs& a, int w, int 
 #pragma unroll
   for (int j = 0; j < 8; ++j) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.f;
 
-  for (int it = 0; it < ntiles; ++it) {
+  for (int t = t_lo; t < t_hi && ok; ++t) {
+    const int it = it0 + (t - t_lo);
     const int s = it % NSTAGE;
     if (!mbar_wait_bounded(&full[s], (it / NSTAGE) & 1)) {
       atomicOr(a.err, ERR_TIMEOUT_FULL);
+      ok = false;
       break;
     }
     const uint32_t kbase = smem_u32(sK + s * tile_bytes + w * TP * 128);
     const uint32_t vbase = smem_u32(sV + s * tile_bytes + w * TP * 128);
-    const int row0 = (t_begin + it) * TP;
+    const int row0 = t * TP;
     const bool patch = appends && app_row >= row0 && app_row < row0 + TP;
     if (patch) {
       const int r = app_row - row0;
@@ -242,9 +336,9 @@ __device__ __forceinline__ void decode_consumer(const DecodeArgs& a, int w, int 
     for (int nt = 0; nt < TP / 8; ++nt) {
 #pragma unroll
       for (int e = 0; e < 2; ++e) {
-        const int t = row0 + nt * 8 + 2 * c + e;
+        const int tr = row0 + nt * 8 + 2 * c + e;
         float sc = (sacc[nt][e] + sacc[nt][2 + e]) * a.score_scale;
-        sc = t < att_rows ? sc : -INFINITY;
+        sc = tr < att_rows ? sc : -INFINITY;
         sacc[nt][e] = sc;
         mt = fmaxf(mt, sc);
       }
@@ -290,7 +384,7 @@ __device__ __forceinline__ void decode_consumer(const DecodeArgs& a, int w, int 
   l_run += __shfl_xor_sync(0xffffffffu, l_run, 1);
   l_run += __shfl_xor_sync(0xffffffffu, l_run, 2);
   if (!row_valid) return;
-  if (a.n_split == 1 && a.mode == 0) {
+  if (whole && a.mode == 0) {
     const float inv = 1.0f / l_run;
     float* dst = a.out + (static_cast<size_t>(i) * a.n_heads + qh) * kHD;
 #pragma unroll
@@ -298,17 +392,17 @@ __device__ __forceinline__ void decode_consumer(const DecodeArgs& a, int w, int 
       *reinterpret_cast<float2*>(dst + 8 * j + 2 * c) =
           make_float2((o[j][0] + o[j][2]) * inv, (o[j][1] + o[j][3]) * inv);
   } else {
-    float* dst = a.part +
-                 ((static_cast<size_t>(i) * a.n_split + split) * a.n_heads + qh) * kPartStride;
+    float* dst = (whole ? a.part_out + static_cast<size_t>(i) * a.n_heads * kPartStride
+                        : a.part + static_cast<size_t>(slot) * a.n_heads * kPartStride) +
+                 qh * kPartStride;
     if (c == 0) {
       dst[0] = m_run;
       dst[1] = l_run;
     }
 #pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      dst[2 + 8 * j + 2 * c] = o[j][0] + o[j][2];
-      dst[3 + 8 * j + 2 * c] = o[j][1] + o[j][3];
-    }
+    for (int j = 0; j < 8; ++j)
+      *reinterpret_cast<float2*>(dst + kPartO + 8 * j + 2 * c) =
+          make_float2(o[j][0] + o[j][2], o[j][1] + o[j][3]);
   }
 }
 
@@ -317,7 +411,8 @@ __global__ void __launch_bounds__(288) decode_kernel(const DecodeArgs a,
                                                      const __grid_constant__ CUtensorMap tmk,
                                                      const __grid_constant__ CUtensorMap tmv) {
   extern __shared__ uint8_t smem_raw[];
-  __shared__ int s_last;
+  __shared__ int s_prefix[kMaxLaunchSeqs + 1];
+  __shared__ int s_warp_sum[9];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
   const int Hk = a.n_kv_heads;
@@ -326,30 +421,81 @@ __global__ void __launch_bounds__(288) decode_kernel(const DecodeArgs a,
   uint8_t* sV = smem + NSTAGE * tile_bytes;
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + 2 * NSTAGE * tile_bytes);
   uint64_t* empty = full + NSTAGE;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int nthr = blockDim.x, n = a.n;
+  // the merge grid may start (and wait on griddepcontrol.wait) right away
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int i = blockIdx.y;
-  const int split = blockIdx.x;
-  const int seq = a.seqs[i];
-  const int pos = a.pos[i];
-  const int att_rows = a.mode == 0 ? pos + 1 : a.n_rows;
-  const int app_row = a.mode == 0 ? pos : (a.append ? pos - a.row0 : -1);
-  const int ntiles_all = (att_rows + TP - 1) / TP;
-  const int chunk = (ntiles_all + a.n_split - 1) / a.n_split;
-  const int t_begin = split * chunk;
-  const int t_end = min(t_begin + chunk, ntiles_all);
-  const int ntiles = max(0, t_end - t_begin);
-  const int slab = seq * a.n_layers + a.layer;
-  const bool appends = app_row >= 0 && app_row >= t_begin * TP && app_row < t_end * TP;
-  // device-side argument check (device-pointer callers): the whole sequence
-  // is skipped -- every CTA of it returns here, so its merge counter stays 0
-  if (seq < 0 || seq >= a.n_slots || pos < 0 || pos >= a.max_seq || att_rows > a.max_seq ||
-      app_row >= a.max_seq) {
-    if (threadIdx.x == 0) atomicOr(a.err, ERR_BAD_ARG);
+  // ---- tile counts and their exclusive prefix sum (every CTA, identical)
+  {
+    const int per = (n + nthr - 1) / nthr;
+    const int i0 = tid * per;
+    int local = 0;
+    for (int i = i0; i < min(n, i0 + per); ++i) {
+      int att_rows, app_row;
+      seq_rows(a, i, att_rows, app_row);
+      const int seq = a.seqs[i], pos = a.pos[i];
+      const bool bad = seq < 0 || seq >= a.n_slots || pos < 0 || pos >= a.max_seq ||
+                       att_rows < 0 || att_rows > a.max_seq || app_row >= a.max_seq;
+      if (bad && blockIdx.x == 0) atomicOr(a.err, ERR_BAD_ARG);
+      const int tiles = bad ? 0 : (att_rows + TP - 1) / TP;
+      s_prefix[i] = tiles;  // counts first, scanned below
+      local += tiles;
+    }
+    // inclusive scan of the per-thread sums across the block
+    int incl = local;
+#pragma unroll
+    for (int d = 1; d < 32; d <<= 1) {
+      const int y = __shfl_up_sync(0xffffffffu, incl, d);
+      if (lane >= d) incl += y;
+    }
+    if (lane == 31) s_warp_sum[warp] = incl;
+    __syncthreads();
+    if (tid == 0) {
+      int acc = 0;
+      for (int w = 0; w < nthr / 32; ++w) {
+        const int t = s_warp_sum[w];
+        s_warp_sum[w] = acc;
+        acc += t;
+      }
+      s_prefix[n] = acc;
+    }
+    __syncthreads();
+    int run = s_warp_sum[warp] + incl - local;  // exclusive prefix of this thread
+    for (int i = i0; i < min(n, i0 + per); ++i) {
+      const int t = s_prefix[i];
+      s_prefix[i] = run;
+      run += t;
+    }
+    __syncthreads();
+  }
+  const long long T = s_prefix[n];
+  if (T == 0) {  // no rows anywhere: nothing to merge either
+    if (blockIdx.x == 0)
+      for (int i = tid; i < n; i += nthr) a.seg_info[i] = make_int2(0, 0);
     return;
   }
+  const long long grid_ctas = static_cast<long long>(gridDim.x);
+  Partition P{s_prefix, T, static_cast<int>(grid_ctas < T ? grid_ctas : T)};
+  const int cta = blockIdx.x;
+  if (cta == 0)
+    for (int i = tid; i < n; i += nthr)
+      a.seg_info[i] = s_prefix[i + 1] > s_prefix[i]
+                          ? make_int2(P.slot(i, 0), P.n_seg(i)) : make_int2(0, 0);
+  if (cta >= P.G) return;
+  const long long x0 = P.begin(cta), x1 = P.begin(cta + 1);
+  // first sequence with tiles in [x0, x1)
+  int i_first = 0;
+  {
+    int lo = 0, hi = n - 1;
+    while (lo < hi) {  // smallest i with prefix[i+1] > x0
+      const int mid = (lo + hi) >> 1;
+      if (s_prefix[mid + 1] > x0) hi = mid; else lo = mid + 1;
+    }
+    i_first = lo;
+  }
 
-  if (threadIdx.x == 0) {
+  if (tid == 0) {
     for (int s = 0; s < NSTAGE; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], Hk);
@@ -358,81 +504,159 @@ __global__ void __launch_bounds__(288) decode_kernel(const DecodeArgs a,
   }
   __syncthreads();
 
+  bool ok = true;
   if (warp == Hk) {
     // ------------------------------------------------------------ producer
-    if (lane == 0 && ntiles > 0) {
+    if (lane == 0) {
       tma_prefetch_desc(&tmk);
       tma_prefetch_desc(&tmv);
-      int issued = 0;
-      for (int it = 0; it < ntiles; ++it) {
+      int i = i_first;
+      long long issued = 0;
+      for (long long x = x0; x < x1; ++x) {
+        while (s_prefix[i + 1] <= x) ++i;
+        const int it = static_cast<int>(x - x0);
         const int s = it % NSTAGE;
         if (it >= NSTAGE && !mbar_wait_bounded(&empty[s], ((it / NSTAGE) - 1) & 1)) {
           atomicOr(a.err, ERR_TIMEOUT_EMPTY);
           break;
         }
         mbar_arrive_expect_tx(&full[s], 2u * tile_bytes);
-        const int row = (t_begin + it) * TP;
+        const int row = static_cast<int>(x - s_prefix[i]) * TP;
+        const int slab = a.seqs[i] * a.n_layers + a.layer;
         tma_load_4d(sK + s * tile_bytes, &tmk, &full[s], 0, row, 0, slab);
         tma_load_4d(sV + s * tile_bytes, &tmv, &full[s], 0, row, 0, slab);
         ++issued;
       }
       // never leave with copies in flight: the last use of each stage must land
-      for (int j = issued - NSTAGE; j < issued; ++j)
-        if (j >= 0) mbar_wait_bounded(&full[j % NSTAGE], (j / NSTAGE) & 1);
+      for (long long j = issued - NSTAGE; j < issued; ++j)
+        if (j >= 0) mbar_wait_bounded(&full[j % NSTAGE], static_cast<uint32_t>((j / NSTAGE) & 1));
     }
   } else {
-    decode_consumer<TP, NSTAGE>(a, warp, lane, i, split, pos, att_rows, app_row, t_begin,
-                                ntiles, slab, appends, sK, sV, tile_bytes, full, empty);
+    // ------------------------------------------------------------ consumers
+    for (int i = i_first; i < n && s_prefix[i] < x1 && ok; ++i) {
+      const long long p0 = s_prefix[i], p1 = s_prefix[i + 1];
+      const long long a0 = x0 > p0 ? x0 : p0, a1 = x1 < p1 ? x1 : p1;
+      if (a1 <= a0) continue;
+      const int t_lo = static_cast<int>(a0 - s_prefix[i]), t_hi = static_cast<int>(a1 - s_prefix[i]);
+      const int ns = P.n_seg(i);
+      const int j = cta - P.cta_of(s_prefix[i]);
+      consume_segment<TP, NSTAGE>(a, warp, lane, i, t_lo, t_hi, static_cast<int>(a0 - x0),
+                                  ns == 1, P.slot(i, j), sK, sV, tile_bytes, full, empty, ok);
+    }
   }
-  if ((a.n_split == 1 && a.mode == 0) || !a.merge_in_kernel) return;
 
-  // -------------------------------------------------- in-kernel split merge
-  __threadfence();  // this thread's partial writes, device-wide
-  __syncthreads();
-  if (threadIdx.x == 0) s_last = atomicAdd(&a.counters[i], 1) == a.n_split - 1;
-  __syncthreads();
-  if (!s_last) return;
-  __threadfence();
-  const size_t per_seq = static_cast<size_t>(a.n_heads) * kPartStride;
-  merge_partials(a.n_split, a.n_heads, a.part + static_cast<size_t>(i) * a.n_split * per_seq,
-                 a.mode == 0 ? a.out + static_cast<size_t>(i) * a.n_heads * kHD : nullptr,
-                 a.mode == 0 ? nullptr : a.part_out + static_cast<size_t>(i) * per_seq,
-                 threadIdx.x, blockDim.x);
-  if (threadIdx.x == 0) a.counters[i] = 0;
 }
 
-// Separate log-sum-exp merge for many splits (and for partials gathered
-// from several devices): grid = (n_heads, n), block = 64 (one per dim).
-// part [n][n_split][n_heads][66]; writes out [n][n_heads*64] or, if out is
-// null, the merged partial to part_out [n][n_heads][66].
-__global__ void __launch_bounds__(64) combine_kernel(int n_split, int n_heads,
-                                                     const float* __restrict__ part,
-                                                     float* __restrict__ out,
-                                                     float* __restrict__ part_out) {
-  const int h = blockIdx.x, i = blockIdx.y, d = threadIdx.x;
-  const float* base = part + (static_cast<size_t>(i) * n_split * n_heads + h) * kPartStride;
-  const size_t step = static_cast<size_t>(n_heads) * kPartStride;
-  float M = -INFINITY;
-  for (int j = 0; j < n_split; ++j) M = fmaxf(M, __ldcg(base + j * step));
-  float L = 0.f, O = 0.f;
-  if (M != -INFINITY) {
-    for (int j = 0; j < n_split; ++j) {
-      const float* pj = base + j * step;
-      const float w = ex2(__ldcg(pj) - M);
-      L += w * __ldcg(pj + 1);
-      O += w * __ldcg(pj + 2 + d);
+// Merge of the segment partials of one decode launch.  grid = (n,
+// ceil(n_heads / HB)), block = HB * 16 * LANES threads, dynamic shared
+// memory 3 * max_segments * HB floats + one float4 per thread.  Launched
+// with programmatic stream serialisation behind decode_kernel: it waits on
+// griddepcontrol.wait until the decode grid has finished and its writes are
+// visible.  Thread (lane j, head hh, float4 q4) sums segments j, j+LANES,
+// ...; the lanes are reduced through shared memory.
+template <int kMergeHeads, int kMergeLanes>
+__global__ void __launch_bounds__(kMergeHeads * (kHD / 4) * kMergeLanes)
+    merge_kernel(const DecodeArgs a) {
+  constexpr int kMergeThreads = kMergeHeads * (kHD / 4) * kMergeLanes;
+  extern __shared__ float4 smem4[];
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  const int i = blockIdx.x, h0 = blockIdx.y * kMergeHeads, tid = threadIdx.x;
+  const int2 si = a.seg_info[i];
+  const int ns = si.y;
+  if (ns <= 1) return;  // finished by its single segment (or no rows)
+  const size_t slot_stride = static_cast<size_t>(a.n_heads) * kPartStride;
+  const float* src0 = a.part + static_cast<size_t>(si.x) * slot_stride;
+  float4* s_acc = smem4;                                    // [kMergeThreads]
+  float* s_m = reinterpret_cast<float*>(smem4 + kMergeThreads);  // [ns][kMergeHeads]
+  float* s_l = s_m + ns * kMergeHeads;
+  float* s_w = s_l + ns * kMergeHeads;
+  __shared__ float sM[kMergeHeads], sL[kMergeHeads];
+  for (int t = tid; t < ns * kMergeHeads; t += kMergeThreads) {
+    const int j = t / kMergeHeads, hh = t - j * kMergeHeads;
+    float2 ml = make_float2(-INFINITY, 0.f);
+    if (h0 + hh < a.n_heads)
+      ml = __ldcg(reinterpret_cast<const float2*>(src0 + j * slot_stride +
+                                                  (h0 + hh) * kPartStride));
+    s_m[t] = ml.x;
+    s_l[t] = ml.y;
+  }
+  __syncthreads();
+  if (tid < kMergeHeads) {
+    float M = -INFINITY;
+    for (int j = 0; j < ns; ++j) M = fmaxf(M, s_m[j * kMergeHeads + tid]);
+    float L = 0.f;
+    for (int j = 0; j < ns; ++j) {
+      const float w = M == -INFINITY ? 0.f : ex2(s_m[j * kMergeHeads + tid] - M);
+      s_w[j * kMergeHeads + tid] = w;
+      L += w * s_l[j * kMergeHeads + tid];
+    }
+    sM[tid] = M;
+    sL[tid] = L;
+    if (a.mode == 0) {
+      const float inv = 1.0f / L;
+      for (int j = 0; j < ns; ++j) s_w[j * kMergeHeads + tid] *= inv;
     }
   }
-  if (out) {
-    out[(static_cast<size_t>(i) * n_heads + h) * kHD + d] = O / L;
-  } else {
-    float* dst = part_out + (static_cast<size_t>(i) * n_heads + h) * kPartStride;
-    if (d == 0) {
-      dst[0] = M;
-      dst[1] = L;
+  __syncthreads();
+  const int pair = tid % (kMergeHeads * (kHD / 4)), lane_j = tid / (kMergeHeads * (kHD / 4));
+  const int hh = pair / (kHD / 4), q4 = pair % (kHD / 4);
+  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+  if (h0 + hh < a.n_heads) {
+    const float* base = src0 + (h0 + hh) * kPartStride + kPartO + 4 * q4;
+    for (int j0 = lane_j; j0 < ns; j0 += 8 * kMergeLanes) {  // 8 loads in flight
+      float4 v[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const int j = j0 + u * kMergeLanes;
+        if (j < ns) v[u] = __ldcg(reinterpret_cast<const float4*>(base + j * slot_stride));
+      }
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const int j = j0 + u * kMergeLanes;
+        if (j < ns) {
+          const float w = s_w[j * kMergeHeads + hh];
+          acc.x += w * v[u].x;
+          acc.y += w * v[u].y;
+          acc.z += w * v[u].z;
+          acc.w += w * v[u].w;
+        }
+      }
     }
-    dst[2 + d] = O;
   }
+  s_acc[tid] = acc;
+  __syncthreads();
+  if (lane_j == 0 && h0 + hh < a.n_heads) {
+#pragma unroll
+    for (int l = 1; l < kMergeLanes; ++l) {
+      const float4 o = s_acc[tid + l * kMergeHeads * (kHD / 4)];
+      acc.x += o.x;
+      acc.y += o.y;
+      acc.z += o.z;
+      acc.w += o.w;
+    }
+    if (a.mode == 0) {
+      reinterpret_cast<float4*>(a.out + (static_cast<size_t>(i) * a.n_heads + h0 + hh) * kHD)[q4] =
+          acc;
+    } else {
+      float* dst = a.part_out + (static_cast<size_t>(i) * a.n_heads + h0 + hh) * kPartStride;
+      reinterpret_cast<float4*>(dst + kPartO)[q4] = acc;
+      if (q4 == 0) {
+        dst[0] = sM[hh];
+        dst[1] = sL[hh];
+      }
+    }
+  }
+}
+
+// Log-sum-exp merge of partials gathered from several devices (one
+// sequence): n_part <= kMaxCombineParts blocks of [n_heads][kPartStride]
+// back to back.  grid = 1, block = 256.
+__global__ void __launch_bounds__(256) combine_kernel(int n_part, int n_heads,
+                                                      const float* __restrict__ parts,
+                                                      float* __restrict__ out) {
+  extern __shared__ float smem_w[];
+  merge_slots<kMaxCombineParts>(parts, static_cast<size_t>(n_heads) * kPartStride, n_part, n_heads,
+                                out, nullptr, smem_w);
 }
 
 }  // namespace pl

@@ -51,7 +51,7 @@ struct Ctx {
   // split-KV partials
   float* d_part = nullptr;
   size_t part_cap = 0;        // floats
-  int* d_counters = nullptr;  // [n_seqs] per-sequence split counters (self-resetting)
+  int2* d_seg_info = nullptr; // [kMaxLaunchSeqs] (first slot, segments) per decode sequence
   // prefill FP16 q staging
   uint16_t* d_q16 = nullptr;
   size_t q16_cap = 0;         // elements
@@ -204,46 +204,20 @@ int check_err_word(uint32_t w) {
   return PL_OK;
 }
 
-int n_split_for(int n, int max_rows) {
-  const int tiles = (max_rows + g->tp - 1) / g->tp;
-  int ns = g->decode_slots / (n > 0 ? n : 1);
-  if (ns < 1) ns = 1;
-  if (ns > tiles) ns = tiles;
-  if (ns > 1024) ns = 1024;
-  return ns;
+// Grid of the decode kernel: one CTA per resident slot, but never more CTAs
+// than tiles (max_rows bounds every sequence's rows).
+int decode_grid(int n, int max_rows) {
+  const long long tiles = static_cast<long long>(n) * ((max_rows + g->tp - 1) / g->tp);
+  long long G = g->decode_slots;
+  if (G > tiles) G = tiles;
+  return G < 1 ? 1 : static_cast<int>(G);
 }
 
-template <int TP>
-int launch_decode_tp(const pl::DecodeArgs& a, int n, cudaStream_t st) {
-  const int smem = kDecodeStages * 2 * TP * g->n_kv_heads * 128 + 1024 + 2 * kDecodeStages * 8;
-  auto kern = pl::decode_kernel<TP, kDecodeStages>;
-  static bool attr_done = false;
-  if (!attr_done) {
-    PL_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-    attr_done = true;
-  }
-  dim3 grid(a.n_split, n);
-  dim3 block((g->n_kv_heads + 1) * 32);
-  prof_begin(st);
-  kern<<<grid, block, smem, st>>>(a, g->tm_k_dec, g->tm_v_dec);
-  PL_CUDA(cudaGetLastError());
-  prof_end(st);
-  count_launch();
-  return PL_OK;
-}
-
-// Launch the fused decode (+ combine when split).  All pointers are device
-// pointers.  mode/row0/n_rows/append as in DecodeArgs.  If part_out is not
-// null the merged partials are written there instead of out.
-int launch_decode(int layer, int n, const int* d_seqs, const int* d_pos, int max_rows,
-                  const float* d_q, const float* d_k, const float* d_v, float* d_out,
-                  int mode, int row0, int n_rows, int append, float* part_out,
-                  cudaStream_t st) {
-  int ns = n_split_for(n, max_rows);
-  if (mode == 1 && ns < 1) ns = 1;
-  const size_t need = static_cast<size_t>(n) * ns * g->n_heads * kPartStride;
-  int rc = ensure_part(need);
-  if (rc) return rc;
+// Decode arguments shared by every launch path.
+pl::DecodeArgs decode_args(int layer, int n, const int* d_seqs, const int* d_pos,
+                           const float* d_q, const float* d_k, const float* d_v, float* d_out,
+                           int mode, int row0, int n_rows, int append, float* part_out,
+                           float* part, int2* seg_info) {
   pl::DecodeArgs a;
   a.n_layers = g->n_layers;
   a.max_seq = g->max_seq;
@@ -257,36 +231,132 @@ int launch_decode(int layer, int n, const int* d_seqs, const int* d_pos, int max
   a.sin_tab = g->d_sin;
   a.kc = g->d_k;
   a.vc = g->d_v;
+  a.n = n;
   a.seqs = d_seqs;
   a.pos = d_pos;
   a.q = d_q;
   a.k = d_k;
   a.v = d_v;
   a.out = d_out;
-  a.part = g->d_part;
+  a.part = part;
   a.part_out = part_out;
-  a.counters = g->d_counters;
-  a.n_split = ns;
-  a.merge_in_kernel = ns <= pl::kMaxInKernelMerge ? 1 : 0;
+  a.seg_info = seg_info;
   a.mode = mode;
   a.row0 = row0;
   a.n_rows = n_rows;
   a.append = append;
   a.score_scale = pl::kLog2e / sqrtf(static_cast<float>(kHD));
   a.err = g->d_err;
+  return a;
+}
+
+int decode_smem_bytes(int tp) {
+  return kDecodeStages * 2 * tp * g->n_kv_heads * 128 + 1024 + 2 * kDecodeStages * 8;
+}
+
+template <int TP>
+cudaError_t decode_occupancy(int* per_sm, int threads, int smem) {
+  auto kern = pl::decode_kernel<TP, kDecodeStages>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  if (e != cudaSuccess) return e;
+  return cudaOccupancyMaxActiveBlocksPerMultiprocessor(per_sm, kern, threads, smem);
+}
+
+template <int TP>
+int launch_decode_tp(const pl::DecodeArgs& a, int grid, cudaStream_t st, bool profile) {
+  const int smem = decode_smem_bytes(TP);
+  auto kern = pl::decode_kernel<TP, kDecodeStages>;
+  static bool attr_done = false;
+  if (!attr_done) {
+    PL_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    attr_done = true;
+  }
+  if (profile) prof_begin(st);
+  kern<<<grid, (g->n_kv_heads + 1) * 32, smem, st>>>(a, g->tm_k_dec, g->tm_v_dec);
+  PL_CUDA(cudaGetLastError());
+  if (profile) {
+    prof_end(st);
+    count_launch();
+  }
+  return PL_OK;
+}
+
+// The split merge, queued behind the decode grid with programmatic stream
+// serialisation: its CTAs become resident while the decode grid runs and
+// wait on griddepcontrol.wait (grid = sequences x head groups).
+template <int HB, int LANES>
+int launch_merge_shape(const pl::DecodeArgs& a, int decode_grid_ctas, cudaStream_t st,
+                       bool profile) {
+  auto kern = pl::merge_kernel<HB, LANES>;
+  const int threads = HB * (kHD / 4) * LANES;
+  const size_t smem = threads * sizeof(float4) +
+                      static_cast<size_t>(3) * decode_grid_ctas * HB * sizeof(float);
+  static size_t smem_attr = 0;
+  if (smem > 48 * 1024 && smem > smem_attr) {
+    PL_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 static_cast<int>(smem)));
+    smem_attr = smem;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(a.n, (g->n_heads + HB - 1) / HB);
+  cfg.blockDim = dim3(threads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  PL_CUDA(cudaLaunchKernelEx(&cfg, kern, a));
+  if (profile) count_launch();
+  return PL_OK;
+}
+
+// The split merge, queued behind the decode grid with programmatic stream
+// serialisation: its CTAs become resident while the decode grid runs and
+// wait on griddepcontrol.wait (grid = sequences x head groups).
+int launch_merge(const pl::DecodeArgs& a, int decode_grid_ctas, cudaStream_t st, bool profile) {
+  if (decode_grid_ctas <= 1) return PL_OK;  // one CTA: every sequence is one segment
+  // segments per sequence are at most about grid / n + 2
+  if (decode_grid_ctas / a.n + 2 > pl::kMergeWideSegs)
+    return launch_merge_shape<2, 16>(a, decode_grid_ctas, st, profile);
+  return launch_merge_shape<4, 4>(a, decode_grid_ctas, st, profile);
+}
+
+int launch_decode_kernel(const pl::DecodeArgs& a, int grid, cudaStream_t st, bool profile) {
+  int rc;
   switch (g->tp) {
-    case 16: rc = launch_decode_tp<16>(a, n, st); break;
-    case 32: rc = launch_decode_tp<32>(a, n, st); break;
-    case 64: rc = launch_decode_tp<64>(a, n, st); break;
-    case 128: rc = launch_decode_tp<128>(a, n, st); break;
+    case 16: rc = launch_decode_tp<16>(a, grid, st, profile); break;
+    case 32: rc = launch_decode_tp<32>(a, grid, st, profile); break;
+    case 64: rc = launch_decode_tp<64>(a, grid, st, profile); break;
+    case 128: rc = launch_decode_tp<128>(a, grid, st, profile); break;
     default: return PL_EUNSUPPORTED;
   }
   if (rc) return rc;
-  if (!a.merge_in_kernel) {
-    pl::combine_kernel<<<dim3(g->n_heads, n), 64, 0, st>>>(ns, g->n_heads, g->d_part,
-                                                           mode == 1 ? nullptr : d_out, part_out);
-    PL_CUDA(cudaGetLastError());
-    count_launch();
+  return launch_merge(a, grid, st, profile);
+}
+
+// Launch the fused decode for n sequences (chunks of kMaxLaunchSeqs).  All
+// pointers are device pointers; mode/row0/n_rows/append as in DecodeArgs.
+// In mode 1 the merged partials go to part_out instead of out.
+int launch_decode(int layer, int n, const int* d_seqs, const int* d_pos, int max_rows,
+                  const float* d_q, const float* d_k, const float* d_v, float* d_out,
+                  int mode, int row0, int n_rows, int append, float* part_out,
+                  cudaStream_t st) {
+  for (int s0 = 0; s0 < n; s0 += pl::kMaxLaunchSeqs) {
+    const int m = n - s0 < pl::kMaxLaunchSeqs ? n - s0 : pl::kMaxLaunchSeqs;
+    const int grid = decode_grid(m, max_rows);
+    const size_t need = static_cast<size_t>(grid + m) * g->n_heads * kPartStride;
+    int rc = ensure_part(need);
+    if (rc) return rc;
+    const pl::DecodeArgs a = decode_args(
+        layer, m, d_seqs + s0, d_pos + s0, d_q + static_cast<size_t>(s0) * g->q_dim,
+        d_k + static_cast<size_t>(s0) * g->kv_dim, d_v + static_cast<size_t>(s0) * g->kv_dim,
+        d_out ? d_out + static_cast<size_t>(s0) * g->q_dim : nullptr, mode, row0, n_rows, append,
+        part_out ? part_out + static_cast<size_t>(s0) * g->n_heads * kPartStride : nullptr,
+        g->d_part, g->d_seg_info);
+    rc = launch_decode_kernel(a, grid, st, true);
+    if (rc) return rc;
   }
   return PL_OK;
 }
@@ -331,7 +401,7 @@ void free_ctx(Ctx* c) {
   cudaFree(c->d_stage);
   cudaFreeHost(c->h_stage);
   cudaFree(c->d_part);
-  cudaFree(c->d_counters);
+  cudaFree(c->d_seg_info);
   cudaFree(c->d_q16);
   cudaFree(c->d_err);
   for (cudaEvent_t e : c->ev_pool) cudaEventDestroy(e);
@@ -415,14 +485,14 @@ int pl_attn_init(int n_layers, int n_heads, int n_kv_heads, int head_dim, int ma
       cudaMalloc(&c->d_cos, sizeof(float) * max_seq_len * (kHD / 2)) != cudaSuccess ||
       cudaMalloc(&c->d_sin, sizeof(float) * max_seq_len * (kHD / 2)) != cudaSuccess ||
       cudaMalloc(&c->d_err, 256) != cudaSuccess ||
-      cudaMalloc(&c->d_counters, sizeof(int) * (n_seqs + 1)) != cudaSuccess) {
+      cudaMalloc(&c->d_seg_info, sizeof(int2) * pl::kMaxLaunchSeqs) != cudaSuccess) {
     free_ctx(c);
     return PL_ENOMEM;
   }
   cudaMemsetAsync(c->d_k, 0, cache_elems * 2, c->stream);
   cudaMemsetAsync(c->d_v, 0, cache_elems * 2, c->stream);
   cudaMemsetAsync(c->d_err, 0, 256, c->stream);
-  cudaMemsetAsync(c->d_counters, 0, sizeof(int) * (n_seqs + 1), c->stream);
+  cudaMemsetAsync(c->d_seg_info, 0, sizeof(int2) * pl::kMaxLaunchSeqs, c->stream);
   {
     const size_t n = static_cast<size_t>(max_seq_len) * (kHD / 2);
     float* hc = static_cast<float*>(std::malloc(n * sizeof(float)));
@@ -451,11 +521,26 @@ int pl_attn_init(int n_layers, int n_heads, int n_kv_heads, int head_dim, int ma
     free_ctx(c);
     return rc;
   }
-  // decode occupancy: concurrent CTAs the split heuristic aims to fill
+  // decode grid: as many CTAs as can be resident at once (registers, shared
+  // memory), so the balanced partition runs in a single wave
+  g = c;
   {
-    const int smem = kDecodeStages * 2 * 128 * 128 + 1024 + 2 * kDecodeStages * 8;
-    const int per_sm = (227 * 1024) / smem;
-    c->decode_slots = c->num_sms * (per_sm > 0 ? per_sm : 1);
+    int per_sm = 0;
+    const int smem = decode_smem_bytes(c->tp);
+    const int threads = (n_kv_heads + 1) * 32;
+    cudaError_t e = cudaSuccess;
+    switch (c->tp) {
+      case 16: e = decode_occupancy<16>(&per_sm, threads, smem); break;
+      case 32: e = decode_occupancy<32>(&per_sm, threads, smem); break;
+      case 64: e = decode_occupancy<64>(&per_sm, threads, smem); break;
+      default: e = decode_occupancy<128>(&per_sm, threads, smem); break;
+    }
+    g = nullptr;
+    if (e != cudaSuccess || per_sm < 1) {
+      free_ctx(c);
+      return PL_ECUDA;
+    }
+    c->decode_slots = c->num_sms * per_sm;
   }
   if (cudaStreamSynchronize(c->stream) != cudaSuccess) {
     free_ctx(c);
@@ -561,17 +646,25 @@ int pl_attn_decode_partial_dev(int seq, int layer, int pos, int row0, int n_rows
   const int hv[2] = {seq, pos};
   cudaStream_t st = pick_stream(stream);
   PL_CUDA(cudaMemcpyAsync(d_ints, hv, sizeof hv, cudaMemcpyHostToDevice, st));
-  return launch_decode(layer, 1, d_ints, d_ints + 1, n_rows > 0 ? n_rows : 1, d_q,
-                       d_k ? d_k : d_q, d_v ? d_v : d_q, nullptr, 1, row0, n_rows,
-                       append ? 1 : 0, d_part, st);
+  if (n_rows == 0) {
+    // an empty shard contributes nothing: m = -inf, l = 0, o = 0
+    std::vector<float> empty(static_cast<size_t>(g->n_heads) * kPartStride, 0.f);
+    for (int h = 0; h < g->n_heads; ++h) empty[static_cast<size_t>(h) * kPartStride] = -INFINITY;
+    PL_CUDA(cudaMemcpyAsync(d_part, empty.data(), empty.size() * sizeof(float),
+                            cudaMemcpyHostToDevice, st));
+    return PL_OK;
+  }
+  return launch_decode(layer, 1, d_ints, d_ints + 1, n_rows, d_q, d_k ? d_k : d_q,
+                       d_v ? d_v : d_q, nullptr, 1, row0, n_rows, append ? 1 : 0, d_part, st);
 }
 
 int pl_attn_combine_dev(int n_part, const float* d_parts, float* d_out, void* stream) {
   if (!g) return PL_ESTATE;
   if (n_part <= 0 || !d_parts || !d_out) return PL_EARG;
+  if (n_part > pl::kMaxCombineParts) return PL_EARG;
   cudaStream_t st = pick_stream(stream);
-  pl::combine_kernel<<<dim3(g->n_heads, 1), 64, 0, st>>>(n_part, g->n_heads, d_parts, d_out,
-                                                         nullptr);
+  const size_t smem = static_cast<size_t>(3 * pl::kMaxCombineParts + 2) * g->n_heads * sizeof(float);
+  pl::combine_kernel<<<1, 256, smem, st>>>(n_part, g->n_heads, d_parts, d_out);
   PL_CUDA(cudaGetLastError());
   count_launch();
   return PL_OK;
@@ -768,13 +861,13 @@ int pl_attn_profile_read(double* attn_ms, long* attn_launches, long* all_launche
 // =====================================================================
 namespace {
 
-constexpr int kNoAllocMaxSeqs = 1024;                       // merge counters
-constexpr size_t kNoAllocPartBytes = static_cast<size_t>(4) << 20;  // partials
-constexpr size_t kNoAllocCounterBytes = kNoAllocMaxSeqs * sizeof(int);
-constexpr size_t kNoAllocScratchBytes = kNoAllocCounterBytes + kNoAllocPartBytes;
+constexpr int kNoAllocMaxSeqs = pl::kMaxLaunchSeqs;                 // per call
+constexpr size_t kNoAllocInfoBytes = static_cast<size_t>(kNoAllocMaxSeqs) * sizeof(int2);  // 8 KiB
+constexpr size_t kNoAllocPartBytes = static_cast<size_t>(4) << 20;  // 4 MiB of partials
+constexpr size_t kNoAllocScratchBytes = kNoAllocInfoBytes + kNoAllocPartBytes;
 constexpr int kNoAllocMaxDevices = 64;
 
-// 4 MiB + 4 KiB, held by every GPU that loads this library until exit.  In
+// 4 MiB + 8 KiB, held by every GPU that loads this library until exit.  In
 // host code the name is only a host-side stand-in for the symbol: its
 // device address comes from cudaGetSymbolAddress, once per device.
 static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
@@ -805,17 +898,6 @@ int noalloc_scratch(int device, uint8_t** addr) {
   return PL_OK;
 }
 
-template <int TP>
-int noalloc_launch_tp(const pl::DecodeArgs& a, int n, cudaStream_t st) {
-  const int smem = kDecodeStages * 2 * TP * g->n_kv_heads * 128 + 1024 + 2 * kDecodeStages * 8;
-  auto kern = pl::decode_kernel<TP, kDecodeStages>;
-  PL_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-  kern<<<dim3(a.n_split, n), dim3((g->n_kv_heads + 1) * 32), smem, st>>>(a, g->tm_k_dec,
-                                                                          g->tm_v_dec);
-  PL_CUDA(cudaGetLastError());
-  return PL_OK;
-}
-
 }  // namespace
 
 extern "C" int pl_attn_decode_batch_dev_noalloc(int layer, int n, const int* d_seqs,
@@ -827,68 +909,30 @@ extern "C" int pl_attn_decode_batch_dev_noalloc(int layer, int n, const int* d_s
       max_pos >= g->max_seq)
     return PL_EARG;
   if (!d_seqs || !d_pos || !d_q || !d_k || !d_v || !d_out) return PL_EARG;
-  if (n > kNoAllocMaxSeqs) {
+  // partial slots needed: one per CTA plus one per sequence
+  const size_t slot_bytes = static_cast<size_t>(g->n_heads) * kPartStride * sizeof(float);
+  const long long fit = static_cast<long long>(kNoAllocPartBytes / slot_bytes) - n;
+  if (n > kNoAllocMaxSeqs || fit < 1) {
     std::fprintf(stderr,
-                 "pl_attn_decode_batch_dev_noalloc: %d sequences exceed the fixed maximum of %d "
-                 "(its scratch is a static %zu-byte device array)\n",
-                 n, kNoAllocMaxSeqs, kNoAllocScratchBytes);
+                 "pl_attn_decode_batch_dev_noalloc: %d sequences exceed its fixed scratch "
+                 "(at most %d sequences and %zu partial slots of %zu bytes in a static "
+                 "%zu-byte device array)\n",
+                 n, kNoAllocMaxSeqs, kNoAllocPartBytes / slot_bytes, slot_bytes,
+                 kNoAllocScratchBytes);
     return PL_EARG;
   }
   uint8_t* scratch = nullptr;
   int rc = noalloc_scratch(g->device, &scratch);
   if (rc) return rc;
-  int* counters = reinterpret_cast<int*>(scratch);
-  float* part = reinterpret_cast<float*>(scratch + kNoAllocCounterBytes);
-  // as many splits as the decode heuristic wants, capped to what fits
-  int ns = n_split_for(n, max_pos + 1);
-  const size_t per_split = static_cast<size_t>(n) * g->n_heads * kPartStride * sizeof(float);
-  const int fit = static_cast<int>(kNoAllocPartBytes / per_split);
-  if (ns > fit) ns = fit > 1 ? fit : 1;
+  int2* seg_info = reinterpret_cast<int2*>(scratch);
+  float* part = reinterpret_cast<float*>(scratch + kNoAllocInfoBytes);
+  int grid = decode_grid(n, max_pos + 1);
+  if (grid > fit) grid = static_cast<int>(fit);  // fewer, longer CTAs when slots run short
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  // the array keeps the previous call's contents: the merge counters must
-  // start at zero
-  PL_CUDA(cudaMemsetAsync(counters, 0, sizeof(int) * n, st));
-  pl::DecodeArgs a;
-  a.n_layers = g->n_layers;
-  a.max_seq = g->max_seq;
-  a.n_heads = g->n_heads;
-  a.n_kv_heads = g->n_kv_heads;
-  a.kv_mul = g->kv_mul;
-  a.layer = layer;
-  a.n_slots = g->n_seqs;
-  a.rope_type = g->rope_type;
-  a.cos_tab = g->d_cos;
-  a.sin_tab = g->d_sin;
-  a.kc = g->d_k;
-  a.vc = g->d_v;
-  a.seqs = d_seqs;
-  a.pos = d_pos;
-  a.q = d_q;
-  a.k = d_k;
-  a.v = d_v;
-  a.out = d_out;
-  a.part = part;
-  a.part_out = nullptr;
-  a.counters = counters;
-  a.n_split = ns;
-  a.merge_in_kernel = ns <= pl::kMaxInKernelMerge ? 1 : 0;
-  a.mode = 0;
-  a.row0 = 0;
-  a.n_rows = 0;
-  a.append = 1;
-  a.score_scale = pl::kLog2e / sqrtf(static_cast<float>(kHD));
-  a.err = g->d_err;
-  switch (g->tp) {
-    case 16: rc = noalloc_launch_tp<16>(a, n, st); break;
-    case 32: rc = noalloc_launch_tp<32>(a, n, st); break;
-    case 64: rc = noalloc_launch_tp<64>(a, n, st); break;
-    case 128: rc = noalloc_launch_tp<128>(a, n, st); break;
-    default: return PL_EUNSUPPORTED;
-  }
-  if (rc) return rc;
-  if (!a.merge_in_kernel) {
-    pl::combine_kernel<<<dim3(g->n_heads, n), 64, 0, st>>>(ns, g->n_heads, part, d_out, nullptr);
-    PL_CUDA(cudaGetLastError());
-  }
-  return PL_OK;
+  // the array keeps the previous call's contents; every word the kernels
+  // read (the segment table, the partial slots of this launch) is written
+  // by this launch first, so nothing needs clearing
+  const pl::DecodeArgs a = decode_args(layer, n, d_seqs, d_pos, d_q, d_k, d_v, d_out, 0, 0, 0,
+                                       1, nullptr, part, seg_info);
+  return launch_decode_kernel(a, grid, st, false);
 }
