@@ -257,7 +257,7 @@ def run_batched_decode(args, rank, world, local, peaks):
                      "unit": "GB/s", "frac": achieved / peaks["hbm_gbs"],
                      "peak_source": peaks["source"] + " (hbm_gbs, burst copy)",
                      "traffic": profile_traffic("decode_kernel_config4.txt"),
-                     "kernel": "pl::decode_kernel<32,3> (fused RoPE + append + split-KV "
+                     "kernel": "pl::decode_kernel<32,4> (fused RoPE + append + split-KV "
                                "attention; the split merge is a second, PDL-overlapped kernel)",
                      "bytes_per_launch": total_bytes / args.steps},
         "gpu_launches": int(round(launches_per_step * args.steps)),

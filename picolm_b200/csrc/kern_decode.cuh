@@ -59,10 +59,6 @@ constexpr int kPartStride = kHD + 4;    // floats per partial: m, l, 2 pad, o[64
 constexpr int kPartO = 4;               // offset of o in a partial (16-byte aligned)
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr int kMaxLaunchSeqs = 1024;    // sequences per launch (prefix scan in smem)
-// merge_kernel shapes: HB heads per block x 16 float4 columns x LANES
-// segment lanes.  Many short merges: (4, 4) = 256 threads; few long merges
-// (a long single sequence split over every CTA): (2, 16) = 512 threads.
-constexpr int kMergeWideSegs = 32;      // use the wide shape above this many segments
 constexpr int kMaxCombineParts = 16;    // device partials merged by combine_kernel
 
 struct DecodeArgs {
@@ -547,103 +543,99 @@ __global__ void __launch_bounds__(288) decode_kernel(const DecodeArgs a,
 
 }
 
-// Merge of the segment partials of one decode launch.  grid = (n,
-// ceil(n_heads / HB)), block = HB * 16 * LANES threads, dynamic shared
-// memory 3 * max_segments * HB floats + one float4 per thread.  Launched
-// with programmatic stream serialisation behind decode_kernel: it waits on
-// griddepcontrol.wait until the decode grid has finished and its writes are
-// visible.  Thread (lane j, head hh, float4 q4) sums segments j, j+LANES,
-// ...; the lanes are reduced through shared memory.
-template <int kMergeHeads, int kMergeLanes>
-__global__ void __launch_bounds__(kMergeHeads * (kHD / 4) * kMergeLanes)
-    merge_kernel(const DecodeArgs a) {
-  constexpr int kMergeThreads = kMergeHeads * (kHD / 4) * kMergeLanes;
-  extern __shared__ float4 smem4[];
+// Merge of the segment partials of one decode launch.
+// grid = (n, ceil(n_heads / hpb)), block = kMergeThreads; a block merges
+// heads [h0, h0 + hpb) of sequence i.  Thread t owns float4 column q4 of
+// head hh and every lanes-th segment (lanes = kMergeThreads / (hpb * 16)).
+// Launched with programmatic stream serialisation behind decode_kernel, the
+// grid (sized to stay resident) waits on griddepcontrol.wait; after it, one
+// round trip reads the segment table and one more reads everything else:
+// each thread loads (m, l) and o of all its segments at once, reduces them
+// locally in log-sum-exp form, and the lanes are merged through shared
+// memory.
+constexpr int kMergeThreads = 256;
+
+__global__ void __launch_bounds__(kMergeThreads) merge_kernel(const DecodeArgs a, int hpb) {
+  __shared__ float4 s_acc[kMergeThreads];
+  __shared__ float2 s_ml[kMergeThreads];
   asm volatile("griddepcontrol.wait;" ::: "memory");
-  const int i = blockIdx.x, h0 = blockIdx.y * kMergeHeads, tid = threadIdx.x;
+  const int i = blockIdx.x, h0 = blockIdx.y * hpb, tid = threadIdx.x;
+  const int pairs = hpb * (kHD / 4), lanes = kMergeThreads / pairs;
+  const int pair = tid % pairs, lane_j = tid / pairs;
+  const int hh = pair / (kHD / 4), q4 = pair % (kHD / 4), h = h0 + hh;
   const int2 si = a.seg_info[i];
   const int ns = si.y;
   if (ns <= 1) return;  // finished by its single segment (or no rows)
   const size_t slot_stride = static_cast<size_t>(a.n_heads) * kPartStride;
-  const float* src0 = a.part + static_cast<size_t>(si.x) * slot_stride;
-  float4* s_acc = smem4;                                    // [kMergeThreads]
-  float* s_m = reinterpret_cast<float*>(smem4 + kMergeThreads);  // [ns][kMergeHeads]
-  float* s_l = s_m + ns * kMergeHeads;
-  float* s_w = s_l + ns * kMergeHeads;
-  __shared__ float sM[kMergeHeads], sL[kMergeHeads];
-  for (int t = tid; t < ns * kMergeHeads; t += kMergeThreads) {
-    const int j = t / kMergeHeads, hh = t - j * kMergeHeads;
-    float2 ml = make_float2(-INFINITY, 0.f);
-    if (h0 + hh < a.n_heads)
-      ml = __ldcg(reinterpret_cast<const float2*>(src0 + j * slot_stride +
-                                                  (h0 + hh) * kPartStride));
-    s_m[t] = ml.x;
-    s_l[t] = ml.y;
-  }
-  __syncthreads();
-  if (tid < kMergeHeads) {
-    float M = -INFINITY;
-    for (int j = 0; j < ns; ++j) M = fmaxf(M, s_m[j * kMergeHeads + tid]);
-    float L = 0.f;
-    for (int j = 0; j < ns; ++j) {
-      const float w = M == -INFINITY ? 0.f : ex2(s_m[j * kMergeHeads + tid] - M);
-      s_w[j * kMergeHeads + tid] = w;
-      L += w * s_l[j * kMergeHeads + tid];
-    }
-    sM[tid] = M;
-    sL[tid] = L;
-    if (a.mode == 0) {
-      const float inv = 1.0f / L;
-      for (int j = 0; j < ns; ++j) s_w[j * kMergeHeads + tid] *= inv;
-    }
-  }
-  __syncthreads();
-  const int pair = tid % (kMergeHeads * (kHD / 4)), lane_j = tid / (kMergeHeads * (kHD / 4));
-  const int hh = pair / (kHD / 4), q4 = pair % (kHD / 4);
+  float m_loc = -INFINITY, l_loc = 0.f;
   float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-  if (h0 + hh < a.n_heads) {
-    const float* base = src0 + (h0 + hh) * kPartStride + kPartO + 4 * q4;
-    for (int j0 = lane_j; j0 < ns; j0 += 8 * kMergeLanes) {  // 8 loads in flight
+  if (lane_j < lanes && h < a.n_heads) {
+    const float* base = a.part + static_cast<size_t>(si.x) * slot_stride + h * kPartStride;
+    for (int j0 = lane_j; j0 < ns; j0 += 8 * lanes) {  // 8 segments in flight
+      float2 ml[8];
       float4 v[8];
 #pragma unroll
       for (int u = 0; u < 8; ++u) {
-        const int j = j0 + u * kMergeLanes;
-        if (j < ns) v[u] = __ldcg(reinterpret_cast<const float4*>(base + j * slot_stride));
-      }
-#pragma unroll
-      for (int u = 0; u < 8; ++u) {
-        const int j = j0 + u * kMergeLanes;
+        const int j = j0 + u * lanes;
         if (j < ns) {
-          const float w = s_w[j * kMergeHeads + hh];
-          acc.x += w * v[u].x;
-          acc.y += w * v[u].y;
-          acc.z += w * v[u].z;
-          acc.w += w * v[u].w;
+          ml[u] = __ldcg(reinterpret_cast<const float2*>(base + j * slot_stride));
+          v[u] = __ldcg(reinterpret_cast<const float4*>(base + j * slot_stride + kPartO) + q4);
         }
+      }
+      float mx = m_loc;
+#pragma unroll
+      for (int u = 0; u < 8; ++u)
+        if (j0 + u * lanes < ns) mx = fmaxf(mx, ml[u].x);
+      if (mx != -INFINITY) {
+        const float sc = ex2(m_loc - mx);
+        l_loc *= sc;
+        acc.x *= sc;
+        acc.y *= sc;
+        acc.z *= sc;
+        acc.w *= sc;
+#pragma unroll
+        for (int u = 0; u < 8; ++u)
+          if (j0 + u * lanes < ns) {
+            const float w = ex2(ml[u].x - mx);
+            l_loc += w * ml[u].y;
+            acc.x += w * v[u].x;
+            acc.y += w * v[u].y;
+            acc.z += w * v[u].z;
+            acc.w += w * v[u].w;
+          }
+        m_loc = mx;
       }
     }
   }
   s_acc[tid] = acc;
+  s_ml[tid] = make_float2(m_loc, l_loc);
   __syncthreads();
-  if (lane_j == 0 && h0 + hh < a.n_heads) {
-#pragma unroll
-    for (int l = 1; l < kMergeLanes; ++l) {
-      const float4 o = s_acc[tid + l * kMergeHeads * (kHD / 4)];
-      acc.x += o.x;
-      acc.y += o.y;
-      acc.z += o.z;
-      acc.w += o.w;
+  if (lane_j != 0 || h >= a.n_heads) return;
+  float M = m_loc;
+  for (int l = 1; l < lanes; ++l) M = fmaxf(M, s_ml[tid + l * pairs].x);
+  float L = 0.f;
+  float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
+  if (M != -INFINITY)
+    for (int l = 0; l < lanes; ++l) {
+      const float2 ml = s_ml[tid + l * pairs];
+      const float4 x = s_acc[tid + l * pairs];
+      const float w = ex2(ml.x - M);
+      L += w * ml.y;
+      o.x += w * x.x;
+      o.y += w * x.y;
+      o.z += w * x.z;
+      o.w += w * x.w;
     }
-    if (a.mode == 0) {
-      reinterpret_cast<float4*>(a.out + (static_cast<size_t>(i) * a.n_heads + h0 + hh) * kHD)[q4] =
-          acc;
-    } else {
-      float* dst = a.part_out + (static_cast<size_t>(i) * a.n_heads + h0 + hh) * kPartStride;
-      reinterpret_cast<float4*>(dst + kPartO)[q4] = acc;
-      if (q4 == 0) {
-        dst[0] = sM[hh];
-        dst[1] = sL[hh];
-      }
+  if (a.mode == 0) {
+    const float inv = 1.0f / L;
+    reinterpret_cast<float4*>(a.out + (static_cast<size_t>(i) * a.n_heads + h) * kHD)[q4] =
+        make_float4(o.x * inv, o.y * inv, o.z * inv, o.w * inv);
+  } else {
+    float* dst = a.part_out + (static_cast<size_t>(i) * a.n_heads + h) * kPartStride;
+    reinterpret_cast<float4*>(dst + kPartO)[q4] = o;
+    if (q4 == 0) {
+      dst[0] = M;
+      dst[1] = L;
     }
   }
 }

@@ -31,7 +31,7 @@ typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t,
                                   const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
 
-constexpr int kDecodeStages = 3;
+constexpr int kDecodeStages = 4;
 
 struct Ctx {
   int device = -1;
@@ -284,43 +284,28 @@ int launch_decode_tp(const pl::DecodeArgs& a, int grid, cudaStream_t st, bool pr
 // The split merge, queued behind the decode grid with programmatic stream
 // serialisation: its CTAs become resident while the decode grid runs and
 // wait on griddepcontrol.wait (grid = sequences x head groups).
-template <int HB, int LANES>
-int launch_merge_shape(const pl::DecodeArgs& a, int decode_grid_ctas, cudaStream_t st,
-                       bool profile) {
-  auto kern = pl::merge_kernel<HB, LANES>;
-  const int threads = HB * (kHD / 4) * LANES;
-  const size_t smem = threads * sizeof(float4) +
-                      static_cast<size_t>(3) * decode_grid_ctas * HB * sizeof(float);
-  static size_t smem_attr = 0;
-  if (smem > 48 * 1024 && smem > smem_attr) {
-    PL_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 static_cast<int>(smem)));
-    smem_attr = smem;
-  }
+// The split merge, queued behind the decode grid with programmatic stream
+// serialisation (its CTAs become resident while the decode grid runs and
+// wait on griddepcontrol.wait).  Heads per block: as many as keep about one
+// block per SM, so the whole merge grid is resident in one wave.
+int launch_merge(const pl::DecodeArgs& a, int decode_grid_ctas, cudaStream_t st, bool profile) {
+  if (decode_grid_ctas <= 1) return PL_OK;  // one CTA: every sequence is one segment
+  int hpb = 16;
+  while (hpb > 1 && static_cast<long long>(a.n) * ((g->n_heads + hpb - 1) / hpb) < g->num_sms)
+    hpb >>= 1;
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(a.n, (g->n_heads + HB - 1) / HB);
-  cfg.blockDim = dim3(threads);
-  cfg.dynamicSmemBytes = smem;
+  cfg.gridDim = dim3(a.n, (g->n_heads + hpb - 1) / hpb);
+  cfg.blockDim = dim3(pl::kMergeThreads);
+  cfg.dynamicSmemBytes = 0;
   cfg.stream = st;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  PL_CUDA(cudaLaunchKernelEx(&cfg, kern, a));
+  PL_CUDA(cudaLaunchKernelEx(&cfg, pl::merge_kernel, a, hpb));
   if (profile) count_launch();
   return PL_OK;
-}
-
-// The split merge, queued behind the decode grid with programmatic stream
-// serialisation: its CTAs become resident while the decode grid runs and
-// wait on griddepcontrol.wait (grid = sequences x head groups).
-int launch_merge(const pl::DecodeArgs& a, int decode_grid_ctas, cudaStream_t st, bool profile) {
-  if (decode_grid_ctas <= 1) return PL_OK;  // one CTA: every sequence is one segment
-  // segments per sequence are at most about grid / n + 2
-  if (decode_grid_ctas / a.n + 2 > pl::kMergeWideSegs)
-    return launch_merge_shape<2, 16>(a, decode_grid_ctas, st, profile);
-  return launch_merge_shape<4, 4>(a, decode_grid_ctas, st, profile);
 }
 
 int launch_decode_kernel(const pl::DecodeArgs& a, int grid, cudaStream_t st, bool profile) {
