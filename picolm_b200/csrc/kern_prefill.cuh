@@ -5,21 +5,38 @@
 // prologue kernel (kern_misc.cuh) has already rotated q/k, appended k/v to
 // the FP16 cache (bit-exact) and staged q as FP16 [n_tok][n_heads][64].
 //
-// One CTA = one (query head, 128-row query tile).  Warp roles:
-//   warps 0-3  softmax + epilogue; thread r owns query row r = TMEM lane r
-//   warp 4     TMA producer: the Q tile once, then K/V tiles of 128 cache
-//              rows through an NS-deep ring (128-byte swizzle)
-//   warp 5     TMEM allocator and the single MMA-issuing thread
-// Per KV tile j:
-//   S_j = Q K_j^T    tcgen05.mma M=128 N=128 K=64 -> TMEM S[j%2] (FP32)
-//   softmax warps: tcgen05.ld S row, causal mask, online max (log2 domain),
-//                  P = 2^(s - m) as FP16 into shared memory (SW128 K-major)
-//   PV_j = P_j V_j   tcgen05.mma M=128 N=64 K=128 -> TMEM O[j%2] (fresh)
-//   softmax warps: tcgen05.ld PV_j, O = O * alpha + PV_j in registers
-// S and O are double-buffered in TMEM so the tensor core computes S_{j+1}
-// and PV_j while the softmax warps work on tile j.  Every wait is bounded;
-// a wait that gives up records an error bit and the CTA winds down (waits
-// for its own MMAs and TMA copies, frees its TMEM) instead of hanging.
+// Work item = two 128-row query tiles ("slots" A and B) sharing one KV
+// head: two query heads of the same GQA group at the same rows (with one
+// query head per KV head, slot B is unused).  Both slots see the same K/V
+// tiles and the same causal range.  The kernel is persistent: one CTA per
+// SM takes items from a global counter, heaviest (latest) query tiles
+// first, and every pipeline below runs on across item boundaries (the next
+// item's Q and first K/V tiles load while the current one finishes).
+//
+// Warp roles (320 threads):
+//   warps 0-3  softmax of slot A; thread r owns query row r = TMEM lane r
+//   warps 4-7  softmax of slot B (same lanes, other TMEM columns)
+//   warp 8     scheduler + TMA producer: fetches items, publishes them in a
+//              two-entry shared-memory queue, loads Q_A/Q_B per item and
+//              K/V tiles of 128 cache rows through a kPfStages ring
+//   warp 9     TMEM allocator and the single MMA-issuing thread
+// Per KV tile j the MMA thread issues, in order,
+//   S_A(j) = Q_A K_j^T, S_B(j) = Q_B K_j^T     (M=128 N=128 K=64 -> TMEM)
+//   PV_A(j-1) = P_A V, PV_B(j-1) = P_B V       (M=128 N=64 K=128 -> TMEM O)
+// so one slot's softmax overlaps the other slot's MMAs (ping-pong).  A
+// softmax thread loads its 128-column S row from TMEM once, takes the row
+// max (causal mask on diagonal tiles only), and writes P = 2^(s*c - m) as
+// FP16 straight into one of the slot's two shared-memory P tiles (SW128
+// K-major, the A operand of the PV MMA).  Three quarters of the 2^x go to
+// the MUFU unit, one quarter to a cubic polynomial on the FMA pipe (see
+// exp2_poly2), which balances the two pipes.  O accumulates in TMEM; the
+// running max used for P is raised only when a row's max grows by more than
+// 2^8 (then the warp rescales its O rows in TMEM), so P <= 2^8 is exact in
+// FP16 and the final O / l is unchanged.
+//
+// Every wait is bounded; a wait that gives up records an error bit and the
+// CTA winds down (waits for its own MMAs and TMA copies, frees its TMEM)
+// instead of hanging.
 #pragma once
 #include <cstdint>
 #include <cuda.h>
@@ -29,10 +46,11 @@
 
 namespace pl {
 
-constexpr int kPfBlockM = 128;  // query rows per CTA
+constexpr int kPfBlockM = 128;  // query rows per slot
 constexpr int kPfBlockN = 128;  // cache rows per KV tile
 constexpr int kPfStages = 2;    // K/V ring depth
-constexpr int kPfThreads = 192;
+constexpr int kPfThreads = 320;
+constexpr float kPfRescaleLog2 = 8.0f;  // raise the running max only past 2^8
 
 struct PrefillArgs {
   const uint16_t* q16;   // [n_tok][n_heads][64] FP16, rotated
@@ -40,30 +58,95 @@ struct PrefillArgs {
   int out_stride;
   int n_tok, start_pos, n_heads, kv_mul, slab;
   float score_scale;     // log2(e)/sqrt(64)
+  int* work;             // [2] item counter, finished-CTA counter; zero at rest
   uint32_t* err;
 };
 
 struct PfSmem {
   // 1024-byte aligned tiles (128-byte swizzle atoms are 8 rows x 128 B)
-  uint8_t q[kPfBlockM * 128];                 // 16 KB
-  uint8_t k[kPfStages][kPfBlockN * 128];      // 16 KB each
-  uint8_t v[kPfStages][kPfBlockN * 128];      // 16 KB each
-  uint8_t p[2][2][kPfBlockM * 128];           // [buf][k-chunk of 64] 16 KB each
-  uint64_t q_full;
+  uint8_t q[2][kPfBlockM * 128];                // Q_A, Q_B: 16 KB each
+  uint8_t k[kPfStages][kPfBlockN * 128];        // 16 KB each
+  uint8_t v[kPfStages][kPfBlockN * 128];        // 16 KB each
+  uint8_t p[2][2][2][kPfBlockM * 128];          // [slot][buffer][k-chunk of 64] 16 KB each
+  uint64_t q_full, q_empty;
   uint64_t kv_full[kPfStages], kv_empty[kPfStages];
-  uint64_t s_full[2], s_free[2], p_full[2], o_full[2], o_free[2];
+  uint64_t s_full[2], s_free[2], p_full[2][2], pv_done[2][2], o_free[2];
+  uint64_t item_full[2], item_empty[2];
   uint64_t mma_done;
+  int item[2];
   uint32_t tmem_base;
-  int abort_flag;
 };
 
 constexpr int kPfSmemBytes = static_cast<int>(sizeof(PfSmem)) + 1024;
 
-// TMEM column map (512 columns allocated)
-constexpr uint32_t kColS0 = 0, kColS1 = 128, kColO0 = 256, kColO1 = 320;
+// TMEM column map (512 columns allocated): S_A, S_B, O_A, O_B
+__device__ __forceinline__ uint32_t pf_col_s(int x) { return x ? 128u : 0u; }
+__device__ __forceinline__ uint32_t pf_col_o(int x) { return x ? 320u : 256u; }
 
-__device__ __forceinline__ uint32_t pf_col_s(int b) { return b ? kColS1 : kColS0; }
-__device__ __forceinline__ uint32_t pf_col_o(int b) { return b ? kColO1 : kColO0; }
+__device__ __forceinline__ void tc_ld_x32(uint32_t taddr, uint32_t* r) {
+  tc_ld_32x32b_x32(taddr, *reinterpret_cast<uint32_t(*)[32]>(r));
+}
+
+// After tcgen05.wait::ld: make every later use of r depend on the wait (the
+// load writes r asynchronously; the compiler must not read r earlier).
+__device__ __forceinline__ void reg_fence32(uint32_t* r) {
+#pragma unroll
+  for (int i = 0; i < 32; ++i) asm volatile("" : "+r"(r[i]));
+}
+
+// 2^x for two x <= 0 on the FMA pipe: x = n + f with n = round(x) (the
+// 1.5*2^23 addition leaves n in the low mantissa bits), 2^f on [-0.5, 0.5]
+// by a cubic fitted for minimum relative error (max 7.5e-5, below the FP16
+// rounding P gets next), and n added to the exponent field.  x is clamped at
+// -126 so the exponent field cannot wrap: there (and for x = -inf) the
+// result is below 2^-125, which is 0 after the FP16 rounding of P.
+__device__ __forceinline__ float2 exp2_poly2(float2 x) {
+  constexpr float kC0 = 0.99992806f, kC1 = 0.69326097f, kC2 = 0.24261113f, kC3 = 0.05517166f;
+  constexpr float kMagic = 12582912.0f;  // 1.5 * 2^23
+  x.x = fmaxf(x.x, -126.f);
+  x.y = fmaxf(x.y, -126.f);
+  const float2 t = add2(x, make_float2(kMagic, kMagic));
+  const float2 n = add2(t, make_float2(-kMagic, -kMagic));
+  const float2 f = add2(x, make_float2(-n.x, -n.y));
+  float2 p = fma2(make_float2(kC3, kC3), f, make_float2(kC2, kC2));
+  p = fma2(p, f, make_float2(kC1, kC1));
+  p = fma2(p, f, make_float2(kC0, kC0));
+  return make_float2(__int_as_float(__float_as_int(p.x) + (__float_as_int(t.x) << 23)),
+                     __int_as_float(__float_as_int(p.y) + (__float_as_int(t.y) << 23)));
+}
+
+struct PfItem {
+  int q_row0, head0, head1, kvh, nkv, p_min;
+};
+
+// Item b, heaviest first: query tile n_qt-1-b/per_tile, head pair b%per_tile.
+__device__ __forceinline__ PfItem pf_item(const PrefillArgs& a, int b) {
+  PfItem it;
+  const bool dual = a.kv_mul >= 2;
+  const int per_tile = dual ? a.n_heads / 2 : a.n_heads;
+  const int n_qt = (a.n_tok + kPfBlockM - 1) / kPfBlockM;
+  const int qt = n_qt - 1 - b / per_tile;
+  const int r_item = b % per_tile;
+  if (dual) {
+    const int pairs = a.kv_mul / 2;
+    it.head0 = (r_item / pairs) * a.kv_mul + 2 * (r_item % pairs);
+    it.head1 = it.head0 + 1;
+  } else {
+    it.head0 = r_item;
+    it.head1 = -1;
+  }
+  it.kvh = it.head0 / a.kv_mul;
+  it.q_row0 = qt * kPfBlockM;
+  const int last_row = min(a.n_tok, it.q_row0 + kPfBlockM) - 1;
+  it.nkv = (a.start_pos + last_row + 1 + kPfBlockN - 1) / kPfBlockN;  // >= 1
+  it.p_min = a.start_pos + it.q_row0;
+  return it;
+}
+
+__device__ __forceinline__ int pf_n_items(const PrefillArgs& a) {
+  const int per_tile = a.kv_mul >= 2 ? a.n_heads / 2 : a.n_heads;
+  return ((a.n_tok + kPfBlockM - 1) / kPfBlockM) * per_tile;
+}
 
 __global__ void __launch_bounds__(kPfThreads, 1)
     prefill_attn_kernel(const PrefillArgs a, const __grid_constant__ CUtensorMap tm_q,
@@ -73,37 +156,30 @@ __global__ void __launch_bounds__(kPfThreads, 1)
   PfSmem& sm = *reinterpret_cast<PfSmem*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-
-  // heaviest (latest) query tiles first: b -> (tile, head)
-  const int n_qt = (a.n_tok + kPfBlockM - 1) / kPfBlockM;
-  const int b = blockIdx.x;
-  const int qt = n_qt - 1 - b / a.n_heads;
-  const int h = b % a.n_heads;
-  const int kvh = h / a.kv_mul;
-  const int q_row0 = qt * kPfBlockM;
-  const int last_row = min(a.n_tok, q_row0 + kPfBlockM) - 1;
-  const int kv_rows = a.start_pos + last_row + 1;         // cache rows this tile needs
-  const int nkv = (kv_rows + kPfBlockN - 1) / kPfBlockN;   // >= 1
-  const int p_min = a.start_pos + q_row0;                   // smallest query position
+  const int n_slots = a.kv_mul >= 2 ? 2 : 1;
 
   if (threadIdx.x == 0) {
     mbar_init(&sm.q_full, 1);
+    mbar_init(&sm.q_empty, 1);
     for (int s = 0; s < kPfStages; ++s) {
       mbar_init(&sm.kv_full[s], 1);
       mbar_init(&sm.kv_empty[s], 1);
     }
-    for (int i = 0; i < 2; ++i) {
-      mbar_init(&sm.s_full[i], 1);
-      mbar_init(&sm.s_free[i], 4);
-      mbar_init(&sm.p_full[i], 4);
-      mbar_init(&sm.o_full[i], 1);
-      mbar_init(&sm.o_free[i], 4);
+    for (int x = 0; x < 2; ++x) {
+      mbar_init(&sm.s_full[x], 1);
+      mbar_init(&sm.s_free[x], 4);
+      mbar_init(&sm.o_free[x], 4);
+      for (int b2 = 0; b2 < 2; ++b2) {
+        mbar_init(&sm.p_full[x][b2], 4);
+        mbar_init(&sm.pv_done[x][b2], 1);
+      }
+      mbar_init(&sm.item_full[x], 1);
+      mbar_init(&sm.item_empty[x], 9);  // the MMA thread + 8 softmax warps
     }
     mbar_init(&sm.mma_done, 1);
-    sm.abort_flag = 0;
     fence_mbar_init();
   }
-  if (warp == 5) {
+  if (warp == 9) {
     tmem_alloc(&sm.tmem_base, 512);
     tmem_relinquish();
   }
@@ -112,194 +188,289 @@ __global__ void __launch_bounds__(kPfThreads, 1)
   tc_fence_after();
   const uint32_t tmem = sm.tmem_base;
 
-  if (warp == 4) {
-    // ------------------------------------------------------------ producer
+  if (warp == 8) {
+    // --------------------------------------------------- scheduler + TMA
     if (lane == 0) {
       tma_prefetch_desc(&tm_q);
       tma_prefetch_desc(&tm_k);
       tma_prefetch_desc(&tm_v);
-      mbar_arrive_expect_tx(&sm.q_full, kPfBlockM * 128);
-      tma_load_3d(sm.q, &tm_q, &sm.q_full, 0, h, q_row0);
-      int issued = 0;
-      for (int j = 0; j < nkv; ++j) {
-        const int s = j % kPfStages;
-        if (j >= kPfStages &&
-            !mbar_wait_bounded(&sm.kv_empty[s], ((j / kPfStages) - 1) & 1)) {
+      const int n_items = pf_n_items(a);
+      int J = 0, k = 0;
+      bool ok = true;
+      while (true) {
+        int item = ok ? atomicAdd(&a.work[0], 1) : -1;
+        if (item >= n_items) item = -1;
+        if (k >= 2 && !mbar_wait_bounded(&sm.item_empty[k & 1], ((k - 2) >> 1) & 1)) {
           atomicOr(a.err, ERR_TIMEOUT_EMPTY);
-          sm.abort_flag = 1;
-          break;
+          break;  // consumers time out on item_full and wind down
         }
-        if (*reinterpret_cast<volatile int*>(&sm.abort_flag)) break;
-        mbar_arrive_expect_tx(&sm.kv_full[s], 2 * kPfBlockN * 128);
-        tma_load_4d(sm.k[s], &tm_k, &sm.kv_full[s], 0, j * kPfBlockN, kvh, a.slab);
-        tma_load_4d(sm.v[s], &tm_v, &sm.kv_full[s], 0, j * kPfBlockN, kvh, a.slab);
-        ++issued;
+        sm.item[k & 1] = item;
+        mbar_arrive(&sm.item_full[k & 1]);
+        if (item < 0) break;
+        const PfItem it = pf_item(a, item);
+        // Q of the previous item is in use until its last S MMAs complete
+        if (k >= 1 && !mbar_wait_bounded(&sm.q_empty, (k - 1) & 1)) {
+          atomicOr(a.err, ERR_TIMEOUT_EMPTY);
+          ok = false;
+          ++k;
+          continue;
+        }
+        mbar_arrive_expect_tx(&sm.q_full, n_slots * kPfBlockM * 128);
+        tma_load_3d(sm.q[0], &tm_q, &sm.q_full, 0, it.head0, it.q_row0);
+        if (n_slots == 2) tma_load_3d(sm.q[1], &tm_q, &sm.q_full, 0, it.head1, it.q_row0);
+        for (int j = 0; j < it.nkv; ++j, ++J) {
+          const int s = J % kPfStages;
+          if (J >= kPfStages && !mbar_wait_bounded(&sm.kv_empty[s], ((J / kPfStages) - 1) & 1)) {
+            atomicOr(a.err, ERR_TIMEOUT_EMPTY);
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&sm.kv_full[s], 2 * kPfBlockN * 128);
+          tma_load_4d(sm.k[s], &tm_k, &sm.kv_full[s], 0, j * kPfBlockN, it.kvh, a.slab);
+          tma_load_4d(sm.v[s], &tm_v, &sm.kv_full[s], 0, j * kPfBlockN, it.kvh, a.slab);
+        }
+        ++k;
       }
       // never leave with copies in flight: the last use of each stage must land
-      for (int j = issued - kPfStages; j < issued; ++j)
+      for (int j = J - kPfStages; j < J; ++j)
         if (j >= 0) mbar_wait_bounded(&sm.kv_full[j % kPfStages], (j / kPfStages) & 1);
-      mbar_wait_bounded(&sm.q_full, 0);
+      if (k >= 1) mbar_wait_bounded(&sm.q_full, (k - 1) & 1);
+      // the last CTA to stop fetching resets the counters for the next launch
+      __threadfence();
+      if (atomicAdd(&a.work[1], 1) == static_cast<int>(gridDim.x) - 1) {
+        a.work[0] = 0;
+        a.work[1] = 0;
+        __threadfence();
+      }
     }
-  } else if (warp == 5) {
+  } else if (warp == 9) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
       const uint32_t idesc_qk = idesc_f16_f32(128, 128, 0);
       const uint32_t idesc_pv = idesc_f16_f32(128, 64, 1);
-      const uint32_t q_addr = smem_u32(sm.q);
-      bool ok = mbar_wait_bounded(&sm.q_full, 0);
-      auto issue_pv = [&](int i) -> bool {
-        const int pb = i & 1, s = i % kPfStages;
-        if (!mbar_wait_bounded(&sm.p_full[pb], (i >> 1) & 1)) return false;
-        if (i >= 2 && !mbar_wait_bounded(&sm.o_free[pb], ((i >> 1) - 1) & 1)) return false;
-        tc_fence_after();
-        const uint32_t p_addr = smem_u32(sm.p[pb][0]);
+      int J = 0, k = 0;
+      bool ok = true;
+      // PV of global tile g (first tile of its item if `first`)
+      auto issue_pv = [&](int g, bool first) -> bool {
+        const int s = g % kPfStages, pb = g & 1;
         const uint32_t v_addr = smem_u32(sm.v[s]);
+        for (int x = 0; x < n_slots; ++x) {
+          if (!mbar_wait_bounded(&sm.p_full[x][pb], (g >> 1) & 1)) return false;
+          // the previous item's O must be read out before it is overwritten
+          if (first && k >= 1 && !mbar_wait_bounded(&sm.o_free[x], (k - 1) & 1)) return false;
+          tc_fence_after();
+          const uint32_t p_addr = smem_u32(sm.p[x][pb][0]);
 #pragma unroll
-        for (int kk = 0; kk < kPfBlockN / 16; ++kk) {
-          const uint64_t ad = smem_desc_sw128(p_addr + (kk >> 2) * (kPfBlockM * 128) + (kk & 3) * 32,
-                                              16, 1024);
-          const uint64_t bd = smem_desc_sw128(v_addr + kk * 16 * 128, 16, 1024);
-          tc_mma_ss(tmem + pf_col_o(pb), ad, bd, idesc_pv, kk > 0 ? 1u : 0u);
+          for (int kk = 0; kk < kPfBlockN / 16; ++kk) {
+            const uint64_t ad = smem_desc_sw128(
+                p_addr + (kk >> 2) * (kPfBlockM * 128) + (kk & 3) * 32, 16, 1024);
+            const uint64_t bd = smem_desc_sw128(v_addr + kk * 16 * 128, 16, 1024);
+            tc_mma_ss(tmem + pf_col_o(x), ad, bd, idesc_pv, (first && kk == 0) ? 0u : 1u);
+          }
+          tc_commit(&sm.pv_done[x][pb]);
         }
-        tc_commit(&sm.o_full[pb]);
         tc_commit(&sm.kv_empty[s]);
         return true;
       };
-      for (int j = 0; ok && j < nkv; ++j) {
-        const int s = j % kPfStages, sb = j & 1;
-        if (!mbar_wait_bounded(&sm.kv_full[s], (j / kPfStages) & 1)) { ok = false; break; }
-        if (j >= 2 && !mbar_wait_bounded(&sm.s_free[sb], ((j >> 1) - 1) & 1)) { ok = false; break; }
-        tc_fence_after();
-        const uint32_t k_addr = smem_u32(sm.k[s]);
+      while (ok) {
+        if (!mbar_wait_bounded(&sm.item_full[k & 1], (k >> 1) & 1)) { ok = false; break; }
+        const int item = *reinterpret_cast<volatile int*>(&sm.item[k & 1]);
+        mbar_arrive(&sm.item_empty[k & 1]);
+        if (item < 0) break;
+        const PfItem it = pf_item(a, item);
+        if (!mbar_wait_bounded(&sm.q_full, k & 1)) { ok = false; break; }
+        for (int j = 0; j < it.nkv && ok; ++j) {
+          const int g = J + j;
+          const int s = g % kPfStages;
+          if (!mbar_wait_bounded(&sm.kv_full[s], (g / kPfStages) & 1)) { ok = false; break; }
+          const uint32_t k_addr = smem_u32(sm.k[s]);
+          for (int x = 0; x < n_slots; ++x) {
+            if (g >= 1 && !mbar_wait_bounded(&sm.s_free[x], (g - 1) & 1)) { ok = false; break; }
+            tc_fence_after();
+            const uint32_t q_addr = smem_u32(sm.q[x]);
 #pragma unroll
-        for (int kk = 0; kk < 4; ++kk) {
-          const uint64_t ad = smem_desc_sw128(q_addr + kk * 32, 16, 1024);
-          const uint64_t bd = smem_desc_sw128(k_addr + kk * 32, 16, 1024);
-          tc_mma_ss(tmem + pf_col_s(sb), ad, bd, idesc_qk, kk > 0 ? 1u : 0u);
+            for (int kk = 0; kk < 4; ++kk) {
+              const uint64_t ad = smem_desc_sw128(q_addr + kk * 32, 16, 1024);
+              const uint64_t bd = smem_desc_sw128(k_addr + kk * 32, 16, 1024);
+              tc_mma_ss(tmem + pf_col_s(x), ad, bd, idesc_qk, kk > 0 ? 1u : 0u);
+            }
+            tc_commit(&sm.s_full[x]);
+          }
+          if (!ok) break;
+          if (j == it.nkv - 1) tc_commit(&sm.q_empty);  // Q free once these S MMAs land
+          if (j >= 1 && !issue_pv(g - 1, j == 1)) ok = false;
         }
-        tc_commit(&sm.s_full[sb]);
-        if (j >= 1 && !issue_pv(j - 1)) { ok = false; break; }
+        if (ok && !issue_pv(J + it.nkv - 1, it.nkv == 1)) ok = false;
+        J += it.nkv;
+        ++k;
       }
-      if (ok) ok = issue_pv(nkv - 1);
-      if (!ok) {
-        atomicOr(a.err, ERR_TIMEOUT_MMA);
-        sm.abort_flag = 1;
-      }
+      if (!ok) atomicOr(a.err, ERR_TIMEOUT_MMA);
       // all issued MMAs must finish before TMEM is freed
       tc_commit(&sm.mma_done);
       mbar_wait_bounded(&sm.mma_done, 0);
     }
   } else {
     // ------------------------------------------------------------ softmax
-    const int r = threadIdx.x;                 // query row in the tile, TMEM lane
-    const uint32_t lane_base = tmem + (static_cast<uint32_t>(warp * 32) << 16);
-    const int p_row = a.start_pos + q_row0 + r;  // this row's position
-    float m_run = -INFINITY, l_run = 0.f, alpha_prev = 0.f;
-    float o[64];
-#pragma unroll
-    for (int d = 0; d < 64; ++d) o[d] = 0.f;
+    const int x = warp >> 2;                     // slot
+    const int r = threadIdx.x & 127;             // query row in the tile, TMEM lane
+    const uint32_t lane_base = tmem + (static_cast<uint32_t>((warp & 3) * 32) << 16);
+    const float sc = a.score_scale;
+    const bool active = x < n_slots;
+    uint32_t sv[128];  // this row of S (one TMEM read per tile); reused for O
+    int J = 0, k = 0;
     bool ok = true;
-
-    auto consume_pv = [&](int i, float alpha) -> bool {
-      const int ob = i & 1;
-      if (!mbar_wait_bounded(&sm.o_full[ob], (i >> 1) & 1)) return false;
-      tc_fence_after();
-      uint32_t x[32];
+    while (ok) {
+      if (!mbar_wait_bounded(&sm.item_full[k & 1], (k >> 1) & 1)) { ok = false; break; }
+      const int item = *reinterpret_cast<volatile int*>(&sm.item[k & 1]);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&sm.item_empty[k & 1]);
+      if (item < 0) break;
+      const PfItem it = pf_item(a, item);
+      if (!active) {  // slot B without a second query head: nothing to do
+        J += it.nkv;
+        ++k;
+        continue;
+      }
+      const int p_row = it.p_min + r;  // this row's position
+      float m_used = -INFINITY, l_run = 0.f;
+      for (int j = 0; j < it.nkv; ++j) {
+        const int g = J + j;
+        if (!mbar_wait_bounded(&sm.s_full[x], g & 1)) { ok = false; break; }
+        tc_fence_after();
+        const int t0 = j * kPfBlockN;
+        const bool need_mask = t0 + kPfBlockN - 1 > it.p_min;  // diagonal tile
+        const int lim = p_row - t0;  // columns c <= lim are visible
 #pragma unroll
-      for (int half = 0; half < 2; ++half) {
-        tc_ld_32x32b_x32(lane_base + pf_col_o(ob) + 32 * half, x);
+        for (int c4 = 0; c4 < 4; ++c4) tc_ld_x32(lane_base + pf_col_s(x) + 32 * c4, sv + 32 * c4);
         tc_wait_ld();
 #pragma unroll
-        for (int d = 0; d < 32; ++d) o[32 * half + d] = fmaf(o[32 * half + d], alpha, __uint_as_float(x[d]));
-      }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&sm.o_free[ob]);
-      return true;
-    };
-
-    for (int j = 0; j < nkv; ++j) {
-      const int sb = j & 1;
-      if (!mbar_wait_bounded(&sm.s_full[sb], (j >> 1) & 1)) { ok = false; break; }
-      tc_fence_after();
-      uint32_t sv[128];
+        for (int c4 = 0; c4 < 4; ++c4) reg_fence32(sv + 32 * c4);
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&sm.s_free[x]);  // S may be overwritten now
+        if (need_mask) {
 #pragma unroll
-      for (int c4 = 0; c4 < 4; ++c4) {
-        tc_ld_32x32b_x32(lane_base + pf_col_s(sb) + 32 * c4,
-                         *reinterpret_cast<uint32_t(*)[32]>(&sv[32 * c4]));
-      }
-      tc_wait_ld();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&sm.s_free[sb]);
-
-      // scale, causal mask, tile max
-      const int t0 = j * kPfBlockN;
-      const bool need_mask = t0 + kPfBlockN - 1 > p_min;
-      float mt = -INFINITY;
-#pragma unroll
-      for (int cidx = 0; cidx < 128; ++cidx) {
-        float s = __uint_as_float(sv[cidx]) * a.score_scale;
-        if (need_mask && t0 + cidx > p_row) s = -INFINITY;
-        sv[cidx] = __float_as_uint(s);
-        mt = fmaxf(mt, s);
-      }
-      const float m_new = fmaxf(m_run, mt);
-      const float alpha = ex2(m_run - m_new);
-      // P = 2^(s - m_new) -> FP16 into the SW128 K-major P buffer
-      float rs = 0.f;
-      uint8_t* pbuf = sm.p[sb][0];
-#pragma unroll
-      for (int ch = 0; ch < 16; ++ch) {       // 16 chunks of 8 columns
-        uint32_t w4[4];
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const float p0 = ex2(__uint_as_float(sv[8 * ch + 2 * e]) - m_new);
-          const float p1 = ex2(__uint_as_float(sv[8 * ch + 2 * e + 1]) - m_new);
-          rs += p0 + p1;
-          w4[e] = pack_half2(p0, p1);
+          for (int c = 0; c < 128; ++c)
+            if (c > lim) sv[c] = __float_as_uint(-INFINITY);
         }
-        const int kc = ch >> 3, c16 = ch & 7;
-        uint8_t* dst = pbuf + kc * (kPfBlockM * 128) + r * 128 + ((c16 ^ (r & 7)) << 4);
-        *reinterpret_cast<uint4*>(dst) = make_uint4(w4[0], w4[1], w4[2], w4[3]);
+        // row max as a tree: 8 independent partial maxima, then combine
+        float mp[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) mp[u] = __uint_as_float(sv[u]);
+#pragma unroll
+        for (int c = 8; c < 128; c += 16)
+#pragma unroll
+          for (int u = 0; u < 8; ++u)
+            mp[u] = max3(mp[u], __uint_as_float(sv[c + u]), __uint_as_float(sv[c + 8 + u]));
+        const float m_tile = max3(max3(mp[0], mp[1], mp[2]), max3(mp[3], mp[4], mp[5]),
+                                  fmaxf(mp[6], mp[7])) * sc;
+        // lazy rescale: only when some row of the warp outgrew its max by 2^8
+        // (O itself is rescaled below, once this tile's P is written)
+        const bool rescale = __any_sync(0xffffffffu, m_tile > m_used + kPfRescaleLog2);
+        float alpha = 1.f;
+        if (rescale) {
+          const float m_new = fmaxf(m_used, m_tile);
+          alpha = ex2(m_used - m_new);  // 0 on the first tile
+          l_run *= alpha;
+          m_used = m_new;
+        }
+        // this slot's P buffer g&1 was last read by PV(g-2)
+        if (g >= 2 && !mbar_wait_bounded(&sm.pv_done[x][g & 1], ((g - 2) >> 1) & 1)) {
+          ok = false;
+          break;
+        }
+        // P = 2^(s*c - m) as FP16 into the SW128 K-major P tile (masked -> 0)
+        uint8_t* pbuf = sm.p[x][g & 1][0];
+        const float2 sc2 = make_float2(sc, sc), nm2 = make_float2(-m_used, -m_used);
+        float2 rs2[4];  // 4 independent partial row sums
+#pragma unroll
+        for (int e = 0; e < 4; ++e) rs2[e] = make_float2(0.f, 0.f);
+#pragma unroll
+        for (int cc = 0; cc < 16; ++cc) {  // 16 chunks of 8 columns
+          uint32_t w4[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const int c = 8 * cc + 2 * e;
+            const float2 arg =
+                fma2(make_float2(__uint_as_float(sv[c]), __uint_as_float(sv[c + 1])), sc2, nm2);
+            // three pairs on MUFU, the fourth on the FMA pipe (-inf -> 0)
+            const float2 pp = e == 3 ? exp2_poly2(arg) : make_float2(ex2(arg.x), ex2(arg.y));
+            rs2[e] = add2(rs2[e], pp);
+            w4[e] = pack_half2(pp.x, pp.y);
+          }
+          const int kc = cc >> 3, c16 = cc & 7;
+          uint8_t* dst = pbuf + kc * (kPfBlockM * 128) + r * 128 + ((c16 ^ (r & 7)) << 4);
+          *reinterpret_cast<uint4*>(dst) = make_uint4(w4[0], w4[1], w4[2], w4[3]);
+        }
+        if (rescale && j >= 1) {
+          // every PV so far must have landed in O before it is rescaled; PV(g)
+          // is issued only after p_full(g) below
+          if (!mbar_wait_bounded(&sm.pv_done[x][(g - 1) & 1], ((g - 1) >> 1) & 1)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+#pragma unroll
+          for (int half = 0; half < 2; ++half) {
+            uint32_t* ov = sv + 32 * half;
+            tc_ld_x32(lane_base + pf_col_o(x) + 32 * half, ov);
+            tc_wait_ld();
+            reg_fence32(ov);
+#pragma unroll
+            for (int d = 0; d < 32; ++d) ov[d] = __float_as_uint(__uint_as_float(ov[d]) * alpha);
+            tc_st_32x32b_x32(lane_base + pf_col_o(x) + 32 * half,
+                             *reinterpret_cast<uint32_t(*)[32]>(ov));
+          }
+          tc_wait_st();
+          tc_fence_before();
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&sm.p_full[x][g & 1]);
+        const float2 rsa = add2(rs2[0], rs2[1]), rsb = add2(rs2[2], rs2[3]);
+        l_run += (rsa.x + rsa.y) + (rsb.x + rsb.y);
       }
-      l_run = l_run * alpha + rs;
-      fence_proxy_async_smem();
+      if (!ok) break;
+      // O / l once the item's last PV has landed; then O is free again
+      const int g_last = J + it.nkv - 1;
+      if (!mbar_wait_bounded(&sm.pv_done[x][g_last & 1], (g_last >> 1) & 1)) { ok = false; break; }
+      tc_fence_after();
+      tc_ld_x32(lane_base + pf_col_o(x), sv);
+      tc_ld_x32(lane_base + pf_col_o(x) + 32, sv + 32);
+      tc_wait_ld();
+      reg_fence32(sv);
+      reg_fence32(sv + 32);
+      tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&sm.p_full[sb]);
-      if (j >= 1 && !consume_pv(j - 1, alpha_prev)) { ok = false; break; }
-      alpha_prev = alpha;
-      m_run = m_new;
-    }
-    if (ok) ok = consume_pv(nkv - 1, alpha_prev);
-    if (!ok) {
-      atomicOr(a.err, ERR_TIMEOUT_MMA);
-      sm.abort_flag = 1;
-    } else {
-      const int row = q_row0 + r;
+      if (lane == 0) mbar_arrive(&sm.o_free[x]);
+      const int row = it.q_row0 + r;
       if (row < a.n_tok) {
         const float inv = 1.0f / l_run;
-        float* dst = a.out + static_cast<size_t>(row) * a.out_stride + h * 64;
+        float* dst = a.out + static_cast<size_t>(row) * a.out_stride + (x ? it.head1 : it.head0) * 64;
 #pragma unroll
         for (int d = 0; d < 64; d += 4)
           *reinterpret_cast<float4*>(dst + d) =
-              make_float4(o[d] * inv, o[d + 1] * inv, o[d + 2] * inv, o[d + 3] * inv);
+              make_float4(__uint_as_float(sv[d]) * inv, __uint_as_float(sv[d + 1]) * inv,
+                          __uint_as_float(sv[d + 2]) * inv, __uint_as_float(sv[d + 3]) * inv);
       }
+      J += it.nkv;
+      ++k;
     }
+    if (!ok) atomicOr(a.err, ERR_TIMEOUT_MMA);
   }
 
   tc_fence_before();
   __syncthreads();
-  if (warp == 5) {
+  if (warp == 9) {
     tc_fence_after();
     tmem_dealloc(tmem, 512);
   }
 }
 
-// Host side: encode the Q map (over the FP16 q staging buffer) and launch.
+// Host side: one persistent CTA per SM (never more than there are items).
 inline int launch_prefill_attention(const PrefillArgs& a, const CUtensorMap& tm_q,
                                     const CUtensorMap& tm_k, const CUtensorMap& tm_v,
-                                    cudaStream_t st) {
+                                    int num_sms, cudaStream_t st) {
   static bool attr_done = false;
   if (!attr_done) {
     if (cudaFuncSetAttribute(prefill_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -307,8 +478,10 @@ inline int launch_prefill_attention(const PrefillArgs& a, const CUtensorMap& tm_
       return -4;
     attr_done = true;
   }
-  const int n_qt = (a.n_tok + kPfBlockM - 1) / kPfBlockM;
-  prefill_attn_kernel<<<n_qt * a.n_heads, kPfThreads, kPfSmemBytes, st>>>(a, tm_q, tm_k, tm_v);
+  const int per_tile = a.kv_mul >= 2 ? a.n_heads / 2 : a.n_heads;
+  const int n_items = ((a.n_tok + kPfBlockM - 1) / kPfBlockM) * per_tile;
+  const int grid = n_items < num_sms ? n_items : num_sms;
+  prefill_attn_kernel<<<grid, kPfThreads, kPfSmemBytes, st>>>(a, tm_q, tm_k, tm_v);
   return cudaGetLastError() == cudaSuccess ? 0 : -4;
 }
 

@@ -52,6 +52,7 @@ struct Ctx {
   float* d_part = nullptr;
   size_t part_cap = 0;        // floats
   int2* d_seg_info = nullptr; // [kMaxLaunchSeqs] (first slot, segments) per decode sequence
+  int* d_work = nullptr;      // [2] prefill work-queue counters (self-resetting)
   // prefill FP16 q staging
   uint16_t* d_q16 = nullptr;
   size_t q16_cap = 0;         // elements
@@ -387,6 +388,7 @@ void free_ctx(Ctx* c) {
   cudaFreeHost(c->h_stage);
   cudaFree(c->d_part);
   cudaFree(c->d_seg_info);
+  cudaFree(c->d_work);
   cudaFree(c->d_q16);
   cudaFree(c->d_err);
   for (cudaEvent_t e : c->ev_pool) cudaEventDestroy(e);
@@ -470,7 +472,8 @@ int pl_attn_init(int n_layers, int n_heads, int n_kv_heads, int head_dim, int ma
       cudaMalloc(&c->d_cos, sizeof(float) * max_seq_len * (kHD / 2)) != cudaSuccess ||
       cudaMalloc(&c->d_sin, sizeof(float) * max_seq_len * (kHD / 2)) != cudaSuccess ||
       cudaMalloc(&c->d_err, 256) != cudaSuccess ||
-      cudaMalloc(&c->d_seg_info, sizeof(int2) * pl::kMaxLaunchSeqs) != cudaSuccess) {
+      cudaMalloc(&c->d_seg_info, sizeof(int2) * pl::kMaxLaunchSeqs) != cudaSuccess ||
+      cudaMalloc(&c->d_work, 2 * sizeof(int)) != cudaSuccess) {
     free_ctx(c);
     return PL_ENOMEM;
   }
@@ -478,6 +481,7 @@ int pl_attn_init(int n_layers, int n_heads, int n_kv_heads, int head_dim, int ma
   cudaMemsetAsync(c->d_v, 0, cache_elems * 2, c->stream);
   cudaMemsetAsync(c->d_err, 0, 256, c->stream);
   cudaMemsetAsync(c->d_seg_info, 0, sizeof(int2) * pl::kMaxLaunchSeqs, c->stream);
+  cudaMemsetAsync(c->d_work, 0, 2 * sizeof(int), c->stream);
   {
     const size_t n = static_cast<size_t>(max_seq_len) * (kHD / 2);
     float* hc = static_cast<float*>(std::malloc(n * sizeof(float)));
@@ -723,10 +727,10 @@ static int launch_prefill(int seq, int layer, int start_pos, int n_tok, const fl
   int rc = ensure_q16(n_tok);
   if (rc) return rc;
   const size_t off = static_cast<size_t>(start_pos) * g->kv_dim;
-  const dim3 pgrid(n_tok, (g->n_heads + g->n_kv_heads + 7) / 8);
+  const int pgrid = (n_tok + pl::kPrologueRows - 1) / pl::kPrologueRows;
   pl::prefill_prologue_kernel<<<pgrid, 256, 0, st>>>(
-      d_q, d_k, d_v, g->d_q16, slab_k(seq, layer) + off, slab_v(seq, layer) + off, g->n_heads,
-      g->n_kv_heads, start_pos, g->d_cos, g->d_sin, g->rope_type);
+      d_q, d_k, d_v, g->d_q16, slab_k(seq, layer) + off, slab_v(seq, layer) + off, n_tok,
+      g->n_heads, g->n_kv_heads, start_pos, g->d_cos, g->d_sin, g->rope_type);
   PL_CUDA(cudaGetLastError());
   count_launch();
   pl::PrefillArgs a;
@@ -739,9 +743,10 @@ static int launch_prefill(int seq, int layer, int start_pos, int n_tok, const fl
   a.kv_mul = g->kv_mul;
   a.slab = seq * g->n_layers + layer;
   a.score_scale = pl::kLog2e / sqrtf(static_cast<float>(kHD));
+  a.work = g->d_work;
   a.err = g->d_err;
   prof_begin(st);
-  if (pl::launch_prefill_attention(a, g->tm_q16, g->tm_k_pf, g->tm_v_pf, st) != 0)
+  if (pl::launch_prefill_attention(a, g->tm_q16, g->tm_k_pf, g->tm_v_pf, g->num_sms, st) != 0)
     return PL_ECUDA;
   prof_end(st);
   count_launch();
