@@ -21,13 +21,15 @@
 //              K/V tiles of 128 cache rows through a kPfStages ring
 //   warp 9     TMEM allocator and the single MMA-issuing thread
 // Per KV tile j the MMA thread issues, in order,
-//   S_A(j) = Q_A K_j^T, S_B(j) = Q_B K_j^T     (M=128 N=128 K=64 -> TMEM)
-//   PV_A(j-1) = P_A V, PV_B(j-1) = P_B V       (M=128 N=64 K=128 -> TMEM O)
+//   S_A(j) = Q_A K_j^T, S_B(j) = Q_B K_j^T     (M=128 N=128 K=64, smem x smem -> TMEM)
+//   PV_A(j-1) = P_A V, PV_B(j-1) = P_B V       (M=128 N=64 K=128, TMEM x smem -> TMEM O)
 // so one slot's softmax overlaps the other slot's MMAs (ping-pong).  A
 // softmax thread loads its 128-column S row from TMEM once, takes the row
 // max (causal mask on diagonal tiles only), and writes P = 2^(s*c - m) as
-// FP16 straight into one of the slot's two shared-memory P tiles (SW128
-// K-major, the A operand of the PV MMA).  Three quarters of the 2^x go to
+// FP16 back into tensor memory (its own lane, two halves per 32-bit
+// column), where the PV MMA takes it as the A operand: P never touches
+// shared memory, whose bandwidth the S MMAs and the TMA ring need.  Three
+// quarters of the 2^x go to
 // the MUFU unit, one quarter to a cubic polynomial on the FMA pipe (see
 // exp2_poly2), which balances the two pipes.  O accumulates in TMEM; the
 // running max used for P is raised only when a row's max grows by more than
@@ -48,7 +50,7 @@ namespace pl {
 
 constexpr int kPfBlockM = 128;  // query rows per slot
 constexpr int kPfBlockN = 128;  // cache rows per KV tile
-constexpr int kPfStages = 2;    // K/V ring depth
+constexpr int kPfStages = 4;    // K/V ring depth
 constexpr int kPfThreads = 320;
 constexpr float kPfRescaleLog2 = 8.0f;  // raise the running max only past 2^8
 
@@ -67,7 +69,6 @@ struct PfSmem {
   uint8_t q[2][kPfBlockM * 128];                // Q_A, Q_B: 16 KB each
   uint8_t k[kPfStages][kPfBlockN * 128];        // 16 KB each
   uint8_t v[kPfStages][kPfBlockN * 128];        // 16 KB each
-  uint8_t p[2][2][2][kPfBlockM * 128];          // [slot][buffer][k-chunk of 64] 16 KB each
   uint64_t q_full, q_empty;
   uint64_t kv_full[kPfStages], kv_empty[kPfStages];
   uint64_t s_full[2], s_free[2], p_full[2][2], pv_done[2][2], o_free[2];
@@ -79,9 +80,11 @@ struct PfSmem {
 
 constexpr int kPfSmemBytes = static_cast<int>(sizeof(PfSmem)) + 1024;
 
-// TMEM column map (512 columns allocated): S_A, S_B, O_A, O_B
+// TMEM column map (512 columns allocated): S_A, S_B (128 FP32 columns
+// each), O_A, O_B (64 FP32), P_A, P_B (128 FP16 = 64 columns)
 __device__ __forceinline__ uint32_t pf_col_s(int x) { return x ? 128u : 0u; }
 __device__ __forceinline__ uint32_t pf_col_o(int x) { return x ? 320u : 256u; }
+__device__ __forceinline__ uint32_t pf_col_p(int x) { return x ? 448u : 384u; }
 
 __device__ __forceinline__ void tc_ld_x32(uint32_t taddr, uint32_t* r) {
   tc_ld_32x32b_x32(taddr, *reinterpret_cast<uint32_t(*)[32]>(r));
@@ -259,13 +262,11 @@ __global__ void __launch_bounds__(kPfThreads, 1)
           // the previous item's O must be read out before it is overwritten
           if (first && k >= 1 && !mbar_wait_bounded(&sm.o_free[x], (k - 1) & 1)) return false;
           tc_fence_after();
-          const uint32_t p_addr = smem_u32(sm.p[x][pb][0]);
 #pragma unroll
-          for (int kk = 0; kk < kPfBlockN / 16; ++kk) {
-            const uint64_t ad = smem_desc_sw128(
-                p_addr + (kk >> 2) * (kPfBlockM * 128) + (kk & 3) * 32, 16, 1024);
+          for (int kk = 0; kk < kPfBlockN / 16; ++kk) {  // 16 keys = 8 P columns per MMA
             const uint64_t bd = smem_desc_sw128(v_addr + kk * 16 * 128, 16, 1024);
-            tc_mma_ss(tmem + pf_col_o(x), ad, bd, idesc_pv, (first && kk == 0) ? 0u : 1u);
+            tc_mma_ts(tmem + pf_col_o(x), tmem + pf_col_p(x) + kk * 8, bd, idesc_pv,
+                      (first && kk == 0) ? 0u : 1u);
           }
           tc_commit(&sm.pv_done[x][pb]);
         }
@@ -365,7 +366,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
         const float m_tile = max3(max3(mp[0], mp[1], mp[2]), max3(mp[3], mp[4], mp[5]),
                                   fmaxf(mp[6], mp[7])) * sc;
         // lazy rescale: only when some row of the warp outgrew its max by 2^8
-        // (O itself is rescaled below, once this tile's P is written)
+        // (O itself is rescaled below, once PV(g-1) has landed in it)
         const bool rescale = __any_sync(0xffffffffu, m_tile > m_used + kPfRescaleLog2);
         float alpha = 1.f;
         if (rescale) {
@@ -374,57 +375,55 @@ __global__ void __launch_bounds__(kPfThreads, 1)
           l_run *= alpha;
           m_used = m_new;
         }
-        // this slot's P buffer g&1 was last read by PV(g-2)
-        if (g >= 2 && !mbar_wait_bounded(&sm.pv_done[x][g & 1], ((g - 2) >> 1) & 1)) {
-          ok = false;
-          break;
-        }
-        // P = 2^(s*c - m) as FP16 into the SW128 K-major P tile (masked -> 0)
-        uint8_t* pbuf = sm.p[x][g & 1][0];
+        // P = 2^(s*c - m) packed as FP16 pairs (masked -> 0), in two halves of
+        // 64 columns, each stored to TMEM as soon as it is ready
         const float2 sc2 = make_float2(sc, sc), nm2 = make_float2(-m_used, -m_used);
         float2 rs2[4];  // 4 independent partial row sums
 #pragma unroll
         for (int e = 0; e < 4; ++e) rs2[e] = make_float2(0.f, 0.f);
 #pragma unroll
-        for (int cc = 0; cc < 16; ++cc) {  // 16 chunks of 8 columns
-          uint32_t w4[4];
+        for (int h = 0; h < 2; ++h) {
+          uint32_t pw[32];
 #pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const int c = 8 * cc + 2 * e;
-            const float2 arg =
-                fma2(make_float2(__uint_as_float(sv[c]), __uint_as_float(sv[c + 1])), sc2, nm2);
-            // three pairs on MUFU, the fourth on the FMA pipe (-inf -> 0)
-            const float2 pp = e == 3 ? exp2_poly2(arg) : make_float2(ex2(arg.x), ex2(arg.y));
-            rs2[e] = add2(rs2[e], pp);
-            w4[e] = pack_half2(pp.x, pp.y);
+          for (int cc = 0; cc < 8; ++cc) {  // 8 chunks of 8 columns
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const int c = 64 * h + 8 * cc + 2 * e;
+              const float2 arg =
+                  fma2(make_float2(__uint_as_float(sv[c]), __uint_as_float(sv[c + 1])), sc2, nm2);
+              // three pairs on MUFU, the fourth on the FMA pipe (-inf -> 0)
+              const float2 pp = e == 3 ? exp2_poly2(arg) : make_float2(ex2(arg.x), ex2(arg.y));
+              rs2[e] = add2(rs2[e], pp);
+              pw[4 * cc + e] = pack_half2(pp.x, pp.y);
+            }
           }
-          const int kc = cc >> 3, c16 = cc & 7;
-          uint8_t* dst = pbuf + kc * (kPfBlockM * 128) + r * 128 + ((c16 ^ (r & 7)) << 4);
-          *reinterpret_cast<uint4*>(dst) = make_uint4(w4[0], w4[1], w4[2], w4[3]);
+          if (h == 0) {
+            // P(g) overwrites P(g-1) and O is rescaled: both need PV(g-1)
+            // done (PV(g) is issued only after p_full(g) below)
+            if (g >= 1 && !mbar_wait_bounded(&sm.pv_done[x][(g - 1) & 1], ((g - 1) >> 1) & 1)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            if (rescale && j >= 1) {
+#pragma unroll
+              for (int q4 = 0; q4 < 4; ++q4) {  // O in 4 chunks of 16 columns
+                uint32_t ov[16];
+                tc_ld_32x32b_x16(lane_base + pf_col_o(x) + 16 * q4, ov);
+                tc_wait_ld();
+#pragma unroll
+                for (int d = 0; d < 16; ++d) asm volatile("" : "+r"(ov[d]));
+#pragma unroll
+                for (int d = 0; d < 16; ++d) ov[d] = __float_as_uint(__uint_as_float(ov[d]) * alpha);
+                tc_st_32x32b_x16(lane_base + pf_col_o(x) + 16 * q4, ov);
+              }
+            }
+          }
+          tc_st_32x32b_x32(lane_base + pf_col_p(x) + 32 * h, pw);
         }
-        if (rescale && j >= 1) {
-          // every PV so far must have landed in O before it is rescaled; PV(g)
-          // is issued only after p_full(g) below
-          if (!mbar_wait_bounded(&sm.pv_done[x][(g - 1) & 1], ((g - 1) >> 1) & 1)) {
-            ok = false;
-            break;
-          }
-          tc_fence_after();
-#pragma unroll
-          for (int half = 0; half < 2; ++half) {
-            uint32_t* ov = sv + 32 * half;
-            tc_ld_x32(lane_base + pf_col_o(x) + 32 * half, ov);
-            tc_wait_ld();
-            reg_fence32(ov);
-#pragma unroll
-            for (int d = 0; d < 32; ++d) ov[d] = __float_as_uint(__uint_as_float(ov[d]) * alpha);
-            tc_st_32x32b_x32(lane_base + pf_col_o(x) + 32 * half,
-                             *reinterpret_cast<uint32_t(*)[32]>(ov));
-          }
-          tc_wait_st();
-          tc_fence_before();
-        }
-        fence_proxy_async_smem();
+        if (!ok) break;
+        tc_wait_st();
+        tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&sm.p_full[x][g & 1]);
         const float2 rsa = add2(rs2[0], rs2[1]), rsb = add2(rs2[2], rs2[3]);
