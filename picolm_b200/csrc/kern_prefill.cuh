@@ -13,17 +13,24 @@
 // first, and every pipeline below runs on across item boundaries (the next
 // item's Q and first K/V tiles load while the current one finishes).
 //
-// Warp roles (320 threads):
+// Warp roles (352 threads):
 //   warps 0-3  softmax of slot A; thread r owns query row r = TMEM lane r
 //   warps 4-7  softmax of slot B (same lanes, other TMEM columns)
 //   warp 8     scheduler + TMA producer: fetches items, publishes them in a
 //              two-entry shared-memory queue, loads Q_A/Q_B per item and
 //              K/V tiles of 128 cache rows through a kPfStages ring
-//   warp 9     TMEM allocator and the single MMA-issuing thread
-// Per KV tile j the MMA thread issues, in order,
-//   S_A(j) = Q_A K_j^T, S_B(j) = Q_B K_j^T     (M=128 N=128 K=64, smem x smem -> TMEM)
-//   PV_A(j-1) = P_A V, PV_B(j-1) = P_B V       (M=128 N=64 K=128, TMEM x smem -> TMEM O)
-// so one slot's softmax overlaps the other slot's MMAs (ping-pong).  A
+//   warp 9     TMEM allocator; MMA issuer of slot A
+//   warp 10    MMA issuer of slot B
+// Per KV tile j the issuer of slot x issues, in order,
+//   S_x(j) = Q_x K_j^T      (M=128 N=128 K=64, smem x smem -> TMEM)
+//   PV_x(j-1) = P_x V       (M=128 N=64 K=128, TMEM x smem -> TMEM O_x)
+// so one slot's softmax overlaps the other slot's MMAs (ping-pong).  Issue
+// of tcgen05.mma is close to synchronous with its execution, and every
+// mbarrier check in the issuing thread leaves the tensor pipe idle for
+// about a hundred cycles; with one issuer per slot, the other slot's MMAs
+// fill those gaps.  The slots touch disjoint TMEM columns, so the two
+// issuers need no ordering between them; a K/V stage is released when both
+// have committed their MMAs on it.  A
 // softmax thread loads its 128-column S row from TMEM once, takes the row
 // max (causal mask on diagonal tiles only), and writes P = 2^(s*c - m) as
 // FP16 back into tensor memory (its own lane, two halves per 32-bit
@@ -51,7 +58,7 @@ namespace pl {
 constexpr int kPfBlockM = 128;  // query rows per slot
 constexpr int kPfBlockN = 128;  // cache rows per KV tile
 constexpr int kPfStages = 4;    // K/V ring depth
-constexpr int kPfThreads = 320;
+constexpr int kPfThreads = 352;
 constexpr float kPfRescaleLog2 = 8.0f;  // raise the running max only past 2^8
 
 struct PrefillArgs {
@@ -73,7 +80,7 @@ struct PfSmem {
   uint64_t kv_full[kPfStages], kv_empty[kPfStages];
   uint64_t s_full[2], s_free[2], p_full[2][2], pv_done[2][2], o_free[2];
   uint64_t item_full[2], item_empty[2];
-  uint64_t mma_done;
+  uint64_t mma_done[2];
   int item[2];
   uint32_t tmem_base;
 };
@@ -110,7 +117,7 @@ __device__ __forceinline__ float2 exp2_poly2(float2 x) {
   x.y = fmaxf(x.y, -126.f);
   const float2 t = add2(x, make_float2(kMagic, kMagic));
   const float2 n = add2(t, make_float2(-kMagic, -kMagic));
-  const float2 f = add2(x, make_float2(-n.x, -n.y));
+  const float2 f = fma2(n, make_float2(-1.f, -1.f), x);  // x - n, exact
   float2 p = fma2(make_float2(kC3, kC3), f, make_float2(kC2, kC2));
   p = fma2(p, f, make_float2(kC1, kC1));
   p = fma2(p, f, make_float2(kC0, kC0));
@@ -163,10 +170,10 @@ __global__ void __launch_bounds__(kPfThreads, 1)
 
   if (threadIdx.x == 0) {
     mbar_init(&sm.q_full, 1);
-    mbar_init(&sm.q_empty, 1);
+    mbar_init(&sm.q_empty, n_slots);  // one commit per active issuer
     for (int s = 0; s < kPfStages; ++s) {
       mbar_init(&sm.kv_full[s], 1);
-      mbar_init(&sm.kv_empty[s], 1);
+      mbar_init(&sm.kv_empty[s], n_slots);
     }
     for (int x = 0; x < 2; ++x) {
       mbar_init(&sm.s_full[x], 1);
@@ -177,9 +184,9 @@ __global__ void __launch_bounds__(kPfThreads, 1)
         mbar_init(&sm.pv_done[x][b2], 1);
       }
       mbar_init(&sm.item_full[x], 1);
-      mbar_init(&sm.item_empty[x], 9);  // the MMA thread + 8 softmax warps
+      mbar_init(&sm.item_empty[x], 10);  // 2 MMA issuers + 8 softmax warps
+      mbar_init(&sm.mma_done[x], 1);
     }
-    mbar_init(&sm.mma_done, 1);
     fence_mbar_init();
   }
   if (warp == 9) {
@@ -246,30 +253,32 @@ __global__ void __launch_bounds__(kPfThreads, 1)
         __threadfence();
       }
     }
-  } else if (warp == 9) {
-    // ------------------------------------------------------------ MMA issuer
+  } else if (warp >= 9) {
+    // ------------------------------------------------- MMA issuer of slot x
+    const int x = warp - 9;
     if (lane == 0) {
       const uint32_t idesc_qk = idesc_f16_f32(128, 128, 0);
       const uint32_t idesc_pv = idesc_f16_f32(128, 64, 1);
+      const bool active = x < n_slots;
+      const uint32_t q_addr = smem_u32(sm.q[x]);
       int J = 0, k = 0;
       bool ok = true;
-      // PV of global tile g (first tile of its item if `first`)
+      // PV_x of global tile g (first tile of its item if `first`), then
+      // release of its K/V stage
       auto issue_pv = [&](int g, bool first) -> bool {
         const int s = g % kPfStages, pb = g & 1;
+        if (!mbar_wait_bounded(&sm.p_full[x][pb], (g >> 1) & 1)) return false;
+        // the previous item's O must be read out before it is overwritten
+        if (first && k >= 1 && !mbar_wait_bounded(&sm.o_free[x], (k - 1) & 1)) return false;
+        tc_fence_after();
         const uint32_t v_addr = smem_u32(sm.v[s]);
-        for (int x = 0; x < n_slots; ++x) {
-          if (!mbar_wait_bounded(&sm.p_full[x][pb], (g >> 1) & 1)) return false;
-          // the previous item's O must be read out before it is overwritten
-          if (first && k >= 1 && !mbar_wait_bounded(&sm.o_free[x], (k - 1) & 1)) return false;
-          tc_fence_after();
 #pragma unroll
-          for (int kk = 0; kk < kPfBlockN / 16; ++kk) {  // 16 keys = 8 P columns per MMA
-            const uint64_t bd = smem_desc_sw128(v_addr + kk * 16 * 128, 16, 1024);
-            tc_mma_ts(tmem + pf_col_o(x), tmem + pf_col_p(x) + kk * 8, bd, idesc_pv,
-                      (first && kk == 0) ? 0u : 1u);
-          }
-          tc_commit(&sm.pv_done[x][pb]);
+        for (int kk = 0; kk < kPfBlockN / 16; ++kk) {  // 16 keys = 8 P columns per MMA
+          const uint64_t bd = smem_desc_sw128(v_addr + kk * 16 * 128, 16, 1024);
+          tc_mma_ts(tmem + pf_col_o(x), tmem + pf_col_p(x) + kk * 8, bd, idesc_pv,
+                    (first && kk == 0) ? 0u : 1u);
         }
+        tc_commit(&sm.pv_done[x][pb]);
         tc_commit(&sm.kv_empty[s]);
         return true;
       };
@@ -279,26 +288,27 @@ __global__ void __launch_bounds__(kPfThreads, 1)
         mbar_arrive(&sm.item_empty[k & 1]);
         if (item < 0) break;
         const PfItem it = pf_item(a, item);
+        if (!active) {  // no second query head: nothing to issue
+          J += it.nkv;
+          ++k;
+          continue;
+        }
         if (!mbar_wait_bounded(&sm.q_full, k & 1)) { ok = false; break; }
         for (int j = 0; j < it.nkv && ok; ++j) {
           const int g = J + j;
           const int s = g % kPfStages;
           if (!mbar_wait_bounded(&sm.kv_full[s], (g / kPfStages) & 1)) { ok = false; break; }
+          if (g >= 1 && !mbar_wait_bounded(&sm.s_free[x], (g - 1) & 1)) { ok = false; break; }
+          tc_fence_after();
           const uint32_t k_addr = smem_u32(sm.k[s]);
-          for (int x = 0; x < n_slots; ++x) {
-            if (g >= 1 && !mbar_wait_bounded(&sm.s_free[x], (g - 1) & 1)) { ok = false; break; }
-            tc_fence_after();
-            const uint32_t q_addr = smem_u32(sm.q[x]);
 #pragma unroll
-            for (int kk = 0; kk < 4; ++kk) {
-              const uint64_t ad = smem_desc_sw128(q_addr + kk * 32, 16, 1024);
-              const uint64_t bd = smem_desc_sw128(k_addr + kk * 32, 16, 1024);
-              tc_mma_ss(tmem + pf_col_s(x), ad, bd, idesc_qk, kk > 0 ? 1u : 0u);
-            }
-            tc_commit(&sm.s_full[x]);
+          for (int kk = 0; kk < 4; ++kk) {
+            const uint64_t ad = smem_desc_sw128(q_addr + kk * 32, 16, 1024);
+            const uint64_t bd = smem_desc_sw128(k_addr + kk * 32, 16, 1024);
+            tc_mma_ss(tmem + pf_col_s(x), ad, bd, idesc_qk, kk > 0 ? 1u : 0u);
           }
-          if (!ok) break;
-          if (j == it.nkv - 1) tc_commit(&sm.q_empty);  // Q free once these S MMAs land
+          tc_commit(&sm.s_full[x]);
+          if (j == it.nkv - 1) tc_commit(&sm.q_empty);  // Q_x free once these S MMAs land
           if (j >= 1 && !issue_pv(g - 1, j == 1)) ok = false;
         }
         if (ok && !issue_pv(J + it.nkv - 1, it.nkv == 1)) ok = false;
@@ -307,8 +317,8 @@ __global__ void __launch_bounds__(kPfThreads, 1)
       }
       if (!ok) atomicOr(a.err, ERR_TIMEOUT_MMA);
       // all issued MMAs must finish before TMEM is freed
-      tc_commit(&sm.mma_done);
-      mbar_wait_bounded(&sm.mma_done, 0);
+      tc_commit(&sm.mma_done[x]);
+      mbar_wait_bounded(&sm.mma_done[x], 0);
     }
   } else {
     // ------------------------------------------------------------ softmax
