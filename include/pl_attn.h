@@ -133,7 +133,8 @@ int  pl_attn_decode_batch_dev(int layer, int n, const int *d_seqs,
                               const float *d_k, const float *d_v, float *d_out,
                               void *stream);
 
-/* pl_attn_prefill with device arrays. */
+/* pl_attn_prefill with device arrays.  d_q, d_k, d_v and d_out must be
+ * 16-byte aligned and out_stride a multiple of 4 (PL_EARG otherwise). */
 int  pl_attn_prefill_dev(int seq, int layer, int start_pos, int n_tok,
                          const float *d_q, const float *d_k, const float *d_v,
                          float *d_out, int out_stride, void *stream);

@@ -41,45 +41,130 @@ __global__ void rope_inplace_kernel(float* q, float* k, int n_heads, int n_kv_he
 //                                                     round-to-nearest-even)
 //   kc[start+r]   = picolm_FP16(RoPE(k[r]))          (bit-exact append)
 //   vc[start+r]   = picolm_FP16(v[r])
-// grid = ceil(n_tok / kPrologueRows), block = 256: each warp takes (row,
-// head) tasks of its block in turn, lane l the element pair 2l.
-constexpr int kPrologueRows = 4;
+// grid = n_tok (one block per token row), block = kPrologueThreads.  A row
+// is cut into units of 8 elements of one head (q heads, then k heads, then
+// v heads); thread t takes units t, t + 256, ...  LLaMA units are 8
+// consecutive elements (4 rotated pairs); Qwen units are elements 4c..4c+3
+// and 32+4c..32+4c+3, which rotate into each other.  Every input and all
+// RoPE factors of a unit are 16-byte loads, and a thread issues the loads of
+// two units before it computes either, so the kernel streams at HBM rate
+// instead of waiting on one load at a time.  q, k, v rows and the cache
+// rows must be 16-byte aligned.
+constexpr int kPrologueThreads = 256;
 
-__global__ void __launch_bounds__(256)
+struct PrologueUnit {
+  float4 xa, xb, c, s;  // inputs (xa: first 4, xb: second 4) and RoPE factors
+  int kind;             // 0 q, 1 k, 2 v, -1 none
+  int head, part;
+};
+
+__device__ __forceinline__ PrologueUnit prologue_load(int u, int r, const float* __restrict__ q,
+                                                      const float* __restrict__ k,
+                                                      const float* __restrict__ v, int n_heads,
+                                                      int n_kv_heads, const float* cs,
+                                                      const float* sn, int rope_type) {
+  PrologueUnit pu;
+  const int nq = n_heads * 8, nk = n_kv_heads * 8;
+  const int kv_dim = n_kv_heads * kHD;
+  const float* x;
+  if (u < nq) {
+    pu.kind = 0;
+    pu.head = u >> 3;
+    x = q + (static_cast<size_t>(r) * n_heads + pu.head) * kHD;
+  } else if (u < nq + nk) {
+    pu.kind = 1;
+    pu.head = (u - nq) >> 3;
+    x = k + static_cast<size_t>(r) * kv_dim + pu.head * kHD;
+  } else {
+    pu.kind = 2;
+    pu.head = (u - nq - nk) >> 3;
+    x = v + static_cast<size_t>(r) * kv_dim + pu.head * kHD;
+  }
+  pu.part = u & 7;
+  if (pu.kind == 2 || rope_type == 0) {
+    pu.xa = *reinterpret_cast<const float4*>(x + 8 * pu.part);
+    pu.xb = *reinterpret_cast<const float4*>(x + 8 * pu.part + 4);
+  } else {
+    pu.xa = *reinterpret_cast<const float4*>(x + 4 * pu.part);
+    pu.xb = *reinterpret_cast<const float4*>(x + kHD / 2 + 4 * pu.part);
+  }
+  if (pu.kind != 2) {
+    pu.c = *reinterpret_cast<const float4*>(cs + 4 * pu.part);
+    pu.s = *reinterpret_cast<const float4*>(sn + 4 * pu.part);
+  }
+  return pu;
+}
+
+// q goes to the tensor-core staging with round-to-nearest-even; k and v use
+// picolm's FP16 rounding (bit-exact cache rows).
+__device__ __forceinline__ uint32_t prologue_pack(float a, float b, bool picolm_rounding) {
+  if (!picolm_rounding) return pack_half2(a, b);
+  return static_cast<uint32_t>(picolm_f32_to_f16(a)) |
+         (static_cast<uint32_t>(picolm_f32_to_f16(b)) << 16);
+}
+
+__device__ __forceinline__ void prologue_store(const PrologueUnit& pu, int r, uint16_t* q16,
+                                               uint16_t* kc_rows, uint16_t* vc_rows, int n_heads,
+                                               int n_kv_heads, int rope_type) {
+  const int kv_dim = n_kv_heads * kHD;
+  uint16_t* dst;
+  if (pu.kind == 0)
+    dst = q16 + (static_cast<size_t>(r) * n_heads + pu.head) * kHD;
+  else
+    dst = (pu.kind == 1 ? kc_rows : vc_rows) + static_cast<size_t>(r) * kv_dim + pu.head * kHD;
+  const bool pr = pu.kind != 0;
+  if (pu.kind == 2) {
+    *reinterpret_cast<uint4*>(dst + 8 * pu.part) =
+        make_uint4(prologue_pack(pu.xa.x, pu.xa.y, true), prologue_pack(pu.xa.z, pu.xa.w, true),
+                   prologue_pack(pu.xb.x, pu.xb.y, true), prologue_pack(pu.xb.z, pu.xb.w, true));
+  } else if (rope_type == 0) {
+    float y[8];
+    rope_pair(pu.xa.x, pu.xa.y, pu.c.x, pu.s.x, y[0], y[1]);
+    rope_pair(pu.xa.z, pu.xa.w, pu.c.y, pu.s.y, y[2], y[3]);
+    rope_pair(pu.xb.x, pu.xb.y, pu.c.z, pu.s.z, y[4], y[5]);
+    rope_pair(pu.xb.z, pu.xb.w, pu.c.w, pu.s.w, y[6], y[7]);
+    *reinterpret_cast<uint4*>(dst + 8 * pu.part) =
+        make_uint4(prologue_pack(y[0], y[1], pr), prologue_pack(y[2], y[3], pr),
+                   prologue_pack(y[4], y[5], pr), prologue_pack(y[6], y[7], pr));
+  } else {
+    // Qwen: element j (< 32) and j + 32 rotate together
+    const float xa[4] = {pu.xa.x, pu.xa.y, pu.xa.z, pu.xa.w};
+    const float xb[4] = {pu.xb.x, pu.xb.y, pu.xb.z, pu.xb.w};
+    const float c[4] = {pu.c.x, pu.c.y, pu.c.z, pu.c.w};
+    const float sv[4] = {pu.s.x, pu.s.y, pu.s.z, pu.s.w};
+    float lo[4], hi[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      lo[i] = __fsub_rn(__fmul_rn(xa[i], c[i]), __fmul_rn(xb[i], sv[i]));
+      hi[i] = __fadd_rn(__fmul_rn(xa[i], sv[i]), __fmul_rn(xb[i], c[i]));
+    }
+    *reinterpret_cast<uint2*>(dst + 4 * pu.part) =
+        make_uint2(prologue_pack(lo[0], lo[1], pr), prologue_pack(lo[2], lo[3], pr));
+    *reinterpret_cast<uint2*>(dst + kHD / 2 + 4 * pu.part) =
+        make_uint2(prologue_pack(hi[0], hi[1], pr), prologue_pack(hi[2], hi[3], pr));
+  }
+}
+
+__global__ void __launch_bounds__(kPrologueThreads)
     prefill_prologue_kernel(const float* __restrict__ q, const float* __restrict__ k,
                             const float* __restrict__ v, uint16_t* __restrict__ q16,
                             uint16_t* __restrict__ kc_rows, uint16_t* __restrict__ vc_rows,
                             int n_tok, int n_heads, int n_kv_heads, int start_pos,
                             const float* cos_tab, const float* sin_tab, int rope_type) {
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int heads = n_heads + n_kv_heads;
-  const int kv_dim = n_kv_heads * kHD;
-  const int r0 = blockIdx.x * kPrologueRows;
-  for (int task = warp; task < kPrologueRows * heads; task += 8) {
-    const int r = r0 + task / heads, head = task % heads;
-    if (r >= n_tok) break;
-    const int pos = start_pos + r;
-    const float* cs = cos_tab + static_cast<size_t>(pos) * (kHD / 2);
-    const float* sn = sin_tab + static_cast<size_t>(pos) * (kHD / 2);
-    if (head < n_heads) {
-      const float* x = q + (static_cast<size_t>(r) * n_heads + head) * kHD;
-      const float2 y = rope_two(x, 2 * lane, cs, sn, rope_type);
-      reinterpret_cast<uint32_t*>(q16 + (static_cast<size_t>(r) * n_heads + head) * kHD)[lane] =
-          pack_half2(y.x, y.y);
-    } else {
-      const int hk = head - n_heads;
-      const float* x = k + static_cast<size_t>(r) * kv_dim + hk * kHD;
-      const float2 y = rope_two(x, 2 * lane, cs, sn, rope_type);
-      const float2 vv = *reinterpret_cast<const float2*>(v + static_cast<size_t>(r) * kv_dim +
-                                                         hk * kHD + 2 * lane);
-      const size_t off = static_cast<size_t>(r) * kv_dim + hk * kHD;
-      reinterpret_cast<uint32_t*>(kc_rows + off)[lane] =
-          static_cast<uint32_t>(picolm_f32_to_f16(y.x)) |
-          (static_cast<uint32_t>(picolm_f32_to_f16(y.y)) << 16);
-      reinterpret_cast<uint32_t*>(vc_rows + off)[lane] =
-          static_cast<uint32_t>(picolm_f32_to_f16(vv.x)) |
-          (static_cast<uint32_t>(picolm_f32_to_f16(vv.y)) << 16);
-    }
+  const int r = blockIdx.x;
+  if (r >= n_tok) return;
+  const int pos = start_pos + r;
+  const float* cs = cos_tab + static_cast<size_t>(pos) * (kHD / 2);
+  const float* sn = sin_tab + static_cast<size_t>(pos) * (kHD / 2);
+  const int n_units = (n_heads + 2 * n_kv_heads) * 8;
+  for (int u = threadIdx.x; u < n_units; u += 2 * kPrologueThreads) {
+    const int u2 = u + kPrologueThreads;
+    const PrologueUnit a = prologue_load(u, r, q, k, v, n_heads, n_kv_heads, cs, sn, rope_type);
+    PrologueUnit b;
+    b.kind = -1;
+    if (u2 < n_units) b = prologue_load(u2, r, q, k, v, n_heads, n_kv_heads, cs, sn, rope_type);
+    prologue_store(a, r, q16, kc_rows, vc_rows, n_heads, n_kv_heads, rope_type);
+    if (b.kind >= 0) prologue_store(b, r, q16, kc_rows, vc_rows, n_heads, n_kv_heads, rope_type);
   }
 }
 

@@ -721,14 +721,15 @@ int pl_attn_kv_ptr(int seq, int layer, uint16_t** d_k, uint16_t** d_v) {
 }
 
 // ---------------------------------------------------------------- prefill
+static bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
 static int launch_prefill(int seq, int layer, int start_pos, int n_tok, const float* d_q,
                           const float* d_k, const float* d_v, float* d_out, int out_stride,
                           cudaStream_t st) {
   int rc = ensure_q16(n_tok);
   if (rc) return rc;
   const size_t off = static_cast<size_t>(start_pos) * g->kv_dim;
-  const int pgrid = (n_tok + pl::kPrologueRows - 1) / pl::kPrologueRows;
-  pl::prefill_prologue_kernel<<<pgrid, 256, 0, st>>>(
+  pl::prefill_prologue_kernel<<<n_tok, pl::kPrologueThreads, 0, st>>>(
       d_q, d_k, d_v, g->d_q16, slab_k(seq, layer) + off, slab_v(seq, layer) + off, n_tok,
       g->n_heads, g->n_kv_heads, start_pos, g->d_cos, g->d_sin, g->rope_type);
   PL_CUDA(cudaGetLastError());
@@ -804,6 +805,15 @@ int pl_attn_prefill_dev(int seq, int layer, int start_pos, int n_tok, const floa
   if (n_tok <= 0 || start_pos < 0 || start_pos + n_tok > g->max_seq || !d_q || !d_k || !d_v ||
       !d_out || out_stride < g->q_dim)
     return PL_EARG;
+  // the prologue reads q, k, v and the attention kernel writes out rows in
+  // 16-byte vectors
+  if (!aligned16(d_q) || !aligned16(d_k) || !aligned16(d_v) || !aligned16(d_out) ||
+      out_stride % 4 != 0) {
+    std::fprintf(stderr,
+                 "pl_attn_prefill_dev: q, k, v and out must be 16-byte aligned and out_stride a "
+                 "multiple of 4\n");
+    return PL_EARG;
+  }
   return launch_prefill(seq, layer, start_pos, n_tok, d_q, d_k, d_v, d_out, out_stride,
                         pick_stream(stream));
 }
