@@ -376,7 +376,7 @@ def run_prefill(args, local, peaks):
                         "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
                         "frac": tflops_kernel / peaks["bf16_tflops"],
                         "peak_source": peaks["source"] + " (bf16 dense burst; fp16 taken equal)",
-                        "traffic": profile_traffic("prefill_kernel_config3.txt"),
+                        "traffic": profile_traffic("prefill_attn_kernel_config3.txt"),
                         "kernel": "pl::prefill_attn_kernel (tcgen05, TMEM accumulators, TMA)",
                         "flops_per_launch": flops_layer},
            "gpu_launches": n_all}
