@@ -450,6 +450,70 @@ def run_long_ctx(args, local, peaks):
                                    "32768 cached + 32 steps, KV N(0,1) seed 4"}}
 
 
+def run_long_ctx_split(args, rank, world, local, peaks):
+    """Config 5 split along the KV axis over `world` GPUs: rank r holds a
+    contiguous 1/world of the 32768 cached positions (the last rank also the
+    appended ones); per layer and step each rank computes its partial
+    (m, l, o), NCCL all-gathers the partials and merges them
+    (picolm_b200/shard.py).  Timed on every rank, max over ranks."""
+    import torch
+    import picolm_b200 as pb
+    from picolm_b200.shard import PART_STRIDE, AttnShardOps, KVSplitDecoder
+    L, HK5, CTX5, NS5 = 16, 8, 32768, 32
+    kv5 = HK5 * HD
+    dev = torch.device("cuda", local)
+    # the RoPE tables are indexed by global position, so every rank's
+    # context spans all positions; only its shard's rows are filled
+    at = pb.Attn(L, H, HK5, CTX5 + NS5, rope_base=500000.0, device=local)
+    stream = torch.cuda.current_stream(dev)
+    dec = KVSplitDecoder(rank=rank, world=world, n_cached=CTX5,
+                         ops=AttnShardOps(at, stream.cuda_stream))
+    rng = np.random.default_rng(4)
+    for l in range(L):
+        kc = make_cache_host(rng, CTX5, kv5)
+        vc = make_cache_host(rng, CTX5, kv5)
+        if dec.n_rows:
+            at.kv_upload(0, l, 0, np.ascontiguousarray(kc[dec.row0:dec.row0 + dec.n_rows]),
+                         np.ascontiguousarray(vc[dec.row0:dec.row0 + dec.n_rows]))
+    gen = torch.Generator(device=dev).manual_seed(4)
+    q = torch.randn(NS5, L, Q_DIM, device=dev, generator=gen)
+    k = torch.randn(NS5, L, kv5, device=dev, generator=gen)
+    v = torch.randn(NS5, L, kv5, device=dev, generator=gen)
+    out = torch.empty(L, Q_DIM, device=dev)
+    part = torch.empty(H * PART_STRIDE, device=dev)
+    parts_all = torch.empty(world * H * PART_STRIDE, device=dev)
+
+    def step(s):
+        for l in range(L):
+            dec.step(l, CTX5 + s, q[s, l], k[s, l], v[s, l], part, parts_all, out[l])
+
+    # the first step appends position CTX5; re-running a step rewrites the
+    # same row with the same values, so the warm-up reuses step 0
+    step(0)
+    torch.cuda.synchronize()
+    barrier(world)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    nbytes = 0
+    for s in range(NS5):
+        step(s)
+        nbytes += L * ((CTX5 + s + 1) * kv5 * 4 + Q_DIM * 8 + kv5 * 12)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ms = max_over_ranks(e0.elapsed_time(e1), world)
+    barrier(world)
+    at.close()
+    return {"metric": f"long-context decode-attn HBM GB/s (config 5, KV split over {world} GPUs)",
+            "value": nbytes / (ms / 1e3) / 1e9, "unit": "GB/s",
+            "pct_peak_per_gpu": 100.0 * nbytes / (ms / 1e3) / 1e9 / world / peaks["hbm_gbs"],
+            "tok_per_s": NS5 / (ms / 1e3), "ms_per_step_16_layers": ms / NS5,
+            "scaling": "strong", "collective": "NCCL all_gather of 32 x 68 FP32 partials per "
+                                             "layer, then LSE combine on every rank",
+            "config": {"workload": "config5 16 layers, 32/8 heads, hd 64, theta 5e5, "
+                                   "32768 cached + 32 steps, KV N(0,1) seed 4",
+                       "shard": f"{dec.n_rows} cached positions on rank {rank}"}}
+
+
 def run_decode1(local):
     """Config 1: one TinyLlama decode layer at position 255 (latency)."""
     import picolm_b200 as pb
@@ -517,6 +581,13 @@ def main():
         build.build()
     barrier(world)
     peaks = load_peaks()
+    if args.workload == "long_ctx" and world > 1:
+        r = run_long_ctx_split(args, rank, world, local, peaks)
+        if rank == 0:
+            print(json.dumps(r), flush=True)
+        import torch.distributed as dist
+        dist.destroy_process_group()
+        return
     if args.workload in ("prefill", "long_ctx", "decode1"):
         if rank == 0:
             fn = {"prefill": lambda: run_prefill(args, local, peaks),
@@ -530,6 +601,8 @@ def main():
                  "tok_per_s": res["tok_per_s"], "pct_peak": res["pct_peak"],
                  "roofline": res["roofline"], "e2e": res["e2e"],
                  "gpu_launches": res["gpu_launches"], "clocks": res["clocks"]})
+    if world > 1 and args.workload == "all":
+        line["long_ctx_split"] = run_long_ctx_split(args, rank, world, local, peaks)
     if world == 1 and args.workload == "all":
         line["prefill"] = run_prefill(args, local, peaks)
         line["long_ctx"] = run_long_ctx(args, local, peaks)

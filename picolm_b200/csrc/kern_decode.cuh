@@ -70,8 +70,9 @@ struct DecodeArgs {
   uint16_t* vc;
   // per-launch inputs
   int n;                 // sequences in this launch (<= kMaxLaunchSeqs)
-  const int* seqs;       // cache slot per sequence
-  const int* pos;        // global position of the new token
+  const int* seqs;       // cache slot per sequence (nullptr: seq1 for all)
+  const int* pos;        // global position of the new token (nullptr: pos1)
+  int seq1, pos1;        // scalar slot / position when the arrays are null
   const float* q;        // [n][n_heads*64]   before RoPE
   const float* k;        // [n][kv_dim]       before RoPE
   const float* v;        // [n][kv_dim]
@@ -143,10 +144,17 @@ struct Partition {
   __device__ __forceinline__ int slot(int i, int j) const { return cta_of(prefix[i]) + j + i; }
 };
 
+__device__ __forceinline__ int seq_of(const DecodeArgs& a, int i) {
+  return a.seqs ? a.seqs[i] : a.seq1;
+}
+__device__ __forceinline__ int pos_of(const DecodeArgs& a, int i) {
+  return a.pos ? a.pos[i] : a.pos1;
+}
+
 // Rows attended and the append row of sequence i.
 __device__ __forceinline__ void seq_rows(const DecodeArgs& a, int i, int& att_rows,
                                          int& app_row) {
-  const int pos = a.pos[i];
+  const int pos = pos_of(a, i);
   att_rows = a.mode == 0 ? pos + 1 : a.n_rows;
   app_row = a.mode == 0 ? pos : (a.append ? pos - a.row0 : -1);
 }
@@ -242,10 +250,10 @@ __device__ __forceinline__ void consume_segment(const DecodeArgs& a, int w, int 
   const int kv_mul = a.kv_mul;
   const bool row_valid = g < kv_mul;
   const int qh = w * kv_mul + (row_valid ? g : 0);
-  const int pos = a.pos[i];
+  const int pos = pos_of(a, i);
   int att_rows, app_row;
   seq_rows(a, i, att_rows, app_row);
-  const int slab = a.seqs[i] * a.n_layers + a.layer;
+  const int slab = seq_of(a, i) * a.n_layers + a.layer;
   const float* cs = a.cos_tab + static_cast<size_t>(pos) * (kHD / 2);
   const float* sn = a.sin_tab + static_cast<size_t>(pos) * (kHD / 2);
   const bool appends = app_row >= t_lo * TP && app_row < t_hi * TP;
@@ -430,7 +438,7 @@ __global__ void __launch_bounds__(288) decode_kernel(const DecodeArgs a,
     for (int i = i0; i < min(n, i0 + per); ++i) {
       int att_rows, app_row;
       seq_rows(a, i, att_rows, app_row);
-      const int seq = a.seqs[i], pos = a.pos[i];
+      const int seq = seq_of(a, i), pos = pos_of(a, i);
       const bool bad = seq < 0 || seq >= a.n_slots || pos < 0 || pos >= a.max_seq ||
                        att_rows < 0 || att_rows > a.max_seq || app_row >= a.max_seq;
       if (bad && blockIdx.x == 0) atomicOr(a.err, ERR_BAD_ARG);
@@ -518,7 +526,7 @@ __global__ void __launch_bounds__(288) decode_kernel(const DecodeArgs a,
         }
         mbar_arrive_expect_tx(&full[s], 2u * tile_bytes);
         const int row = static_cast<int>(x - s_prefix[i]) * TP;
-        const int slab = a.seqs[i] * a.n_layers + a.layer;
+        const int slab = seq_of(a, i) * a.n_layers + a.layer;
         tma_load_4d(sK + s * tile_bytes, &tmk, &full[s], 0, row, 0, slab);
         tma_load_4d(sV + s * tile_bytes, &tmv, &full[s], 0, row, 0, slab);
         ++issued;

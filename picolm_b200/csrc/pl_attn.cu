@@ -235,6 +235,8 @@ pl::DecodeArgs decode_args(int layer, int n, const int* d_seqs, const int* d_pos
   a.n = n;
   a.seqs = d_seqs;
   a.pos = d_pos;
+  a.seq1 = 0;
+  a.pos1 = 0;
   a.q = d_q;
   a.k = d_k;
   a.v = d_v;
@@ -282,9 +284,6 @@ int launch_decode_tp(const pl::DecodeArgs& a, int grid, cudaStream_t st, bool pr
   return PL_OK;
 }
 
-// The split merge, queued behind the decode grid with programmatic stream
-// serialisation: its CTAs become resident while the decode grid runs and
-// wait on griddepcontrol.wait (grid = sequences x head groups).
 // The split merge, queued behind the decode grid with programmatic stream
 // serialisation (its CTAs become resident while the decode grid runs and
 // wait on griddepcontrol.wait).  Heads per block: as many as keep about one
@@ -630,11 +629,7 @@ int pl_attn_decode_partial_dev(int seq, int layer, int pos, int row0, int n_rows
   if (append && (pos - row0 < 0 || pos - row0 >= n_rows || !d_k || !d_v)) return PL_EARG;
   // the RoPE table must cover the global position
   if (pos >= g->max_seq) return PL_EARG;
-  // seq and pos as one-element device arrays in the error-word page
-  int* d_ints = reinterpret_cast<int*>(g->d_err) + 16;
-  const int hv[2] = {seq, pos};
   cudaStream_t st = pick_stream(stream);
-  PL_CUDA(cudaMemcpyAsync(d_ints, hv, sizeof hv, cudaMemcpyHostToDevice, st));
   if (n_rows == 0) {
     // an empty shard contributes nothing: m = -inf, l = 0, o = 0
     std::vector<float> empty(static_cast<size_t>(g->n_heads) * kPartStride, 0.f);
@@ -643,8 +638,17 @@ int pl_attn_decode_partial_dev(int seq, int layer, int pos, int row0, int n_rows
                             cudaMemcpyHostToDevice, st));
     return PL_OK;
   }
-  return launch_decode(layer, 1, d_ints, d_ints + 1, n_rows, d_q, d_k ? d_k : d_q,
-                       d_v ? d_v : d_q, nullptr, 1, row0, n_rows, append ? 1 : 0, d_part, st);
+  // seq and pos travel as kernel arguments (no copy, nothing that could
+  // make the host wait for the stream)
+  const int grid = decode_grid(1, n_rows);
+  int rc2 = ensure_part(static_cast<size_t>(grid + 1) * g->n_heads * kPartStride);
+  if (rc2) return rc2;
+  pl::DecodeArgs a = decode_args(layer, 1, nullptr, nullptr, d_q, d_k ? d_k : d_q,
+                                 d_v ? d_v : d_q, nullptr, 1, row0, n_rows, append ? 1 : 0,
+                                 d_part, g->d_part, g->d_seg_info);
+  a.seq1 = seq;
+  a.pos1 = pos;
+  return launch_decode_kernel(a, grid, st, true);
 }
 
 int pl_attn_combine_dev(int n_part, const float* d_parts, float* d_out, void* stream) {
