@@ -1,0 +1,105 @@
+/* e2e_harness.c -- greedy-decoding driver for the end-to-end check (config 2).
+ *
+ * Test infrastructure.  It stands in for picolm's main (picolm.c:91-318)
+ * without the tokenizer: it loads a GGUF file with picolm's model_load,
+ * feeds a prompt of random token ids through model_forward_prefill, then
+ * generates greedily with model_forward, taking the argmax of the logits as
+ * sampler_sample does at temperature 0 (sampler.c:43-51).  The same source
+ * is linked twice: with picolm's unmodified model.c (the CPU reference), and
+ * with the copy of model.c whose attention blocks call the B200 module
+ * (built with -DUSE_PL_ATTN).  Each generated token is printed with the
+ * margin between the best and the second-best logit.
+ *
+ * usage: e2e MODEL.gguf N_PROMPT N_GEN SEED THREADS
+ */
+#include <stdint.h>
+#include <stdio.h>
+#include <stdlib.h>
+#include <time.h>
+
+#include "model.h"
+#include "tensor.h"
+#ifdef USE_PL_ATTN
+#include "pl_attn.h"
+#endif
+
+static uint64_t splitmix64(uint64_t *s) {
+    uint64_t z = (*s += 0x9E3779B97F4A7C15ull);
+    z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+    z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+    return z ^ (z >> 31);
+}
+
+static double now_s(void) {
+    struct timespec ts;
+    clock_gettime(CLOCK_MONOTONIC, &ts);
+    return (double)ts.tv_sec + 1e-9 * (double)ts.tv_nsec;
+}
+
+int main(int argc, char **argv) {
+    if (argc != 6) {
+        fprintf(stderr, "usage: %s MODEL.gguf N_PROMPT N_GEN SEED THREADS\n", argv[0]);
+        return 2;
+    }
+    const char *path = argv[1];
+    const int n_prompt = atoi(argv[2]), n_gen = atoi(argv[3]), threads = atoi(argv[5]);
+    uint64_t seed = (uint64_t)strtoull(argv[4], NULL, 10);
+    tensor_set_threads(threads);
+
+    model_t model;
+    if (model_load(&model, path, 0) != 0) {
+        fprintf(stderr, "model_load failed\n");
+        return 1;
+    }
+    const model_config_t *c = &model.config;
+    if (n_prompt < 1 || n_gen < 1 || n_prompt + n_gen > c->max_seq_len) {
+        fprintf(stderr, "prompt + generation exceeds the context (%d)\n", c->max_seq_len);
+        return 2;
+    }
+#ifdef USE_PL_ATTN
+    int rc = pl_attn_init(c->n_layers, c->n_heads, c->n_kv_heads, c->head_dim, c->max_seq_len,
+                          c->rope_freq_base, c->rope_type, 1, 0);
+    if (rc == PL_OK)
+        rc = pl_attn_set_rope(model.state.rope_cos, model.state.rope_sin, c->max_seq_len,
+                              c->head_dim / 2);
+    if (rc != PL_OK) {
+        fprintf(stderr, "pl_attn: %s\n", pl_attn_strerror(rc));
+        return 1;
+    }
+#endif
+    int *prompt = (int *)malloc((size_t)n_prompt * sizeof(int));
+    for (int i = 0; i < n_prompt; i++)
+        prompt[i] = 3 + (int)(splitmix64(&seed) % (uint64_t)(c->vocab_size - 3));
+
+    const double t0 = now_s();
+    model_forward_prefill(&model, prompt, n_prompt, 0);
+    const double t1 = now_s();
+    const float *logits = model.state.logits;
+    int pos = n_prompt - 1;
+    for (int i = 0; i < n_gen; i++) {
+        int best = 0, second = -1;
+        for (int v = 1; v < c->vocab_size; v++) {
+            if (logits[v] > logits[best]) {
+                second = best;
+                best = v;
+            } else if (second < 0 || logits[v] > logits[second]) {
+                second = v;
+            }
+        }
+        printf("T %d %d %.9g\n", i, best, (double)(logits[best] - logits[second]));
+        if (i + 1 < n_gen) {
+            pos++;
+            logits = model_forward(&model, best, pos);
+        }
+    }
+    const double t2 = now_s();
+    printf("S prefill_tokens=%d prefill_s=%.6f decode_tokens=%d decode_s=%.6f threads=%d\n",
+           n_prompt, t1 - t0, n_gen - 1, t2 - t1, threads);
+    fflush(stdout);
+#ifdef USE_PL_ATTN
+    pl_attn_shutdown();
+#endif
+    free(prompt);
+    model_free(&model);
+    return 0;
+}

@@ -1,0 +1,94 @@
+"""Build step: a copy of picolm's model.c whose attention calls the B200 module.
+
+Test infrastructure for the end-to-end check.  Reads REF/model.c, finds the
+two attention blocks by their text (not by line number, so a different
+reference revision fails loudly instead of being mis-patched) and writes
+the copy with each block replaced by one C-ABI call:
+
+* decode (model.c:820-892): from the RoPE call `rope(s->q, k_tmp, ...)`
+  through the end of the online-softmax loop, up to `/* Output projection */`
+  -> pl_attn_decode(0, l, pos, s->q, k_tmp, v_tmp, s->xb);
+* prefill (model.c:1019-1090): the per-position QK-norm / RoPE / KV store /
+  attention loop, up to `/* f. Batch output projection */`
+  -> the QK-norm (Qwen3 only) on the host, then
+     pl_attn_prefill(0, l, start_pos, n_tokens, q_batch, k_batch, v_batch,
+                     xb_batch, dim).
+A failing call prints pl_attn_strerror and exits: there is no CPU fallback.
+The copy is written to a temporary directory by the oracle Makefile and
+deleted after compiling.
+
+usage: python pl_model_patch.py REF/model.c OUT/model_pl.c
+"""
+import sys
+
+DECODE_CALL = """\
+        /* RoPE, FP16 KV append and attention of this token on the B200 */
+        {
+            int pl_rc = pl_attn_decode(0, l, pos, s->q, k_tmp, v_tmp, s->xb);
+            if (pl_rc != PL_OK) {
+                fprintf(stderr, "pl_attn_decode: %s\\n", pl_attn_strerror(pl_rc));
+                exit(1);
+            }
+        }
+"""
+
+PREFILL_CALL = """\
+        /* e. QK-norm (Qwen3) on the host, then RoPE, KV append and causal
+         *    attention of all positions on the B200 */
+        if (lw->attn_q_norm) {
+            for (int bi = 0; bi < n_tokens; bi++) {
+                float *qb = q_batch + bi * q_dim, *kb = k_batch + bi * kv_dim;
+                for (int h = 0; h < n_heads; h++)
+                    rmsnorm(qb + h * head_dim, qb + h * head_dim,
+                            s->attn_q_norm_w[l], head_dim, c->rms_norm_eps);
+                for (int h = 0; h < n_kv_heads; h++)
+                    rmsnorm(kb + h * head_dim, kb + h * head_dim,
+                            s->attn_k_norm_w[l], head_dim, c->rms_norm_eps);
+            }
+        }
+        {
+            int pl_rc = pl_attn_prefill(0, l, start_pos, n_tokens, q_batch, k_batch,
+                                        v_batch, xb_batch, dim);
+            if (pl_rc != PL_OK) {
+                fprintf(stderr, "pl_attn_prefill: %s\\n", pl_attn_strerror(pl_rc));
+                exit(1);
+            }
+        }
+
+"""
+
+
+def find(lines, pred, start=0):
+    for i in range(start, len(lines)):
+        if pred(lines[i]):
+            return i
+    raise SystemExit(f"pl_model_patch: anchor not found after line {start + 1}")
+
+
+def main():
+    src, dst = sys.argv[1], sys.argv[2]
+    lines = open(src).read().split("\n")
+
+    ds = find(lines, lambda s: "rope(s->q, k_tmp," in s)
+    de = find(lines, lambda s: s.strip() == "/* Output projection */", ds)
+    block = "\n".join(lines[ds:de])
+    for must in ("fp32_to_fp16(k_tmp[d])", "Flash Attention", "acc[d] * inv_sum"):
+        if must not in block:
+            raise SystemExit(f"pl_model_patch: decode block does not contain {must!r}")
+
+    ps = find(lines, lambda s: s.strip().startswith("/* e. Per-position: QK-norm, RoPE, KV store"), de)
+    pe = find(lines, lambda s: s.strip() == "/* f. Batch output projection */", ps)
+    block = "\n".join(lines[ps:pe])
+    for must in ("rope(q_pos, k_pos", "fp32_to_fp16(k_pos[d])", "xb_batch + bi * dim"):
+        if must not in block:
+            raise SystemExit(f"pl_model_patch: prefill block does not contain {must!r}")
+
+    inc = find(lines, lambda s: s.strip() == '#include "model.h"')
+    out = (lines[:inc + 1] + ['#include "pl_attn.h"'] + lines[inc + 1:ds]
+           + DECODE_CALL.split("\n") + lines[de:ps] + PREFILL_CALL.split("\n") + lines[pe:])
+    with open(dst, "w") as f:
+        f.write("\n".join(out))
+
+
+if __name__ == "__main__":
+    main()

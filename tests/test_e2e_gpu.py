@@ -1,0 +1,61 @@
+"""End to end: picolm's greedy decoding with attention on the B200 (config 2).
+
+The same driver (oracle/e2e_harness.c) is linked with picolm's own model.c
+and with the copy whose attention blocks call this module.  On the same
+random-init Q4_K model and prompt, the generated token ids must be
+identical: every next-token argmax agrees.  A failure reports the first
+divergent step and the top-2 logit margin there.
+
+The full config-2 shape (22 layers, dim 2048, 128 + 128 tokens, ~620 MB
+model) takes minutes of CPU time for the matmuls and runs only when
+PL_E2E_FULL=1; its timings go to the JSON file named by PL_E2E_OUT.
+"""
+import json
+import os
+
+import pytest
+
+from oracle.make_gguf import make_model
+from tests import e2e_util as E
+
+pytestmark = pytest.mark.gpu
+
+
+def _need_binaries():
+    if not (E.have(E.E2E_REF) and E.have(E.E2E_PL)):
+        pytest.skip("oracle/_ref/e2e_ref / e2e_pl not built (make -C oracle e2e)")
+
+
+def _compare(gguf, n_prompt, n_gen, threads):
+    ref = E.run(E.E2E_REF, gguf, n_prompt, n_gen, threads=threads)
+    ours = E.run(E.E2E_PL, gguf, n_prompt, n_gen, threads=threads)
+    d = E.first_divergence(ref[0], ours[0])
+    assert d is None, (f"greedy tokens diverge at step {d}: reference {ref[0][d]} "
+                       f"(margin {ref[1][d]:.3g}), B200 attention {ours[0][d]} "
+                       f"(margin {ours[1][d]:.3g})")
+    return ref, ours
+
+
+def test_greedy_tokens_identical_small_model(tmp_path):
+    _need_binaries()
+    path = str(tmp_path / "small.gguf")
+    # 4 layers, 8 query / 2 KV heads of 64: the GQA shape of the configs
+    make_model(path, layers=4, dim=512, ffn=1024, heads=8, kv_heads=2, vocab=2000, ctx=512)
+    ref, ours = _compare(path, 96, 48, threads=4)
+    assert len(ours[0]) == 48
+
+
+def test_greedy_tokens_identical_config2_full(tmp_path):
+    if os.environ.get("PL_E2E_FULL") != "1":
+        pytest.skip("full config 2 runs with PL_E2E_FULL=1 (minutes of CPU matmuls)")
+    _need_binaries()
+    path = str(tmp_path / "tinyllama_q4k.gguf")
+    make_model(path)  # 22 layers, dim 2048, ffn 5632, 32/4 heads, vocab 32000, seed 1
+    threads = min(16, os.cpu_count() or 1)
+    ref, ours = _compare(path, 128, 128, threads=threads)
+    out = os.environ.get("PL_E2E_OUT")
+    if out:
+        with open(out, "w") as f:
+            json.dump({"threads": threads, "tokens_identical": len(ours[0]),
+                       "min_margin": min(ref[1]), "reference": ref[2], "b200_attention": ours[2],
+                       "first_tokens": ours[0][:16]}, f, indent=1)
