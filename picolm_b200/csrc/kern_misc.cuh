@@ -151,6 +151,9 @@ __global__ void __launch_bounds__(kPrologueThreads)
                             uint16_t* __restrict__ kc_rows, uint16_t* __restrict__ vc_rows,
                             int n_tok, int n_heads, int n_kv_heads, int start_pos,
                             const float* cos_tab, const float* sin_tab, int rope_type) {
+  // the attention grid queued behind (programmatic dependent launch) may
+  // start its set-up now; it waits for this grid before touching its output
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   const int r = blockIdx.x;
   if (r >= n_tok) return;
   const int pos = start_pos + r;

@@ -196,6 +196,10 @@ __global__ void __launch_bounds__(kPfThreads, 1)
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
+  // launched behind the prologue with programmatic dependent launch: the
+  // set-up above overlapped its tail; q16, the cache rows it appended and
+  // the work counters are read only after it has finished
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   const uint32_t tmem = sm.tmem_base;
 
   if (warp == 8) {
@@ -477,9 +481,11 @@ __global__ void __launch_bounds__(kPfThreads, 1)
 }
 
 // Host side: one persistent CTA per SM (never more than there are items).
+// With `overlap`, the launch may begin while the previous grid on the stream
+// (the prologue) is still running (programmatic stream serialisation).
 inline int launch_prefill_attention(const PrefillArgs& a, const CUtensorMap& tm_q,
                                     const CUtensorMap& tm_k, const CUtensorMap& tm_v,
-                                    int num_sms, cudaStream_t st) {
+                                    int num_sms, cudaStream_t st, bool overlap) {
   static bool attr_done = false;
   if (!attr_done) {
     if (cudaFuncSetAttribute(prefill_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -490,7 +496,17 @@ inline int launch_prefill_attention(const PrefillArgs& a, const CUtensorMap& tm_
   const int per_tile = a.kv_mul >= 2 ? a.n_heads / 2 : a.n_heads;
   const int n_items = ((a.n_tok + kPfBlockM - 1) / kPfBlockM) * per_tile;
   const int grid = n_items < num_sms ? n_items : num_sms;
-  prefill_attn_kernel<<<grid, kPfThreads, kPfSmemBytes, st>>>(a, tm_q, tm_k, tm_v);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(kPfThreads);
+  cfg.dynamicSmemBytes = kPfSmemBytes;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = overlap ? 1 : 0;
+  if (cudaLaunchKernelEx(&cfg, prefill_attn_kernel, a, tm_q, tm_k, tm_v) != cudaSuccess) return -4;
   return cudaGetLastError() == cudaSuccess ? 0 : -4;
 }
 

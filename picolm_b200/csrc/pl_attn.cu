@@ -751,7 +751,9 @@ static int launch_prefill(int seq, int layer, int start_pos, int n_tok, const fl
   a.work = g->d_work;
   a.err = g->d_err;
   prof_begin(st);
-  if (pl::launch_prefill_attention(a, g->tm_q16, g->tm_k_pf, g->tm_v_pf, g->num_sms, st) != 0)
+  // overlap with the prologue except when events separate the two for timing
+  if (pl::launch_prefill_attention(a, g->tm_q16, g->tm_k_pf, g->tm_v_pf, g->num_sms, st,
+                                   !g->profiling) != 0)
     return PL_ECUDA;
   prof_end(st);
   count_launch();
