@@ -431,15 +431,25 @@ def run_long_ctx(args, local, peaks):
 
     step(0)
     torch.cuda.synchronize()
+    # the 32 steps captured once and replayed, as in the split version
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        sh_cap = torch.cuda.current_stream(dev).cuda_stream
+        for s in range(NS5):
+            for l in range(L):
+                at.decode_batch_dev(l, 1, seq0.data_ptr(), posd[s:s + 1].data_ptr(),
+                                    CTX5 + NS5 - 1, q[s, l].data_ptr(), k[s, l].data_ptr(),
+                                    v[s, l].data_ptr(), out[l].data_ptr(), sh_cap)
+    graph.replay()
+    torch.cuda.synchronize()
+    nbytes = sum(L * ((CTX5 + s + 1) * kv5 * 4 + Q_DIM * 8 + kv5 * 12) for s in range(NS5))
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record()
-    nbytes = 0
-    for s in range(NS5):
-        step(s)
-        nbytes += L * ((CTX5 + s + 1) * kv5 * 4 + Q_DIM * 8 + kv5 * 12)
+    graph.replay()
     e1.record()
     torch.cuda.synchronize()
     ms = e0.elapsed_time(e1)
+    del graph
     # decode kernels alone (module events; costs the decode/merge overlap)
     at.profile(True)
     for s in range(NS5):
@@ -461,11 +471,11 @@ def run_long_ctx_split(args, rank, world, local, peaks):
     """Config 5 split along the KV axis over `world` GPUs: rank r holds a
     contiguous 1/world of the 32768 cached positions (the last rank also the
     appended ones); per layer and step each rank computes its partial
-    (m, l, o), NCCL all-gathers the partials and merges them
+    (m, l, o), pushes it to every rank over NVLink and merges
     (picolm_b200/shard.py).  Timed on every rank, max over ranks."""
     import torch
     import picolm_b200 as pb
-    from picolm_b200.shard import PART_STRIDE, AttnShardOps, KVSplitDecoder
+    from picolm_b200.shard import PART_STRIDE, KVSplitDecoder, P2PShardOps
     L, HK5, CTX5, NS5 = 16, 8, 32768, 32
     kv5 = HK5 * HD
     dev = torch.device("cuda", local)
@@ -474,7 +484,7 @@ def run_long_ctx_split(args, rank, world, local, peaks):
     at = pb.Attn(L, H, HK5, CTX5 + NS5, rope_base=500000.0, device=local)
     stream = torch.cuda.current_stream(dev)
     dec = KVSplitDecoder(rank=rank, world=world, n_cached=CTX5,
-                         ops=AttnShardOps(at, stream.cuda_stream))
+                         ops=P2PShardOps(at, stream.cuda_stream, rank, world))
     rng = np.random.default_rng(4)
     for l in range(L):
         kc = make_cache_host(rng, CTX5, kv5)
@@ -498,24 +508,36 @@ def run_long_ctx_split(args, rank, world, local, peaks):
     # same row with the same values, so the warm-up reuses step 0
     step(0)
     torch.cuda.synchronize()
+    # all 32 steps x 16 layers captured once and replayed: launched one by
+    # one from Python, the host rather than the GPUs would set the pace
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        dec.ops.stream = torch.cuda.current_stream(dev).cuda_stream
+        for s in range(NS5):
+            step(s)
+    dec.ops.stream = stream.cuda_stream
     barrier(world)
+    graph.replay()
+    torch.cuda.synchronize()
+    barrier(world)
+    nbytes = sum(L * ((CTX5 + s + 1) * kv5 * 4 + Q_DIM * 8 + kv5 * 12) for s in range(NS5))
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(stream)
-    nbytes = 0
-    for s in range(NS5):
-        step(s)
-        nbytes += L * ((CTX5 + s + 1) * kv5 * 4 + Q_DIM * 8 + kv5 * 12)
+    graph.replay()
     e1.record(stream)
     torch.cuda.synchronize()
     ms = max_over_ranks(e0.elapsed_time(e1), world)
+    del graph
     barrier(world)
     at.close()
     return {"metric": f"long-context decode-attn HBM GB/s (config 5, KV split over {world} GPUs)",
             "value": nbytes / (ms / 1e3) / 1e9, "unit": "GB/s",
             "pct_peak_per_gpu": 100.0 * nbytes / (ms / 1e3) / 1e9 / world / peaks["hbm_gbs"],
             "tok_per_s": NS5 / (ms / 1e3), "ms_per_step_16_layers": ms / NS5,
-            "scaling": "strong", "collective": "NCCL all_gather of 32 x 68 FP32 partials per "
-                                             "layer, then LSE combine on every rank",
+            "timing": "one CUDA graph of all 32 steps, replayed",
+            "scaling": "strong", "collective": "per layer one kernel on every rank pushes its "
+                                             "32 x 68 FP32 partial into every rank's buffer over "
+                                             "NVLink (P2P stores, epoch stamps) and merges (LSE)",
             "config": {"workload": "config5 16 layers, 32/8 heads, hd 64, theta 5e5, "
                                    "32768 cached + 32 steps, KV N(0,1) seed 4",
                        "shard": f"{dec.n_rows} cached positions on rank {rank}"}}

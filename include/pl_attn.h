@@ -168,6 +168,29 @@ int  pl_attn_combine_dev(int n_part, const float *d_parts, float *d_out,
  * *d_v, each [max_seq][kv_dim].  For engines that share the cache. */
 int  pl_attn_kv_ptr(int seq, int layer, uint16_t **d_k, uint16_t **d_v);
 
+/* ---- KV-split merge over NVLink peer memory (one process per GPU).  No
+ *      counterpart in the reference, which runs on one CPU; this is the
+ *      multi-GPU form of the merge that pl_attn_combine_dev does locally. ---- */
+
+/* Bytes of the handle pl_attn_xfer_setup writes (a CUDA IPC handle). */
+int  pl_attn_xfer_handle_bytes(void);
+
+/* Allocate this rank's receive buffer for a split over `world` (1..8)
+ * ranks and write its IPC handle to handle_out.  Once per context. */
+int  pl_attn_xfer_setup(int world, int rank, void *handle_out);
+
+/* Map every other rank's buffer: `handles` holds world handles back to back,
+ * in rank order (exchange them between the processes first). */
+int  pl_attn_xfer_connect(const void *handles);
+
+/* Push this rank's partial block d_part (as pl_attn_decode_partial_dev
+ * writes it) to every rank over NVLink, wait (bounded) for all ranks'
+ * blocks of the same merge, and write the merged attention output to d_out
+ * [n_heads*head_dim].  Every rank calls it once per merge, in the same
+ * order; the merges are numbered on the device, so a captured CUDA graph
+ * of these calls can be replayed. */
+int  pl_attn_combine_p2p_dev(const float *d_part, float *d_out, void *stream);
+
 /* pl_attn_decode_batch_dev for callers that cannot allow the library to
  * allocate device memory.  No counterpart in the reference: picolm's
  * attention runs on the CPU and allocates nothing per step.

@@ -84,6 +84,10 @@ def load(path: str = LIB_PATH) -> C.CDLL:
         "pl_attn_decode_partial_dev": (i, [i, i, i, i, i, i, _vp, _vp, _vp, _vp, _vp]),
         "pl_attn_combine_dev": (i, [i, _vp, _vp, _vp]),
         "pl_attn_kv_ptr": (i, [i, i, C.POINTER(_vp), C.POINTER(_vp)]),
+        "pl_attn_xfer_handle_bytes": (i, []),
+        "pl_attn_xfer_setup": (i, [i, i, _vp]),
+        "pl_attn_xfer_connect": (i, [_vp]),
+        "pl_attn_combine_p2p_dev": (i, [_vp, _vp, _vp]),
         "pl_attn_decode_batch_dev_noalloc": (i, [i, i, _vp, _vp, i, _vp, _vp, _vp, _vp, _vp]),
         "pl_attn_profile": (i, [i]),
         "pl_attn_profile_read": (i, [C.POINTER(C.c_double), C.POINTER(C.c_long),
@@ -238,6 +242,21 @@ class Attn:
         _check(self.lib.pl_attn_profile_read(C.byref(ms), C.byref(na), C.byref(nl)),
                "pl_attn_profile_read")
         return ms.value, na.value, nl.value
+
+    def xfer_setup(self, world: int, rank: int) -> bytes:
+        """Receive buffer of the P2P KV-split merge; returns its IPC handle."""
+        buf = C.create_string_buffer(self.lib.pl_attn_xfer_handle_bytes())
+        _check(self.lib.pl_attn_xfer_setup(world, rank, buf), "pl_attn_xfer_setup")
+        return buf.raw
+
+    def xfer_connect(self, handles) -> None:
+        """Map the other ranks' buffers; `handles` in rank order."""
+        blob = C.create_string_buffer(b"".join(handles))
+        _check(self.lib.pl_attn_xfer_connect(blob), "pl_attn_xfer_connect")
+
+    def combine_p2p_dev(self, d_part, d_out, stream=None) -> None:
+        _check(self.lib.pl_attn_combine_p2p_dev(d_part, d_out, stream),
+               "pl_attn_combine_p2p_dev")
 
     def kv_ptr(self, seq: int, layer: int):
         k = _vp()

@@ -566,6 +566,8 @@ constexpr int kMergeThreads = 256;
 __global__ void __launch_bounds__(kMergeThreads) merge_kernel(const DecodeArgs a, int hpb) {
   __shared__ float4 s_acc[kMergeThreads];
   __shared__ float2 s_ml[kMergeThreads];
+  // a merge of KV shards queued behind this grid may become resident now
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   asm volatile("griddepcontrol.wait;" ::: "memory");
   const int i = blockIdx.x, h0 = blockIdx.y * hpb, tid = threadIdx.x;
   const int pairs = hpb * (kHD / 4), lanes = kMergeThreads / pairs;

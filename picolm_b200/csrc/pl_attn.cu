@@ -20,6 +20,7 @@
 #include "kern_decode.cuh"
 #include "kern_misc.cuh"
 #include "kern_prefill.cuh"
+#include "kern_xfer.cuh"
 
 namespace {
 
@@ -32,6 +33,14 @@ typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t,
                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
 
 constexpr int kDecodeStages = 4;
+
+// Receive buffer of the KV-split exchange and the peers' buffers mapped here.
+struct Xfer {
+  int world = 0, rank = 0;
+  uint8_t* local = nullptr;              // this rank's buffer (cudaMalloc)
+  pl::XferPeers peers = {};              // every rank's buffer as seen from this GPU
+  void* opened[pl::kXferMaxRanks] = {};  // IPC mappings to close
+};
 
 struct Ctx {
   int device = -1;
@@ -70,6 +79,16 @@ struct Ctx {
 };
 
 Ctx* g = nullptr;
+Xfer* g_xfer = nullptr;  // KV-split exchange of the current context, if set up
+
+void xfer_free() {
+  if (!g_xfer) return;
+  for (int r = 0; r < pl::kXferMaxRanks; ++r)
+    if (g_xfer->opened[r]) cudaIpcCloseMemHandle(g_xfer->opened[r]);
+  cudaFree(g_xfer->local);
+  delete g_xfer;
+  g_xfer = nullptr;
+}
 std::mutex g_mu;
 
 #define PL_CUDA(call)                                                     \
@@ -540,6 +559,8 @@ int pl_attn_init(int n_layers, int n_heads, int n_kv_heads, int head_dim, int ma
 
 void pl_attn_shutdown(void) {
   std::lock_guard<std::mutex> lk(g_mu);
+  if (g && g->device >= 0) cudaSetDevice(g->device);
+  xfer_free();
   free_ctx(g);
   g = nullptr;
 }
@@ -659,6 +680,75 @@ int pl_attn_combine_dev(int n_part, const float* d_parts, float* d_out, void* st
   const size_t smem = static_cast<size_t>(3 * pl::kMaxCombineParts + 2) * g->n_heads * sizeof(float);
   pl::combine_kernel<<<1, 256, smem, st>>>(n_part, g->n_heads, d_parts, d_out);
   PL_CUDA(cudaGetLastError());
+  count_launch();
+  return PL_OK;
+}
+
+// ------------------------------------------------ KV-split exchange (P2P)
+int pl_attn_xfer_handle_bytes(void) { return static_cast<int>(sizeof(cudaIpcMemHandle_t)); }
+
+int pl_attn_xfer_setup(int world, int rank, void* handle_out) {
+  if (!g) return PL_ESTATE;
+  if (g_xfer) return PL_ESTATE;
+  if (world < 1 || world > pl::kXferMaxRanks || rank < 0 || rank >= world || !handle_out)
+    return PL_EARG;
+  if (cudaSetDevice(g->device) != cudaSuccess) return PL_ECUDA;
+  const size_t bytes = pl::kXferStampBytes +
+                       2 * static_cast<size_t>(world) * g->n_heads * kPartStride * sizeof(float);
+  Xfer* x = new Xfer;
+  x->world = world;
+  x->rank = rank;
+  if (cudaMalloc(&x->local, bytes) != cudaSuccess) {
+    delete x;
+    return PL_ENOMEM;
+  }
+  if (cudaMemset(x->local, 0, bytes) != cudaSuccess ||
+      cudaIpcGetMemHandle(static_cast<cudaIpcMemHandle_t*>(handle_out), x->local) != cudaSuccess) {
+    cudaFree(x->local);
+    delete x;
+    return PL_ECUDA;
+  }
+  x->peers.base[rank] = x->local;
+  g_xfer = x;
+  return PL_OK;
+}
+
+int pl_attn_xfer_connect(const void* handles) {
+  if (!g || !g_xfer) return PL_ESTATE;
+  if (!handles) return PL_EARG;
+  if (cudaSetDevice(g->device) != cudaSuccess) return PL_ECUDA;
+  const auto* h = static_cast<const cudaIpcMemHandle_t*>(handles);
+  for (int r = 0; r < g_xfer->world; ++r) {
+    if (r == g_xfer->rank || g_xfer->opened[r]) continue;
+    void* p = nullptr;
+    if (cudaIpcOpenMemHandle(&p, h[r], cudaIpcMemLazyEnablePeerAccess) != cudaSuccess)
+      return PL_ECUDA;
+    g_xfer->opened[r] = p;
+    g_xfer->peers.base[r] = static_cast<uint8_t*>(p);
+  }
+  return PL_OK;
+}
+
+int pl_attn_combine_p2p_dev(const float* d_part, float* d_out, void* stream) {
+  if (!g || !g_xfer) return PL_ESTATE;
+  if (!d_part || !d_out) return PL_EARG;
+  for (int r = 0; r < g_xfer->world; ++r)
+    if (!g_xfer->peers.base[r]) return PL_ESTATE;  // not connected yet
+  cudaStream_t st = pick_stream(stream);
+  const size_t smem = static_cast<size_t>(3 * pl::kXferMaxRanks + 2) * g->n_heads * sizeof(float);
+  // queued behind the partial's kernels (programmatic dependent launch)
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(1);
+  cfg.blockDim = dim3(pl::kXferThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  PL_CUDA(cudaLaunchKernelEx(&cfg, pl::combine_p2p_kernel, d_part, g_xfer->peers, g_xfer->world,
+                             g_xfer->rank, g->n_heads, d_out, g->d_err));
   count_launch();
   return PL_OK;
 }

@@ -9,9 +9,10 @@ is too long for one device's bandwidth, it is split along the sequence axis:
 * the LAST rank also holds every position appended after n_cached (its
   local row pos - row0), so a decode step appends on exactly one rank;
 * per layer and step every rank computes the partial triple (m, l, o) of
-  its rows with pl_attn_decode_partial_dev, the partials are all-gathered
-  (NCCL over NVLink; 8,704 bytes per rank for 32 heads), and every rank
-  merges them in rank order with pl_attn_combine_dev:
+  its rows with pl_attn_decode_partial_dev (8,704 bytes for 32 heads) and
+  the partials are merged in rank order on every rank, either after an
+  NCCL all-gather with pl_attn_combine_dev (AttnShardOps) or by one kernel
+  that pushes them over NVLink peer memory (P2PShardOps):
       M = max_g m_g,  L = sum_g l_g 2^(m_g - M),  O = sum_g 2^(m_g - M) o_g / L.
 
 The arithmetic of the merge is the log-sum-exp form of the online softmax
@@ -19,7 +20,7 @@ of model.c:848-892 applied to whole shards instead of single rows.
 
 `KVSplitDecoder` holds the per-rank bookkeeping and is independent of the
 backend: `ops` supplies `partial(...)` and `combine(...)`; `AttnShardOps`
-is the CUDA implementation on top of the C ABI.
+and `P2PShardOps` are the CUDA implementations on top of the C ABI.
 """
 from __future__ import annotations
 
@@ -99,3 +100,36 @@ class AttnShardOps:
 
     def combine(self, world, parts_all, out):
         self.attn.combine_dev(world, parts_all.data_ptr(), out.data_ptr(), self.stream)
+
+
+class P2PShardOps(AttnShardOps):
+    """CUDA backend whose merge pushes the partials over NVLink peer memory.
+
+    At construction every rank allocates its receive buffer, the IPC handles
+    are exchanged once over `group` (any backend; they are 64-byte objects),
+    and each rank maps the others.  Per merge, pl_attn_combine_p2p_dev stores
+    this rank's partial into every rank's buffer, stamps it and, once every
+    rank's stamp has arrived, merges locally: one kernel instead of an
+    all-gather plus a merge, so `gather` has nothing left to do.  The merges
+    are numbered on the device, so the calls can be captured in a CUDA
+    graph and replayed."""
+
+    def __init__(self, attn, stream_handle: int, rank: int, world: int, group=None,
+                 seq: int = 0):
+        super().__init__(attn, stream_handle, group, seq)
+        import torch.distributed as dist
+        handle = attn.xfer_setup(world, rank)
+        handles = [None] * world
+        dist.all_gather_object(handles, handle, group=group)
+        attn.xfer_connect(handles)
+        self._part = None
+
+    def partial(self, layer, pos, row0, n_rows, append, q, k, v, part):
+        self._part = part
+        super().partial(layer, pos, row0, n_rows, append, q, k, v, part)
+
+    def gather(self, part, parts_all):
+        pass
+
+    def combine(self, world, parts_all, out):
+        self.attn.combine_p2p_dev(self._part.data_ptr(), out.data_ptr(), self.stream)
