@@ -10,11 +10,17 @@
  * (built with -DUSE_PL_ATTN).  Each generated token is printed with the
  * margin between the best and the second-best logit.
  *
- * usage: e2e MODEL.gguf N_PROMPT N_GEN SEED THREADS
+ * usage: e2e MODEL.gguf N_PROMPT N_GEN SEED THREADS [--save F] [--load F]
+ *   --load F  kvcache_load(F) first (model.c:1199-1259) and skip the cached
+ *             prompt positions in the prefill, as picolm.c:214-236 does;
+ *             the last prompt token is always recomputed for its logits
+ *   --save F  kvcache_save(F) of the whole prompt (model.c:1158-1196):
+ *             after the prefill, or, with --load, right after the load
  */
 #include <stdint.h>
 #include <stdio.h>
 #include <stdlib.h>
+#include <string.h>
 #include <time.h>
 
 #include "model.h"
@@ -37,8 +43,15 @@ static double now_s(void) {
 }
 
 int main(int argc, char **argv) {
-    if (argc != 6) {
-        fprintf(stderr, "usage: %s MODEL.gguf N_PROMPT N_GEN SEED THREADS\n", argv[0]);
+    const char *save_path = NULL, *load_path = NULL;
+    for (int i = 6; i + 1 < argc; i += 2) {
+        if (strcmp(argv[i], "--save") == 0) save_path = argv[i + 1];
+        else if (strcmp(argv[i], "--load") == 0) load_path = argv[i + 1];
+        else argc = -1;
+    }
+    if (argc < 6 || (argc - 6) % 2) {
+        fprintf(stderr, "usage: %s MODEL.gguf N_PROMPT N_GEN SEED THREADS [--save F] [--load F]\n",
+                argv[0]);
         return 2;
     }
     const char *path = argv[1];
@@ -71,9 +84,20 @@ int main(int argc, char **argv) {
     for (int i = 0; i < n_prompt; i++)
         prompt[i] = 3 + (int)(splitmix64(&seed) % (uint64_t)(c->vocab_size - 3));
 
+    int cache_pos = 0;
+    if (load_path) {
+        cache_pos = kvcache_load(&model, load_path);
+        if (cache_pos <= 0) {
+            fprintf(stderr, "kvcache_load failed\n");
+            return 1;
+        }
+        if (save_path && kvcache_save(&model, save_path, cache_pos) != 0) return 1;
+        if (cache_pos > n_prompt - 1) cache_pos = n_prompt - 1;
+    }
     const double t0 = now_s();
-    model_forward_prefill(&model, prompt, n_prompt, 0);
+    model_forward_prefill(&model, prompt + cache_pos, n_prompt - cache_pos, cache_pos);
     const double t1 = now_s();
+    if (save_path && !load_path && kvcache_save(&model, save_path, n_prompt) != 0) return 1;
     const float *logits = model.state.logits;
     int pos = n_prompt - 1;
     for (int i = 0; i < n_gen; i++) {
@@ -94,7 +118,7 @@ int main(int argc, char **argv) {
     }
     const double t2 = now_s();
     printf("S prefill_tokens=%d prefill_s=%.6f decode_tokens=%d decode_s=%.6f threads=%d\n",
-           n_prompt, t1 - t0, n_gen - 1, t2 - t1, threads);
+           n_prompt - cache_pos, t1 - t0, n_gen - 1, t2 - t1, threads);
     fflush(stdout);
 #ifdef USE_PL_ATTN
     pl_attn_shutdown();

@@ -13,6 +13,12 @@ the copy with each block replaced by one C-ABI call:
   -> the QK-norm (Qwen3 only) on the host, then
      pl_attn_prefill(0, l, start_pos, n_tokens, q_batch, k_batch, v_batch,
                      xb_batch, dim).
+* kvcache_save (model.c:1158-1196): before the file is written, every
+  layer's first n_pos cache rows are downloaded from the device into
+  picolm's host cache arrays (pl_kv_download), so the KVCP file keeps its
+  exact format;
+* kvcache_load (model.c:1199-1259): after the rows are read into the host
+  arrays, they are uploaded to the device (pl_kv_upload).
 A failing call prints pl_attn_strerror and exits: there is no CPU fallback.
 The copy is written to a temporary directory by the oracle Makefile and
 deleted after compiling.
@@ -58,6 +64,34 @@ PREFILL_CALL = """\
 """
 
 
+KV_SAVE_SYNC = """\
+    /* the cache lives on the B200: bring its rows into the host arrays */
+    for (int pl_l = 0; pl_l < c->n_layers; pl_l++) {
+        int pl_rc = pl_kv_download(0, pl_l, 0, n_pos,
+                                   m->state.key_cache + (size_t)pl_l * seq_len * kv_dim,
+                                   m->state.val_cache + (size_t)pl_l * seq_len * kv_dim);
+        if (pl_rc != PL_OK) {
+            fprintf(stderr, "pl_kv_download: %s\\n", pl_attn_strerror(pl_rc));
+            return -1;
+        }
+    }
+"""
+
+KV_LOAD_SYNC = """\
+    /* the cache lives on the B200: send the rows just read there */
+    for (int pl_l = 0; pl_l < c->n_layers; pl_l++) {
+        int pl_rc = pl_kv_upload(0, pl_l, 0, n_pos,
+                                 m->state.key_cache + (size_t)pl_l * seq_len * kv_dim,
+                                 m->state.val_cache + (size_t)pl_l * seq_len * kv_dim);
+        if (pl_rc != PL_OK) {
+            fprintf(stderr, "pl_kv_upload: %s\\n", pl_attn_strerror(pl_rc));
+            fclose(f);
+            return 0;
+        }
+    }
+"""
+
+
 def find(lines, pred, start=0):
     for i in range(start, len(lines)):
         if pred(lines[i]):
@@ -83,9 +117,19 @@ def main():
         if must not in block:
             raise SystemExit(f"pl_model_patch: prefill block does not contain {must!r}")
 
+    # kvcache_save: after its n_pos check; kvcache_load: before its success message
+    ss = find(lines, lambda s: s.startswith("int kvcache_save("), pe)
+    sc = find(lines, lambda s: s.strip() == "if (n_pos <= 0 || n_pos > seq_len) return -1;", ss)
+    ls = find(lines, lambda s: s.startswith("int kvcache_load("), sc)
+    lm = find(lines, lambda s: 'fprintf(stderr, "KV cache loaded:' in s, ls)
+    for must, blk in (("m->state.key_cache", lines[ss:sc + 40]), ("m->state.key_cache", lines[ls:lm])):
+        if must not in "\n".join(blk):
+            raise SystemExit("pl_model_patch: kvcache block does not read the host cache")
     inc = find(lines, lambda s: s.strip() == '#include "model.h"')
     out = (lines[:inc + 1] + ['#include "pl_attn.h"'] + lines[inc + 1:ds]
-           + DECODE_CALL.split("\n") + lines[de:ps] + PREFILL_CALL.split("\n") + lines[pe:])
+           + DECODE_CALL.split("\n") + lines[de:ps] + PREFILL_CALL.split("\n")
+           + lines[pe:sc + 1] + KV_SAVE_SYNC.split("\n") + lines[sc + 1:lm - 1]
+           + KV_LOAD_SYNC.split("\n") + lines[lm - 1:])
     with open(dst, "w") as f:
         f.write("\n".join(out))
 

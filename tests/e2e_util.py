@@ -17,10 +17,15 @@ def have(binary: str) -> bool:
 
 
 def run(binary: str, gguf: str, n_prompt: int, n_gen: int, seed: int = 1, threads: int = 4,
-        timeout: int = 1800):
-    """(tokens, margins, summary dict) of one greedy run."""
-    p = subprocess.run([binary, gguf, str(n_prompt), str(n_gen), str(seed), str(threads)],
-                       capture_output=True, text=True, timeout=timeout)
+        timeout: int = 1800, save: str | None = None, load: str | None = None):
+    """(tokens, margins, summary dict) of one greedy run; `save` / `load`
+    name KVCP files for picolm's kvcache_save / kvcache_load."""
+    cmd = [binary, gguf, str(n_prompt), str(n_gen), str(seed), str(threads)]
+    if save:
+        cmd += ["--save", save]
+    if load:
+        cmd += ["--load", load]
+    p = subprocess.run(cmd, capture_output=True, text=True, timeout=timeout)
     if p.returncode != 0:
         raise RuntimeError(f"{os.path.basename(binary)} failed ({p.returncode}):\n{p.stderr[-2000:]}")
     toks, margins, summary = [], [], {}
@@ -39,3 +44,16 @@ def first_divergence(a, b):
         if x != y:
             return i
     return None if len(a) == len(b) else min(len(a), len(b))
+
+
+def read_kvcp(path: str):
+    """picolm's KVCP file (model.c:1144-1156): header (magic, n_pos, n_layers,
+    kv_dim) and the K and V rows as [n_layers][n_pos][kv_dim] FP16 words."""
+    import numpy as np
+    raw = np.fromfile(path, np.uint8)
+    head = raw[:16].view(np.uint32)
+    n_pos, n_layers, kv_dim = (int(x) for x in head[1:4])
+    body = raw[16:].view(np.uint16)
+    n = n_layers * n_pos * kv_dim
+    assert body.size == 2 * n, (body.size, n)
+    return head, body[:n].reshape(n_layers, n_pos, kv_dim), body[n:].reshape(n_layers, n_pos, kv_dim)
