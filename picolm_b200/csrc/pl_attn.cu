@@ -13,7 +13,10 @@
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
+#include <atomic>
+#include <condition_variable>
 #include <mutex>
+#include <thread>
 #include <vector>
 
 #include "../../include/pl_attn.h"
@@ -148,6 +151,101 @@ int ensure_stage(size_t bytes) {
   if (cudaMallocHost(&g->h_stage, cap) != cudaSuccess) return PL_ENOMEM;
   g->stage_cap = cap;
   return PL_OK;
+}
+
+// ---- parallel copies between caller buffers and the pinned staging area ---
+// The host-buffer entry points move every input and output through the
+// pinned staging area; one thread copies only about 10 GB/s, which made
+// those copies most of a host-buffer call.  A few sleeping helper threads
+// (started on the first such call; PL_ATTN_COPY_THREADS overrides their
+// number, 0 turns them off) split each copy with the calling thread.
+struct CopyPiece {
+  uint8_t* dst;
+  const uint8_t* src;
+  size_t bytes;
+};
+
+class CopyPool {
+ public:
+  explicit CopyPool(int n) {
+    for (int i = 0; i < n; ++i) th_.emplace_back([this, i] { run(i + 1); });
+  }
+  ~CopyPool() {
+    {
+      std::lock_guard<std::mutex> lk(mu_);
+      stop_ = true;
+    }
+    cv_.notify_all();
+    for (auto& t : th_) t.join();
+  }
+  // all pieces copied when this returns
+  void copy(const CopyPiece* pc, int n_pc) {
+    size_t total = 0;
+    for (int i = 0; i < n_pc; ++i) total += pc[i].bytes;
+    const int parts = static_cast<int>(th_.size()) + 1;
+    if (parts == 1 || total < (256u << 10)) {
+      for (int i = 0; i < n_pc; ++i) std::memcpy(pc[i].dst, pc[i].src, pc[i].bytes);
+      return;
+    }
+    {
+      std::lock_guard<std::mutex> lk(mu_);
+      pc_ = pc;
+      n_pc_ = n_pc;
+      total_ = total;
+      parts_ = parts;
+      left_.store(parts - 1);
+      ++gen_;
+    }
+    cv_.notify_all();
+    part(0);
+    while (left_.load(std::memory_order_acquire) != 0) std::this_thread::yield();
+  }
+
+ private:
+  // bytes [p*total/parts, (p+1)*total/parts) of the concatenated pieces
+  void part(int p) {
+    const size_t lo = total_ * p / parts_, hi = total_ * (p + 1) / parts_;
+    size_t s0 = 0;
+    for (int i = 0; i < n_pc_; s0 += pc_[i].bytes, ++i) {
+      const size_t a = lo > s0 ? lo : s0, b = hi < s0 + pc_[i].bytes ? hi : s0 + pc_[i].bytes;
+      if (a < b) std::memcpy(pc_[i].dst + (a - s0), pc_[i].src + (a - s0), b - a);
+    }
+  }
+  void run(int p) {
+    uint64_t seen = 0;
+    while (true) {
+      {
+        std::unique_lock<std::mutex> lk(mu_);
+        cv_.wait(lk, [&] { return stop_ || gen_ != seen; });
+        if (stop_) return;
+        seen = gen_;
+      }
+      part(p);
+      left_.fetch_sub(1, std::memory_order_release);
+    }
+  }
+  std::vector<std::thread> th_;
+  std::mutex mu_;
+  std::condition_variable cv_;
+  bool stop_ = false;
+  uint64_t gen_ = 0;
+  const CopyPiece* pc_ = nullptr;
+  int n_pc_ = 0, parts_ = 1;
+  size_t total_ = 0;
+  std::atomic<int> left_{0};
+};
+
+CopyPool* g_copy = nullptr;  // lives as long as the context
+
+void host_copy(const CopyPiece* pc, int n_pc) {
+  if (!g_copy) {
+    int n = static_cast<int>(std::thread::hardware_concurrency()) / 2;
+    if (n > 7) n = 7;
+    if (const char* e = std::getenv("PL_ATTN_COPY_THREADS")) n = std::atoi(e);
+    if (n < 0) n = 0;
+    g_copy = new CopyPool(n);
+  }
+  g_copy->copy(pc, n_pc);
 }
 
 int ensure_part(size_t floats) {
@@ -559,6 +657,8 @@ int pl_attn_init(int n_layers, int n_heads, int n_kv_heads, int head_dim, int ma
 
 void pl_attn_shutdown(void) {
   std::lock_guard<std::mutex> lk(g_mu);
+  delete g_copy;
+  g_copy = nullptr;
   if (g && g->device >= 0) cudaSetDevice(g->device);
   xfer_free();
   free_ctx(g);
@@ -599,11 +699,14 @@ int pl_attn_decode_batch(int layer, int n, const int* seqs, const int* pos, cons
   int rc = ensure_stage(total);
   if (rc) return rc;
   uint8_t* h = g->h_stage;
-  std::memcpy(h, q, qb);
-  std::memcpy(h + qb, k, kb);
-  std::memcpy(h + qb + kb, v, kb);
-  std::memcpy(h + qb + 2 * kb, seqs, ib);
-  std::memcpy(h + qb + 2 * kb + ib, pos, ib);
+  {
+    const CopyPiece in[5] = {{h, reinterpret_cast<const uint8_t*>(q), qb},
+                             {h + qb, reinterpret_cast<const uint8_t*>(k), kb},
+                             {h + qb + kb, reinterpret_cast<const uint8_t*>(v), kb},
+                             {h + qb + 2 * kb, reinterpret_cast<const uint8_t*>(seqs), ib},
+                             {h + qb + 2 * kb + ib, reinterpret_cast<const uint8_t*>(pos), ib}};
+    host_copy(in, 5);
+  }
   uint8_t* d = g->d_stage;
   PL_CUDA(cudaMemcpyAsync(d, h, in_bytes, cudaMemcpyHostToDevice, g->stream));
   float* d_out = reinterpret_cast<float*>(d + out_off);
@@ -620,7 +723,8 @@ int pl_attn_decode_batch(int layer, int n, const int* seqs, const int* pos, cons
                           g->stream));
   rc = finish_host_call(reinterpret_cast<uint32_t*>(h + out_off + qb));
   if (rc) return rc;
-  std::memcpy(out, h + out_off, qb);
+  const CopyPiece o = {reinterpret_cast<uint8_t*>(out), h + out_off, qb};
+  host_copy(&o, 1);
   return PL_OK;
 }
 
@@ -867,9 +971,12 @@ int pl_attn_prefill(int seq, int layer, int start_pos, int n_tok, const float* q
   if (rc) return rc;
   uint8_t* h = g->h_stage;
   uint8_t* d = g->d_stage;
-  std::memcpy(h, q, qb);
-  std::memcpy(h + qb, k, kb);
-  std::memcpy(h + qb + kb, v, kb);
+  {
+    const CopyPiece in[3] = {{h, reinterpret_cast<const uint8_t*>(q), qb},
+                             {h + qb, reinterpret_cast<const uint8_t*>(k), kb},
+                             {h + qb + kb, reinterpret_cast<const uint8_t*>(v), kb}};
+    host_copy(in, 3);
+  }
   PL_CUDA(cudaMemcpyAsync(d, h, in_bytes, cudaMemcpyHostToDevice, g->stream));
   float* d_out = reinterpret_cast<float*>(d + out_off);
   rc = launch_prefill(seq, layer, start_pos, n_tok, reinterpret_cast<float*>(d),
@@ -883,7 +990,8 @@ int pl_attn_prefill(int seq, int layer, int start_pos, int n_tok, const float* q
   rc = finish_host_call(reinterpret_cast<uint32_t*>(h + out_off + qb));
   if (rc) return rc;
   if (out_stride == g->q_dim) {
-    std::memcpy(out, h + out_off, qb);
+    const CopyPiece o = {reinterpret_cast<uint8_t*>(out), h + out_off, qb};
+    host_copy(&o, 1);
   } else {
     for (int r = 0; r < n_tok; ++r)
       std::memcpy(out + static_cast<size_t>(r) * out_stride,
