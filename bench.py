@@ -268,16 +268,18 @@ def run_batched_decode(args, rank, world, local, peaks):
     kh = k.cpu().numpy()
     vh = v.cpu().numpy()
     seqs_h = np.arange(SEQS_PER_GPU, dtype=np.int32)
+    out_h = np.empty(SEQS_PER_GPU * Q_DIM, np.float32)  # reused, like model.c's s->xb
     n_e2e = max(16, min(args.steps, 256))
     for i in range(3):
         at.decode_batch(0, seqs_h, np.full(SEQS_PER_GPU, CTX + i % NSTEP, np.int32), qh[i % NSTEP],
-                        kh[i % NSTEP], vh[i % NSTEP])
+                        kh[i % NSTEP], vh[i % NSTEP], out=out_h)
     barrier(world)
     e2e_bytes = 0
     t0 = time.perf_counter()
     for j in range(n_e2e):
         s = j % NSTEP
-        at.decode_batch(0, seqs_h, np.full(SEQS_PER_GPU, CTX + s, np.int32), qh[s], kh[s], vh[s])
+        at.decode_batch(0, seqs_h, np.full(SEQS_PER_GPU, CTX + s, np.int32), qh[s], kh[s], vh[s],
+                        out=out_h)
         e2e_bytes += step_bytes(CTX + s, SEQS_PER_GPU)
     t_e2e = max_over_ranks(time.perf_counter() - t0, world)
     h2d = SEQS_PER_GPU * (Q_DIM + 2 * KV_DIM) * 4 + 2 * SEQS_PER_GPU * 4
@@ -389,11 +391,12 @@ def run_prefill(args, local, peaks):
            "gpu_launches": n_all}
     # end to end through the host-buffer entry point, one layer
     qh, kh, vh = q[0].cpu().numpy(), k[0].cpu().numpy(), v[0].cpu().numpy()
-    at.prefill(0, 0, 0, qh, kh, vh)
+    out_h = np.empty(S * Q_DIM, np.float32)  # reused, like model.c's xb_batch
+    at.prefill(0, 0, 0, qh, kh, vh, out=out_h)
     t0 = time.perf_counter()
     n = 5
     for _ in range(n):
-        at.prefill(0, 0, 0, qh, kh, vh)
+        at.prefill(0, 0, 0, qh, kh, vh, out=out_h)
     dt = (time.perf_counter() - t0) / n
     res["e2e"] = {"value": flops_layer / dt / 1e12, "unit": "TFLOP/s",
                   "h2d_bytes_per_step": S * (Q_DIM + 2 * KV_DIM) * 4,

@@ -161,21 +161,30 @@ class Attn:
                "pl_attn_decode")
         return out
 
-    def decode_batch(self, layer: int, seqs, pos, q, k, v) -> np.ndarray:
+    def decode_batch(self, layer: int, seqs, pos, q, k, v, out=None) -> np.ndarray:
+        """`out` (float32, n*q_dim, contiguous) is reused if given, as a
+        caller such as model.c reuses its s->xb."""
         seqs = np.ascontiguousarray(seqs, np.int32)
         pos = np.ascontiguousarray(pos, np.int32)
         n = seqs.size
-        out = np.empty(n * self.q_dim, np.float32)
+        if out is None:
+            out = np.empty(n * self.q_dim, np.float32)
+        elif out.dtype != np.float32 or not out.flags.c_contiguous or out.size != n * self.q_dim:
+            raise ValueError("out must be a contiguous float32 array of n * q_dim")
         _check(self.lib.pl_attn_decode_batch(layer, n, seqs, pos, _f32(q), _f32(k), _f32(v),
                                              out), "pl_attn_decode_batch")
         return out.reshape(n, self.q_dim)
 
     def prefill(self, seq: int, layer: int, start_pos: int, q, k, v,
-                out_stride: int | None = None) -> np.ndarray:
+                out_stride: int | None = None, out=None) -> np.ndarray:
+        """`out` (float32, n_tok*out_stride, contiguous) is reused if given."""
         q = _f32(q)
         n_tok = q.size // self.q_dim
         stride = self.q_dim if out_stride is None else out_stride
-        out = np.zeros(n_tok * stride, np.float32)
+        if out is None:
+            out = np.zeros(n_tok * stride, np.float32)
+        elif out.dtype != np.float32 or not out.flags.c_contiguous or out.size != n_tok * stride:
+            raise ValueError("out must be a contiguous float32 array of n_tok * out_stride")
         _check(self.lib.pl_attn_prefill(seq, layer, start_pos, n_tok, q, _f32(k), _f32(v),
                                         out, stride), "pl_attn_prefill")
         return out.reshape(n_tok, stride)
