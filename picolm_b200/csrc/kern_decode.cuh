@@ -42,9 +42,11 @@
 // a scratch buffer and CTA 0 records each sequence's (first slot, segment
 // count).  merge_kernel, launched right behind with programmatic dependent
 // launch (it is resident and waiting on griddepcontrol.wait when the decode
-// grid ends), merges them with 256 threads per 4 heads.  Merging inside the
-// decode grid instead puts a chain of L2 round trips at the end of the
-// slowest CTA; measured on B200 that tail cost 13 us of a 46 us step.
+// grid ends), merges them: 256 threads per group of 1 to 16 heads, sized so
+// the merge grid covers the SMs in one wave.  Merging inside the decode grid
+// instead, by the CTA (or, tried later, the warp) that finishes a sequence's
+// last segment, puts atomics, fences and L2 round trips at the end of the
+// slowest CTA: measured on B200 it was slower than this separate grid.
 #pragma once
 #include <cstdint>
 #include <cuda.h>
