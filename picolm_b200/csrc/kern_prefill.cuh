@@ -13,7 +13,7 @@
 // first, and every pipeline below runs on across item boundaries (the next
 // item's Q and first K/V tiles load while the current one finishes).
 //
-// Warp roles (352 threads):
+// Warp roles (384 threads = three warpgroups):
 //   warps 0-3  softmax of slot A; thread r owns query row r = TMEM lane r
 //   warps 4-7  softmax of slot B (same lanes, other TMEM columns)
 //   warp 8     scheduler + TMA producer: fetches items, publishes them in a
@@ -21,6 +21,11 @@
 //              K/V tiles of 128 cache rows through a kPfStages ring
 //   warp 9     TMEM allocator; MMA issuer of slot A
 //   warp 10    MMA issuer of slot B
+//   warp 11    idle (completes the third warpgroup for the register split)
+// The block launches at kPfLaunchRegs registers per thread; the two softmax
+// warpgroups then raise theirs to kPfSoftmaxRegs (a 128-column S row lives
+// in registers) and the third drops to kPfOtherRegs:
+// 256 * 232 + 128 * 40 = 384 * 168.
 // Per KV tile j the issuer of slot x issues, in order,
 //   S_x(j) = Q_x K_j^T      (M=128 N=128 K=64, smem x smem -> TMEM)
 //   PV_x(j-1) = P_x V       (M=128 N=64 K=128, TMEM x smem -> TMEM O_x)
@@ -58,7 +63,12 @@ namespace pl {
 constexpr int kPfBlockM = 128;  // query rows per slot
 constexpr int kPfBlockN = 128;  // cache rows per KV tile
 constexpr int kPfStages = 4;    // K/V ring depth
-constexpr int kPfThreads = 352;
+constexpr int kPfThreads = 384;
+constexpr int kPfLaunchRegs = 168;   // 65536 / 384 rounded down to 8
+constexpr int kPfSoftmaxRegs = 232;
+constexpr int kPfOtherRegs = 40;
+static_assert(256 * kPfSoftmaxRegs + 128 * kPfOtherRegs <= kPfThreads * kPfLaunchRegs,
+              "register split exceeds the launch allocation");
 constexpr float kPfRescaleLog2 = 8.0f;  // raise the running max only past 2^8
 
 struct PrefillArgs {
@@ -201,130 +211,133 @@ __global__ void __launch_bounds__(kPfThreads, 1)
   // the work counters are read only after it has finished
   asm volatile("griddepcontrol.wait;" ::: "memory");
   const uint32_t tmem = sm.tmem_base;
-
-  if (warp == 8) {
-    // --------------------------------------------------- scheduler + TMA
-    if (lane == 0) {
-      tma_prefetch_desc(&tm_q);
-      tma_prefetch_desc(&tm_k);
-      tma_prefetch_desc(&tm_v);
-      const int n_items = pf_n_items(a);
-      int J = 0, k = 0;
-      bool ok = true;
-      while (true) {
-        int item = ok ? atomicAdd(&a.work[0], 1) : -1;
-        if (item >= n_items) item = -1;
-        if (k >= 2 && !mbar_wait_bounded(&sm.item_empty[k & 1], ((k - 2) >> 1) & 1)) {
-          atomicOr(a.err, ERR_TIMEOUT_EMPTY);
-          break;  // consumers time out on item_full and wind down
-        }
-        sm.item[k & 1] = item;
-        mbar_arrive(&sm.item_full[k & 1]);
-        if (item < 0) break;
-        const PfItem it = pf_item(a, item);
-        // Q of the previous item is in use until its last S MMAs complete
-        if (k >= 1 && !mbar_wait_bounded(&sm.q_empty, (k - 1) & 1)) {
-          atomicOr(a.err, ERR_TIMEOUT_EMPTY);
-          ok = false;
-          ++k;
-          continue;
-        }
-        mbar_arrive_expect_tx(&sm.q_full, n_slots * kPfBlockM * 128);
-        tma_load_3d(sm.q[0], &tm_q, &sm.q_full, 0, it.head0, it.q_row0);
-        if (n_slots == 2) tma_load_3d(sm.q[1], &tm_q, &sm.q_full, 0, it.head1, it.q_row0);
-        for (int j = 0; j < it.nkv; ++j, ++J) {
-          const int s = J % kPfStages;
-          if (J >= kPfStages && !mbar_wait_bounded(&sm.kv_empty[s], ((J / kPfStages) - 1) & 1)) {
+  if (warp >= 8) {
+    regs_dec<kPfOtherRegs>();  // warp 11 only completes the warpgroup
+    if (warp == 8) {
+      // --------------------------------------------------- scheduler + TMA
+      if (lane == 0) {
+        tma_prefetch_desc(&tm_q);
+        tma_prefetch_desc(&tm_k);
+        tma_prefetch_desc(&tm_v);
+        const int n_items = pf_n_items(a);
+        int J = 0, k = 0;
+        bool ok = true;
+        while (true) {
+          int item = ok ? atomicAdd(&a.work[0], 1) : -1;
+          if (item >= n_items) item = -1;
+          if (k >= 2 && !mbar_wait_bounded(&sm.item_empty[k & 1], ((k - 2) >> 1) & 1)) {
+            atomicOr(a.err, ERR_TIMEOUT_EMPTY);
+            break;  // consumers time out on item_full and wind down
+          }
+          sm.item[k & 1] = item;
+          mbar_arrive(&sm.item_full[k & 1]);
+          if (item < 0) break;
+          const PfItem it = pf_item(a, item);
+          // Q of the previous item is in use until its last S MMAs complete
+          if (k >= 1 && !mbar_wait_bounded(&sm.q_empty, (k - 1) & 1)) {
             atomicOr(a.err, ERR_TIMEOUT_EMPTY);
             ok = false;
-            break;
+            ++k;
+            continue;
           }
-          mbar_arrive_expect_tx(&sm.kv_full[s], 2 * kPfBlockN * 128);
-          tma_load_4d(sm.k[s], &tm_k, &sm.kv_full[s], 0, j * kPfBlockN, it.kvh, a.slab);
-          tma_load_4d(sm.v[s], &tm_v, &sm.kv_full[s], 0, j * kPfBlockN, it.kvh, a.slab);
+          mbar_arrive_expect_tx(&sm.q_full, n_slots * kPfBlockM * 128);
+          tma_load_3d(sm.q[0], &tm_q, &sm.q_full, 0, it.head0, it.q_row0);
+          if (n_slots == 2) tma_load_3d(sm.q[1], &tm_q, &sm.q_full, 0, it.head1, it.q_row0);
+          for (int j = 0; j < it.nkv; ++j, ++J) {
+            const int s = J % kPfStages;
+            if (J >= kPfStages && !mbar_wait_bounded(&sm.kv_empty[s], ((J / kPfStages) - 1) & 1)) {
+              atomicOr(a.err, ERR_TIMEOUT_EMPTY);
+              ok = false;
+              break;
+            }
+            mbar_arrive_expect_tx(&sm.kv_full[s], 2 * kPfBlockN * 128);
+            tma_load_4d(sm.k[s], &tm_k, &sm.kv_full[s], 0, j * kPfBlockN, it.kvh, a.slab);
+            tma_load_4d(sm.v[s], &tm_v, &sm.kv_full[s], 0, j * kPfBlockN, it.kvh, a.slab);
+          }
+          ++k;
         }
-        ++k;
-      }
-      // never leave with copies in flight: the last use of each stage must land
-      for (int j = J - kPfStages; j < J; ++j)
-        if (j >= 0) mbar_wait_bounded(&sm.kv_full[j % kPfStages], (j / kPfStages) & 1);
-      if (k >= 1) mbar_wait_bounded(&sm.q_full, (k - 1) & 1);
-      // the last CTA to stop fetching resets the counters for the next launch
-      __threadfence();
-      if (atomicAdd(&a.work[1], 1) == static_cast<int>(gridDim.x) - 1) {
-        a.work[0] = 0;
-        a.work[1] = 0;
+        // never leave with copies in flight: the last use of each stage must land
+        for (int j = J - kPfStages; j < J; ++j)
+          if (j >= 0) mbar_wait_bounded(&sm.kv_full[j % kPfStages], (j / kPfStages) & 1);
+        if (k >= 1) mbar_wait_bounded(&sm.q_full, (k - 1) & 1);
+        // the last CTA to stop fetching resets the counters for the next launch
         __threadfence();
-      }
-    }
-  } else if (warp >= 9) {
-    // ------------------------------------------------- MMA issuer of slot x
-    const int x = warp - 9;
-    if (lane == 0) {
-      const uint32_t idesc_qk = idesc_f16_f32(128, 128, 0);
-      const uint32_t idesc_pv = idesc_f16_f32(128, 64, 1);
-      const bool active = x < n_slots;
-      const uint32_t q_addr = smem_u32(sm.q[x]);
-      int J = 0, k = 0;
-      bool ok = true;
-      // PV_x of global tile g (first tile of its item if `first`), then
-      // release of its K/V stage
-      auto issue_pv = [&](int g, bool first) -> bool {
-        const int s = g % kPfStages, pb = g & 1;
-        if (!mbar_wait_bounded(&sm.p_full[x][pb], (g >> 1) & 1)) return false;
-        // the previous item's O must be read out before it is overwritten
-        if (first && k >= 1 && !mbar_wait_bounded(&sm.o_free[x], (k - 1) & 1)) return false;
-        tc_fence_after();
-        const uint32_t v_addr = smem_u32(sm.v[s]);
-#pragma unroll
-        for (int kk = 0; kk < kPfBlockN / 16; ++kk) {  // 16 keys = 8 P columns per MMA
-          const uint64_t bd = smem_desc_sw128(v_addr + kk * 16 * 128, 16, 1024);
-          tc_mma_ts(tmem + pf_col_o(x), tmem + pf_col_p(x) + kk * 8, bd, idesc_pv,
-                    (first && kk == 0) ? 0u : 1u);
+        if (atomicAdd(&a.work[1], 1) == static_cast<int>(gridDim.x) - 1) {
+          a.work[0] = 0;
+          a.work[1] = 0;
+          __threadfence();
         }
-        tc_commit(&sm.pv_done[x][pb]);
-        tc_commit(&sm.kv_empty[s]);
-        return true;
-      };
-      while (ok) {
-        if (!mbar_wait_bounded(&sm.item_full[k & 1], (k >> 1) & 1)) { ok = false; break; }
-        const int item = *reinterpret_cast<volatile int*>(&sm.item[k & 1]);
-        mbar_arrive(&sm.item_empty[k & 1]);
-        if (item < 0) break;
-        const PfItem it = pf_item(a, item);
-        if (!active) {  // no second query head: nothing to issue
+      }
+    } else if (warp <= 10) {
+      // ------------------------------------------------- MMA issuer of slot x
+      const int x = warp - 9;
+      if (lane == 0) {
+        const uint32_t idesc_qk = idesc_f16_f32(128, 128, 0);
+        const uint32_t idesc_pv = idesc_f16_f32(128, 64, 1);
+        const bool active = x < n_slots;
+        const uint32_t q_addr = smem_u32(sm.q[x]);
+        int J = 0, k = 0;
+        bool ok = true;
+        // PV_x of global tile g (first tile of its item if `first`), then
+        // release of its K/V stage
+        auto issue_pv = [&](int g, bool first) -> bool {
+          const int s = g % kPfStages, pb = g & 1;
+          if (!mbar_wait_bounded(&sm.p_full[x][pb], (g >> 1) & 1)) return false;
+          // the previous item's O must be read out before it is overwritten
+          if (first && k >= 1 && !mbar_wait_bounded(&sm.o_free[x], (k - 1) & 1)) return false;
+          tc_fence_after();
+          const uint32_t v_addr = smem_u32(sm.v[s]);
+  #pragma unroll
+          for (int kk = 0; kk < kPfBlockN / 16; ++kk) {  // 16 keys = 8 P columns per MMA
+            const uint64_t bd = smem_desc_sw128(v_addr + kk * 16 * 128, 16, 1024);
+            tc_mma_ts(tmem + pf_col_o(x), tmem + pf_col_p(x) + kk * 8, bd, idesc_pv,
+                      (first && kk == 0) ? 0u : 1u);
+          }
+          tc_commit(&sm.pv_done[x][pb]);
+          tc_commit(&sm.kv_empty[s]);
+          return true;
+        };
+        while (ok) {
+          if (!mbar_wait_bounded(&sm.item_full[k & 1], (k >> 1) & 1)) { ok = false; break; }
+          const int item = *reinterpret_cast<volatile int*>(&sm.item[k & 1]);
+          mbar_arrive(&sm.item_empty[k & 1]);
+          if (item < 0) break;
+          const PfItem it = pf_item(a, item);
+          if (!active) {  // no second query head: nothing to issue
+            J += it.nkv;
+            ++k;
+            continue;
+          }
+          if (!mbar_wait_bounded(&sm.q_full, k & 1)) { ok = false; break; }
+          for (int j = 0; j < it.nkv && ok; ++j) {
+            const int g = J + j;
+            const int s = g % kPfStages;
+            if (!mbar_wait_bounded(&sm.kv_full[s], (g / kPfStages) & 1)) { ok = false; break; }
+            if (g >= 1 && !mbar_wait_bounded(&sm.s_free[x], (g - 1) & 1)) { ok = false; break; }
+            tc_fence_after();
+            const uint32_t k_addr = smem_u32(sm.k[s]);
+  #pragma unroll
+            for (int kk = 0; kk < 4; ++kk) {
+              const uint64_t ad = smem_desc_sw128(q_addr + kk * 32, 16, 1024);
+              const uint64_t bd = smem_desc_sw128(k_addr + kk * 32, 16, 1024);
+              tc_mma_ss(tmem + pf_col_s(x), ad, bd, idesc_qk, kk > 0 ? 1u : 0u);
+            }
+            tc_commit(&sm.s_full[x]);
+            if (j == it.nkv - 1) tc_commit(&sm.q_empty);  // Q_x free once these S MMAs land
+            if (j >= 1 && !issue_pv(g - 1, j == 1)) ok = false;
+          }
+          if (ok && !issue_pv(J + it.nkv - 1, it.nkv == 1)) ok = false;
           J += it.nkv;
           ++k;
-          continue;
         }
-        if (!mbar_wait_bounded(&sm.q_full, k & 1)) { ok = false; break; }
-        for (int j = 0; j < it.nkv && ok; ++j) {
-          const int g = J + j;
-          const int s = g % kPfStages;
-          if (!mbar_wait_bounded(&sm.kv_full[s], (g / kPfStages) & 1)) { ok = false; break; }
-          if (g >= 1 && !mbar_wait_bounded(&sm.s_free[x], (g - 1) & 1)) { ok = false; break; }
-          tc_fence_after();
-          const uint32_t k_addr = smem_u32(sm.k[s]);
-#pragma unroll
-          for (int kk = 0; kk < 4; ++kk) {
-            const uint64_t ad = smem_desc_sw128(q_addr + kk * 32, 16, 1024);
-            const uint64_t bd = smem_desc_sw128(k_addr + kk * 32, 16, 1024);
-            tc_mma_ss(tmem + pf_col_s(x), ad, bd, idesc_qk, kk > 0 ? 1u : 0u);
-          }
-          tc_commit(&sm.s_full[x]);
-          if (j == it.nkv - 1) tc_commit(&sm.q_empty);  // Q_x free once these S MMAs land
-          if (j >= 1 && !issue_pv(g - 1, j == 1)) ok = false;
-        }
-        if (ok && !issue_pv(J + it.nkv - 1, it.nkv == 1)) ok = false;
-        J += it.nkv;
-        ++k;
+        if (!ok) atomicOr(a.err, ERR_TIMEOUT_MMA);
+        // all issued MMAs must finish before TMEM is freed
+        tc_commit(&sm.mma_done[x]);
+        mbar_wait_bounded(&sm.mma_done[x], 0);
       }
-      if (!ok) atomicOr(a.err, ERR_TIMEOUT_MMA);
-      // all issued MMAs must finish before TMEM is freed
-      tc_commit(&sm.mma_done[x]);
-      mbar_wait_bounded(&sm.mma_done[x], 0);
     }
   } else {
+    regs_inc<kPfSoftmaxRegs>();
     // ------------------------------------------------------------ softmax
     const int x = warp >> 2;                     // slot
     const int r = threadIdx.x & 127;             // query row in the tile, TMEM lane
@@ -491,6 +504,16 @@ inline int launch_prefill_attention(const PrefillArgs& a, const CUtensorMap& tm_
     if (cudaFuncSetAttribute(prefill_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              kPfSmemBytes) != cudaSuccess)
       return -4;
+    // the warpgroup register split assumes exactly this launch allocation:
+    // with fewer registers per thread the softmax warps' increase could
+    // never be granted
+    cudaFuncAttributes fa;
+    if (cudaFuncGetAttributes(&fa, prefill_attn_kernel) != cudaSuccess ||
+        fa.numRegs != kPfLaunchRegs) {
+      fprintf(stderr, "pl_attn: prefill kernel built with %d registers per thread, needs %d\n",
+              fa.numRegs, kPfLaunchRegs);
+      return -4;
+    }
     attr_done = true;
   }
   const int per_tile = a.kv_mul >= 2 ? a.n_heads / 2 : a.n_heads;
