@@ -69,6 +69,7 @@ constexpr int kPfSoftmaxRegs = 232;
 constexpr int kPfOtherRegs = 40;
 static_assert(256 * kPfSoftmaxRegs + 128 * kPfOtherRegs <= kPfThreads * kPfLaunchRegs,
               "register split exceeds the launch allocation");
+constexpr int kPfStagePitch = 36;    // floats per row of the output staging buffer
 constexpr float kPfRescaleLog2 = 8.0f;  // raise the running max only past 2^8
 
 struct PrefillArgs {
@@ -86,6 +87,9 @@ struct PfSmem {
   uint8_t q[2][kPfBlockM * 128];                // Q_A, Q_B: 16 KB each
   uint8_t k[kPfStages][kPfBlockN * 128];        // 16 KB each
   uint8_t v[kPfStages][kPfBlockN * 128];        // 16 KB each
+  // per softmax warp, 32 rows x 32 output columns (row pitch padded so
+  // that both the row-wise writes and the transposed reads are conflict-free)
+  float stage[8][32 * kPfStagePitch];
   uint64_t q_full, q_empty;
   uint64_t kv_full[kPfStages], kv_empty[kPfStages];
   uint64_t s_full[2], s_free[2], p_full[2][2], pv_done[2][2], o_free[2];
@@ -96,6 +100,7 @@ struct PfSmem {
 };
 
 constexpr int kPfSmemBytes = static_cast<int>(sizeof(PfSmem)) + 1024;
+static_assert(kPfSmemBytes <= 227 * 1024, "prefill shared memory above the per-CTA limit");
 
 // TMEM column map (512 columns allocated): S_A, S_B (128 FP32 columns
 // each), O_A, O_B (64 FP32), P_A, P_B (128 FP16 = 64 columns)
@@ -469,15 +474,32 @@ __global__ void __launch_bounds__(kPfThreads, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&sm.o_free[x]);
-      const int row = it.q_row0 + r;
-      if (row < a.n_tok) {
-        const float inv = 1.0f / l_run;
-        float* dst = a.out + static_cast<size_t>(row) * a.out_stride + (x ? it.head1 : it.head0) * 64;
+      // O / l to the output through the warp's staging buffer, 32 columns
+      // at a time: a thread holds one row, so direct stores would touch 32
+      // rows per instruction; read back transposed, each store instruction
+      // covers four rows x 128 contiguous bytes
+      const float inv = 1.0f / l_run;
+      float* stg = sm.stage[warp];
+      const int row_base = it.q_row0 + (warp & 3) * 32;
+      float* dst = a.out + (x ? it.head1 : it.head0) * 64 + (lane & 7) * 4;
 #pragma unroll
-        for (int d = 0; d < 64; d += 4)
-          *reinterpret_cast<float4*>(dst + d) =
-              make_float4(__uint_as_float(sv[d]) * inv, __uint_as_float(sv[d + 1]) * inv,
-                          __uint_as_float(sv[d + 2]) * inv, __uint_as_float(sv[d + 3]) * inv);
+      for (int hc = 0; hc < 2; ++hc) {
+#pragma unroll
+        for (int c = 0; c < 32; c += 4)
+          *reinterpret_cast<float4*>(stg + lane * kPfStagePitch + c) = make_float4(
+              __uint_as_float(sv[32 * hc + c]) * inv, __uint_as_float(sv[32 * hc + c + 1]) * inv,
+              __uint_as_float(sv[32 * hc + c + 2]) * inv, __uint_as_float(sv[32 * hc + c + 3]) * inv);
+        __syncwarp();
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const int rr = 4 * i + (lane >> 3);
+          const float4 val =
+              *reinterpret_cast<const float4*>(stg + rr * kPfStagePitch + (lane & 7) * 4);
+          if (row_base + rr < a.n_tok)
+            *reinterpret_cast<float4*>(dst + static_cast<size_t>(row_base + rr) * a.out_stride +
+                                       32 * hc) = val;
+        }
+        __syncwarp();
       }
       J += it.nkv;
       ++k;
