@@ -34,8 +34,13 @@ PL_EDEVICE = -7
 PL_EUNSUPPORTED = -8
 PL_ROPE_LLAMA = 0
 PL_ROPE_QWEN = 1
-HEAD_DIM = 64
-PART_STRIDE = HEAD_DIM + 4   # floats per partial: m, l, 2 pad, o[64]
+HEAD_DIM = 64                # default head_dim; 64 and 128 are supported
+PART_STRIDE = HEAD_DIM + 4   # floats per partial at head_dim 64: m, l, 2 pad, o[64]
+
+
+def part_stride(head_dim: int = HEAD_DIM) -> int:
+    """Floats per head in a partial block: m, l, 2 pad, o[head_dim]."""
+    return head_dim + 4
 
 
 class PlAttnError(RuntimeError):
@@ -131,6 +136,7 @@ class Attn:
         self.head_dim, self.max_seq, self.n_seqs = head_dim, max_seq, n_seqs
         self.q_dim = n_heads * head_dim
         self.kv_dim = n_kv_heads * head_dim
+        self.part_stride = part_stride(head_dim)
         _check(self.lib.pl_attn_init(n_layers, n_heads, n_kv_heads, head_dim, max_seq,
                                      float(rope_base), rope_type, n_seqs, device),
                "pl_attn_init")

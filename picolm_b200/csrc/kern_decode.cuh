@@ -56,9 +56,13 @@
 
 namespace pl {
 
-constexpr int kHD = 64;                 // head_dim supported by the kernels
-constexpr int kPartStride = kHD + 4;    // floats per partial: m, l, 2 pad, o[64]
+// Head dims supported by the kernels: 64 and 128 (template parameter HD).
+// The KV tiles are staged as 64-element (128-byte) halves under the 128-byte
+// swizzle, one region per half.
+constexpr int kHD = 64;                 // head_dim of the tensor-core prefill
 constexpr int kPartO = 4;               // offset of o in a partial (16-byte aligned)
+// floats per partial of one head: m, l, 2 pad, o[HD]
+__host__ __device__ constexpr int part_stride(int hd) { return hd + kPartO; }
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr int kMaxLaunchSeqs = 1024;    // sequences per launch (prefix scan in smem)
 constexpr int kMaxCombineParts = 16;    // device partials merged by combine_kernel
@@ -74,15 +78,18 @@ struct DecodeArgs {
   int n;                 // sequences in this launch (<= kMaxLaunchSeqs)
   const int* seqs;       // cache slot per sequence (nullptr: seq1 for all)
   const int* pos;        // global position of the new token (nullptr: pos1)
-  int seq1, pos1;        // scalar slot / position when the arrays are null
-  const float* q;        // [n][n_heads*64]   before RoPE
+  int seq1, pos1;        // slot / position when the arrays are null: sequence i of the
+  int pos_inc;           //   launch is at position pos1 + i * pos_inc
+  const float* q;        // [n][n_heads*HD]   before RoPE
   const float* k;        // [n][kv_dim]       before RoPE
   const float* v;        // [n][kv_dim]
-  float* out;            // [n][n_heads*64]   normalised output (mode 0)
-  float* part;           // [gridDim.x + n][n_heads][kPartStride] segment partials
-  float* part_out;       // mode 1: merged partial per sequence [n][n_heads][kPartStride]
+  float* out;            // [n][out_stride]   normalised output (mode 0), head h at h*HD
+  int out_stride;        // floats between the output rows of consecutive sequences
+  float* part;           // [gridDim.x + n][n_heads][part_stride(HD)] segment partials
+  float* part_out;       // mode 1: merged partial per sequence [n][n_heads][part_stride(HD)]
   int2* seg_info;        // [n] (first slot, segment count), written by CTA 0
-  // mode 0: attend rows [0, pos], append at row pos.
+  // mode 0: attend rows [0, pos], append at row pos (if append; else the row
+  //         is already in the cache).
   // mode 1: shard of a KV-split sequence: attend local rows [0, n_rows),
   //         append (if append) at local row pos - row0.
   int mode, row0, n_rows, append;
@@ -92,7 +99,8 @@ struct DecodeArgs {
 
 // RoPE of the element pair (d, d+1) of one head (d even), as picolm's
 // rope() computes it (tensor.c:537-601).  LLaMA rotates (d, d+1) together;
-// Qwen pairs element e with e +/- 32.
+// Qwen pairs element e with e +/- HD/2.
+template <int HD>
 __device__ __forceinline__ float2 rope_two(const float* x, int d, const float* cs,
                                            const float* sn, int rope_type) {
   float2 y;
@@ -104,11 +112,11 @@ __device__ __forceinline__ float2 rope_two(const float* x, int d, const float* c
 #pragma unroll
     for (int e = 0; e < 2; ++e) {
       const int j = d + e;
-      if (j < kHD / 2)
-        r[e] = __fsub_rn(__fmul_rn(x[j], cs[j]), __fmul_rn(x[j + kHD / 2], sn[j]));
+      if (j < HD / 2)
+        r[e] = __fsub_rn(__fmul_rn(x[j], cs[j]), __fmul_rn(x[j + HD / 2], sn[j]));
       else
-        r[e] = __fadd_rn(__fmul_rn(x[j - kHD / 2], sn[j - kHD / 2]),
-                         __fmul_rn(x[j], cs[j - kHD / 2]));
+        r[e] = __fadd_rn(__fmul_rn(x[j - HD / 2], sn[j - HD / 2]),
+                         __fmul_rn(x[j], cs[j - HD / 2]));
     }
     y.x = r[0];
     y.y = r[1];
@@ -150,7 +158,7 @@ __device__ __forceinline__ int seq_of(const DecodeArgs& a, int i) {
   return a.seqs ? a.seqs[i] : a.seq1;
 }
 __device__ __forceinline__ int pos_of(const DecodeArgs& a, int i) {
-  return a.pos ? a.pos[i] : a.pos1;
+  return a.pos ? a.pos[i] : a.pos1 + i * a.pos_inc;
 }
 
 // Rows attended and the append row of sequence i.
@@ -158,17 +166,17 @@ __device__ __forceinline__ void seq_rows(const DecodeArgs& a, int i, int& att_ro
                                          int& app_row) {
   const int pos = pos_of(a, i);
   att_rows = a.mode == 0 ? pos + 1 : a.n_rows;
-  app_row = a.mode == 0 ? pos : (a.append ? pos - a.row0 : -1);
+  app_row = a.mode == 0 ? (a.append ? pos : -1) : (a.append ? pos - a.row0 : -1);
 }
 
 // -------------------------------------------------------------- merge
 // Log-sum-exp merge of `cnt` <= MAXC partials (slots src0 + j*slot_stride)
-// into either a normalised output out[n_heads*64] or a partial at dst
+// into either a normalised output out[n_heads*HD] or a partial at dst
 // (which may be the first source slot).  Whole block.  The partials were
 // written by other CTAs moments ago, so the merge is bound by L2 latency,
 // not bandwidth: every thread issues all of its loads before using any.
 // smem_w >= 3 * MAXC * n_heads + 2 * n_heads floats.
-template <int MAXC>
+template <int MAXC, int HD>
 __device__ __forceinline__ void merge_slots(const float* src0, size_t slot_stride, int cnt,
                                             int n_heads, float* out, float* dst, float* smem_w) {
   const int tid = threadIdx.x, nthr = blockDim.x;
@@ -181,7 +189,7 @@ __device__ __forceinline__ void merge_slots(const float* src0, size_t slot_strid
   for (int t = tid; t < cnt * n_heads; t += nthr) {
     const int j = t / n_heads, h = t - j * n_heads;
     const float2 ml = __ldcg(reinterpret_cast<const float2*>(src0 + j * slot_stride +
-                                                             h * kPartStride));
+                                                             h * part_stride(HD)));
     sm_m[t] = ml.x;
     sm_l[t] = ml.y;
   }
@@ -205,9 +213,9 @@ __device__ __forceinline__ void merge_slots(const float* src0, size_t slot_strid
   }
   __syncthreads();
   // (3) the weighted sums, float4 at a time, all loads of an output issued together
-  for (int idx = tid; idx < n_heads * (kHD / 4); idx += nthr) {
-    const int h = idx / (kHD / 4), q4 = idx % (kHD / 4);
-    const float* base = src0 + h * kPartStride + kPartO + 4 * q4;
+  for (int idx = tid; idx < n_heads * (HD / 4); idx += nthr) {
+    const int h = idx / (HD / 4), q4 = idx % (HD / 4);
+    const float* base = src0 + h * part_stride(HD) + kPartO + 4 * q4;
     float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
     for (int j0 = 0; j0 < cnt; j0 += 8) {  // 8 loads in flight per thread per round
       float4 v[8];
@@ -225,14 +233,14 @@ __device__ __forceinline__ void merge_slots(const float* src0, size_t slot_strid
         }
     }
     if (out)
-      reinterpret_cast<float4*>(out + h * kHD)[q4] = acc;
+      reinterpret_cast<float4*>(out + h * HD)[q4] = acc;
     else
-      reinterpret_cast<float4*>(dst + h * kPartStride + kPartO)[q4] = acc;
+      reinterpret_cast<float4*>(dst + h * part_stride(HD) + kPartO)[q4] = acc;
   }
   if (!out)
     for (int h = tid; h < n_heads; h += nthr) {
-      dst[h * kPartStride] = sM[h];
-      dst[h * kPartStride + 1] = sL[h];
+      dst[h * part_stride(HD)] = sM[h];
+      dst[h * part_stride(HD) + 1] = sL[h];
     }
   __syncthreads();
 }
@@ -240,14 +248,17 @@ __device__ __forceinline__ void merge_slots(const float* src0, size_t slot_strid
 // ------------------------------------------------------------ consumer
 // KV head w of sequence i over local tiles [t_lo, t_hi); pipeline index of
 // tile t_lo is it0.  Writes the final result if the segment is the whole
-// sequence, else its partial to slot.
-template <int TP, int NSTAGE>
+// sequence, else its partial to slot.  A K (or V) tile is HD/64 regions of
+// region_bytes (the 64-element halves of every row, all KV heads), each in
+// the 128-byte swizzle; head w's rows start at w * TP * 128 in a region.
+template <int TP, int NSTAGE, int HD>
 __device__ __forceinline__ void consume_segment(const DecodeArgs& a, int w, int lane, int i,
                                                 int t_lo, int t_hi, int it0, bool whole,
                                                 int slot, const uint8_t* sK, const uint8_t* sV,
-                                                int tile_bytes, uint64_t* full, uint64_t* empty,
-                                                bool& ok) {
-  const int kv_dim = a.n_kv_heads * kHD;
+                                                int tile_bytes, int region_bytes, uint64_t* full,
+                                                uint64_t* empty, bool& ok) {
+  constexpr int kHalves = HD / 64;
+  const int kv_dim = a.n_kv_heads * HD;
   const int g = lane >> 2, c = lane & 3;
   const int kv_mul = a.kv_mul;
   const bool row_valid = g < kv_mul;
@@ -256,20 +267,20 @@ __device__ __forceinline__ void consume_segment(const DecodeArgs& a, int w, int 
   int att_rows, app_row;
   seq_rows(a, i, att_rows, app_row);
   const int slab = seq_of(a, i) * a.n_layers + a.layer;
-  const float* cs = a.cos_tab + static_cast<size_t>(pos) * (kHD / 2);
-  const float* sn = a.sin_tab + static_cast<size_t>(pos) * (kHD / 2);
+  const float* cs = a.cos_tab + static_cast<size_t>(pos) * (HD / 2);
+  const float* sn = a.sin_tab + static_cast<size_t>(pos) * (HD / 2);
   const bool appends = app_row >= t_lo * TP && app_row < t_hi * TP;
 
   // q fragments: this thread needs dims 16kk+2c, +1 and 16kk+8+2c, +1
-  uint32_t qa[4][4];
+  uint32_t qa[HD / 16][4];
   {
-    const float* qrow = a.q + (static_cast<size_t>(i) * a.n_heads + qh) * kHD;
+    const float* qrow = a.q + (static_cast<size_t>(i) * a.n_heads + qh) * HD;
 #pragma unroll
-    for (int kk = 0; kk < 4; ++kk) {
+    for (int kk = 0; kk < HD / 16; ++kk) {
 #pragma unroll
       for (int hf = 0; hf < 2; ++hf) {
         const int d = 16 * kk + 8 * hf + 2 * c;
-        float2 y = rope_two(qrow, d, cs, sn, a.rope_type);
+        float2 y = rope_two<HD>(qrow, d, cs, sn, a.rope_type);
         if (!row_valid) y = make_float2(0.f, 0.f);
         uint32_t hi, lo;
         split_hi_lo(y.x, y.y, hi, lo);
@@ -280,26 +291,34 @@ __device__ __forceinline__ void consume_segment(const DecodeArgs& a, int w, int 
   }
 
   // the appended row: rotate k, encode k and v with picolm's FP16 rounding
-  uint32_t kword = 0, vword = 0;
+  // (lane l holds the element pair 2l of every 64-element half)
+  uint32_t kword[kHalves] = {}, vword[kHalves] = {};
   if (appends) {
-    const float* krow = a.k + static_cast<size_t>(i) * kv_dim + w * kHD;
-    const float* vrow = a.v + static_cast<size_t>(i) * kv_dim + w * kHD;
-    const float2 kr = rope_two(krow, 2 * lane, cs, sn, a.rope_type);
-    const float2 vv = *reinterpret_cast<const float2*>(vrow + 2 * lane);
-    kword = static_cast<uint32_t>(picolm_f32_to_f16(kr.x)) |
-            (static_cast<uint32_t>(picolm_f32_to_f16(kr.y)) << 16);
-    vword = static_cast<uint32_t>(picolm_f32_to_f16(vv.x)) |
-            (static_cast<uint32_t>(picolm_f32_to_f16(vv.y)) << 16);
-    const size_t off = (static_cast<size_t>(slab) * a.max_seq + app_row) * kv_dim + w * kHD;
-    reinterpret_cast<uint32_t*>(a.kc + off)[lane] = kword;
-    reinterpret_cast<uint32_t*>(a.vc + off)[lane] = vword;
+    const float* krow = a.k + static_cast<size_t>(i) * kv_dim + w * HD;
+    const float* vrow = a.v + static_cast<size_t>(i) * kv_dim + w * HD;
+    const size_t off = (static_cast<size_t>(slab) * a.max_seq + app_row) * kv_dim + w * HD;
+#pragma unroll
+    for (int hv = 0; hv < kHalves; ++hv) {
+      const int d = 64 * hv + 2 * lane;
+      const float2 kr = rope_two<HD>(krow, d, cs, sn, a.rope_type);
+      const float2 vv = *reinterpret_cast<const float2*>(vrow + d);
+      kword[hv] = static_cast<uint32_t>(picolm_f32_to_f16(kr.x)) |
+                  (static_cast<uint32_t>(picolm_f32_to_f16(kr.y)) << 16);
+      vword[hv] = static_cast<uint32_t>(picolm_f32_to_f16(vv.x)) |
+                  (static_cast<uint32_t>(picolm_f32_to_f16(vv.y)) << 16);
+    }
+#pragma unroll
+    for (int hv = 0; hv < kHalves; ++hv) {
+      reinterpret_cast<uint32_t*>(a.kc + off)[32 * hv + lane] = kword[hv];
+      reinterpret_cast<uint32_t*>(a.vc + off)[32 * hv + lane] = vword[hv];
+    }
   }
 
   float m_run = -INFINITY;  // running max of row g (log2 domain)
   float l_run = 0.f;        // this thread's share of the row sum
-  float o[8][4];
+  float o[HD / 8][4];
 #pragma unroll
-  for (int j = 0; j < 8; ++j) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.f;
+  for (int j = 0; j < HD / 8; ++j) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.f;
 
   for (int t = t_lo; t < t_hi && ok; ++t) {
     const int it = it0 + (t - t_lo);
@@ -316,8 +335,12 @@ __device__ __forceinline__ void consume_segment(const DecodeArgs& a, int w, int 
     if (patch) {
       const int r = app_row - row0;
       const uint32_t off = sw128(r, lane >> 2) + (lane & 3) * 4;
-      asm volatile("st.shared.u32 [%0], %1;" ::"r"(kbase + off), "r"(kword) : "memory");
-      asm volatile("st.shared.u32 [%0], %1;" ::"r"(vbase + off), "r"(vword) : "memory");
+#pragma unroll
+      for (int hv = 0; hv < kHalves; ++hv) {
+        const uint32_t ro = off + hv * region_bytes;
+        asm volatile("st.shared.u32 [%0], %1;" ::"r"(kbase + ro), "r"(kword[hv]) : "memory");
+        asm volatile("st.shared.u32 [%0], %1;" ::"r"(vbase + ro), "r"(vword[hv]) : "memory");
+      }
       __syncwarp();
     }
 
@@ -327,11 +350,11 @@ __device__ __forceinline__ void consume_segment(const DecodeArgs& a, int w, int 
     for (int nt = 0; nt < TP / 8; ++nt) {
       sacc[nt][0] = sacc[nt][1] = sacc[nt][2] = sacc[nt][3] = 0.f;
 #pragma unroll
-      for (int kp = 0; kp < 2; ++kp) {
+      for (int kp = 0; kp < HD / 32; ++kp) {
         const int r = nt * 8 + (lane & 7);
-        const int ch = 4 * kp + (lane >> 3);
+        const int ch = 4 * kp + (lane >> 3);  // 16-byte chunk of the row, HD/8 of them
         uint32_t b0, b1, b2, b3;
-        ldmatrix_x4(kbase + sw128(r, ch), b0, b1, b2, b3);
+        ldmatrix_x4(kbase + (ch >> 3) * region_bytes + sw128(r, ch & 7), b0, b1, b2, b3);
         mma_16816(sacc[nt], qa[2 * kp], b0, b1);
         mma_16816(sacc[nt], qa[2 * kp + 1], b2, b3);
       }
@@ -355,7 +378,7 @@ __device__ __forceinline__ void consume_segment(const DecodeArgs& a, int w, int 
     const float alpha = ex2(m_run - m_new);
     l_run *= alpha;
 #pragma unroll
-    for (int j = 0; j < 8; ++j) {
+    for (int j = 0; j < HD / 8; ++j) {
       o[j][0] *= alpha;
       o[j][1] *= alpha;
       o[j][2] *= alpha;
@@ -371,11 +394,11 @@ __device__ __forceinline__ void consume_segment(const DecodeArgs& a, int w, int 
       split_hi_lo(p00, p01, pa[0], pa[1]);
       split_hi_lo(p10, p11, pa[2], pa[3]);
 #pragma unroll
-      for (int j2 = 0; j2 < 4; ++j2) {
+      for (int j2 = 0; j2 < HD / 16; ++j2) {
         const int r = 16 * kk + ((lane >> 3) & 1) * 8 + (lane & 7);
         const int ch = 2 * j2 + (lane >> 4);
         uint32_t b0, b1, b2, b3;
-        ldmatrix_x4_trans(vbase + sw128(r, ch), b0, b1, b2, b3);
+        ldmatrix_x4_trans(vbase + (ch >> 3) * region_bytes + sw128(r, ch & 7), b0, b1, b2, b3);
         mma_16816(o[2 * j2], pa, b0, b1);
         mma_16816(o[2 * j2 + 1], pa, b2, b3);
       }
@@ -392,27 +415,28 @@ __device__ __forceinline__ void consume_segment(const DecodeArgs& a, int w, int 
   if (!row_valid) return;
   if (whole && a.mode == 0) {
     const float inv = 1.0f / l_run;
-    float* dst = a.out + (static_cast<size_t>(i) * a.n_heads + qh) * kHD;
+    float* dst = a.out + static_cast<size_t>(i) * a.out_stride + qh * HD;
 #pragma unroll
-    for (int j = 0; j < 8; ++j)
+    for (int j = 0; j < HD / 8; ++j)
       *reinterpret_cast<float2*>(dst + 8 * j + 2 * c) =
           make_float2((o[j][0] + o[j][2]) * inv, (o[j][1] + o[j][3]) * inv);
   } else {
-    float* dst = (whole ? a.part_out + static_cast<size_t>(i) * a.n_heads * kPartStride
-                        : a.part + static_cast<size_t>(slot) * a.n_heads * kPartStride) +
-                 qh * kPartStride;
+    constexpr int PS = part_stride(HD);
+    float* dst = (whole ? a.part_out + static_cast<size_t>(i) * a.n_heads * PS
+                        : a.part + static_cast<size_t>(slot) * a.n_heads * PS) +
+                 qh * PS;
     if (c == 0) {
       dst[0] = m_run;
       dst[1] = l_run;
     }
 #pragma unroll
-    for (int j = 0; j < 8; ++j)
+    for (int j = 0; j < HD / 8; ++j)
       *reinterpret_cast<float2*>(dst + kPartO + 8 * j + 2 * c) =
           make_float2(o[j][0] + o[j][2], o[j][1] + o[j][3]);
   }
 }
 
-template <int TP, int NSTAGE>
+template <int TP, int NSTAGE, int HD>
 __global__ void __launch_bounds__(288) decode_kernel(const DecodeArgs a,
                                                      const __grid_constant__ CUtensorMap tmk,
                                                      const __grid_constant__ CUtensorMap tmv) {
@@ -422,7 +446,9 @@ __global__ void __launch_bounds__(288) decode_kernel(const DecodeArgs a,
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
   const int Hk = a.n_kv_heads;
-  const int tile_bytes = TP * Hk * 128;  // one K (or V) tile: TP rows x all KV heads
+  // one K (or V) tile: TP rows x all KV heads, as HD/64 regions of 64 elements
+  const int region_bytes = TP * Hk * 128;
+  const int tile_bytes = region_bytes * (HD / 64);
   uint8_t* sK = smem;
   uint8_t* sV = smem + NSTAGE * tile_bytes;
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + 2 * NSTAGE * tile_bytes);
@@ -529,8 +555,13 @@ __global__ void __launch_bounds__(288) decode_kernel(const DecodeArgs a,
         mbar_arrive_expect_tx(&full[s], 2u * tile_bytes);
         const int row = static_cast<int>(x - s_prefix[i]) * TP;
         const int slab = seq_of(a, i) * a.n_layers + a.layer;
-        tma_load_4d(sK + s * tile_bytes, &tmk, &full[s], 0, row, 0, slab);
-        tma_load_4d(sV + s * tile_bytes, &tmv, &full[s], 0, row, 0, slab);
+#pragma unroll
+        for (int hv = 0; hv < HD / 64; ++hv) {
+          tma_load_4d(sK + s * tile_bytes + hv * region_bytes, &tmk, &full[s], 64 * hv, row, 0,
+                      slab);
+          tma_load_4d(sV + s * tile_bytes + hv * region_bytes, &tmv, &full[s], 64 * hv, row, 0,
+                      slab);
+        }
         ++issued;
       }
       // never leave with copies in flight: the last use of each stage must land
@@ -546,8 +577,9 @@ __global__ void __launch_bounds__(288) decode_kernel(const DecodeArgs a,
       const int t_lo = static_cast<int>(a0 - s_prefix[i]), t_hi = static_cast<int>(a1 - s_prefix[i]);
       const int ns = P.n_seg(i);
       const int j = cta - P.cta_of(s_prefix[i]);
-      consume_segment<TP, NSTAGE>(a, warp, lane, i, t_lo, t_hi, static_cast<int>(a0 - x0),
-                                  ns == 1, P.slot(i, j), sK, sV, tile_bytes, full, empty, ok);
+      consume_segment<TP, NSTAGE, HD>(a, warp, lane, i, t_lo, t_hi, static_cast<int>(a0 - x0),
+                                      ns == 1, P.slot(i, j), sK, sV, tile_bytes, region_bytes,
+                                      full, empty, ok);
     }
   }
 
@@ -556,7 +588,8 @@ __global__ void __launch_bounds__(288) decode_kernel(const DecodeArgs a,
 // Merge of the segment partials of one decode launch.
 // grid = (n, ceil(n_heads / hpb)), block = kMergeThreads; a block merges
 // heads [h0, h0 + hpb) of sequence i.  Thread t owns float4 column q4 of
-// head hh and every lanes-th segment (lanes = kMergeThreads / (hpb * 16)).
+// head hh and every lanes-th segment (lanes = kMergeThreads / (hpb * HD/4);
+// hpb * HD/4 <= kMergeThreads).
 // Launched with programmatic stream serialisation behind decode_kernel, the
 // grid (sized to stay resident) waits on griddepcontrol.wait; after it, one
 // round trip reads the segment table and one more reads everything else:
@@ -565,6 +598,7 @@ __global__ void __launch_bounds__(288) decode_kernel(const DecodeArgs a,
 // memory.
 constexpr int kMergeThreads = 256;
 
+template <int HD>
 __global__ void __launch_bounds__(kMergeThreads) merge_kernel(const DecodeArgs a, int hpb) {
   __shared__ float4 s_acc[kMergeThreads];
   __shared__ float2 s_ml[kMergeThreads];
@@ -572,17 +606,18 @@ __global__ void __launch_bounds__(kMergeThreads) merge_kernel(const DecodeArgs a
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   asm volatile("griddepcontrol.wait;" ::: "memory");
   const int i = blockIdx.x, h0 = blockIdx.y * hpb, tid = threadIdx.x;
-  const int pairs = hpb * (kHD / 4), lanes = kMergeThreads / pairs;
+  constexpr int PS = part_stride(HD);
+  const int pairs = hpb * (HD / 4), lanes = kMergeThreads / pairs;
   const int pair = tid % pairs, lane_j = tid / pairs;
-  const int hh = pair / (kHD / 4), q4 = pair % (kHD / 4), h = h0 + hh;
+  const int hh = pair / (HD / 4), q4 = pair % (HD / 4), h = h0 + hh;
   const int2 si = a.seg_info[i];
   const int ns = si.y;
   if (ns <= 1) return;  // finished by its single segment (or no rows)
-  const size_t slot_stride = static_cast<size_t>(a.n_heads) * kPartStride;
+  const size_t slot_stride = static_cast<size_t>(a.n_heads) * PS;
   float m_loc = -INFINITY, l_loc = 0.f;
   float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
   if (lane_j < lanes && h < a.n_heads) {
-    const float* base = a.part + static_cast<size_t>(si.x) * slot_stride + h * kPartStride;
+    const float* base = a.part + static_cast<size_t>(si.x) * slot_stride + h * PS;
     for (int j0 = lane_j; j0 < ns; j0 += 8 * lanes) {  // 8 segments in flight
       float2 ml[8];
       float4 v[8];
@@ -640,10 +675,10 @@ __global__ void __launch_bounds__(kMergeThreads) merge_kernel(const DecodeArgs a
     }
   if (a.mode == 0) {
     const float inv = 1.0f / L;
-    reinterpret_cast<float4*>(a.out + (static_cast<size_t>(i) * a.n_heads + h) * kHD)[q4] =
+    reinterpret_cast<float4*>(a.out + static_cast<size_t>(i) * a.out_stride + h * HD)[q4] =
         make_float4(o.x * inv, o.y * inv, o.z * inv, o.w * inv);
   } else {
-    float* dst = a.part_out + (static_cast<size_t>(i) * a.n_heads + h) * kPartStride;
+    float* dst = a.part_out + (static_cast<size_t>(i) * a.n_heads + h) * PS;
     reinterpret_cast<float4*>(dst + kPartO)[q4] = o;
     if (q4 == 0) {
       dst[0] = M;
@@ -653,14 +688,15 @@ __global__ void __launch_bounds__(kMergeThreads) merge_kernel(const DecodeArgs a
 }
 
 // Log-sum-exp merge of partials gathered from several devices (one
-// sequence): n_part <= kMaxCombineParts blocks of [n_heads][kPartStride]
+// sequence): n_part <= kMaxCombineParts blocks of [n_heads][part_stride(HD)]
 // back to back.  grid = 1, block = 256.
+template <int HD>
 __global__ void __launch_bounds__(256) combine_kernel(int n_part, int n_heads,
                                                       const float* __restrict__ parts,
                                                       float* __restrict__ out) {
   extern __shared__ float smem_w[];
-  merge_slots<kMaxCombineParts>(parts, static_cast<size_t>(n_heads) * kPartStride, n_part, n_heads,
-                                out, nullptr, smem_w);
+  merge_slots<kMaxCombineParts, HD>(parts, static_cast<size_t>(n_heads) * part_stride(HD), n_part,
+                                    n_heads, out, nullptr, smem_w);
 }
 
 }  // namespace pl

@@ -10,30 +10,35 @@
 
 namespace pl {
 
-// RoPE in place on n_tok rows of q [n_tok][n_heads*64] and k
-// [n_tok][n_kv_heads*64]; row r uses the table row pos0 + r.
+// RoPE in place on n_tok rows of q [n_tok][n_heads*HD] and k
+// [n_tok][n_kv_heads*HD]; row r uses the table row pos0 + r.
 // grid = (n_tok, ceil((n_heads + n_kv_heads) / 8)), block = 256: warp w of
-// block (r, y) handles head 8y + w of row r, lane l its element pair 2l.
+// block (r, y) handles head 8y + w of row r, lane l its element pairs 2l,
+// 2l + 64, ...
+template <int HD>
 __global__ void rope_inplace_kernel(float* q, float* k, int n_heads, int n_kv_heads, int pos0,
                                     const float* cos_tab, const float* sin_tab, int rope_type) {
   const int r = blockIdx.x;
   const int head = blockIdx.y * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
   if (head >= n_heads + n_kv_heads) return;
   const int pos = pos0 + r;
-  const float* cs = cos_tab + static_cast<size_t>(pos) * (kHD / 2);
-  const float* sn = sin_tab + static_cast<size_t>(pos) * (kHD / 2);
+  const float* cs = cos_tab + static_cast<size_t>(pos) * (HD / 2);
+  const float* sn = sin_tab + static_cast<size_t>(pos) * (HD / 2);
   float* x;
   if (head < n_heads) {
     if (!q) return;
-    x = q + (static_cast<size_t>(r) * n_heads + head) * kHD;
+    x = q + (static_cast<size_t>(r) * n_heads + head) * HD;
   } else {
     if (!k) return;
-    x = k + (static_cast<size_t>(r) * n_kv_heads + (head - n_heads)) * kHD;
+    x = k + (static_cast<size_t>(r) * n_kv_heads + (head - n_heads)) * HD;
   }
   // all reads of the head happen before any write (Qwen pairs cross lanes)
-  const float2 y = rope_two(x, 2 * lane, cs, sn, rope_type);
+  float2 y[HD / 64];
+#pragma unroll
+  for (int hv = 0; hv < HD / 64; ++hv) y[hv] = rope_two<HD>(x, 64 * hv + 2 * lane, cs, sn, rope_type);
   __syncwarp();
-  *reinterpret_cast<float2*>(x + 2 * lane) = y;
+#pragma unroll
+  for (int hv = 0; hv < HD / 64; ++hv) *reinterpret_cast<float2*>(x + 64 * hv + 2 * lane) = y[hv];
 }
 
 // Prefill prologue for n_tok rows starting at position start_pos:
@@ -43,9 +48,10 @@ __global__ void rope_inplace_kernel(float* q, float* k, int n_heads, int n_kv_he
 //   vc[start+r]   = picolm_FP16(v[r])
 // grid = n_tok (one block per token row), block = kPrologueThreads.  A row
 // is cut into units of 8 elements of one head (q heads, then k heads, then
-// v heads); thread t takes units t, t + 256, ...  LLaMA units are 8
-// consecutive elements (4 rotated pairs); Qwen units are elements 4c..4c+3
-// and 32+4c..32+4c+3, which rotate into each other.  Every input and all
+// v heads; HD/8 units per head); thread t takes units t, t + 256, ...
+// LLaMA units are 8 consecutive elements (4 rotated pairs); Qwen units are
+// elements 4c..4c+3 and HD/2+4c..HD/2+4c+3, which rotate into each other.
+// With q16 null the q units are skipped (the cache rows alone).  Every input and all
 // RoPE factors of a unit are 16-byte loads, and a thread issues the loads of
 // two units before it computes either, so the kernel streams at HBM rate
 // instead of waiting on one load at a time.  q, k, v rows and the cache
@@ -58,35 +64,37 @@ struct PrologueUnit {
   int head, part;
 };
 
+template <int HD>
 __device__ __forceinline__ PrologueUnit prologue_load(int u, int r, const float* __restrict__ q,
                                                       const float* __restrict__ k,
                                                       const float* __restrict__ v, int n_heads,
                                                       int n_kv_heads, const float* cs,
                                                       const float* sn, int rope_type) {
   PrologueUnit pu;
-  const int nq = n_heads * 8, nk = n_kv_heads * 8;
-  const int kv_dim = n_kv_heads * kHD;
+  constexpr int kUnits = HD / 8;  // units per head
+  const int nq = n_heads * kUnits, nk = n_kv_heads * kUnits;
+  const int kv_dim = n_kv_heads * HD;
   const float* x;
   if (u < nq) {
     pu.kind = 0;
-    pu.head = u >> 3;
-    x = q + (static_cast<size_t>(r) * n_heads + pu.head) * kHD;
+    pu.head = u / kUnits;
+    x = q + (static_cast<size_t>(r) * n_heads + pu.head) * HD;
   } else if (u < nq + nk) {
     pu.kind = 1;
-    pu.head = (u - nq) >> 3;
-    x = k + static_cast<size_t>(r) * kv_dim + pu.head * kHD;
+    pu.head = (u - nq) / kUnits;
+    x = k + static_cast<size_t>(r) * kv_dim + pu.head * HD;
   } else {
     pu.kind = 2;
-    pu.head = (u - nq - nk) >> 3;
-    x = v + static_cast<size_t>(r) * kv_dim + pu.head * kHD;
+    pu.head = (u - nq - nk) / kUnits;
+    x = v + static_cast<size_t>(r) * kv_dim + pu.head * HD;
   }
-  pu.part = u & 7;
+  pu.part = u % kUnits;
   if (pu.kind == 2 || rope_type == 0) {
     pu.xa = *reinterpret_cast<const float4*>(x + 8 * pu.part);
     pu.xb = *reinterpret_cast<const float4*>(x + 8 * pu.part + 4);
   } else {
     pu.xa = *reinterpret_cast<const float4*>(x + 4 * pu.part);
-    pu.xb = *reinterpret_cast<const float4*>(x + kHD / 2 + 4 * pu.part);
+    pu.xb = *reinterpret_cast<const float4*>(x + HD / 2 + 4 * pu.part);
   }
   if (pu.kind != 2) {
     pu.c = *reinterpret_cast<const float4*>(cs + 4 * pu.part);
@@ -103,15 +111,16 @@ __device__ __forceinline__ uint32_t prologue_pack(float a, float b, bool picolm_
          (static_cast<uint32_t>(picolm_f32_to_f16(b)) << 16);
 }
 
+template <int HD>
 __device__ __forceinline__ void prologue_store(const PrologueUnit& pu, int r, uint16_t* q16,
                                                uint16_t* kc_rows, uint16_t* vc_rows, int n_heads,
                                                int n_kv_heads, int rope_type) {
-  const int kv_dim = n_kv_heads * kHD;
+  const int kv_dim = n_kv_heads * HD;
   uint16_t* dst;
   if (pu.kind == 0)
-    dst = q16 + (static_cast<size_t>(r) * n_heads + pu.head) * kHD;
+    dst = q16 + (static_cast<size_t>(r) * n_heads + pu.head) * HD;
   else
-    dst = (pu.kind == 1 ? kc_rows : vc_rows) + static_cast<size_t>(r) * kv_dim + pu.head * kHD;
+    dst = (pu.kind == 1 ? kc_rows : vc_rows) + static_cast<size_t>(r) * kv_dim + pu.head * HD;
   const bool pr = pu.kind != 0;
   if (pu.kind == 2) {
     *reinterpret_cast<uint4*>(dst + 8 * pu.part) =
@@ -127,7 +136,7 @@ __device__ __forceinline__ void prologue_store(const PrologueUnit& pu, int r, ui
         make_uint4(prologue_pack(y[0], y[1], pr), prologue_pack(y[2], y[3], pr),
                    prologue_pack(y[4], y[5], pr), prologue_pack(y[6], y[7], pr));
   } else {
-    // Qwen: element j (< 32) and j + 32 rotate together
+    // Qwen: element j (< HD/2) and j + HD/2 rotate together
     const float xa[4] = {pu.xa.x, pu.xa.y, pu.xa.z, pu.xa.w};
     const float xb[4] = {pu.xb.x, pu.xb.y, pu.xb.z, pu.xb.w};
     const float c[4] = {pu.c.x, pu.c.y, pu.c.z, pu.c.w};
@@ -140,11 +149,12 @@ __device__ __forceinline__ void prologue_store(const PrologueUnit& pu, int r, ui
     }
     *reinterpret_cast<uint2*>(dst + 4 * pu.part) =
         make_uint2(prologue_pack(lo[0], lo[1], pr), prologue_pack(lo[2], lo[3], pr));
-    *reinterpret_cast<uint2*>(dst + kHD / 2 + 4 * pu.part) =
+    *reinterpret_cast<uint2*>(dst + HD / 2 + 4 * pu.part) =
         make_uint2(prologue_pack(hi[0], hi[1], pr), prologue_pack(hi[2], hi[3], pr));
   }
 }
 
+template <int HD>
 __global__ void __launch_bounds__(kPrologueThreads)
     prefill_prologue_kernel(const float* __restrict__ q, const float* __restrict__ k,
                             const float* __restrict__ v, uint16_t* __restrict__ q16,
@@ -157,17 +167,21 @@ __global__ void __launch_bounds__(kPrologueThreads)
   const int r = blockIdx.x;
   if (r >= n_tok) return;
   const int pos = start_pos + r;
-  const float* cs = cos_tab + static_cast<size_t>(pos) * (kHD / 2);
-  const float* sn = sin_tab + static_cast<size_t>(pos) * (kHD / 2);
-  const int n_units = (n_heads + 2 * n_kv_heads) * 8;
-  for (int u = threadIdx.x; u < n_units; u += 2 * kPrologueThreads) {
+  const float* cs = cos_tab + static_cast<size_t>(pos) * (HD / 2);
+  const float* sn = sin_tab + static_cast<size_t>(pos) * (HD / 2);
+  const int u0 = q16 ? 0 : n_heads * (HD / 8);  // without q16: the cache rows alone
+  const int n_units = (n_heads + 2 * n_kv_heads) * (HD / 8);
+  for (int u = u0 + threadIdx.x; u < n_units; u += 2 * kPrologueThreads) {
     const int u2 = u + kPrologueThreads;
-    const PrologueUnit a = prologue_load(u, r, q, k, v, n_heads, n_kv_heads, cs, sn, rope_type);
+    const PrologueUnit a =
+        prologue_load<HD>(u, r, q, k, v, n_heads, n_kv_heads, cs, sn, rope_type);
     PrologueUnit b;
     b.kind = -1;
-    if (u2 < n_units) b = prologue_load(u2, r, q, k, v, n_heads, n_kv_heads, cs, sn, rope_type);
-    prologue_store(a, r, q16, kc_rows, vc_rows, n_heads, n_kv_heads, rope_type);
-    if (b.kind >= 0) prologue_store(b, r, q16, kc_rows, vc_rows, n_heads, n_kv_heads, rope_type);
+    if (u2 < n_units)
+      b = prologue_load<HD>(u2, r, q, k, v, n_heads, n_kv_heads, cs, sn, rope_type);
+    prologue_store<HD>(a, r, q16, kc_rows, vc_rows, n_heads, n_kv_heads, rope_type);
+    if (b.kind >= 0)
+      prologue_store<HD>(b, r, q16, kc_rows, vc_rows, n_heads, n_kv_heads, rope_type);
   }
 }
 

@@ -50,6 +50,7 @@ __device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
 }
 
 // grid 1, block kXferThreads, dynamic smem (3 * kXferMaxRanks + 2) * n_heads floats
+template <int HD>
 __global__ void __launch_bounds__(kXferThreads) combine_p2p_kernel(
     const float* __restrict__ part, XferPeers peers, int world, int rank, int n_heads,
     float* __restrict__ out, uint32_t* err) {
@@ -68,7 +69,7 @@ __global__ void __launch_bounds__(kXferThreads) combine_p2p_kernel(
   asm volatile("griddepcontrol.wait;" ::: "memory");
   __syncthreads();
   const uint32_t epoch = s_epoch;
-  const int n = n_heads * kPartStride;  // floats per partial, a multiple of 4
+  const int n = n_heads * part_stride(HD);  // floats per partial, a multiple of 4
   const int n4 = n / 4;
   const int parity = static_cast<int>(epoch & 1u);
   // 1. this rank's partial into every rank's slot (parity, rank)
@@ -102,7 +103,8 @@ __global__ void __launch_bounds__(kXferThreads) combine_p2p_kernel(
   // 4. log-sum-exp merge of the world partials of this epoch
   const float* slots = reinterpret_cast<const float*>(peers.base[rank] + kXferStampBytes) +
                        static_cast<size_t>(parity) * world * n;
-  merge_slots<kXferMaxRanks>(slots, static_cast<size_t>(n), world, n_heads, out, nullptr, smem_w);
+  merge_slots<kXferMaxRanks, HD>(slots, static_cast<size_t>(n), world, n_heads, out, nullptr,
+                                 smem_w);
 }
 
 }  // namespace pl

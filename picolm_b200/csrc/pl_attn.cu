@@ -28,14 +28,14 @@
 namespace {
 
 using pl::kHD;
-using pl::kPartStride;
+using pl::part_stride;
 
 typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
                                   const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
                                   const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
 
-constexpr int kDecodeStages = 4;
+constexpr int kDecodeStages = 4;  // K/V ring depth, 3 where a stage would exceed 32 KB
 
 // Receive buffer of the KV-split exchange and the peers' buffers mapped here.
 struct Xfer {
@@ -48,13 +48,15 @@ struct Xfer {
 struct Ctx {
   int device = -1;
   int n_layers = 0, n_heads = 0, n_kv_heads = 0, max_seq = 0, n_seqs = 0, rope_type = 0;
-  int kv_dim = 0, q_dim = 0, kv_mul = 0;
-  int tp = 0;                 // decode tile rows (TP * n_kv_heads == 128)
+  int head_dim = 0, kv_dim = 0, q_dim = 0, kv_mul = 0;
+  int part_floats = 0;        // floats of one partial block: n_heads * (head_dim + 4)
+  int tp = 0;                 // decode tile rows: TP * n_kv_heads * head_dim == 8192, TP >= 16
+  int nstage = 0;             // decode ring depth
   int num_sms = 0, decode_slots = 0;
   size_t layer_elems = 0;     // FP16 words per (seq, layer) slab
   uint16_t* d_k = nullptr;    // [n_seqs][n_layers][max_seq][kv_dim]
   uint16_t* d_v = nullptr;
-  float* d_cos = nullptr;     // [max_seq][32]
+  float* d_cos = nullptr;     // [max_seq][head_dim / 2]
   float* d_sin = nullptr;
   // staging for host-buffer calls
   uint8_t* d_stage = nullptr;
@@ -70,7 +72,7 @@ struct Ctx {
   size_t q16_cap = 0;         // elements
   uint32_t* d_err = nullptr;  // device error word
   cudaStream_t stream = nullptr;
-  CUtensorMap tm_k_dec, tm_v_dec;  // decode: box {64, tp, Hk, 1}
+  CUtensorMap tm_k_dec, tm_v_dec;  // decode: box {64, tp, Hk, 1}, head_dim/64 per tile
   CUtensorMap tm_k_pf, tm_v_pf;    // prefill: box {64, 128 rows, 1, 1}
   CUtensorMap tm_q16;              // prefill q staging: box {64, 1 head, 128 rows}
   EncodeTiledFn encode = nullptr;
@@ -104,16 +106,17 @@ std::mutex g_mu;
     }                                                                     \
   } while (0)
 
-int make_map(EncodeTiledFn enc, CUtensorMap* m, uint16_t* base, int max_seq, int n_kv_heads,
-             int n_slabs, int box_rows, int box_heads) {
-  // dims, innermost first: head_dim, row, kv head, (seq, layer) slab
-  const cuuint64_t dims[4] = {static_cast<cuuint64_t>(kHD), static_cast<cuuint64_t>(max_seq),
+int make_map(EncodeTiledFn enc, CUtensorMap* m, uint16_t* base, int head_dim, int max_seq,
+             int n_kv_heads, int n_slabs, int box_rows, int box_heads) {
+  // dims, innermost first: head_dim, row, kv head, (seq, layer) slab; the box
+  // is 64 elements (128 bytes, the swizzle span) wide
+  const cuuint64_t dims[4] = {static_cast<cuuint64_t>(head_dim), static_cast<cuuint64_t>(max_seq),
                               static_cast<cuuint64_t>(n_kv_heads),
                               static_cast<cuuint64_t>(n_slabs)};
-  const cuuint64_t kv_bytes = static_cast<cuuint64_t>(n_kv_heads) * kHD * 2;
-  const cuuint64_t strides[3] = {kv_bytes, static_cast<cuuint64_t>(kHD) * 2,
+  const cuuint64_t kv_bytes = static_cast<cuuint64_t>(n_kv_heads) * head_dim * 2;
+  const cuuint64_t strides[3] = {kv_bytes, static_cast<cuuint64_t>(head_dim) * 2,
                                  kv_bytes * static_cast<cuuint64_t>(max_seq)};
-  const cuuint32_t box[4] = {static_cast<cuuint32_t>(kHD), static_cast<cuuint32_t>(box_rows),
+  const cuuint32_t box[4] = {64u, static_cast<cuuint32_t>(box_rows),
                              static_cast<cuuint32_t>(box_heads), 1u};
   const cuuint32_t estr[4] = {1, 1, 1, 1};
   CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4, base, dims, strides, box, estr,
@@ -126,12 +129,12 @@ int make_map(EncodeTiledFn enc, CUtensorMap* m, uint16_t* base, int max_seq, int
   return PL_OK;
 }
 
-void host_rope_tables(float* c, float* s, int max_seq, float base) {
+void host_rope_tables(float* c, float* s, int max_seq, int head_dim, float base) {
   // picolm/model.c:545-556, same libm calls in FP32
-  const int half = kHD / 2;
+  const int half = head_dim / 2;
   for (int p = 0; p < max_seq; ++p)
     for (int i = 0; i < half; ++i) {
-      const float inv = powf(base, static_cast<float>(2 * i) / static_cast<float>(kHD));
+      const float inv = powf(base, static_cast<float>(2 * i) / static_cast<float>(head_dim));
       const float theta = static_cast<float>(p) / inv;
       c[static_cast<size_t>(p) * half + i] = cosf(theta);
       s[static_cast<size_t>(p) * half + i] = sinf(theta);
@@ -354,10 +357,12 @@ pl::DecodeArgs decode_args(int layer, int n, const int* d_seqs, const int* d_pos
   a.pos = d_pos;
   a.seq1 = 0;
   a.pos1 = 0;
+  a.pos_inc = 0;
   a.q = d_q;
   a.k = d_k;
   a.v = d_v;
   a.out = d_out;
+  a.out_stride = g->q_dim;
   a.part = part;
   a.part_out = part_out;
   a.seg_info = seg_info;
@@ -365,27 +370,29 @@ pl::DecodeArgs decode_args(int layer, int n, const int* d_seqs, const int* d_pos
   a.row0 = row0;
   a.n_rows = n_rows;
   a.append = append;
-  a.score_scale = pl::kLog2e / sqrtf(static_cast<float>(kHD));
+  a.score_scale = pl::kLog2e / sqrtf(static_cast<float>(g->head_dim));
   a.err = g->d_err;
   return a;
 }
 
-int decode_smem_bytes(int tp) {
-  return kDecodeStages * 2 * tp * g->n_kv_heads * 128 + 1024 + 2 * kDecodeStages * 8;
+int decode_smem_bytes(int tp, int nstage, int head_dim) {
+  return nstage * 2 * tp * g->n_kv_heads * head_dim * 2 + 1024 + 2 * nstage * 8;
 }
 
-template <int TP>
+// The decode kernel instantiations: (tile rows, ring depth, head_dim) for
+// n_kv_heads 8, 4, 2, 1 at head_dim 64 and 128.
+template <int TP, int NS, int HD>
 cudaError_t decode_occupancy(int* per_sm, int threads, int smem) {
-  auto kern = pl::decode_kernel<TP, kDecodeStages>;
+  auto kern = pl::decode_kernel<TP, NS, HD>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return e;
   return cudaOccupancyMaxActiveBlocksPerMultiprocessor(per_sm, kern, threads, smem);
 }
 
-template <int TP>
+template <int TP, int NS, int HD>
 int launch_decode_tp(const pl::DecodeArgs& a, int grid, cudaStream_t st, bool profile) {
-  const int smem = decode_smem_bytes(TP);
-  auto kern = pl::decode_kernel<TP, kDecodeStages>;
+  const int smem = decode_smem_bytes(TP, NS, HD);
+  auto kern = pl::decode_kernel<TP, NS, HD>;
   static bool attr_done = false;
   if (!attr_done) {
     PL_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
@@ -407,7 +414,7 @@ int launch_decode_tp(const pl::DecodeArgs& a, int grid, cudaStream_t st, bool pr
 // block per SM, so the whole merge grid is resident in one wave.
 int launch_merge(const pl::DecodeArgs& a, int decode_grid_ctas, cudaStream_t st, bool profile) {
   if (decode_grid_ctas <= 1) return PL_OK;  // one CTA: every sequence is one segment
-  int hpb = 16;
+  int hpb = pl::kMergeThreads / (g->head_dim / 4);  // 16 at head_dim 64, 8 at 128
   while (hpb > 1 && static_cast<long long>(a.n) * ((g->n_heads + hpb - 1) / hpb) < g->num_sms)
     hpb >>= 1;
   cudaLaunchConfig_t cfg = {};
@@ -420,20 +427,57 @@ int launch_merge(const pl::DecodeArgs& a, int decode_grid_ctas, cudaStream_t st,
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  PL_CUDA(cudaLaunchKernelEx(&cfg, pl::merge_kernel, a, hpb));
+  if (g->head_dim == 128)
+    PL_CUDA(cudaLaunchKernelEx(&cfg, pl::merge_kernel<128>, a, hpb));
+  else
+    PL_CUDA(cudaLaunchKernelEx(&cfg, pl::merge_kernel<64>, a, hpb));
   if (profile) count_launch();
   return PL_OK;
 }
 
-int launch_decode_kernel(const pl::DecodeArgs& a, int grid, cudaStream_t st, bool profile) {
-  int rc;
-  switch (g->tp) {
-    case 16: rc = launch_decode_tp<16>(a, grid, st, profile); break;
-    case 32: rc = launch_decode_tp<32>(a, grid, st, profile); break;
-    case 64: rc = launch_decode_tp<64>(a, grid, st, profile); break;
-    case 128: rc = launch_decode_tp<128>(a, grid, st, profile); break;
-    default: return PL_EUNSUPPORTED;
+// Calls F.template operator()<TP, NS, HD>() for the context's decode
+// configuration; PL_EUNSUPPORTED for any other.
+template <typename F>
+auto with_decode_config(int tp, int nstage, int head_dim, F&& f) -> decltype(f.template operator()<16, 4, 64>()) {
+  if (head_dim == 64 && nstage == kDecodeStages) {
+    switch (tp) {
+      case 16: return f.template operator()<16, kDecodeStages, 64>();
+      case 32: return f.template operator()<32, kDecodeStages, 64>();
+      case 64: return f.template operator()<64, kDecodeStages, 64>();
+      case 128: return f.template operator()<128, kDecodeStages, 64>();
+    }
+  } else if (head_dim == 128) {
+    if (nstage == 3 && tp == 16) return f.template operator()<16, 3, 128>();
+    if (nstage == kDecodeStages) switch (tp) {
+        case 16: return f.template operator()<16, kDecodeStages, 128>();
+        case 32: return f.template operator()<32, kDecodeStages, 128>();
+        case 64: return f.template operator()<64, kDecodeStages, 128>();
+      }
   }
+  return f.unsupported();
+}
+
+struct DecodeLaunch {
+  const pl::DecodeArgs& a;
+  int grid;
+  cudaStream_t st;
+  bool profile;
+  template <int TP, int NS, int HD>
+  int operator()() const { return launch_decode_tp<TP, NS, HD>(a, grid, st, profile); }
+  int unsupported() const { return PL_EUNSUPPORTED; }
+};
+
+struct DecodeOccupancy {
+  int* per_sm;
+  int threads, smem;
+  template <int TP, int NS, int HD>
+  cudaError_t operator()() const { return decode_occupancy<TP, NS, HD>(per_sm, threads, smem); }
+  cudaError_t unsupported() const { return cudaErrorInvalidValue; }
+};
+
+int launch_decode_kernel(const pl::DecodeArgs& a, int grid, cudaStream_t st, bool profile) {
+  const int rc =
+      with_decode_config(g->tp, g->nstage, g->head_dim, DecodeLaunch{a, grid, st, profile});
   if (rc) return rc;
   return launch_merge(a, grid, st, profile);
 }
@@ -448,14 +492,14 @@ int launch_decode(int layer, int n, const int* d_seqs, const int* d_pos, int max
   for (int s0 = 0; s0 < n; s0 += pl::kMaxLaunchSeqs) {
     const int m = n - s0 < pl::kMaxLaunchSeqs ? n - s0 : pl::kMaxLaunchSeqs;
     const int grid = decode_grid(m, max_rows);
-    const size_t need = static_cast<size_t>(grid + m) * g->n_heads * kPartStride;
+    const size_t need = static_cast<size_t>(grid + m) * g->part_floats;
     int rc = ensure_part(need);
     if (rc) return rc;
     const pl::DecodeArgs a = decode_args(
         layer, m, d_seqs + s0, d_pos + s0, d_q + static_cast<size_t>(s0) * g->q_dim,
         d_k + static_cast<size_t>(s0) * g->kv_dim, d_v + static_cast<size_t>(s0) * g->kv_dim,
         d_out ? d_out + static_cast<size_t>(s0) * g->q_dim : nullptr, mode, row0, n_rows, append,
-        part_out ? part_out + static_cast<size_t>(s0) * g->n_heads * kPartStride : nullptr,
+        part_out ? part_out + static_cast<size_t>(s0) * g->part_floats : nullptr,
         g->d_part, g->d_seg_info);
     rc = launch_decode_kernel(a, grid, st, true);
     if (rc) return rc;
@@ -540,7 +584,7 @@ int pl_attn_init(int n_layers, int n_heads, int n_kv_heads, int head_dim, int ma
   if (n_layers <= 0 || n_heads <= 0 || n_kv_heads <= 0 || max_seq_len <= 0 || n_seqs <= 0 ||
       device < 0 || !(rope_freq_base > 0.f))
     return PL_EARG;
-  if (head_dim != kHD) return PL_EUNSUPPORTED;
+  if (head_dim != 64 && head_dim != 128) return PL_EUNSUPPORTED;
   if (n_heads % n_kv_heads) return PL_EUNSUPPORTED;
   const int kv_mul = n_heads / n_kv_heads;
   if (!(n_kv_heads == 1 || n_kv_heads == 2 || n_kv_heads == 4 || n_kv_heads == 8))
@@ -563,10 +607,16 @@ int pl_attn_init(int n_layers, int n_heads, int n_kv_heads, int head_dim, int ma
   c->max_seq = max_seq_len;
   c->n_seqs = n_seqs;
   c->rope_type = rope_type;
-  c->kv_dim = n_kv_heads * kHD;
-  c->q_dim = n_heads * kHD;
+  c->head_dim = head_dim;
+  c->kv_dim = n_kv_heads * head_dim;
+  c->q_dim = n_heads * head_dim;
+  c->part_floats = n_heads * part_stride(head_dim);
   c->kv_mul = kv_mul;
-  c->tp = 128 / n_kv_heads;
+  // a K (or V) tile of 16 KB: all KV heads, TP rows (at least 16, the MMA
+  // row block); at 128 x 8 KV heads that is 32 KB and the ring is 3 deep
+  c->tp = 8192 / (n_kv_heads * head_dim);
+  if (c->tp < 16) c->tp = 16;
+  c->nstage = c->tp * n_kv_heads * head_dim > 8192 ? 3 : kDecodeStages;
   c->num_sms = prop.multiProcessorCount;
   c->layer_elems = static_cast<size_t>(max_seq_len) * c->kv_dim;
   const size_t cache_elems = c->layer_elems * n_layers * n_seqs;
@@ -585,8 +635,8 @@ int pl_attn_init(int n_layers, int n_heads, int n_kv_heads, int head_dim, int ma
   if (cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking) != cudaSuccess ||
       cudaMalloc(&c->d_k, cache_elems * 2) != cudaSuccess ||
       cudaMalloc(&c->d_v, cache_elems * 2) != cudaSuccess ||
-      cudaMalloc(&c->d_cos, sizeof(float) * max_seq_len * (kHD / 2)) != cudaSuccess ||
-      cudaMalloc(&c->d_sin, sizeof(float) * max_seq_len * (kHD / 2)) != cudaSuccess ||
+      cudaMalloc(&c->d_cos, sizeof(float) * max_seq_len * (head_dim / 2)) != cudaSuccess ||
+      cudaMalloc(&c->d_sin, sizeof(float) * max_seq_len * (head_dim / 2)) != cudaSuccess ||
       cudaMalloc(&c->d_err, 256) != cudaSuccess ||
       cudaMalloc(&c->d_seg_info, sizeof(int2) * pl::kMaxLaunchSeqs) != cudaSuccess ||
       cudaMalloc(&c->d_work, 2 * sizeof(int)) != cudaSuccess) {
@@ -599,7 +649,7 @@ int pl_attn_init(int n_layers, int n_heads, int n_kv_heads, int head_dim, int ma
   cudaMemsetAsync(c->d_seg_info, 0, sizeof(int2) * pl::kMaxLaunchSeqs, c->stream);
   cudaMemsetAsync(c->d_work, 0, 2 * sizeof(int), c->stream);
   {
-    const size_t n = static_cast<size_t>(max_seq_len) * (kHD / 2);
+    const size_t n = static_cast<size_t>(max_seq_len) * (head_dim / 2);
     float* hc = static_cast<float*>(std::malloc(n * sizeof(float)));
     float* hs = static_cast<float*>(std::malloc(n * sizeof(float)));
     if (!hc || !hs) {
@@ -608,20 +658,20 @@ int pl_attn_init(int n_layers, int n_heads, int n_kv_heads, int head_dim, int ma
       free_ctx(c);
       return PL_ENOMEM;
     }
-    host_rope_tables(hc, hs, max_seq_len, rope_freq_base);
+    host_rope_tables(hc, hs, max_seq_len, head_dim, rope_freq_base);
     cudaMemcpy(c->d_cos, hc, n * sizeof(float), cudaMemcpyHostToDevice);
     cudaMemcpy(c->d_sin, hs, n * sizeof(float), cudaMemcpyHostToDevice);
     std::free(hc);
     std::free(hs);
   }
   const int n_slabs = n_seqs * n_layers;
-  if ((rc = make_map(c->encode, &c->tm_k_dec, c->d_k, max_seq_len, n_kv_heads, n_slabs, c->tp,
-                     n_kv_heads)) ||
-      (rc = make_map(c->encode, &c->tm_v_dec, c->d_v, max_seq_len, n_kv_heads, n_slabs, c->tp,
-                     n_kv_heads)) ||
-      (rc = make_map(c->encode, &c->tm_k_pf, c->d_k, max_seq_len, n_kv_heads, n_slabs,
+  if ((rc = make_map(c->encode, &c->tm_k_dec, c->d_k, head_dim, max_seq_len, n_kv_heads, n_slabs,
+                     c->tp, n_kv_heads)) ||
+      (rc = make_map(c->encode, &c->tm_v_dec, c->d_v, head_dim, max_seq_len, n_kv_heads, n_slabs,
+                     c->tp, n_kv_heads)) ||
+      (rc = make_map(c->encode, &c->tm_k_pf, c->d_k, head_dim, max_seq_len, n_kv_heads, n_slabs,
                      pl::kPfBlockN, 1)) ||
-      (rc = make_map(c->encode, &c->tm_v_pf, c->d_v, max_seq_len, n_kv_heads, n_slabs,
+      (rc = make_map(c->encode, &c->tm_v_pf, c->d_v, head_dim, max_seq_len, n_kv_heads, n_slabs,
                      pl::kPfBlockN, 1))) {
     free_ctx(c);
     return rc;
@@ -631,15 +681,10 @@ int pl_attn_init(int n_layers, int n_heads, int n_kv_heads, int head_dim, int ma
   g = c;
   {
     int per_sm = 0;
-    const int smem = decode_smem_bytes(c->tp);
+    const int smem = decode_smem_bytes(c->tp, c->nstage, head_dim);
     const int threads = (n_kv_heads + 1) * 32;
-    cudaError_t e = cudaSuccess;
-    switch (c->tp) {
-      case 16: e = decode_occupancy<16>(&per_sm, threads, smem); break;
-      case 32: e = decode_occupancy<32>(&per_sm, threads, smem); break;
-      case 64: e = decode_occupancy<64>(&per_sm, threads, smem); break;
-      default: e = decode_occupancy<128>(&per_sm, threads, smem); break;
-    }
+    const cudaError_t e =
+        with_decode_config(c->tp, c->nstage, head_dim, DecodeOccupancy{&per_sm, threads, smem});
     g = nullptr;
     if (e != cudaSuccess || per_sm < 1) {
       free_ctx(c);
@@ -667,7 +712,7 @@ void pl_attn_shutdown(void) {
 
 int pl_attn_set_rope(const float* cos_tab, const float* sin_tab, int n_rows, int half_dim) {
   if (!g) return PL_ESTATE;
-  if (!cos_tab || !sin_tab || half_dim != kHD / 2 || n_rows <= 0) return PL_EARG;
+  if (!cos_tab || !sin_tab || half_dim != g->head_dim / 2 || n_rows <= 0) return PL_EARG;
   const int rows = n_rows < g->max_seq ? n_rows : g->max_seq;
   const size_t bytes = static_cast<size_t>(rows) * half_dim * sizeof(float);
   PL_CUDA(cudaMemcpyAsync(g->d_cos, cos_tab, bytes, cudaMemcpyHostToDevice, g->stream));
@@ -757,8 +802,9 @@ int pl_attn_decode_partial_dev(int seq, int layer, int pos, int row0, int n_rows
   cudaStream_t st = pick_stream(stream);
   if (n_rows == 0) {
     // an empty shard contributes nothing: m = -inf, l = 0, o = 0
-    std::vector<float> empty(static_cast<size_t>(g->n_heads) * kPartStride, 0.f);
-    for (int h = 0; h < g->n_heads; ++h) empty[static_cast<size_t>(h) * kPartStride] = -INFINITY;
+    const int ps = part_stride(g->head_dim);
+    std::vector<float> empty(static_cast<size_t>(g->part_floats), 0.f);
+    for (int h = 0; h < g->n_heads; ++h) empty[static_cast<size_t>(h) * ps] = -INFINITY;
     PL_CUDA(cudaMemcpyAsync(d_part, empty.data(), empty.size() * sizeof(float),
                             cudaMemcpyHostToDevice, st));
     return PL_OK;
@@ -766,7 +812,7 @@ int pl_attn_decode_partial_dev(int seq, int layer, int pos, int row0, int n_rows
   // seq and pos travel as kernel arguments (no copy, nothing that could
   // make the host wait for the stream)
   const int grid = decode_grid(1, n_rows);
-  int rc2 = ensure_part(static_cast<size_t>(grid + 1) * g->n_heads * kPartStride);
+  int rc2 = ensure_part(static_cast<size_t>(grid + 1) * g->part_floats);
   if (rc2) return rc2;
   pl::DecodeArgs a = decode_args(layer, 1, nullptr, nullptr, d_q, d_k ? d_k : d_q,
                                  d_v ? d_v : d_q, nullptr, 1, row0, n_rows, append ? 1 : 0,
@@ -782,7 +828,10 @@ int pl_attn_combine_dev(int n_part, const float* d_parts, float* d_out, void* st
   if (n_part > pl::kMaxCombineParts) return PL_EARG;
   cudaStream_t st = pick_stream(stream);
   const size_t smem = static_cast<size_t>(3 * pl::kMaxCombineParts + 2) * g->n_heads * sizeof(float);
-  pl::combine_kernel<<<1, 256, smem, st>>>(n_part, g->n_heads, d_parts, d_out);
+  if (g->head_dim == 128)
+    pl::combine_kernel<128><<<1, 256, smem, st>>>(n_part, g->n_heads, d_parts, d_out);
+  else
+    pl::combine_kernel<64><<<1, 256, smem, st>>>(n_part, g->n_heads, d_parts, d_out);
   PL_CUDA(cudaGetLastError());
   count_launch();
   return PL_OK;
@@ -798,7 +847,7 @@ int pl_attn_xfer_setup(int world, int rank, void* handle_out) {
     return PL_EARG;
   if (cudaSetDevice(g->device) != cudaSuccess) return PL_ECUDA;
   const size_t bytes = pl::kXferStampBytes +
-                       2 * static_cast<size_t>(world) * g->n_heads * kPartStride * sizeof(float);
+                       2 * static_cast<size_t>(world) * g->part_floats * sizeof(float);
   Xfer* x = new Xfer;
   x->world = world;
   x->rank = rank;
@@ -851,8 +900,12 @@ int pl_attn_combine_p2p_dev(const float* d_part, float* d_out, void* stream) {
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  PL_CUDA(cudaLaunchKernelEx(&cfg, pl::combine_p2p_kernel, d_part, g_xfer->peers, g_xfer->world,
-                             g_xfer->rank, g->n_heads, d_out, g->d_err));
+  if (g->head_dim == 128)
+    PL_CUDA(cudaLaunchKernelEx(&cfg, pl::combine_p2p_kernel<128>, d_part, g_xfer->peers,
+                               g_xfer->world, g_xfer->rank, g->n_heads, d_out, g->d_err));
+  else
+    PL_CUDA(cudaLaunchKernelEx(&cfg, pl::combine_p2p_kernel<64>, d_part, g_xfer->peers,
+                               g_xfer->world, g_xfer->rank, g->n_heads, d_out, g->d_err));
   count_launch();
   return PL_OK;
 }
@@ -870,8 +923,12 @@ int pl_attn_rope(int pos0, int n_tok, float* q, float* k) {
   float* dq = q ? reinterpret_cast<float*>(g->d_stage) : nullptr;
   float* dk = k ? reinterpret_cast<float*>(g->d_stage + qb) : nullptr;
   const dim3 rgrid(n_tok, (g->n_heads + g->n_kv_heads + 7) / 8);
-  pl::rope_inplace_kernel<<<rgrid, 256, 0, g->stream>>>(
-      dq, dk, g->n_heads, g->n_kv_heads, pos0, g->d_cos, g->d_sin, g->rope_type);
+  if (g->head_dim == 128)
+    pl::rope_inplace_kernel<128><<<rgrid, 256, 0, g->stream>>>(
+        dq, dk, g->n_heads, g->n_kv_heads, pos0, g->d_cos, g->d_sin, g->rope_type);
+  else
+    pl::rope_inplace_kernel<64><<<rgrid, 256, 0, g->stream>>>(
+        dq, dk, g->n_heads, g->n_kv_heads, pos0, g->d_cos, g->d_sin, g->rope_type);
   PL_CUDA(cudaGetLastError());
   PL_CUDA(cudaMemcpyAsync(g->h_stage, g->d_stage, qb + kb, cudaMemcpyDeviceToHost, g->stream));
   PL_CUDA(cudaStreamSynchronize(g->stream));
@@ -921,13 +978,50 @@ int pl_attn_kv_ptr(int seq, int layer, uint16_t** d_k, uint16_t** d_v) {
 // ---------------------------------------------------------------- prefill
 static bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
+// head_dim 128: the cache rows first (the prologue without the q staging),
+// then the batched decode kernel with one entry per token -- entry i is row
+// start_pos + i of the same slot and attends rows [0, start_pos + i], all of
+// them already in the cache, so it appends nothing.  Causal attention,
+// FP32 softmax and FP16 cache rows as in the tensor-core path; the partition
+// of the decode kernel splits the n_tok * rows tiles over the SMs.
+static int launch_prefill_by_decode(int seq, int layer, int start_pos, int n_tok,
+                                    const float* d_q, const float* d_k, const float* d_v,
+                                    float* d_out, int out_stride, cudaStream_t st) {
+  const size_t off = static_cast<size_t>(start_pos) * g->kv_dim;
+  pl::prefill_prologue_kernel<128><<<n_tok, pl::kPrologueThreads, 0, st>>>(
+      d_q, d_k, d_v, nullptr, slab_k(seq, layer) + off, slab_v(seq, layer) + off, n_tok,
+      g->n_heads, g->n_kv_heads, start_pos, g->d_cos, g->d_sin, g->rope_type);
+  PL_CUDA(cudaGetLastError());
+  count_launch();
+  for (int t0 = 0; t0 < n_tok; t0 += pl::kMaxLaunchSeqs) {
+    const int m = n_tok - t0 < pl::kMaxLaunchSeqs ? n_tok - t0 : pl::kMaxLaunchSeqs;
+    const int grid = decode_grid(m, start_pos + t0 + m);
+    int rc = ensure_part(static_cast<size_t>(grid + m) * g->part_floats);
+    if (rc) return rc;
+    const float* q = d_q + static_cast<size_t>(t0) * g->q_dim;
+    pl::DecodeArgs a = decode_args(layer, m, nullptr, nullptr, q, q, q,
+                                   d_out + static_cast<size_t>(t0) * out_stride, 0, 0, 0, 0,
+                                   nullptr, g->d_part, g->d_seg_info);
+    a.seq1 = seq;
+    a.pos1 = start_pos + t0;
+    a.pos_inc = 1;
+    a.out_stride = out_stride;
+    rc = launch_decode_kernel(a, grid, st, true);
+    if (rc) return rc;
+  }
+  return PL_OK;
+}
+
 static int launch_prefill(int seq, int layer, int start_pos, int n_tok, const float* d_q,
                           const float* d_k, const float* d_v, float* d_out, int out_stride,
                           cudaStream_t st) {
+  if (g->head_dim != kHD)
+    return launch_prefill_by_decode(seq, layer, start_pos, n_tok, d_q, d_k, d_v, d_out,
+                                    out_stride, st);
   int rc = ensure_q16(n_tok);
   if (rc) return rc;
   const size_t off = static_cast<size_t>(start_pos) * g->kv_dim;
-  pl::prefill_prologue_kernel<<<n_tok, pl::kPrologueThreads, 0, st>>>(
+  pl::prefill_prologue_kernel<kHD><<<n_tok, pl::kPrologueThreads, 0, st>>>(
       d_q, d_k, d_v, g->d_q16, slab_k(seq, layer) + off, slab_v(seq, layer) + off, n_tok,
       g->n_heads, g->n_kv_heads, start_pos, g->d_cos, g->d_sin, g->rope_type);
   PL_CUDA(cudaGetLastError());
@@ -1114,7 +1208,7 @@ extern "C" int pl_attn_decode_batch_dev_noalloc(int layer, int n, const int* d_s
     return PL_EARG;
   if (!d_seqs || !d_pos || !d_q || !d_k || !d_v || !d_out) return PL_EARG;
   // partial slots needed: one per CTA plus one per sequence
-  const size_t slot_bytes = static_cast<size_t>(g->n_heads) * kPartStride * sizeof(float);
+  const size_t slot_bytes = static_cast<size_t>(g->part_floats) * sizeof(float);
   const long long fit = static_cast<long long>(kNoAllocPartBytes / slot_bytes) - n;
   if (n > kNoAllocMaxSeqs || fit < 1) {
     std::fprintf(stderr,

@@ -26,7 +26,7 @@ from __future__ import annotations
 
 from dataclasses import dataclass
 
-PART_STRIDE = 68  # floats per head in a partial block: m, l, 2 pad, o[64]
+PART_STRIDE = 68  # floats per head in a partial block at head_dim 64: m, l, 2 pad, o[64]
 
 
 def shard_range(n_cached: int, world: int, rank: int) -> tuple[int, int]:

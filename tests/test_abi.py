@@ -51,7 +51,9 @@ def test_calls_before_init_report_state_error():
 def test_init_argument_checks_need_no_device():
     lib = pb.load()
     # unsupported head_dim / GQA ratios are rejected before any device call
-    assert lib.pl_attn_init(1, 32, 4, 128, 64, 1e4, 0, 1, 0) == pb.PL_EUNSUPPORTED
+    # (head_dim 64 and 128 are supported; 80, 96, 256 are not)
+    for hd in (32, 80, 96, 256):
+        assert lib.pl_attn_init(1, 32, 4, hd, 64, 1e4, 0, 1, 0) == pb.PL_EUNSUPPORTED
     assert lib.pl_attn_init(1, 48, 4, 64, 64, 1e4, 0, 1, 0) == pb.PL_EUNSUPPORTED
     assert lib.pl_attn_init(1, 32, 3, 64, 64, 1e4, 0, 1, 0) == pb.PL_EUNSUPPORTED
     assert lib.pl_attn_init(1, 16, 16, 64, 64, 1e4, 0, 1, 0) == pb.PL_EUNSUPPORTED

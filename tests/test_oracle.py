@@ -153,9 +153,12 @@ def test_decode_seqs_threads_equal_single(orc):
 
 @pytest.mark.skipif(not __import__("oracle.oracle", fromlist=["x"]).ref_available(),
                     reason="oracle/_ref (the reference compiled here) is absent")
-def test_port_equals_genuine_reference_live(orc):
-    rng = np.random.default_rng(7)
-    H, Hk, hd, ms, n = 32, 4, 64, 300, 4
+@pytest.mark.parametrize("H,Hk,hd", [(32, 4, 64), (32, 8, 128), (16, 2, 128)])
+def test_port_equals_genuine_reference_live(orc, H, Hk, hd):
+    # head_dim 128 (model.c:856 takes any hd <= 256) pins the restatement at
+    # the second head size the CUDA kernels support
+    rng = np.random.default_rng(7 + hd + Hk)
+    ms, n = 300, 4
     c = orc.cfg(H, Hk, hd, ms)
     ct, st = orc.rope_tables(ms, hd, 10000.0)
     ct2 = np.empty_like(ct)
@@ -187,3 +190,25 @@ def test_port_equals_genuine_reference_live(orc):
     dec = np.empty(65536, np.float32)
     orc.ref().ref_fp16_to_fp32_array(h, dec, 65536)
     np.testing.assert_array_equal(orc.fp16_to_fp32(h).view(np.uint32), dec.view(np.uint32))
+
+
+@pytest.mark.skipif(not __import__("oracle.oracle", fromlist=["x"]).ref_available(),
+                    reason="oracle/_ref (the reference compiled here) is absent")
+@pytest.mark.parametrize("hd,rope_type", [(64, 0), (64, 1), (128, 0), (128, 1)])
+def test_rope_port_equals_genuine_reference(orc, hd, rope_type):
+    # the restated rotation against picolm's own rope() (tensor.c:533-601),
+    # both pairings, at both supported head sizes, bit for bit
+    rng = np.random.default_rng(hd + rope_type)
+    H, Hk, ms = 8, 2, 64
+    ct, st = orc.rope_tables(ms, hd, 10000.0)
+    half = hd // 2
+    for pos in (0, 1, 37, 63):
+        q = rng.standard_normal(H * hd, dtype=np.float32) * 3
+        k = rng.standard_normal(Hk * hd, dtype=np.float32) * 3
+        cs = np.ascontiguousarray(ct[pos * half:(pos + 1) * half])
+        sn = np.ascontiguousarray(st[pos * half:(pos + 1) * half])
+        q1, k1, q2, k2 = q.copy(), k.copy(), q.copy(), k.copy()
+        orc.port().orc_rope(q1, k1, hd, H, Hk, cs, sn, rope_type)
+        orc.ref().rope(q2, k2, hd, H, Hk, cs, sn, rope_type)
+        np.testing.assert_array_equal(q1.view(np.uint32), q2.view(np.uint32))
+        np.testing.assert_array_equal(k1.view(np.uint32), k2.view(np.uint32))

@@ -28,9 +28,9 @@ def random_cache(rng, n_rows, kv_dim, scale=1.0):
     return O.fp32_to_fp16(x).reshape(n_rows, kv_dim)
 
 
-def oracle_decode_layer(H, Hk, ms, kc, vc, pos, q, k, v, tables, rope_type=0):
+def oracle_decode_layer(H, Hk, ms, kc, vc, pos, q, k, v, tables, rope_type=0, hd=64):
     """Oracle decode on copies of the layer views; returns (out, kc', vc')."""
-    c = O.cfg(H, Hk, 64, ms, rope_type)
+    c = O.cfg(H, Hk, hd, ms, rope_type)
     kc2, vc2 = kc.copy(), vc.copy()
     out, _, _ = O.attn_decode(c, kc2.ravel(), vc2.ravel(), pos, q, k, v, *tables)
     return out, kc2, vc2
