@@ -470,6 +470,105 @@ def run_long_ctx(args, local, peaks):
                                    "32768 cached + 32 steps, KV N(0,1) seed 4"}}
 
 
+def run_hd128(args, local, peaks):
+    """head_dim 128 (LLaMA-3-8B heads 32/8): batched decode of 32 sequences
+    x 2048 cached rows (L2 flushed before every timed step, as the headline),
+    and the prefill of 2048 positions of one layer (appended rows, then the
+    batched decode kernel over the positions)."""
+    import torch
+    import picolm_b200 as pb
+    H8, HK8, HD8, NSEQ, CTX8, NST = 32, 8, 128, 32, 2048, 16
+    q_dim, kv_dim = H8 * HD8, HK8 * HD8
+    dev = torch.device("cuda", local)
+    sh = torch.cuda.current_stream(dev).cuda_stream
+    rng = np.random.default_rng(6)
+    res = {"config": {"workload": "head_dim 128, heads 32/8 (LLaMA-3-8B), theta 5e5; decode: "
+                                  f"{NSEQ} seqs x {CTX8} cached, {NST} steps; prefill: 2048 "
+                                  "positions of one layer", "data": "synthetic, seed 6"}}
+    # ---- batched decode
+    at = pb.Attn(1, H8, HK8, CTX8 + NST, rope_base=500000.0, n_seqs=NSEQ, device=local,
+                 head_dim=HD8)
+    for s in range(NSEQ):
+        at.kv_upload(s, 0, 0, make_cache_host(rng, CTX8, kv_dim), make_cache_host(rng, CTX8, kv_dim))
+    gen = torch.Generator(device=dev).manual_seed(6)
+    q = torch.randn(NST, NSEQ, q_dim, device=dev, generator=gen)
+    k = torch.randn(NST, NSEQ, kv_dim, device=dev, generator=gen)
+    v = torch.randn(NST, NSEQ, kv_dim, device=dev, generator=gen)
+    out = torch.empty(NSEQ, q_dim, device=dev)
+    seqs = torch.arange(NSEQ, dtype=torch.int32, device=dev)
+    pos = (CTX8 + torch.arange(NST, dtype=torch.int32, device=dev))[:, None].repeat(
+        1, NSEQ).contiguous()
+    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
+    flush_rd = torch.ones(L2_FLUSH_BYTES // 4, dtype=torch.int32, device=dev)
+
+    def step(s):
+        at.decode_batch_dev(0, NSEQ, seqs.data_ptr(), pos[s].data_ptr(), CTX8 + NST - 1,
+                            q[s].data_ptr(), k[s].data_ptr(), v[s].data_ptr(), out.data_ptr(), sh)
+
+    def nbytes(s):
+        rows = CTX8 + s + 1
+        return NSEQ * (rows * kv_dim * 4 + q_dim * 8 + kv_dim * 12)
+
+    for s in range(3):
+        flush.zero_(); flush_rd.sum(); step(s)
+    torch.cuda.synchronize()
+    tot_ms, tot_b = 0.0, 0
+    for s in range(NST):
+        flush.zero_(); flush_rd.sum()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(); step(s); e1.record()
+        torch.cuda.synchronize()
+        tot_ms += e0.elapsed_time(e1)
+        tot_b += nbytes(s)
+    at.profile(True)
+    prof_b = 0
+    for s in range(NST):
+        flush.zero_(); flush_rd.sum(); step(s)
+        prof_b += nbytes(s)
+    torch.cuda.synchronize()
+    kern_ms, _, _ = at.profile_read()
+    at.profile(False)
+    at.close()
+    del flush, flush_rd
+    gbs = tot_b / (tot_ms / 1e3) / 1e9
+    res["decode"] = {"metric": "decode-attn HBM GB/s (head_dim 128)", "value": gbs,
+                     "unit": "GB/s", "pct_peak": 100.0 * gbs / peaks["hbm_gbs"],
+                     "ms_per_step": tot_ms / NST,
+                     "kernel_gbs": prof_b / (kern_ms / 1e3) / 1e9,
+                     "kernel_frac": prof_b / (kern_ms / 1e3) / 1e9 / peaks["hbm_gbs"]}
+    # ---- prefill of one layer
+    S = 2048
+    at = pb.Attn(1, H8, HK8, S, rope_base=500000.0, device=local, head_dim=HD8)
+    qp = torch.randn(S, q_dim, device=dev, generator=gen).half().float()
+    kp = torch.randn(S, kv_dim, device=dev, generator=gen).half().float()
+    vp = torch.randn(S, kv_dim, device=dev, generator=gen).half().float()
+    op = torch.empty(S, q_dim, device=dev)
+
+    def pf():
+        at.prefill_dev(0, 0, 0, S, qp.data_ptr(), kp.data_ptr(), vp.data_ptr(), op.data_ptr(),
+                       None, sh)
+
+    for _ in range(3):
+        pf()
+    torch.cuda.synchronize()
+    reps = 5
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(reps):
+        pf()
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / reps
+    at.close()
+    flops = 4.0 * H8 * HD8 * S * (S + 1) / 2
+    res["prefill"] = {"metric": "prefill-attn TFLOP/s (head_dim 128, causal FLOPs / call time)",
+                      "value": flops / (ms / 1e3) / 1e12, "unit": "TFLOP/s",
+                      "ms_per_layer": ms,
+                      "path": "prologue (RoPE + append) then the batched decode kernel over "
+                              "the 2048 positions"}
+    return res
+
+
 def run_long_ctx_split(args, rank, world, local, peaks):
     """Config 5 split along the KV axis over `world` GPUs: rank r holds a
     contiguous 1/world of the 32768 cached positions (the last rank also the
@@ -574,10 +673,11 @@ def main():
     ap.add_argument("--steps", type=int, default=2000)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["all", "decode", "prefill", "long_ctx", "decode1"],
+    ap.add_argument("--workload", choices=["all", "decode", "prefill", "long_ctx", "decode1",
+                                           "hd128"],
                     default="all",
                     help="all: headline + configs 1/3/5 + CPU baseline; decode: headline only; "
-                         "prefill / long_ctx / decode1: that workload alone (for profiling)")
+                         "prefill / long_ctx / decode1 / hd128: that workload alone")
     args = ap.parse_args()
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -620,11 +720,12 @@ def main():
         import torch.distributed as dist
         dist.destroy_process_group()
         return
-    if args.workload in ("prefill", "long_ctx", "decode1"):
+    if args.workload in ("prefill", "long_ctx", "decode1", "hd128"):
         if rank == 0:
             fn = {"prefill": lambda: run_prefill(args, local, peaks),
                   "long_ctx": lambda: run_long_ctx(args, local, peaks),
-                  "decode1": lambda: run_decode1(local)}[args.workload]
+                  "decode1": lambda: run_decode1(local),
+                  "hd128": lambda: run_hd128(args, local, peaks)}[args.workload]
             print(json.dumps(fn()), flush=True)
         return
     res = run_batched_decode(args, rank, world, local, peaks)
@@ -639,6 +740,7 @@ def main():
         line["prefill"] = run_prefill(args, local, peaks)
         line["long_ctx"] = run_long_ctx(args, local, peaks)
         line["decode1"] = run_decode1(local)
+        line["hd128"] = run_hd128(args, local, peaks)
         cb = cpu_decode_sample(max_seconds=15.0)
         line["cpu_baseline"] = {k: cb[k] for k in ("value", "unit", "cores", "kind", "sample")}
     if rank == 0:
