@@ -473,8 +473,7 @@ def run_long_ctx(args, local, peaks):
 def run_hd128(args, local, peaks):
     """head_dim 128 (LLaMA-3-8B heads 32/8): batched decode of 32 sequences
     x 2048 cached rows (L2 flushed before every timed step, as the headline),
-    and the prefill of 2048 positions of one layer (appended rows, then the
-    batched decode kernel over the positions)."""
+    and the causal prefill of 2048 positions of one layer."""
     import torch
     import picolm_b200 as pb
     H8, HK8, HD8, NSEQ, CTX8, NST = 32, 8, 128, 32, 2048, 16
@@ -564,8 +563,8 @@ def run_hd128(args, local, peaks):
     res["prefill"] = {"metric": "prefill-attn TFLOP/s (head_dim 128, causal FLOPs / call time)",
                       "value": flops / (ms / 1e3) / 1e12, "unit": "TFLOP/s",
                       "ms_per_layer": ms,
-                      "path": "prologue (RoPE + append) then the batched decode kernel over "
-                              "the 2048 positions"}
+                      "path": "prologue (RoPE + append + FP16 q) then the tcgen05 kernel, "
+                              "64-row KV tiles"}
     return res
 
 

@@ -28,9 +28,7 @@
  * Supported shapes: head_dim 64 or 128 (model.c:856 accepts up to 256);
  * n_kv_heads in {1, 2, 4, 8}; n_heads / n_kv_heads in {1, 2, 4, 8}; LLaMA
  * (pairwise) or Qwen (half-split) RoPE.  Other shapes are rejected with
- * PL_EUNSUPPORTED at pl_attn_init.  At head_dim 64 the prefill runs on the
- * tensor cores (tcgen05); at 128 it appends the rows and runs the batched
- * decode kernel over the n_tok positions (same results, same tolerances).
+ * PL_EUNSUPPORTED at pl_attn_init.
  */
 #ifndef PL_ATTN_H
 #define PL_ATTN_H

@@ -78,8 +78,7 @@ struct DecodeArgs {
   int n;                 // sequences in this launch (<= kMaxLaunchSeqs)
   const int* seqs;       // cache slot per sequence (nullptr: seq1 for all)
   const int* pos;        // global position of the new token (nullptr: pos1)
-  int seq1, pos1;        // slot / position when the arrays are null: sequence i of the
-  int pos_inc;           //   launch is at position pos1 + i * pos_inc
+  int seq1, pos1;        // scalar slot / position when the arrays are null
   const float* q;        // [n][n_heads*HD]   before RoPE
   const float* k;        // [n][kv_dim]       before RoPE
   const float* v;        // [n][kv_dim]
@@ -158,7 +157,7 @@ __device__ __forceinline__ int seq_of(const DecodeArgs& a, int i) {
   return a.seqs ? a.seqs[i] : a.seq1;
 }
 __device__ __forceinline__ int pos_of(const DecodeArgs& a, int i) {
-  return a.pos ? a.pos[i] : a.pos1 + i * a.pos_inc;
+  return a.pos ? a.pos[i] : a.pos1;
 }
 
 // Rows attended and the append row of sequence i.

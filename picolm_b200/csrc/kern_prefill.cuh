@@ -3,7 +3,7 @@
 //
 // Replaces the position-by-position loop of picolm/model.c:1054-1089.  The
 // prologue kernel (kern_misc.cuh) has already rotated q/k, appended k/v to
-// the FP16 cache (bit-exact) and staged q as FP16 [n_tok][n_heads][64].
+// the FP16 cache (bit-exact) and staged q as FP16 [n_tok][n_heads][HD].
 //
 // Work item = two 128-row query tiles ("slots" A and B) sharing one KV
 // head: two query heads of the same GQA group at the same rows (with one
@@ -18,17 +18,18 @@
 //   warps 4-7  softmax of slot B (same lanes, other TMEM columns)
 //   warp 8     scheduler + TMA producer: fetches items, publishes them in a
 //              two-entry shared-memory queue, loads Q_A/Q_B per item and
-//              K/V tiles of 128 cache rows through a kPfStages ring
+//              K/V tiles of BN cache rows through a STAGES-deep ring
 //   warp 9     TMEM allocator; MMA issuer of slot A
 //   warp 10    MMA issuer of slot B
 //   warp 11    idle (completes the third warpgroup for the register split)
 // The block launches at kPfLaunchRegs registers per thread; the two softmax
-// warpgroups then raise theirs to kPfSoftmaxRegs (a 128-column S row lives
+// warpgroups then raise theirs to kPfSoftmaxRegs (a BN-column S row lives
 // in registers) and the third drops to kPfOtherRegs:
 // 256 * 232 + 128 * 40 = 384 * 168.
 // Per KV tile j the issuer of slot x issues, in order,
-//   S_x(j) = Q_x K_j^T      (M=128 N=128 K=64, smem x smem -> TMEM)
-//   PV_x(j-1) = P_x V       (M=128 N=64 K=128, TMEM x smem -> TMEM O_x)
+//   S_x(j) = Q_x K_j^T      (M=128 N=BN K=HD, smem x smem -> TMEM)
+//   PV_x(j-1) = P_x V       (M=128 N=64 K=BN per 64 columns of O, TMEM x smem
+//                            -> TMEM O_x)
 // so one slot's softmax overlaps the other slot's MMAs (ping-pong).  Issue
 // of tcgen05.mma is close to synchronous with its execution, and every
 // mbarrier check in the issuing thread leaves the tensor pipe idle for
@@ -36,7 +37,7 @@
 // fill those gaps.  The slots touch disjoint TMEM columns, so the two
 // issuers need no ordering between them; a K/V stage is released when both
 // have committed their MMAs on it.  A
-// softmax thread loads its 128-column S row from TMEM once, takes the row
+// softmax thread loads its BN-column S row from TMEM once, takes the row
 // max (causal mask on diagonal tiles only), and writes P = 2^(s*c - m) as
 // FP16 back into tensor memory (its own lane, two halves per 32-bit
 // column), where the PV MMA takes it as the A operand: P never touches
@@ -61,8 +62,6 @@
 namespace pl {
 
 constexpr int kPfBlockM = 128;  // query rows per slot
-constexpr int kPfBlockN = 128;  // cache rows per KV tile
-constexpr int kPfStages = 4;    // K/V ring depth
 constexpr int kPfThreads = 384;
 constexpr int kPfLaunchRegs = 168;   // 65536 / 384 rounded down to 8
 constexpr int kPfSoftmaxRegs = 232;
@@ -73,25 +72,47 @@ constexpr int kPfStagePitch = 36;    // floats per row of the output staging buf
 constexpr float kPfRescaleLog2 = 8.0f;  // raise the running max only past 2^8
 
 struct PrefillArgs {
-  const uint16_t* q16;   // [n_tok][n_heads][64] FP16, rotated
-  float* out;            // row r at out + r*out_stride, head h at +h*64
+  const uint16_t* q16;   // [n_tok][n_heads][HD] FP16, rotated
+  float* out;            // row r at out + r*out_stride, head h at +h*HD
   int out_stride;
   int n_tok, start_pos, n_heads, kv_mul, slab;
-  float score_scale;     // log2(e)/sqrt(64)
+  float score_scale;     // log2(e)/sqrt(HD)
   int* work;             // [2] item counter, finished-CTA counter; zero at rest
   uint32_t* err;
 };
 
+// The two shapes of the kernel: head_dim HD, KV tiles of BN cache rows,
+// a STAGES-deep K/V ring.  <64, 128, 4>: S 128 + O 64 + P 64 TMEM columns per
+// slot.  <128, 64, 3>: S 64 + O 128 + P 32 (448 of 512 columns), and 196 KB
+// of shared memory.  A row of Q, K or V is HD/64 halves of 64 elements
+// (128 bytes, the swizzle span); each half of a tile is its own 128-byte
+// swizzled region, loaded by its own TMA box (x = 0 or 64).
+template <int HD, int BN, int STAGES>
+struct PfShape {
+  static constexpr int kHalves = HD / 64;
+  static constexpr int kQHalf = kPfBlockM * 128;       // bytes of one half of a Q tile
+  static constexpr int kQBytes = kQHalf * kHalves;
+  static constexpr int kKVHalf = BN * 128;             // bytes of one half of a K or V tile
+  static constexpr int kKVBytes = kKVHalf * kHalves;
+  // TMEM columns: S_A, S_B (BN FP32 each), O_A, O_B (HD), P_A, P_B (BN FP16)
+  static __device__ __forceinline__ uint32_t col_s(int x) { return x * BN; }
+  static __device__ __forceinline__ uint32_t col_o(int x) { return 2 * BN + x * HD; }
+  static __device__ __forceinline__ uint32_t col_p(int x) { return 2 * BN + 2 * HD + x * (BN / 2); }
+  static_assert(2 * BN + 2 * HD + BN <= 512, "TMEM columns");
+  static_assert(BN % 64 == 0 && HD % 64 == 0, "tiles are whole 64-element halves");
+};
+
+template <int HD, int BN, int STAGES>
 struct PfSmem {
   // 1024-byte aligned tiles (128-byte swizzle atoms are 8 rows x 128 B)
-  uint8_t q[2][kPfBlockM * 128];                // Q_A, Q_B: 16 KB each
-  uint8_t k[kPfStages][kPfBlockN * 128];        // 16 KB each
-  uint8_t v[kPfStages][kPfBlockN * 128];        // 16 KB each
+  uint8_t q[2][PfShape<HD, BN, STAGES>::kQBytes];      // Q_A, Q_B
+  uint8_t k[STAGES][PfShape<HD, BN, STAGES>::kKVBytes];
+  uint8_t v[STAGES][PfShape<HD, BN, STAGES>::kKVBytes];
   // per softmax warp, 32 rows x 32 output columns (row pitch padded so
   // that both the row-wise writes and the transposed reads are conflict-free)
   float stage[8][32 * kPfStagePitch];
   uint64_t q_full, q_empty;
-  uint64_t kv_full[kPfStages], kv_empty[kPfStages];
+  uint64_t kv_full[STAGES], kv_empty[STAGES];
   uint64_t s_full[2], s_free[2], p_full[2][2], pv_done[2][2], o_free[2];
   uint64_t item_full[2], item_empty[2];
   uint64_t mma_done[2];
@@ -99,14 +120,12 @@ struct PfSmem {
   uint32_t tmem_base;
 };
 
-constexpr int kPfSmemBytes = static_cast<int>(sizeof(PfSmem)) + 1024;
-static_assert(kPfSmemBytes <= 227 * 1024, "prefill shared memory above the per-CTA limit");
-
-// TMEM column map (512 columns allocated): S_A, S_B (128 FP32 columns
-// each), O_A, O_B (64 FP32), P_A, P_B (128 FP16 = 64 columns)
-__device__ __forceinline__ uint32_t pf_col_s(int x) { return x ? 128u : 0u; }
-__device__ __forceinline__ uint32_t pf_col_o(int x) { return x ? 320u : 256u; }
-__device__ __forceinline__ uint32_t pf_col_p(int x) { return x ? 448u : 384u; }
+template <int HD, int BN, int STAGES>
+constexpr int pf_smem_bytes() {
+  return static_cast<int>(sizeof(PfSmem<HD, BN, STAGES>)) + 1024;
+}
+static_assert(pf_smem_bytes<64, 128, 4>() <= 227 * 1024, "prefill shared memory above the limit");
+static_assert(pf_smem_bytes<128, 64, 3>() <= 227 * 1024, "prefill shared memory above the limit");
 
 __device__ __forceinline__ void tc_ld_x32(uint32_t taddr, uint32_t* r) {
   tc_ld_32x32b_x32(taddr, *reinterpret_cast<uint32_t(*)[32]>(r));
@@ -145,6 +164,7 @@ struct PfItem {
 };
 
 // Item b, heaviest first: query tile n_qt-1-b/per_tile, head pair b%per_tile.
+template <int BN>
 __device__ __forceinline__ PfItem pf_item(const PrefillArgs& a, int b) {
   PfItem it;
   const bool dual = a.kv_mul >= 2;
@@ -163,7 +183,7 @@ __device__ __forceinline__ PfItem pf_item(const PrefillArgs& a, int b) {
   it.kvh = it.head0 / a.kv_mul;
   it.q_row0 = qt * kPfBlockM;
   const int last_row = min(a.n_tok, it.q_row0 + kPfBlockM) - 1;
-  it.nkv = (a.start_pos + last_row + 1 + kPfBlockN - 1) / kPfBlockN;  // >= 1
+  it.nkv = (a.start_pos + last_row + 1 + BN - 1) / BN;  // >= 1
   it.p_min = a.start_pos + it.q_row0;
   return it;
 }
@@ -173,12 +193,14 @@ __device__ __forceinline__ int pf_n_items(const PrefillArgs& a) {
   return ((a.n_tok + kPfBlockM - 1) / kPfBlockM) * per_tile;
 }
 
+template <int HD, int BN, int STAGES>
 __global__ void __launch_bounds__(kPfThreads, 1)
     prefill_attn_kernel(const PrefillArgs a, const __grid_constant__ CUtensorMap tm_q,
                         const __grid_constant__ CUtensorMap tm_k,
                         const __grid_constant__ CUtensorMap tm_v) {
+  using Sh = PfShape<HD, BN, STAGES>;
   extern __shared__ uint8_t smem_raw[];
-  PfSmem& sm = *reinterpret_cast<PfSmem*>(
+  PfSmem<HD, BN, STAGES>& sm = *reinterpret_cast<PfSmem<HD, BN, STAGES>*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int n_slots = a.kv_mul >= 2 ? 2 : 1;
@@ -186,7 +208,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
   if (threadIdx.x == 0) {
     mbar_init(&sm.q_full, 1);
     mbar_init(&sm.q_empty, n_slots);  // one commit per active issuer
-    for (int s = 0; s < kPfStages; ++s) {
+    for (int s = 0; s < STAGES; ++s) {
       mbar_init(&sm.kv_full[s], 1);
       mbar_init(&sm.kv_empty[s], n_slots);
     }
@@ -237,7 +259,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
           sm.item[k & 1] = item;
           mbar_arrive(&sm.item_full[k & 1]);
           if (item < 0) break;
-          const PfItem it = pf_item(a, item);
+          const PfItem it = pf_item<BN>(a, item);
           // Q of the previous item is in use until its last S MMAs complete
           if (k >= 1 && !mbar_wait_bounded(&sm.q_empty, (k - 1) & 1)) {
             atomicOr(a.err, ERR_TIMEOUT_EMPTY);
@@ -245,25 +267,36 @@ __global__ void __launch_bounds__(kPfThreads, 1)
             ++k;
             continue;
           }
-          mbar_arrive_expect_tx(&sm.q_full, n_slots * kPfBlockM * 128);
-          tma_load_3d(sm.q[0], &tm_q, &sm.q_full, 0, it.head0, it.q_row0);
-          if (n_slots == 2) tma_load_3d(sm.q[1], &tm_q, &sm.q_full, 0, it.head1, it.q_row0);
+          mbar_arrive_expect_tx(&sm.q_full, n_slots * Sh::kQBytes);
+#pragma unroll
+          for (int hv = 0; hv < Sh::kHalves; ++hv) {
+            tma_load_3d(sm.q[0] + hv * Sh::kQHalf, &tm_q, &sm.q_full, 64 * hv, it.head0,
+                        it.q_row0);
+            if (n_slots == 2)
+              tma_load_3d(sm.q[1] + hv * Sh::kQHalf, &tm_q, &sm.q_full, 64 * hv, it.head1,
+                          it.q_row0);
+          }
           for (int j = 0; j < it.nkv; ++j, ++J) {
-            const int s = J % kPfStages;
-            if (J >= kPfStages && !mbar_wait_bounded(&sm.kv_empty[s], ((J / kPfStages) - 1) & 1)) {
+            const int s = J % STAGES;
+            if (J >= STAGES && !mbar_wait_bounded(&sm.kv_empty[s], ((J / STAGES) - 1) & 1)) {
               atomicOr(a.err, ERR_TIMEOUT_EMPTY);
               ok = false;
               break;
             }
-            mbar_arrive_expect_tx(&sm.kv_full[s], 2 * kPfBlockN * 128);
-            tma_load_4d(sm.k[s], &tm_k, &sm.kv_full[s], 0, j * kPfBlockN, it.kvh, a.slab);
-            tma_load_4d(sm.v[s], &tm_v, &sm.kv_full[s], 0, j * kPfBlockN, it.kvh, a.slab);
+            mbar_arrive_expect_tx(&sm.kv_full[s], 2 * Sh::kKVBytes);
+#pragma unroll
+            for (int hv = 0; hv < Sh::kHalves; ++hv) {
+              tma_load_4d(sm.k[s] + hv * Sh::kKVHalf, &tm_k, &sm.kv_full[s], 64 * hv, j * BN,
+                          it.kvh, a.slab);
+              tma_load_4d(sm.v[s] + hv * Sh::kKVHalf, &tm_v, &sm.kv_full[s], 64 * hv, j * BN,
+                          it.kvh, a.slab);
+            }
           }
           ++k;
         }
         // never leave with copies in flight: the last use of each stage must land
-        for (int j = J - kPfStages; j < J; ++j)
-          if (j >= 0) mbar_wait_bounded(&sm.kv_full[j % kPfStages], (j / kPfStages) & 1);
+        for (int j = J - STAGES; j < J; ++j)
+          if (j >= 0) mbar_wait_bounded(&sm.kv_full[j % STAGES], (j / STAGES) & 1);
         if (k >= 1) mbar_wait_bounded(&sm.q_full, (k - 1) & 1);
         // the last CTA to stop fetching resets the counters for the next launch
         __threadfence();
@@ -277,8 +310,8 @@ __global__ void __launch_bounds__(kPfThreads, 1)
       // ------------------------------------------------- MMA issuer of slot x
       const int x = warp - 9;
       if (lane == 0) {
-        const uint32_t idesc_qk = idesc_f16_f32(128, 128, 0);
-        const uint32_t idesc_pv = idesc_f16_f32(128, 64, 1);
+        const uint32_t idesc_qk = idesc_f16_f32(128, BN, 0);
+        const uint32_t idesc_pv = idesc_f16_f32(128, 64, 1);  // one 64-column half of O
         const bool active = x < n_slots;
         const uint32_t q_addr = smem_u32(sm.q[x]);
         int J = 0, k = 0;
@@ -286,17 +319,21 @@ __global__ void __launch_bounds__(kPfThreads, 1)
         // PV_x of global tile g (first tile of its item if `first`), then
         // release of its K/V stage
         auto issue_pv = [&](int g, bool first) -> bool {
-          const int s = g % kPfStages, pb = g & 1;
+          const int s = g % STAGES, pb = g & 1;
           if (!mbar_wait_bounded(&sm.p_full[x][pb], (g >> 1) & 1)) return false;
           // the previous item's O must be read out before it is overwritten
           if (first && k >= 1 && !mbar_wait_bounded(&sm.o_free[x], (k - 1) & 1)) return false;
           tc_fence_after();
           const uint32_t v_addr = smem_u32(sm.v[s]);
-  #pragma unroll
-          for (int kk = 0; kk < kPfBlockN / 16; ++kk) {  // 16 keys = 8 P columns per MMA
-            const uint64_t bd = smem_desc_sw128(v_addr + kk * 16 * 128, 16, 1024);
-            tc_mma_ts(tmem + pf_col_o(x), tmem + pf_col_p(x) + kk * 8, bd, idesc_pv,
-                      (first && kk == 0) ? 0u : 1u);
+#pragma unroll
+          for (int hv = 0; hv < Sh::kHalves; ++hv) {   // O columns 64hv .. 64hv+63
+#pragma unroll
+            for (int kk = 0; kk < BN / 16; ++kk) {  // 16 keys = 8 P columns per MMA
+              const uint64_t bd =
+                  smem_desc_sw128(v_addr + hv * Sh::kKVHalf + kk * 16 * 128, 16, 1024);
+              tc_mma_ts(tmem + Sh::col_o(x) + 64 * hv, tmem + Sh::col_p(x) + kk * 8, bd,
+                        idesc_pv, (first && kk == 0) ? 0u : 1u);
+            }
           }
           tc_commit(&sm.pv_done[x][pb]);
           tc_commit(&sm.kv_empty[s]);
@@ -307,7 +344,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
           const int item = *reinterpret_cast<volatile int*>(&sm.item[k & 1]);
           mbar_arrive(&sm.item_empty[k & 1]);
           if (item < 0) break;
-          const PfItem it = pf_item(a, item);
+          const PfItem it = pf_item<BN>(a, item);
           if (!active) {  // no second query head: nothing to issue
             J += it.nkv;
             ++k;
@@ -316,16 +353,18 @@ __global__ void __launch_bounds__(kPfThreads, 1)
           if (!mbar_wait_bounded(&sm.q_full, k & 1)) { ok = false; break; }
           for (int j = 0; j < it.nkv && ok; ++j) {
             const int g = J + j;
-            const int s = g % kPfStages;
-            if (!mbar_wait_bounded(&sm.kv_full[s], (g / kPfStages) & 1)) { ok = false; break; }
+            const int s = g % STAGES;
+            if (!mbar_wait_bounded(&sm.kv_full[s], (g / STAGES) & 1)) { ok = false; break; }
             if (g >= 1 && !mbar_wait_bounded(&sm.s_free[x], (g - 1) & 1)) { ok = false; break; }
             tc_fence_after();
             const uint32_t k_addr = smem_u32(sm.k[s]);
-  #pragma unroll
-            for (int kk = 0; kk < 4; ++kk) {
-              const uint64_t ad = smem_desc_sw128(q_addr + kk * 32, 16, 1024);
-              const uint64_t bd = smem_desc_sw128(k_addr + kk * 32, 16, 1024);
-              tc_mma_ss(tmem + pf_col_s(x), ad, bd, idesc_qk, kk > 0 ? 1u : 0u);
+#pragma unroll
+            for (int kk = 0; kk < HD / 16; ++kk) {  // 16 dims per MMA, 4 per 128-byte half
+              const uint32_t off_q = (kk >> 2) * Sh::kQHalf + (kk & 3) * 32;
+              const uint32_t off_k = (kk >> 2) * Sh::kKVHalf + (kk & 3) * 32;
+              const uint64_t ad = smem_desc_sw128(q_addr + off_q, 16, 1024);
+              const uint64_t bd = smem_desc_sw128(k_addr + off_k, 16, 1024);
+              tc_mma_ss(tmem + Sh::col_s(x), ad, bd, idesc_qk, kk > 0 ? 1u : 0u);
             }
             tc_commit(&sm.s_full[x]);
             if (j == it.nkv - 1) tc_commit(&sm.q_empty);  // Q_x free once these S MMAs land
@@ -349,7 +388,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
     const uint32_t lane_base = tmem + (static_cast<uint32_t>((warp & 3) * 32) << 16);
     const float sc = a.score_scale;
     const bool active = x < n_slots;
-    uint32_t sv[128];  // this row of S (one TMEM read per tile); reused for O
+    uint32_t sv[BN];   // this row of S (one TMEM read per tile)
     int J = 0, k = 0;
     bool ok = true;
     while (ok) {
@@ -358,7 +397,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(&sm.item_empty[k & 1]);
       if (item < 0) break;
-      const PfItem it = pf_item(a, item);
+      const PfItem it = pf_item<BN>(a, item);
       if (!active) {  // slot B without a second query head: nothing to do
         J += it.nkv;
         ++k;
@@ -370,20 +409,21 @@ __global__ void __launch_bounds__(kPfThreads, 1)
         const int g = J + j;
         if (!mbar_wait_bounded(&sm.s_full[x], g & 1)) { ok = false; break; }
         tc_fence_after();
-        const int t0 = j * kPfBlockN;
-        const bool need_mask = t0 + kPfBlockN - 1 > it.p_min;  // diagonal tile
+        const int t0 = j * BN;
+        const bool need_mask = t0 + BN - 1 > it.p_min;  // diagonal tile
         const int lim = p_row - t0;  // columns c <= lim are visible
 #pragma unroll
-        for (int c4 = 0; c4 < 4; ++c4) tc_ld_x32(lane_base + pf_col_s(x) + 32 * c4, sv + 32 * c4);
+        for (int c4 = 0; c4 < BN / 32; ++c4)
+          tc_ld_x32(lane_base + Sh::col_s(x) + 32 * c4, sv + 32 * c4);
         tc_wait_ld();
 #pragma unroll
-        for (int c4 = 0; c4 < 4; ++c4) reg_fence32(sv + 32 * c4);
+        for (int c4 = 0; c4 < BN / 32; ++c4) reg_fence32(sv + 32 * c4);
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&sm.s_free[x]);  // S may be overwritten now
         if (need_mask) {
 #pragma unroll
-          for (int c = 0; c < 128; ++c)
+          for (int c = 0; c < BN; ++c)
             if (c > lim) sv[c] = __float_as_uint(-INFINITY);
         }
         // row max as a tree: 8 independent partial maxima, then combine
@@ -391,7 +431,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
 #pragma unroll
         for (int u = 0; u < 8; ++u) mp[u] = __uint_as_float(sv[u]);
 #pragma unroll
-        for (int c = 8; c < 128; c += 16)
+        for (int c = 8; c < BN; c += 16)
 #pragma unroll
           for (int u = 0; u < 8; ++u)
             mp[u] = max3(mp[u], __uint_as_float(sv[c + u]), __uint_as_float(sv[c + 8 + u]));
@@ -407,14 +447,14 @@ __global__ void __launch_bounds__(kPfThreads, 1)
           l_run *= alpha;
           m_used = m_new;
         }
-        // P = 2^(s*c - m) packed as FP16 pairs (masked -> 0), in two halves of
+        // P = 2^(s*c - m) packed as FP16 pairs (masked -> 0), in BN/64 parts of
         // 64 columns, each stored to TMEM as soon as it is ready
         const float2 sc2 = make_float2(sc, sc), nm2 = make_float2(-m_used, -m_used);
         float2 rs2[4];  // 4 independent partial row sums
 #pragma unroll
         for (int e = 0; e < 4; ++e) rs2[e] = make_float2(0.f, 0.f);
 #pragma unroll
-        for (int h = 0; h < 2; ++h) {
+        for (int h = 0; h < BN / 64; ++h) {
           uint32_t pw[32];
 #pragma unroll
           for (int cc = 0; cc < 8; ++cc) {  // 8 chunks of 8 columns
@@ -442,19 +482,19 @@ __global__ void __launch_bounds__(kPfThreads, 1)
             tc_fence_after();
             if (rescale && j >= 1) {
 #pragma unroll
-              for (int q4 = 0; q4 < 4; ++q4) {  // O in 4 chunks of 16 columns
+              for (int q4 = 0; q4 < HD / 16; ++q4) {  // O in chunks of 16 columns
                 uint32_t ov[16];
-                tc_ld_32x32b_x16(lane_base + pf_col_o(x) + 16 * q4, ov);
+                tc_ld_32x32b_x16(lane_base + Sh::col_o(x) + 16 * q4, ov);
                 tc_wait_ld();
 #pragma unroll
                 for (int d = 0; d < 16; ++d) asm volatile("" : "+r"(ov[d]));
 #pragma unroll
                 for (int d = 0; d < 16; ++d) ov[d] = __float_as_uint(__uint_as_float(ov[d]) * alpha);
-                tc_st_32x32b_x16(lane_base + pf_col_o(x) + 16 * q4, ov);
+                tc_st_32x32b_x16(lane_base + Sh::col_o(x) + 16 * q4, ov);
               }
             }
           }
-          tc_st_32x32b_x32(lane_base + pf_col_p(x) + 32 * h, pw);
+          tc_st_32x32b_x32(lane_base + Sh::col_p(x) + 32 * h, pw);
         }
         if (!ok) break;
         tc_wait_st();
@@ -469,11 +509,18 @@ __global__ void __launch_bounds__(kPfThreads, 1)
       const int g_last = J + it.nkv - 1;
       if (!mbar_wait_bounded(&sm.pv_done[x][g_last & 1], (g_last >> 1) & 1)) { ok = false; break; }
       tc_fence_after();
-      tc_ld_x32(lane_base + pf_col_o(x), sv);
-      tc_ld_x32(lane_base + pf_col_o(x) + 32, sv + 32);
+      // O (HD columns) lands in the dead S row where it fits
+      uint32_t ov_own[HD > BN ? HD : 1];
+      uint32_t* ov;
+      if constexpr (HD > BN)
+        ov = ov_own;
+      else
+        ov = sv;
+#pragma unroll
+      for (int c4 = 0; c4 < HD / 32; ++c4) tc_ld_x32(lane_base + Sh::col_o(x) + 32 * c4, ov + 32 * c4);
       tc_wait_ld();
-      reg_fence32(sv);
-      reg_fence32(sv + 32);
+#pragma unroll
+      for (int c4 = 0; c4 < HD / 32; ++c4) reg_fence32(ov + 32 * c4);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&sm.o_free[x]);
@@ -484,14 +531,14 @@ __global__ void __launch_bounds__(kPfThreads, 1)
       const float inv = 1.0f / l_run;
       float* stg = sm.stage[warp];
       const int row_base = it.q_row0 + (warp & 3) * 32;
-      float* dst = a.out + (x ? it.head1 : it.head0) * 64 + (lane & 7) * 4;
+      float* dst = a.out + (x ? it.head1 : it.head0) * HD + (lane & 7) * 4;
 #pragma unroll
-      for (int hc = 0; hc < 2; ++hc) {
+      for (int hc = 0; hc < HD / 32; ++hc) {
 #pragma unroll
         for (int c = 0; c < 32; c += 4)
           *reinterpret_cast<float4*>(stg + lane * kPfStagePitch + c) = make_float4(
-              __uint_as_float(sv[32 * hc + c]) * inv, __uint_as_float(sv[32 * hc + c + 1]) * inv,
-              __uint_as_float(sv[32 * hc + c + 2]) * inv, __uint_as_float(sv[32 * hc + c + 3]) * inv);
+              __uint_as_float(ov[32 * hc + c]) * inv, __uint_as_float(ov[32 * hc + c + 1]) * inv,
+              __uint_as_float(ov[32 * hc + c + 2]) * inv, __uint_as_float(ov[32 * hc + c + 3]) * inv);
         __syncwarp();
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
@@ -521,20 +568,24 @@ __global__ void __launch_bounds__(kPfThreads, 1)
 // Host side: one persistent CTA per SM (never more than there are items).
 // With `overlap`, the launch may begin while the previous grid on the stream
 // (the prologue) is still running (programmatic stream serialisation).
-inline int launch_prefill_attention(const PrefillArgs& a, const CUtensorMap& tm_q,
-                                    const CUtensorMap& tm_k, const CUtensorMap& tm_v,
-                                    int num_sms, cudaStream_t st, bool overlap) {
+// HD 64 runs <64, 128, 4>, HD 128 runs <128, 64, 3>; the tensor maps carry
+// boxes of 64 elements x 128 query rows (q) and 64 x BN cache rows (k, v).
+template <int HD, int BN, int STAGES>
+inline int launch_prefill_shape(const PrefillArgs& a, const CUtensorMap& tm_q,
+                                const CUtensorMap& tm_k, const CUtensorMap& tm_v, int num_sms,
+                                cudaStream_t st, bool overlap) {
+  auto kern = prefill_attn_kernel<HD, BN, STAGES>;
+  constexpr int smem = pf_smem_bytes<HD, BN, STAGES>();
   static bool attr_done = false;
   if (!attr_done) {
-    if (cudaFuncSetAttribute(prefill_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             kPfSmemBytes) != cudaSuccess)
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) !=
+        cudaSuccess)
       return -4;
     // the warpgroup register split assumes exactly this launch allocation:
     // with fewer registers per thread the softmax warps' increase could
     // never be granted
     cudaFuncAttributes fa;
-    if (cudaFuncGetAttributes(&fa, prefill_attn_kernel) != cudaSuccess ||
-        fa.numRegs != kPfLaunchRegs) {
+    if (cudaFuncGetAttributes(&fa, kern) != cudaSuccess || fa.numRegs != kPfLaunchRegs) {
       fprintf(stderr, "pl_attn: prefill kernel built with %d registers per thread, needs %d\n",
               fa.numRegs, kPfLaunchRegs);
       return -4;
@@ -547,15 +598,26 @@ inline int launch_prefill_attention(const PrefillArgs& a, const CUtensorMap& tm_
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid);
   cfg.blockDim = dim3(kPfThreads);
-  cfg.dynamicSmemBytes = kPfSmemBytes;
+  cfg.dynamicSmemBytes = smem;
   cfg.stream = st;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = overlap ? 1 : 0;
-  if (cudaLaunchKernelEx(&cfg, prefill_attn_kernel, a, tm_q, tm_k, tm_v) != cudaSuccess) return -4;
+  if (cudaLaunchKernelEx(&cfg, kern, a, tm_q, tm_k, tm_v) != cudaSuccess) return -4;
   return cudaGetLastError() == cudaSuccess ? 0 : -4;
+}
+
+// KV tile rows of the prefill kernel at a head_dim (the tensor-map box).
+constexpr int pf_block_n(int head_dim) { return head_dim == 128 ? 64 : 128; }
+
+inline int launch_prefill_attention(int head_dim, const PrefillArgs& a, const CUtensorMap& tm_q,
+                                    const CUtensorMap& tm_k, const CUtensorMap& tm_v,
+                                    int num_sms, cudaStream_t st, bool overlap) {
+  if (head_dim == 128)
+    return launch_prefill_shape<128, 64, 3>(a, tm_q, tm_k, tm_v, num_sms, st, overlap);
+  return launch_prefill_shape<64, 128, 4>(a, tm_q, tm_k, tm_v, num_sms, st, overlap);
 }
 
 }  // namespace pl

@@ -27,7 +27,6 @@
 
 namespace {
 
-using pl::kHD;
 using pl::part_stride;
 
 typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
@@ -74,7 +73,7 @@ struct Ctx {
   cudaStream_t stream = nullptr;
   CUtensorMap tm_k_dec, tm_v_dec;  // decode: box {64, tp, Hk, 1}, head_dim/64 per tile
   CUtensorMap tm_k_pf, tm_v_pf;    // prefill: box {64, 128 rows, 1, 1}
-  CUtensorMap tm_q16;              // prefill q staging: box {64, 1 head, 128 rows}
+  CUtensorMap tm_q16;              // prefill q staging: box {64, 1 head, 128 rows}, HD/64 per row
   EncodeTiledFn encode = nullptr;
   // profiling: event pairs around each attention kernel (see pl_attn_profile)
   int profiling = 0;
@@ -261,7 +260,7 @@ int ensure_part(size_t floats) {
   return PL_OK;
 }
 
-// FP16 q staging for the prefill, [rows][n_heads][64], with its TMA map.
+// FP16 q staging for the prefill, [rows][n_heads][head_dim], with its TMA map.
 // Rows past the current n_tok hold stale data; they only feed query rows
 // whose output is never stored.
 int ensure_q16(int n_tok) {
@@ -276,12 +275,12 @@ int ensure_q16(int n_tok) {
     return PL_ENOMEM;
   if (cudaMemset(g->d_q16, 0, cap_rows * g->q_dim * sizeof(uint16_t)) != cudaSuccess)
     return PL_ECUDA;
-  const cuuint64_t dims[3] = {static_cast<cuuint64_t>(kHD), static_cast<cuuint64_t>(g->n_heads),
+  const cuuint64_t dims[3] = {static_cast<cuuint64_t>(g->head_dim),
+                              static_cast<cuuint64_t>(g->n_heads),
                               static_cast<cuuint64_t>(cap_rows)};
-  const cuuint64_t strides[2] = {static_cast<cuuint64_t>(kHD) * 2,
+  const cuuint64_t strides[2] = {static_cast<cuuint64_t>(g->head_dim) * 2,
                                  static_cast<cuuint64_t>(g->q_dim) * 2};
-  const cuuint32_t box[3] = {static_cast<cuuint32_t>(kHD), 1u,
-                             static_cast<cuuint32_t>(pl::kPfBlockM)};
+  const cuuint32_t box[3] = {64u, 1u, static_cast<cuuint32_t>(pl::kPfBlockM)};
   const cuuint32_t estr[3] = {1, 1, 1};
   if (g->encode(&g->tm_q16, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, g->d_q16, dims, strides, box, estr,
                 CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
@@ -357,7 +356,6 @@ pl::DecodeArgs decode_args(int layer, int n, const int* d_seqs, const int* d_pos
   a.pos = d_pos;
   a.seq1 = 0;
   a.pos1 = 0;
-  a.pos_inc = 0;
   a.q = d_q;
   a.k = d_k;
   a.v = d_v;
@@ -670,9 +668,9 @@ int pl_attn_init(int n_layers, int n_heads, int n_kv_heads, int head_dim, int ma
       (rc = make_map(c->encode, &c->tm_v_dec, c->d_v, head_dim, max_seq_len, n_kv_heads, n_slabs,
                      c->tp, n_kv_heads)) ||
       (rc = make_map(c->encode, &c->tm_k_pf, c->d_k, head_dim, max_seq_len, n_kv_heads, n_slabs,
-                     pl::kPfBlockN, 1)) ||
+                     pl::pf_block_n(head_dim), 1)) ||
       (rc = make_map(c->encode, &c->tm_v_pf, c->d_v, head_dim, max_seq_len, n_kv_heads, n_slabs,
-                     pl::kPfBlockN, 1))) {
+                     pl::pf_block_n(head_dim), 1))) {
     free_ctx(c);
     return rc;
   }
@@ -978,52 +976,20 @@ int pl_attn_kv_ptr(int seq, int layer, uint16_t** d_k, uint16_t** d_v) {
 // ---------------------------------------------------------------- prefill
 static bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
-// head_dim 128: the cache rows first (the prologue without the q staging),
-// then the batched decode kernel with one entry per token -- entry i is row
-// start_pos + i of the same slot and attends rows [0, start_pos + i], all of
-// them already in the cache, so it appends nothing.  Causal attention,
-// FP32 softmax and FP16 cache rows as in the tensor-core path; the partition
-// of the decode kernel splits the n_tok * rows tiles over the SMs.
-static int launch_prefill_by_decode(int seq, int layer, int start_pos, int n_tok,
-                                    const float* d_q, const float* d_k, const float* d_v,
-                                    float* d_out, int out_stride, cudaStream_t st) {
-  const size_t off = static_cast<size_t>(start_pos) * g->kv_dim;
-  pl::prefill_prologue_kernel<128><<<n_tok, pl::kPrologueThreads, 0, st>>>(
-      d_q, d_k, d_v, nullptr, slab_k(seq, layer) + off, slab_v(seq, layer) + off, n_tok,
-      g->n_heads, g->n_kv_heads, start_pos, g->d_cos, g->d_sin, g->rope_type);
-  PL_CUDA(cudaGetLastError());
-  count_launch();
-  for (int t0 = 0; t0 < n_tok; t0 += pl::kMaxLaunchSeqs) {
-    const int m = n_tok - t0 < pl::kMaxLaunchSeqs ? n_tok - t0 : pl::kMaxLaunchSeqs;
-    const int grid = decode_grid(m, start_pos + t0 + m);
-    int rc = ensure_part(static_cast<size_t>(grid + m) * g->part_floats);
-    if (rc) return rc;
-    const float* q = d_q + static_cast<size_t>(t0) * g->q_dim;
-    pl::DecodeArgs a = decode_args(layer, m, nullptr, nullptr, q, q, q,
-                                   d_out + static_cast<size_t>(t0) * out_stride, 0, 0, 0, 0,
-                                   nullptr, g->d_part, g->d_seg_info);
-    a.seq1 = seq;
-    a.pos1 = start_pos + t0;
-    a.pos_inc = 1;
-    a.out_stride = out_stride;
-    rc = launch_decode_kernel(a, grid, st, true);
-    if (rc) return rc;
-  }
-  return PL_OK;
-}
-
 static int launch_prefill(int seq, int layer, int start_pos, int n_tok, const float* d_q,
                           const float* d_k, const float* d_v, float* d_out, int out_stride,
                           cudaStream_t st) {
-  if (g->head_dim != kHD)
-    return launch_prefill_by_decode(seq, layer, start_pos, n_tok, d_q, d_k, d_v, d_out,
-                                    out_stride, st);
   int rc = ensure_q16(n_tok);
   if (rc) return rc;
   const size_t off = static_cast<size_t>(start_pos) * g->kv_dim;
-  pl::prefill_prologue_kernel<kHD><<<n_tok, pl::kPrologueThreads, 0, st>>>(
-      d_q, d_k, d_v, g->d_q16, slab_k(seq, layer) + off, slab_v(seq, layer) + off, n_tok,
-      g->n_heads, g->n_kv_heads, start_pos, g->d_cos, g->d_sin, g->rope_type);
+  if (g->head_dim == 128)
+    pl::prefill_prologue_kernel<128><<<n_tok, pl::kPrologueThreads, 0, st>>>(
+        d_q, d_k, d_v, g->d_q16, slab_k(seq, layer) + off, slab_v(seq, layer) + off, n_tok,
+        g->n_heads, g->n_kv_heads, start_pos, g->d_cos, g->d_sin, g->rope_type);
+  else
+    pl::prefill_prologue_kernel<64><<<n_tok, pl::kPrologueThreads, 0, st>>>(
+        d_q, d_k, d_v, g->d_q16, slab_k(seq, layer) + off, slab_v(seq, layer) + off, n_tok,
+        g->n_heads, g->n_kv_heads, start_pos, g->d_cos, g->d_sin, g->rope_type);
   PL_CUDA(cudaGetLastError());
   count_launch();
   pl::PrefillArgs a;
@@ -1035,13 +1001,13 @@ static int launch_prefill(int seq, int layer, int start_pos, int n_tok, const fl
   a.n_heads = g->n_heads;
   a.kv_mul = g->kv_mul;
   a.slab = seq * g->n_layers + layer;
-  a.score_scale = pl::kLog2e / sqrtf(static_cast<float>(kHD));
+  a.score_scale = pl::kLog2e / sqrtf(static_cast<float>(g->head_dim));
   a.work = g->d_work;
   a.err = g->d_err;
   prof_begin(st);
   // overlap with the prologue except when events separate the two for timing
-  if (pl::launch_prefill_attention(a, g->tm_q16, g->tm_k_pf, g->tm_v_pf, g->num_sms, st,
-                                   !g->profiling) != 0)
+  if (pl::launch_prefill_attention(g->head_dim, a, g->tm_q16, g->tm_k_pf, g->tm_v_pf,
+                                   g->num_sms, st, !g->profiling) != 0)
     return PL_ECUDA;
   prof_end(st);
   count_launch();

@@ -2,10 +2,10 @@
 
 picolm's model.c takes any head_dim up to 256 (model.c:856); the kernels
 support 64 and 128, which covers the GGUF models the parser accepts in
-practice (LLaMA-3 8B, Mistral 7B, Qwen2.5 7B use 128).  At 128 a KV tile is
-staged as two 64-element halves, and the prefill appends the rows and runs
-the batched decode kernel over the positions.  KV rows must be bit-identical
-to picolm's; outputs within max-abs 2e-3 / rel 1e-2 of the oracle.
+practice (LLaMA-3 8B, Mistral 7B, Qwen2.5 7B use 128).  At 128 every row of a
+Q, K or V tile is staged as two 64-element halves; the prefill runs the
+tcgen05 kernel with 64-row KV tiles.  KV rows must be bit-identical to
+picolm's; outputs within max-abs 2e-3 / rel 1e-2 of the oracle.
 """
 import numpy as np
 import pytest
@@ -80,7 +80,7 @@ def test_long_context_split():
 
 @pytest.mark.parametrize("H,Hk,start,n_tok,rope_type", [
     (8, 2, 0, 1, 0), (8, 2, 0, 130, 0), (32, 8, 77, 200, 0), (16, 2, 5, 150, 1),
-    (8, 1, 0, 1100, 0)])   # 1100 rows: two launches of at most 1024 positions
+    (32, 4, 0, 1100, 0), (8, 8, 0, 300, 0), (8, 1, 3, 190, 0)])
 def test_prefill_vs_oracle(H, Hk, start, n_tok, rope_type):
     rng = np.random.default_rng(2000 + H + Hk + start + n_tok)
     ms = start + n_tok + 16
