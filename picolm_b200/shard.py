@@ -9,7 +9,8 @@ is too long for one device's bandwidth, it is split along the sequence axis:
 * the LAST rank also holds every position appended after n_cached (its
   local row pos - row0), so a decode step appends on exactly one rank;
 * per layer and step every rank computes the partial triple (m, l, o) of
-  its rows with pl_attn_decode_partial_dev (8,704 bytes for 32 heads) and
+  its rows with pl_attn_decode_partial_dev (8,704 bytes for 32 heads of
+  64) and
   the partials are merged in rank order on every rank, either after an
   NCCL all-gather with pl_attn_combine_dev (AttnShardOps) or by one kernel
   that pushes them over NVLink peer memory (P2PShardOps):
@@ -26,7 +27,10 @@ from __future__ import annotations
 
 from dataclasses import dataclass
 
-PART_STRIDE = 68  # floats per head in a partial block at head_dim 64: m, l, 2 pad, o[64]
+# Floats per head in a partial block at head_dim 64: m, l, 2 pad, o[64].  A
+# caller sizes `part` as n_heads * attn.part_stride floats (head_dim + 4 per
+# head, so 132 at head_dim 128) and `parts_all` as world times that.
+PART_STRIDE = 68
 
 
 def shard_range(n_cached: int, world: int, rank: int) -> tuple[int, int]:
