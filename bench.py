@@ -558,11 +558,22 @@ def run_hd128(args, local, peaks):
     e1.record()
     torch.cuda.synchronize()
     ms = e0.elapsed_time(e1) / reps
+    # the attention kernel alone (module events; they separate it from the
+    # prologue)
+    at.profile(True)
+    for _ in range(reps):
+        pf()
+    torch.cuda.synchronize()
+    kern_ms, _, _ = at.profile_read()
+    at.profile(False)
     at.close()
     flops = 4.0 * H8 * HD8 * S * (S + 1) / 2
+    kern_tf = flops * reps / (kern_ms / 1e3) / 1e12
     res["prefill"] = {"metric": "prefill-attn TFLOP/s (head_dim 128, causal FLOPs / call time)",
                       "value": flops / (ms / 1e3) / 1e12, "unit": "TFLOP/s",
-                      "ms_per_layer": ms,
+                      "ms_per_layer": ms, "attn_kernel_tflops": kern_tf,
+                      "attn_kernel_frac": kern_tf / peaks["bf16_tflops"],
+                      "traffic": profile_traffic("prefill_attn_kernel_hd128.txt"),
                       "path": "prologue (RoPE + append + FP16 q) then the tcgen05 kernel, "
                               "64-row KV tiles"}
     return res
