@@ -110,6 +110,17 @@ int  pl_attn_prefill(int seq, int layer, int start_pos, int n_tok,
                      const float *q, const float *k, const float *v,
                      float *out, int out_stride);
 
+/* Page-lock a caller buffer for the host-buffer calls above: an input or
+ * output that lies inside a registered range moves directly between it and
+ * the device, without the copy through the module's staging area.  model.c
+ * allocates s->q, s->k, s->v and s->xb once (model.c:597-619) and can
+ * register them after pl_attn_init.  Ranges must not overlap (PL_EARG); a
+ * range is unregistered by its start address, and must be before the memory
+ * is freed (pl_attn_shutdown unregisters what is left).  No counterpart in
+ * the reference: picolm has no device memory. */
+int  pl_attn_host_register(void *ptr, size_t bytes);
+int  pl_attn_host_unregister(void *ptr);
+
 /* RoPE alone, in place on host buffers, bit-identical to rope()
  * (tensor.c:533-603): q [n_tok][n_heads*head_dim], k [n_tok][kv_dim]
  * (either may be NULL), position of row i = pos0 + i. */

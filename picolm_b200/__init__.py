@@ -73,6 +73,8 @@ def load(path: str = LIB_PATH) -> C.CDLL:
     lib = C.CDLL(path)
     i = C.c_int
     sig = {
+        "pl_attn_host_register": (i, [C.c_void_p, C.c_size_t]),
+        "pl_attn_host_unregister": (i, [C.c_void_p]),
         "pl_attn_init": (i, [i, i, i, i, i, C.c_float, i, i, i]),
         "pl_attn_set_rope": (i, [_f32p, _f32p, i, i]),
         "pl_attn_available": (i, []),
@@ -201,6 +203,17 @@ class Attn:
         n_tok = (qa.size // self.q_dim) if qa is not None else (ka.size // self.kv_dim)
         _check(self.lib.pl_attn_rope(pos0, n_tok, _ptr(qa), _ptr(ka)), "pl_attn_rope")
         return qa, ka
+
+    def host_register(self, arr: np.ndarray) -> None:
+        """Page-lock `arr` (a contiguous array the caller keeps alive) so
+        that host-buffer calls move it without staging."""
+        if not arr.flags.c_contiguous:
+            raise ValueError("host_register needs a contiguous array")
+        _check(self.lib.pl_attn_host_register(arr.ctypes.data, arr.nbytes),
+               "pl_attn_host_register")
+
+    def host_unregister(self, arr: np.ndarray) -> None:
+        _check(self.lib.pl_attn_host_unregister(arr.ctypes.data), "pl_attn_host_unregister")
 
     def kv_download(self, seq: int, layer: int, pos0: int, n_pos: int):
         k = np.empty(n_pos * self.kv_dim, np.uint16)

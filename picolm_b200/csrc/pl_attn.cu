@@ -155,6 +155,23 @@ int ensure_stage(size_t bytes) {
   return PL_OK;
 }
 
+// ---- caller buffers page-locked with pl_attn_host_register ----------------
+// A host-buffer call moves an input or output that lies inside a registered
+// range directly between it and the device (no copy through the staging
+// area).  model.c allocates s->q, s->k, s->v and s->xb once and reuses them
+// for every call, so it can register them at start-up.
+struct HostRange {
+  uintptr_t lo, hi;
+};
+std::vector<HostRange> g_pinned;
+
+bool pinned(const void* p, size_t bytes) {
+  const uintptr_t a = reinterpret_cast<uintptr_t>(p);
+  for (const HostRange& r : g_pinned)
+    if (a >= r.lo && a + bytes <= r.hi) return true;
+  return false;
+}
+
 // ---- parallel copies between caller buffers and the pinned staging area ---
 // The host-buffer entry points move every input and output through the
 // pinned staging area; one thread copies only about 10 GB/s, which made
@@ -700,6 +717,8 @@ int pl_attn_init(int n_layers, int n_heads, int n_kv_heads, int head_dim, int ma
 
 void pl_attn_shutdown(void) {
   std::lock_guard<std::mutex> lk(g_mu);
+  for (const HostRange& r : g_pinned) cudaHostUnregister(reinterpret_cast<void*>(r.lo));
+  g_pinned.clear();
   delete g_copy;
   g_copy = nullptr;
   if (g && g->device >= 0) cudaSetDevice(g->device);
@@ -716,6 +735,27 @@ int pl_attn_set_rope(const float* cos_tab, const float* sin_tab, int n_rows, int
   PL_CUDA(cudaMemcpyAsync(g->d_cos, cos_tab, bytes, cudaMemcpyHostToDevice, g->stream));
   PL_CUDA(cudaMemcpyAsync(g->d_sin, sin_tab, bytes, cudaMemcpyHostToDevice, g->stream));
   PL_CUDA(cudaStreamSynchronize(g->stream));
+  return PL_OK;
+}
+
+// Output (qb bytes at d_out on the device) and the error word to the caller:
+// straight into a registered `out`, else through the staging area at h (qb
+// + 4 bytes) with one read-back.  Waits for the stream.
+static int read_back(const float* d_out, float* out, size_t qb, uint8_t* h) {
+  uint8_t* d = reinterpret_cast<uint8_t*>(const_cast<float*>(d_out));
+  PL_CUDA(cudaMemcpyAsync(d + qb, g->d_err, sizeof(uint32_t), cudaMemcpyDeviceToDevice,
+                          g->stream));
+  const bool direct = pinned(out, qb);
+  if (direct) {
+    PL_CUDA(cudaMemcpyAsync(out, d, qb, cudaMemcpyDeviceToHost, g->stream));
+    PL_CUDA(cudaMemcpyAsync(h + qb, d + qb, sizeof(uint32_t), cudaMemcpyDeviceToHost, g->stream));
+  } else {
+    PL_CUDA(cudaMemcpyAsync(h, d, qb + sizeof(uint32_t), cudaMemcpyDeviceToHost, g->stream));
+  }
+  const int rc = finish_host_call(reinterpret_cast<uint32_t*>(h + qb));
+  if (rc || direct) return rc;
+  const CopyPiece o = {reinterpret_cast<uint8_t*>(out), h, qb};
+  host_copy(&o, 1);
   return PL_OK;
 }
 
@@ -742,16 +782,25 @@ int pl_attn_decode_batch(int layer, int n, const int* seqs, const int* pos, cons
   int rc = ensure_stage(total);
   if (rc) return rc;
   uint8_t* h = g->h_stage;
-  {
+  uint8_t* d = g->d_stage;
+  if (pinned(q, qb) && pinned(k, kb) && pinned(v, kb)) {
+    // registered inputs go straight to the device; seqs and pos are staged
+    PL_CUDA(cudaMemcpyAsync(d, q, qb, cudaMemcpyHostToDevice, g->stream));
+    PL_CUDA(cudaMemcpyAsync(d + qb, k, kb, cudaMemcpyHostToDevice, g->stream));
+    PL_CUDA(cudaMemcpyAsync(d + qb + kb, v, kb, cudaMemcpyHostToDevice, g->stream));
+    std::memcpy(h + qb + 2 * kb, seqs, ib);
+    std::memcpy(h + qb + 2 * kb + ib, pos, ib);
+    PL_CUDA(cudaMemcpyAsync(d + qb + 2 * kb, h + qb + 2 * kb, 2 * ib, cudaMemcpyHostToDevice,
+                            g->stream));
+  } else {
     const CopyPiece in[5] = {{h, reinterpret_cast<const uint8_t*>(q), qb},
                              {h + qb, reinterpret_cast<const uint8_t*>(k), kb},
                              {h + qb + kb, reinterpret_cast<const uint8_t*>(v), kb},
                              {h + qb + 2 * kb, reinterpret_cast<const uint8_t*>(seqs), ib},
                              {h + qb + 2 * kb + ib, reinterpret_cast<const uint8_t*>(pos), ib}};
     host_copy(in, 5);
+    PL_CUDA(cudaMemcpyAsync(d, h, in_bytes, cudaMemcpyHostToDevice, g->stream));
   }
-  uint8_t* d = g->d_stage;
-  PL_CUDA(cudaMemcpyAsync(d, h, in_bytes, cudaMemcpyHostToDevice, g->stream));
   float* d_out = reinterpret_cast<float*>(d + out_off);
   rc = launch_decode(layer, n, reinterpret_cast<int*>(d + qb + 2 * kb),
                      reinterpret_cast<int*>(d + qb + 2 * kb + ib), max_pos + 1,
@@ -759,21 +808,46 @@ int pl_attn_decode_batch(int layer, int n, const int* seqs, const int* pos, cons
                      reinterpret_cast<float*>(d + qb + kb), d_out, 0, 0, 0, 1, nullptr,
                      g->stream);
   if (rc) return rc;
-  // output and the error word in one read-back
-  PL_CUDA(cudaMemcpyAsync(d + out_off + qb, g->d_err, sizeof(uint32_t), cudaMemcpyDeviceToDevice,
-                          g->stream));
-  PL_CUDA(cudaMemcpyAsync(h + out_off, d + out_off, qb + sizeof(uint32_t), cudaMemcpyDeviceToHost,
-                          g->stream));
-  rc = finish_host_call(reinterpret_cast<uint32_t*>(h + out_off + qb));
-  if (rc) return rc;
-  const CopyPiece o = {reinterpret_cast<uint8_t*>(out), h + out_off, qb};
-  host_copy(&o, 1);
-  return PL_OK;
+  return read_back(d_out, out, qb, h + out_off);
 }
 
 int pl_attn_decode(int seq, int layer, int pos, const float* q, const float* k, const float* v,
                    float* out) {
   return pl_attn_decode_batch(layer, 1, &seq, &pos, q, k, v, out);
+}
+
+int pl_attn_host_register(void* ptr, size_t bytes) {
+  if (!g) return PL_ESTATE;
+  if (!ptr || bytes == 0) return PL_EARG;
+  const uintptr_t a = reinterpret_cast<uintptr_t>(ptr);
+  for (const HostRange& r : g_pinned)
+    if (a < r.hi && a + bytes > r.lo) return PL_EARG;  // overlaps a registered range
+  if (cudaSetDevice(g->device) != cudaSuccess) return PL_ECUDA;
+  const cudaError_t e = cudaHostRegister(ptr, bytes, cudaHostRegisterDefault);
+  if (e != cudaSuccess) {
+    cudaGetLastError();  // the call stays usable through the staging area
+    std::fprintf(stderr, "pl_attn_host_register: %s\n", cudaGetErrorString(e));
+    return PL_ECUDA;
+  }
+  g_pinned.push_back({a, a + bytes});
+  return PL_OK;
+}
+
+int pl_attn_host_unregister(void* ptr) {
+  if (!g) return PL_ESTATE;
+  const uintptr_t a = reinterpret_cast<uintptr_t>(ptr);
+  for (size_t i = 0; i < g_pinned.size(); ++i)
+    if (g_pinned[i].lo == a) {
+      PL_CUDA(cudaStreamSynchronize(g->stream));
+      const cudaError_t e = cudaHostUnregister(ptr);
+      g_pinned.erase(g_pinned.begin() + static_cast<long>(i));
+      if (e != cudaSuccess) {
+        cudaGetLastError();
+        return PL_ECUDA;
+      }
+      return PL_OK;
+    }
+  return PL_EARG;
 }
 
 int pl_attn_decode_batch_dev(int layer, int n, const int* d_seqs, const int* d_pos, int max_pos,
@@ -1031,33 +1105,33 @@ int pl_attn_prefill(int seq, int layer, int start_pos, int n_tok, const float* q
   if (rc) return rc;
   uint8_t* h = g->h_stage;
   uint8_t* d = g->d_stage;
-  {
+  if (pinned(q, qb) && pinned(k, kb) && pinned(v, kb)) {
+    PL_CUDA(cudaMemcpyAsync(d, q, qb, cudaMemcpyHostToDevice, g->stream));
+    PL_CUDA(cudaMemcpyAsync(d + qb, k, kb, cudaMemcpyHostToDevice, g->stream));
+    PL_CUDA(cudaMemcpyAsync(d + qb + kb, v, kb, cudaMemcpyHostToDevice, g->stream));
+  } else {
     const CopyPiece in[3] = {{h, reinterpret_cast<const uint8_t*>(q), qb},
                              {h + qb, reinterpret_cast<const uint8_t*>(k), kb},
                              {h + qb + kb, reinterpret_cast<const uint8_t*>(v), kb}};
     host_copy(in, 3);
+    PL_CUDA(cudaMemcpyAsync(d, h, in_bytes, cudaMemcpyHostToDevice, g->stream));
   }
-  PL_CUDA(cudaMemcpyAsync(d, h, in_bytes, cudaMemcpyHostToDevice, g->stream));
   float* d_out = reinterpret_cast<float*>(d + out_off);
   rc = launch_prefill(seq, layer, start_pos, n_tok, reinterpret_cast<float*>(d),
                       reinterpret_cast<float*>(d + qb), reinterpret_cast<float*>(d + qb + kb),
                       d_out, g->q_dim, g->stream);
   if (rc) return rc;
+  if (out_stride == g->q_dim) return read_back(d_out, out, qb, h + out_off);
   PL_CUDA(cudaMemcpyAsync(d + out_off + qb, g->d_err, sizeof(uint32_t), cudaMemcpyDeviceToDevice,
                           g->stream));
   PL_CUDA(cudaMemcpyAsync(h + out_off, d + out_off, qb + sizeof(uint32_t), cudaMemcpyDeviceToHost,
                           g->stream));
   rc = finish_host_call(reinterpret_cast<uint32_t*>(h + out_off + qb));
   if (rc) return rc;
-  if (out_stride == g->q_dim) {
-    const CopyPiece o = {reinterpret_cast<uint8_t*>(out), h + out_off, qb};
-    host_copy(&o, 1);
-  } else {
-    for (int r = 0; r < n_tok; ++r)
-      std::memcpy(out + static_cast<size_t>(r) * out_stride,
-                  h + out_off + static_cast<size_t>(r) * g->q_dim * sizeof(float),
-                  g->q_dim * sizeof(float));
-  }
+  for (int r = 0; r < n_tok; ++r)
+    std::memcpy(out + static_cast<size_t>(r) * out_stride,
+                h + out_off + static_cast<size_t>(r) * g->q_dim * sizeof(float),
+                g->q_dim * sizeof(float));
   return PL_OK;
 }
 

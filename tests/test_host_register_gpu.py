@@ -1,0 +1,86 @@
+"""pl_attn_host_register: host-buffer calls whose inputs and outputs lie in
+registered (page-locked) caller memory move them directly between the caller
+and the device.  Results must equal the staged path bit for bit; the error
+cases return status codes and leave the module usable."""
+import numpy as np
+import pytest
+
+import picolm_b200 as pb
+from tests.util import random_cache
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module", autouse=True)
+def _built():
+    from picolm_b200 import build
+    build.build()
+
+
+def _inputs(rng, n, q_dim, kv_dim):
+    return (rng.standard_normal((n, q_dim), dtype=np.float32),
+            rng.standard_normal((n, kv_dim), dtype=np.float32),
+            rng.standard_normal((n, kv_dim), dtype=np.float32))
+
+
+def test_decode_batch_registered_equals_staged():
+    rng = np.random.default_rng(31)
+    H, Hk, ms, n = 32, 4, 300, 6
+    pos = np.array([0, 3, 64, 127, 200, 299], np.int32)
+    seqs = np.arange(n, dtype=np.int32)
+    q, k, v = _inputs(rng, n, H * 64, Hk * 64)
+    caches = [(random_cache(rng, ms, Hk * 64), random_cache(rng, ms, Hk * 64)) for _ in range(n)]
+    results = []
+    for mode in ("staged", "registered", "out only"):
+        with pb.Attn(1, H, Hk, ms, n_seqs=n) as at:
+            for s, (kc, vc) in enumerate(caches):
+                at.kv_upload(s, 0, 0, kc, vc)
+            qq, kk, vv = q.copy(), k.copy(), v.copy()
+            out = np.zeros(n * H * 64, np.float32)
+            if mode == "registered":
+                for a in (qq, kk, vv):
+                    at.host_register(a)
+            if mode != "staged":
+                at.host_register(out)
+            at.decode_batch(0, seqs, pos, qq, kk, vv, out=out)
+            gk, gv = at.kv_download(3, 0, 0, ms)
+            if mode != "staged":
+                at.host_unregister(out)
+            results.append((out.copy(), gk, gv))
+    for got in results[1:]:
+        np.testing.assert_array_equal(got[0].view(np.uint32), results[0][0].view(np.uint32))
+        np.testing.assert_array_equal(got[1], results[0][1])
+        np.testing.assert_array_equal(got[2], results[0][2])
+
+
+def test_prefill_registered_equals_staged():
+    rng = np.random.default_rng(32)
+    H, Hk, ms, n = 32, 4, 400, 333
+    q, k, v = _inputs(rng, n, H * 64, Hk * 64)
+    outs = []
+    for registered in (False, True):
+        with pb.Attn(1, H, Hk, ms) as at:
+            qq, kk, vv = q.copy(), k.copy(), v.copy()
+            out = np.zeros((n, H * 64), np.float32)
+            if registered:
+                for a in (qq, kk, vv, out):
+                    at.host_register(a)
+            got = at.prefill(0, 0, 7, qq, kk, vv, out=out)
+            outs.append(np.array(got))
+    np.testing.assert_array_equal(outs[1].view(np.uint32), outs[0].view(np.uint32))
+
+
+def test_register_errors_leave_module_usable():
+    rng = np.random.default_rng(33)
+    H, Hk, ms = 8, 2, 64
+    buf = np.zeros(1 << 16, np.float32)
+    with pb.Attn(1, H, Hk, ms) as at:
+        at.host_register(buf)
+        # a range overlapping a registered one, and an address that starts none
+        assert at.lib.pl_attn_host_register(buf.ctypes.data + 64, 1024) == pb.PL_EARG
+        assert at.lib.pl_attn_host_unregister(buf.ctypes.data + 4) == pb.PL_EARG
+        at.host_unregister(buf)
+        assert at.lib.pl_attn_host_unregister(buf.ctypes.data) == pb.PL_EARG
+        q, k, v = _inputs(rng, 1, H * 64, Hk * 64)
+        out = at.decode(0, 0, 0, q[0], k[0], v[0])
+        assert np.isfinite(out).all()
