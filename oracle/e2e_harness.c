@@ -75,6 +75,11 @@ int main(int argc, char **argv) {
     if (rc == PL_OK)
         rc = pl_attn_set_rope(model.state.rope_cos, model.state.rope_sin, c->max_seq_len,
                               c->head_dim / 2);
+    /* the run-state block holds s->q, k_tmp, v_tmp and s->xb (model.c:593-627):
+       page-locked once, the decode calls DMA them without staging */
+    if (rc == PL_OK)
+        rc = pl_attn_host_register(model.state.mem_block,
+                                   model.state.mem_size - model.state.kv_size);
     if (rc != PL_OK) {
         fprintf(stderr, "pl_attn: %s\n", pl_attn_strerror(rc));
         return 1;
@@ -121,6 +126,7 @@ int main(int argc, char **argv) {
            n_prompt - cache_pos, t1 - t0, n_gen - 1, t2 - t1, threads);
     fflush(stdout);
 #ifdef USE_PL_ATTN
+    pl_attn_host_unregister(model.state.mem_block);
     pl_attn_shutdown();
 #endif
     free(prompt);
