@@ -221,3 +221,36 @@ def test_kv_split_partials_and_combine():
         rk, _ = at.kv_download(2, 0, P - bounds[2], 1)
     np.testing.assert_array_equal(rk[0], kc2[P])
     assert_attn_close(got, want, "3-shard combine")
+
+
+def test_batch_over_one_launch():
+    # 1100 sequences: more than one launch holds (1024), so the call runs the
+    # decode kernel and merge twice; sequences on both sides of the chunk
+    # edge, and the first and last, against the oracle
+    rng = np.random.default_rng(41)
+    H, Hk, ms, n = 8, 2, 48, 1100
+    kv = Hk * 64
+    tables = O.rope_tables(ms, 64, 10000.0)
+    pos = rng.integers(0, ms, n).astype(np.int32)
+    pos[[0, 1023, 1024, n - 1]] = [ms - 1, 0, ms - 1, 17]
+    seqs = rng.permutation(n).astype(np.int32)
+    q = rng.standard_normal((n, H * 64), dtype=np.float32)
+    k = rng.standard_normal((n, kv), dtype=np.float32)
+    v = rng.standard_normal((n, kv), dtype=np.float32)
+    check = [0, 1, 500, 1022, 1023, 1024, 1025, n - 1]
+    with pb.Attn(1, H, Hk, ms, n_seqs=n) as at:
+        caches = {}
+        for i in check:
+            s = int(seqs[i])
+            caches[s] = (random_cache(rng, ms, kv), random_cache(rng, ms, kv))
+            at.kv_upload(s, 0, 0, *caches[s])
+        out = at.decode_batch(0, seqs, pos, q, k, v).reshape(n, H * 64)
+        for i in check:
+            s = int(seqs[i])
+            kc, vc = caches[s]
+            want, kc2, vc2 = oracle_decode_layer(H, Hk, ms, kc, vc, int(pos[i]), q[i], k[i], v[i],
+                                                 tables)
+            gk, gv = at.kv_download(s, 0, 0, ms)
+            np.testing.assert_array_equal(gk, kc2)
+            np.testing.assert_array_equal(gv, vc2)
+            assert_attn_close(out[i], want, f"batch of {n}: entry {i} (slot {s}, pos {pos[i]})")
