@@ -689,6 +689,78 @@ def run_long_ctx_split(args, rank, world, local, peaks):
                        "shard": f"{dec.n_rows} cached positions on rank {rank}"}}
 
 
+def run_long_ctx_heads(args, rank, world, local, peaks):
+    """Config 5 split by KV head over `world` GPUs (attention tensor
+    parallelism): rank r holds all 32768 cached positions of KV heads
+    [8r/world, 8(r+1)/world) and runs their query heads; its output is that
+    slice of heads of every layer's attention row, which a row-parallel
+    output projection consumes without a gather.  Same data, step structure
+    and timing as the KV split (one CUDA graph of the 32 steps x 16 layers,
+    max over ranks)."""
+    import torch
+    import picolm_b200 as pb
+    from picolm_b200.shard import head_shard
+    L, HK5, CTX5, NS5 = 16, 8, 32768, 32
+    kv5 = HK5 * HD
+    h0, hq, k0, hk = head_shard(H, HK5, world, rank)
+    dev = torch.device("cuda", local)
+    at = pb.Attn(L, hq, hk, CTX5 + NS5, rope_base=500000.0, device=local)
+    stream = torch.cuda.current_stream(dev)
+    rng = np.random.default_rng(4)
+    for l in range(L):
+        kc = make_cache_host(rng, CTX5, kv5)
+        vc = make_cache_host(rng, CTX5, kv5)
+        at.kv_upload(0, l, 0, np.ascontiguousarray(kc[:, k0 * HD:(k0 + hk) * HD]),
+                     np.ascontiguousarray(vc[:, k0 * HD:(k0 + hk) * HD]))
+    gen = torch.Generator(device=dev).manual_seed(4)
+    q = torch.randn(NS5, L, Q_DIM, device=dev, generator=gen)[:, :, h0 * HD:(h0 + hq) * HD]
+    k = torch.randn(NS5, L, kv5, device=dev, generator=gen)[:, :, k0 * HD:(k0 + hk) * HD]
+    v = torch.randn(NS5, L, kv5, device=dev, generator=gen)[:, :, k0 * HD:(k0 + hk) * HD]
+    q, k, v = q.contiguous(), k.contiguous(), v.contiguous()
+    out = torch.empty(L, hq * HD, device=dev)
+    seq0 = torch.zeros(1, dtype=torch.int32, device=dev)
+    posd = (CTX5 + torch.arange(NS5, dtype=torch.int32, device=dev)).contiguous()
+
+    def step(s, sh):
+        for l in range(L):
+            at.decode_batch_dev(l, 1, seq0.data_ptr(), posd[s:s + 1].data_ptr(), CTX5 + NS5 - 1,
+                                q[s, l].data_ptr(), k[s, l].data_ptr(), v[s, l].data_ptr(),
+                                out[l].data_ptr(), sh)
+
+    step(0, stream.cuda_stream)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        sh_cap = torch.cuda.current_stream(dev).cuda_stream
+        for s in range(NS5):
+            step(s, sh_cap)
+    barrier(world)
+    graph.replay()
+    torch.cuda.synchronize()
+    barrier(world)
+    nbytes = sum(L * ((CTX5 + s + 1) * kv5 * 4 + Q_DIM * 8 + kv5 * 12) for s in range(NS5))
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    graph.replay()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ms = max_over_ranks(e0.elapsed_time(e1), world)
+    del graph
+    barrier(world)
+    at.close()
+    return {"metric": f"long-context decode-attn HBM GB/s (config 5, split by KV head over "
+                      f"{world} GPUs)",
+            "value": nbytes / (ms / 1e3) / 1e9, "unit": "GB/s",
+            "pct_peak_per_gpu": 100.0 * nbytes / (ms / 1e3) / 1e9 / world / peaks["hbm_gbs"],
+            "tok_per_s": NS5 / (ms / 1e3), "ms_per_step_16_layers": ms / NS5,
+            "timing": "one CUDA graph of all 32 steps, replayed", "scaling": "strong",
+            "collective": "none: each rank's output is its slice of heads",
+            "config": {"workload": "config5 16 layers, 32/8 heads, hd 64, theta 5e5, "
+                                   "32768 cached + 32 steps, KV N(0,1) seed 4",
+                       "shard": f"KV heads {k0}..{k0 + hk - 1} (query heads {h0}..{h0 + hq - 1}) "
+                                f"on rank {rank}"}}
+
+
 def run_decode1(local):
     """Config 1: one TinyLlama decode layer at position 255 (latency)."""
     import picolm_b200 as pb
@@ -759,6 +831,7 @@ def main():
     peaks = load_peaks()
     if args.workload == "long_ctx" and world > 1:
         r = run_long_ctx_split(args, rank, world, local, peaks)
+        r["by_kv_head"] = run_long_ctx_heads(args, rank, world, local, peaks)
         if rank == 0:
             print(json.dumps(r), flush=True)
         import torch.distributed as dist
@@ -780,6 +853,7 @@ def main():
                  "gpu_launches": res["gpu_launches"], "clocks": res["clocks"]})
     if world > 1 and args.workload == "all":
         line["long_ctx_split"] = run_long_ctx_split(args, rank, world, local, peaks)
+        line["long_ctx_heads"] = run_long_ctx_heads(args, rank, world, local, peaks)
     if world == 1 and args.workload == "all":
         line["prefill"] = run_prefill(args, local, peaks)
         line["long_ctx"] = run_long_ctx(args, local, peaks)

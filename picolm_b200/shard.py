@@ -19,6 +19,10 @@ is too long for one device's bandwidth, it is split along the sequence axis:
 The arithmetic of the merge is the log-sum-exp form of the online softmax
 of model.c:848-892 applied to whole shards instead of single rows.
 
+A long sequence can instead be split by KV head (`head_shard`): every rank
+holds all positions of its heads and runs the unchanged decode on them, and
+the per-head outputs need no merge.
+
 `KVSplitDecoder` holds the per-rank bookkeeping and is independent of the
 backend: `ops` supplies `partial(...)` and `combine(...)`; `AttnShardOps`
 and `P2PShardOps` are the CUDA implementations on top of the C ABI.
@@ -31,6 +35,22 @@ from dataclasses import dataclass
 # caller sizes `part` as n_heads * attn.part_stride floats (head_dim + 4 per
 # head, so 132 at head_dim 128) and `parts_all` as world times that.
 PART_STRIDE = 68
+
+
+def head_shard(n_heads: int, n_kv_heads: int, world: int, rank: int) -> tuple[int, int, int, int]:
+    """(head0, n_heads_r, kv_head0, n_kv_heads_r): the query and KV heads of
+    `rank` when attention is split by KV head instead of by position.
+
+    Each rank holds every position of n_kv_heads / world KV heads and runs
+    their kv_mul query heads (model.c:848's kv_h = h / kv_mul keeps them
+    together), so its output is a disjoint slice of heads and no merge is
+    needed.  The slices of q, k, v and out are contiguous: head h occupies
+    [h * head_dim, (h + 1) * head_dim) of its row."""
+    if world < 1 or not 0 <= rank < world or n_kv_heads % world or n_heads % n_kv_heads:
+        raise ValueError(f"cannot split {n_heads}/{n_kv_heads} heads over {world} ranks")
+    hk = n_kv_heads // world
+    hq = hk * (n_heads // n_kv_heads)
+    return rank * hq, hq, rank * hk, hk
 
 
 def shard_range(n_cached: int, world: int, rank: int) -> tuple[int, int]:

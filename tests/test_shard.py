@@ -173,3 +173,21 @@ def test_split_decode_equals_unsplit_attention(tmp_path, world):
     for i, (q, k, v) in enumerate(steps):
         want, _, _ = O.attn_decode(c, fk.ravel(), fv.ravel(), N_CACHED + i, q, k, v, *tables)
         np.testing.assert_allclose(got[i], want, atol=ATOL, rtol=RTOL)
+
+
+def test_head_shard_covers_heads_in_rank_order():
+    from picolm_b200.shard import head_shard
+    for H_, Hk_ in ((32, 8), (32, 4), (8, 8), (16, 2)):
+        for world in (1, 2, 4, 8):
+            if Hk_ % world:
+                with pytest.raises(ValueError):
+                    head_shard(H_, Hk_, world, 0)
+                continue
+            q_heads, kv_heads = [], []
+            for r in range(world):
+                h0, hq, k0, hk = head_shard(H_, Hk_, world, r)
+                assert hq == hk * (H_ // Hk_)
+                assert h0 == k0 * (H_ // Hk_)   # query heads stay with their KV head
+                q_heads.extend(range(h0, h0 + hq))
+                kv_heads.extend(range(k0, k0 + hk))
+            assert q_heads == list(range(H_)) and kv_heads == list(range(Hk_))
