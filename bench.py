@@ -154,6 +154,18 @@ def dist_setup():
     return rank, world, local
 
 
+def per_rank(x: float, world: int) -> list:
+    """x of every rank, in rank order (a list of one on a single GPU)."""
+    if world == 1:
+        return [x]
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    out = [torch.zeros_like(t) for _ in range(world)]
+    dist.all_gather(out, t)
+    return [float(v.item()) for v in out]
+
+
 def max_over_ranks(x: float, world: int) -> float:
     if world == 1:
         return x
@@ -246,11 +258,13 @@ def run_batched_decode(args, rank, world, local, peaks):
     at.profile(False)
     launches_per_step = n_all / n_prof
     t_local = sum(step_ms) / 1e3
-    t_max = max_over_ranks(t_local, world)
+    t_ranks = per_rank(t_local, world)
+    t_max = max(t_ranks)
     value = total_bytes * world / t_max / 1e9
     achieved = prof_bytes / (kern_ms / 1e3) / 1e9     # per launch bytes / launch time
     res = {
         "value": value, "ms_per_step": t_max * 1e3 / args.steps,
+        "rank_ms_per_step": [t * 1e3 / args.steps for t in t_ranks],
         "tok_per_s": SEQS_PER_GPU * world * args.steps / t_max,
         "pct_peak": 100.0 * value / world / peaks["hbm_gbs"],
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"],
@@ -850,7 +864,8 @@ def main():
     line.update({"impl": "ours", "value": res["value"], "ms_per_step": res["ms_per_step"],
                  "tok_per_s": res["tok_per_s"], "pct_peak": res["pct_peak"],
                  "roofline": res["roofline"], "e2e": res["e2e"],
-                 "gpu_launches": res["gpu_launches"], "clocks": res["clocks"]})
+                 "gpu_launches": res["gpu_launches"], "clocks": res["clocks"],
+                 "rank_ms_per_step": res["rank_ms_per_step"]})
     if world > 1 and args.workload == "all":
         line["long_ctx_split"] = run_long_ctx_split(args, rank, world, local, peaks)
         line["long_ctx_heads"] = run_long_ctx_heads(args, rank, world, local, peaks)
