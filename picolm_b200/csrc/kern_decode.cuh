@@ -31,6 +31,12 @@
 // issue rate, so a CUDA-core dot product would cap the kernel below the HBM
 // roofline.  On the tensor pipe the same work costs a few percent.
 //
+// head_dim is the template parameter HD (64 or 128).  A tile row of 128
+// elements is staged as two 64-element halves, each its own region under
+// the 128-byte swizzle and its own TMA box; tiles stay at 16 KB (TP rows x
+// all KV heads), with a 3-deep ring where the 16-row minimum makes them
+// larger (128 x 8 KV heads).
+//
 // The row at `pos` is appended by the segment that contains it: the warp of
 // each KV head rotates k (bit-exact picolm RoPE), encodes k and v with
 // picolm's FP16 rounding, stores them to HBM and patches them into the
