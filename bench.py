@@ -775,6 +775,127 @@ def run_long_ctx_heads(args, rank, world, local, peaks):
                                 f"on rank {rank}"}}
 
 
+def random_q4k(rng, rows: int, n: int) -> np.ndarray:
+    """Raw GGUF Q4_K rows (picolm/quant.h:65-72) with dequantised weights of
+    standard deviation about 0.02: random quants and 6-bit scales, FP16 d
+    and dmin."""
+    nb = rows * n // 256
+    blk = rng.integers(0, 256, (nb, 144), dtype=np.uint8)
+    d = (rng.uniform(0.5, 1.5, nb) * 0.02 / 180).astype(np.float16).view(np.uint8)
+    dmin = (rng.uniform(0.5, 1.5, nb) * 0.02 / 60).astype(np.float16).view(np.uint8)
+    blk[:, 0:2] = d.reshape(-1, 2)
+    blk[:, 2:4] = dmin.reshape(-1, 2)
+    return blk.reshape(rows, -1)
+
+
+def run_block(args, local, peaks):
+    """The whole attention sub-block with its projections (RMSNorm, Q/K/V,
+    RoPE, append, attention, output projection, residual) on TinyLlama
+    shapes with Q4_K weights (config 2's weight type), one layer:
+      * batched decode, 64 sequences x 2048 cached rows (the headline's
+        context), L2 flushed before each step, against the attention-only
+        step on the same cache;
+      * one sequence x 2048 cached rows (a single-stream decode step);
+      * causal prefill of 2048 positions, against the attention-only prefill.
+    The projections' time is the block's minus the attention's."""
+    import torch
+    import picolm_b200 as pb
+    DIM = 2048
+    dev = torch.device("cuda", local)
+    sh = torch.cuda.current_stream(dev).cuda_stream
+    rng = np.random.default_rng(8)
+    gen = torch.Generator(device=dev).manual_seed(8)
+    w = [random_q4k(rng, Q_DIM, DIM), random_q4k(rng, KV_DIM, DIM), random_q4k(rng, KV_DIM, DIM),
+         random_q4k(rng, DIM, Q_DIM)]
+    w_bytes = sum(x.nbytes for x in w)
+    norm = (1.0 + 0.1 * rng.standard_normal(DIM)).astype(np.float32)
+    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
+    flush_rd = torch.ones(L2_FLUSH_BYTES // 4, dtype=torch.int32, device=dev)
+    res = {"config": {"workload": "attention sub-block with projections, TinyLlama shapes "
+                                  "(dim 2048, 32/4 heads), Q4_K weights, one layer",
+                      "weights_bytes": w_bytes, "data": "synthetic, seed 8"}}
+
+    def timed(fn, reps, flush_l2):
+        for _ in range(3):
+            fn()
+        torch.cuda.synchronize()
+        tot = 0.0
+        for _ in range(reps):
+            if flush_l2:
+                flush.zero_(); flush_rd.sum()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(); fn(); e1.record()
+            torch.cuda.synchronize()
+            tot += e0.elapsed_time(e1)
+        return tot / reps
+
+    for n_seq, key in ((SEQS_PER_GPU, "decode_batch64"), (1, "decode_single")):
+        at = pb.Attn(1, H, HK, CTX + 8, n_seqs=n_seq, device=local)
+        at.set_layer(0, DIM, w[0], pb.PL_GGUF_Q4_K, w[1], pb.PL_GGUF_Q4_K, w[2], pb.PL_GGUF_Q4_K,
+                     w[3], pb.PL_GGUF_Q4_K, attn_norm=norm, eps=1e-5)
+        for s_ in range(n_seq):
+            at.kv_upload(s_, 0, 0, make_cache_host(rng, CTX, KV_DIM),
+                         make_cache_host(rng, CTX, KV_DIM))
+        x = torch.randn(n_seq, DIM, device=dev, generator=gen)
+        q = torch.randn(n_seq, Q_DIM, device=dev, generator=gen)
+        k = torch.randn(n_seq, KV_DIM, device=dev, generator=gen)
+        v = torch.randn(n_seq, KV_DIM, device=dev, generator=gen)
+        out = torch.empty(n_seq, Q_DIM, device=dev)
+        seqs = torch.arange(n_seq, dtype=torch.int32, device=dev)
+        pos = torch.full((n_seq,), CTX, dtype=torch.int32, device=dev)
+        blk = lambda: at.block_decode_dev(0, n_seq, seqs.data_ptr(), pos.data_ptr(), CTX,
+                                          x.data_ptr(), sh)
+        att = lambda: at.decode_batch_dev(0, n_seq, seqs.data_ptr(), pos.data_ptr(), CTX,
+                                          q.data_ptr(), k.data_ptr(), v.data_ptr(),
+                                          out.data_ptr(), sh)
+        reps = 20 if n_seq > 1 else 200
+        ms_blk = timed(blk, reps, flush_l2=True)
+        ms_att = timed(att, reps, flush_l2=True)
+        # host-buffer call as model.c makes it (registered residual stream)
+        xh = np.ascontiguousarray(x.cpu().numpy())
+        at.host_register(xh)
+        sq, ps = np.arange(n_seq, dtype=np.int32), np.full(n_seq, CTX, np.int32)
+        for _ in range(5):
+            at.lib.pl_attn_block_decode(0, n_seq, sq, ps, xh.ravel())
+        t0 = time.perf_counter()
+        for _ in range(reps):
+            at.lib.pl_attn_block_decode(0, n_seq, sq, ps, xh.ravel())
+        host_ms = (time.perf_counter() - t0) / reps * 1e3
+        at.host_unregister(xh)
+        at.close()
+        kv_b = n_seq * ((CTX + 1) * KV_DIM * 4)
+        proj_ms = ms_blk - ms_att
+        flops = 2.0 * n_seq * (Q_DIM * DIM + 2 * KV_DIM * DIM + DIM * Q_DIM)
+        res[key] = {"sequences": n_seq, "cached_rows": CTX, "ms_block": ms_blk,
+                    "ms_attention_only": ms_att, "ms_projections": proj_ms,
+                    "projection_weight_gbs": w_bytes / (proj_ms / 1e3) / 1e9,
+                    "projection_tflops_fp32": flops / (proj_ms / 1e3) / 1e12,
+                    "block_gbs": (kv_b + w_bytes) / (ms_blk / 1e3) / 1e9,
+                    "host_call_ms": host_ms,
+                    "timing": "CUDA events per step, L2 flushed before each; host call "
+                              "wall clock, synchronous"}
+    # ---- prefill of 2048 positions
+    S = 2048
+    at = pb.Attn(1, H, HK, S, device=local)
+    at.set_layer(0, DIM, w[0], pb.PL_GGUF_Q4_K, w[1], pb.PL_GGUF_Q4_K, w[2], pb.PL_GGUF_Q4_K,
+                 w[3], pb.PL_GGUF_Q4_K, attn_norm=norm, eps=1e-5)
+    xp = torch.randn(S, DIM, device=dev, generator=gen)
+    qp = torch.randn(S, Q_DIM, device=dev, generator=gen)
+    kp = torch.randn(S, KV_DIM, device=dev, generator=gen)
+    vp = torch.randn(S, KV_DIM, device=dev, generator=gen)
+    op = torch.empty(S, Q_DIM, device=dev)
+    ms_blk = timed(lambda: at.block_prefill_dev(0, 0, 0, S, xp.data_ptr(), sh), 5, False)
+    ms_att = timed(lambda: at.prefill_dev(0, 0, 0, S, qp.data_ptr(), kp.data_ptr(),
+                                          vp.data_ptr(), op.data_ptr(), None, sh), 5, False)
+    at.close()
+    flops = 2.0 * S * (Q_DIM * DIM + 2 * KV_DIM * DIM + DIM * Q_DIM)
+    res["prefill_2048"] = {"ms_block": ms_blk, "ms_attention_only": ms_att,
+                           "ms_projections": ms_blk - ms_att,
+                           "projection_tflops_fp32": flops / ((ms_blk - ms_att) / 1e3) / 1e12}
+    del flush, flush_rd
+    return res
+
+
 def run_decode1(local):
     """Config 1: one TinyLlama decode layer at position 255 (latency)."""
     import picolm_b200 as pb
@@ -804,10 +925,10 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", choices=["all", "decode", "prefill", "long_ctx", "decode1",
-                                           "hd128"],
+                                           "hd128", "block"],
                     default="all",
                     help="all: headline + configs 1/3/5 + CPU baseline; decode: headline only; "
-                         "prefill / long_ctx / decode1 / hd128: that workload alone")
+                         "prefill / long_ctx / decode1 / hd128 / block: that workload alone")
     args = ap.parse_args()
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -856,7 +977,8 @@ def main():
             fn = {"prefill": lambda: run_prefill(args, local, peaks),
                   "long_ctx": lambda: run_long_ctx(args, local, peaks),
                   "decode1": lambda: run_decode1(local),
-                  "hd128": lambda: run_hd128(args, local, peaks)}[args.workload]
+                  "hd128": lambda: run_hd128(args, local, peaks),
+                  "block": lambda: run_block(args, local, peaks)}[args.workload]
             print(json.dumps(fn()), flush=True)
         return
     res = run_batched_decode(args, rank, world, local, peaks)
@@ -874,6 +996,7 @@ def main():
         line["long_ctx"] = run_long_ctx(args, local, peaks)
         line["decode1"] = run_decode1(local)
         line["hd128"] = run_hd128(args, local, peaks)
+        line["block"] = run_block(args, local, peaks)
         cb = cpu_decode_sample(max_seconds=15.0)
         line["cpu_baseline"] = {k: cb[k] for k in ("value", "unit", "cores", "kind", "sample")}
     if rank == 0:

@@ -229,6 +229,67 @@ int  pl_attn_decode_batch_dev_noalloc(int layer, int n, const int *d_seqs,
                                       const float *d_v, float *d_out,
                                       void *stream);
 
+/* ---- The whole attention sub-block, projections included ----
+ *
+ * The calls above take q, k, v already projected.  These take the residual
+ * stream instead and run, per layer, everything model.c does between the
+ * two residual adds on the device: RMSNorm (attn_norm), the Q, K, V
+ * projections and their biases, QK-norm, RoPE, the FP16 KV append,
+ * attention, the output projection, its bias and the residual add.  The
+ * weights stay on the device in their GGUF quantisation. */
+
+/* GGUF tensor types the projections take (picolm/quant.h:49-63) */
+#define PL_GGUF_F32   0
+#define PL_GGUF_F16   1
+#define PL_GGUF_Q8_0  8
+#define PL_GGUF_Q4_K 12
+#define PL_GGUF_Q6_K 14
+
+/* Upload one layer's attention weights, the tensors model.c:779-817 and
+ * 894-897 read (layer_weights_t, model.h:39-72): wq [n_heads*head_dim rows]
+ * x [dim], wk and wv [n_kv_heads*head_dim] x [dim], wo [dim] x
+ * [n_heads*head_dim], each as raw GGUF rows of type type_* (F32, F16, Q8_0,
+ * Q4_K or Q6_K; a row length must be a multiple of the type's block,
+ * PL_EUNSUPPORTED otherwise).  attn_norm [dim] and rms_eps are the RMSNorm
+ * applied to x first (s->attn_norm_w[l], c->rms_norm_eps; NULL: none).
+ * Biases bq, bk, bv, bo are F32 (s->attn_q_bias[l] ...; NULL: none).
+ * q_norm and k_norm [head_dim] are the QK-norm weights (Qwen3,
+ * s->attn_q_norm_w[l]; both NULL or both set).  The data are copied; a
+ * second call for the same layer replaces the first. */
+int  pl_attn_set_layer(int layer, int dim, const float *attn_norm,
+                       float rms_eps, const void *wq, int type_q,
+                       const void *wk, int type_k, const void *wv,
+                       int type_v, const void *wo, int type_o,
+                       const float *bq, const float *bk, const float *bv,
+                       const float *bo, const float *q_norm,
+                       const float *k_norm);
+
+/* Decode: replaces model.c:779-897 for n sequences, sequence slot seqs[i]
+ * at position pos[i] (distinct slots).  x [n][dim] is the residual stream
+ * (model.c's s->x), updated in place: x += attention sub-block(x).  The K
+ * and V rows appended to the cache are picolm's FP16 encoding of k and v
+ * as this module computes them; the projections sum in a different order
+ * than the CPU, so they agree with picolm's to FP32 rounding. */
+int  pl_attn_block_decode(int layer, int n, const int *seqs, const int *pos,
+                          float *x);
+
+/* Prefill: replaces model.c:990-1100 (RMSNorm through the residual add) for
+ * n_tok positions start_pos.. of one sequence; x [n_tok][dim] in place. */
+int  pl_attn_block_prefill(int seq, int layer, int start_pos, int n_tok,
+                           float *x);
+
+/* The same with x in device memory (16-byte aligned), on `stream`. */
+int  pl_attn_block_decode_dev(int layer, int n, const int *d_seqs,
+                              const int *d_pos, int max_pos, float *d_x,
+                              void *stream);
+int  pl_attn_block_prefill_dev(int seq, int layer, int start_pos, int n_tok,
+                               float *d_x, void *stream);
+
+/* One uploaded projection alone, matmul_bias (tensor.c:230-238) on n input
+ * rows: y[i] = W x[i] + b for which = 0 (Wq), 1 (Wk), 2 (Wv), 3 (Wo); x
+ * [n][dim] (Wo: [n][n_heads*head_dim]), y [n][rows of W].  No RMSNorm. */
+int  pl_attn_proj(int layer, int which, int n, const float *x, float *y);
+
 /* ---- Profiling (cf. picolm's timing stats, picolm.c:285-302) ---- */
 
 /* Enable (1) or disable (0) device timing: every later call records CUDA

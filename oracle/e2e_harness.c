@@ -7,8 +7,11 @@
  * sampler_sample does at temperature 0 (sampler.c:43-51).  The same source
  * is linked twice: with picolm's unmodified model.c (the CPU reference), and
  * with the copy of model.c whose attention blocks call the B200 module
- * (built with -DUSE_PL_ATTN).  Each generated token is printed with the
- * margin between the best and the second-best logit.
+ * (built with -DUSE_PL_ATTN), and with the copy whose whole attention
+ * sub-blocks, projections included, call it (-DUSE_PL_BLOCK as well; the
+ * layers' attention weights are uploaded once after model_load).  Each
+ * generated token is printed with the margin between the best and the
+ * second-best logit.
  *
  * usage: e2e MODEL.gguf N_PROMPT N_GEN SEED THREADS [--save F] [--load F]
  *   --load F  kvcache_load(F) first (model.c:1199-1259) and skip the cached
@@ -80,6 +83,25 @@ int main(int argc, char **argv) {
     if (rc == PL_OK)
         rc = pl_attn_host_register(model.state.mem_block,
                                    model.state.mem_size - model.state.kv_size);
+#ifdef USE_PL_BLOCK
+    /* each layer's attention weights (model.h:39-72) in their GGUF types,
+     * with the F32 norm weights and biases picolm prepared at load
+     * (model.c:640-712) */
+    for (int l = 0; l < c->n_layers && rc == PL_OK; l++) {
+        const layer_weights_t *lw = &model.weights.layers[l];
+        const run_state_t *s = &model.state;
+        rc = pl_attn_set_layer(l, c->n_embd, s->attn_norm_w[l], c->rms_norm_eps,
+                               lw->attn_q, lw->type_attn_q, lw->attn_k, lw->type_attn_k,
+                               lw->attn_v, lw->type_attn_v, lw->attn_output,
+                               lw->type_attn_output,
+                               lw->attn_q_b ? s->attn_q_bias[l] : NULL,
+                               lw->attn_k_b ? s->attn_k_bias[l] : NULL,
+                               lw->attn_v_b ? s->attn_v_bias[l] : NULL,
+                               lw->attn_output_b ? s->attn_output_bias[l] : NULL,
+                               lw->attn_q_norm ? s->attn_q_norm_w[l] : NULL,
+                               lw->attn_q_norm ? s->attn_k_norm_w[l] : NULL);
+    }
+#endif
     if (rc != PL_OK) {
         fprintf(stderr, "pl_attn: %s\n", pl_attn_strerror(rc));
         return 1;

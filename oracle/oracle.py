@@ -69,6 +69,12 @@ def port() -> C.CDLL:
                                              _i32p, _f32p, _f32p, _f32p, _f32p,
                                              _f32p, _f32p, C.c_int]
         lib.orc_matvec.argtypes = [_f32p, _f32p, _f32p, C.c_int, C.c_int]
+        lib.orc_vec_dot.restype = C.c_float
+        lib.orc_vec_dot.argtypes = [C.c_void_p, _f32p, C.c_int, C.c_int]
+        lib.orc_row_bytes.restype = C.c_long
+        lib.orc_row_bytes.argtypes = [C.c_int, C.c_int]
+        lib.orc_matmul.argtypes = [_f32p, _f32p, C.c_void_p, C.c_int, C.c_int, C.c_int]
+        lib.orc_rmsnorm.argtypes = [_f32p, _f32p, _f32p, C.c_int, C.c_float]
         _port = lib
     return _port
 
@@ -102,6 +108,10 @@ def ref() -> C.CDLL:
         lib.ref_attn_decode_seqs.argtypes = [C.c_int, C.c_int, C.c_int, C.c_int, _u16p,
                                              _u16p, C.c_long, _i32p, _f32p, _f32p,
                                              _f32p, _f32p, _f32p, _f32p, C.c_int]
+        lib.matmul.argtypes = [_f32p, _f32p, C.c_void_p, C.c_int, C.c_int, C.c_int]
+        lib.vec_dot.restype = C.c_float
+        lib.vec_dot.argtypes = [C.c_void_p, _f32p, C.c_int, C.c_int]
+        lib.rmsnorm.argtypes = [_f32p, _f32p, _f32p, C.c_int, C.c_float]
         _ref = lib
     return _ref
 
@@ -173,3 +183,29 @@ def attn_decode_seqs(c: OrcCfg, kc, vc, seq_stride, pos, q, k, v, cos_t, sin_t,
         port().orc_attn_decode_seqs(C.byref(c), n_seq, kc, vc, int(seq_stride), pos, q,
                                     k, v, cos_t, sin_t, out, int(n_threads))
     return out
+
+
+# ------------------------------------------------- projections (GGUF GEMV)
+def matmul(W: np.ndarray, x, n: int, d: int, gtype: int, use_ref: bool = False) -> np.ndarray:
+    """out[d] = W x for raw GGUF rows W (bytes) of type gtype, as picolm's
+    matmul; the restatement, or the genuine reference with use_ref."""
+    W = np.ascontiguousarray(W)
+    x = np.ascontiguousarray(x, np.float32).ravel()
+    out = np.empty(d, np.float32)
+    if use_ref:
+        ref().matmul(out, x, W.ctypes.data, n, d, gtype)
+    else:
+        port().orc_matmul(out, x, W.ctypes.data, n, d, gtype)
+    return out
+
+
+def rmsnorm(x, w, eps: float, use_ref: bool = False) -> np.ndarray:
+    x = np.ascontiguousarray(x, np.float32).ravel()
+    w = np.ascontiguousarray(w, np.float32).ravel()
+    out = np.empty_like(x)
+    (ref().rmsnorm if use_ref else port().orc_rmsnorm)(out, x, w, x.size, float(eps))
+    return out
+
+
+def row_bytes(gtype: int, n: int) -> int:
+    return int(port().orc_row_bytes(gtype, n))

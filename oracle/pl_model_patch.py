@@ -23,7 +23,18 @@ A failing call prints pl_attn_strerror and exits: there is no CPU fallback.
 The copy is written to a temporary directory by the oracle Makefile and
 deleted after compiling.
 
-usage: python pl_model_patch.py REF/model.c OUT/model_pl.c
+With --block the whole attention sub-block goes to the device instead,
+projections included (the harness uploads each layer's weights with
+pl_attn_set_layer):
+
+* decode (model.c:779-897): from `rmsnorm(s->xb, s->x, s->attn_norm_w[l], ...)`
+  through the residual `vec_add(s->x, s->xb2, dim)`
+  -> pl_attn_block_decode(l, 1, &seq, &pos, s->x);
+* prefill (model.c:990-1100): from `/* a. Batch RMSNorm */` up to
+  `/* h. Batch FFN RMSNorm */`
+  -> pl_attn_block_prefill(0, l, start_pos, n_tokens, x_batch).
+
+usage: python pl_model_patch.py [--block] REF/model.c OUT/model_pl.c
 """
 import sys
 
@@ -92,6 +103,34 @@ KV_LOAD_SYNC = """\
 """
 
 
+BLOCK_DECODE_CALL = """\
+        /* the attention sub-block on the B200: RMSNorm, Q/K/V projections,
+         * QK-norm, RoPE, FP16 KV append, attention, output projection and
+         * the residual add, s->x updated in place */
+        {
+            int pl_seq = 0;
+            int pl_rc = pl_attn_block_decode(l, 1, &pl_seq, &pos, s->x);
+            if (pl_rc != PL_OK) {
+                fprintf(stderr, "pl_attn_block_decode: %s\\n", pl_attn_strerror(pl_rc));
+                exit(1);
+            }
+        }
+"""
+
+BLOCK_PREFILL_CALL = """\
+        /* a.-g. the attention sub-block of every position on the B200,
+         *       x_batch updated in place */
+        {
+            int pl_rc = pl_attn_block_prefill(0, l, start_pos, n_tokens, x_batch);
+            if (pl_rc != PL_OK) {
+                fprintf(stderr, "pl_attn_block_prefill: %s\\n", pl_attn_strerror(pl_rc));
+                exit(1);
+            }
+        }
+
+"""
+
+
 def find(lines, pred, start=0):
     for i in range(start, len(lines)):
         if pred(lines[i]):
@@ -100,7 +139,9 @@ def find(lines, pred, start=0):
 
 
 def main():
-    src, dst = sys.argv[1], sys.argv[2]
+    args = sys.argv[1:]
+    block = "--block" in args
+    src, dst = [a for a in args if a != "--block"]
     lines = open(src).read().split("\n")
 
     ds = find(lines, lambda s: "rope(s->q, k_tmp," in s)
@@ -126,8 +167,24 @@ def main():
         if must not in "\n".join(blk):
             raise SystemExit("pl_model_patch: kvcache block does not read the host cache")
     inc = find(lines, lambda s: s.strip() == '#include "model.h"')
+    if block:
+        # widen both blocks to the whole attention sub-block
+        ds = find(lines, lambda s: s.strip().startswith(
+            "rmsnorm(s->xb, s->x, s->attn_norm_w[l]"), inc)
+        de = find(lines, lambda s: s.strip() == "vec_add(s->x, s->xb2, dim);", ds) + 1
+        ps = find(lines, lambda s: s.strip().startswith("/* a. Batch RMSNorm"), de)
+        pe = find(lines, lambda s: s.strip().startswith("/* h. Batch FFN RMSNorm"), ps)
+        for must, blk in (("matmul_dual(k_tmp, v_tmp", lines[ds:de]),
+                          ("lw->attn_output", lines[ds:de]),
+                          ("matmul_dual_batch(k_batch", lines[ps:pe]),
+                          ("xbi[d] += xoi[d]", lines[ps:pe])):
+            if must not in "\n".join(blk):
+                raise SystemExit(f"pl_model_patch: block does not contain {must!r}")
+        dec, pre = BLOCK_DECODE_CALL, BLOCK_PREFILL_CALL
+    else:
+        dec, pre = DECODE_CALL, PREFILL_CALL
     out = (lines[:inc + 1] + ['#include "pl_attn.h"'] + lines[inc + 1:ds]
-           + DECODE_CALL.split("\n") + lines[de:ps] + PREFILL_CALL.split("\n")
+           + dec.split("\n") + lines[de:ps] + pre.split("\n")
            + lines[pe:sc + 1] + KV_SAVE_SYNC.split("\n") + lines[sc + 1:lm - 1]
            + KV_LOAD_SYNC.split("\n") + lines[lm - 1:])
     with open(dst, "w") as f:

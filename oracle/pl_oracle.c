@@ -253,3 +253,174 @@ void orc_matvec(const float *W, const float *x, float *out, int n, int d) {
         out[i] = s;
     }
 }
+
+/* ==================================================================
+ * The projections on either side of the attention path (model.c:779-817,
+ * 894-897): vec_dot per GGUF type, matmul, rmsnorm.  The summation orders
+ * are those of the reference as compiled for plain x86-64: the scalar
+ * branches of the quantised dots (quant.c:496-505, 583-617, 695-709) and
+ * the SSE2 branch of the F32 dot (quant.c:366-377).
+ * ================================================================== */
+
+static float orc_sse2_dot(const float *w, const float *x, int n) {
+    /* quant.c:366-377: two 4-wide accumulators over steps of 8, the
+     * horizontal sum of their sum (hsum_sse, quant.h:23-29), then the tail */
+    float a0[4] = {0, 0, 0, 0}, a1[4] = {0, 0, 0, 0};
+    int i = 0;
+    for (; i + 7 < n; i += 8)
+        for (int l = 0; l < 4; ++l) {
+            a0[l] = a0[l] + w[i + l] * x[i + l];
+            a1[l] = a1[l] + w[i + 4 + l] * x[i + 4 + l];
+        }
+    float v[4];
+    for (int l = 0; l < 4; ++l) v[l] = a0[l] + a1[l];
+    float sum = (v[0] + v[2]) + (v[1] + v[3]);
+    for (; i < n; i++) sum += w[i] * x[i];
+    return sum;
+}
+
+static void orc_scale_min_k4(int j, const uint8_t *q, uint8_t *sc, uint8_t *mn) {
+    /* quant.c:82-90 */
+    if (j < 4) {
+        *sc = q[j] & 63;
+        *mn = q[j + 4] & 63;
+    } else {
+        *sc = (uint8_t)((q[j + 4] & 0xF) | ((q[j - 4] >> 6) << 4));
+        *mn = (uint8_t)((q[j + 4] >> 4) | ((q[j] >> 6) << 4));
+    }
+}
+
+static float orc_dot_q4_K(const uint8_t *src, const float *x, int n) {
+    /* quant.c:390-512, scalar branch; block {d, dmin, scales[12], qs[128]} */
+    float sumf = 0.0f;
+    for (int i = 0; i < n / 256; i++) {
+        const uint8_t *b = src + (size_t)i * 144;
+        uint16_t dh, mh;
+        memcpy(&dh, b, 2);
+        memcpy(&mh, b + 2, 2);
+        const float d = orc_fp16_to_fp32(dh), dmin = orc_fp16_to_fp32(mh);
+        const uint8_t *scales = b + 4, *q = b + 16;
+        const float *xp = x + i * 256;
+        for (int j = 0, is = 0; j < 4; j++, is += 2, xp += 64, q += 32) {
+            uint8_t sc, mn;
+            orc_scale_min_k4(is, scales, &sc, &mn);
+            const float d1 = d * (float)sc, m1 = dmin * (float)mn;
+            orc_scale_min_k4(is + 1, scales, &sc, &mn);
+            const float d2 = d * (float)sc, m2 = dmin * (float)mn;
+            float sum_qx1 = 0.0f, sum_x1 = 0.0f, sum_qx2 = 0.0f, sum_x2 = 0.0f;
+            for (int l = 0; l < 32; l++) {
+                sum_qx1 += (float)(q[l] & 0xF) * xp[l];
+                sum_x1 += xp[l];
+                sum_qx2 += (float)(q[l] >> 4) * xp[l + 32];
+                sum_x2 += xp[l + 32];
+            }
+            sumf += d1 * sum_qx1 - m1 * sum_x1 + d2 * sum_qx2 - m2 * sum_x2;
+        }
+    }
+    return sumf;
+}
+
+static float orc_dot_q6_K(const uint8_t *src, const float *x, int n) {
+    /* quant.c:517-625, scalar branch; block {ql[128], qh[64], scales[16], d} */
+    float sumf = 0.0f;
+    for (int i = 0; i < n / 256; i++) {
+        const uint8_t *b = src + (size_t)i * 210;
+        const uint8_t *ql = b, *qh = b + 128;
+        const int8_t *sc = (const int8_t *)(b + 192);
+        uint16_t dh;
+        memcpy(&dh, b + 208, 2);
+        const float d = orc_fp16_to_fp32(dh);
+        const float *xp = x + i * 256;
+        float sums[16] = {0};
+        for (int chunk = 0; chunk < 2; chunk++) {
+            const int is = chunk * 8;
+            const uint8_t *qlc = ql + chunk * 64, *qhc = qh + chunk * 32;
+            const float *xc = xp + chunk * 128;
+            for (int half = 0; half < 2; half++)
+                for (int l = half * 16; l < half * 16 + 16; l++) {
+                    const int q1 = (int)((qlc[l] & 0xF) | (((qhc[l] >> 0) & 3) << 4)) - 32;
+                    const int q2 = (int)((qlc[l + 32] & 0xF) | (((qhc[l] >> 2) & 3) << 4)) - 32;
+                    const int q3 = (int)((qlc[l] >> 4) | (((qhc[l] >> 4) & 3) << 4)) - 32;
+                    const int q4 = (int)((qlc[l + 32] >> 4) | (((qhc[l] >> 6) & 3) << 4)) - 32;
+                    sums[is + half + 0] += (float)q1 * xc[l];
+                    sums[is + half + 2] += (float)q2 * xc[l + 32];
+                    sums[is + half + 4] += (float)q3 * xc[l + 64];
+                    sums[is + half + 6] += (float)q4 * xc[l + 96];
+                }
+        }
+        for (int j = 0; j < 16; j++) sumf += d * (float)sc[j] * sums[j];
+    }
+    return sumf;
+}
+
+static float orc_dot_q8_0(const uint8_t *src, const float *x, int n) {
+    /* quant.c:627-711, scalar branch; block {d, qs[32]} */
+    float sumf = 0.0f;
+    for (int i = 0; i < n / 32; i++) {
+        const uint8_t *b = src + (size_t)i * 34;
+        uint16_t dh;
+        memcpy(&dh, b, 2);
+        const float d = orc_fp16_to_fp32(dh);
+        const int8_t *qs = (const int8_t *)(b + 2);
+        float sum = 0.0f;
+        for (int j = 0; j + 1 < 32; j += 2)
+            sum += (float)qs[j] * x[j] + (float)qs[j + 1] * x[j + 1];
+        sumf += d * sum;
+        x += 32;
+    }
+    return sumf;
+}
+
+float orc_vec_dot(const void *src, const float *x, int n, int type) {
+    /* quant.c:713-730 */
+    switch (type) {
+        case 12: return orc_dot_q4_K((const uint8_t *)src, x, n);
+        case 14: return orc_dot_q6_K((const uint8_t *)src, x, n);
+        case 8: return orc_dot_q8_0((const uint8_t *)src, x, n);
+        case 0: return orc_sse2_dot((const float *)src, x, n);
+        case 1: {
+            /* default branch: dequantize_row_f16 (quant.c:254-259), then the
+             * F32 dot */
+            float *buf = (float *)malloc((size_t)n * sizeof(float));
+            const uint16_t *h = (const uint16_t *)src;
+            for (int i = 0; i < n; i++) buf[i] = orc_fp16_to_fp32(h[i]);
+            const float s = orc_sse2_dot(buf, x, n);
+            free(buf);
+            return s;
+        }
+        default: return NAN;
+    }
+}
+
+long orc_row_bytes(int type, int n) {
+    /* gguf_type_row_size (quant.c:322-330) for the types above */
+    switch (type) {
+        case 0: return (long)n * 4;
+        case 1: return (long)n * 2;
+        case 8: return (long)(n / 32) * 34;
+        case 12: return (long)(n / 256) * 144;
+        case 14: return (long)(n / 256) * 210;
+        default: return -1;
+    }
+}
+
+void orc_matmul(float *out, const float *x, const void *W, int n, int d, int type) {
+    /* tensor.c:202-227: one vec_dot per output row (the thread split does
+     * not change any row's arithmetic) */
+    const long rb = orc_row_bytes(type, n);
+    for (int i = 0; i < d; i++)
+        out[i] = orc_vec_dot((const uint8_t *)W + (size_t)i * (size_t)rb, x, n, type);
+}
+
+void orc_rmsnorm(float *out, const float *x, const float *weight, int size, float eps) {
+    /* tensor.c:425-490, SSE2 branch (4-wide sum of squares, hsum_sse, tail);
+     * the scale is applied as (x * ss) * w */
+    float a[4] = {0, 0, 0, 0};
+    int i = 0;
+    for (; i + 3 < size; i += 4)
+        for (int l = 0; l < 4; ++l) a[l] = a[l] + x[i + l] * x[i + l];
+    float ss = (a[0] + a[2]) + (a[1] + a[3]);
+    for (; i < size; i++) ss += x[i] * x[i];
+    ss = 1.0f / sqrtf(ss / (float)size + eps);
+    for (i = 0; i < size; i++) out[i] = x[i] * ss * weight[i];
+}

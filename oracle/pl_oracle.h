@@ -87,6 +87,16 @@ void orc_attn_decode_seqs(const orc_cfg *c, int n_seq, uint16_t *kc,
 /* out[d] = sum_i W[d][i] * x[i], plain sequential FP32 (input generation). */
 void orc_matvec(const float *W, const float *x, float *out, int n, int d);
 
+/* The projections around the attention path.  vec_dot (quant.c:713-730) for
+ * GGUF types F32 (0), F16 (1), Q8_0 (8), Q4_K (12), Q6_K (14) in the
+ * reference's plain x86-64 summation order; matmul (tensor.c:202-227) over
+ * d rows of raw GGUF bytes; rmsnorm (tensor.c:425-490).  orc_row_bytes is
+ * gguf_type_row_size for those types (-1 otherwise). */
+float orc_vec_dot(const void *src, const float *x, int n, int type);
+long  orc_row_bytes(int type, int n);
+void  orc_matmul(float *out, const float *x, const void *W, int n, int d, int type);
+void  orc_rmsnorm(float *out, const float *x, const float *weight, int size, float eps);
+
 #ifdef __cplusplus
 }
 #endif

@@ -34,6 +34,12 @@ PL_EDEVICE = -7
 PL_EUNSUPPORTED = -8
 PL_ROPE_LLAMA = 0
 PL_ROPE_QWEN = 1
+# GGUF tensor types the projections take (picolm/quant.h:49-63)
+PL_GGUF_F32 = 0
+PL_GGUF_F16 = 1
+PL_GGUF_Q8_0 = 8
+PL_GGUF_Q4_K = 12
+PL_GGUF_Q6_K = 14
 HEAD_DIM = 64                # default head_dim; 64 and 128 are supported
 PART_STRIDE = HEAD_DIM + 4   # floats per partial at head_dim 64: m, l, 2 pad, o[64]
 
@@ -96,6 +102,13 @@ def load(path: str = LIB_PATH) -> C.CDLL:
         "pl_attn_xfer_connect": (i, [_vp]),
         "pl_attn_combine_p2p_dev": (i, [_vp, _vp, _vp]),
         "pl_attn_decode_batch_dev_noalloc": (i, [i, i, _vp, _vp, i, _vp, _vp, _vp, _vp, _vp]),
+        "pl_attn_set_layer": (i, [i, i, _vp, C.c_float, _vp, i, _vp, i, _vp, i, _vp, i,
+                                  _vp, _vp, _vp, _vp, _vp, _vp]),
+        "pl_attn_block_decode": (i, [i, i, _i32p, _i32p, _f32p]),
+        "pl_attn_block_prefill": (i, [i, i, i, i, _f32p]),
+        "pl_attn_block_decode_dev": (i, [i, i, _vp, _vp, i, _vp, _vp]),
+        "pl_attn_block_prefill_dev": (i, [i, i, i, i, _vp, _vp]),
+        "pl_attn_proj": (i, [i, i, i, _f32p, _f32p]),
         "pl_attn_profile": (i, [i]),
         "pl_attn_profile_read": (i, [C.POINTER(C.c_double), C.POINTER(C.c_long),
                                      C.POINTER(C.c_long)]),
@@ -228,6 +241,56 @@ class Attn:
         n_pos = k.size // self.kv_dim
         _check(self.lib.pl_kv_upload(seq, layer, pos0, n_pos, _ptr(k), _ptr(v)),
                "pl_kv_upload")
+
+    # the attention sub-block with its projections ----------------------
+    def set_layer(self, layer: int, dim: int, wq, type_q: int, wk, type_k: int, wv,
+                  type_v: int, wo, type_o: int, attn_norm=None, eps: float = 1e-5,
+                  bq=None, bk=None, bv=None, bo=None, q_norm=None, k_norm=None) -> None:
+        """Upload one layer's attention weights: w* are raw GGUF row bytes
+        (numpy arrays of any dtype, contiguous) of GGUF type type_*; norms
+        and biases float32 or None."""
+        ws = [np.ascontiguousarray(w) for w in (wq, wk, wv, wo)]
+        fs = [None if a is None else _f32(a) for a in (attn_norm, bq, bk, bv, bo, q_norm, k_norm)]
+        p = [None if a is None else a.ctypes.data for a in fs]
+        _check(self.lib.pl_attn_set_layer(layer, dim, p[0], float(eps),
+                                          ws[0].ctypes.data, type_q, ws[1].ctypes.data, type_k,
+                                          ws[2].ctypes.data, type_v, ws[3].ctypes.data, type_o,
+                                          p[1], p[2], p[3], p[4], p[5], p[6]),
+               "pl_attn_set_layer")
+
+    def block_decode(self, layer: int, seqs, pos, x) -> np.ndarray:
+        """x [n][dim] residual stream; returns x + attention sub-block(x)
+        (a new array; the argument is not modified)."""
+        seqs = np.ascontiguousarray(seqs, np.int32)
+        pos = np.ascontiguousarray(pos, np.int32)
+        xo = np.array(x, np.float32, order="C")
+        _check(self.lib.pl_attn_block_decode(layer, seqs.size, seqs, pos, xo.ravel()),
+               "pl_attn_block_decode")
+        return xo.reshape(seqs.size, -1)
+
+    def block_prefill(self, seq: int, layer: int, start_pos: int, x) -> np.ndarray:
+        xo = np.array(x, np.float32, order="C")
+        n_tok = xo.shape[0] if xo.ndim == 2 else 1
+        _check(self.lib.pl_attn_block_prefill(seq, layer, start_pos, n_tok, xo.ravel()),
+               "pl_attn_block_prefill")
+        return xo.reshape(n_tok, -1)
+
+    def block_decode_dev(self, layer, n, d_seqs, d_pos, max_pos, d_x, stream=None) -> None:
+        _check(self.lib.pl_attn_block_decode_dev(layer, n, d_seqs, d_pos, max_pos, d_x, stream),
+               "pl_attn_block_decode_dev")
+
+    def block_prefill_dev(self, seq, layer, start_pos, n_tok, d_x, stream=None) -> None:
+        _check(self.lib.pl_attn_block_prefill_dev(seq, layer, start_pos, n_tok, d_x, stream),
+               "pl_attn_block_prefill_dev")
+
+    def proj(self, layer: int, which: int, x, rows: int) -> np.ndarray:
+        """matmul_bias with uploaded weight `which` (0 q, 1 k, 2 v, 3 o) on
+        the rows of x; rows = output rows of that weight."""
+        xa = np.array(x, np.float32, order="C")
+        n = xa.shape[0] if xa.ndim == 2 else 1
+        y = np.empty(n * rows, np.float32)
+        _check(self.lib.pl_attn_proj(layer, which, n, xa.ravel(), y), "pl_attn_proj")
+        return y.reshape(n, rows)
 
     # device-pointer entry points --------------------------------------
     def decode_batch_dev(self, layer, n, d_seqs, d_pos, max_pos, d_q, d_k, d_v, d_out,

@@ -23,6 +23,7 @@
 #include "kern_decode.cuh"
 #include "kern_misc.cuh"
 #include "kern_prefill.cuh"
+#include "kern_proj.cuh"
 #include "kern_xfer.cuh"
 
 namespace {
@@ -42,6 +43,22 @@ struct Xfer {
   uint8_t* local = nullptr;              // this rank's buffer (cudaMalloc)
   pl::XferPeers peers = {};              // every rank's buffer as seen from this GPU
   void* opened[pl::kXferMaxRanks] = {};  // IPC mappings to close
+};
+
+// One layer's attention weights on the device (pl_attn_set_layer), all in one
+// allocation: Wq, Wk, Wv, Wo rows in the kern_proj.cuh layout, then the F32
+// RMSNorm weights, biases and QK-norm weights (nullptr where absent).
+struct LayerW {
+  uint8_t* mem = nullptr;
+  const uint8_t* w[4] = {};   // q, k, v, o
+  size_t row_bytes[4] = {};
+  int type[4] = {};
+  const float* bias[4] = {};
+  const float* attn_norm = nullptr;
+  const float* q_norm = nullptr;
+  const float* k_norm = nullptr;
+  float eps = 0.f;
+  int dim = 0;
 };
 
 struct Ctx {
@@ -80,6 +97,11 @@ struct Ctx {
   std::vector<cudaEvent_t> ev_pool;  // even index: start, odd: end
   size_t ev_used = 0;                // events recorded since the last read
   long n_attn = 0, n_all = 0;        // attention launches / all launches
+  // attention-block projections
+  std::vector<LayerW> lw;            // [n_layers]
+  float* d_blk = nullptr;            // q, k, v, attention output of a block call
+  size_t blk_cap = 0;                // floats
+  bool proj_smem_set = false;
 };
 
 Ctx* g = nullptr;
@@ -566,6 +588,8 @@ void free_ctx(Ctx* c) {
   cudaFree(c->d_work);
   cudaFree(c->d_q16);
   cudaFree(c->d_err);
+  cudaFree(c->d_blk);
+  for (LayerW& l : c->lw) cudaFree(l.mem);
   for (cudaEvent_t e : c->ev_pool) cudaEventDestroy(e);
   if (c->stream) cudaStreamDestroy(c->stream);
   delete c;
@@ -707,6 +731,7 @@ int pl_attn_init(int n_layers, int n_heads, int n_kv_heads, int head_dim, int ma
     }
     c->decode_slots = c->num_sms * per_sm;
   }
+  c->lw.resize(static_cast<size_t>(n_layers));
   if (cudaStreamSynchronize(c->stream) != cudaSuccess) {
     free_ctx(c);
     return PL_ECUDA;
@@ -1274,3 +1299,373 @@ extern "C" int pl_attn_decode_batch_dev_noalloc(int layer, int n, const int* d_s
                                        1, nullptr, part, seg_info);
   return launch_decode_kernel(a, grid, st, false);
 }
+
+// ---- the projections around the attention path ---------------------------
+// pl_attn_set_layer keeps one layer's attention weights on the device in
+// their GGUF quantisation; the block calls then run model.c's whole
+// attention sub-block (model.c:779-897 for decode, 990-1100 for prefill) on
+// the device: RMSNorm, Q/K/V projections and biases, QK-norm, RoPE, the FP16
+// KV append, attention, the output projection, its bias and the residual
+// add, with only the residual stream x crossing PCIe.
+
+namespace {
+
+size_t gguf_row_bytes(int type, int n) {
+  // picolm/quant.c:290-320 (block size and bytes per block)
+  switch (type) {
+    case pl::kGgufF32: return static_cast<size_t>(n) * 4;
+    case pl::kGgufF16: return static_cast<size_t>(n) * 2;
+    case pl::kGgufQ8_0: return static_cast<size_t>(n / 32) * 34;
+    case pl::kGgufQ4K: return static_cast<size_t>(n / 256) * pl::kQ4KBytes;
+    case pl::kGgufQ6K: return static_cast<size_t>(n / 256) * pl::kQ6KGgufBytes;
+    default: return 0;
+  }
+}
+
+// `rows` GGUF rows of n inputs -> the device layout of kern_proj.cuh
+void repack_rows(int type, const uint8_t* src, int rows, int n, uint8_t* dst) {
+  const size_t drb = pl::proj_row_bytes(type, n);
+  const size_t srb = gguf_row_bytes(type, n);
+  if (type == pl::kGgufF32 || type == pl::kGgufF16 || type == pl::kGgufQ4K) {
+    std::memcpy(dst, src, drb * static_cast<size_t>(rows));
+    return;
+  }
+  for (int r = 0; r < rows; ++r) {
+    const uint8_t* s = src + static_cast<size_t>(r) * srb;
+    uint8_t* d = dst + static_cast<size_t>(r) * drb;
+    std::memset(d, 0, drb);
+    if (type == pl::kGgufQ8_0) {
+      // {d, qs[32]} blocks -> all quants, then all scales
+      for (int b = 0; b < n / 32; ++b) {
+        std::memcpy(d + static_cast<size_t>(b) * 32, s + static_cast<size_t>(b) * 34 + 2, 32);
+        std::memcpy(d + n + static_cast<size_t>(b) * 2, s + static_cast<size_t>(b) * 34, 2);
+      }
+    } else {  // Q6_K: 210-byte blocks -> 224-byte blocks, same field order
+      for (int b = 0; b < n / 256; ++b)
+        std::memcpy(d + static_cast<size_t>(b) * pl::kQ6KBytes,
+                    s + static_cast<size_t>(b) * pl::kQ6KGgufBytes, pl::kQ6KGgufBytes);
+    }
+  }
+}
+
+int ensure_blk(size_t floats) {
+  if (floats <= g->blk_cap) return PL_OK;
+  if (g->d_blk) {
+    cudaStreamSynchronize(g->stream);
+    cudaFree(g->d_blk);
+  }
+  g->d_blk = nullptr;
+  g->blk_cap = 0;
+  if (cudaMalloc(&g->d_blk, floats * sizeof(float)) != cudaSuccess) return PL_ENOMEM;
+  g->blk_cap = floats;
+  return PL_OK;
+}
+
+// one launch of proj_kernel; mc (input rows per CTA) as large as the staged
+// rows fit in shared memory, at most kProjMaxM
+int launch_proj(pl::ProjArgs a, cudaStream_t st) {
+  const size_t row_b = static_cast<size_t>(a.n) * sizeof(float);
+  long long mc = pl::kProjSmemCap / static_cast<long long>(row_b);
+  if (mc > pl::kProjMaxM) mc = pl::kProjMaxM;
+  if (mc > a.M) mc = a.M;
+  if (mc < 1) return PL_EUNSUPPORTED;
+  a.mc = static_cast<int>(mc);
+  const long long gy = (a.M + mc - 1) / mc;
+  const int gx = (a.total_rows + pl::kProjWarps - 1) / pl::kProjWarps;
+  if (gy > 65535) return PL_EUNSUPPORTED;
+  if (!g->proj_smem_set) {
+    PL_CUDA(cudaFuncSetAttribute(pl::proj_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 pl::kProjSmemCap));
+    g->proj_smem_set = true;
+  }
+  pl::proj_kernel<<<dim3(gx, static_cast<unsigned>(gy)), pl::kProjThreads, mc * row_b, st>>>(a);
+  PL_CUDA(cudaGetLastError());
+  count_launch();
+  return PL_OK;
+}
+
+// the activations of one block call in d_blk: q [rows][q_dim], k and v
+// [rows][kv_dim], attention output [rows][q_dim] (all 16-byte aligned)
+struct BlkBufs {
+  float *q, *k, *v, *att;
+};
+int blk_bufs(int rows, BlkBufs* b) {
+  const size_t r = static_cast<size_t>(rows);
+  const int rc = ensure_blk(r * (2 * static_cast<size_t>(g->q_dim) + 2 * g->kv_dim));
+  if (rc) return rc;
+  b->q = g->d_blk;
+  b->k = b->q + r * g->q_dim;
+  b->v = b->k + r * g->kv_dim;
+  b->att = b->v + r * g->kv_dim;
+  return PL_OK;
+}
+
+pl::ProjMat proj_mat(const LayerW& L, int which, float* out, int ld_out) {
+  pl::ProjMat m;
+  m.w = L.w[which];
+  m.bias = L.bias[which];
+  m.out = out;
+  m.row_bytes = L.row_bytes[which];
+  m.type = L.type[which];
+  m.rows = which == 0 ? g->q_dim : (which == 3 ? L.dim : g->kv_dim);
+  m.ld_out = ld_out;
+  return m;
+}
+
+// rmsnorm + Q, K, V projections + biases of M rows of x [M][dim]
+int run_qkv(const LayerW& L, const float* d_x, int M, const BlkBufs& b, cudaStream_t st) {
+  pl::ProjArgs a = {};
+  a.mat[0] = proj_mat(L, 0, b.q, g->q_dim);
+  a.mat[1] = proj_mat(L, 1, b.k, g->kv_dim);
+  a.mat[2] = proj_mat(L, 2, b.v, g->kv_dim);
+  a.n_mat = 3;
+  a.total_rows = g->q_dim + 2 * g->kv_dim;
+  a.x = d_x;
+  a.ldx = L.dim;
+  a.n = L.dim;
+  a.M = M;
+  a.norm_w = L.attn_norm;
+  a.eps = L.eps;
+  int rc = launch_proj(a, st);
+  if (rc || !L.q_norm) return rc;
+  const dim3 grid(static_cast<unsigned>(M), (g->n_heads + g->n_kv_heads + 7) / 8);
+  pl::qk_norm_kernel<<<grid, 256, 0, st>>>(b.q, b.k, g->n_heads, g->n_kv_heads, g->head_dim,
+                                           L.q_norm, L.k_norm, L.eps);
+  PL_CUDA(cudaGetLastError());
+  count_launch();
+  return PL_OK;
+}
+
+// x [M][dim] += Wo att + bo
+int run_out(const LayerW& L, const float* d_att, int M, float* d_x, cudaStream_t st) {
+  pl::ProjArgs a = {};
+  a.mat[0] = proj_mat(L, 3, d_x, L.dim);
+  a.n_mat = 1;
+  a.total_rows = L.dim;
+  a.x = d_att;
+  a.ldx = g->q_dim;
+  a.n = g->q_dim;
+  a.M = M;
+  a.resid = d_x;
+  a.ld_res = L.dim;
+  return launch_proj(a, st);
+}
+
+int block_decode(int layer, int n, const int* d_seqs, const int* d_pos, int max_rows, float* d_x,
+                 cudaStream_t st) {
+  const LayerW& L = g->lw[static_cast<size_t>(layer)];
+  BlkBufs b;
+  int rc = blk_bufs(n, &b);
+  if (!rc) rc = run_qkv(L, d_x, n, b, st);
+  if (!rc)
+    rc = launch_decode(layer, n, d_seqs, d_pos, max_rows, b.q, b.k, b.v, b.att, 0, 0, 0, 1,
+                       nullptr, st);
+  if (!rc) rc = run_out(L, b.att, n, d_x, st);
+  return rc;
+}
+
+int block_prefill(int seq, int layer, int start_pos, int n_tok, float* d_x, cudaStream_t st) {
+  const LayerW& L = g->lw[static_cast<size_t>(layer)];
+  BlkBufs b;
+  int rc = blk_bufs(n_tok, &b);
+  if (!rc) rc = run_qkv(L, d_x, n_tok, b, st);
+  if (!rc) rc = launch_prefill(seq, layer, start_pos, n_tok, b.q, b.k, b.v, b.att, g->q_dim, st);
+  if (!rc) rc = run_out(L, b.att, n_tok, d_x, st);
+  return rc;
+}
+
+int check_layer_set(int layer) {
+  if (!g) return PL_ESTATE;
+  if (layer < 0 || layer >= g->n_layers) return PL_EARG;
+  return g->lw[static_cast<size_t>(layer)].mem ? PL_OK : PL_ESTATE;
+}
+
+}  // namespace
+
+extern "C" {
+
+int pl_attn_set_layer(int layer, int dim, const float* attn_norm, float rms_eps, const void* wq,
+                      int type_q, const void* wk, int type_k, const void* wv, int type_v,
+                      const void* wo, int type_o, const float* bq, const float* bk,
+                      const float* bv, const float* bo, const float* q_norm,
+                      const float* k_norm) {
+  if (!g) return PL_ESTATE;
+  if (layer < 0 || layer >= g->n_layers || dim <= 0 || !wq || !wk || !wv || !wo ||
+      (q_norm == nullptr) != (k_norm == nullptr) || !(rms_eps >= 0.f))
+    return PL_EARG;
+  const int types[4] = {type_q, type_k, type_v, type_o};
+  const int in[4] = {dim, dim, dim, g->q_dim};
+  const int rows[4] = {g->q_dim, g->kv_dim, g->kv_dim, dim};
+  const void* src[4] = {wq, wk, wv, wo};
+  for (int i = 0; i < 4; ++i)
+    if (!pl::proj_type_ok(types[i]) || in[i] % pl::proj_granule(types[i]) != 0) {
+      std::fprintf(stderr,
+                   "pl_attn_set_layer: weight %d: GGUF type %d over %d inputs is not supported "
+                   "(F32, F16, Q8_0, Q4_K, Q6_K; inputs a multiple of the block size)\n",
+                   i, types[i], in[i]);
+      return PL_EUNSUPPORTED;
+    }
+  // section offsets in the layer's allocation, 256-byte aligned
+  auto up = [](size_t v) { return (v + 255) & ~static_cast<size_t>(255); };
+  size_t off[4], total = 0;
+  for (int i = 0; i < 4; ++i) {
+    off[i] = total;
+    total = up(total + pl::proj_row_bytes(types[i], in[i]) * static_cast<size_t>(rows[i]));
+  }
+  const float* fsrc[7] = {attn_norm, bq, bk, bv, bo, q_norm, k_norm};
+  const int flen[7] = {dim, g->q_dim, g->kv_dim, g->kv_dim, dim, g->head_dim, g->head_dim};
+  size_t foff[7];
+  for (int i = 0; i < 7; ++i) {
+    foff[i] = total;
+    if (fsrc[i]) total = up(total + static_cast<size_t>(flen[i]) * sizeof(float));
+  }
+  std::vector<uint8_t> h(total);
+  for (int i = 0; i < 4; ++i)
+    repack_rows(types[i], static_cast<const uint8_t*>(src[i]), rows[i], in[i], h.data() + off[i]);
+  for (int i = 0; i < 7; ++i)
+    if (fsrc[i]) std::memcpy(h.data() + foff[i], fsrc[i], static_cast<size_t>(flen[i]) * 4);
+  if (cudaSetDevice(g->device) != cudaSuccess) return PL_ECUDA;
+  uint8_t* mem = nullptr;
+  if (cudaMalloc(&mem, total) != cudaSuccess) return PL_ENOMEM;
+  if (cudaMemcpy(mem, h.data(), total, cudaMemcpyHostToDevice) != cudaSuccess) {
+    cudaFree(mem);
+    return PL_ECUDA;
+  }
+  LayerW& L = g->lw[static_cast<size_t>(layer)];
+  if (L.mem) {
+    cudaStreamSynchronize(g->stream);
+    cudaFree(L.mem);
+  }
+  L = LayerW();
+  L.mem = mem;
+  L.dim = dim;
+  L.eps = rms_eps;
+  for (int i = 0; i < 4; ++i) {
+    L.w[i] = mem + off[i];
+    L.row_bytes[i] = pl::proj_row_bytes(types[i], in[i]);
+    L.type[i] = types[i];
+  }
+  auto fp = [&](int i) { return fsrc[i] ? reinterpret_cast<const float*>(mem + foff[i]) : nullptr; };
+  L.attn_norm = fp(0);
+  for (int i = 0; i < 4; ++i) L.bias[i] = fp(1 + i);
+  L.q_norm = fp(5);
+  L.k_norm = fp(6);
+  return PL_OK;
+}
+
+int pl_attn_block_decode(int layer, int n, const int* seqs, const int* pos, float* x) {
+  int rc = check_layer_set(layer);
+  if (rc) return rc;
+  if (n <= 0 || n > g->n_seqs || !seqs || !pos || !x) return PL_EARG;
+  int max_pos = 0;
+  for (int i = 0; i < n; ++i) {
+    if (seqs[i] < 0 || seqs[i] >= g->n_seqs || pos[i] < 0 || pos[i] >= g->max_seq)
+      return PL_EARG;
+    for (int j = 0; j < i; ++j)
+      if (seqs[j] == seqs[i]) return PL_EARG;
+    if (pos[i] > max_pos) max_pos = pos[i];
+  }
+  if (cudaSetDevice(g->device) != cudaSuccess) return PL_ECUDA;
+  const size_t xb = static_cast<size_t>(n) * g->lw[static_cast<size_t>(layer)].dim * sizeof(float);
+  const size_t ib = static_cast<size_t>(n) * sizeof(int);
+  const size_t x_off = (2 * ib + 255) & ~static_cast<size_t>(255);
+  rc = ensure_stage(x_off + xb + 256);
+  if (rc) return rc;
+  uint8_t* h = g->h_stage;
+  uint8_t* d = g->d_stage;
+  std::memcpy(h, seqs, ib);
+  std::memcpy(h + ib, pos, ib);
+  if (pinned(x, xb)) {
+    PL_CUDA(cudaMemcpyAsync(d, h, 2 * ib, cudaMemcpyHostToDevice, g->stream));
+    PL_CUDA(cudaMemcpyAsync(d + x_off, x, xb, cudaMemcpyHostToDevice, g->stream));
+  } else {
+    const CopyPiece in = {h + x_off, reinterpret_cast<const uint8_t*>(x), xb};
+    host_copy(&in, 1);
+    PL_CUDA(cudaMemcpyAsync(d, h, x_off + xb, cudaMemcpyHostToDevice, g->stream));
+  }
+  float* d_x = reinterpret_cast<float*>(d + x_off);
+  rc = block_decode(layer, n, reinterpret_cast<int*>(d), reinterpret_cast<int*>(d + ib),
+                    max_pos + 1, d_x, g->stream);
+  if (rc) return rc;
+  return read_back(d_x, x, xb, h + x_off);
+}
+
+int pl_attn_block_decode_dev(int layer, int n, const int* d_seqs, const int* d_pos, int max_pos,
+                             float* d_x, void* stream) {
+  int rc = check_layer_set(layer);
+  if (rc) return rc;
+  if (n <= 0 || n > g->n_seqs || max_pos < 0 || max_pos >= g->max_seq || !d_seqs || !d_pos ||
+      !d_x || !aligned16(d_x))
+    return PL_EARG;
+  return block_decode(layer, n, d_seqs, d_pos, max_pos + 1, d_x, pick_stream(stream));
+}
+
+int pl_attn_block_prefill(int seq, int layer, int start_pos, int n_tok, float* x) {
+  int rc = check_layer_set(layer);
+  if (rc) return rc;
+  if (seq < 0 || seq >= g->n_seqs || n_tok <= 0 || start_pos < 0 ||
+      start_pos + n_tok > g->max_seq || !x)
+    return PL_EARG;
+  if (cudaSetDevice(g->device) != cudaSuccess) return PL_ECUDA;
+  const size_t xb =
+      static_cast<size_t>(n_tok) * g->lw[static_cast<size_t>(layer)].dim * sizeof(float);
+  rc = ensure_stage(xb + 256);
+  if (rc) return rc;
+  uint8_t* h = g->h_stage;
+  uint8_t* d = g->d_stage;
+  if (pinned(x, xb)) {
+    PL_CUDA(cudaMemcpyAsync(d, x, xb, cudaMemcpyHostToDevice, g->stream));
+  } else {
+    const CopyPiece in = {h, reinterpret_cast<const uint8_t*>(x), xb};
+    host_copy(&in, 1);
+    PL_CUDA(cudaMemcpyAsync(d, h, xb, cudaMemcpyHostToDevice, g->stream));
+  }
+  float* d_x = reinterpret_cast<float*>(d);
+  rc = block_prefill(seq, layer, start_pos, n_tok, d_x, g->stream);
+  if (rc) return rc;
+  return read_back(d_x, x, xb, h);
+}
+
+int pl_attn_block_prefill_dev(int seq, int layer, int start_pos, int n_tok, float* d_x,
+                              void* stream) {
+  int rc = check_layer_set(layer);
+  if (rc) return rc;
+  if (seq < 0 || seq >= g->n_seqs || n_tok <= 0 || start_pos < 0 ||
+      start_pos + n_tok > g->max_seq || !d_x || !aligned16(d_x))
+    return PL_EARG;
+  return block_prefill(seq, layer, start_pos, n_tok, d_x, pick_stream(stream));
+}
+
+int pl_attn_proj(int layer, int which, int n, const float* x, float* y) {
+  int rc = check_layer_set(layer);
+  if (rc) return rc;
+  if (which < 0 || which > 3 || n <= 0 || !x || !y) return PL_EARG;
+  if (cudaSetDevice(g->device) != cudaSuccess) return PL_ECUDA;
+  const LayerW& L = g->lw[static_cast<size_t>(layer)];
+  const int in = which == 3 ? g->q_dim : L.dim;
+  const int rows = which == 0 ? g->q_dim : (which == 3 ? L.dim : g->kv_dim);
+  const size_t xb = static_cast<size_t>(n) * in * sizeof(float);
+  const size_t yb = static_cast<size_t>(n) * rows * sizeof(float);
+  const size_t y_off = (xb + 255) & ~static_cast<size_t>(255);
+  rc = ensure_stage(y_off + yb + 256);
+  if (rc) return rc;
+  uint8_t* h = g->h_stage;
+  uint8_t* d = g->d_stage;
+  const CopyPiece cp = {h, reinterpret_cast<const uint8_t*>(x), xb};
+  host_copy(&cp, 1);
+  PL_CUDA(cudaMemcpyAsync(d, h, xb, cudaMemcpyHostToDevice, g->stream));
+  float* d_y = reinterpret_cast<float*>(d + y_off);
+  pl::ProjArgs a = {};
+  a.mat[0] = proj_mat(L, which, d_y, rows);
+  a.n_mat = 1;
+  a.total_rows = rows;
+  a.x = reinterpret_cast<const float*>(d);
+  a.ldx = in;
+  a.n = in;
+  a.M = n;
+  rc = launch_proj(a, g->stream);
+  if (rc) return rc;
+  return read_back(d_y, y, yb, h + y_off);
+}
+
+}  // extern "C"

@@ -1,7 +1,9 @@
 """Running the end-to-end harness (oracle/e2e_harness.c) from the tests.
 
 oracle/_ref/e2e_ref is picolm with its own attention loops; oracle/_ref/e2e_pl
-is the same program with model.c's attention blocks calling this module.
+is the same program with model.c's attention blocks calling this module, and
+oracle/_ref/e2e_blk the program whose whole attention sub-blocks (RMSNorm,
+projections, attention, residual) call it.
 Both are built by `make -C oracle e2e` where the reference sources exist.
 """
 import os
@@ -10,6 +12,7 @@ import subprocess
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 E2E_REF = os.path.join(ROOT, "oracle", "_ref", "e2e_ref")
 E2E_PL = os.path.join(ROOT, "oracle", "_ref", "e2e_pl")
+E2E_BLK = os.path.join(ROOT, "oracle", "_ref", "e2e_blk")
 
 
 def have(binary: str) -> bool:

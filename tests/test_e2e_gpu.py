@@ -76,6 +76,22 @@ def test_kv_cache_file_through_the_device(tmp_path):
     assert ref[0] == ours[0]
 
 
+def test_block_greedy_tokens_identical_small_model(tmp_path):
+    """The whole attention sub-block on the device (pl_attn_set_layer +
+    pl_attn_block_prefill / pl_attn_block_decode): the projections sum in
+    another order than picolm's, and the greedy tokens must still agree."""
+    if not (E.have(E.E2E_REF) and E.have(E.E2E_BLK)):
+        pytest.skip("oracle/_ref/e2e_ref / e2e_blk not built (make -C oracle e2e)")
+    path = str(tmp_path / "small.gguf")
+    make_model(path, layers=4, dim=512, ffn=1024, heads=8, kv_heads=2, vocab=2000, ctx=512)
+    ref = E.run(E.E2E_REF, path, 96, 48, threads=4)
+    blk = E.run(E.E2E_BLK, path, 96, 48, threads=4)
+    d = E.first_divergence(ref[0], blk[0])
+    assert d is None, (f"greedy tokens diverge at step {d}: reference {ref[0][d]} "
+                       f"(margin {ref[1][d]:.3g}), B200 attention block {blk[0][d]} "
+                       f"(margin {blk[1][d]:.3g})")
+
+
 def test_greedy_tokens_identical_config2_full(tmp_path):
     if os.environ.get("PL_E2E_FULL") != "1":
         pytest.skip("full config 2 runs with PL_E2E_FULL=1 (minutes of CPU matmuls)")
@@ -84,9 +100,16 @@ def test_greedy_tokens_identical_config2_full(tmp_path):
     make_model(path)  # 22 layers, dim 2048, ffn 5632, 32/4 heads, vocab 32000, seed 1
     threads = min(16, os.cpu_count() or 1)
     ref, ours = _compare(path, 128, 128, threads=threads)
+    blk = E.run(E.E2E_BLK, path, 128, 128, threads=threads) if E.have(E.E2E_BLK) else None
     out = os.environ.get("PL_E2E_OUT")
     if out:
         with open(out, "w") as f:
             json.dump({"threads": threads, "tokens_identical": len(ours[0]),
                        "min_margin": min(ref[1]), "reference": ref[2], "b200_attention": ours[2],
+                       "b200_attention_block": blk[2] if blk else None,
+                       "block_tokens_identical": (E.first_divergence(ref[0], blk[0]) is None
+                                                  if blk else None),
                        "first_tokens": ours[0][:16]}, f, indent=1)
+    if blk:
+        d = E.first_divergence(ref[0], blk[0])
+        assert d is None, f"attention block: greedy tokens diverge at step {d}"

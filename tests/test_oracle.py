@@ -212,3 +212,37 @@ def test_rope_port_equals_genuine_reference(orc, hd, rope_type):
         orc.ref().rope(q2, k2, hd, H, Hk, cs, sn, rope_type)
         np.testing.assert_array_equal(q1.view(np.uint32), q2.view(np.uint32))
         np.testing.assert_array_equal(k1.view(np.uint32), k2.view(np.uint32))
+
+
+# ---- projections around the attention path (matmul per GGUF type, rmsnorm)
+@pytest.mark.parametrize("name", ["f32", "f16", "q8_0", "q4_k", "q6_k"])
+def test_matmul_port_equals_golden(golden, orc, name):
+    from tests.util import GGUF_TYPES
+    w, x, want = golden[f"proj_{name}_w"], golden[f"proj_{name}_x"], golden[f"proj_{name}_out"]
+    got = orc.matmul(w, x, x.size, want.size, GGUF_TYPES[name])
+    np.testing.assert_array_equal(got.view(np.uint32), want.view(np.uint32))
+
+
+@pytest.mark.parametrize("size", [2048, 61])
+def test_rmsnorm_port_equals_golden(golden, orc, size):
+    x, w, want = golden[f"rms{size}_x"], golden[f"rms{size}_w"], golden[f"rms{size}_out"]
+    got = orc.rmsnorm(x, w, 1e-5)
+    np.testing.assert_array_equal(got.view(np.uint32), want.view(np.uint32))
+
+
+@pytest.mark.skipif(not __import__("oracle.oracle", fromlist=["x"]).ref_available(),
+                    reason="oracle/_ref (the reference compiled here) is absent")
+@pytest.mark.parametrize("name", ["f32", "f16", "q8_0", "q4_k", "q6_k"])
+def test_matmul_port_equals_genuine_reference(orc, name):
+    # TinyLlama's projection shapes: 256 rows of 2048 inputs (Wk) and 2048
+    # inputs of a 2048-wide Wo slice, fresh weights, bit for bit
+    from tests.util import GGUF_TYPES, random_gguf
+    t = GGUF_TYPES[name]
+    rng = np.random.default_rng(100 + t)
+    for rows, n in ((256, 2048), (40, 4096)):
+        w = random_gguf(rng, t, rows, n)
+        assert w.shape[1] == orc.row_bytes(t, n)
+        x = rng.standard_normal(n, dtype=np.float32)
+        a = orc.matmul(w, x, n, rows, t)
+        b = orc.matmul(w, x, n, rows, t, use_ref=True)
+        np.testing.assert_array_equal(a.view(np.uint32), b.view(np.uint32))
