@@ -972,7 +972,7 @@ def main():
         import torch.distributed as dist
         dist.destroy_process_group()
         return
-    if args.workload in ("prefill", "long_ctx", "decode1", "hd128"):
+    if args.workload in ("prefill", "long_ctx", "decode1", "hd128", "block"):
         if rank == 0:
             fn = {"prefill": lambda: run_prefill(args, local, peaks),
                   "long_ctx": lambda: run_long_ctx(args, local, peaks),

@@ -140,7 +140,7 @@ def find(lines, pred, start=0):
 
 def main():
     args = sys.argv[1:]
-    block = "--block" in args
+    whole_block = "--block" in args
     src, dst = [a for a in args if a != "--block"]
     lines = open(src).read().split("\n")
 
@@ -167,7 +167,7 @@ def main():
         if must not in "\n".join(blk):
             raise SystemExit("pl_model_patch: kvcache block does not read the host cache")
     inc = find(lines, lambda s: s.strip() == '#include "model.h"')
-    if block:
+    if whole_block:
         # widen both blocks to the whole attention sub-block
         ds = find(lines, lambda s: s.strip().startswith(
             "rmsnorm(s->xb, s->x, s->attn_norm_w[l]"), inc)

@@ -44,6 +44,8 @@ __global__ void rope_inplace_kernel(float* q, float* k, int n_heads, int n_kv_he
 // Prefill prologue for n_tok rows starting at position start_pos:
 //   q16[r][h][d]  = FP16(RoPE(q[r][h][:]))[d]       (tensor-core operand,
 //                                                     round-to-nearest-even)
+//   q16lo[r][h][d] = FP16(y - q16[r][h][d]), y the rotated FP32 value: the
+//                    residual, so that hi + lo carries y to about 2^-22
 //   kc[start+r]   = picolm_FP16(RoPE(k[r]))          (bit-exact append)
 //   vc[start+r]   = picolm_FP16(v[r])
 // grid = n_tok (one block per token row), block = kPrologueThreads.  A row
@@ -103,25 +105,46 @@ __device__ __forceinline__ PrologueUnit prologue_load(int u, int r, const float*
   return pu;
 }
 
-// q goes to the tensor-core staging with round-to-nearest-even; k and v use
-// picolm's FP16 rounding (bit-exact cache rows).
+// k and v use picolm's FP16 rounding (bit-exact cache rows); q goes to the
+// tensor-core staging as an FP16 high part and FP16 residual (split_hi_lo).
 __device__ __forceinline__ uint32_t prologue_pack(float a, float b, bool picolm_rounding) {
   if (!picolm_rounding) return pack_half2(a, b);
   return static_cast<uint32_t>(picolm_f32_to_f16(a)) |
          (static_cast<uint32_t>(picolm_f32_to_f16(b)) << 16);
 }
 
+// Store 2n rotated values as FP16 words: picolm's rounding for the cache
+// rows (kind 1), the hi/lo split for q (kind 0, lo at dst + lo_off).
+template <int N>
+__device__ __forceinline__ void store_words(uint16_t* dst, long lo_off, const float* y, int kind) {
+  uint32_t hi[N], lo[N];
+#pragma unroll
+  for (int i = 0; i < N; ++i) {
+    if (kind == 0)
+      split_hi_lo(y[2 * i], y[2 * i + 1], hi[i], lo[i]);
+    else
+      hi[i] = prologue_pack(y[2 * i], y[2 * i + 1], true);
+  }
+  if constexpr (N == 4) {
+    *reinterpret_cast<uint4*>(dst) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+    if (kind == 0) *reinterpret_cast<uint4*>(dst + lo_off) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+  } else {
+    *reinterpret_cast<uint2*>(dst) = make_uint2(hi[0], hi[1]);
+    if (kind == 0) *reinterpret_cast<uint2*>(dst + lo_off) = make_uint2(lo[0], lo[1]);
+  }
+}
+
 template <int HD>
 __device__ __forceinline__ void prologue_store(const PrologueUnit& pu, int r, uint16_t* q16,
-                                               uint16_t* kc_rows, uint16_t* vc_rows, int n_heads,
-                                               int n_kv_heads, int rope_type) {
+                                               long q16_lo_off, uint16_t* kc_rows,
+                                               uint16_t* vc_rows, int n_heads, int n_kv_heads,
+                                               int rope_type) {
   const int kv_dim = n_kv_heads * HD;
   uint16_t* dst;
   if (pu.kind == 0)
     dst = q16 + (static_cast<size_t>(r) * n_heads + pu.head) * HD;
   else
     dst = (pu.kind == 1 ? kc_rows : vc_rows) + static_cast<size_t>(r) * kv_dim + pu.head * HD;
-  const bool pr = pu.kind != 0;
   if (pu.kind == 2) {
     *reinterpret_cast<uint4*>(dst + 8 * pu.part) =
         make_uint4(prologue_pack(pu.xa.x, pu.xa.y, true), prologue_pack(pu.xa.z, pu.xa.w, true),
@@ -132,9 +155,7 @@ __device__ __forceinline__ void prologue_store(const PrologueUnit& pu, int r, ui
     rope_pair(pu.xa.z, pu.xa.w, pu.c.y, pu.s.y, y[2], y[3]);
     rope_pair(pu.xb.x, pu.xb.y, pu.c.z, pu.s.z, y[4], y[5]);
     rope_pair(pu.xb.z, pu.xb.w, pu.c.w, pu.s.w, y[6], y[7]);
-    *reinterpret_cast<uint4*>(dst + 8 * pu.part) =
-        make_uint4(prologue_pack(y[0], y[1], pr), prologue_pack(y[2], y[3], pr),
-                   prologue_pack(y[4], y[5], pr), prologue_pack(y[6], y[7], pr));
+    store_words<4>(dst + 8 * pu.part, q16_lo_off, y, pu.kind);
   } else {
     // Qwen: element j (< HD/2) and j + HD/2 rotate together
     const float xa[4] = {pu.xa.x, pu.xa.y, pu.xa.z, pu.xa.w};
@@ -147,10 +168,8 @@ __device__ __forceinline__ void prologue_store(const PrologueUnit& pu, int r, ui
       lo[i] = __fsub_rn(__fmul_rn(xa[i], c[i]), __fmul_rn(xb[i], sv[i]));
       hi[i] = __fadd_rn(__fmul_rn(xa[i], sv[i]), __fmul_rn(xb[i], c[i]));
     }
-    *reinterpret_cast<uint2*>(dst + 4 * pu.part) =
-        make_uint2(prologue_pack(lo[0], lo[1], pr), prologue_pack(lo[2], lo[3], pr));
-    *reinterpret_cast<uint2*>(dst + HD / 2 + 4 * pu.part) =
-        make_uint2(prologue_pack(hi[0], hi[1], pr), prologue_pack(hi[2], hi[3], pr));
+    store_words<2>(dst + 4 * pu.part, q16_lo_off, lo, pu.kind);
+    store_words<2>(dst + HD / 2 + 4 * pu.part, q16_lo_off, hi, pu.kind);
   }
 }
 
@@ -158,7 +177,8 @@ template <int HD>
 __global__ void __launch_bounds__(kPrologueThreads)
     prefill_prologue_kernel(const float* __restrict__ q, const float* __restrict__ k,
                             const float* __restrict__ v, uint16_t* __restrict__ q16,
-                            uint16_t* __restrict__ kc_rows, uint16_t* __restrict__ vc_rows,
+                            long q16_lo_off, uint16_t* __restrict__ kc_rows,
+                            uint16_t* __restrict__ vc_rows,
                             int n_tok, int n_heads, int n_kv_heads, int start_pos,
                             const float* cos_tab, const float* sin_tab, int rope_type) {
   // the attention grid queued behind (programmatic dependent launch) may
@@ -179,9 +199,10 @@ __global__ void __launch_bounds__(kPrologueThreads)
     b.kind = -1;
     if (u2 < n_units)
       b = prologue_load<HD>(u2, r, q, k, v, n_heads, n_kv_heads, cs, sn, rope_type);
-    prologue_store<HD>(a, r, q16, kc_rows, vc_rows, n_heads, n_kv_heads, rope_type);
+    prologue_store<HD>(a, r, q16, q16_lo_off, kc_rows, vc_rows, n_heads, n_kv_heads, rope_type);
     if (b.kind >= 0)
-      prologue_store<HD>(b, r, q16, kc_rows, vc_rows, n_heads, n_kv_heads, rope_type);
+      prologue_store<HD>(b, r, q16, q16_lo_off, kc_rows, vc_rows, n_heads, n_kv_heads,
+                         rope_type);
   }
 }
 

@@ -3,7 +3,13 @@
 //
 // Replaces the position-by-position loop of picolm/model.c:1054-1089.  The
 // prologue kernel (kern_misc.cuh) has already rotated q/k, appended k/v to
-// the FP16 cache (bit-exact) and staged q as FP16 [n_tok][n_heads][HD].
+// the FP16 cache (bit-exact) and staged q as two FP16 arrays
+// [n_tok][n_heads][HD]: the high part and the residual.  S = Q_hi K^T +
+// Q_lo K^T (two MMAs into the same accumulator) carries q to about 2^-22,
+// as the FP32 reference does; with q rounded to FP16 alone, near-tied
+// scores of large q and k moved outputs by up to 2.7e-3 on projected
+// inputs.  The second MMA costs tensor-pipe time, which the softmax-bound
+// loop has to spare.
 //
 // Work item = two 128-row query tiles ("slots" A and B) sharing one KV
 // head: two query heads of the same GQA group at the same rows (with one
@@ -27,7 +33,8 @@
 // in registers) and the third drops to kPfOtherRegs:
 // 256 * 232 + 128 * 40 = 384 * 168.
 // Per KV tile j the issuer of slot x issues, in order,
-//   S_x(j) = Q_x K_j^T      (M=128 N=BN K=HD, smem x smem -> TMEM)
+//   S_x(j) = Q_x K_j^T      (M=128 N=BN K=HD, twice: hi and lo parts of Q;
+//                            smem x smem -> TMEM)
 //   PV_x(j-1) = P_x V       (M=128 N=64 K=BN per 64 columns of O, TMEM x smem
 //                            -> TMEM O_x)
 // so one slot's softmax overlaps the other slot's MMAs (ping-pong).  Issue
@@ -68,11 +75,11 @@ constexpr int kPfSoftmaxRegs = 232;
 constexpr int kPfOtherRegs = 40;
 static_assert(256 * kPfSoftmaxRegs + 128 * kPfOtherRegs <= kPfThreads * kPfLaunchRegs,
               "register split exceeds the launch allocation");
-constexpr int kPfStagePitch = 36;    // floats per row of the output staging buffer
+constexpr int kPfStagePitch = 32;    // floats per row of the output staging buffer
 constexpr float kPfRescaleLog2 = 8.0f;  // raise the running max only past 2^8
 
 struct PrefillArgs {
-  const uint16_t* q16;   // [n_tok][n_heads][HD] FP16, rotated
+  const uint16_t* q16;   // [n_tok][n_heads][HD] FP16, rotated (high part; TMA reads it)
   float* out;            // row r at out + r*out_stride, head h at +h*HD
   int out_stride;
   int n_tok, start_pos, n_heads, kv_mul, slab;
@@ -83,8 +90,9 @@ struct PrefillArgs {
 
 // The two shapes of the kernel: head_dim HD, KV tiles of BN cache rows,
 // a STAGES-deep K/V ring.  <64, 128, 4>: S 128 + O 64 + P 64 TMEM columns per
-// slot.  <128, 64, 3>: S 64 + O 128 + P 32 (448 of 512 columns), and 196 KB
-// of shared memory.  A row of Q, K or V is HD/64 halves of 64 elements
+// slot.  <128, 64, 3>: S 64 + O 128 + P 32 (448 of 512 columns).  Both use
+// 225 KB of shared memory, most of it Q (hi and lo) and the K/V ring; at
+// HD 128 the output is stored without the staging buffer.  A row of Q, K or V is HD/64 halves of 64 elements
 // (128 bytes, the swizzle span); each half of a tile is its own 128-byte
 // swizzled region, loaded by its own TMA box (x = 0 or 64).
 template <int HD, int BN, int STAGES>
@@ -99,18 +107,23 @@ struct PfShape {
   static __device__ __forceinline__ uint32_t col_o(int x) { return 2 * BN + x * HD; }
   static __device__ __forceinline__ uint32_t col_p(int x) { return 2 * BN + 2 * HD + x * (BN / 2); }
   static_assert(2 * BN + 2 * HD + BN <= 512, "TMEM columns");
+  // output staged through shared memory (HD 64) or stored from registers
+  static constexpr bool kStaged = HD <= 64;
   static_assert(BN % 64 == 0 && HD % 64 == 0, "tiles are whole 64-element halves");
 };
 
 template <int HD, int BN, int STAGES>
 struct PfSmem {
   // 1024-byte aligned tiles (128-byte swizzle atoms are 8 rows x 128 B)
-  uint8_t q[2][PfShape<HD, BN, STAGES>::kQBytes];      // Q_A, Q_B
+  uint8_t q[2][PfShape<HD, BN, STAGES>::kQBytes];      // Q_A, Q_B (FP16 high parts)
+  uint8_t ql[2][PfShape<HD, BN, STAGES>::kQBytes];     // their FP16 residuals
   uint8_t k[STAGES][PfShape<HD, BN, STAGES>::kKVBytes];
   uint8_t v[STAGES][PfShape<HD, BN, STAGES>::kKVBytes];
-  // per softmax warp, 32 rows x 32 output columns (row pitch padded so
-  // that both the row-wise writes and the transposed reads are conflict-free)
-  float stage[8][32 * kPfStagePitch];
+  // per softmax warp, 32 rows x 32 output columns; 16-byte chunk c of row r
+  // sits at chunk c ^ (r & 7), so that both the row-wise writes and the
+  // transposed reads are conflict-free without padding
+  float stage[PfShape<HD, BN, STAGES>::kStaged ? 8 : 1]
+             [PfShape<HD, BN, STAGES>::kStaged ? 32 * kPfStagePitch : 4];
   uint64_t q_full, q_empty;
   uint64_t kv_full[STAGES], kv_empty[STAGES];
   uint64_t s_full[2], s_free[2], p_full[2][2], pv_done[2][2], o_free[2];
@@ -196,6 +209,7 @@ __device__ __forceinline__ int pf_n_items(const PrefillArgs& a) {
 template <int HD, int BN, int STAGES>
 __global__ void __launch_bounds__(kPfThreads, 1)
     prefill_attn_kernel(const PrefillArgs a, const __grid_constant__ CUtensorMap tm_q,
+                        const __grid_constant__ CUtensorMap tm_ql,
                         const __grid_constant__ CUtensorMap tm_k,
                         const __grid_constant__ CUtensorMap tm_v) {
   using Sh = PfShape<HD, BN, STAGES>;
@@ -244,6 +258,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
       // --------------------------------------------------- scheduler + TMA
       if (lane == 0) {
         tma_prefetch_desc(&tm_q);
+        tma_prefetch_desc(&tm_ql);
         tma_prefetch_desc(&tm_k);
         tma_prefetch_desc(&tm_v);
         const int n_items = pf_n_items(a);
@@ -267,14 +282,19 @@ __global__ void __launch_bounds__(kPfThreads, 1)
             ++k;
             continue;
           }
-          mbar_arrive_expect_tx(&sm.q_full, n_slots * Sh::kQBytes);
+          mbar_arrive_expect_tx(&sm.q_full, 2 * n_slots * Sh::kQBytes);
 #pragma unroll
           for (int hv = 0; hv < Sh::kHalves; ++hv) {
             tma_load_3d(sm.q[0] + hv * Sh::kQHalf, &tm_q, &sm.q_full, 64 * hv, it.head0,
                         it.q_row0);
-            if (n_slots == 2)
+            tma_load_3d(sm.ql[0] + hv * Sh::kQHalf, &tm_ql, &sm.q_full, 64 * hv, it.head0,
+                        it.q_row0);
+            if (n_slots == 2) {
               tma_load_3d(sm.q[1] + hv * Sh::kQHalf, &tm_q, &sm.q_full, 64 * hv, it.head1,
                           it.q_row0);
+              tma_load_3d(sm.ql[1] + hv * Sh::kQHalf, &tm_ql, &sm.q_full, 64 * hv, it.head1,
+                          it.q_row0);
+            }
           }
           for (int j = 0; j < it.nkv; ++j, ++J) {
             const int s = J % STAGES;
@@ -314,6 +334,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
         const uint32_t idesc_pv = idesc_f16_f32(128, 64, 1);  // one 64-column half of O
         const bool active = x < n_slots;
         const uint32_t q_addr = smem_u32(sm.q[x]);
+        const uint32_t ql_addr = smem_u32(sm.ql[x]);
         int J = 0, k = 0;
         bool ok = true;
         // PV_x of global tile g (first tile of its item if `first`), then
@@ -362,9 +383,12 @@ __global__ void __launch_bounds__(kPfThreads, 1)
             for (int kk = 0; kk < HD / 16; ++kk) {  // 16 dims per MMA, 4 per 128-byte half
               const uint32_t off_q = (kk >> 2) * Sh::kQHalf + (kk & 3) * 32;
               const uint32_t off_k = (kk >> 2) * Sh::kKVHalf + (kk & 3) * 32;
-              const uint64_t ad = smem_desc_sw128(q_addr + off_q, 16, 1024);
               const uint64_t bd = smem_desc_sw128(k_addr + off_k, 16, 1024);
-              tc_mma_ss(tmem + Sh::col_s(x), ad, bd, idesc_qk, kk > 0 ? 1u : 0u);
+              // Q_hi K^T, then Q_lo K^T into the same S
+              tc_mma_ss(tmem + Sh::col_s(x), smem_desc_sw128(q_addr + off_q, 16, 1024), bd,
+                        idesc_qk, kk > 0 ? 1u : 0u);
+              tc_mma_ss(tmem + Sh::col_s(x), smem_desc_sw128(ql_addr + off_q, 16, 1024), bd,
+                        idesc_qk, 1u);
             }
             tc_commit(&sm.s_full[x]);
             if (j == it.nkv - 1) tc_commit(&sm.q_empty);  // Q_x free once these S MMAs land
@@ -527,24 +551,38 @@ __global__ void __launch_bounds__(kPfThreads, 1)
       // O / l to the output through the warp's staging buffer, 32 columns
       // at a time: a thread holds one row, so direct stores would touch 32
       // rows per instruction; read back transposed, each store instruction
-      // covers four rows x 128 contiguous bytes
+      // covers four rows x 128 contiguous bytes.  At head_dim 128 the
+      // shared memory goes to a deeper K/V ring instead and the rows are
+      // stored directly.
       const float inv = 1.0f / l_run;
-      float* stg = sm.stage[warp];
       const int row_base = it.q_row0 + (warp & 3) * 32;
+      if constexpr (!Sh::kStaged) {
+        float* drow = a.out + static_cast<size_t>(row_base + lane) * a.out_stride +
+                      (x ? it.head1 : it.head0) * HD;
+        if (row_base + lane < a.n_tok) {
+#pragma unroll
+          for (int c = 0; c < HD; c += 4)
+            *reinterpret_cast<float4*>(drow + c) = make_float4(
+                __uint_as_float(ov[c]) * inv, __uint_as_float(ov[c + 1]) * inv,
+                __uint_as_float(ov[c + 2]) * inv, __uint_as_float(ov[c + 3]) * inv);
+        }
+      }
+      float* stg = sm.stage[Sh::kStaged ? warp : 0];
       float* dst = a.out + (x ? it.head1 : it.head0) * HD + (lane & 7) * 4;
 #pragma unroll
-      for (int hc = 0; hc < HD / 32; ++hc) {
+      for (int hc = 0; hc < (Sh::kStaged ? HD / 32 : 0); ++hc) {
 #pragma unroll
         for (int c = 0; c < 32; c += 4)
-          *reinterpret_cast<float4*>(stg + lane * kPfStagePitch + c) = make_float4(
+          *reinterpret_cast<float4*>(stg + lane * kPfStagePitch + 4 * ((c >> 2) ^ (lane & 7))) =
+              make_float4(
               __uint_as_float(ov[32 * hc + c]) * inv, __uint_as_float(ov[32 * hc + c + 1]) * inv,
               __uint_as_float(ov[32 * hc + c + 2]) * inv, __uint_as_float(ov[32 * hc + c + 3]) * inv);
         __syncwarp();
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
           const int rr = 4 * i + (lane >> 3);
-          const float4 val =
-              *reinterpret_cast<const float4*>(stg + rr * kPfStagePitch + (lane & 7) * 4);
+          const float4 val = *reinterpret_cast<const float4*>(
+              stg + rr * kPfStagePitch + 4 * ((lane & 7) ^ (rr & 7)));
           if (row_base + rr < a.n_tok)
             *reinterpret_cast<float4*>(dst + static_cast<size_t>(row_base + rr) * a.out_stride +
                                        32 * hc) = val;
@@ -569,11 +607,13 @@ __global__ void __launch_bounds__(kPfThreads, 1)
 // With `overlap`, the launch may begin while the previous grid on the stream
 // (the prologue) is still running (programmatic stream serialisation).
 // HD 64 runs <64, 128, 4>, HD 128 runs <128, 64, 3>; the tensor maps carry
-// boxes of 64 elements x 128 query rows (q) and 64 x BN cache rows (k, v).
+// boxes of 64 elements x 128 query rows (q hi and lo) and 64 x BN cache rows
+// (k, v).
 template <int HD, int BN, int STAGES>
 inline int launch_prefill_shape(const PrefillArgs& a, const CUtensorMap& tm_q,
-                                const CUtensorMap& tm_k, const CUtensorMap& tm_v, int num_sms,
-                                cudaStream_t st, bool overlap) {
+                                const CUtensorMap& tm_ql, const CUtensorMap& tm_k,
+                                const CUtensorMap& tm_v, int num_sms, cudaStream_t st,
+                                bool overlap) {
   auto kern = prefill_attn_kernel<HD, BN, STAGES>;
   constexpr int smem = pf_smem_bytes<HD, BN, STAGES>();
   static bool attr_done = false;
@@ -605,7 +645,7 @@ inline int launch_prefill_shape(const PrefillArgs& a, const CUtensorMap& tm_q,
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = overlap ? 1 : 0;
-  if (cudaLaunchKernelEx(&cfg, kern, a, tm_q, tm_k, tm_v) != cudaSuccess) return -4;
+  if (cudaLaunchKernelEx(&cfg, kern, a, tm_q, tm_ql, tm_k, tm_v) != cudaSuccess) return -4;
   return cudaGetLastError() == cudaSuccess ? 0 : -4;
 }
 
@@ -613,11 +653,12 @@ inline int launch_prefill_shape(const PrefillArgs& a, const CUtensorMap& tm_q,
 constexpr int pf_block_n(int head_dim) { return head_dim == 128 ? 64 : 128; }
 
 inline int launch_prefill_attention(int head_dim, const PrefillArgs& a, const CUtensorMap& tm_q,
-                                    const CUtensorMap& tm_k, const CUtensorMap& tm_v,
-                                    int num_sms, cudaStream_t st, bool overlap) {
+                                    const CUtensorMap& tm_ql, const CUtensorMap& tm_k,
+                                    const CUtensorMap& tm_v, int num_sms, cudaStream_t st,
+                                    bool overlap) {
   if (head_dim == 128)
-    return launch_prefill_shape<128, 64, 3>(a, tm_q, tm_k, tm_v, num_sms, st, overlap);
-  return launch_prefill_shape<64, 128, 4>(a, tm_q, tm_k, tm_v, num_sms, st, overlap);
+    return launch_prefill_shape<128, 64, 3>(a, tm_q, tm_ql, tm_k, tm_v, num_sms, st, overlap);
+  return launch_prefill_shape<64, 128, 4>(a, tm_q, tm_ql, tm_k, tm_v, num_sms, st, overlap);
 }
 
 }  // namespace pl

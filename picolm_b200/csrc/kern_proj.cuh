@@ -265,34 +265,55 @@ __device__ __forceinline__ void row_q6k(const uint8_t* wr, const float* xs, int 
 __global__ void __launch_bounds__(kProjThreads) proj_kernel(const __grid_constant__ ProjArgs a) {
   extern __shared__ float4 proj_xs4[];
   float* xs = reinterpret_cast<float*>(proj_xs4);
+  __shared__ float ss_part[kProjWarps][kProjMaxM];
   __shared__ float inv_rms[kProjMaxM];
   const int m0 = blockIdx.y * a.mc;
   const int mc = min(a.mc, a.M - m0);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int n4 = a.n / 4;
+  // stage the input rows with 16-byte loads from all threads; with norm_w
+  // each thread also sums the squares of what it staged, per row
+  float ss[kProjMaxM];
+#pragma unroll
+  for (int m = 0; m < kProjMaxM; ++m) ss[m] = 0.f;
+#pragma unroll
+  for (int m = 0; m < kProjMaxM; ++m) {
+    if (m < mc) {
+      const float4* xr = reinterpret_cast<const float4*>(a.x + static_cast<size_t>(m0 + m) * a.ldx);
+      for (int i4 = threadIdx.x; i4 < n4; i4 += kProjThreads) {
+        const float4 v = __ldg(xr + i4);
+        proj_xs4[m * n4 + i4] = v;
+        ss[m] = fmaf(v.w, v.w, fmaf(v.z, v.z, fmaf(v.y, v.y, fmaf(v.x, v.x, ss[m]))));
+      }
+    }
+  }
   if (a.norm_w) {
     // picolm/tensor.c:425-490: 1 / sqrtf(sum(x^2) / n + eps)
-    for (int m = warp; m < mc; m += kProjWarps) {
-      const float* xr = a.x + static_cast<size_t>(m0 + m) * a.ldx;
-      float ss = 0.f;
-      for (int i = lane; i < a.n; i += 32) ss = fmaf(xr[i], xr[i], ss);
 #pragma unroll
-      for (int o = 16; o; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-      if (lane == 0) inv_rms[m] = 1.0f / sqrtf(ss / static_cast<float>(a.n) + a.eps);
+    for (int m = 0; m < kProjMaxM; ++m) {
+      float t = ss[m];
+#pragma unroll
+      for (int o = 16; o; o >>= 1) t += __shfl_xor_sync(0xffffffffu, t, o);
+      if (lane == 0) ss_part[warp][m] = t;
     }
     __syncthreads();
-  }
-  const int n4 = a.n / 4;
-  for (int idx = threadIdx.x; idx < mc * n4; idx += kProjThreads) {
-    const int m = idx / n4, i4 = idx - m * n4;
-    float4 v = __ldg(reinterpret_cast<const float4*>(a.x + static_cast<size_t>(m0 + m) * a.ldx) + i4);
-    if (a.norm_w) {
-      // (x * ss) * w, two rounded products as the reference
+    if (threadIdx.x < mc) {
+      float t = 0.f;
+#pragma unroll
+      for (int w = 0; w < kProjWarps; ++w) t += ss_part[w][threadIdx.x];
+      inv_rms[threadIdx.x] = 1.0f / sqrtf(t / static_cast<float>(a.n) + a.eps);
+    }
+    __syncthreads();
+    // (x * ss) * w, two rounded products as the reference, in place
+    for (int idx = threadIdx.x; idx < mc * n4; idx += kProjThreads) {
+      const int m = idx / n4, i4 = idx - m * n4;
       const float s = inv_rms[m];
       const float4 w = __ldg(reinterpret_cast<const float4*>(a.norm_w) + i4);
-      v = make_float4(__fmul_rn(__fmul_rn(v.x, s), w.x), __fmul_rn(__fmul_rn(v.y, s), w.y),
+      const float4 v = proj_xs4[idx];
+      proj_xs4[idx] =
+          make_float4(__fmul_rn(__fmul_rn(v.x, s), w.x), __fmul_rn(__fmul_rn(v.y, s), w.y),
                       __fmul_rn(__fmul_rn(v.z, s), w.z), __fmul_rn(__fmul_rn(v.w, s), w.w));
     }
-    proj_xs4[idx] = v;
   }
   __syncthreads();
   const int row = blockIdx.x * kProjWarps + warp;

@@ -84,13 +84,14 @@ struct Ctx {
   int2* d_seg_info = nullptr; // [kMaxLaunchSeqs] (first slot, segments) per decode sequence
   int* d_work = nullptr;      // [2] prefill work-queue counters (self-resetting)
   // prefill FP16 q staging
-  uint16_t* d_q16 = nullptr;
-  size_t q16_cap = 0;         // elements
+  uint16_t* d_q16 = nullptr;  // high parts, then the residuals at d_q16 + q16_cap
+  size_t q16_cap = 0;         // elements of each
   uint32_t* d_err = nullptr;  // device error word
   cudaStream_t stream = nullptr;
   CUtensorMap tm_k_dec, tm_v_dec;  // decode: box {64, tp, Hk, 1}, head_dim/64 per tile
   CUtensorMap tm_k_pf, tm_v_pf;    // prefill: box {64, 128 rows, 1, 1}
   CUtensorMap tm_q16;              // prefill q staging: box {64, 1 head, 128 rows}, HD/64 per row
+  CUtensorMap tm_q16lo;            // the same over the residuals
   EncodeTiledFn encode = nullptr;
   // profiling: event pairs around each attention kernel (see pl_attn_profile)
   int profiling = 0;
@@ -299,9 +300,10 @@ int ensure_part(size_t floats) {
   return PL_OK;
 }
 
-// FP16 q staging for the prefill, [rows][n_heads][head_dim], with its TMA map.
-// Rows past the current n_tok hold stale data; they only feed query rows
-// whose output is never stored.
+// FP16 q staging for the prefill, [rows][n_heads][head_dim] twice (the high
+// parts, then the residuals), with a TMA map over each.  Rows past the
+// current n_tok hold stale data; they only feed query rows whose output is
+// never stored.
 int ensure_q16(int n_tok) {
   const size_t rows = static_cast<size_t>(n_tok);
   if (rows * g->q_dim <= g->q16_cap) return PL_OK;
@@ -310,10 +312,9 @@ int ensure_q16(int n_tok) {
   if (g->d_q16) cudaFree(g->d_q16);
   g->d_q16 = nullptr;
   g->q16_cap = 0;
-  if (cudaMalloc(&g->d_q16, cap_rows * g->q_dim * sizeof(uint16_t)) != cudaSuccess)
-    return PL_ENOMEM;
-  if (cudaMemset(g->d_q16, 0, cap_rows * g->q_dim * sizeof(uint16_t)) != cudaSuccess)
-    return PL_ECUDA;
+  const size_t elems = cap_rows * g->q_dim;
+  if (cudaMalloc(&g->d_q16, 2 * elems * sizeof(uint16_t)) != cudaSuccess) return PL_ENOMEM;
+  if (cudaMemset(g->d_q16, 0, 2 * elems * sizeof(uint16_t)) != cudaSuccess) return PL_ECUDA;
   const cuuint64_t dims[3] = {static_cast<cuuint64_t>(g->head_dim),
                               static_cast<cuuint64_t>(g->n_heads),
                               static_cast<cuuint64_t>(cap_rows)};
@@ -321,12 +322,14 @@ int ensure_q16(int n_tok) {
                                  static_cast<cuuint64_t>(g->q_dim) * 2};
   const cuuint32_t box[3] = {64u, 1u, static_cast<cuuint32_t>(pl::kPfBlockM)};
   const cuuint32_t estr[3] = {1, 1, 1};
-  if (g->encode(&g->tm_q16, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, g->d_q16, dims, strides, box, estr,
-                CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
-    return PL_ECUDA;
-  g->q16_cap = cap_rows * g->q_dim;
+  for (int part = 0; part < 2; ++part)
+    if (g->encode(part ? &g->tm_q16lo : &g->tm_q16, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3,
+                  g->d_q16 + part * elems, dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+      return PL_ECUDA;
+  g->q16_cap = elems;
   return PL_OK;
 }
 
@@ -1083,11 +1086,11 @@ static int launch_prefill(int seq, int layer, int start_pos, int n_tok, const fl
   const size_t off = static_cast<size_t>(start_pos) * g->kv_dim;
   if (g->head_dim == 128)
     pl::prefill_prologue_kernel<128><<<n_tok, pl::kPrologueThreads, 0, st>>>(
-        d_q, d_k, d_v, g->d_q16, slab_k(seq, layer) + off, slab_v(seq, layer) + off, n_tok,
+        d_q, d_k, d_v, g->d_q16, static_cast<long>(g->q16_cap), slab_k(seq, layer) + off, slab_v(seq, layer) + off, n_tok,
         g->n_heads, g->n_kv_heads, start_pos, g->d_cos, g->d_sin, g->rope_type);
   else
     pl::prefill_prologue_kernel<64><<<n_tok, pl::kPrologueThreads, 0, st>>>(
-        d_q, d_k, d_v, g->d_q16, slab_k(seq, layer) + off, slab_v(seq, layer) + off, n_tok,
+        d_q, d_k, d_v, g->d_q16, static_cast<long>(g->q16_cap), slab_k(seq, layer) + off, slab_v(seq, layer) + off, n_tok,
         g->n_heads, g->n_kv_heads, start_pos, g->d_cos, g->d_sin, g->rope_type);
   PL_CUDA(cudaGetLastError());
   count_launch();
@@ -1105,7 +1108,7 @@ static int launch_prefill(int seq, int layer, int start_pos, int n_tok, const fl
   a.err = g->d_err;
   prof_begin(st);
   // overlap with the prologue except when events separate the two for timing
-  if (pl::launch_prefill_attention(g->head_dim, a, g->tm_q16, g->tm_k_pf, g->tm_v_pf,
+  if (pl::launch_prefill_attention(g->head_dim, a, g->tm_q16, g->tm_q16lo, g->tm_k_pf, g->tm_v_pf,
                                    g->num_sms, st, !g->profiling) != 0)
     return PL_ECUDA;
   prof_end(st);
