@@ -109,159 +109,276 @@ __device__ __forceinline__ float dot4(float4 a, float4 b, float s) {
 }
 __device__ __forceinline__ float sum4(float4 a) { return (a.x + a.y) + (a.z + a.w); }
 
-// Each lane takes work units u = lane, lane + 32, ... of the row (4 to 16
-// weights each, consecutive lanes on consecutive bytes) and adds its partial
-// dot with every staged input row m < mc into acc[m].
+// Small unsigned integers (< 2^23) to float without the conversion unit:
+// byte k of w becomes the low byte of 0x4B000000 (2^23 with the integer in
+// its mantissa); subtracting 2^23 + bias is exact.  One byte permute and one
+// add instead of an I2F, which runs at an eighth of the FMA rate.
+__device__ __forceinline__ float4 bytes_to_f4(uint32_t w, float bias) {
+  const float base = 8388608.0f + bias;
+  return make_float4(__int_as_float(static_cast<int>(__byte_perm(w, 0x4B000000u, 0x7440))) - base,
+                     __int_as_float(static_cast<int>(__byte_perm(w, 0x4B000000u, 0x7441))) - base,
+                     __int_as_float(static_cast<int>(__byte_perm(w, 0x4B000000u, 0x7442))) - base,
+                     __int_as_float(static_cast<int>(__byte_perm(w, 0x4B000000u, 0x7443))) - base);
+}
 
-__device__ __forceinline__ void row_f32(const uint8_t* wr, const float* xs, int n, int mc,
-                                        int lane, float* acc) {
-  const float4* w4 = reinterpret_cast<const float4*>(wr);
+// Each lane takes work units u = lane, lane + 32, ... of a row (4 to 16
+// weights each, consecutive lanes on consecutive bytes) for R consecutive
+// rows at once, U units per step with all their loads issued first, and
+// adds its partial dots with every staged input row m < mc into acc[i][m].
+// The R rows share the block layout, so one read of the x chunk (and of
+// its sums) from shared memory serves all of them; the weights are turned
+// into floats once per unit, outside the loop over input rows.
+
+template <int R, int U>
+__device__ __forceinline__ void rows_f32(const uint8_t* w0, size_t rb, const float* xs, int n,
+                                         int mc, int lane, float (*acc)[kProjMaxM]) {
   const float4* x4 = reinterpret_cast<const float4*>(xs);
   const int units = n / 4, n4 = n / 4;
-  for (int u = lane; u < units; u += 32) {
-    const float4 w = __ldg(w4 + u);
+  for (int u0 = lane; u0 < units; u0 += 32 * U) {
+    float4 w[U][R];
 #pragma unroll
-    for (int m = 0; m < kProjMaxM; ++m)
-      if (m < mc) acc[m] = dot4(w, x4[m * n4 + u], acc[m]);
+    for (int k = 0; k < U; ++k)
+#pragma unroll
+      for (int i = 0; i < R; ++i)
+        w[k][i] = u0 + 32 * k < units
+                      ? __ldg(reinterpret_cast<const float4*>(w0 + i * rb) + u0 + 32 * k)
+                      : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+    for (int k = 0; k < U; ++k) {
+      const int u = u0 + 32 * k;
+      if (u >= units) break;
+#pragma unroll
+      for (int m = 0; m < kProjMaxM; ++m)
+        if (m < mc) {
+          const float4 xv = x4[m * n4 + u];
+#pragma unroll
+          for (int i = 0; i < R; ++i) acc[i][m] = dot4(w[k][i], xv, acc[i][m]);
+        }
+    }
   }
 }
 
-__device__ __forceinline__ void row_f16(const uint8_t* wr, const float* xs, int n, int mc,
-                                        int lane, float* acc) {
-  const uint4* w8 = reinterpret_cast<const uint4*>(wr);
+template <int R, int U>
+__device__ __forceinline__ void rows_f16(const uint8_t* w0, size_t rb, const float* xs, int n,
+                                         int mc, int lane, float (*acc)[kProjMaxM]) {
   const float4* x4 = reinterpret_cast<const float4*>(xs);
   const int units = n / 8, n4 = n / 4;
-  for (int u = lane; u < units; u += 32) {
-    const uint4 q = __ldg(w8 + u);
-    const float4 wa = make_float4(f16_bits(q.x & 0xFFFFu), f16_bits(q.x >> 16),
-                                  f16_bits(q.y & 0xFFFFu), f16_bits(q.y >> 16));
-    const float4 wb = make_float4(f16_bits(q.z & 0xFFFFu), f16_bits(q.z >> 16),
-                                  f16_bits(q.w & 0xFFFFu), f16_bits(q.w >> 16));
+  for (int u0 = lane; u0 < units; u0 += 32 * U) {
+    uint4 q[U][R];
 #pragma unroll
-    for (int m = 0; m < kProjMaxM; ++m)
-      if (m < mc) acc[m] = dot4(wb, x4[m * n4 + 2 * u + 1], dot4(wa, x4[m * n4 + 2 * u], acc[m]));
+    for (int k = 0; k < U; ++k)
+#pragma unroll
+      for (int i = 0; i < R; ++i)
+        q[k][i] = u0 + 32 * k < units
+                      ? __ldg(reinterpret_cast<const uint4*>(w0 + i * rb) + u0 + 32 * k)
+                      : make_uint4(0u, 0u, 0u, 0u);
+#pragma unroll
+    for (int k = 0; k < U; ++k) {
+      const int u = u0 + 32 * k;
+      if (u >= units) break;
+      float4 wa[R], wb[R];
+#pragma unroll
+      for (int i = 0; i < R; ++i) {
+        const float2 p0 = __half22float2(*reinterpret_cast<const __half2*>(&q[k][i].x));
+        const float2 p1 = __half22float2(*reinterpret_cast<const __half2*>(&q[k][i].y));
+        const float2 p2 = __half22float2(*reinterpret_cast<const __half2*>(&q[k][i].z));
+        const float2 p3 = __half22float2(*reinterpret_cast<const __half2*>(&q[k][i].w));
+        wa[i] = make_float4(p0.x, p0.y, p1.x, p1.y);
+        wb[i] = make_float4(p2.x, p2.y, p3.x, p3.y);
+      }
+#pragma unroll
+      for (int m = 0; m < kProjMaxM; ++m)
+        if (m < mc) {
+          const float4 xa = x4[m * n4 + 2 * u], xb = x4[m * n4 + 2 * u + 1];
+#pragma unroll
+          for (int i = 0; i < R; ++i) acc[i][m] = dot4(wb[i], xb, dot4(wa[i], xa, acc[i][m]));
+        }
+    }
   }
-}
-
-__device__ __forceinline__ float4 s8x4(uint32_t w) {
-  return make_float4(static_cast<float>(static_cast<int8_t>(w & 0xFFu)),
-                     static_cast<float>(static_cast<int8_t>((w >> 8) & 0xFFu)),
-                     static_cast<float>(static_cast<int8_t>((w >> 16) & 0xFFu)),
-                     static_cast<float>(static_cast<int8_t>(w >> 24)));
 }
 
 // Q8_0: a unit is half a 32-weight block
-__device__ __forceinline__ void row_q8_0(const uint8_t* wr, const float* xs, int n, int mc,
-                                         int lane, float* acc) {
-  const uint4* q16 = reinterpret_cast<const uint4*>(wr);
-  const unsigned short* dv = reinterpret_cast<const unsigned short*>(wr + n);
+template <int R, int U>
+__device__ __forceinline__ void rows_q8_0(const uint8_t* w0, size_t rb, const float* xs, int n,
+                                          int mc, int lane, float (*acc)[kProjMaxM]) {
   const float4* x4 = reinterpret_cast<const float4*>(xs);
   const int units = n / 16, n4 = n / 4;
-  for (int u = lane; u < units; u += 32) {
-    const uint4 q = __ldg(q16 + u);
-    const float d = __half2float(__ushort_as_half(__ldg(dv + (u >> 1))));
-    const float4 a = s8x4(q.x), b = s8x4(q.y), c = s8x4(q.z), e = s8x4(q.w);
+  for (int u0 = lane; u0 < units; u0 += 32 * U) {
+    uint4 q[U][R];
+    unsigned short dh[U][R];
 #pragma unroll
-    for (int m = 0; m < kProjMaxM; ++m)
-      if (m < mc) {
-        const float4* xm = x4 + m * n4 + 4 * u;
-        const float s = dot4(e, xm[3], dot4(c, xm[2], dot4(b, xm[1], dot4(a, xm[0], 0.f))));
-        acc[m] = fmaf(d, s, acc[m]);
+    for (int k = 0; k < U; ++k)
+#pragma unroll
+      for (int i = 0; i < R; ++i) {
+        const int u = u0 + 32 * k < units ? u0 + 32 * k : u0;
+        q[k][i] = __ldg(reinterpret_cast<const uint4*>(w0 + i * rb) + u);
+        dh[k][i] = __ldg(reinterpret_cast<const unsigned short*>(w0 + i * rb + n) + (u >> 1));
       }
+#pragma unroll
+    for (int k = 0; k < U; ++k) {
+      const int u = u0 + 32 * k;
+      if (u >= units) break;
+      // int8 quants: flip the sign bit to get q + 128 as an unsigned byte
+      float4 qa[R], qb[R], qc[R], qd[R];
+      float d[R];
+#pragma unroll
+      for (int i = 0; i < R; ++i) {
+        qa[i] = bytes_to_f4(q[k][i].x ^ 0x80808080u, 128.f);
+        qb[i] = bytes_to_f4(q[k][i].y ^ 0x80808080u, 128.f);
+        qc[i] = bytes_to_f4(q[k][i].z ^ 0x80808080u, 128.f);
+        qd[i] = bytes_to_f4(q[k][i].w ^ 0x80808080u, 128.f);
+        d[i] = __half2float(__ushort_as_half(dh[k][i]));
+      }
+#pragma unroll
+      for (int m = 0; m < kProjMaxM; ++m)
+        if (m < mc) {
+          const float4* xm = x4 + m * n4 + 4 * u;
+          const float4 x0 = xm[0], x1 = xm[1], x2 = xm[2], x3 = xm[3];
+#pragma unroll
+          for (int i = 0; i < R; ++i) {
+            const float s = dot4(qd[i], x3, dot4(qc[i], x2, dot4(qb[i], x1, dot4(qa[i], x0, 0.f))));
+            acc[i][m] = fmaf(d[i], s, acc[i][m]);
+          }
+        }
+    }
   }
-}
-
-__device__ __forceinline__ float4 nib4(uint32_t w, int shift) {
-  return make_float4(static_cast<float>((w >> shift) & 0xFu),
-                     static_cast<float>((w >> (shift + 8)) & 0xFu),
-                     static_cast<float>((w >> (shift + 16)) & 0xFu),
-                     static_cast<float>((w >> (shift + 24)) & 0xFu));
 }
 
 // Q4_K: a unit is 8 quant bytes of one 32-byte pair j of a block: their low
 // nibbles weigh x of sub-block 2j, their high nibbles x of sub-block 2j+1
 // (quant.c:96-128, 388-512).
-__device__ __forceinline__ void row_q4k(const uint8_t* wr, const float* xs, int n, int mc,
-                                        int lane, float* acc) {
+template <int R, int U>
+__device__ __forceinline__ void rows_q4k(const uint8_t* w0, size_t rb, const float* xs, int n,
+                                         int mc, int lane, float (*acc)[kProjMaxM]) {
   const float4* x4 = reinterpret_cast<const float4*>(xs);
   const int units = n / 16, n4 = n / 4;
-  for (int u = lane; u < units; u += 32) {
-    const int b = u >> 4, t = u & 15, j = t >> 2, part = t & 3;
-    const uint8_t* blk = wr + static_cast<size_t>(b) * kQ4KBytes;
-    const uint4 hdr = __ldg(reinterpret_cast<const uint4*>(blk));
-    const uint2 q = __ldg(reinterpret_cast<const uint2*>(blk + 16 + j * 32 + part * 8));
-    const float d = f16_bits(hdr.x & 0xFFFFu), dmin = f16_bits(hdr.x >> 16);
-    float sc, mn;
-    scale_min_k4(2 * j, hdr.y, hdr.z, hdr.w, sc, mn);
-    const float d1 = d * sc, m1 = dmin * mn;
-    scale_min_k4(2 * j + 1, hdr.y, hdr.z, hdr.w, sc, mn);
-    const float d2 = d * sc, m2 = dmin * mn;
-    const float4 l0 = nib4(q.x, 0), l1 = nib4(q.y, 0), h0 = nib4(q.x, 4), h1 = nib4(q.y, 4);
-    const int xo = (b * 256 + j * 64 + part * 8) / 4;  // float4 index of the low-nibble x
+  for (int u0 = lane; u0 < units; u0 += 32 * U) {
+    uint4 hdr[U][R];
+    uint2 q[U][R];
 #pragma unroll
-    for (int m = 0; m < kProjMaxM; ++m)
-      if (m < mc) {
-        const float4* xm = x4 + m * n4 + xo;
-        const float4 xa = xm[0], xb = xm[1], xc = xm[8], xd = xm[9];
-        const float sqx1 = dot4(l1, xb, dot4(l0, xa, 0.f));
-        const float sqx2 = dot4(h1, xd, dot4(h0, xc, 0.f));
-        const float sx1 = sum4(xa) + sum4(xb), sx2 = sum4(xc) + sum4(xd);
-        acc[m] += d1 * sqx1 - m1 * sx1 + d2 * sqx2 - m2 * sx2;
+    for (int k = 0; k < U; ++k)
+#pragma unroll
+      for (int i = 0; i < R; ++i) {
+        const int u = u0 + 32 * k < units ? u0 + 32 * k : u0;
+        const int b = u >> 4, t = u & 15;
+        const uint8_t* blk = w0 + i * rb + static_cast<size_t>(b) * kQ4KBytes;
+        hdr[k][i] = __ldg(reinterpret_cast<const uint4*>(blk));
+        q[k][i] = __ldg(reinterpret_cast<const uint2*>(blk + 16 + (t >> 2) * 32 + (t & 3) * 8));
       }
-  }
-}
-
-__device__ __forceinline__ float4 q6x4(uint32_t ql, uint32_t qh, int lshift, int hshift) {
-  float v[4];
 #pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const int q = static_cast<int>(((ql >> (8 * i + lshift)) & 0xFu) |
-                                   (((qh >> (8 * i + hshift)) & 3u) << 4)) - 32;
-    v[i] = static_cast<float>(q);
+    for (int k = 0; k < U; ++k) {
+      const int u = u0 + 32 * k;
+      if (u >= units) break;
+      const int b = u >> 4, t = u & 15, j = t >> 2, part = t & 3;
+      float4 l0[R], l1[R], h0[R], h1[R];
+      float d1[R], m1[R], d2[R], m2[R];
+#pragma unroll
+      for (int i = 0; i < R; ++i) {
+        const float d = f16_bits(hdr[k][i].x & 0xFFFFu), dmin = f16_bits(hdr[k][i].x >> 16);
+        float sc, mn;
+        scale_min_k4(2 * j, hdr[k][i].y, hdr[k][i].z, hdr[k][i].w, sc, mn);
+        d1[i] = d * sc;
+        m1[i] = dmin * mn;
+        scale_min_k4(2 * j + 1, hdr[k][i].y, hdr[k][i].z, hdr[k][i].w, sc, mn);
+        d2[i] = d * sc;
+        m2[i] = dmin * mn;
+        l0[i] = bytes_to_f4(q[k][i].x & 0x0F0F0F0Fu, 0.f);
+        l1[i] = bytes_to_f4(q[k][i].y & 0x0F0F0F0Fu, 0.f);
+        h0[i] = bytes_to_f4((q[k][i].x >> 4) & 0x0F0F0F0Fu, 0.f);
+        h1[i] = bytes_to_f4((q[k][i].y >> 4) & 0x0F0F0F0Fu, 0.f);
+      }
+      const int xo = (b * 256 + j * 64 + part * 8) / 4;  // float4 index of the low-nibble x
+#pragma unroll
+      for (int m = 0; m < kProjMaxM; ++m)
+        if (m < mc) {
+          const float4* xm = x4 + m * n4 + xo;
+          const float4 xa = xm[0], xb = xm[1], xc = xm[8], xd = xm[9];
+          const float sx1 = sum4(xa) + sum4(xb), sx2 = sum4(xc) + sum4(xd);
+#pragma unroll
+          for (int i = 0; i < R; ++i) {
+            const float sqx1 = dot4(l1[i], xb, dot4(l0[i], xa, 0.f));
+            const float sqx2 = dot4(h1[i], xd, dot4(h0[i], xc, 0.f));
+            acc[i][m] += d1[i] * sqx1 - m1[i] * sx1 + d2[i] * sqx2 - m2[i] * sx2;
+          }
+        }
+    }
   }
-  return make_float4(v[0], v[1], v[2], v[3]);
 }
 
 // Q6_K: a unit is 4 consecutive l of one 128-weight half c of a block; each
 // l carries four weights (l, l+32, l+64, l+96 of the half), in four scale
-// groups of 16 (quant.c:193-222, 517-625).
-__device__ __forceinline__ void row_q6k(const uint8_t* wr, const float* xs, int n, int mc,
-                                        int lane, float* acc) {
+// groups of 16 (quant.c:193-222, 517-625).  Quant bytes q + 32 = low 4 bits
+// from ql, high 2 from qh, assembled four at a time.
+template <int R, int U>
+__device__ __forceinline__ void rows_q6k(const uint8_t* w0, size_t rb, const float* xs, int n,
+                                         int mc, int lane, float (*acc)[kProjMaxM]) {
   const float4* x4 = reinterpret_cast<const float4*>(xs);
   const int units = n / 16, n4 = n / 4;
-  for (int u = lane; u < units; u += 32) {
-    const int b = u >> 4, t = u & 15, c = t >> 3, lg = (t & 7) * 4;
-    const uint8_t* blk = wr + static_cast<size_t>(b) * kQ6KBytes;
-    const uint32_t qla = __ldg(reinterpret_cast<const uint32_t*>(blk + c * 64 + lg));
-    const uint32_t qlb = __ldg(reinterpret_cast<const uint32_t*>(blk + c * 64 + 32 + lg));
-    const uint32_t qh = __ldg(reinterpret_cast<const uint32_t*>(blk + 128 + c * 32 + lg));
-    const int is = c * 8 + lg / 16;
-    const int8_t* scl = reinterpret_cast<const int8_t*>(blk + 192);
-    const float d = __half2float(__ushort_as_half(__ldg(reinterpret_cast<const unsigned short*>(blk + 208))));
-    const float s0 = d * static_cast<float>(__ldg(scl + is)),
-                s1 = d * static_cast<float>(__ldg(scl + is + 2)),
-                s2 = d * static_cast<float>(__ldg(scl + is + 4)),
-                s3 = d * static_cast<float>(__ldg(scl + is + 6));
-    const float4 q1 = q6x4(qla, qh, 0, 0), q2 = q6x4(qlb, qh, 0, 2), q3 = q6x4(qla, qh, 4, 4),
-                 q4 = q6x4(qlb, qh, 4, 6);
-    const int xo = (b * 256 + c * 128 + lg) / 4;
+  for (int u0 = lane; u0 < units; u0 += 32 * U) {
+    uint32_t qla[U][R], qlb[U][R], qh[U][R], scw[U][R];
+    unsigned short dh[U][R];
 #pragma unroll
-    for (int m = 0; m < kProjMaxM; ++m)
-      if (m < mc) {
-        const float4* xm = x4 + m * n4 + xo;
-        float s = s0 * dot4(q1, xm[0], 0.f);
-        s = fmaf(s1, dot4(q2, xm[8], 0.f), s);
-        s = fmaf(s2, dot4(q3, xm[16], 0.f), s);
-        s = fmaf(s3, dot4(q4, xm[24], 0.f), s);
-        acc[m] += s;
+    for (int k = 0; k < U; ++k)
+#pragma unroll
+      for (int i = 0; i < R; ++i) {
+        const int u = u0 + 32 * k < units ? u0 + 32 * k : u0;
+        const int b = u >> 4, t = u & 15, c = t >> 3, lg = (t & 7) * 4;
+        const uint8_t* blk = w0 + i * rb + static_cast<size_t>(b) * kQ6KBytes;
+        qla[k][i] = __ldg(reinterpret_cast<const uint32_t*>(blk + c * 64 + lg));
+        qlb[k][i] = __ldg(reinterpret_cast<const uint32_t*>(blk + c * 64 + 32 + lg));
+        qh[k][i] = __ldg(reinterpret_cast<const uint32_t*>(blk + 128 + c * 32 + lg));
+        // scales is, is+2, is+4, is+6 (is = 8c + lg/16): bytes of two words
+        const uint32_t* sw = reinterpret_cast<const uint32_t*>(blk + 192 + c * 8);
+        scw[k][i] = (lg < 16) ? __byte_perm(__ldg(sw), __ldg(sw + 1), 0x6420)
+                              : __byte_perm(__ldg(sw), __ldg(sw + 1), 0x7531);
+        dh[k][i] = __ldg(reinterpret_cast<const unsigned short*>(blk + 208));
       }
+#pragma unroll
+    for (int k = 0; k < U; ++k) {
+      const int u = u0 + 32 * k;
+      if (u >= units) break;
+      const int b = u >> 4, t = u & 15, c = t >> 3, lg = (t & 7) * 4;
+      float4 q1[R], q2[R], q3[R], q4[R];
+      float s0[R], s1[R], s2[R], s3[R];
+#pragma unroll
+      for (int i = 0; i < R; ++i) {
+        const uint32_t la = qla[k][i], lb = qlb[k][i], h = qh[k][i];
+        q1[i] = bytes_to_f4((la & 0x0F0F0F0Fu) | ((h & 0x03030303u) << 4), 32.f);
+        q2[i] = bytes_to_f4((lb & 0x0F0F0F0Fu) | (((h >> 2) & 0x03030303u) << 4), 32.f);
+        q3[i] = bytes_to_f4(((la >> 4) & 0x0F0F0F0Fu) | (((h >> 4) & 0x03030303u) << 4), 32.f);
+        q4[i] = bytes_to_f4(((lb >> 4) & 0x0F0F0F0Fu) | (((h >> 6) & 0x03030303u) << 4), 32.f);
+        const float d = __half2float(__ushort_as_half(dh[k][i]));
+        const uint32_t sc = scw[k][i];
+        s0[i] = d * static_cast<float>(static_cast<int8_t>(sc & 0xFFu));
+        s1[i] = d * static_cast<float>(static_cast<int8_t>((sc >> 8) & 0xFFu));
+        s2[i] = d * static_cast<float>(static_cast<int8_t>((sc >> 16) & 0xFFu));
+        s3[i] = d * static_cast<float>(static_cast<int8_t>(sc >> 24));
+      }
+      const int xo = (b * 256 + c * 128 + lg) / 4;
+#pragma unroll
+      for (int m = 0; m < kProjMaxM; ++m)
+        if (m < mc) {
+          const float4* xm = x4 + m * n4 + xo;
+          const float4 xa = xm[0], xb = xm[8], xc = xm[16], xd = xm[24];
+#pragma unroll
+          for (int i = 0; i < R; ++i) {
+            float s = s0[i] * dot4(q1[i], xa, 0.f);
+            s = fmaf(s1[i], dot4(q2[i], xb, 0.f), s);
+            s = fmaf(s2[i], dot4(q3[i], xc, 0.f), s);
+            s = fmaf(s3[i], dot4(q4[i], xd, 0.f), s);
+            acc[i][m] += s;
+          }
+        }
+    }
   }
 }
 
-// grid = (ceil(total_rows / kProjWarps), ceil(M / mc)), block = kProjThreads,
-// dynamic shared memory mc * n * 4 bytes.  The CTA stages its mc input rows
-// (normalised when norm_w is set) in shared memory; warp w then computes
-// output row blockIdx.x * kProjWarps + w for all of them.
+// grid = (ceil(total_rows / (kProjWarps * R)), ceil(M / mc)), block =
+// kProjThreads, dynamic shared memory mc * n * 4 bytes.  The CTA stages its
+// mc input rows (normalised when norm_w is set) in shared memory; warp w
+// then computes output rows (blockIdx.x * kProjWarps + w) * R .. + R - 1,
+// which lie in one matrix (every matrix's row count is a multiple of R).
+template <int R>
 __global__ void __launch_bounds__(kProjThreads) proj_kernel(const __grid_constant__ ProjArgs a) {
   extern __shared__ float4 proj_xs4[];
   float* xs = reinterpret_cast<float*>(proj_xs4);
@@ -316,7 +433,7 @@ __global__ void __launch_bounds__(kProjThreads) proj_kernel(const __grid_constan
     }
   }
   __syncthreads();
-  const int row = blockIdx.x * kProjWarps + warp;
+  const int row = (blockIdx.x * kProjWarps + warp) * R;
   if (row >= a.total_rows) return;
   int mi = 0, r = row;
   while (mi + 1 < a.n_mat && r >= a.mat[mi].rows) {
@@ -325,33 +442,40 @@ __global__ void __launch_bounds__(kProjThreads) proj_kernel(const __grid_constan
   }
   const ProjMat& mt = a.mat[mi];
   const uint8_t* wr = mt.w + static_cast<size_t>(r) * mt.row_bytes;
-  float acc[kProjMaxM];
+  constexpr int kU = R == 1 ? 2 : 1;  // one row per warp: two units' loads in flight
+  float acc[R][kProjMaxM];
 #pragma unroll
-  for (int m = 0; m < kProjMaxM; ++m) acc[m] = 0.f;
+  for (int i = 0; i < R; ++i)
+#pragma unroll
+    for (int m = 0; m < kProjMaxM; ++m) acc[i][m] = 0.f;
   switch (mt.type) {
-    case kGgufF32: row_f32(wr, xs, a.n, mc, lane, acc); break;
-    case kGgufF16: row_f16(wr, xs, a.n, mc, lane, acc); break;
-    case kGgufQ8_0: row_q8_0(wr, xs, a.n, mc, lane, acc); break;
-    case kGgufQ4K: row_q4k(wr, xs, a.n, mc, lane, acc); break;
-    default: row_q6k(wr, xs, a.n, mc, lane, acc); break;
+    case kGgufF32: rows_f32<R, kU>(wr, mt.row_bytes, xs, a.n, mc, lane, acc); break;
+    case kGgufF16: rows_f16<R, kU>(wr, mt.row_bytes, xs, a.n, mc, lane, acc); break;
+    case kGgufQ8_0: rows_q8_0<R, kU>(wr, mt.row_bytes, xs, a.n, mc, lane, acc); break;
+    case kGgufQ4K: rows_q4k<R, kU>(wr, mt.row_bytes, xs, a.n, mc, lane, acc); break;
+    default: rows_q6k<R, kU>(wr, mt.row_bytes, xs, a.n, mc, lane, acc); break;
   }
+  // lane i * 8 + m ends up holding the total of (row i, input row m)
   float mine = 0.f;
 #pragma unroll
-  for (int m = 0; m < kProjMaxM; ++m) {
-    if (m < mc) {
-      float s = acc[m];
+  for (int i = 0; i < R; ++i)
 #pragma unroll
-      for (int o = 16; o; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
-      if (lane == m) mine = s;
+    for (int m = 0; m < kProjMaxM; ++m) {
+      if (m < mc) {
+        float s = acc[i][m];
+#pragma unroll
+        for (int o = 16; o; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+        if (lane == i * kProjMaxM + m) mine = s;
+      }
     }
-  }
-  if (lane < mc) {
+  const int i = lane / kProjMaxM, m = lane % kProjMaxM;
+  if (i < R && m < mc) {
     // matmul_bias (tensor.c:230-238): out = W x, then out += b; the residual
     // add of model.c:897 is x += out
     float v = mine;
-    if (mt.bias) v = v + __ldg(mt.bias + r);
-    if (a.resid) v = a.resid[static_cast<size_t>(m0 + lane) * a.ld_res + r] + v;
-    mt.out[static_cast<size_t>(m0 + lane) * mt.ld_out + r] = v;
+    if (mt.bias) v = v + __ldg(mt.bias + r + i);
+    if (a.resid) v = a.resid[static_cast<size_t>(m0 + m) * a.ld_res + r + i] + v;
+    mt.out[static_cast<size_t>(m0 + m) * mt.ld_out + r + i] = v;
   }
 }
 

@@ -1365,7 +1365,9 @@ int ensure_blk(size_t floats) {
 }
 
 // one launch of proj_kernel; mc (input rows per CTA) as large as the staged
-// rows fit in shared memory, at most kProjMaxM
+// rows fit in shared memory, at most kProjMaxM.  With a few input rows a
+// warp takes one output row (most CTAs for a latency-bound GEMV); with more,
+// four rows that share its reads of the staged x.
 int launch_proj(pl::ProjArgs a, cudaStream_t st) {
   const size_t row_b = static_cast<size_t>(a.n) * sizeof(float);
   long long mc = pl::kProjSmemCap / static_cast<long long>(row_b);
@@ -1374,14 +1376,23 @@ int launch_proj(pl::ProjArgs a, cudaStream_t st) {
   if (mc < 1) return PL_EUNSUPPORTED;
   a.mc = static_cast<int>(mc);
   const long long gy = (a.M + mc - 1) / mc;
-  const int gx = (a.total_rows + pl::kProjWarps - 1) / pl::kProjWarps;
   if (gy > 65535) return PL_EUNSUPPORTED;
+  bool by4 = a.M >= 4;
+  for (int i = 0; i < a.n_mat; ++i) by4 = by4 && a.mat[i].rows % 4 == 0;
+  const int rows_per_cta = pl::kProjWarps * (by4 ? 4 : 1);
+  const int gx = (a.total_rows + rows_per_cta - 1) / rows_per_cta;
   if (!g->proj_smem_set) {
-    PL_CUDA(cudaFuncSetAttribute(pl::proj_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    PL_CUDA(cudaFuncSetAttribute(pl::proj_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 pl::kProjSmemCap));
+    PL_CUDA(cudaFuncSetAttribute(pl::proj_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  pl::kProjSmemCap));
     g->proj_smem_set = true;
   }
-  pl::proj_kernel<<<dim3(gx, static_cast<unsigned>(gy)), pl::kProjThreads, mc * row_b, st>>>(a);
+  const dim3 grid(gx, static_cast<unsigned>(gy));
+  if (by4)
+    pl::proj_kernel<4><<<grid, pl::kProjThreads, mc * row_b, st>>>(a);
+  else
+    pl::proj_kernel<1><<<grid, pl::kProjThreads, mc * row_b, st>>>(a);
   PL_CUDA(cudaGetLastError());
   count_launch();
   return PL_OK;
