@@ -777,12 +777,13 @@ def run_long_ctx_heads(args, rank, world, local, peaks):
 
 def random_q4k(rng, rows: int, n: int) -> np.ndarray:
     """Raw GGUF Q4_K rows (picolm/quant.h:65-72) with dequantised weights of
-    standard deviation about 0.02: random quants and 6-bit scales, FP16 d
-    and dmin."""
+    mean about 0 and standard deviation about 0.02: random quants and 6-bit
+    scales, FP16 d and dmin = 7.5 d (which centres d*sc*q - dmin*mn)."""
     nb = rows * n // 256
     blk = rng.integers(0, 256, (nb, 144), dtype=np.uint8)
-    d = (rng.uniform(0.5, 1.5, nb) * 0.02 / 180).astype(np.float16).view(np.uint8)
-    dmin = (rng.uniform(0.5, 1.5, nb) * 0.02 / 60).astype(np.float16).view(np.uint8)
+    d32 = rng.uniform(0.5, 1.5, nb) * 0.02 / 260
+    d = d32.astype(np.float16).view(np.uint8)
+    dmin = (d32 * 7.5).astype(np.float16).view(np.uint8)
     blk[:, 0:2] = d.reshape(-1, 2)
     blk[:, 2:4] = dmin.reshape(-1, 2)
     return blk.reshape(rows, -1)

@@ -121,6 +121,11 @@ def cfg(n_heads, n_kv_heads, head_dim, max_seq, rope_type=0) -> OrcCfg:
     return OrcCfg(n_heads, n_kv_heads, head_dim, max_seq, rope_type)
 
 
+def ctypes_ref(c: OrcCfg):
+    """A config as the pointer argument of the orc_* functions."""
+    return C.byref(c)
+
+
 def fp32_to_fp16(x: np.ndarray) -> np.ndarray:
     x = np.ascontiguousarray(x, dtype=np.float32).ravel()
     out = np.empty(x.size, np.uint16)

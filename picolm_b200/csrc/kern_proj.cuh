@@ -19,6 +19,8 @@
 #include <cstdint>
 #include <cuda_fp16.h>
 
+#include "sm100.cuh"
+
 namespace pl {
 
 // GGUF tensor type ids (picolm/quant.h:49-63) that the projections take
@@ -79,6 +81,11 @@ struct ProjArgs {
   const float* resid;  // out = resid + (W x + b) when set (in place allowed: resid == out)
   int ld_res;
   int mc;              // input rows per CTA; grid.y = ceil(M / mc)
+  // tensor-core path with the inputs split over grid.z slices: slice z
+  // writes its raw partial sums to part[(z * M + m) * total_rows + launch
+  // row], and proj_reduce_kernel adds the slices, bias and residual
+  float* part;
+  int ksplit;
 };
 
 __device__ __forceinline__ float f16_bits(uint32_t h) {
@@ -477,6 +484,342 @@ __global__ void __launch_bounds__(kProjThreads) proj_kernel(const __grid_constan
     if (a.resid) v = a.resid[static_cast<size_t>(m0 + m) * a.ld_res + r + i] + v;
     mt.out[static_cast<size_t>(m0 + m) * mt.ld_out + r + i] = v;
   }
+}
+
+// ---------------------------------------------------------------------------
+// The same projections on the tensor cores, for 16 or more input rows
+// (batched decode, prefill) and Q4_K, Q8_0 or F16 weights.
+//
+// mma.sync m16n8k16 (FP16 in, FP32 accumulate) with the quants as the A
+// operand and x as B.  Quants are small integers, exact in FP16; x is split
+// into an FP16 high part and the FP16 rounding of its residual (two MMAs),
+// which carries it to about 2^-22.  So an MMA over one scale group gives
+// sum(q * x) of that group at FP32 accuracy, and the group's scale (and, for
+// Q4_K, min * sum(x)) is applied to the FP32 fragment: the factored form of
+// picolm's vec_dot, with the products summed by the tensor core.  Scales
+// vary every 32 inputs, so they must be applied to partial sums per group;
+// register fragments allow that, a TMEM accumulator would not without a
+// round trip per group.
+//
+// CTA: kMmaWarps warps of 16 output rows each, kMmaN input rows (two n8
+// tiles).  Per chunk of kMmaKC inputs the CTA stages the input rows
+// (normalised when norm_w is set) as FP16 hi and lo, row pitch padded by 16
+// bytes so that ldmatrix reads are conflict-free, plus sum(x) of every
+// 32-input group.  A lane loads the 32-byte quant runs of its rows g and
+// g + 8 straight from global memory (the four lanes of a row share them).
+constexpr int kMmaWarps = 4;
+constexpr int kMmaThreads = 32 * kMmaWarps;
+constexpr int kMmaRows = 16 * kMmaWarps;   // output rows per CTA
+constexpr int kMmaN = 16;                  // input rows per CTA
+constexpr int kMmaKC = 256;                // inputs per staged chunk
+constexpr int kMmaPitch = kMmaKC + 8;      // halves per staged row
+
+__host__ __device__ inline bool proj_mma_type(int type) {
+  return type == kGgufQ4K || type == kGgufQ8_0 || type == kGgufF16;
+}
+
+struct MmaStage {
+  uint16_t hi[kMmaN][kMmaPitch];
+  uint16_t lo[kMmaN][kMmaPitch];
+  float xsum[kMmaN][kMmaKC / 32];
+  float inv_rms[kMmaN];
+  float ss_part[kMmaWarps][kMmaN];
+};
+
+// two FP16 quants (as 1024 + q, exact) -> subtract 1024 + bias
+__device__ __forceinline__ uint32_t h2_sub(uint32_t p, float bias) {
+  const __half2 r = __hsub2(*reinterpret_cast<const __half2*>(&p),
+                            __float2half2_rn(1024.f + bias));
+  return *reinterpret_cast<const uint32_t*>(&r);
+}
+// the low (hi_nib = 0) or high nibbles of the two bytes of v as an FP16 pair
+__device__ __forceinline__ uint32_t nib_pair(uint32_t v, int hi_nib) {
+  const uint32_t p = hi_nib ? (((v >> 4) & 0x000Fu) | ((v & 0xF000u) << 4))
+                            : ((v & 0x000Fu) | ((v & 0x0F00u) << 8));
+  return h2_sub(p | 0x64006400u, 0.f);
+}
+// the two int8 bytes of v as an FP16 pair
+__device__ __forceinline__ uint32_t s8_pair(uint32_t v) {
+  const uint32_t u = v ^ 0x8080u;
+  return h2_sub(((u & 0x00FFu) | ((u & 0xFF00u) << 8)) | 0x64006400u, 128.f);
+}
+// 16-bit half `h` of word w of a 32-byte run held as two uint4
+__device__ __forceinline__ uint32_t run_u16(const uint4 (&r)[2], int w, int h) {
+  const uint4 v = r[w >> 2];
+  const uint32_t x = (w & 3) == 0 ? v.x : (w & 3) == 1 ? v.y : (w & 3) == 2 ? v.z : v.w;
+  return (x >> (16 * h)) & 0xFFFFu;
+}
+
+// A fragment of the k-step ks (16 inputs) of a 32-input run for rows g and
+// g + 8: bytes 16ks + 2t, +1 (a0a1 / a2a3) and 16ks + 2t + 8, +9 (a4a5 / a6a7)
+template <typename F>
+__device__ __forceinline__ void a_frag(const uint4 (&rg)[2], const uint4 (&rg8)[2], int ks, int t,
+                                       F conv, uint32_t (&a)[4]) {
+  const int w0 = 4 * ks + (t >> 1), w1 = w0 + 2, h = t & 1;
+  a[0] = conv(run_u16(rg, w0, h));
+  a[1] = conv(run_u16(rg8, w0, h));
+  a[2] = conv(run_u16(rg, w1, h));
+  a[3] = conv(run_u16(rg8, w1, h));
+}
+
+// B fragments (hi and lo) of both n8 tiles for inputs kk .. kk+15 of the chunk
+__device__ __forceinline__ void b_frags(const MmaStage& st, int kk, int lane, uint32_t (&bh)[4],
+                                        uint32_t (&bl)[4]) {
+  const int mi = lane >> 3, n = (mi >> 1) * 8 + (lane & 7), ko = (mi & 1) * 8;
+  ldmatrix_x4(smem_u32(&st.hi[n][kk + ko]), bh[0], bh[1], bh[2], bh[3]);
+  ldmatrix_x4(smem_u32(&st.lo[n][kk + ko]), bl[0], bl[1], bl[2], bl[3]);
+}
+
+__device__ __forceinline__ void mma_hilo(float (&c)[2][4], const uint32_t (&a)[4],
+                                         const uint32_t (&bh)[4], const uint32_t (&bl)[4]) {
+  mma_16816(c[0], a, bh[0], bh[1]);
+  mma_16816(c[0], a, bl[0], bl[1]);
+  mma_16816(c[1], a, bh[2], bh[3]);
+  mma_16816(c[1], a, bl[2], bl[3]);
+}
+
+// acc += scale_row * c - min_row * sum(x) for both n8 tiles (rows g, g + 8;
+// input rows 8nt + 2t, +1)
+__device__ __forceinline__ void apply_group(float (&acc)[2][4], const float (&c)[2][4], float dg,
+                                            float dg8, float mg, float mg8, const MmaStage& st,
+                                            int grp, int t) {
+#pragma unroll
+  for (int nt = 0; nt < 2; ++nt) {
+    const float s0 = st.xsum[8 * nt + 2 * t][grp], s1 = st.xsum[8 * nt + 2 * t + 1][grp];
+    acc[nt][0] += dg * c[nt][0] - mg * s0;
+    acc[nt][1] += dg * c[nt][1] - mg * s1;
+    acc[nt][2] += dg8 * c[nt][2] - mg8 * s0;
+    acc[nt][3] += dg8 * c[nt][3] - mg8 * s1;
+  }
+}
+
+// one staged chunk (inputs k0 .. k0 + kMmaKC) of a warp's 16 rows
+__device__ __forceinline__ void mma_chunk(int type, const uint8_t* wg, const uint8_t* wg8, int n,
+                                          int k0, const MmaStage& st, int lane,
+                                          float (&acc)[2][4]) {
+  const int t = lane & 3;
+  if (type == kGgufQ4K) {
+    // one super-block: four runs of 32 quant bytes, each the low nibbles of
+    // sub-block 2j and the high nibbles of sub-block 2j + 1
+    const uint8_t* bg = wg + static_cast<size_t>(k0 / 256) * kQ4KBytes;
+    const uint8_t* bg8 = wg8 + static_cast<size_t>(k0 / 256) * kQ4KBytes;
+    const uint4 hg = __ldg(reinterpret_cast<const uint4*>(bg));
+    const uint4 hg8 = __ldg(reinterpret_cast<const uint4*>(bg8));
+    const float d_g = f16_bits(hg.x & 0xFFFFu), dm_g = f16_bits(hg.x >> 16);
+    const float d_g8 = f16_bits(hg8.x & 0xFFFFu), dm_g8 = f16_bits(hg8.x >> 16);
+    // all four runs of both rows in flight before any arithmetic
+    uint4 qg[4][2], qg8[4][2];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      qg[j][0] = __ldg(reinterpret_cast<const uint4*>(bg + 16 + 32 * j));
+      qg[j][1] = __ldg(reinterpret_cast<const uint4*>(bg + 32 + 32 * j));
+      qg8[j][0] = __ldg(reinterpret_cast<const uint4*>(bg8 + 16 + 32 * j));
+      qg8[j][1] = __ldg(reinterpret_cast<const uint4*>(bg8 + 32 + 32 * j));
+    }
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const uint4(&rg)[2] = qg[j];
+      const uint4(&rg8)[2] = qg8[j];
+#pragma unroll
+      for (int hn = 0; hn < 2; ++hn) {
+        const int sb = 2 * j + hn;
+        float sc, mn, sc8, mn8;
+        scale_min_k4(sb, hg.y, hg.z, hg.w, sc, mn);
+        scale_min_k4(sb, hg8.y, hg8.z, hg8.w, sc8, mn8);
+        float c[2][4] = {};
+#pragma unroll
+        for (int ks = 0; ks < 2; ++ks) {
+          uint32_t a[4], bh[4], bl[4];
+          a_frag(rg, rg8, ks, t, [hn](uint32_t v) { return nib_pair(v, hn); }, a);
+          b_frags(st, 32 * sb + 16 * ks, lane, bh, bl);
+          mma_hilo(c, a, bh, bl);
+        }
+        apply_group(acc, c, d_g * sc, d_g8 * sc8, dm_g * mn, dm_g8 * mn8, st, sb, t);
+      }
+    }
+  } else if (type == kGgufQ8_0) {
+    // eight blocks of 32: quants at [k], the block's scale after all quants;
+    // four blocks' loads in flight at a time
+#pragma unroll 1
+    for (int b4 = 0; b4 < kMmaKC / 32; b4 += 4) {
+    uint4 qg[4][2], qg8[4][2];
+    unsigned short sg[4], sg8[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int k = k0 + 32 * (b4 + i);
+      qg[i][0] = __ldg(reinterpret_cast<const uint4*>(wg + k));
+      qg[i][1] = __ldg(reinterpret_cast<const uint4*>(wg + k + 16));
+      qg8[i][0] = __ldg(reinterpret_cast<const uint4*>(wg8 + k));
+      qg8[i][1] = __ldg(reinterpret_cast<const uint4*>(wg8 + k + 16));
+      sg[i] = __ldg(reinterpret_cast<const unsigned short*>(wg + n) + k / 32);
+      sg8[i] = __ldg(reinterpret_cast<const unsigned short*>(wg8 + n) + k / 32);
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int blk = b4 + i;
+      const uint4(&rg)[2] = qg[i];
+      const uint4(&rg8)[2] = qg8[i];
+      const float d_g = __half2float(__ushort_as_half(sg[i]));
+      const float d_g8 = __half2float(__ushort_as_half(sg8[i]));
+      float c[2][4] = {};
+#pragma unroll
+      for (int ks = 0; ks < 2; ++ks) {
+        uint32_t a[4], bh[4], bl[4];
+        a_frag(rg, rg8, ks, t, [](uint32_t v) { return s8_pair(v); }, a);
+        b_frags(st, 32 * blk + 16 * ks, lane, bh, bl);
+        mma_hilo(c, a, bh, bl);
+      }
+      apply_group(acc, c, d_g, d_g8, 0.f, 0.f, st, blk, t);
+    }
+    }
+  } else {
+    // F16 weights are the A operand as they are; no groups
+    const uint32_t* rg = reinterpret_cast<const uint32_t*>(wg) + k0 / 2;
+    const uint32_t* rg8 = reinterpret_cast<const uint32_t*>(wg8) + k0 / 2;
+    float c[2][4] = {};
+#pragma unroll 4
+    for (int ks = 0; ks < kMmaKC / 16; ++ks) {
+      uint32_t a[4], bh[4], bl[4];
+      a[0] = __ldg(rg + 8 * ks + t);
+      a[1] = __ldg(rg8 + 8 * ks + t);
+      a[2] = __ldg(rg + 8 * ks + t + 4);
+      a[3] = __ldg(rg8 + 8 * ks + t + 4);
+      b_frags(st, 16 * ks, lane, bh, bl);
+      mma_hilo(c, a, bh, bl);
+    }
+#pragma unroll
+    for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) acc[nt][e] += c[nt][e];
+  }
+}
+
+// grid = (ceil(total_rows / kMmaRows), ceil(M / kMmaN)), block = kMmaThreads.
+// Every matrix's row count is a multiple of 16 and n a multiple of kMmaKC
+// (the host checks).
+__global__ void __launch_bounds__(kMmaThreads) proj_mma_kernel(const __grid_constant__ ProjArgs a) {
+  __shared__ __align__(16) MmaStage st;
+  const int m0 = blockIdx.y * kMmaN;
+  const int mn = min(kMmaN, a.M - m0);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int n4 = a.n / 4;
+  // RMSNorm scale of each input row (tensor.c:425-490)
+  if (a.norm_w) {
+    float ss[kMmaN];
+#pragma unroll
+    for (int m = 0; m < kMmaN; ++m) {
+      ss[m] = 0.f;
+      if (m < mn) {
+        const float4* xr =
+            reinterpret_cast<const float4*>(a.x + static_cast<size_t>(m0 + m) * a.ldx);
+        for (int i4 = threadIdx.x; i4 < n4; i4 += kMmaThreads) {
+          const float4 v = __ldg(xr + i4);
+          ss[m] = fmaf(v.w, v.w, fmaf(v.z, v.z, fmaf(v.y, v.y, fmaf(v.x, v.x, ss[m]))));
+        }
+      }
+#pragma unroll
+      for (int o = 16; o; o >>= 1) ss[m] += __shfl_xor_sync(0xffffffffu, ss[m], o);
+      if (lane == 0) st.ss_part[warp][m] = ss[m];
+    }
+    __syncthreads();
+    if (threadIdx.x < kMmaN) {
+      float t = 0.f;
+#pragma unroll
+      for (int w = 0; w < kMmaWarps; ++w) t += st.ss_part[w][threadIdx.x];
+      st.inv_rms[threadIdx.x] = 1.0f / sqrtf(t / static_cast<float>(a.n) + a.eps);
+    }
+  }
+  // this warp's 16 rows, all in one matrix
+  const int row = (blockIdx.x * kMmaWarps + warp) * 16;
+  const bool active = row < a.total_rows;
+  int mi = 0, r = active ? row : 0;
+  while (mi + 1 < a.n_mat && r >= a.mat[mi].rows) {
+    r -= a.mat[mi].rows;
+    ++mi;
+  }
+  const ProjMat& mt = a.mat[mi];
+  const int g = lane >> 2, t = lane & 3;
+  const uint8_t* wg = mt.w + static_cast<size_t>(r + g) * mt.row_bytes;
+  const uint8_t* wg8 = mt.w + static_cast<size_t>(r + g + 8) * mt.row_bytes;
+  float acc[2][4] = {};
+  // this CTA's slice of the inputs (whole chunks)
+  const int n_chunks = a.n / kMmaKC;
+  const int c_lo = static_cast<int>(blockIdx.z) * n_chunks / a.ksplit;
+  const int c_hi = (static_cast<int>(blockIdx.z) + 1) * n_chunks / a.ksplit;
+  for (int k0 = c_lo * kMmaKC; k0 < c_hi * kMmaKC; k0 += kMmaKC) {
+    __syncthreads();  // the previous chunk's reads are done (and inv_rms is ready)
+    // stage inputs k0 .. k0 + kMmaKC of the input rows: FP16 hi / lo and
+    // the sum of every 32-input group (8 lanes = 32 consecutive inputs)
+    for (int idx = threadIdx.x; idx < kMmaN * (kMmaKC / 4); idx += kMmaThreads) {
+      const int m = idx / (kMmaKC / 4), c4 = idx - m * (kMmaKC / 4);
+      float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (m < mn) {
+        v = __ldg(reinterpret_cast<const float4*>(a.x + static_cast<size_t>(m0 + m) * a.ldx + k0) + c4);
+        if (a.norm_w) {
+          const float s = st.inv_rms[m];
+          const float4 w = __ldg(reinterpret_cast<const float4*>(a.norm_w + k0) + c4);
+          v = make_float4(__fmul_rn(__fmul_rn(v.x, s), w.x), __fmul_rn(__fmul_rn(v.y, s), w.y),
+                          __fmul_rn(__fmul_rn(v.z, s), w.z), __fmul_rn(__fmul_rn(v.w, s), w.w));
+        }
+      }
+      const __half2 h0 = __floats2half2_rn(v.x, v.y), h1 = __floats2half2_rn(v.z, v.w);
+      const float2 f0 = __half22float2(h0), f1 = __half22float2(h1);
+      const __half2 l0 = __floats2half2_rn(v.x - f0.x, v.y - f0.y);
+      const __half2 l1 = __floats2half2_rn(v.z - f1.x, v.w - f1.y);
+      *reinterpret_cast<uint2*>(&st.hi[m][4 * c4]) =
+          make_uint2(*reinterpret_cast<const uint32_t*>(&h0), *reinterpret_cast<const uint32_t*>(&h1));
+      *reinterpret_cast<uint2*>(&st.lo[m][4 * c4]) =
+          make_uint2(*reinterpret_cast<const uint32_t*>(&l0), *reinterpret_cast<const uint32_t*>(&l1));
+      float gs = sum4(v);
+      gs += __shfl_xor_sync(0xffffffffu, gs, 1);
+      gs += __shfl_xor_sync(0xffffffffu, gs, 2);
+      gs += __shfl_xor_sync(0xffffffffu, gs, 4);
+      if ((c4 & 7) == 0) st.xsum[m][c4 >> 3] = gs;
+    }
+    __syncthreads();
+    if (active) mma_chunk(mt.type, wg, wg8, a.n, k0, st, lane, acc);
+  }
+  if (!active) return;
+  // epilogue: (row r + g (+8), input row 8nt + 2t (+1)); matmul_bias then
+  // the residual add, as in proj_kernel, or the raw slice sums
+#pragma unroll
+  for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const int rr = r + g + (e >= 2 ? 8 : 0);
+      const int m = 8 * nt + 2 * t + (e & 1);
+      if (m >= mn) continue;
+      float v = acc[nt][e];
+      if (a.ksplit > 1) {
+        a.part[(static_cast<size_t>(blockIdx.z) * a.M + m0 + m) * a.total_rows + row + g +
+               (e >= 2 ? 8 : 0)] = v;
+        continue;
+      }
+      if (mt.bias) v = v + __ldg(mt.bias + rr);
+      if (a.resid) v = a.resid[static_cast<size_t>(m0 + m) * a.ld_res + rr] + v;
+      mt.out[static_cast<size_t>(m0 + m) * mt.ld_out + rr] = v;
+    }
+}
+
+// Sum of the ksplit slices of proj_mma_kernel in slice order (the result
+// does not depend on timing), then bias and residual.  One thread per
+// (input row, launch row).
+__global__ void __launch_bounds__(256) proj_reduce_kernel(const __grid_constant__ ProjArgs a) {
+  const size_t idx = static_cast<size_t>(blockIdx.x) * 256 + threadIdx.x;
+  if (idx >= static_cast<size_t>(a.M) * a.total_rows) return;
+  const int m = static_cast<int>(idx / a.total_rows);
+  const int row = static_cast<int>(idx - static_cast<size_t>(m) * a.total_rows);
+  float v = 0.f;
+  for (int z = 0; z < a.ksplit; ++z) v += a.part[(static_cast<size_t>(z) * a.M + m) * a.total_rows + row];
+  int mi = 0, r = row;
+  while (mi + 1 < a.n_mat && r >= a.mat[mi].rows) {
+    r -= a.mat[mi].rows;
+    ++mi;
+  }
+  const ProjMat& mt = a.mat[mi];
+  if (mt.bias) v = v + __ldg(mt.bias + r);
+  if (a.resid) v = a.resid[static_cast<size_t>(m) * a.ld_res + r] + v;
+  mt.out[static_cast<size_t>(m) * mt.ld_out + r] = v;
 }
 
 // QK-norm (model.c:807-817): RMSNorm of every q head with qn and every k head

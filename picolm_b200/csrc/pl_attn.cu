@@ -102,6 +102,8 @@ struct Ctx {
   std::vector<LayerW> lw;            // [n_layers]
   float* d_blk = nullptr;            // q, k, v, attention output of a block call
   size_t blk_cap = 0;                // floats
+  float* d_proj_part = nullptr;      // split-input partial sums of the projections
+  size_t proj_part_cap = 0;          // floats
   bool proj_smem_set = false;
 };
 
@@ -592,6 +594,7 @@ void free_ctx(Ctx* c) {
   cudaFree(c->d_q16);
   cudaFree(c->d_err);
   cudaFree(c->d_blk);
+  cudaFree(c->d_proj_part);
   for (LayerW& l : c->lw) cudaFree(l.mem);
   for (cudaEvent_t e : c->ev_pool) cudaEventDestroy(e);
   if (c->stream) cudaStreamDestroy(c->stream);
@@ -1364,11 +1367,56 @@ int ensure_blk(size_t floats) {
   return PL_OK;
 }
 
-// one launch of proj_kernel; mc (input rows per CTA) as large as the staged
-// rows fit in shared memory, at most kProjMaxM.  With a few input rows a
-// warp takes one output row (most CTAs for a latency-bound GEMV); with more,
-// four rows that share its reads of the staged x.
-int launch_proj(pl::ProjArgs a, cudaStream_t st) {
+// One projection launch.  With 16 or more input rows, Q4_K / Q8_0 / F16
+// weights and tile-aligned shapes, proj_mma_kernel (tensor cores; x passes
+// as FP16 high part and residual, so |x| must stay below 65504: true of
+// RMSNorm outputs and attention outputs, which is why only the block calls
+// allow it).  Otherwise proj_kernel: mc (input rows per CTA) as large as the
+// staged rows fit in shared memory, at most kProjMaxM; with a few input
+// rows a warp takes one output row (most CTAs for a latency-bound GEMV),
+// with more, four rows that share its reads of the staged x.
+int launch_proj(pl::ProjArgs a, cudaStream_t st, bool allow_mma) {
+  bool mma = allow_mma && a.M >= pl::kMmaN && a.n % pl::kMmaKC == 0;
+  for (int i = 0; i < a.n_mat; ++i)
+    mma = mma && pl::proj_mma_type(a.mat[i].type) && a.mat[i].rows % 16 == 0;
+  if (mma) {
+    const long long gy = (a.M + pl::kMmaN - 1) / pl::kMmaN;
+    if (gy > 65535) return PL_EUNSUPPORTED;
+    const int gx = (a.total_rows + pl::kMmaRows - 1) / pl::kMmaRows;
+    // a few tiles (batched decode): split the inputs so that about four
+    // CTAs per SM run, the slices summed by a second, deterministic kernel
+    const long long tiles = gx * gy;
+    int ks = static_cast<int>((4LL * g->num_sms + tiles - 1) / tiles);
+    if (ks > a.n / pl::kMmaKC) ks = a.n / pl::kMmaKC;
+    if (ks < 1) ks = 1;
+    a.ksplit = ks;
+    a.part = nullptr;
+    if (ks > 1) {
+      const size_t need = static_cast<size_t>(ks) * a.M * a.total_rows;
+      if (need > g->proj_part_cap) {
+        if (g->d_proj_part) {
+          cudaStreamSynchronize(g->stream);
+          cudaFree(g->d_proj_part);
+        }
+        g->d_proj_part = nullptr;
+        g->proj_part_cap = 0;
+        if (cudaMalloc(&g->d_proj_part, need * sizeof(float)) != cudaSuccess) return PL_ENOMEM;
+        g->proj_part_cap = need;
+      }
+      a.part = g->d_proj_part;
+    }
+    const dim3 grid(gx, static_cast<unsigned>(gy), ks);
+    pl::proj_mma_kernel<<<grid, pl::kMmaThreads, 0, st>>>(a);
+    PL_CUDA(cudaGetLastError());
+    count_launch();
+    if (ks > 1) {
+      const size_t n_out = static_cast<size_t>(a.M) * a.total_rows;
+      pl::proj_reduce_kernel<<<static_cast<unsigned>((n_out + 255) / 256), 256, 0, st>>>(a);
+      PL_CUDA(cudaGetLastError());
+      count_launch();
+    }
+    return PL_OK;
+  }
   const size_t row_b = static_cast<size_t>(a.n) * sizeof(float);
   long long mc = pl::kProjSmemCap / static_cast<long long>(row_b);
   if (mc > pl::kProjMaxM) mc = pl::kProjMaxM;
@@ -1440,7 +1488,7 @@ int run_qkv(const LayerW& L, const float* d_x, int M, const BlkBufs& b, cudaStre
   a.M = M;
   a.norm_w = L.attn_norm;
   a.eps = L.eps;
-  int rc = launch_proj(a, st);
+  int rc = launch_proj(a, st, true);
   if (rc || !L.q_norm) return rc;
   const dim3 grid(static_cast<unsigned>(M), (g->n_heads + g->n_kv_heads + 7) / 8);
   pl::qk_norm_kernel<<<grid, 256, 0, st>>>(b.q, b.k, g->n_heads, g->n_kv_heads, g->head_dim,
@@ -1462,7 +1510,7 @@ int run_out(const LayerW& L, const float* d_att, int M, float* d_x, cudaStream_t
   a.M = M;
   a.resid = d_x;
   a.ld_res = L.dim;
-  return launch_proj(a, st);
+  return launch_proj(a, st, true);
 }
 
 int block_decode(int layer, int n, const int* d_seqs, const int* d_pos, int max_rows, float* d_x,
@@ -1677,7 +1725,11 @@ int pl_attn_proj(int layer, int which, int n, const float* x, float* y) {
   a.ldx = in;
   a.n = in;
   a.M = n;
-  rc = launch_proj(a, g->stream);
+  // the tensor-core path carries x as FP16 parts: only for inputs in range
+  bool in_range = true;
+  for (size_t i = 0; i < static_cast<size_t>(n) * in && in_range; ++i)
+    in_range = std::fabs(x[i]) < 60000.f;
+  rc = launch_proj(a, g->stream, in_range);
   if (rc) return rc;
   return read_back(d_y, y, yb, h + y_off);
 }
