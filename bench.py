@@ -622,7 +622,8 @@ def run_hd128(args, local, peaks):
                       "ms_per_layer": ms, "attn_kernel_tflops": kern_tf,
                       "attn_kernel_frac": kern_tf / peaks["bf16_tflops"],
                       "traffic": profile_traffic("prefill_attn_kernel_hd128.txt"),
-                      "path": "prologue (RoPE + append + FP16 q) then the tcgen05 kernel, "
+                      "path": "prologue (RoPE + append + q as FP16 high part and residual) "
+                              "then the tcgen05 kernel, "
                               "64-row KV tiles"}
     return res
 
