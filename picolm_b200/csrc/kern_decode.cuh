@@ -12,6 +12,12 @@
 // "segments" (the part of one sequence inside the slice); the TMA pipeline
 // runs on across segment boundaries.
 //
+// The grid is launched with programmatic dependent launch: its CTAs take the
+// SMs that the kernel before it on the stream frees and run that set-up
+// (from the slots and positions read as a hint) and an L2 prefetch of their
+// first tiles before griddepcontrol.wait; after the wait the counts are
+// checked against fresh loads and the scan redone if one differs.
+//
 // Inside a CTA:
 //   warp Hk      (producer)  one lane streams K and V tiles into an
 //                            NSTAGE-deep ring with 4-D TMA loads (128-byte
@@ -172,6 +178,83 @@ __device__ __forceinline__ void seq_rows(const DecodeArgs& a, int i, int& att_ro
   const int pos = pos_of(a, i);
   att_rows = a.mode == 0 ? pos + 1 : a.n_rows;
   app_row = a.mode == 0 ? (a.append ? pos : -1) : (a.append ? pos - a.row0 : -1);
+}
+
+// Tile count of sequence i of a launch; 0, with `bad` set, for a sequence
+// whose slot or rows are out of range.  With `hint` the slot and position
+// are read through L2 only (ld.global.cg): before griddepcontrol.wait they
+// may still be changing, and no L1 line of them may outlive the wait.
+template <int TP>
+__device__ __forceinline__ int seq_tiles(const DecodeArgs& a, int i, bool hint, bool& bad,
+                                         int& seq) {
+  seq = a.seqs ? (hint ? __ldcg(a.seqs + i) : a.seqs[i]) : a.seq1;
+  const int pos = a.pos ? (hint ? __ldcg(a.pos + i) : a.pos[i]) : a.pos1;
+  const int att_rows = a.mode == 0 ? pos + 1 : a.n_rows;
+  const int app_row = a.mode == 0 ? (a.append ? pos : -1) : (a.append ? pos - a.row0 : -1);
+  bad = seq < 0 || seq >= a.n_slots || pos < 0 || pos >= a.max_seq || att_rows < 0 ||
+        att_rows > a.max_seq || app_row >= a.max_seq;
+  return bad ? 0 : (att_rows + TP - 1) / TP;
+}
+
+// Exclusive prefix sum of the launch's tile counts into s_prefix[0..n]
+// (s_prefix[n] = total), the same in every CTA.  Each thread counts a
+// contiguous run of sequences; returns whether one of them is out of range.
+// With `hint`, s_seq[i] keeps the slot read for sequence i.
+template <int TP>
+__device__ bool scan_tiles(const DecodeArgs& a, int* s_prefix, int* s_warp_sum, int* s_seq,
+                           bool hint) {
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int nthr = blockDim.x, n = a.n;
+  const int per = (n + nthr - 1) / nthr;
+  const int i0 = tid * per;
+  int local = 0;
+  bool any_bad = false;
+  for (int i = i0; i < min(n, i0 + per); ++i) {
+    bool bad;
+    int seq;
+    const int tiles = seq_tiles<TP>(a, i, hint, bad, seq);
+    any_bad |= bad;
+    if (hint) s_seq[i] = seq;
+    s_prefix[i] = tiles;  // counts first, scanned below
+    local += tiles;
+  }
+  // inclusive scan of the per-thread sums across the block
+  int incl = local;
+#pragma unroll
+  for (int d = 1; d < 32; d <<= 1) {
+    const int y = __shfl_up_sync(0xffffffffu, incl, d);
+    if (lane >= d) incl += y;
+  }
+  if (lane == 31) s_warp_sum[warp] = incl;
+  __syncthreads();
+  if (tid == 0) {
+    int acc = 0;
+    for (int w = 0; w < nthr / 32; ++w) {
+      const int t = s_warp_sum[w];
+      s_warp_sum[w] = acc;
+      acc += t;
+    }
+    s_prefix[n] = acc;
+  }
+  __syncthreads();
+  int run = s_warp_sum[warp] + incl - local;  // exclusive prefix of this thread
+  for (int i = i0; i < min(n, i0 + per); ++i) {
+    const int t = s_prefix[i];
+    s_prefix[i] = run;
+    run += t;
+  }
+  __syncthreads();
+  return any_bad;
+}
+
+// Smallest sequence i with prefix[i + 1] > x (x below the total).
+__device__ __forceinline__ int first_seq_after(const int* prefix, int n, long long x) {
+  int lo = 0, hi = n - 1;
+  while (lo < hi) {
+    const int mid = (lo + hi) >> 1;
+    if (prefix[mid + 1] > x) hi = mid; else lo = mid + 1;
+  }
+  return lo;
 }
 
 // -------------------------------------------------------------- merge
@@ -448,6 +531,7 @@ __global__ void __launch_bounds__(288) decode_kernel(const DecodeArgs a,
   extern __shared__ uint8_t smem_raw[];
   __shared__ int s_prefix[kMaxLaunchSeqs + 1];
   __shared__ int s_warp_sum[9];
+  __shared__ int s_seq_hint[kMaxLaunchSeqs];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
   const int Hk = a.n_kv_heads;
@@ -463,48 +547,61 @@ __global__ void __launch_bounds__(288) decode_kernel(const DecodeArgs a,
   // the merge grid may start (and wait on griddepcontrol.wait) right away
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 
-  // ---- tile counts and their exclusive prefix sum (every CTA, identical)
-  {
-    const int per = (n + nthr - 1) / nthr;
-    const int i0 = tid * per;
-    int local = 0;
-    for (int i = i0; i < min(n, i0 + per); ++i) {
-      int att_rows, app_row;
-      seq_rows(a, i, att_rows, app_row);
-      const int seq = seq_of(a, i), pos = pos_of(a, i);
-      const bool bad = seq < 0 || seq >= a.n_slots || pos < 0 || pos >= a.max_seq ||
-                       att_rows < 0 || att_rows > a.max_seq || app_row >= a.max_seq;
-      if (bad && blockIdx.x == 0) atomicOr(a.err, ERR_BAD_ARG);
-      const int tiles = bad ? 0 : (att_rows + TP - 1) / TP;
-      s_prefix[i] = tiles;  // counts first, scanned below
-      local += tiles;
-    }
-    // inclusive scan of the per-thread sums across the block
-    int incl = local;
+  // ---- set-up, overlapped with the end of the kernel queued before this one.
+  // Launched with programmatic stream serialisation, this grid may start
+  // while that kernel still runs.  Until griddepcontrol.wait it writes no
+  // global memory and reads only the slots and positions, through L2, as a
+  // hint: it scans the tile counts, partitions the tiles and prefetches this
+  // CTA's first NSTAGE tiles into L2.  After the wait every count is taken
+  // again from fresh loads and the scan is redone if one differs, so a stale
+  // hint costs time, never a wrong result.
+  scan_tiles<TP>(a, s_prefix, s_warp_sum, s_seq_hint, true);
+  if (warp == Hk && lane == 0) {
+    tma_prefetch_desc(&tmk);
+    tma_prefetch_desc(&tmv);
+    const long long Th = s_prefix[n];
+    const long long Gh = static_cast<long long>(gridDim.x) < Th ? gridDim.x : Th;
+    if (blockIdx.x < Gh) {
+      const Partition Ph{s_prefix, Th, static_cast<int>(Gh)};
+      const long long x0 = Ph.begin(blockIdx.x), x1 = Ph.begin(blockIdx.x + 1);
+      int i = first_seq_after(s_prefix, n, x0);
+      for (long long x = x0; x < x1 && x < x0 + NSTAGE; ++x) {
+        while (s_prefix[i + 1] <= x) ++i;
+        const int seq = s_seq_hint[i];  // in range: its tile count is not 0
+        const int row = static_cast<int>(x - s_prefix[i]) * TP;
+        const int slab = seq * a.n_layers + a.layer;
 #pragma unroll
-    for (int d = 1; d < 32; d <<= 1) {
-      const int y = __shfl_up_sync(0xffffffffu, incl, d);
-      if (lane >= d) incl += y;
-    }
-    if (lane == 31) s_warp_sum[warp] = incl;
-    __syncthreads();
-    if (tid == 0) {
-      int acc = 0;
-      for (int w = 0; w < nthr / 32; ++w) {
-        const int t = s_warp_sum[w];
-        s_warp_sum[w] = acc;
-        acc += t;
+        for (int hv = 0; hv < HD / 64; ++hv) {
+          tma_prefetch_l2_4d(&tmk, 64 * hv, row, 0, slab);
+          tma_prefetch_l2_4d(&tmv, 64 * hv, row, 0, slab);
+        }
       }
-      s_prefix[n] = acc;
     }
-    __syncthreads();
-    int run = s_warp_sum[warp] + incl - local;  // exclusive prefix of this thread
+  }
+  if (tid == 0) {
+    for (int s = 0; s < NSTAGE; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], Hk);
+    }
+    fence_mbar_init();
+  }
+  // everything the kernel queued before this one wrote is visible from here on
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  {
+    const int per = (n + nthr - 1) / nthr, i0 = tid * per;
+    bool any_bad = false;
+    int differs = 0;
     for (int i = i0; i < min(n, i0 + per); ++i) {
-      const int t = s_prefix[i];
-      s_prefix[i] = run;
-      run += t;
+      bool bad;
+      int seq;
+      const int tiles = seq_tiles<TP>(a, i, false, bad, seq);
+      any_bad |= bad;
+      differs |= tiles != s_prefix[i + 1] - s_prefix[i];
     }
-    __syncthreads();
+    // (also the barrier that publishes the mbarrier initialisation)
+    if (__syncthreads_or(differs))
+      any_bad = scan_tiles<TP>(a, s_prefix, s_warp_sum, s_seq_hint, false);
+    if (any_bad && blockIdx.x == 0) atomicOr(a.err, ERR_BAD_ARG);
   }
   const long long T = s_prefix[n];
   if (T == 0) {  // no rows anywhere: nothing to merge either
@@ -522,31 +619,12 @@ __global__ void __launch_bounds__(288) decode_kernel(const DecodeArgs a,
   if (cta >= P.G) return;
   const long long x0 = P.begin(cta), x1 = P.begin(cta + 1);
   // first sequence with tiles in [x0, x1)
-  int i_first = 0;
-  {
-    int lo = 0, hi = n - 1;
-    while (lo < hi) {  // smallest i with prefix[i+1] > x0
-      const int mid = (lo + hi) >> 1;
-      if (s_prefix[mid + 1] > x0) hi = mid; else lo = mid + 1;
-    }
-    i_first = lo;
-  }
-
-  if (tid == 0) {
-    for (int s = 0; s < NSTAGE; ++s) {
-      mbar_init(&full[s], 1);
-      mbar_init(&empty[s], Hk);
-    }
-    fence_mbar_init();
-  }
-  __syncthreads();
+  const int i_first = first_seq_after(s_prefix, n, x0);
 
   bool ok = true;
   if (warp == Hk) {
     // ------------------------------------------------------------ producer
     if (lane == 0) {
-      tma_prefetch_desc(&tmk);
-      tma_prefetch_desc(&tmv);
       int i = i_first;
       long long issued = 0;
       for (long long x = x0; x < x1; ++x) {

@@ -441,8 +441,21 @@ int launch_decode_tp(const pl::DecodeArgs& a, int grid, cudaStream_t st, bool pr
     attr_done = true;
   }
   if (profile) prof_begin(st);
-  kern<<<grid, (g->n_kv_heads + 1) * 32, smem, st>>>(a, g->tm_k_dec, g->tm_v_dec);
-  PL_CUDA(cudaGetLastError());
+  // Programmatic stream serialisation: the grid may become resident while
+  // the kernel queued before it finishes and run its set-up then; the kernel
+  // reads nothing that kernel writes before griddepcontrol.wait (positions
+  // and slots only as a hint that it checks after the wait).
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3((g->n_kv_heads + 1) * 32);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  PL_CUDA(cudaLaunchKernelEx(&cfg, kern, a, g->tm_k_dec, g->tm_v_dec));
   if (profile) {
     prof_end(st);
     count_launch();

@@ -92,6 +92,18 @@ __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* m) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(m)) : "memory");
 }
 
+// 4-D tiled prefetch of one box into L2 (no shared memory, no completion
+// signal).  A hint only: L2 is coherent for the whole GPU, so a box that
+// another kernel is still writing is simply refetched by the real load.
+__device__ __forceinline__ void tma_prefetch_l2_4d(const CUtensorMap* m, int c0, int c1, int c2,
+                                                   int c3) {
+  asm volatile(
+      "cp.async.bulk.prefetch.tensor.4d.L2.global.tile [%0, {%1, %2, %3, %4}];" ::"l"(
+          reinterpret_cast<uint64_t>(m)),
+      "r"(c0), "r"(c1), "r"(c2), "r"(c3)
+      : "memory");
+}
+
 // 4-D tiled load (no multicast) into this CTA's shared memory; completion is
 // signalled on `bar` as transaction bytes.
 __device__ __forceinline__ void tma_load_4d(void* dst, const CUtensorMap* m, uint64_t* bar,

@@ -254,3 +254,67 @@ def test_batch_over_one_launch():
             np.testing.assert_array_equal(gk, kc2)
             np.testing.assert_array_equal(gv, vc2)
             assert_attn_close(out[i], want, f"batch of {n}: entry {i} (slot {s}, pos {pos[i]})")
+
+
+def test_dev_steps_with_positions_written_just_before():
+    # Device-pointer decode steps queued back to back with no host
+    # synchronisation, as an engine drives them.  Before each step a kernel on
+    # the same stream writes that step's slots and positions into the SAME two
+    # arrays, right before the decode launch.  The decode grid is launched
+    # with programmatic stream serialisation and may start its set-up while
+    # the kernel before it finishes; what it reads then is only a hint, checked
+    # after griddepcontrol.wait.  The batch order of the slots changes every
+    # step, so a stale hint would partition the tiles differently.  Every
+    # step's output and the final caches against the oracle.
+    import torch
+    rng = np.random.default_rng(53)
+    H, Hk, ms, n, steps = 32, 4, 320, 24, 6
+    kv = Hk * 64
+    tables = O.rope_tables(ms, 64, 10000.0)
+    base = rng.integers(1, ms - steps, n).astype(np.int32)
+    base[[0, 1]] = [ms - steps, 0]          # the longest cache and an empty one
+    order = np.stack([rng.permutation(n) for _ in range(steps)]).astype(np.int32)
+    pos_all = np.stack([base[order[s]] + s for s in range(steps)]).astype(np.int32)
+    q = rng.standard_normal((steps, n, H * 64), dtype=np.float32)
+    k = rng.standard_normal((steps, n, kv), dtype=np.float32)
+    v = rng.standard_normal((steps, n, kv), dtype=np.float32)
+    caches = []
+    for s in range(n):
+        kc = np.zeros((ms, kv), np.uint16)
+        vc = np.zeros((ms, kv), np.uint16)
+        kc[:base[s]] = random_cache(rng, int(base[s]), kv)
+        vc[:base[s]] = random_cache(rng, int(base[s]), kv)
+        caches.append((kc, vc))
+    dev = torch.device("cuda", 0)
+    with pb.Attn(1, H, Hk, ms, n_seqs=n) as at:
+        for s in range(n):
+            at.kv_upload(s, 0, 0, *caches[s])
+        d_order = torch.from_numpy(order).to(dev)
+        d_pos_all = torch.from_numpy(pos_all).to(dev)
+        dq, dk, dv = (torch.from_numpy(x).to(dev) for x in (q, k, v))
+        d_seqs = torch.full((n,), -1, dtype=torch.int32, device=dev)
+        d_pos = torch.full((n,), -1, dtype=torch.int32, device=dev)
+        out = torch.full((steps, n, H * 64), float("nan"), device=dev)
+        zero = torch.zeros((), dtype=torch.int32, device=dev)
+        st = torch.cuda.current_stream().cuda_stream
+        torch.cuda.synchronize()
+        for s in range(steps):
+            torch.add(d_order[s], zero, out=d_seqs)    # elementwise kernels, not copies
+            torch.add(d_pos_all[s], zero, out=d_pos)
+            at.decode_batch_dev(0, n, d_seqs.data_ptr(), d_pos.data_ptr(), ms - 1,
+                                dq[s].data_ptr(), dk[s].data_ptr(), dv[s].data_ptr(),
+                                out[s].data_ptr(), st)
+        torch.cuda.synchronize()
+        got = out.cpu().numpy()
+        for s in range(steps):
+            for i in range(n):
+                slot = int(order[s, i])
+                kc, vc = caches[slot]
+                want, kc, vc = oracle_decode_layer(H, Hk, ms, kc, vc, int(pos_all[s, i]),
+                                                   q[s, i], k[s, i], v[s, i], tables)
+                caches[slot] = (kc, vc)
+                assert_attn_close(got[s, i], want, f"step {s} entry {i} (slot {slot})")
+        for slot in range(n):
+            gk, gv = at.kv_download(slot, 0, 0, ms)
+            np.testing.assert_array_equal(gk, caches[slot][0])
+            np.testing.assert_array_equal(gv, caches[slot][1])
