@@ -139,7 +139,10 @@ int  pl_kv_upload(int seq, int layer, int pos0, int n_pos, const uint16_t *k,
  *      cudaStream_t passed as void*; NULL = the CUDA default stream) ---- */
 
 /* pl_attn_decode_batch with every array already in device memory.
- * max_pos must bound every d_pos[i] (it sizes the KV split). */
+ * max_pos must bound every d_pos[i] (it sizes the KV split).  The decode
+ * grid is launched with programmatic dependent launch, so it may start its
+ * set-up while the kernel queued before it on `stream` finishes; arrays that
+ * kernel writes are still read correctly (after griddepcontrol.wait). */
 int  pl_attn_decode_batch_dev(int layer, int n, const int *d_seqs,
                               const int *d_pos, int max_pos, const float *d_q,
                               const float *d_k, const float *d_v, float *d_out,
