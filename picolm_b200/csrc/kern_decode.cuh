@@ -701,11 +701,16 @@ __global__ void __launch_bounds__(kMergeThreads) merge_kernel(const DecodeArgs a
   float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
   if (lane_j < lanes && h < a.n_heads) {
     const float* base = a.part + static_cast<size_t>(si.x) * slot_stride + h * PS;
-    for (int j0 = lane_j; j0 < ns; j0 += 8 * lanes) {  // 8 segments in flight
-      float2 ml[8];
-      float4 v[8];
+    // U segments in flight per thread: at head_dim 64 and one head per
+    // block (16 lanes) one round trip covers the 148 segments of a sequence
+    // split over every SM.  At head_dim 128 more would cost the registers
+    // that let a merge block sit beside a decode CTA.
+    constexpr int U = HD == 64 ? 10 : 8;
+    for (int j0 = lane_j; j0 < ns; j0 += U * lanes) {
+      float2 ml[U];
+      float4 v[U];
 #pragma unroll
-      for (int u = 0; u < 8; ++u) {
+      for (int u = 0; u < U; ++u) {
         const int j = j0 + u * lanes;
         if (j < ns) {
           ml[u] = __ldcg(reinterpret_cast<const float2*>(base + j * slot_stride));
@@ -714,7 +719,7 @@ __global__ void __launch_bounds__(kMergeThreads) merge_kernel(const DecodeArgs a
       }
       float mx = m_loc;
 #pragma unroll
-      for (int u = 0; u < 8; ++u)
+      for (int u = 0; u < U; ++u)
         if (j0 + u * lanes < ns) mx = fmaxf(mx, ml[u].x);
       if (mx != -INFINITY) {
         const float sc = ex2(m_loc - mx);
@@ -724,7 +729,7 @@ __global__ void __launch_bounds__(kMergeThreads) merge_kernel(const DecodeArgs a
         acc.z *= sc;
         acc.w *= sc;
 #pragma unroll
-        for (int u = 0; u < 8; ++u)
+        for (int u = 0; u < U; ++u)
           if (j0 + u * lanes < ns) {
             const float w = ex2(ml[u].x - mx);
             l_loc += w * ml[u].y;
