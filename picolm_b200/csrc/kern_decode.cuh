@@ -55,7 +55,7 @@
 // count).  merge_kernel, launched right behind with programmatic dependent
 // launch (it is resident and waiting on griddepcontrol.wait when the decode
 // grid ends), merges them: 256 threads per group of 1 to 16 heads, sized so
-// the merge grid covers the SMs in one wave.  Merging inside the decode grid
+// the merge grid has at most one block per SM.  Merging inside the decode grid
 // instead, by the CTA (or, tried later, the warp) that finishes a sequence's
 // last segment, puts atomics, fences and L2 round trips at the end of the
 // slowest CTA: measured on B200 it was slower than this separate grid.
