@@ -13,7 +13,7 @@ steps run back to back.
 
   metric  decode-attn HBM GB/s = algorithmic bytes / device time, summed
           over all ranks (KV rows read + q/k/v read + KV row and output
-          written; bytes per step in DESIGN.md)
+          written; bytes per step in step_bytes())
   e2e     the same metric through the host-buffer C entry point
           pl_attn_decode_batch (pinned staging, H2D of q/k/v, D2H of out,
           synchronous), i.e. what a C caller of the library sees

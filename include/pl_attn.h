@@ -218,9 +218,12 @@ int  pl_attn_combine_p2p_dev(const float *d_part, float *d_out, void *stream);
  * file-scope device array of 4 MiB + 8 KiB, which every GPU that loads the
  * library holds until the process exits; it calls no cudaMalloc, cudaFree
  * or other allocating routine.  Limits: n <= 1024 sequences, and at most
- * 4 MiB / (n_heads * 272 bytes) partial slots (one per CTA plus one per
- * sequence: 481 for 32 query heads), so the KV split is capped to fit;
- * larger n fails with PL_EARG and a message on stderr.  The first call on a
+ * 4 MiB / (n_heads * (head_dim + 4) * 4 bytes) partial slots, one per CTA
+ * plus one per sequence (32 query heads: 481 slots at head_dim 64, 248 at
+ * head_dim 128), so the KV split is capped to fit (fewer, longer CTAs); an
+ * n that leaves no slot for a CTA fails with PL_EARG and a message on
+ * stderr.  The current device must be the module's (PL_EDEVICE otherwise).
+ * The first call on a
  * device looks up the array's device address (cudaGetSymbolAddress); make
  * that first call before any stream capture.  All calls share the one
  * array, so calls that overlap on the GPU (e.g. on two streams at once)
@@ -308,31 +311,164 @@ int  pl_attn_profile(int enable);
 int  pl_attn_profile_read(double *attn_ms, long *attn_launches,
                           long *all_launches);
 
-#else /* PL_ATTN_DISABLED: inline stubs, as gpu.h does without USE_VULKAN */
-
-static inline int  pl_attn_init(int a, int b, int c, int d, int e, float f,
-                                int g, int h, int i) {
-    (void)a; (void)b; (void)c; (void)d; (void)e; (void)f; (void)g; (void)h;
-    (void)i; return PL_EDEVICE;
+#else /* PL_ATTN_DISABLED: inline stubs for every entry point, as gpu.h does
+        without USE_VULKAN (picolm/gpu.h:33-42).  pl_attn_init reports
+        PL_EDEVICE, so a caller keeps its CPU loops; nothing else is
+        reachable without it and reports PL_ESTATE. */
+static inline int pl_attn_init(int n_layers, int n_heads, int n_kv_heads,
+                               int head_dim, int max_seq_len,
+                               float rope_freq_base, int rope_type, int n_seqs,
+                               int device) {
+    (void)n_layers; (void)n_heads; (void)n_kv_heads; (void)head_dim;
+    (void)max_seq_len; (void)rope_freq_base; (void)rope_type; (void)n_seqs;
+    (void)device; return PL_EDEVICE;
 }
-static inline int  pl_attn_set_rope(const float *a, const float *b, int c, int d) {
-    (void)a; (void)b; (void)c; (void)d; return PL_ESTATE;
-}
-static inline int  pl_attn_available(void) { return 0; }
-static inline void pl_attn_shutdown(void) {}
-static inline const char *pl_attn_strerror(int rc) {
-    (void)rc; return "attention backend compiled out";
-}
-static inline int  pl_attn_decode(int a, int b, int c, const float *d,
-                                  const float *e, const float *f, float *g) {
-    (void)a; (void)b; (void)c; (void)d; (void)e; (void)f; (void)g;
+static inline int pl_attn_set_rope(const float *cos_tab, const float *sin_tab,
+                                   int n_rows, int half_dim) {
+    (void)cos_tab; (void)sin_tab; (void)n_rows; (void)half_dim;
     return PL_ESTATE;
 }
-static inline int  pl_attn_prefill(int a, int b, int c, int d, const float *e,
-                                   const float *f, const float *g, float *h,
-                                   int i) {
-    (void)a; (void)b; (void)c; (void)d; (void)e; (void)f; (void)g; (void)h;
-    (void)i; return PL_ESTATE;
+static inline int pl_attn_available(void) { return 0; }
+static inline void pl_attn_shutdown(void) {}
+static inline const char *pl_attn_strerror(int rc) {
+    (void)rc; return "attention backend compiled out (PL_ATTN_DISABLED)";
+}
+static inline int pl_attn_decode(int seq, int layer, int pos, const float *q,
+                                 const float *k, const float *v, float *out) {
+    (void)seq; (void)layer; (void)pos; (void)q; (void)k; (void)v; (void)out;
+    return PL_ESTATE;
+}
+static inline int pl_attn_decode_batch(int layer, int n, const int *seqs,
+                                       const int *pos, const float *q,
+                                       const float *k, const float *v,
+                                       float *out) {
+    (void)layer; (void)n; (void)seqs; (void)pos; (void)q; (void)k; (void)v;
+    (void)out; return PL_ESTATE;
+}
+static inline int pl_attn_prefill(int seq, int layer, int start_pos, int n_tok,
+                                  const float *q, const float *k,
+                                  const float *v, float *out, int out_stride) {
+    (void)seq; (void)layer; (void)start_pos; (void)n_tok; (void)q; (void)k;
+    (void)v; (void)out; (void)out_stride; return PL_ESTATE;
+}
+static inline int pl_attn_host_register(void *ptr, size_t bytes) {
+    (void)ptr; (void)bytes; return PL_ESTATE;
+}
+static inline int pl_attn_host_unregister(void *ptr) {
+    (void)ptr; return PL_ESTATE;
+}
+static inline int pl_attn_rope(int pos0, int n_tok, float *q, float *k) {
+    (void)pos0; (void)n_tok; (void)q; (void)k; return PL_ESTATE;
+}
+static inline int pl_kv_download(int seq, int layer, int pos0, int n_pos,
+                                 uint16_t *k, uint16_t *v) {
+    (void)seq; (void)layer; (void)pos0; (void)n_pos; (void)k; (void)v;
+    return PL_ESTATE;
+}
+static inline int pl_kv_upload(int seq, int layer, int pos0, int n_pos,
+                               const uint16_t *k, const uint16_t *v) {
+    (void)seq; (void)layer; (void)pos0; (void)n_pos; (void)k; (void)v;
+    return PL_ESTATE;
+}
+static inline int pl_attn_decode_batch_dev(int layer, int n, const int *d_seqs,
+                                           const int *d_pos, int max_pos,
+                                           const float *d_q, const float *d_k,
+                                           const float *d_v, float *d_out,
+                                           void *stream) {
+    (void)layer; (void)n; (void)d_seqs; (void)d_pos; (void)max_pos; (void)d_q;
+    (void)d_k; (void)d_v; (void)d_out; (void)stream; return PL_ESTATE;
+}
+static inline int pl_attn_prefill_dev(int seq, int layer, int start_pos,
+                                      int n_tok, const float *d_q,
+                                      const float *d_k, const float *d_v,
+                                      float *d_out, int out_stride,
+                                      void *stream) {
+    (void)seq; (void)layer; (void)start_pos; (void)n_tok; (void)d_q; (void)d_k;
+    (void)d_v; (void)d_out; (void)out_stride; (void)stream; return PL_ESTATE;
+}
+static inline int pl_attn_decode_partial_dev(int seq, int layer, int pos,
+                                             int row0, int n_rows, int append,
+                                             const float *d_q,
+                                             const float *d_k,
+                                             const float *d_v, float *d_part,
+                                             void *stream) {
+    (void)seq; (void)layer; (void)pos; (void)row0; (void)n_rows; (void)append;
+    (void)d_q; (void)d_k; (void)d_v; (void)d_part; (void)stream;
+    return PL_ESTATE;
+}
+static inline int pl_attn_combine_dev(int n_part, const float *d_parts,
+                                      float *d_out, void *stream) {
+    (void)n_part; (void)d_parts; (void)d_out; (void)stream; return PL_ESTATE;
+}
+static inline int pl_attn_kv_ptr(int seq, int layer, uint16_t **d_k,
+                                 uint16_t **d_v) {
+    (void)seq; (void)layer; (void)d_k; (void)d_v; return PL_ESTATE;
+}
+static inline int pl_attn_xfer_handle_bytes(void) { return 0; }
+static inline int pl_attn_xfer_setup(int world, int rank, void *handle_out) {
+    (void)world; (void)rank; (void)handle_out; return PL_ESTATE;
+}
+static inline int pl_attn_xfer_connect(const void *handles) {
+    (void)handles; return PL_ESTATE;
+}
+static inline int pl_attn_combine_p2p_dev(const float *d_part, float *d_out,
+                                          void *stream) {
+    (void)d_part; (void)d_out; (void)stream; return PL_ESTATE;
+}
+static inline int pl_attn_decode_batch_dev_noalloc(int layer, int n,
+                                                   const int *d_seqs,
+                                                   const int *d_pos,
+                                                   int max_pos,
+                                                   const float *d_q,
+                                                   const float *d_k,
+                                                   const float *d_v,
+                                                   float *d_out, void *stream) {
+    (void)layer; (void)n; (void)d_seqs; (void)d_pos; (void)max_pos; (void)d_q;
+    (void)d_k; (void)d_v; (void)d_out; (void)stream; return PL_ESTATE;
+}
+static inline int pl_attn_set_layer(int layer, int dim, const float *attn_norm,
+                                    float rms_eps, const void *wq, int type_q,
+                                    const void *wk, int type_k, const void *wv,
+                                    int type_v, const void *wo, int type_o,
+                                    const float *bq, const float *bk,
+                                    const float *bv, const float *bo,
+                                    const float *q_norm, const float *k_norm) {
+    (void)layer; (void)dim; (void)attn_norm; (void)rms_eps; (void)wq;
+    (void)type_q; (void)wk; (void)type_k; (void)wv; (void)type_v; (void)wo;
+    (void)type_o; (void)bq; (void)bk; (void)bv; (void)bo; (void)q_norm;
+    (void)k_norm; return PL_ESTATE;
+}
+static inline int pl_attn_block_decode(int layer, int n, const int *seqs,
+                                       const int *pos, float *x) {
+    (void)layer; (void)n; (void)seqs; (void)pos; (void)x; return PL_ESTATE;
+}
+static inline int pl_attn_block_prefill(int seq, int layer, int start_pos,
+                                        int n_tok, float *x) {
+    (void)seq; (void)layer; (void)start_pos; (void)n_tok; (void)x;
+    return PL_ESTATE;
+}
+static inline int pl_attn_block_decode_dev(int layer, int n, const int *d_seqs,
+                                           const int *d_pos, int max_pos,
+                                           float *d_x, void *stream) {
+    (void)layer; (void)n; (void)d_seqs; (void)d_pos; (void)max_pos; (void)d_x;
+    (void)stream; return PL_ESTATE;
+}
+static inline int pl_attn_block_prefill_dev(int seq, int layer, int start_pos,
+                                            int n_tok, float *d_x, void *stream)
+{
+    (void)seq; (void)layer; (void)start_pos; (void)n_tok; (void)d_x;
+    (void)stream; return PL_ESTATE;
+}
+static inline int pl_attn_proj(int layer, int which, int n, const float *x,
+                               float *y) {
+    (void)layer; (void)which; (void)n; (void)x; (void)y; return PL_ESTATE;
+}
+static inline int pl_attn_profile(int enable) {
+    (void)enable; return PL_ESTATE;
+}
+static inline int pl_attn_profile_read(double *attn_ms, long *attn_launches,
+                                       long *all_launches) {
+    (void)attn_ms; (void)attn_launches; (void)all_launches; return PL_ESTATE;
 }
 
 #endif /* PL_ATTN_DISABLED */

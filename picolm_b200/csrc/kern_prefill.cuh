@@ -60,6 +60,7 @@
 // CTA winds down (waits for its own MMAs and TMA copies, frees its TMEM)
 // instead of hanging.
 #pragma once
+#include <atomic>
 #include <cstdint>
 #include <cuda.h>
 #include <cuda_runtime.h>
@@ -616,8 +617,13 @@ inline int launch_prefill_shape(const PrefillArgs& a, const CUtensorMap& tm_q,
                                 bool overlap) {
   auto kern = prefill_attn_kernel<HD, BN, STAGES>;
   constexpr int smem = pf_smem_bytes<HD, BN, STAGES>();
-  static bool attr_done = false;
-  if (!attr_done) {
+  // kernel attributes are per device: set them the first time this kernel
+  // launches on each device (one bit per device)
+  static std::atomic<unsigned long long> attr_done{0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return -4;
+  const unsigned long long bit = dev < 64 ? 1ull << dev : 0ull;
+  if (!bit || !(attr_done.load(std::memory_order_acquire) & bit)) {
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) !=
         cudaSuccess)
       return -4;
@@ -630,7 +636,7 @@ inline int launch_prefill_shape(const PrefillArgs& a, const CUtensorMap& tm_q,
               fa.numRegs, kPfLaunchRegs);
       return -4;
     }
-    attr_done = true;
+    attr_done.fetch_or(bit, std::memory_order_release);
   }
   const int per_tile = a.kv_mul >= 2 ? a.n_heads / 2 : a.n_heads;
   const int n_items = ((a.n_tok + kPfBlockM - 1) / kPfBlockM) * per_tile;

@@ -435,10 +435,15 @@ template <int TP, int NS, int HD>
 int launch_decode_tp(const pl::DecodeArgs& a, int grid, cudaStream_t st, bool profile) {
   const int smem = decode_smem_bytes(TP, NS, HD);
   auto kern = pl::decode_kernel<TP, NS, HD>;
-  static bool attr_done = false;
-  if (!attr_done) {
+  // the shared-memory attribute is per device: set it the first time this
+  // instantiation launches on each device (one bit per device)
+  static std::atomic<unsigned long long> attr_done{0};
+  int dev = 0;
+  PL_CUDA(cudaGetDevice(&dev));
+  const unsigned long long bit = dev < 64 ? 1ull << dev : 0ull;
+  if (!bit || !(attr_done.load(std::memory_order_acquire) & bit)) {
     PL_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-    attr_done = true;
+    attr_done.fetch_or(bit, std::memory_order_release);
   }
   if (profile) prof_begin(st);
   // Programmatic stream serialisation: the grid may become resident while
@@ -1262,18 +1267,14 @@ static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratch
 void* g_noalloc_addr[kNoAllocMaxDevices];
 std::mutex g_noalloc_mu;
 
-// Device address of g_noalloc_scratch on `device`, looked up on the first
-// call for that device with the device current.
+// Device address of g_noalloc_scratch on `device`, which the caller has
+// checked is the current device; looked up on the first call for it.
 int noalloc_scratch(int device, uint8_t** addr) {
   if (device < 0 || device >= kNoAllocMaxDevices) return PL_EDEVICE;
   std::lock_guard<std::mutex> lk(g_noalloc_mu);
   if (!g_noalloc_addr[device]) {
-    int cur = -1;
-    PL_CUDA(cudaGetDevice(&cur));
-    if (cur != device) PL_CUDA(cudaSetDevice(device));
     void* p = nullptr;
     const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
-    if (cur != device) cudaSetDevice(cur);
     if (e != cudaSuccess || !p) {
       std::fprintf(stderr, "pl_attn: cudaGetSymbolAddress(scratch) failed: %s\n",
                    cudaGetErrorString(e));
@@ -1307,6 +1308,16 @@ extern "C" int pl_attn_decode_batch_dev_noalloc(int layer, int n, const int* d_s
                  n, kNoAllocMaxSeqs, kNoAllocPartBytes / slot_bytes, slot_bytes,
                  kNoAllocScratchBytes);
     return PL_EARG;
+  }
+  // the kernels run on the caller's current device, with this context's
+  // cache pointers: it must be the context's device
+  int cur = -1;
+  PL_CUDA(cudaGetDevice(&cur));
+  if (cur != g->device) {
+    std::fprintf(stderr,
+                 "pl_attn_decode_batch_dev_noalloc: current device %d is not the module's "
+                 "device %d\n", cur, g->device);
+    return PL_EDEVICE;
   }
   uint8_t* scratch = nullptr;
   int rc = noalloc_scratch(g->device, &scratch);

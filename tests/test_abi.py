@@ -68,3 +68,21 @@ def test_init_without_device_fails_cleanly():
     with pytest.raises(pb.PlAttnError) as ei:
         pb.Attn(1, 32, 4, 256)
     assert ei.value.rc == pb.PL_EDEVICE
+
+
+def test_prefill_register_allocation_checked_at_build():
+    """The build records ptxas' resource report and refuses a library whose
+    prefill kernels would launch without the registers their warpgroup split
+    (setmaxnreg) hands out."""
+    import json
+    from picolm_b200 import build
+    build.build()
+    res = json.load(open(build.RESOURCES))
+    pf = {k: v for k, v in res.items() if "prefill_attn_kernel" in k}
+    assert len(pf) == 2, sorted(pf)
+    assert all(v["registers"] == build.PREFILL_LAUNCH_REGS for v in pf.values()), pf
+    # the decode kernels at head_dim 64 run without spills
+    dec64 = {k: v for k, v in res.items() if "decode_kernel" in k and k.endswith("Li64EEEvNS_10DecodeArgsE14CUtensorMap_stS2_")}
+    assert dec64 and all(v.get("spill_stores", 0) == 0 for v in dec64.values()), dec64
+    with pytest.raises(RuntimeError):
+        build.check_resources({k: dict(v, registers=160) for k, v in pf.items()})
