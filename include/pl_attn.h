@@ -296,6 +296,26 @@ int  pl_attn_block_prefill_dev(int seq, int layer, int start_pos, int n_tok,
  * [n][dim] (Wo: [n][n_heads*head_dim]), y [n][rows of W].  No RMSNorm. */
 int  pl_attn_proj(int layer, int which, int n, const float *x, float *y);
 
+/* ---- Status and failure detection ---- */
+
+/* Wait for the work queued on `stream` (a cudaStream_t as void*; NULL = the
+ * CUDA default stream), then read and clear the module's device error word:
+ * PL_ETIMEOUT if a device-side wait gave up since the last check (a TMA
+ * tile, a tensor-core commit, or another rank's partial in
+ * pl_attn_combine_p2p_dev), PL_EARG if a kernel found a slot or position
+ * out of range in a device array, PL_OK otherwise.  The module stays usable after either.  Host-buffer calls
+ * check the word themselves; callers of the _dev entry points use this.
+ * No counterpart in the reference, whose Vulkan backend waits on a fence
+ * with a 5 s timeout (picolm/gpu.c:693-698). */
+int  pl_attn_status(void *stream);
+
+/* Bound on every device-side wait, in seconds (1e-4 .. 60; default 2,
+ * restored by pl_attn_init).  A healthy wait lasts microseconds; the bound
+ * only turns a lost peer or a stalled pipeline into PL_ETIMEOUT instead of
+ * a hang.  A multi-GPU engine with its own failure detector may shorten it
+ * so that a rank that left is noticed within its heartbeat period. */
+int  pl_attn_set_wait_limit(double seconds);
+
 /* ---- Profiling (cf. picolm's timing stats, picolm.c:285-302) ---- */
 
 /* Enable (1) or disable (0) device timing: every later call records CUDA
@@ -462,6 +482,12 @@ static inline int pl_attn_block_prefill_dev(int seq, int layer, int start_pos,
 static inline int pl_attn_proj(int layer, int which, int n, const float *x,
                                float *y) {
     (void)layer; (void)which; (void)n; (void)x; (void)y; return PL_ESTATE;
+}
+static inline int pl_attn_status(void *stream) {
+    (void)stream; return PL_ESTATE;
+}
+static inline int pl_attn_set_wait_limit(double seconds) {
+    (void)seconds; return PL_ESTATE;
 }
 static inline int pl_attn_profile(int enable) {
     (void)enable; return PL_ESTATE;

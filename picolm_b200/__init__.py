@@ -109,6 +109,8 @@ def load(path: str = LIB_PATH) -> C.CDLL:
         "pl_attn_block_decode_dev": (i, [i, i, _vp, _vp, i, _vp, _vp]),
         "pl_attn_block_prefill_dev": (i, [i, i, i, i, _vp, _vp]),
         "pl_attn_proj": (i, [i, i, i, _f32p, _f32p]),
+        "pl_attn_status": (i, [_vp]),
+        "pl_attn_set_wait_limit": (i, [C.c_double]),
         "pl_attn_profile": (i, [i]),
         "pl_attn_profile_read": (i, [C.POINTER(C.c_double), C.POINTER(C.c_long),
                                      C.POINTER(C.c_long)]),
@@ -291,6 +293,15 @@ class Attn:
         y = np.empty(n * rows, np.float32)
         _check(self.lib.pl_attn_proj(layer, which, n, xa.ravel(), y), "pl_attn_proj")
         return y.reshape(n, rows)
+
+    # status and failure detection -------------------------------------
+    def status(self, stream=None) -> int:
+        """pl_attn_status: wait for `stream`, read and clear the device
+        error word; returns the status code (PL_OK, PL_ETIMEOUT, PL_EARG)."""
+        return self.lib.pl_attn_status(stream)
+
+    def set_wait_limit(self, seconds: float) -> None:
+        _check(self.lib.pl_attn_set_wait_limit(float(seconds)), "pl_attn_set_wait_limit")
 
     # device-pointer entry points --------------------------------------
     def decode_batch_dev(self, layer, n, d_seqs, d_pos, max_pos, d_q, d_k, d_v, d_out,

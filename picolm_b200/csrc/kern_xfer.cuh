@@ -88,9 +88,9 @@ __global__ void __launch_bounds__(kXferThreads) combine_p2p_kernel(
   if (tid < world) {
     const uint32_t* stamp = reinterpret_cast<const uint32_t*>(peers.base[rank]) + tid;
     if (static_cast<int>(ld_acquire_sys(stamp) - epoch) < 0) {
-      const uint64_t t0 = globaltimer();
+      const uint64_t t0 = globaltimer(), lim = wait_limit_ns();
       while (static_cast<int>(ld_acquire_sys(stamp) - epoch) < 0) {
-        if (globaltimer() - t0 > kWaitLimitNs) {
+        if (globaltimer() - t0 > lim) {
           atomicOr(err, ERR_TIMEOUT_FULL);
           s_ok = 0;
           break;

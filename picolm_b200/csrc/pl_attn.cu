@@ -130,6 +130,39 @@ std::mutex g_mu;
     }                                                                     \
   } while (0)
 
+// ---- device and pinned-host allocations ------------------------------
+// Every allocation of the module goes through these two.  Failure injection
+// for callers' tests, on the host: with PL_ATTN_FAIL_ALLOC=n in the
+// environment when pl_attn_init runs, the n-th allocation the module then
+// attempts (1 = the first, counting init's own) fails as if the device or
+// the pinned host pool were exhausted, without calling CUDA, so PL_ENOMEM
+// paths can be exercised without filling a GPU.
+std::atomic<long> g_fail_alloc{0};  // countdown; 0 = off
+
+bool inject_alloc_failure() {
+  long v = g_fail_alloc.load();
+  while (v > 0)
+    if (g_fail_alloc.compare_exchange_weak(v, v - 1)) return v == 1;
+  return false;
+}
+
+template <typename T>
+cudaError_t dev_alloc(T** p, size_t bytes) {
+  void* v = nullptr;
+  const cudaError_t e = inject_alloc_failure() ? cudaErrorMemoryAllocation : cudaMalloc(&v, bytes);
+  *p = static_cast<T*>(v);
+  return e;
+}
+
+template <typename T>
+cudaError_t host_alloc(T** p, size_t bytes) {
+  void* v = nullptr;
+  const cudaError_t e =
+      inject_alloc_failure() ? cudaErrorMemoryAllocation : cudaMallocHost(&v, bytes);
+  *p = static_cast<T*>(v);
+  return e;
+}
+
 int make_map(EncodeTiledFn enc, CUtensorMap* m, uint16_t* base, int head_dim, int max_seq,
              int n_kv_heads, int n_slabs, int box_rows, int box_heads) {
   // dims, innermost first: head_dim, row, kv head, (seq, layer) slab; the box
@@ -174,8 +207,8 @@ int ensure_stage(size_t bytes) {
   g->d_stage = nullptr;
   g->h_stage = nullptr;
   g->stage_cap = 0;
-  if (cudaMalloc(&g->d_stage, cap) != cudaSuccess) return PL_ENOMEM;
-  if (cudaMallocHost(&g->h_stage, cap) != cudaSuccess) return PL_ENOMEM;
+  if (dev_alloc(&g->d_stage, cap) != cudaSuccess) return PL_ENOMEM;
+  if (host_alloc(&g->h_stage, cap) != cudaSuccess) return PL_ENOMEM;
   g->stage_cap = cap;
   return PL_OK;
 }
@@ -297,7 +330,7 @@ int ensure_part(size_t floats) {
   if (g->d_part) cudaFree(g->d_part);
   g->d_part = nullptr;
   g->part_cap = 0;
-  if (cudaMalloc(&g->d_part, floats * sizeof(float)) != cudaSuccess) return PL_ENOMEM;
+  if (dev_alloc(&g->d_part, floats * sizeof(float)) != cudaSuccess) return PL_ENOMEM;
   g->part_cap = floats;
   return PL_OK;
 }
@@ -315,7 +348,7 @@ int ensure_q16(int n_tok) {
   g->d_q16 = nullptr;
   g->q16_cap = 0;
   const size_t elems = cap_rows * g->q_dim;
-  if (cudaMalloc(&g->d_q16, 2 * elems * sizeof(uint16_t)) != cudaSuccess) return PL_ENOMEM;
+  if (dev_alloc(&g->d_q16, 2 * elems * sizeof(uint16_t)) != cudaSuccess) return PL_ENOMEM;
   if (cudaMemset(g->d_q16, 0, 2 * elems * sizeof(uint16_t)) != cudaSuccess) return PL_ECUDA;
   const cuuint64_t dims[3] = {static_cast<cuuint64_t>(g->head_dim),
                               static_cast<cuuint64_t>(g->n_heads),
@@ -364,6 +397,7 @@ void count_launch() {
 // Read (and clear) the device error word.
 int check_err_word(uint32_t w) {
   if (w & (pl::ERR_TIMEOUT_FULL | pl::ERR_TIMEOUT_EMPTY | pl::ERR_TIMEOUT_MMA)) return PL_ETIMEOUT;
+  if (w & pl::ERR_BAD_ARG) return PL_EARG;  // a slot or position out of range on the device
   if (w) return PL_EFAIL;
   return PL_OK;
 }
@@ -666,6 +700,10 @@ int pl_attn_init(int n_layers, int n_heads, int n_kv_heads, int head_dim, int ma
   if (cudaGetDeviceProperties(&prop, device) != cudaSuccess) return PL_EDEVICE;
   if (prop.major != 10) return PL_EDEVICE;
   if (cudaSetDevice(device) != cudaSuccess) return PL_EDEVICE;
+  {
+    const char* fa = std::getenv("PL_ATTN_FAIL_ALLOC");
+    g_fail_alloc.store(fa ? std::atol(fa) : 0);
+  }
 
   Ctx* c = new Ctx();
   c->device = device;
@@ -701,13 +739,13 @@ int pl_attn_init(int n_layers, int n_heads, int n_kv_heads, int head_dim, int ma
   c->encode = reinterpret_cast<EncodeTiledFn>(fn);
 
   if (cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking) != cudaSuccess ||
-      cudaMalloc(&c->d_k, cache_elems * 2) != cudaSuccess ||
-      cudaMalloc(&c->d_v, cache_elems * 2) != cudaSuccess ||
-      cudaMalloc(&c->d_cos, sizeof(float) * max_seq_len * (head_dim / 2)) != cudaSuccess ||
-      cudaMalloc(&c->d_sin, sizeof(float) * max_seq_len * (head_dim / 2)) != cudaSuccess ||
-      cudaMalloc(&c->d_err, 256) != cudaSuccess ||
-      cudaMalloc(&c->d_seg_info, sizeof(int2) * pl::kMaxLaunchSeqs) != cudaSuccess ||
-      cudaMalloc(&c->d_work, 2 * sizeof(int)) != cudaSuccess) {
+      dev_alloc(&c->d_k, cache_elems * 2) != cudaSuccess ||
+      dev_alloc(&c->d_v, cache_elems * 2) != cudaSuccess ||
+      dev_alloc(&c->d_cos, sizeof(float) * max_seq_len * (head_dim / 2)) != cudaSuccess ||
+      dev_alloc(&c->d_sin, sizeof(float) * max_seq_len * (head_dim / 2)) != cudaSuccess ||
+      dev_alloc(&c->d_err, 256) != cudaSuccess ||
+      dev_alloc(&c->d_seg_info, sizeof(int2) * pl::kMaxLaunchSeqs) != cudaSuccess ||
+      dev_alloc(&c->d_work, 2 * sizeof(int)) != cudaSuccess) {
     free_ctx(c);
     return PL_ENOMEM;
   }
@@ -716,6 +754,11 @@ int pl_attn_init(int n_layers, int n_heads, int n_kv_heads, int head_dim, int ma
   cudaMemsetAsync(c->d_err, 0, 256, c->stream);
   cudaMemsetAsync(c->d_seg_info, 0, sizeof(int2) * pl::kMaxLaunchSeqs, c->stream);
   cudaMemsetAsync(c->d_work, 0, 2 * sizeof(int), c->stream);
+  {
+    const uint64_t ns = pl::kDefaultWaitLimitNs;
+    cudaMemcpyToSymbolAsync(pl::g_wait_limit_ns, &ns, sizeof(ns), 0, cudaMemcpyHostToDevice,
+                            c->stream);
+  }
   {
     const size_t n = static_cast<size_t>(max_seq_len) * (head_dim / 2);
     float* hc = static_cast<float*>(std::malloc(n * sizeof(float)));
@@ -977,7 +1020,7 @@ int pl_attn_xfer_setup(int world, int rank, void* handle_out) {
   Xfer* x = new Xfer;
   x->world = world;
   x->rank = rank;
-  if (cudaMalloc(&x->local, bytes) != cudaSuccess) {
+  if (dev_alloc(&x->local, bytes) != cudaSuccess) {
     delete x;
     return PL_ENOMEM;
   }
@@ -1210,6 +1253,25 @@ int pl_attn_prefill_dev(int seq, int layer, int start_pos, int n_tok, const floa
                         pick_stream(stream));
 }
 
+int pl_attn_set_wait_limit(double seconds) {
+  if (!g) return PL_ESTATE;
+  if (!(seconds >= 1e-4 && seconds <= 60.0)) return PL_EARG;
+  const uint64_t ns = static_cast<uint64_t>(seconds * 1e9);
+  if (cudaSetDevice(g->device) != cudaSuccess) return PL_ECUDA;
+  PL_CUDA(cudaMemcpyToSymbol(pl::g_wait_limit_ns, &ns, sizeof(ns)));
+  return PL_OK;
+}
+
+int pl_attn_status(void* stream) {
+  if (!g) return PL_ESTATE;
+  if (cudaSetDevice(g->device) != cudaSuccess) return PL_ECUDA;
+  PL_CUDA(cudaStreamSynchronize(pick_stream(stream)));
+  uint32_t w = 0;
+  PL_CUDA(cudaMemcpy(&w, g->d_err, sizeof(w), cudaMemcpyDeviceToHost));
+  if (w) PL_CUDA(cudaMemset(g->d_err, 0, sizeof(uint32_t)));
+  return check_err_word(w);
+}
+
 int pl_attn_profile(int enable) {
   if (!g) return PL_ESTATE;
   g->profiling = enable ? 1 : 0;
@@ -1391,7 +1453,7 @@ int ensure_blk(size_t floats) {
   }
   g->d_blk = nullptr;
   g->blk_cap = 0;
-  if (cudaMalloc(&g->d_blk, floats * sizeof(float)) != cudaSuccess) return PL_ENOMEM;
+  if (dev_alloc(&g->d_blk, floats * sizeof(float)) != cudaSuccess) return PL_ENOMEM;
   g->blk_cap = floats;
   return PL_OK;
 }
@@ -1429,7 +1491,7 @@ int launch_proj(pl::ProjArgs a, cudaStream_t st, bool allow_mma) {
         }
         g->d_proj_part = nullptr;
         g->proj_part_cap = 0;
-        if (cudaMalloc(&g->d_proj_part, need * sizeof(float)) != cudaSuccess) return PL_ENOMEM;
+        if (dev_alloc(&g->d_proj_part, need * sizeof(float)) != cudaSuccess) return PL_ENOMEM;
         g->proj_part_cap = need;
       }
       a.part = g->d_proj_part;
@@ -1617,7 +1679,7 @@ int pl_attn_set_layer(int layer, int dim, const float* attn_norm, float rms_eps,
     if (fsrc[i]) std::memcpy(h.data() + foff[i], fsrc[i], static_cast<size_t>(flen[i]) * 4);
   if (cudaSetDevice(g->device) != cudaSuccess) return PL_ECUDA;
   uint8_t* mem = nullptr;
-  if (cudaMalloc(&mem, total) != cudaSuccess) return PL_ENOMEM;
+  if (dev_alloc(&mem, total) != cudaSuccess) return PL_ENOMEM;
   if (cudaMemcpy(mem, h.data(), total, cudaMemcpyHostToDevice) != cudaSuccess) {
     cudaFree(mem);
     return PL_ECUDA;

@@ -16,9 +16,16 @@ enum : uint32_t {
   ERR_BAD_ARG = 8u,         // device-side argument check failed
 };
 
-// Bound on any spin-wait: 2 s of %globaltimer.  A healthy wait here lasts
-// microseconds; the bound only turns a would-be hang into an error status.
-constexpr uint64_t kWaitLimitNs = 2000000000ull;
+// Bound on any spin-wait, in ns of %globaltimer: 2 s unless the host sets
+// another (pl_attn_set_wait_limit; one copy per device).  A healthy wait
+// here lasts microseconds; the bound only turns a would-be hang into an
+// error status.  Read once per wait that does not complete at once.
+constexpr uint64_t kDefaultWaitLimitNs = 2000000000ull;
+__device__ uint64_t g_wait_limit_ns = kDefaultWaitLimitNs;
+
+__device__ __forceinline__ uint64_t wait_limit_ns() {
+  return *reinterpret_cast<volatile uint64_t*>(&g_wait_limit_ns);
+}
 
 __device__ __forceinline__ uint64_t globaltimer() {
   uint64_t t;
@@ -70,11 +77,11 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 // winds down.
 __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity) {
   if (mbar_try_wait(bar, parity)) return true;
-  const uint64_t t0 = globaltimer();
+  const uint64_t t0 = globaltimer(), lim = wait_limit_ns();
   while (true) {
     for (int i = 0; i < 64; ++i)
       if (mbar_try_wait(bar, parity)) return true;
-    if (globaltimer() - t0 > kWaitLimitNs) return false;
+    if (globaltimer() - t0 > lim) return false;
   }
 }
 
