@@ -345,10 +345,13 @@ def register_all(at, arrays):
     return done
 
 
-def cpu_decode_sample(max_seconds: float = 15.0, n_threads: int | None = None):
+def cpu_decode_sample(max_seconds: float = 15.0, n_threads: int | None = None,
+                      steps: int | None = None, warmup: int = 0):
     """picolm's CPU attention on the config-4 workload: full decode steps of
     all 64 sequences (2048+ cached rows each), independent sequences spread
-    over the host's threads, until ~max_seconds of work."""
+    over the host's threads.  With `steps`, `warmup` untimed steps and then
+    exactly `steps` timed ones (the reference arm); else timed steps until
+    ~max_seconds of work."""
     from oracle import oracle as O
     use_ref = O.ref_available()
     n_threads = n_threads or os.cpu_count() or 1
@@ -362,26 +365,135 @@ def cpu_decode_sample(max_seconds: float = 15.0, n_threads: int | None = None):
     kf, vf = kc.reshape(-1), vc.reshape(-1)
     c = O.cfg(H, HK, HD, ms)
     tables = O.rope_tables(ms, HD, 10000.0)
-    total_bytes, steps = 0, 0
-    t0 = time.perf_counter()
-    while steps < NSTEP:
-        p = CTX + steps
+    def one_step(j):
+        p = CTX + j % NSTEP  # the config's 64 positions, cycled like the GPU arm
         q = rng.standard_normal(SEQS_PER_GPU * Q_DIM, dtype=np.float32)
         k = rng.standard_normal(SEQS_PER_GPU * KV_DIM, dtype=np.float32)
         v = rng.standard_normal(SEQS_PER_GPU * KV_DIM, dtype=np.float32)
         O.attn_decode_seqs(c, kf, vf, ms * KV_DIM, np.full(SEQS_PER_GPU, p, np.int32), q, k, v,
                            *tables, n_threads=n_threads, use_ref=use_ref)
-        total_bytes += step_bytes(p, SEQS_PER_GPU)
+        return step_bytes(p, SEQS_PER_GPU)
+
+    for j in range(warmup):
+        one_step(j)
+    total_bytes, n = 0, 0
+    t0 = time.perf_counter()
+    while (n < steps) if steps is not None else (n < NSTEP):
+        total_bytes += one_step(warmup + n)
+        n += 1
+        if steps is None and time.perf_counter() - t0 > max_seconds:
+            break
+    dt = time.perf_counter() - t0
+    return {"value": total_bytes / dt / 1e9, "unit": "GB/s", "cores": n_threads,
+            "kind": "reference" if use_ref else "port", "steps": n,
+            "sample": f"{n} full decode steps x {SEQS_PER_GPU} seqs at positions {CTX}.."
+                      f"{CTX + NSTEP - 1} cycled (config 4), {n_threads} threads, one sequence "
+                      f"per thread at a time (picolm's attention loop is single-threaded)",
+            "s_per_step": dt / n}
+
+
+def cpu_config1_sample(max_seconds: float = 3.0):
+    """picolm's CPU attention on config 1: one TinyLlama decode layer at
+    position 255 (255 cached rows), one call at a time on one thread, as
+    model_forward_ex runs it."""
+    from oracle import oracle as O
+    use_ref = O.ref_available()
+    rng = np.random.default_rng(0)
+    ms = 256
+    kc0 = np.zeros((ms, KV_DIM), np.uint16)
+    vc0 = np.zeros((ms, KV_DIM), np.uint16)
+    kc0[:255] = make_cache_host(rng, 255, KV_DIM)
+    vc0[:255] = make_cache_host(rng, 255, KV_DIM)
+    c = O.cfg(H, HK, HD, ms)
+    tables = O.rope_tables(ms, HD, 10000.0)
+    q = rng.standard_normal(Q_DIM, dtype=np.float32)
+    k = rng.standard_normal(KV_DIM, dtype=np.float32)
+    v = rng.standard_normal(KV_DIM, dtype=np.float32)
+    pos = np.array([255], np.int32)
+    kc, vc = kc0.ravel().copy(), vc0.ravel().copy()
+    n, t_sum = 0, 0.0
+    while t_sum < max_seconds or n < 3:
+        qq, kk = q.copy(), k.copy()  # the loop rotates q and k in place
+        t0 = time.perf_counter()
+        O.attn_decode_seqs(c, kc, vc, ms * KV_DIM, pos, qq, kk, v, *tables, n_threads=1,
+                           use_ref=use_ref)
+        t_sum += time.perf_counter() - t0
+        n += 1
+    return {"value": t_sum / n * 1e6, "unit": "us per call", "cores": 1,
+            "kind": "reference" if use_ref else "port",
+            "sample": f"{n} calls of one decode layer at position 255 (config 1), one thread "
+                      f"(picolm's attention loop is single-threaded)"}
+
+
+def cpu_prefill_sample(n_threads: int | None = None):
+    """picolm's CPU attention on config 3: full causal prefills of 2048
+    positions, each layer's positions one after another on one thread (as
+    model_forward_prefill runs them), independent layers on separate host
+    threads -- one full layer per thread, min(threads, 22) layers."""
+    from oracle import oracle as O
+    use_ref = O.ref_available()
+    n_threads = n_threads or os.cpu_count() or 1
+    L, S = min(n_threads, 22), 2048
+    rng = np.random.default_rng(2)
+    kc = np.zeros(L * S * KV_DIM, np.uint16)
+    vc = np.zeros(L * S * KV_DIM, np.uint16)
+    q = rng.standard_normal((L, S, Q_DIM), dtype=np.float32).astype(np.float16).astype(np.float32)
+    k = rng.standard_normal((L, S, KV_DIM), dtype=np.float32).astype(np.float16).astype(np.float32)
+    v = rng.standard_normal((L, S, KV_DIM), dtype=np.float32).astype(np.float16).astype(np.float32)
+    c = O.cfg(H, HK, HD, S)
+    tables = O.rope_tables(S, HD, 10000.0)
+    t0 = time.perf_counter()
+    O.attn_prefill_seqs(c, kc, vc, S * KV_DIM, 0, S, q, k, v, *tables, n_threads=L,
+                        use_ref=use_ref)
+    dt = time.perf_counter() - t0
+    flops = 4.0 * H * HD * S * (S + 1) / 2
+    return {"value": flops * L / dt / 1e12, "unit": "TFLOP/s", "cores": L,
+            "kind": "reference" if use_ref else "port",
+            "s_per_layer": dt, "layers_per_s": L / dt,
+            "sample": f"{L} full causal prefill layers of 2048 positions (config 3), one layer "
+                      f"per thread on {L} threads; s_per_layer is one layer's time on one "
+                      f"thread (measured, not extrapolated)"}
+
+
+def cpu_long_ctx_sample(max_seconds: float = 12.0, n_threads: int | None = None):
+    """picolm's CPU attention on config 5: decode steps of one sequence with
+    32768 cached rows over 16 layers (32/8 heads, theta 5e5); the 16 layers
+    of a step are independent here and run on separate host threads, each
+    layer's loop on one thread as in picolm."""
+    from oracle import oracle as O
+    use_ref = O.ref_available()
+    n_threads = n_threads or os.cpu_count() or 1
+    L, HK5, CTX5, NS5 = 16, 8, 32768, 32
+    kv5 = HK5 * HD
+    ms = CTX5 + NS5
+    rng = np.random.default_rng(4)
+    kc = np.zeros((L, ms, kv5), np.uint16)
+    vc = np.zeros((L, ms, kv5), np.uint16)
+    # one layer's rows, copied to all 16 (the loop's time does not depend on
+    # the values; this keeps the set-up short)
+    kc[:, :CTX5] = make_cache_host(rng, CTX5, kv5)
+    vc[:, :CTX5] = make_cache_host(rng, CTX5, kv5)
+    kf, vf = kc.reshape(-1), vc.reshape(-1)
+    c = O.cfg(H, HK5, HD, ms)
+    tables = O.rope_tables(ms, HD, 500000.0)
+    total, steps = 0, 0
+    t0 = time.perf_counter()
+    while steps < NS5:
+        p = CTX5 + steps
+        q = rng.standard_normal(L * Q_DIM, dtype=np.float32)
+        k = rng.standard_normal(L * kv5, dtype=np.float32)
+        v = rng.standard_normal(L * kv5, dtype=np.float32)
+        O.attn_decode_seqs(c, kf, vf, ms * kv5, np.full(L, p, np.int32), q, k, v, *tables,
+                           n_threads=min(n_threads, L), use_ref=use_ref)
+        total += L * ((p + 1) * kv5 * 4 + Q_DIM * 8 + kv5 * 12)
         steps += 1
         if time.perf_counter() - t0 > max_seconds:
             break
     dt = time.perf_counter() - t0
-    return {"value": total_bytes / dt / 1e9, "unit": "GB/s", "cores": n_threads,
-            "kind": "reference" if use_ref else "port",
-            "sample": f"{steps} full decode steps x {SEQS_PER_GPU} seqs at pos {CTX}..{CTX + steps - 1} "
-                      f"(config 4), {n_threads} threads, one sequence per thread at a time "
-                      f"(picolm's attention loop is single-threaded)",
-            "s_per_step": dt / steps}
+    return {"value": total / dt / 1e9, "unit": "GB/s", "cores": min(n_threads, L),
+            "kind": "reference" if use_ref else "port", "ms_per_step_16_layers": dt / steps * 1e3,
+            "sample": f"{steps} decode steps (16 layers each) at positions {CTX5}.."
+                      f"{CTX5 + steps - 1} (config 5), layers on {min(n_threads, L)} threads"}
 
 
 def run_prefill(args, local, peaks):
@@ -977,15 +1089,15 @@ def main():
     if args.impl == "reference":
         if rank != 0:
             return
-        r = cpu_decode_sample(max_seconds=20.0)
+        r = cpu_decode_sample(steps=args.steps, warmup=args.warmup)
         line = dict(base)
         line.update({"impl": "reference", "value": r["value"],
-                     "ms_per_step": r["s_per_step"] * 1e3,
+                     "ms_per_step": r["s_per_step"] * 1e3, "steps": r["steps"],
+                     "warmup": args.warmup,
                      "cpu_baseline": {k: r[k] for k in ("value", "unit", "cores", "kind",
                                                         "sample")},
                      "e2e": {"value": r["value"], "unit": "GB/s", "h2d_bytes_per_step": 0,
                              "d2h_bytes_per_step": 0}})
-        line["steps"] = args.steps
         print(json.dumps(line), flush=True)
         return
 
@@ -1030,6 +1142,10 @@ def main():
         line["block"] = run_block(args, local, peaks)
         cb = cpu_decode_sample(max_seconds=15.0)
         line["cpu_baseline"] = {k: cb[k] for k in ("value", "unit", "cores", "kind", "sample")}
+        # the reference CPU path beside the other configs' GPU numbers
+        line["decode1"]["cpu_baseline"] = cpu_config1_sample()
+        line["prefill"]["cpu_baseline"] = cpu_prefill_sample()
+        line["long_ctx"]["cpu_baseline"] = cpu_long_ctx_sample()
     if rank == 0:
         print(json.dumps(line), flush=True)
     if world > 1:

@@ -108,6 +108,9 @@ def ref() -> C.CDLL:
         lib.ref_attn_decode_seqs.argtypes = [C.c_int, C.c_int, C.c_int, C.c_int, _u16p,
                                              _u16p, C.c_long, _i32p, _f32p, _f32p,
                                              _f32p, _f32p, _f32p, _f32p, C.c_int]
+        lib.ref_attn_prefill_seqs.argtypes = [C.c_int, C.c_int, C.c_int, C.c_int, _u16p,
+                                              _u16p, C.c_long, C.c_int, C.c_int, _f32p,
+                                              _f32p, _f32p, _f32p, _f32p, _f32p, C.c_int]
         lib.matmul.argtypes = [_f32p, _f32p, C.c_void_p, C.c_int, C.c_int, C.c_int]
         lib.vec_dot.restype = C.c_float
         lib.vec_dot.argtypes = [C.c_void_p, _f32p, C.c_int, C.c_int]
@@ -187,6 +190,39 @@ def attn_decode_seqs(c: OrcCfg, kc, vc, seq_stride, pos, q, k, v, cos_t, sin_t,
     else:
         port().orc_attn_decode_seqs(C.byref(c), n_seq, kc, vc, int(seq_stride), pos, q,
                                     k, v, cos_t, sin_t, out, int(n_threads))
+    return out
+
+
+def attn_prefill_seqs(c: OrcCfg, kc, vc, seq_stride, start_pos, n_tok, q, k, v, cos_t, sin_t,
+                      n_threads=1, use_ref=False):
+    """Causal prefill of n_seq independent sequences (flat uint16 caches,
+    slab s at s*seq_stride; q [n_seq][n_tok][H*hd], k/v [n_seq][n_tok][kv_dim])
+    over n_threads threads, one sequence per thread at a time."""
+    q = np.array(q, np.float32)
+    k = np.array(k, np.float32)
+    v = np.ascontiguousarray(v, np.float32)
+    n_seq = q.shape[0]
+    qd = c.n_heads * c.head_dim
+    out = np.empty((n_seq, n_tok, qd), np.float32)
+    if use_ref:
+        ref().ref_attn_prefill_seqs(c.n_heads, c.n_kv_heads, c.head_dim, n_seq, kc, vc,
+                                    int(seq_stride), int(start_pos), int(n_tok), q.ravel(),
+                                    k.ravel(), v.ravel(), cos_t, sin_t, out.ravel(),
+                                    int(n_threads))
+        return out
+    from concurrent.futures import ThreadPoolExecutor
+    kv_dim = c.n_kv_heads * c.head_dim
+
+    def one(s):
+        sl = slice(s * seq_stride, (s + 1) * seq_stride)
+        o = np.empty((n_tok, qd), np.float32)
+        port().orc_attn_prefill(C.byref(c), kc[sl], vc[sl], int(start_pos), int(n_tok),
+                                q[s].ravel(), k[s].ravel(), v[s].reshape(-1, kv_dim).ravel(),
+                                cos_t, sin_t, o.ravel(), qd)
+        out[s] = o
+
+    with ThreadPoolExecutor(max(1, int(n_threads))) as ex:
+        list(ex.map(one, range(n_seq)))
     return out
 
 

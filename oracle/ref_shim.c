@@ -309,6 +309,65 @@ int ref_attn_decode_seqs(int n_heads, int n_kv_heads, int head_dim, int n_seq,
     return 0;
 }
 
+/* ---- Causal prefill attention of independent sequences (or layers) ----
+ * model.c:1039-1089 per position: position start_pos + i is rotated,
+ * appended and attends rows [0, start_pos + i], the positions one after
+ * another as model_forward_prefill runs them (the same per-position steps
+ * as decode, ref_decode_one).  Sequence s has cache slab kc + s*seq_stride,
+ * q [n_tok][n_heads*head_dim], k/v [n_tok][kv_dim] at s*n_tok rows, out
+ * likewise.  Independent sequences (for the CPU baseline: the independent
+ * layers of a prefill) are spread over n_threads threads; each sequence
+ * runs on one thread, as picolm's loop does.                              */
+typedef struct {
+    int n_heads, n_kv_heads, head_dim, n_tok, start_pos, s0, s1;
+    uint16_t *kc, *vc;
+    long seq_stride;
+    float *q, *k;
+    const float *v, *cos_tab, *sin_tab;
+    float *out;
+} ref_pf_job;
+
+static void *ref_pf_worker(void *arg) {
+    ref_pf_job *j = (ref_pf_job *)arg;
+    int q_dim = j->n_heads * j->head_dim;
+    int kv_dim = j->n_kv_heads * j->head_dim;
+    int half = j->head_dim / 2;
+    for (int s = j->s0; s < j->s1; ++s)
+        for (int i = 0; i < j->n_tok; ++i) {
+            size_t row = (size_t)s * j->n_tok + i;
+            int pos = j->start_pos + i;
+            ref_decode_one(j->n_heads, j->n_kv_heads, j->head_dim,
+                           j->kc + s * j->seq_stride, j->vc + s * j->seq_stride, pos,
+                           j->q + row * q_dim, j->k + row * kv_dim, j->v + row * kv_dim,
+                           j->cos_tab + (size_t)pos * half, j->sin_tab + (size_t)pos * half,
+                           j->out + row * q_dim);
+        }
+    return NULL;
+}
+
+int ref_attn_prefill_seqs(int n_heads, int n_kv_heads, int head_dim, int n_seq,
+                          uint16_t *kc, uint16_t *vc, long seq_stride, int start_pos,
+                          int n_tok, float *q, float *k, const float *v,
+                          const float *cos_tab, const float *sin_tab, float *out,
+                          int n_threads) {
+    if (n_threads < 1) n_threads = 1;
+    if (n_threads > n_seq) n_threads = n_seq;
+    if (n_threads > 256) n_threads = 256;
+    ref_pf_job jobs[256];
+    pthread_t tid[256];
+    for (int t = 0; t < n_threads; ++t) {
+        ref_pf_job j = {n_heads, n_kv_heads, head_dim, n_tok, start_pos,
+                        (int)((long)n_seq * t / n_threads),
+                        (int)((long)n_seq * (t + 1) / n_threads), kc, vc, seq_stride,
+                        q, k, v, cos_tab, sin_tab, out};
+        jobs[t] = j;
+    }
+    for (int t = 1; t < n_threads; ++t) pthread_create(&tid[t], NULL, ref_pf_worker, &jobs[t]);
+    ref_pf_worker(&jobs[0]);
+    for (int t = 1; t < n_threads; ++t) pthread_join(tid[t], NULL);
+    return 0;
+}
+
 /* ---- Array forms of the reference's FP16 conversions (quant.c:11-78), so
  * that bit patterns (NaN payloads included) never pass through a host
  * language's float type on the way in or out.                           */

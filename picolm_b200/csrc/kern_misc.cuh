@@ -48,16 +48,13 @@ __global__ void rope_inplace_kernel(float* q, float* k, int n_heads, int n_kv_he
 //                    residual, so that hi + lo carries y to about 2^-22
 //   kc[start+r]   = picolm_FP16(RoPE(k[r]))          (bit-exact append)
 //   vc[start+r]   = picolm_FP16(v[r])
-// grid = n_tok (one block per token row), block = kPrologueThreads.  A row
-// is cut into units of 8 elements of one head (q heads, then k heads, then
-// v heads; HD/8 units per head); thread t takes units t, t + 256, ...
+// A row is cut into units of 8 elements of one head (q heads, then k heads,
+// then v heads; HD/8 units per head).
 // LLaMA units are 8 consecutive elements (4 rotated pairs); Qwen units are
 // elements 4c..4c+3 and HD/2+4c..HD/2+4c+3, which rotate into each other.
 // With q16 null the q units are skipped (the cache rows alone).  Every input and all
-// RoPE factors of a unit are 16-byte loads, and a thread issues the loads of
-// two units before it computes either, so the kernel streams at HBM rate
-// instead of waiting on one load at a time.  q, k, v rows and the cache
-// rows must be 16-byte aligned.
+// RoPE factors of a unit are 16-byte loads.  q, k, v rows and the cache rows
+// must be 16-byte aligned.
 constexpr int kPrologueThreads = 256;
 
 struct PrologueUnit {
@@ -173,8 +170,16 @@ __device__ __forceinline__ void prologue_store(const PrologueUnit& pu, int r, ui
   }
 }
 
+// The (row, unit) pairs of the call are one flattened list, walked by a
+// persistent grid of kPrologueBlocksPerSm blocks per SM: each thread takes
+// kPrologueUnitsInFlight units per round, all their loads issued before any
+// compute, so every SM keeps ~100 KB of loads in flight (HBM latency x
+// bandwidth is ~45 KB per SM) and no block waits out one load at a time.
+constexpr int kPrologueBlocksPerSm = 3;
+constexpr int kPrologueUnitsInFlight = 2;
+
 template <int HD>
-__global__ void __launch_bounds__(kPrologueThreads)
+__global__ void __launch_bounds__(kPrologueThreads, kPrologueBlocksPerSm)
     prefill_prologue_kernel(const float* __restrict__ q, const float* __restrict__ k,
                             const float* __restrict__ v, uint16_t* __restrict__ q16,
                             long q16_lo_off, uint16_t* __restrict__ kc_rows,
@@ -184,26 +189,47 @@ __global__ void __launch_bounds__(kPrologueThreads)
   // the attention grid queued behind (programmatic dependent launch) may
   // start its set-up now; it waits for this grid before touching its output
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
-  const int r = blockIdx.x;
-  if (r >= n_tok) return;
-  const int pos = start_pos + r;
-  const float* cs = cos_tab + static_cast<size_t>(pos) * (HD / 2);
-  const float* sn = sin_tab + static_cast<size_t>(pos) * (HD / 2);
+  constexpr int U = kPrologueUnitsInFlight;
   const int u0 = q16 ? 0 : n_heads * (HD / 8);  // without q16: the cache rows alone
-  const int n_units = (n_heads + 2 * n_kv_heads) * (HD / 8);
-  for (int u = u0 + threadIdx.x; u < n_units; u += 2 * kPrologueThreads) {
-    const int u2 = u + kPrologueThreads;
-    const PrologueUnit a =
-        prologue_load<HD>(u, r, q, k, v, n_heads, n_kv_heads, cs, sn, rope_type);
-    PrologueUnit b;
-    b.kind = -1;
-    if (u2 < n_units)
-      b = prologue_load<HD>(u2, r, q, k, v, n_heads, n_kv_heads, cs, sn, rope_type);
-    prologue_store<HD>(a, r, q16, q16_lo_off, kc_rows, vc_rows, n_heads, n_kv_heads, rope_type);
-    if (b.kind >= 0)
-      prologue_store<HD>(b, r, q16, q16_lo_off, kc_rows, vc_rows, n_heads, n_kv_heads,
-                         rope_type);
+  const int per_row = (n_heads + 2 * n_kv_heads) * (HD / 8) - u0;
+  const long total = static_cast<long>(n_tok) * per_row;
+  const long stride = static_cast<long>(gridDim.x) * kPrologueThreads * U;
+  for (long f0 = static_cast<long>(blockIdx.x) * kPrologueThreads * U + threadIdx.x; f0 < total;
+       f0 += stride) {
+    PrologueUnit pu[U];
+    int row[U];
+#pragma unroll
+    for (int j = 0; j < U; ++j) {
+      const long f = f0 + static_cast<long>(j) * kPrologueThreads;
+      pu[j].kind = -1;
+      row[j] = 0;
+      if (f < total) {
+        const int r = static_cast<int>(f / per_row);
+        const int u = u0 + static_cast<int>(f - static_cast<long>(r) * per_row);
+        const size_t trow = static_cast<size_t>(start_pos + r) * (HD / 2);
+        pu[j] = prologue_load<HD>(u, r, q, k, v, n_heads, n_kv_heads, cos_tab + trow,
+                                  sin_tab + trow, rope_type);
+        row[j] = r;
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < U; ++j)
+      if (pu[j].kind >= 0)
+        prologue_store<HD>(pu[j], row[j], q16, q16_lo_off, kc_rows, vc_rows, n_heads,
+                           n_kv_heads, rope_type);
   }
+}
+
+// Blocks of the prologue grid: enough for every unit, at most
+// kPrologueBlocksPerSm per SM.
+inline int prologue_grid(int n_tok, int n_heads, int n_kv_heads, int head_dim, bool with_q,
+                         int num_sms) {
+  const long per_row = static_cast<long>(with_q ? n_heads + 2 * n_kv_heads : 2 * n_kv_heads) *
+                       (head_dim / 8);
+  const long per_block = static_cast<long>(kPrologueThreads) * kPrologueUnitsInFlight;
+  const long need = (static_cast<long>(n_tok) * per_row + per_block - 1) / per_block;
+  const long cap = static_cast<long>(num_sms) * kPrologueBlocksPerSm;
+  return static_cast<int>(need < cap ? (need < 1 ? 1 : need) : cap);
 }
 
 }  // namespace pl

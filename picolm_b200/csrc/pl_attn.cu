@@ -1153,14 +1153,18 @@ static int launch_prefill(int seq, int layer, int start_pos, int n_tok, const fl
   int rc = ensure_q16(n_tok);
   if (rc) return rc;
   const size_t off = static_cast<size_t>(start_pos) * g->kv_dim;
+  const int pgrid =
+      pl::prologue_grid(n_tok, g->n_heads, g->n_kv_heads, g->head_dim, true, g->num_sms);
   if (g->head_dim == 128)
-    pl::prefill_prologue_kernel<128><<<n_tok, pl::kPrologueThreads, 0, st>>>(
-        d_q, d_k, d_v, g->d_q16, static_cast<long>(g->q16_cap), slab_k(seq, layer) + off, slab_v(seq, layer) + off, n_tok,
-        g->n_heads, g->n_kv_heads, start_pos, g->d_cos, g->d_sin, g->rope_type);
+    pl::prefill_prologue_kernel<128><<<pgrid, pl::kPrologueThreads, 0, st>>>(
+        d_q, d_k, d_v, g->d_q16, static_cast<long>(g->q16_cap), slab_k(seq, layer) + off,
+        slab_v(seq, layer) + off, n_tok, g->n_heads, g->n_kv_heads, start_pos, g->d_cos,
+        g->d_sin, g->rope_type);
   else
-    pl::prefill_prologue_kernel<64><<<n_tok, pl::kPrologueThreads, 0, st>>>(
-        d_q, d_k, d_v, g->d_q16, static_cast<long>(g->q16_cap), slab_k(seq, layer) + off, slab_v(seq, layer) + off, n_tok,
-        g->n_heads, g->n_kv_heads, start_pos, g->d_cos, g->d_sin, g->rope_type);
+    pl::prefill_prologue_kernel<64><<<pgrid, pl::kPrologueThreads, 0, st>>>(
+        d_q, d_k, d_v, g->d_q16, static_cast<long>(g->q16_cap), slab_k(seq, layer) + off,
+        slab_v(seq, layer) + off, n_tok, g->n_heads, g->n_kv_heads, start_pos, g->d_cos,
+        g->d_sin, g->rope_type);
   PL_CUDA(cudaGetLastError());
   count_launch();
   pl::PrefillArgs a;
