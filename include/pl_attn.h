@@ -54,6 +54,9 @@ extern "C" {
 #define PL_ROPE_LLAMA 0       /* pairs (2i, 2i+1)   -- tensor.c:558-601 */
 #define PL_ROPE_QWEN  1       /* pairs (i, i+hd/2)  -- tensor.c:537-557 */
 
+#define PL_SPLIT_SEQS 0       /* pl_attn_init_devices: slots spread over devices */
+#define PL_SPLIT_KV   1       /* pl_attn_init_devices: every slot's rows spread  */
+
 #ifndef PL_ATTN_DISABLED
 
 /* ---- Lifecycle (cf. gpu_init / gpu_available / gpu_shutdown,
@@ -67,6 +70,33 @@ extern "C" {
 int  pl_attn_init(int n_layers, int n_heads, int n_kv_heads, int head_dim,
                   int max_seq_len, float rope_freq_base, int rope_type,
                   int n_seqs, int device);
+
+/* The same context over n_devices GPUs of this process (1..16; an id may
+ * repeat, which runs the split on one GPU).  The host-buffer entry points
+ * below, pl_kv_download / pl_kv_upload, pl_attn_set_rope, pl_attn_rope,
+ * pl_attn_status, pl_attn_set_wait_limit and the profiling calls fan out to
+ * the devices internally, from the one host thread that drives the module;
+ * peer access is enabled between every pair.  No counterpart in the
+ * reference, whose gpu.c drives one device (picolm/gpu.c:34-83).
+ *   PL_SPLIT_SEQS  slots [d*n_seqs/D, (d+1)*n_seqs/D) live on devices[d];
+ *                  a batch is split by slot owner and each device runs its
+ *                  part with no exchange (independent sequences).
+ *   PL_SPLIT_KV    every slot's cache rows are spread over the devices in
+ *                  blocks of 512 positions (block b on devices[b % D]).  A
+ *                  decode step runs a partial over each device's rows in
+ *                  parallel and merges the (max, sum, output) triples on
+ *                  devices[0] with a log-sum-exp combine that reads the
+ *                  other devices' partials over NVLink; a prefill gathers
+ *                  the earlier rows onto devices[0], runs there, and returns
+ *                  each new row to its owner.  Memory per device: about
+ *                  1/D of the cache.
+ * The device-pointer (_dev), KV-exchange (xfer) and projection (block)
+ * entry points need a single-device context and return PL_EUNSUPPORTED on
+ * a multi-device one.  pl_attn_init is pl_attn_init_devices with one device. */
+int  pl_attn_init_devices(int n_layers, int n_heads, int n_kv_heads,
+                          int head_dim, int max_seq_len, float rope_freq_base,
+                          int rope_type, int n_seqs, int n_devices,
+                          const int *devices, int split);
 
 /* Replace the device RoPE tables with host tables [n_rows][half_dim]
  * (model.c's s->rope_cos / s->rope_sin), copied once. */
@@ -342,6 +372,16 @@ static inline int pl_attn_init(int n_layers, int n_heads, int n_kv_heads,
     (void)n_layers; (void)n_heads; (void)n_kv_heads; (void)head_dim;
     (void)max_seq_len; (void)rope_freq_base; (void)rope_type; (void)n_seqs;
     (void)device; return PL_EDEVICE;
+}
+static inline int pl_attn_init_devices(int n_layers, int n_heads,
+                                       int n_kv_heads, int head_dim,
+                                       int max_seq_len, float rope_freq_base,
+                                       int rope_type, int n_seqs,
+                                       int n_devices, const int *devices,
+                                       int split) {
+    (void)n_layers; (void)n_heads; (void)n_kv_heads; (void)head_dim;
+    (void)max_seq_len; (void)rope_freq_base; (void)rope_type; (void)n_seqs;
+    (void)n_devices; (void)devices; (void)split; return PL_EDEVICE;
 }
 static inline int pl_attn_set_rope(const float *cos_tab, const float *sin_tab,
                                    int n_rows, int half_dim) {

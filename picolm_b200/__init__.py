@@ -34,6 +34,8 @@ PL_EDEVICE = -7
 PL_EUNSUPPORTED = -8
 PL_ROPE_LLAMA = 0
 PL_ROPE_QWEN = 1
+PL_SPLIT_SEQS = 0
+PL_SPLIT_KV = 1
 # GGUF tensor types the projections take (picolm/quant.h:49-63)
 PL_GGUF_F32 = 0
 PL_GGUF_F16 = 1
@@ -82,6 +84,7 @@ def load(path: str = LIB_PATH) -> C.CDLL:
         "pl_attn_host_register": (i, [C.c_void_p, C.c_size_t]),
         "pl_attn_host_unregister": (i, [C.c_void_p]),
         "pl_attn_init": (i, [i, i, i, i, i, C.c_float, i, i, i]),
+        "pl_attn_init_devices": (i, [i, i, i, i, i, C.c_float, i, i, i, _i32p, i]),
         "pl_attn_set_rope": (i, [_f32p, _f32p, i, i]),
         "pl_attn_available": (i, []),
         "pl_attn_shutdown": (None, []),
@@ -147,16 +150,26 @@ class Attn:
 
     def __init__(self, n_layers: int, n_heads: int, n_kv_heads: int, max_seq: int,
                  rope_base: float = 10000.0, rope_type: int = PL_ROPE_LLAMA,
-                 n_seqs: int = 1, device: int = 0, head_dim: int = HEAD_DIM):
+                 n_seqs: int = 1, device: int = 0, head_dim: int = HEAD_DIM,
+                 devices=None, split: int = PL_SPLIT_SEQS):
+        """pl_attn_init on `device`, or pl_attn_init_devices over the list
+        `devices` (ids may repeat) with `split` PL_SPLIT_SEQS / PL_SPLIT_KV."""
         self.lib = load()
         self.n_layers, self.n_heads, self.n_kv_heads = n_layers, n_heads, n_kv_heads
         self.head_dim, self.max_seq, self.n_seqs = head_dim, max_seq, n_seqs
         self.q_dim = n_heads * head_dim
         self.kv_dim = n_kv_heads * head_dim
         self.part_stride = part_stride(head_dim)
-        _check(self.lib.pl_attn_init(n_layers, n_heads, n_kv_heads, head_dim, max_seq,
-                                     float(rope_base), rope_type, n_seqs, device),
-               "pl_attn_init")
+        if devices is None:
+            _check(self.lib.pl_attn_init(n_layers, n_heads, n_kv_heads, head_dim, max_seq,
+                                         float(rope_base), rope_type, n_seqs, device),
+                   "pl_attn_init")
+        else:
+            devs = np.ascontiguousarray(devices, np.int32)
+            _check(self.lib.pl_attn_init_devices(n_layers, n_heads, n_kv_heads, head_dim,
+                                                 max_seq, float(rope_base), rope_type, n_seqs,
+                                                 devs.size, devs, split),
+                   "pl_attn_init_devices")
         self._open = True
 
     # lifecycle ---------------------------------------------------------

@@ -82,6 +82,8 @@ constexpr int kMaxCombineParts = 16;    // device partials merged by combine_ker
 struct DecodeArgs {
   // cache geometry
   int n_layers, max_seq, n_heads, n_kv_heads, kv_mul, layer, rope_type, n_slots;
+  int pos_limit;         // positions are < pos_limit (RoPE table rows); max_seq is the
+                         // cache rows per slab (fewer on a device holding a KV shard)
   const float* cos_tab;  // [rope_rows][32]
   const float* sin_tab;
   uint16_t* kc;          // [slots][n_layers][max_seq][kv_dim]
@@ -191,7 +193,7 @@ __device__ __forceinline__ int seq_tiles(const DecodeArgs& a, int i, bool hint, 
   const int pos = a.pos ? (hint ? __ldcg(a.pos + i) : a.pos[i]) : a.pos1;
   const int att_rows = a.mode == 0 ? pos + 1 : a.n_rows;
   const int app_row = a.mode == 0 ? (a.append ? pos : -1) : (a.append ? pos - a.row0 : -1);
-  bad = seq < 0 || seq >= a.n_slots || pos < 0 || pos >= a.max_seq || att_rows < 0 ||
+  bad = seq < 0 || seq >= a.n_slots || pos < 0 || pos >= a.pos_limit || att_rows < 0 ||
         att_rows > a.max_seq || app_row >= a.max_seq;
   return bad ? 0 : (att_rows + TP - 1) / TP;
 }
@@ -785,6 +787,57 @@ __global__ void __launch_bounds__(256) combine_kernel(int n_part, int n_heads,
   extern __shared__ float smem_w[];
   merge_slots<kMaxCombineParts, HD>(parts, static_cast<size_t>(n_heads) * part_stride(HD), n_part,
                                     n_heads, out, nullptr, smem_w);
+}
+
+// Log-sum-exp merge of partials that sit on several devices of one process
+// (a KV split inside one module context): the n_part partial blocks are read
+// straight from the other devices' memory over NVLink (plain loads; the
+// device has peer access to them), after the stream has waited on each
+// producer's event.  grid = ceil(n_heads * HD/4 / 256), block = 256: thread
+// t owns float4 q4 of head h and loads (m, l) and o of every partial first.
+constexpr int kMaxPeerParts = 16;
+struct PeerParts {
+  const float* p[kMaxPeerParts];
+};
+
+template <int HD>
+__global__ void __launch_bounds__(256) combine_peers_kernel(PeerParts parts, int n_part,
+                                                            int n_heads,
+                                                            float* __restrict__ out) {
+  constexpr int PS = part_stride(HD);
+  const int idx = blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= n_heads * (HD / 4)) return;
+  const int h = idx / (HD / 4), q4 = idx % (HD / 4);
+  float2 ml[kMaxPeerParts];
+  float4 o[kMaxPeerParts];
+#pragma unroll
+  for (int j = 0; j < kMaxPeerParts; ++j)
+    if (j < n_part) {
+      const float* base = parts.p[j] + h * PS;
+      ml[j] = __ldcg(reinterpret_cast<const float2*>(base));
+      o[j] = __ldcg(reinterpret_cast<const float4*>(base + kPartO) + q4);
+    }
+  float M = -INFINITY;
+#pragma unroll
+  for (int j = 0; j < kMaxPeerParts; ++j)
+    if (j < n_part) M = fmaxf(M, ml[j].x);
+  float L = 0.f;
+  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+  if (M != -INFINITY) {
+#pragma unroll
+    for (int j = 0; j < kMaxPeerParts; ++j)
+      if (j < n_part) {
+        const float w = ex2(ml[j].x - M);
+        L += w * ml[j].y;
+        acc.x += w * o[j].x;
+        acc.y += w * o[j].y;
+        acc.z += w * o[j].z;
+        acc.w += w * o[j].w;
+      }
+  }
+  const float inv = 1.0f / L;
+  reinterpret_cast<float4*>(out + h * HD)[q4] =
+      make_float4(acc.x * inv, acc.y * inv, acc.z * inv, acc.w * inv);
 }
 
 }  // namespace pl

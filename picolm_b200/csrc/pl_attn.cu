@@ -64,6 +64,8 @@ struct LayerW {
 struct Ctx {
   int device = -1;
   int n_layers = 0, n_heads = 0, n_kv_heads = 0, max_seq = 0, n_seqs = 0, rope_type = 0;
+  int rope_rows = 0;          // positions < rope_rows (the model's max_seq_len); max_seq is the
+                              // cache rows per (slot, layer), fewer on a device of a KV split
   int head_dim = 0, kv_dim = 0, q_dim = 0, kv_mul = 0;
   int part_floats = 0;        // floats of one partial block: n_heads * (head_dim + 4)
   int tp = 0;                 // decode tile rows: TP * n_kv_heads * head_dim == 8192, TP >= 16
@@ -109,6 +111,26 @@ struct Ctx {
 
 Ctx* g = nullptr;
 Xfer* g_xfer = nullptr;  // KV-split exchange of the current context, if set up
+
+// A context over several devices (pl_attn_init_devices with n_devices > 1):
+// g is then its first device's context.  Defined at the end of this file.
+struct Multi;
+Multi* g_multi = nullptr;
+void multi_free();
+int multi_set_rope(const float* cos_tab, const float* sin_tab, int n_rows, int half_dim);
+int multi_decode_batch(int layer, int n, const int* seqs, const int* pos, const float* q,
+                       const float* k, const float* v, float* out);
+int multi_prefill(int seq, int layer, int start_pos, int n_tok, const float* q, const float* k,
+                  const float* v, float* out, int out_stride);
+int multi_kv_copy(int seq, int layer, int pos0, int n_pos, uint16_t* k, uint16_t* v,
+                  bool download);
+int multi_status();
+int multi_set_wait_limit(uint64_t ns);
+void multi_profile(int enable);
+int multi_profile_read(double* attn_ms, long* attn_launches, long* all_launches);
+int multi_init(int n_layers, int n_heads, int n_kv_heads, int head_dim, int max_seq_len,
+               float rope_freq_base, int rope_type, int n_seqs, int n_devices,
+               const int* devices, int split);
 
 void xfer_free() {
   if (!g_xfer) return;
@@ -419,6 +441,7 @@ pl::DecodeArgs decode_args(int layer, int n, const int* d_seqs, const int* d_pos
   pl::DecodeArgs a;
   a.n_layers = g->n_layers;
   a.max_seq = g->max_seq;
+  a.pos_limit = g->rope_rows;
   a.n_heads = g->n_heads;
   a.n_kv_heads = g->n_kv_heads;
   a.kv_mul = g->kv_mul;
@@ -451,8 +474,12 @@ pl::DecodeArgs decode_args(int layer, int n, const int* d_seqs, const int* d_pos
   return a;
 }
 
+int decode_smem_bytes_for(int n_kv_heads, int tp, int nstage, int head_dim) {
+  return nstage * 2 * tp * n_kv_heads * head_dim * 2 + 1024 + 2 * nstage * 8;
+}
+
 int decode_smem_bytes(int tp, int nstage, int head_dim) {
-  return nstage * 2 * tp * g->n_kv_heads * head_dim * 2 + 1024 + 2 * nstage * 8;
+  return decode_smem_bytes_for(g->n_kv_heads, tp, nstage, head_dim);
 }
 
 // The decode kernel instantiations: (tile rows, ring depth, head_dim) for
@@ -606,6 +633,23 @@ int launch_decode(int layer, int n, const int* d_seqs, const int* d_pos, int max
   return PL_OK;
 }
 
+// One KV shard's partial (mode 1) for n_rows > 0 local rows: seq and pos
+// travel as kernel arguments (no copy, nothing that could make the host
+// wait for the stream).
+int partial_launch(int seq, int layer, int pos, int row0, int n_rows, int append,
+                   const float* d_q, const float* d_k, const float* d_v, float* d_part,
+                   cudaStream_t st) {
+  const int grid = decode_grid(1, n_rows);
+  const int rc = ensure_part(static_cast<size_t>(grid + 1) * g->part_floats);
+  if (rc) return rc;
+  pl::DecodeArgs a = decode_args(layer, 1, nullptr, nullptr, d_q, d_k ? d_k : d_q,
+                                 d_v ? d_v : d_q, nullptr, 1, row0, n_rows, append ? 1 : 0,
+                                 d_part, g->d_part, g->d_seg_info);
+  a.seq1 = seq;
+  a.pos1 = pos;
+  return launch_decode_kernel(a, grid, st, true);
+}
+
 // Device-pointer calls run on the caller's stream; NULL is the CUDA
 // default (legacy) stream, as everywhere in CUDA.
 cudaStream_t pick_stream(void* s) { return static_cast<cudaStream_t>(s); }
@@ -658,6 +702,141 @@ void free_ctx(Ctx* c) {
   delete c;
 }
 
+// Shape checks shared by every init path (no device needed).
+int check_shape(int n_layers, int n_heads, int n_kv_heads, int head_dim, int max_seq_len,
+                float rope_freq_base, int rope_type, int n_seqs) {
+  if (n_layers <= 0 || n_heads <= 0 || n_kv_heads <= 0 || max_seq_len <= 0 || n_seqs <= 0 ||
+      !(rope_freq_base > 0.f))
+    return PL_EARG;
+  if (head_dim != 64 && head_dim != 128) return PL_EUNSUPPORTED;
+  if (n_heads % n_kv_heads) return PL_EUNSUPPORTED;
+  const int kv_mul = n_heads / n_kv_heads;
+  if (!(n_kv_heads == 1 || n_kv_heads == 2 || n_kv_heads == 4 || n_kv_heads == 8))
+    return PL_EUNSUPPORTED;
+  if (!(kv_mul == 1 || kv_mul == 2 || kv_mul == 4 || kv_mul == 8)) return PL_EUNSUPPORTED;
+  if (rope_type != PL_ROPE_LLAMA && rope_type != PL_ROPE_QWEN) return PL_EARG;
+  return PL_OK;
+}
+
+// One device's context: `n_slots` sequence slots of `cache_rows` rows per
+// layer, RoPE tables for positions [0, rope_rows).  The shape is checked.
+int create_ctx(int n_layers, int n_heads, int n_kv_heads, int head_dim, int rope_rows,
+               float rope_freq_base, int rope_type, int n_slots, int cache_rows, int device,
+               Ctx** out) {
+  *out = nullptr;
+  int ndev = 0;
+  if (cudaGetDeviceCount(&ndev) != cudaSuccess || device < 0 || device >= ndev) return PL_EDEVICE;
+  cudaDeviceProp prop;
+  if (cudaGetDeviceProperties(&prop, device) != cudaSuccess) return PL_EDEVICE;
+  if (prop.major != 10) return PL_EDEVICE;
+  if (cudaSetDevice(device) != cudaSuccess) return PL_EDEVICE;
+
+  Ctx* c = new Ctx();
+  c->device = device;
+  c->n_layers = n_layers;
+  c->n_heads = n_heads;
+  c->n_kv_heads = n_kv_heads;
+  c->max_seq = cache_rows;
+  c->rope_rows = rope_rows;
+  c->n_seqs = n_slots;
+  c->rope_type = rope_type;
+  c->head_dim = head_dim;
+  c->kv_dim = n_kv_heads * head_dim;
+  c->q_dim = n_heads * head_dim;
+  c->part_floats = n_heads * part_stride(head_dim);
+  c->kv_mul = n_heads / n_kv_heads;
+  // a K (or V) tile of 16 KB: all KV heads, TP rows (at least 16, the MMA
+  // row block); at 128 x 8 KV heads that is 32 KB and the ring is 3 deep
+  c->tp = 8192 / (n_kv_heads * head_dim);
+  if (c->tp < 16) c->tp = 16;
+  c->nstage = c->tp * n_kv_heads * head_dim > 8192 ? 3 : kDecodeStages;
+  c->num_sms = prop.multiProcessorCount;
+  c->layer_elems = static_cast<size_t>(cache_rows) * c->kv_dim;
+  const size_t cache_elems = c->layer_elems * n_layers * n_slots;
+
+  int rc = PL_OK;
+  void* fn = nullptr;
+  cudaDriverEntryPointQueryResult qres;
+  if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &qres) !=
+          cudaSuccess ||
+      qres != cudaDriverEntryPointSuccess || !fn) {
+    free_ctx(c);
+    return PL_ECUDA;
+  }
+  c->encode = reinterpret_cast<EncodeTiledFn>(fn);
+
+  if (cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking) != cudaSuccess ||
+      dev_alloc(&c->d_k, cache_elems * 2) != cudaSuccess ||
+      dev_alloc(&c->d_v, cache_elems * 2) != cudaSuccess ||
+      dev_alloc(&c->d_cos, sizeof(float) * rope_rows * (head_dim / 2)) != cudaSuccess ||
+      dev_alloc(&c->d_sin, sizeof(float) * rope_rows * (head_dim / 2)) != cudaSuccess ||
+      dev_alloc(&c->d_err, 256) != cudaSuccess ||
+      dev_alloc(&c->d_seg_info, sizeof(int2) * pl::kMaxLaunchSeqs) != cudaSuccess ||
+      dev_alloc(&c->d_work, 2 * sizeof(int)) != cudaSuccess) {
+    free_ctx(c);
+    return PL_ENOMEM;
+  }
+  cudaMemsetAsync(c->d_k, 0, cache_elems * 2, c->stream);
+  cudaMemsetAsync(c->d_v, 0, cache_elems * 2, c->stream);
+  cudaMemsetAsync(c->d_err, 0, 256, c->stream);
+  cudaMemsetAsync(c->d_seg_info, 0, sizeof(int2) * pl::kMaxLaunchSeqs, c->stream);
+  cudaMemsetAsync(c->d_work, 0, 2 * sizeof(int), c->stream);
+  {
+    const uint64_t ns = pl::kDefaultWaitLimitNs;
+    cudaMemcpyToSymbolAsync(pl::g_wait_limit_ns, &ns, sizeof(ns), 0, cudaMemcpyHostToDevice,
+                            c->stream);
+  }
+  {
+    const size_t n = static_cast<size_t>(rope_rows) * (head_dim / 2);
+    float* hc = static_cast<float*>(std::malloc(n * sizeof(float)));
+    float* hs = static_cast<float*>(std::malloc(n * sizeof(float)));
+    if (!hc || !hs) {
+      std::free(hc);
+      std::free(hs);
+      free_ctx(c);
+      return PL_ENOMEM;
+    }
+    host_rope_tables(hc, hs, rope_rows, head_dim, rope_freq_base);
+    cudaMemcpy(c->d_cos, hc, n * sizeof(float), cudaMemcpyHostToDevice);
+    cudaMemcpy(c->d_sin, hs, n * sizeof(float), cudaMemcpyHostToDevice);
+    std::free(hc);
+    std::free(hs);
+  }
+  const int n_slabs = n_slots * n_layers;
+  if ((rc = make_map(c->encode, &c->tm_k_dec, c->d_k, head_dim, cache_rows, n_kv_heads, n_slabs,
+                     c->tp, n_kv_heads)) ||
+      (rc = make_map(c->encode, &c->tm_v_dec, c->d_v, head_dim, cache_rows, n_kv_heads, n_slabs,
+                     c->tp, n_kv_heads)) ||
+      (rc = make_map(c->encode, &c->tm_k_pf, c->d_k, head_dim, cache_rows, n_kv_heads, n_slabs,
+                     pl::pf_block_n(head_dim), 1)) ||
+      (rc = make_map(c->encode, &c->tm_v_pf, c->d_v, head_dim, cache_rows, n_kv_heads, n_slabs,
+                     pl::pf_block_n(head_dim), 1))) {
+    free_ctx(c);
+    return rc;
+  }
+  // decode grid: as many CTAs as can be resident at once (registers, shared
+  // memory), so the balanced partition runs in a single wave
+  {
+    int per_sm = 0;
+    const int smem = decode_smem_bytes_for(c->n_kv_heads, c->tp, c->nstage, head_dim);
+    const int threads = (n_kv_heads + 1) * 32;
+    const cudaError_t e =
+        with_decode_config(c->tp, c->nstage, head_dim, DecodeOccupancy{&per_sm, threads, smem});
+    if (e != cudaSuccess || per_sm < 1) {
+      free_ctx(c);
+      return PL_ECUDA;
+    }
+    c->decode_slots = c->num_sms * per_sm;
+  }
+  c->lw.resize(static_cast<size_t>(n_layers));
+  if (cudaStreamSynchronize(c->stream) != cudaSuccess) {
+    free_ctx(c);
+    return PL_ECUDA;
+  }
+  *out = c;
+  return PL_OK;
+}
+
 }  // namespace
 
 extern "C" {
@@ -681,135 +860,36 @@ int pl_attn_available(void) { return g != nullptr; }
 
 int pl_attn_init(int n_layers, int n_heads, int n_kv_heads, int head_dim, int max_seq_len,
                  float rope_freq_base, int rope_type, int n_seqs, int device) {
+  return pl_attn_init_devices(n_layers, n_heads, n_kv_heads, head_dim, max_seq_len,
+                              rope_freq_base, rope_type, n_seqs, 1, &device, PL_SPLIT_SEQS);
+}
+
+int pl_attn_init_devices(int n_layers, int n_heads, int n_kv_heads, int head_dim,
+                         int max_seq_len, float rope_freq_base, int rope_type, int n_seqs,
+                         int n_devices, const int* devices, int split) {
   std::lock_guard<std::mutex> lk(g_mu);
   if (g) return PL_ESTATE;
-  if (n_layers <= 0 || n_heads <= 0 || n_kv_heads <= 0 || max_seq_len <= 0 || n_seqs <= 0 ||
-      device < 0 || !(rope_freq_base > 0.f))
-    return PL_EARG;
-  if (head_dim != 64 && head_dim != 128) return PL_EUNSUPPORTED;
-  if (n_heads % n_kv_heads) return PL_EUNSUPPORTED;
-  const int kv_mul = n_heads / n_kv_heads;
-  if (!(n_kv_heads == 1 || n_kv_heads == 2 || n_kv_heads == 4 || n_kv_heads == 8))
-    return PL_EUNSUPPORTED;
-  if (!(kv_mul == 1 || kv_mul == 2 || kv_mul == 4 || kv_mul == 8)) return PL_EUNSUPPORTED;
-  if (rope_type != PL_ROPE_LLAMA && rope_type != PL_ROPE_QWEN) return PL_EARG;
-
-  int ndev = 0;
-  if (cudaGetDeviceCount(&ndev) != cudaSuccess || device >= ndev) return PL_EDEVICE;
-  cudaDeviceProp prop;
-  if (cudaGetDeviceProperties(&prop, device) != cudaSuccess) return PL_EDEVICE;
-  if (prop.major != 10) return PL_EDEVICE;
-  if (cudaSetDevice(device) != cudaSuccess) return PL_EDEVICE;
+  if (n_devices < 1 || n_devices > 16 || !devices) return PL_EARG;
+  if (split != PL_SPLIT_SEQS && split != PL_SPLIT_KV) return PL_EARG;
+  for (int d = 0; d < n_devices; ++d)
+    if (devices[d] < 0) return PL_EARG;
+  int rc = check_shape(n_layers, n_heads, n_kv_heads, head_dim, max_seq_len, rope_freq_base,
+                       rope_type, n_seqs);
+  if (rc) return rc;
   {
     const char* fa = std::getenv("PL_ATTN_FAIL_ALLOC");
     g_fail_alloc.store(fa ? std::atol(fa) : 0);
   }
-
-  Ctx* c = new Ctx();
-  c->device = device;
-  c->n_layers = n_layers;
-  c->n_heads = n_heads;
-  c->n_kv_heads = n_kv_heads;
-  c->max_seq = max_seq_len;
-  c->n_seqs = n_seqs;
-  c->rope_type = rope_type;
-  c->head_dim = head_dim;
-  c->kv_dim = n_kv_heads * head_dim;
-  c->q_dim = n_heads * head_dim;
-  c->part_floats = n_heads * part_stride(head_dim);
-  c->kv_mul = kv_mul;
-  // a K (or V) tile of 16 KB: all KV heads, TP rows (at least 16, the MMA
-  // row block); at 128 x 8 KV heads that is 32 KB and the ring is 3 deep
-  c->tp = 8192 / (n_kv_heads * head_dim);
-  if (c->tp < 16) c->tp = 16;
-  c->nstage = c->tp * n_kv_heads * head_dim > 8192 ? 3 : kDecodeStages;
-  c->num_sms = prop.multiProcessorCount;
-  c->layer_elems = static_cast<size_t>(max_seq_len) * c->kv_dim;
-  const size_t cache_elems = c->layer_elems * n_layers * n_seqs;
-
-  int rc = PL_OK;
-  void* fn = nullptr;
-  cudaDriverEntryPointQueryResult qres;
-  if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &qres) !=
-          cudaSuccess ||
-      qres != cudaDriverEntryPointSuccess || !fn) {
-    free_ctx(c);
-    return PL_ECUDA;
+  if (n_devices == 1) {
+    Ctx* c = nullptr;
+    rc = create_ctx(n_layers, n_heads, n_kv_heads, head_dim, max_seq_len, rope_freq_base,
+                    rope_type, n_seqs, max_seq_len, devices[0], &c);
+    if (rc) return rc;
+    g = c;
+    return PL_OK;
   }
-  c->encode = reinterpret_cast<EncodeTiledFn>(fn);
-
-  if (cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking) != cudaSuccess ||
-      dev_alloc(&c->d_k, cache_elems * 2) != cudaSuccess ||
-      dev_alloc(&c->d_v, cache_elems * 2) != cudaSuccess ||
-      dev_alloc(&c->d_cos, sizeof(float) * max_seq_len * (head_dim / 2)) != cudaSuccess ||
-      dev_alloc(&c->d_sin, sizeof(float) * max_seq_len * (head_dim / 2)) != cudaSuccess ||
-      dev_alloc(&c->d_err, 256) != cudaSuccess ||
-      dev_alloc(&c->d_seg_info, sizeof(int2) * pl::kMaxLaunchSeqs) != cudaSuccess ||
-      dev_alloc(&c->d_work, 2 * sizeof(int)) != cudaSuccess) {
-    free_ctx(c);
-    return PL_ENOMEM;
-  }
-  cudaMemsetAsync(c->d_k, 0, cache_elems * 2, c->stream);
-  cudaMemsetAsync(c->d_v, 0, cache_elems * 2, c->stream);
-  cudaMemsetAsync(c->d_err, 0, 256, c->stream);
-  cudaMemsetAsync(c->d_seg_info, 0, sizeof(int2) * pl::kMaxLaunchSeqs, c->stream);
-  cudaMemsetAsync(c->d_work, 0, 2 * sizeof(int), c->stream);
-  {
-    const uint64_t ns = pl::kDefaultWaitLimitNs;
-    cudaMemcpyToSymbolAsync(pl::g_wait_limit_ns, &ns, sizeof(ns), 0, cudaMemcpyHostToDevice,
-                            c->stream);
-  }
-  {
-    const size_t n = static_cast<size_t>(max_seq_len) * (head_dim / 2);
-    float* hc = static_cast<float*>(std::malloc(n * sizeof(float)));
-    float* hs = static_cast<float*>(std::malloc(n * sizeof(float)));
-    if (!hc || !hs) {
-      std::free(hc);
-      std::free(hs);
-      free_ctx(c);
-      return PL_ENOMEM;
-    }
-    host_rope_tables(hc, hs, max_seq_len, head_dim, rope_freq_base);
-    cudaMemcpy(c->d_cos, hc, n * sizeof(float), cudaMemcpyHostToDevice);
-    cudaMemcpy(c->d_sin, hs, n * sizeof(float), cudaMemcpyHostToDevice);
-    std::free(hc);
-    std::free(hs);
-  }
-  const int n_slabs = n_seqs * n_layers;
-  if ((rc = make_map(c->encode, &c->tm_k_dec, c->d_k, head_dim, max_seq_len, n_kv_heads, n_slabs,
-                     c->tp, n_kv_heads)) ||
-      (rc = make_map(c->encode, &c->tm_v_dec, c->d_v, head_dim, max_seq_len, n_kv_heads, n_slabs,
-                     c->tp, n_kv_heads)) ||
-      (rc = make_map(c->encode, &c->tm_k_pf, c->d_k, head_dim, max_seq_len, n_kv_heads, n_slabs,
-                     pl::pf_block_n(head_dim), 1)) ||
-      (rc = make_map(c->encode, &c->tm_v_pf, c->d_v, head_dim, max_seq_len, n_kv_heads, n_slabs,
-                     pl::pf_block_n(head_dim), 1))) {
-    free_ctx(c);
-    return rc;
-  }
-  // decode grid: as many CTAs as can be resident at once (registers, shared
-  // memory), so the balanced partition runs in a single wave
-  g = c;
-  {
-    int per_sm = 0;
-    const int smem = decode_smem_bytes(c->tp, c->nstage, head_dim);
-    const int threads = (n_kv_heads + 1) * 32;
-    const cudaError_t e =
-        with_decode_config(c->tp, c->nstage, head_dim, DecodeOccupancy{&per_sm, threads, smem});
-    g = nullptr;
-    if (e != cudaSuccess || per_sm < 1) {
-      free_ctx(c);
-      return PL_ECUDA;
-    }
-    c->decode_slots = c->num_sms * per_sm;
-  }
-  c->lw.resize(static_cast<size_t>(n_layers));
-  if (cudaStreamSynchronize(c->stream) != cudaSuccess) {
-    free_ctx(c);
-    return PL_ECUDA;
-  }
-  g = c;
-  return PL_OK;
+  return multi_init(n_layers, n_heads, n_kv_heads, head_dim, max_seq_len, rope_freq_base,
+                    rope_type, n_seqs, n_devices, devices, split);
 }
 
 void pl_attn_shutdown(void) {
@@ -820,14 +900,20 @@ void pl_attn_shutdown(void) {
   g_copy = nullptr;
   if (g && g->device >= 0) cudaSetDevice(g->device);
   xfer_free();
-  free_ctx(g);
+  if (g_multi) {
+    multi_free();  // every device's context, g included
+  } else {
+    free_ctx(g);
+  }
   g = nullptr;
 }
 
 int pl_attn_set_rope(const float* cos_tab, const float* sin_tab, int n_rows, int half_dim) {
   if (!g) return PL_ESTATE;
   if (!cos_tab || !sin_tab || half_dim != g->head_dim / 2 || n_rows <= 0) return PL_EARG;
-  const int rows = n_rows < g->max_seq ? n_rows : g->max_seq;
+  if (g_multi) return multi_set_rope(cos_tab, sin_tab, n_rows, half_dim);
+  if (cudaSetDevice(g->device) != cudaSuccess) return PL_ECUDA;
+  const int rows = n_rows < g->rope_rows ? n_rows : g->rope_rows;
   const size_t bytes = static_cast<size_t>(rows) * half_dim * sizeof(float);
   PL_CUDA(cudaMemcpyAsync(g->d_cos, cos_tab, bytes, cudaMemcpyHostToDevice, g->stream));
   PL_CUDA(cudaMemcpyAsync(g->d_sin, sin_tab, bytes, cudaMemcpyHostToDevice, g->stream));
@@ -859,6 +945,7 @@ static int read_back(const float* d_out, float* out, size_t qb, uint8_t* h) {
 int pl_attn_decode_batch(int layer, int n, const int* seqs, const int* pos, const float* q,
                          const float* k, const float* v, float* out) {
   if (!g) return PL_ESTATE;
+  if (g_multi) return multi_decode_batch(layer, n, seqs, pos, q, k, v, out);
   if (n <= 0 || n > g->n_seqs || !seqs || !pos || !q || !k || !v || !out) return PL_EARG;
   if (layer < 0 || layer >= g->n_layers) return PL_EARG;
   int max_pos = 0;
@@ -920,7 +1007,8 @@ int pl_attn_host_register(void* ptr, size_t bytes) {
   for (const HostRange& r : g_pinned)
     if (a < r.hi && a + bytes > r.lo) return PL_EARG;  // overlaps a registered range
   if (cudaSetDevice(g->device) != cudaSuccess) return PL_ECUDA;
-  const cudaError_t e = cudaHostRegister(ptr, bytes, cudaHostRegisterDefault);
+  // portable: pinned for every device of a multi-device context
+  const cudaError_t e = cudaHostRegister(ptr, bytes, cudaHostRegisterPortable);
   if (e != cudaSuccess) {
     cudaGetLastError();  // the call stays usable through the staging area
     std::fprintf(stderr, "pl_attn_host_register: %s\n", cudaGetErrorString(e));
@@ -951,6 +1039,7 @@ int pl_attn_decode_batch_dev(int layer, int n, const int* d_seqs, const int* d_p
                              const float* d_q, const float* d_k, const float* d_v, float* d_out,
                              void* stream) {
   if (!g) return PL_ESTATE;
+  if (g_multi) return PL_EUNSUPPORTED;
   if (n <= 0 || n > g->n_seqs || layer < 0 || layer >= g->n_layers || max_pos < 0 ||
       max_pos >= g->max_seq)
     return PL_EARG;
@@ -964,10 +1053,11 @@ int pl_attn_decode_partial_dev(int seq, int layer, int pos, int row0, int n_rows
                                float* d_part, void* stream) {
   int rc = check_seq_layer(seq, layer);
   if (rc) return rc;
+  if (g_multi) return PL_EUNSUPPORTED;
   if (pos < 0 || row0 < 0 || n_rows < 0 || n_rows > g->max_seq || !d_q || !d_part) return PL_EARG;
   if (append && (pos - row0 < 0 || pos - row0 >= n_rows || !d_k || !d_v)) return PL_EARG;
   // the RoPE table must cover the global position
-  if (pos >= g->max_seq) return PL_EARG;
+  if (pos >= g->rope_rows) return PL_EARG;
   cudaStream_t st = pick_stream(stream);
   if (n_rows == 0) {
     // an empty shard contributes nothing: m = -inf, l = 0, o = 0
@@ -978,21 +1068,12 @@ int pl_attn_decode_partial_dev(int seq, int layer, int pos, int row0, int n_rows
                             cudaMemcpyHostToDevice, st));
     return PL_OK;
   }
-  // seq and pos travel as kernel arguments (no copy, nothing that could
-  // make the host wait for the stream)
-  const int grid = decode_grid(1, n_rows);
-  int rc2 = ensure_part(static_cast<size_t>(grid + 1) * g->part_floats);
-  if (rc2) return rc2;
-  pl::DecodeArgs a = decode_args(layer, 1, nullptr, nullptr, d_q, d_k ? d_k : d_q,
-                                 d_v ? d_v : d_q, nullptr, 1, row0, n_rows, append ? 1 : 0,
-                                 d_part, g->d_part, g->d_seg_info);
-  a.seq1 = seq;
-  a.pos1 = pos;
-  return launch_decode_kernel(a, grid, st, true);
+  return partial_launch(seq, layer, pos, row0, n_rows, append, d_q, d_k, d_v, d_part, st);
 }
 
 int pl_attn_combine_dev(int n_part, const float* d_parts, float* d_out, void* stream) {
   if (!g) return PL_ESTATE;
+  if (g_multi) return PL_EUNSUPPORTED;
   if (n_part <= 0 || !d_parts || !d_out) return PL_EARG;
   if (n_part > pl::kMaxCombineParts) return PL_EARG;
   cudaStream_t st = pick_stream(stream);
@@ -1011,6 +1092,7 @@ int pl_attn_xfer_handle_bytes(void) { return static_cast<int>(sizeof(cudaIpcMemH
 
 int pl_attn_xfer_setup(int world, int rank, void* handle_out) {
   if (!g) return PL_ESTATE;
+  if (g_multi) return PL_EUNSUPPORTED;
   if (g_xfer) return PL_ESTATE;
   if (world < 1 || world > pl::kXferMaxRanks || rank < 0 || rank >= world || !handle_out)
     return PL_EARG;
@@ -1037,6 +1119,7 @@ int pl_attn_xfer_setup(int world, int rank, void* handle_out) {
 
 int pl_attn_xfer_connect(const void* handles) {
   if (!g || !g_xfer) return PL_ESTATE;
+  if (g_multi) return PL_EUNSUPPORTED;
   if (!handles) return PL_EARG;
   if (cudaSetDevice(g->device) != cudaSuccess) return PL_ECUDA;
   const auto* h = static_cast<const cudaIpcMemHandle_t*>(handles);
@@ -1053,6 +1136,7 @@ int pl_attn_xfer_connect(const void* handles) {
 
 int pl_attn_combine_p2p_dev(const float* d_part, float* d_out, void* stream) {
   if (!g || !g_xfer) return PL_ESTATE;
+  if (g_multi) return PL_EUNSUPPORTED;
   if (!d_part || !d_out) return PL_EARG;
   for (int r = 0; r < g_xfer->world; ++r)
     if (!g_xfer->peers.base[r]) return PL_ESTATE;  // not connected yet
@@ -1081,7 +1165,8 @@ int pl_attn_combine_p2p_dev(const float* d_part, float* d_out, void* stream) {
 
 int pl_attn_rope(int pos0, int n_tok, float* q, float* k) {
   if (!g) return PL_ESTATE;
-  if (n_tok <= 0 || pos0 < 0 || pos0 + n_tok > g->max_seq || (!q && !k)) return PL_EARG;
+  if (n_tok <= 0 || pos0 < 0 || pos0 + n_tok > g->rope_rows || (!q && !k)) return PL_EARG;
+  if (cudaSetDevice(g->device) != cudaSuccess) return PL_ECUDA;
   const size_t qb = q ? static_cast<size_t>(n_tok) * g->q_dim * sizeof(float) : 0;
   const size_t kb = k ? static_cast<size_t>(n_tok) * g->kv_dim * sizeof(float) : 0;
   int rc = ensure_stage(qb + kb + 256);
@@ -1107,6 +1192,7 @@ int pl_attn_rope(int pos0, int n_tok, float* q, float* k) {
 }
 
 int pl_kv_download(int seq, int layer, int pos0, int n_pos, uint16_t* k, uint16_t* v) {
+  if (g_multi) return multi_kv_copy(seq, layer, pos0, n_pos, k, v, true);
   int rc = check_seq_layer(seq, layer);
   if (rc) return rc;
   if (pos0 < 0 || n_pos < 0 || pos0 + n_pos > g->max_seq) return PL_EARG;
@@ -1122,6 +1208,9 @@ int pl_kv_download(int seq, int layer, int pos0, int n_pos, uint16_t* k, uint16_
 }
 
 int pl_kv_upload(int seq, int layer, int pos0, int n_pos, const uint16_t* k, const uint16_t* v) {
+  if (g_multi)
+    return multi_kv_copy(seq, layer, pos0, n_pos, const_cast<uint16_t*>(k),
+                         const_cast<uint16_t*>(v), false);
   int rc = check_seq_layer(seq, layer);
   if (rc) return rc;
   if (pos0 < 0 || n_pos < 0 || pos0 + n_pos > g->max_seq) return PL_EARG;
@@ -1139,6 +1228,7 @@ int pl_kv_upload(int seq, int layer, int pos0, int n_pos, const uint16_t* k, con
 int pl_attn_kv_ptr(int seq, int layer, uint16_t** d_k, uint16_t** d_v) {
   int rc = check_seq_layer(seq, layer);
   if (rc) return rc;
+  if (g_multi) return PL_EUNSUPPORTED;
   if (d_k) *d_k = slab_k(seq, layer);
   if (d_v) *d_v = slab_v(seq, layer);
   return PL_OK;
@@ -1147,9 +1237,13 @@ int pl_attn_kv_ptr(int seq, int layer, uint16_t** d_k, uint16_t** d_v) {
 // ---------------------------------------------------------------- prefill
 static bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
-static int launch_prefill(int seq, int layer, int start_pos, int n_tok, const float* d_q,
-                          const float* d_k, const float* d_v, float* d_out, int out_stride,
-                          cudaStream_t st) {
+// Prologue + tensor-core attention over the rows of one cache slab: kc_slab /
+// vc_slab are its row 0 (the prologue appends at row start_pos), tmk / tmv
+// and `slab` address it for the attention kernel's TMA loads.
+static int launch_prefill_rows(uint16_t* kc_slab, uint16_t* vc_slab, const CUtensorMap& tmk,
+                               const CUtensorMap& tmv, int slab, int start_pos, int n_tok,
+                               const float* d_q, const float* d_k, const float* d_v,
+                               float* d_out, int out_stride, cudaStream_t st) {
   int rc = ensure_q16(n_tok);
   if (rc) return rc;
   const size_t off = static_cast<size_t>(start_pos) * g->kv_dim;
@@ -1157,14 +1251,12 @@ static int launch_prefill(int seq, int layer, int start_pos, int n_tok, const fl
       pl::prologue_grid(n_tok, g->n_heads, g->n_kv_heads, g->head_dim, true, g->num_sms);
   if (g->head_dim == 128)
     pl::prefill_prologue_kernel<128><<<pgrid, pl::kPrologueThreads, 0, st>>>(
-        d_q, d_k, d_v, g->d_q16, static_cast<long>(g->q16_cap), slab_k(seq, layer) + off,
-        slab_v(seq, layer) + off, n_tok, g->n_heads, g->n_kv_heads, start_pos, g->d_cos,
-        g->d_sin, g->rope_type);
+        d_q, d_k, d_v, g->d_q16, static_cast<long>(g->q16_cap), kc_slab + off, vc_slab + off,
+        n_tok, g->n_heads, g->n_kv_heads, start_pos, g->d_cos, g->d_sin, g->rope_type);
   else
     pl::prefill_prologue_kernel<64><<<pgrid, pl::kPrologueThreads, 0, st>>>(
-        d_q, d_k, d_v, g->d_q16, static_cast<long>(g->q16_cap), slab_k(seq, layer) + off,
-        slab_v(seq, layer) + off, n_tok, g->n_heads, g->n_kv_heads, start_pos, g->d_cos,
-        g->d_sin, g->rope_type);
+        d_q, d_k, d_v, g->d_q16, static_cast<long>(g->q16_cap), kc_slab + off, vc_slab + off,
+        n_tok, g->n_heads, g->n_kv_heads, start_pos, g->d_cos, g->d_sin, g->rope_type);
   PL_CUDA(cudaGetLastError());
   count_launch();
   pl::PrefillArgs a;
@@ -1175,22 +1267,31 @@ static int launch_prefill(int seq, int layer, int start_pos, int n_tok, const fl
   a.start_pos = start_pos;
   a.n_heads = g->n_heads;
   a.kv_mul = g->kv_mul;
-  a.slab = seq * g->n_layers + layer;
+  a.slab = slab;
   a.score_scale = pl::kLog2e / sqrtf(static_cast<float>(g->head_dim));
   a.work = g->d_work;
   a.err = g->d_err;
   prof_begin(st);
   // overlap with the prologue except when events separate the two for timing
-  if (pl::launch_prefill_attention(g->head_dim, a, g->tm_q16, g->tm_q16lo, g->tm_k_pf, g->tm_v_pf,
-                                   g->num_sms, st, !g->profiling) != 0)
+  if (pl::launch_prefill_attention(g->head_dim, a, g->tm_q16, g->tm_q16lo, tmk, tmv, g->num_sms,
+                                   st, !g->profiling) != 0)
     return PL_ECUDA;
   prof_end(st);
   count_launch();
   return PL_OK;
 }
 
+static int launch_prefill(int seq, int layer, int start_pos, int n_tok, const float* d_q,
+                          const float* d_k, const float* d_v, float* d_out, int out_stride,
+                          cudaStream_t st) {
+  return launch_prefill_rows(slab_k(seq, layer), slab_v(seq, layer), g->tm_k_pf, g->tm_v_pf,
+                             seq * g->n_layers + layer, start_pos, n_tok, d_q, d_k, d_v, d_out,
+                             out_stride, st);
+}
+
 int pl_attn_prefill(int seq, int layer, int start_pos, int n_tok, const float* q, const float* k,
                     const float* v, float* out, int out_stride) {
+  if (g_multi) return multi_prefill(seq, layer, start_pos, n_tok, q, k, v, out, out_stride);
   int rc = check_seq_layer(seq, layer);
   if (rc) return rc;
   if (n_tok <= 0 || start_pos < 0 || start_pos + n_tok > g->max_seq || !q || !k || !v || !out ||
@@ -1241,6 +1342,7 @@ int pl_attn_prefill_dev(int seq, int layer, int start_pos, int n_tok, const floa
                         void* stream) {
   int rc = check_seq_layer(seq, layer);
   if (rc) return rc;
+  if (g_multi) return PL_EUNSUPPORTED;
   if (n_tok <= 0 || start_pos < 0 || start_pos + n_tok > g->max_seq || !d_q || !d_k || !d_v ||
       !d_out || out_stride < g->q_dim)
     return PL_EARG;
@@ -1261,6 +1363,7 @@ int pl_attn_set_wait_limit(double seconds) {
   if (!g) return PL_ESTATE;
   if (!(seconds >= 1e-4 && seconds <= 60.0)) return PL_EARG;
   const uint64_t ns = static_cast<uint64_t>(seconds * 1e9);
+  if (g_multi) return multi_set_wait_limit(ns);
   if (cudaSetDevice(g->device) != cudaSuccess) return PL_ECUDA;
   PL_CUDA(cudaMemcpyToSymbol(pl::g_wait_limit_ns, &ns, sizeof(ns)));
   return PL_OK;
@@ -1268,6 +1371,7 @@ int pl_attn_set_wait_limit(double seconds) {
 
 int pl_attn_status(void* stream) {
   if (!g) return PL_ESTATE;
+  if (g_multi) return multi_status();
   if (cudaSetDevice(g->device) != cudaSuccess) return PL_ECUDA;
   PL_CUDA(cudaStreamSynchronize(pick_stream(stream)));
   uint32_t w = 0;
@@ -1278,6 +1382,10 @@ int pl_attn_status(void* stream) {
 
 int pl_attn_profile(int enable) {
   if (!g) return PL_ESTATE;
+  if (g_multi) {
+    multi_profile(enable);
+    return PL_OK;
+  }
   g->profiling = enable ? 1 : 0;
   g->ev_used = 0;
   g->n_attn = 0;
@@ -1287,6 +1395,7 @@ int pl_attn_profile(int enable) {
 
 int pl_attn_profile_read(double* attn_ms, long* attn_launches, long* all_launches) {
   if (!g) return PL_ESTATE;
+  if (g_multi) return multi_profile_read(attn_ms, attn_launches, all_launches);
   double ms = 0.0;
   for (size_t i = 0; i + 1 < g->ev_used; i += 2) {
     PL_CUDA(cudaEventSynchronize(g->ev_pool[i + 1]));
@@ -1359,6 +1468,7 @@ extern "C" int pl_attn_decode_batch_dev_noalloc(int layer, int n, const int* d_s
                                                 const float* d_k, const float* d_v,
                                                 float* d_out, void* stream) {
   if (!g) return PL_ESTATE;
+  if (g_multi) return PL_EUNSUPPORTED;
   if (n <= 0 || n > g->n_seqs || layer < 0 || layer >= g->n_layers || max_pos < 0 ||
       max_pos >= g->max_seq)
     return PL_EARG;
@@ -1633,6 +1743,7 @@ int block_prefill(int seq, int layer, int start_pos, int n_tok, float* d_x, cuda
 
 int check_layer_set(int layer) {
   if (!g) return PL_ESTATE;
+  if (g_multi) return PL_EUNSUPPORTED;
   if (layer < 0 || layer >= g->n_layers) return PL_EARG;
   return g->lw[static_cast<size_t>(layer)].mem ? PL_OK : PL_ESTATE;
 }
@@ -1647,6 +1758,7 @@ int pl_attn_set_layer(int layer, int dim, const float* attn_norm, float rms_eps,
                       const float* bv, const float* bo, const float* q_norm,
                       const float* k_norm) {
   if (!g) return PL_ESTATE;
+  if (g_multi) return PL_EUNSUPPORTED;
   if (layer < 0 || layer >= g->n_layers || dim <= 0 || !wq || !wk || !wv || !wo ||
       (q_norm == nullptr) != (k_norm == nullptr) || !(rms_eps >= 0.f))
     return PL_EARG;
@@ -1830,3 +1942,553 @@ int pl_attn_proj(int layer, int which, int n, const float* x, float* y) {
 }
 
 }  // extern "C"
+
+// =====================================================================
+// One context over several devices of this process (pl_attn_init_devices).
+//
+// Every device has an ordinary context (Ctx); g is the first one.  Host
+// calls fan out from the one host thread that drives the module: inputs
+// are staged per device, every device's kernels are queued on its own
+// stream before any host wait, and the calls return once every stream is
+// done.  Two layouts:
+//   PL_SPLIT_SEQS  device d holds global slots [slot0[d], slot0[d+1]) as its
+//                  local slots 0..; a batch is split by slot owner.
+//   PL_SPLIT_KV    every device holds every slot, but only the rows of the
+//                  position blocks b (kKvBlockRows each) with b % D == d,
+//                  packed in position order: global row r is local row
+//                  (r / B / D) * B + r % B of device (r / B) % D.  A
+//                  device's rows at or below a position are therefore its
+//                  local rows [0, n), so each device attends them with the
+//                  KV-shard partial of the decode kernel (mode 1), and
+//                  devices[0] merges the partials, read over NVLink after
+//                  waiting on each device's event.  A prefill gathers the
+//                  earlier rows of the (slot, layer) onto devices[0], runs
+//                  there, and returns each new row to its owner.
+// =====================================================================
+namespace {
+
+constexpr int kKvBlockRows = 512;
+
+struct Multi {
+  int split = PL_SPLIT_SEQS;
+  int n_seqs = 0, max_seq = 0;        // global slots and positions
+  std::vector<Ctx*> devs;
+  std::vector<int> slot0;             // PL_SPLIT_SEQS: first global slot per device, + n_seqs
+  std::vector<cudaEvent_t> ev;        // per device: its partial is written
+  std::vector<float*> d_mpart;        // PL_SPLIT_KV, per device: partial blocks of one call
+  std::vector<size_t> mpart_cap;      // floats
+  uint16_t* gk = nullptr;             // PL_SPLIT_KV prefill: one (slot, layer) at full length
+  uint16_t* gv = nullptr;             // on devs[0], [max_seq][kv_dim]
+  CUtensorMap tm_gk, tm_gv;
+};
+
+// Makes devs[d] the module context (and its device current) for the helpers
+// above, which all work on g; restores the first device's context.
+struct UseCtx {
+  explicit UseCtx(Ctx* c) {
+    g = c;
+    cudaSetDevice(c->device);
+  }
+  ~UseCtx() {
+    g = g_multi->devs[0];
+    cudaSetDevice(g->device);
+  }
+};
+
+int n_dev() { return static_cast<int>(g_multi->devs.size()); }
+
+// ---- PL_SPLIT_KV row map
+int kv_owner(int r) { return (r / kKvBlockRows) % n_dev(); }
+int kv_local(int r) { return (r / kKvBlockRows / n_dev()) * kKvBlockRows + r % kKvBlockRows; }
+// rows of [0, P) that device d holds
+int kv_rows_below(int d, int P) {
+  const int D = n_dev(), fb = P / kKvBlockRows, rem = P % kKvBlockRows;
+  int n = (fb / D + (d < fb % D ? 1 : 0)) * kKvBlockRows;
+  if (rem && fb % D == d) n += rem;
+  return n;
+}
+// local cache rows of device d for positions [0, max_seq)
+int kv_cache_rows(int d, int D, int max_seq) {
+  const int nb = (max_seq + kKvBlockRows - 1) / kKvBlockRows;
+  const int blocks = nb > d ? (nb - 1 - d) / D + 1 : 0;
+  return (blocks > 0 ? blocks : 1) * kKvBlockRows;
+}
+
+int seq_owner(int seq) {
+  int d = 0;
+  while (seq >= g_multi->slot0[d + 1]) ++d;
+  return d;
+}
+
+void multi_free() {
+  Multi* m = g_multi;
+  if (!m) return;
+  for (size_t d = 0; d < m->devs.size(); ++d) {
+    cudaSetDevice(m->devs[d]->device);
+    cudaStreamSynchronize(m->devs[d]->stream);
+    if (d < m->ev.size() && m->ev[d]) cudaEventDestroy(m->ev[d]);
+    if (d < m->d_mpart.size()) cudaFree(m->d_mpart[d]);
+  }
+  if (!m->devs.empty()) {
+    cudaSetDevice(m->devs[0]->device);
+    cudaFree(m->gk);
+    cudaFree(m->gv);
+  }
+  for (Ctx* c : m->devs) free_ctx(c);
+  delete m;
+  g_multi = nullptr;
+}
+
+int multi_init(int n_layers, int n_heads, int n_kv_heads, int head_dim, int max_seq_len,
+               float rope_freq_base, int rope_type, int n_seqs, int n_devices,
+               const int* devices, int split) {
+  if (split == PL_SPLIT_SEQS && n_seqs < n_devices) return PL_EARG;
+  g_multi = new Multi;
+  Multi* m = g_multi;
+  m->split = split;
+  m->n_seqs = n_seqs;
+  m->max_seq = max_seq_len;
+  const int D = n_devices;
+  for (int d = 0; d <= D; ++d)
+    m->slot0.push_back(static_cast<int>(static_cast<long long>(n_seqs) * d / D));
+  int rc = PL_OK;
+  for (int d = 0; d < D && !rc; ++d) {
+    const int slots = split == PL_SPLIT_SEQS ? m->slot0[d + 1] - m->slot0[d] : n_seqs;
+    const int rows = split == PL_SPLIT_SEQS ? max_seq_len : kv_cache_rows(d, D, max_seq_len);
+    Ctx* c = nullptr;
+    rc = create_ctx(n_layers, n_heads, n_kv_heads, head_dim, max_seq_len, rope_freq_base,
+                    rope_type, slots, rows, devices[d], &c);
+    if (!rc) m->devs.push_back(c);
+  }
+  // the KV split reads other devices' partials and rows: peer access between
+  // every pair of distinct devices (a repeated id needs none)
+  for (int a = 0; a < D && !rc && split == PL_SPLIT_KV; ++a)
+    for (int b = 0; b < D && !rc; ++b) {
+      if (devices[a] == devices[b]) continue;
+      int ok = 0;
+      if (cudaDeviceCanAccessPeer(&ok, devices[a], devices[b]) != cudaSuccess || !ok) {
+        std::fprintf(stderr, "pl_attn_init_devices: device %d cannot access device %d\n",
+                     devices[a], devices[b]);
+        rc = PL_EDEVICE;
+        break;
+      }
+      cudaSetDevice(devices[a]);
+      const cudaError_t e = cudaDeviceEnablePeerAccess(devices[b], 0);
+      if (e == cudaErrorPeerAccessAlreadyEnabled)
+        cudaGetLastError();
+      else if (e != cudaSuccess)
+        rc = PL_ECUDA;
+    }
+  for (int d = 0; d < D && !rc; ++d) {
+    cudaSetDevice(devices[d]);
+    cudaEvent_t e = nullptr;
+    if (cudaEventCreateWithFlags(&e, cudaEventDisableTiming) != cudaSuccess) rc = PL_ECUDA;
+    m->ev.push_back(e);
+    m->d_mpart.push_back(nullptr);
+    m->mpart_cap.push_back(0);
+  }
+  if (!rc && split == PL_SPLIT_KV) {
+    Ctx* c0 = m->devs[0];
+    cudaSetDevice(c0->device);
+    const size_t bytes = static_cast<size_t>(max_seq_len) * c0->kv_dim * 2;
+    if (dev_alloc(&m->gk, bytes) != cudaSuccess || dev_alloc(&m->gv, bytes) != cudaSuccess)
+      rc = PL_ENOMEM;
+    if (!rc)
+      rc = make_map(c0->encode, &m->tm_gk, m->gk, head_dim, max_seq_len, n_kv_heads, 1,
+                    pl::pf_block_n(head_dim), 1);
+    if (!rc)
+      rc = make_map(c0->encode, &m->tm_gv, m->gv, head_dim, max_seq_len, n_kv_heads, 1,
+                    pl::pf_block_n(head_dim), 1);
+  }
+  if (rc) {
+    multi_free();
+    return rc;
+  }
+  g = m->devs[0];
+  cudaSetDevice(g->device);
+  return PL_OK;
+}
+
+// Wait for every device's stream; read and clear every error word.
+int multi_finish() {
+  int rc = PL_OK;
+  for (Ctx* c : g_multi->devs) {
+    UseCtx u(c);
+    if (cudaStreamSynchronize(c->stream) != cudaSuccess) {
+      rc = PL_ECUDA;
+      continue;
+    }
+    uint32_t w = 0;
+    if (cudaMemcpy(&w, c->d_err, sizeof(w), cudaMemcpyDeviceToHost) != cudaSuccess) {
+      rc = PL_ECUDA;
+      continue;
+    }
+    if (w) cudaMemset(c->d_err, 0, sizeof(uint32_t));
+    const int r = check_err_word(w);
+    if (r && !rc) rc = r;
+  }
+  return rc;
+}
+
+int multi_status() { return multi_finish(); }
+
+int multi_set_wait_limit(uint64_t ns) {
+  for (Ctx* c : g_multi->devs) {
+    UseCtx u(c);
+    PL_CUDA(cudaMemcpyToSymbol(pl::g_wait_limit_ns, &ns, sizeof(ns)));
+  }
+  return PL_OK;
+}
+
+int multi_set_rope(const float* cos_tab, const float* sin_tab, int n_rows, int half_dim) {
+  for (Ctx* c : g_multi->devs) {
+    UseCtx u(c);
+    const int rows = n_rows < c->rope_rows ? n_rows : c->rope_rows;
+    const size_t bytes = static_cast<size_t>(rows) * half_dim * sizeof(float);
+    PL_CUDA(cudaMemcpyAsync(c->d_cos, cos_tab, bytes, cudaMemcpyHostToDevice, c->stream));
+    PL_CUDA(cudaMemcpyAsync(c->d_sin, sin_tab, bytes, cudaMemcpyHostToDevice, c->stream));
+  }
+  return multi_finish();
+}
+
+void multi_profile(int enable) {
+  for (Ctx* c : g_multi->devs) {
+    c->profiling = enable ? 1 : 0;
+    c->ev_used = 0;
+    c->n_attn = 0;
+    c->n_all = 0;
+  }
+}
+
+int multi_profile_read(double* attn_ms, long* attn_launches, long* all_launches) {
+  double ms = 0.0;
+  long na = 0, nall = 0;
+  for (Ctx* c : g_multi->devs) {
+    UseCtx u(c);
+    for (size_t i = 0; i + 1 < c->ev_used; i += 2) {
+      PL_CUDA(cudaEventSynchronize(c->ev_pool[i + 1]));
+      float t = 0.f;
+      PL_CUDA(cudaEventElapsedTime(&t, c->ev_pool[i], c->ev_pool[i + 1]));
+      ms += t;
+    }
+    na += c->n_attn;
+    nall += c->n_all;
+    c->ev_used = 0;
+    c->n_attn = 0;
+    c->n_all = 0;
+  }
+  if (attn_ms) *attn_ms = ms;
+  if (attn_launches) *attn_launches = na;
+  if (all_launches) *all_launches = nall;
+  return PL_OK;
+}
+
+int check_batch(int layer, int n, const int* seqs, const int* pos, int* max_pos) {
+  if (n <= 0 || n > g_multi->n_seqs || !seqs || !pos) return PL_EARG;
+  if (layer < 0 || layer >= g->n_layers) return PL_EARG;
+  *max_pos = 0;
+  for (int i = 0; i < n; ++i) {
+    if (seqs[i] < 0 || seqs[i] >= g_multi->n_seqs || pos[i] < 0 || pos[i] >= g_multi->max_seq)
+      return PL_EARG;
+    for (int j = 0; j < i; ++j)
+      if (seqs[j] == seqs[i]) return PL_EARG;
+    if (pos[i] > *max_pos) *max_pos = pos[i];
+  }
+  return PL_OK;
+}
+
+// PL_SPLIT_SEQS decode: each device gets the batch entries of its slots,
+// gathered into its staging area; every device is queued before any wait.
+int multi_decode_seqs(int layer, int n, const int* seqs, const int* pos, const float* q,
+                      const float* k, const float* v, float* out) {
+  Multi* m = g_multi;
+  const int D = n_dev();
+  const size_t qf = g->q_dim, kf = g->kv_dim;
+  std::vector<std::vector<int>> idx(D);
+  for (int i = 0; i < n; ++i) idx[seq_owner(seqs[i])].push_back(i);
+  std::vector<size_t> out_off(D, 0);
+  int rc = PL_OK;
+  for (int d = 0; d < D && !rc; ++d) {
+    const int nd = static_cast<int>(idx[d].size());
+    if (!nd) continue;
+    Ctx* c = m->devs[d];
+    UseCtx u(c);
+    const size_t qb = nd * qf * sizeof(float), kb = nd * kf * sizeof(float);
+    const size_t ib = nd * sizeof(int), in_bytes = qb + 2 * kb + 2 * ib;
+    out_off[d] = (in_bytes + 255) & ~static_cast<size_t>(255);
+    rc = ensure_stage(out_off[d] + qb + 256);
+    if (rc) break;
+    uint8_t* h = c->h_stage;
+    std::vector<CopyPiece> pc;
+    int* hs = reinterpret_cast<int*>(h + qb + 2 * kb);
+    int* hp = hs + nd;
+    int max_pos = 0;
+    for (int j = 0; j < nd; ++j) {
+      const int i = idx[d][j];
+      pc.push_back({h + j * qf * 4, reinterpret_cast<const uint8_t*>(q + i * qf), qf * 4});
+      pc.push_back({h + qb + j * kf * 4, reinterpret_cast<const uint8_t*>(k + i * kf), kf * 4});
+      pc.push_back(
+          {h + qb + kb + j * kf * 4, reinterpret_cast<const uint8_t*>(v + i * kf), kf * 4});
+      hs[j] = seqs[i] - m->slot0[d];
+      hp[j] = pos[i];
+      if (pos[i] > max_pos) max_pos = pos[i];
+    }
+    host_copy(pc.data(), static_cast<int>(pc.size()));
+    uint8_t* dst = c->d_stage;
+    if (cudaMemcpyAsync(dst, h, in_bytes, cudaMemcpyHostToDevice, c->stream) != cudaSuccess) {
+      rc = PL_ECUDA;
+      break;
+    }
+    float* d_out = reinterpret_cast<float*>(dst + out_off[d]);
+    rc = launch_decode(layer, nd, reinterpret_cast<int*>(dst + qb + 2 * kb),
+                       reinterpret_cast<int*>(dst + qb + 2 * kb + ib), max_pos + 1,
+                       reinterpret_cast<float*>(dst), reinterpret_cast<float*>(dst + qb),
+                       reinterpret_cast<float*>(dst + qb + kb), d_out, 0, 0, 0, 1, nullptr,
+                       c->stream);
+    if (!rc && cudaMemcpyAsync(h + out_off[d], d_out, qb, cudaMemcpyDeviceToHost, c->stream) !=
+                   cudaSuccess)
+      rc = PL_ECUDA;
+  }
+  const int rc2 = multi_finish();
+  if (rc) return rc;
+  if (rc2) return rc2;
+  for (int d = 0; d < D; ++d) {
+    const int nd = static_cast<int>(idx[d].size());
+    if (!nd) continue;
+    std::vector<CopyPiece> pc;
+    const uint8_t* h = m->devs[d]->h_stage + out_off[d];
+    for (int j = 0; j < nd; ++j)
+      pc.push_back({reinterpret_cast<uint8_t*>(out + idx[d][j] * qf), h + j * qf * 4, qf * 4});
+    host_copy(pc.data(), static_cast<int>(pc.size()));
+  }
+  return PL_OK;
+}
+
+// PL_SPLIT_KV decode: per sequence, a partial on every device holding rows
+// at or below its position (the owner of the position appends), merged on
+// devices[0] after waiting on each device's event.
+int multi_decode_kv(int layer, int n, const int* seqs, const int* pos, const float* q,
+                    const float* k, const float* v, float* out) {
+  Multi* m = g_multi;
+  const int D = n_dev();
+  const size_t qf = g->q_dim, kf = g->kv_dim;
+  const size_t qb = n * qf * sizeof(float), kb = n * kf * sizeof(float);
+  const size_t in_bytes = qb + 2 * kb;
+  const size_t out_off = (in_bytes + 255) & ~static_cast<size_t>(255);
+  int rc = PL_OK;
+  // stage q, k, v of the whole batch on every device holding rows
+  for (int d = 0; d < D && !rc; ++d) {
+    Ctx* c = m->devs[d];
+    UseCtx u(c);
+    rc = ensure_stage(out_off + qb + 256);
+    const size_t need = static_cast<size_t>(n) * c->part_floats;
+    if (!rc && need > m->mpart_cap[d]) {
+      cudaFree(m->d_mpart[d]);
+      m->d_mpart[d] = nullptr;
+      m->mpart_cap[d] = 0;
+      if (dev_alloc(&m->d_mpart[d], need * sizeof(float)) != cudaSuccess)
+        rc = PL_ENOMEM;
+      else
+        m->mpart_cap[d] = need;
+    }
+    if (rc) break;
+    const CopyPiece in[3] = {{c->h_stage, reinterpret_cast<const uint8_t*>(q), qb},
+                             {c->h_stage + qb, reinterpret_cast<const uint8_t*>(k), kb},
+                             {c->h_stage + qb + kb, reinterpret_cast<const uint8_t*>(v), kb}};
+    host_copy(in, 3);
+    if (cudaMemcpyAsync(c->d_stage, c->h_stage, in_bytes, cudaMemcpyHostToDevice, c->stream) !=
+        cudaSuccess)
+      rc = PL_ECUDA;
+  }
+  Ctx* c0 = m->devs[0];
+  for (int i = 0; i < n && !rc; ++i) {
+    const int p = pos[i], owner = kv_owner(p);
+    pl::PeerParts parts = {};
+    int n_part = 0;
+    for (int d = 0; d < D && !rc; ++d) {
+      const int rows = kv_rows_below(d, p + 1);
+      if (!rows) continue;
+      Ctx* c = m->devs[d];
+      UseCtx u(c);
+      const float* dq = reinterpret_cast<const float*>(c->d_stage) + i * qf;
+      const float* dk = reinterpret_cast<const float*>(c->d_stage + qb) + i * kf;
+      const float* dv = reinterpret_cast<const float*>(c->d_stage + qb + kb) + i * kf;
+      float* part = m->d_mpart[d] + static_cast<size_t>(i) * c->part_floats;
+      const bool app = d == owner;
+      rc = partial_launch(seqs[i], layer, p, app ? p - kv_local(p) : 0, rows, app ? 1 : 0, dq,
+                          dk, dv, part, c->stream);
+      if (!rc && cudaEventRecord(m->ev[d], c->stream) != cudaSuccess) rc = PL_ECUDA;
+      if (!rc && d && cudaStreamWaitEvent(c0->stream, m->ev[d], 0) != cudaSuccess) rc = PL_ECUDA;
+      parts.p[n_part++] = part;
+    }
+    if (rc) break;
+    const int blocks = (g->n_heads * (g->head_dim / 4) + 255) / 256;
+    float* o = reinterpret_cast<float*>(c0->d_stage + out_off) + i * qf;
+    if (g->head_dim == 128)
+      pl::combine_peers_kernel<128><<<blocks, 256, 0, c0->stream>>>(parts, n_part, g->n_heads, o);
+    else
+      pl::combine_peers_kernel<64><<<blocks, 256, 0, c0->stream>>>(parts, n_part, g->n_heads, o);
+    if (cudaGetLastError() != cudaSuccess) rc = PL_ECUDA;
+    count_launch();
+  }
+  if (!rc && cudaMemcpyAsync(c0->h_stage + out_off, c0->d_stage + out_off, qb,
+                             cudaMemcpyDeviceToHost, c0->stream) != cudaSuccess)
+    rc = PL_ECUDA;
+  const int rc2 = multi_finish();
+  if (rc) return rc;
+  if (rc2) return rc2;
+  const CopyPiece o = {reinterpret_cast<uint8_t*>(out), c0->h_stage + out_off, qb};
+  host_copy(&o, 1);
+  return PL_OK;
+}
+
+int multi_decode_batch(int layer, int n, const int* seqs, const int* pos, const float* q,
+                       const float* k, const float* v, float* out) {
+  int max_pos = 0;
+  int rc = check_batch(layer, n, seqs, pos, &max_pos);
+  if (rc) return rc;
+  if (!q || !k || !v || !out) return PL_EARG;
+  if (g_multi->split == PL_SPLIT_SEQS) return multi_decode_seqs(layer, n, seqs, pos, q, k, v, out);
+  return multi_decode_kv(layer, n, seqs, pos, q, k, v, out);
+}
+
+// Copy rows [r0, r1) of (seq, layer) between device d's cache and host or
+// device memory at `other` (a pointer to row r0's K words; V likewise),
+// on stream st.  K and V words of a row are kv_dim apart in the caller's
+// arrays only through the two separate pointers.
+int kv_rows_copy(Ctx* c, int seq_local, int layer, int local_row, int rows, void* k_other,
+                 void* v_other, cudaMemcpyKind kind, cudaStream_t st) {
+  const size_t off = (static_cast<size_t>(seq_local) * c->n_layers + layer) * c->layer_elems +
+                     static_cast<size_t>(local_row) * c->kv_dim;
+  const size_t bytes = static_cast<size_t>(rows) * c->kv_dim * 2;
+  const bool to_dev = kind == cudaMemcpyHostToDevice;
+  if (k_other)
+    PL_CUDA(cudaMemcpyAsync(to_dev ? static_cast<void*>(c->d_k + off) : k_other,
+                            to_dev ? k_other : static_cast<void*>(c->d_k + off), bytes, kind, st));
+  if (v_other)
+    PL_CUDA(cudaMemcpyAsync(to_dev ? static_cast<void*>(c->d_v + off) : v_other,
+                            to_dev ? v_other : static_cast<void*>(c->d_v + off), bytes, kind, st));
+  return PL_OK;
+}
+
+int multi_kv_copy(int seq, int layer, int pos0, int n_pos, uint16_t* k, uint16_t* v,
+                  bool download) {
+  Multi* m = g_multi;
+  if (seq < 0 || seq >= m->n_seqs || layer < 0 || layer >= g->n_layers) return PL_EARG;
+  if (pos0 < 0 || n_pos < 0 || pos0 + n_pos > m->max_seq) return PL_EARG;
+  if (n_pos == 0) return PL_OK;
+  const cudaMemcpyKind kind = download ? cudaMemcpyDeviceToHost : cudaMemcpyHostToDevice;
+  const size_t kv = g->kv_dim;
+  int rc = PL_OK;
+  if (m->split == PL_SPLIT_SEQS) {
+    const int d = seq_owner(seq);
+    Ctx* c = m->devs[d];
+    UseCtx u(c);
+    rc = kv_rows_copy(c, seq - m->slot0[d], layer, pos0, n_pos, k, v, kind, c->stream);
+  } else {
+    for (int r = pos0; r < pos0 + n_pos && !rc;) {
+      const int end_blk = (r / kKvBlockRows + 1) * kKvBlockRows;
+      const int r1 = end_blk < pos0 + n_pos ? end_blk : pos0 + n_pos;
+      Ctx* c = m->devs[kv_owner(r)];
+      UseCtx u(c);
+      const size_t o = static_cast<size_t>(r - pos0) * kv;
+      rc = kv_rows_copy(c, seq, layer, kv_local(r), r1 - r, k ? k + o : nullptr,
+                        v ? v + o : nullptr, kind, c->stream);
+      r = r1;
+    }
+  }
+  const int rc2 = multi_finish();
+  return rc ? rc : rc2;
+}
+
+// Rows [r0, r1) of (seq, layer) between the owners' caches and the
+// gathering slab on devices[0] (to_slab: owners -> slab), on devices[0]'s
+// stream; peer copies where the owner is another GPU.
+int kv_slab_move(int seq, int layer, int r0, int r1, bool to_slab) {
+  Multi* m = g_multi;
+  Ctx* c0 = m->devs[0];
+  const size_t kv = c0->kv_dim;
+  for (int r = r0; r < r1;) {
+    const int end_blk = (r / kKvBlockRows + 1) * kKvBlockRows;
+    const int re = end_blk < r1 ? end_blk : r1;
+    Ctx* c = m->devs[kv_owner(r)];
+    const size_t off = (static_cast<size_t>(seq) * c->n_layers + layer) * c->layer_elems +
+                       static_cast<size_t>(kv_local(r)) * kv;
+    const size_t bytes = static_cast<size_t>(re - r) * kv * 2;
+    for (int x = 0; x < 2; ++x) {
+      uint16_t* own = (x ? c->d_v : c->d_k) + off;
+      uint16_t* slab = (x ? m->gv : m->gk) + static_cast<size_t>(r) * kv;
+      uint16_t* dst = to_slab ? slab : own;
+      uint16_t* src = to_slab ? own : slab;
+      const int ddev = to_slab ? c0->device : c->device, sdev = to_slab ? c->device : c0->device;
+      if (ddev == sdev)
+        PL_CUDA(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDeviceToDevice, c0->stream));
+      else
+        PL_CUDA(cudaMemcpyPeerAsync(dst, ddev, src, sdev, bytes, c0->stream));
+    }
+    r = re;
+  }
+  return PL_OK;
+}
+
+int multi_prefill(int seq, int layer, int start_pos, int n_tok, const float* q, const float* k,
+                  const float* v, float* out, int out_stride) {
+  Multi* m = g_multi;
+  if (seq < 0 || seq >= m->n_seqs || layer < 0 || layer >= g->n_layers) return PL_EARG;
+  if (n_tok <= 0 || start_pos < 0 || start_pos + n_tok > m->max_seq || !q || !k || !v || !out ||
+      out_stride < g->q_dim)
+    return PL_EARG;
+  if (m->split == PL_SPLIT_SEQS) {
+    // the slot's owner runs it as a single device would
+    const int d = seq_owner(seq);
+    Ctx* c = m->devs[d];
+    Multi* saved = g_multi;
+    int rc;
+    {
+      UseCtx u(c);
+      g_multi = nullptr;  // the single-device path, on this device's context
+      rc = pl_attn_prefill(seq - saved->slot0[d], layer, start_pos, n_tok, q, k, v, out,
+                           out_stride);
+      g_multi = saved;
+    }
+    return rc;
+  }
+  Ctx* c0 = m->devs[0];
+  const size_t qb = static_cast<size_t>(n_tok) * g->q_dim * sizeof(float);
+  const size_t kb = static_cast<size_t>(n_tok) * g->kv_dim * sizeof(float);
+  const size_t in_bytes = qb + 2 * kb;
+  const size_t out_off = (in_bytes + 255) & ~static_cast<size_t>(255);
+  int rc = ensure_stage(out_off + qb + 256);
+  if (rc) return rc;
+  cudaSetDevice(c0->device);
+  // the earlier rows of this (slot, layer) onto devices[0]
+  rc = kv_slab_move(seq, layer, 0, start_pos, true);
+  if (rc) return rc;
+  const CopyPiece in[3] = {{c0->h_stage, reinterpret_cast<const uint8_t*>(q), qb},
+                           {c0->h_stage + qb, reinterpret_cast<const uint8_t*>(k), kb},
+                           {c0->h_stage + qb + kb, reinterpret_cast<const uint8_t*>(v), kb}};
+  host_copy(in, 3);
+  PL_CUDA(cudaMemcpyAsync(c0->d_stage, c0->h_stage, in_bytes, cudaMemcpyHostToDevice,
+                          c0->stream));
+  float* d_out = reinterpret_cast<float*>(c0->d_stage + out_off);
+  rc = launch_prefill_rows(m->gk, m->gv, m->tm_gk, m->tm_gv, 0, start_pos, n_tok,
+                           reinterpret_cast<float*>(c0->d_stage),
+                           reinterpret_cast<float*>(c0->d_stage + qb),
+                           reinterpret_cast<float*>(c0->d_stage + qb + kb), d_out, g->q_dim,
+                           c0->stream);
+  // the new rows back to their owners
+  if (!rc) rc = kv_slab_move(seq, layer, start_pos, start_pos + n_tok, false);
+  if (!rc && cudaMemcpyAsync(c0->h_stage + out_off, d_out, qb, cudaMemcpyDeviceToHost,
+                             c0->stream) != cudaSuccess)
+    rc = PL_ECUDA;
+  const int rc2 = multi_finish();
+  if (rc) return rc;
+  if (rc2) return rc2;
+  for (int r = 0; r < n_tok; ++r)
+    std::memcpy(out + static_cast<size_t>(r) * out_stride,
+                c0->h_stage + out_off + static_cast<size_t>(r) * g->q_dim * sizeof(float),
+                g->q_dim * sizeof(float));
+  return PL_OK;
+}
+
+}  // namespace

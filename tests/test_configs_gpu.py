@@ -110,10 +110,12 @@ def test_config4_full_shape_vs_oracle():
             k = rng.standard_normal((n, kv), dtype=np.float32)
             v = rng.standard_normal((n, kv), dtype=np.float32)
             out = torch.full((n, H * hd), float("nan"), device="cuda")
-            at.decode_batch_dev(0, n, seqs.data_ptr(), _dev(pos).data_ptr(), ms - 1,
-                                _dev(q).data_ptr(), _dev(k).data_ptr(), _dev(v).data_ptr(),
-                                out.data_ptr(), st)
+            # the device copies must outlive the asynchronous call
+            dpos, dq, dk, dv = _dev(pos), _dev(q), _dev(k), _dev(v)
+            at.decode_batch_dev(0, n, seqs.data_ptr(), dpos.data_ptr(), ms - 1, dq.data_ptr(),
+                                dk.data_ptr(), dv.data_ptr(), out.data_ptr(), st)
             torch.cuda.synchronize()
+            del dpos, dq, dk, dv
             # the oracle in slot order: batch entry i is slot order[i]
             inv = np.argsort(order)
             want = O.attn_decode_seqs(c, kf, vf, ms * kv, pos, q[inv], k[inv], v[inv], *tables,
@@ -137,11 +139,13 @@ def _special_rows(golden, n_rows, width, finite_only):
     mant = np.arange(0, 1 << 10, 37, dtype=np.uint32)
     ties = ((exps[:, None] << 23) | (mant[None, :] << 13) | 0x1000).ravel()
     ties = np.concatenate([ties, ties | 0x80000000]).view(np.float32)
-    vals = np.concatenate([sp, ties])
     if finite_only:
-        vals = vals[np.isfinite(vals)]
-    idx = np.arange(n_rows * width) * 7 % vals.size  # every value, at shifting lanes
-    return vals[idx].reshape(n_rows, width).astype(np.float32)
+        sp = sp[np.isfinite(sp)]
+    # every special value first (row 0 onwards), then the tie patterns, each
+    # row starting at another offset so the values meet every lane position
+    vals = np.concatenate([sp, ties])
+    flat = np.concatenate([sp, vals[(np.arange(n_rows * width) * 7) % vals.size]])
+    return flat[:n_rows * width].reshape(n_rows, width).astype(np.float32)
 
 
 @pytest.mark.parametrize("hd", [64, 128])

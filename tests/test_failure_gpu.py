@@ -59,7 +59,7 @@ def test_p2p_merge_times_out_when_a_rank_never_arrives():
             h0 = at.xfer_setup(2, 0)
             assert parent.poll(120), "rank 1 did not start"
             h1 = parent.recv()
-            handles = h0 + h1
+            handles = [h0, h1]
             parent.send(handles)
             at.xfer_connect(handles)
             assert parent.poll(60) and parent.recv() == "connected"
