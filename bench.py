@@ -297,7 +297,7 @@ def run_batched_decode(args, rank, world, local, peaks):
     seqs_h = [np.arange(ks * SEQS_PER_GPU, (ks + 1) * SEQS_PER_GPU, dtype=np.int32)
               for ks in range(KV_SETS)]
     out_h = np.empty(SEQS_PER_GPU * Q_DIM, np.float32)  # reused, like model.c's s->xb
-    n_e2e = max(16, min(args.steps, 256))
+    n_e2e = max(64, min(args.steps, 256))
     for i in range(3):
         at.decode_batch(0, seqs_h[i % KV_SETS], np.full(SEQS_PER_GPU, CTX + NSTEP - 1, np.int32),
                         qh[0], kh[0], vh[0], out=out_h)

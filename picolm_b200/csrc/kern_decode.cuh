@@ -108,12 +108,6 @@ struct DecodeArgs {
   int mode, row0, n_rows, append;
   float score_scale;     // log2(e) / sqrt(head_dim)
   uint32_t* err;
-  // Host-buffer calls: q, k and v may still be arriving when the grid starts
-  // (their copy runs on another stream, followed by a stamp of
-  // arrive_epoch at `arrive`); consumers wait for the stamp before reading
-  // them.  nullptr: the inputs are in place before the launch.
-  const uint32_t* arrive;
-  uint32_t arrive_epoch;
   // Host-buffer calls: the last kernel of the call stores the device error
   // word here (pinned host memory mapped into the device), so the host reads
   // it without a copy.  nullptr: not wanted.
@@ -370,17 +364,6 @@ __device__ __forceinline__ void consume_segment(const DecodeArgs& a, int w, int 
   const float* cs = a.cos_tab + static_cast<size_t>(pos) * (HD / 2);
   const float* sn = a.sin_tab + static_cast<size_t>(pos) * (HD / 2);
   const bool appends = app_row >= t_lo * TP && app_row < t_hi * TP;
-
-  // inputs still arriving (host-buffer call): wait for their stamp
-  if (a.arrive) {
-    int arrived = 1;
-    if (lane == 0) arrived = wait_stamp_bounded(a.arrive, a.arrive_epoch) ? 1 : 0;
-    if (!__shfl_sync(0xffffffffu, arrived, 0)) {
-      if (lane == 0) atomicOr(a.err, ERR_TIMEOUT_FULL);
-      ok = false;
-      return;
-    }
-  }
 
   // q fragments: this thread needs dims 16kk+2c, +1 and 16kk+8+2c, +1
   uint32_t qa[HD / 16][4];

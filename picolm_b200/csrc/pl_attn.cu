@@ -90,13 +90,7 @@ struct Ctx {
   size_t q16_cap = 0;         // elements of each
   uint32_t* d_err = nullptr;  // device error word
   cudaStream_t stream = nullptr;
-  // host-buffer decode: inputs travel on copy_stream while the decode grid
-  // already streams the cache; a stamp at d_arrive says they have landed
-  cudaStream_t copy_stream = nullptr;
-  uint32_t* d_arrive = nullptr;   // last stamp written (device)
-  uint32_t* h_stamp = nullptr;    // pinned sources of the stamps, [2]
-  uint32_t arrive_epoch = 0;      // last stamp issued
-  uint32_t* h_err = nullptr;      // pinned, mapped: the error word as the call's last kernel saw it
+  uint32_t* h_err = nullptr;      // pinned, mapped: the error word as a host call's last kernel saw it
   uint32_t* h_err_dev = nullptr;  // its device address
   CUtensorMap tm_k_dec, tm_v_dec;  // decode: box {64, tp, Hk, 1}, head_dim/64 per tile
   CUtensorMap tm_k_pf, tm_v_pf;    // prefill: box {64, 128 rows, 1, 1}
@@ -479,8 +473,6 @@ pl::DecodeArgs decode_args(int layer, int n, const int* d_seqs, const int* d_pos
   a.append = append;
   a.score_scale = pl::kLog2e / sqrtf(static_cast<float>(g->head_dim));
   a.err = g->d_err;
-  a.arrive = nullptr;
-  a.arrive_epoch = 0;
   a.err_host = nullptr;
   return a;
 }
@@ -625,8 +617,7 @@ int launch_decode_kernel(const pl::DecodeArgs& a, int grid, cudaStream_t st, boo
 int launch_decode(int layer, int n, const int* d_seqs, const int* d_pos, int max_rows,
                   const float* d_q, const float* d_k, const float* d_v, float* d_out,
                   int mode, int row0, int n_rows, int append, float* part_out,
-                  cudaStream_t st, const uint32_t* arrive = nullptr, uint32_t arrive_epoch = 0,
-                  uint32_t* err_host = nullptr) {
+                  cudaStream_t st, uint32_t* err_host = nullptr) {
   for (int s0 = 0; s0 < n; s0 += pl::kMaxLaunchSeqs) {
     const int m = n - s0 < pl::kMaxLaunchSeqs ? n - s0 : pl::kMaxLaunchSeqs;
     const int grid = decode_grid(m, max_rows);
@@ -640,8 +631,6 @@ int launch_decode(int layer, int n, const int* d_seqs, const int* d_pos, int max
         part_out ? part_out + static_cast<size_t>(s0) * g->part_floats : nullptr,
         g->d_part, g->d_seg_info);
     pl::DecodeArgs b = a;
-    b.arrive = arrive;
-    b.arrive_epoch = arrive_epoch;
     b.err_host = err_host;
     rc = launch_decode_kernel(b, grid, st, true);
     if (rc) return rc;
@@ -710,10 +699,7 @@ void free_ctx(Ctx* c) {
   cudaFree(c->d_work);
   cudaFree(c->d_q16);
   cudaFree(c->d_err);
-  cudaFree(c->d_arrive);
-  cudaFreeHost(c->h_stamp);
   cudaFreeHost(c->h_err);
-  if (c->copy_stream) cudaStreamDestroy(c->copy_stream);
   cudaFree(c->d_blk);
   cudaFree(c->d_proj_part);
   for (LayerW& l : c->lw) cudaFree(l.mem);
@@ -793,19 +779,15 @@ int create_ctx(int n_layers, int n_heads, int n_kv_heads, int head_dim, int rope
       dev_alloc(&c->d_err, 256) != cudaSuccess ||
       dev_alloc(&c->d_seg_info, sizeof(int2) * pl::kMaxLaunchSeqs) != cudaSuccess ||
       dev_alloc(&c->d_work, 2 * sizeof(int)) != cudaSuccess ||
-      dev_alloc(&c->d_arrive, 256) != cudaSuccess ||
-      host_alloc(&c->h_stamp, 2 * sizeof(uint32_t)) != cudaSuccess ||
       host_alloc(&c->h_err, sizeof(uint32_t)) != cudaSuccess) {
     free_ctx(c);
     return PL_ENOMEM;
   }
-  if (cudaStreamCreateWithFlags(&c->copy_stream, cudaStreamNonBlocking) != cudaSuccess ||
-      cudaHostGetDevicePointer(reinterpret_cast<void**>(&c->h_err_dev), c->h_err, 0) !=
-          cudaSuccess) {
+  if (cudaHostGetDevicePointer(reinterpret_cast<void**>(&c->h_err_dev), c->h_err, 0) !=
+      cudaSuccess) {
     free_ctx(c);
     return PL_ECUDA;
   }
-  cudaMemsetAsync(c->d_arrive, 0, 256, c->stream);
   *c->h_err = 0;
   cudaMemsetAsync(c->d_k, 0, cache_elems * 2, c->stream);
   cudaMemsetAsync(c->d_v, 0, cache_elems * 2, c->stream);
@@ -998,54 +980,36 @@ int pl_attn_decode_batch(int layer, int n, const int* seqs, const int* pos, cons
   if (rc) return rc;
   uint8_t* h = g->h_stage;
   uint8_t* d = g->d_stage;
-  // Slots and positions go first, on the module stream: the decode grid's
-  // set-up reads them.  q, k and v follow on the copy stream with a stamp
-  // behind them, and the grid is launched without waiting for them: its
-  // producer streams the cache while they arrive, its consumers wait for
-  // the stamp (bounded) before reading them.
   std::memcpy(h + qb + 2 * kb, seqs, ib);
   std::memcpy(h + qb + 2 * kb + ib, pos, ib);
-  PL_CUDA(cudaMemcpyAsync(d + qb + 2 * kb, h + qb + 2 * kb, 2 * ib, cudaMemcpyHostToDevice,
-                          g->stream));
-  const bool direct_in = pinned(q, qb) && pinned(k, kb) && pinned(v, kb);
-  if (direct_in) {
-    // registered inputs go straight to the device
-    PL_CUDA(cudaMemcpyAsync(d, q, qb, cudaMemcpyHostToDevice, g->copy_stream));
-    PL_CUDA(cudaMemcpyAsync(d + qb, k, kb, cudaMemcpyHostToDevice, g->copy_stream));
-    PL_CUDA(cudaMemcpyAsync(d + qb + kb, v, kb, cudaMemcpyHostToDevice, g->copy_stream));
+  if (pinned(q, qb) && pinned(k, kb) && pinned(v, kb)) {
+    // registered inputs go straight to the device; seqs and pos are staged
+    PL_CUDA(cudaMemcpyAsync(d, q, qb, cudaMemcpyHostToDevice, g->stream));
+    PL_CUDA(cudaMemcpyAsync(d + qb, k, kb, cudaMemcpyHostToDevice, g->stream));
+    PL_CUDA(cudaMemcpyAsync(d + qb + kb, v, kb, cudaMemcpyHostToDevice, g->stream));
+    PL_CUDA(cudaMemcpyAsync(d + qb + 2 * kb, h + qb + 2 * kb, 2 * ib, cudaMemcpyHostToDevice,
+                            g->stream));
+  } else {
+    const CopyPiece in[3] = {{h, reinterpret_cast<const uint8_t*>(q), qb},
+                             {h + qb, reinterpret_cast<const uint8_t*>(k), kb},
+                             {h + qb + kb, reinterpret_cast<const uint8_t*>(v), kb}};
+    host_copy(in, 3);
+    PL_CUDA(cudaMemcpyAsync(d, h, in_bytes, cudaMemcpyHostToDevice, g->stream));
   }
-  uint32_t ep = ++g->arrive_epoch;
-  if (ep == 0) ep = ++g->arrive_epoch;  // 0 is the stamp's initial value
-  *g->h_err = 0;
+  // the call's last kernel stores the device error word in mapped pinned
+  // memory, so no copy brings it back
+  *reinterpret_cast<volatile uint32_t*>(g->h_err) = 0;
   float* d_out = reinterpret_cast<float*>(d + out_off);
   rc = launch_decode(layer, n, reinterpret_cast<int*>(d + qb + 2 * kb),
                      reinterpret_cast<int*>(d + qb + 2 * kb + ib), max_pos + 1,
                      reinterpret_cast<float*>(d), reinterpret_cast<float*>(d + qb),
                      reinterpret_cast<float*>(d + qb + kb), d_out, 0, 0, 0, 1, nullptr,
-                     g->stream, g->d_arrive, ep, g->h_err_dev);
-  if (!direct_in) {
-    // staged inputs: the host copies them while the grid already runs
-    const CopyPiece in[3] = {{h, reinterpret_cast<const uint8_t*>(q), qb},
-                             {h + qb, reinterpret_cast<const uint8_t*>(k), kb},
-                             {h + qb + kb, reinterpret_cast<const uint8_t*>(v), kb}};
-    host_copy(in, 3);
-    PL_CUDA(cudaMemcpyAsync(d, h, qb + 2 * kb, cudaMemcpyHostToDevice, g->copy_stream));
-  }
-  // the stamp, behind the inputs (its source: one of two pinned words, the
-  // other still possibly read by nothing -- calls are synchronous)
-  g->h_stamp[ep & 1u] = ep;
-  PL_CUDA(cudaMemcpyAsync(g->d_arrive, &g->h_stamp[ep & 1u], sizeof(uint32_t),
-                          cudaMemcpyHostToDevice, g->copy_stream));
-  if (rc) {
-    cudaStreamSynchronize(g->copy_stream);
-    return rc;
-  }
+                     g->stream, g->h_err_dev);
+  if (rc) return rc;
   const bool direct_out = pinned(out, qb);
   PL_CUDA(cudaMemcpyAsync(direct_out ? static_cast<void*>(out) : static_cast<void*>(h + out_off),
                           d_out, qb, cudaMemcpyDeviceToHost, g->stream));
   PL_CUDA(cudaStreamSynchronize(g->stream));
-  PL_CUDA(cudaStreamSynchronize(g->copy_stream));
-  // the call's last kernel stored the device error word in mapped memory
   const uint32_t w = *reinterpret_cast<volatile uint32_t*>(g->h_err);
   if (w) {
     cudaMemsetAsync(g->d_err, 0, sizeof(uint32_t), g->stream);

@@ -85,26 +85,6 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity
   }
 }
 
-// Wait, bounded, until the 32-bit stamp at p reaches `epoch` (wrap-safe
-// comparison).  The stamp is written by a host-to-device copy queued after
-// the data it announces on the same stream, so once it is seen the data
-// has landed in device memory.
-__device__ __forceinline__ uint32_t ld_acquire_gpu_u32(const uint32_t* p) {
-  uint32_t v;
-  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-  return v;
-}
-
-__device__ __forceinline__ bool wait_stamp_bounded(const uint32_t* p, uint32_t epoch) {
-  if (static_cast<int>(ld_acquire_gpu_u32(p) - epoch) >= 0) return true;
-  const uint64_t t0 = globaltimer(), lim = wait_limit_ns();
-  while (true) {
-    for (int i = 0; i < 32; ++i)
-      if (static_cast<int>(ld_acquire_gpu_u32(p) - epoch) >= 0) return true;
-    if (globaltimer() - t0 > lim) return false;
-  }
-}
-
 // ---------------------------------------------------------------- fences
 __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
