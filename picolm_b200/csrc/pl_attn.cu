@@ -21,6 +21,7 @@
 
 #include "../../include/pl_attn.h"
 #include "kern_decode.cuh"
+#include "kern_gemm.cuh"
 #include "kern_misc.cuh"
 #include "kern_prefill.cuh"
 #include "kern_proj.cuh"
@@ -59,6 +60,12 @@ struct LayerW {
   const float* k_norm = nullptr;
   float eps = 0.f;
   int dim = 0;
+  // The same weights dequantised for the tensor-core GEMM of many input rows
+  // (kern_gemm.cuh): FP16 high part and 2^11-scaled residual, Q/K/V rows
+  // concatenated [q_dim + 2 kv_dim][dim], O [dim][q_dim]; one allocation.
+  uint8_t* gmem = nullptr;
+  bool gemm = false;
+  CUtensorMap tm_qkv_h, tm_qkv_l, tm_o_h, tm_o_l;
 };
 
 struct Ctx {
@@ -108,6 +115,10 @@ struct Ctx {
   size_t blk_cap = 0;                // floats
   float* d_proj_part = nullptr;      // split-input partial sums of the projections
   size_t proj_part_cap = 0;          // floats
+  __half* d_xh = nullptr;            // GEMM activations: FP16 high parts, then
+  __half* d_xl = nullptr;            // the 2^11-scaled residuals
+  size_t act_cap = 0;                // elements of each
+  bool gemm_smem_set = false;
   bool proj_smem_set = false;
 };
 
@@ -702,7 +713,12 @@ void free_ctx(Ctx* c) {
   cudaFreeHost(c->h_err);
   cudaFree(c->d_blk);
   cudaFree(c->d_proj_part);
-  for (LayerW& l : c->lw) cudaFree(l.mem);
+  for (LayerW& l : c->lw) {
+    cudaFree(l.mem);
+    cudaFree(l.gmem);
+  }
+  cudaFree(c->d_xh);
+  cudaFree(c->d_xl);
   for (cudaEvent_t e : c->ev_pool) cudaEventDestroy(e);
   if (c->stream) cudaStreamDestroy(c->stream);
   delete c;
@@ -1707,6 +1723,124 @@ pl::ProjMat proj_mat(const LayerW& L, int which, float* out, int ld_out) {
   return m;
 }
 
+// ---- tensor-core GEMM of many input rows (kern_gemm.cuh) -------------------
+// A row-major FP16 matrix [rows][k] as a 2-D TMA map, box 64 x 128 under the
+// 128-byte swizzle.
+int make_map_2d(CUtensorMap* m, const __half* base, int k, int rows) {
+  const cuuint64_t dims[2] = {static_cast<cuuint64_t>(k), static_cast<cuuint64_t>(rows)};
+  const cuuint64_t strides[1] = {static_cast<cuuint64_t>(k) * 2};
+  const cuuint32_t box[2] = {static_cast<cuuint32_t>(pl::kGmBK), static_cast<cuuint32_t>(pl::kGmBM)};
+  const cuuint32_t estr[2] = {1, 1};
+  if (g->encode(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<__half*>(base), dims, strides,
+                box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+    return PL_ECUDA;
+  return PL_OK;
+}
+
+// The layer's weights as the GEMM's FP16 high parts and scaled residuals,
+// dequantised on the device from the uploaded rows.  Layers whose shapes do
+// not tile (q_dim, kv_dim, dim multiples of 128), or with a weight beyond
+// FP16's range, keep the CUDA-core / mma.sync paths for every row count.
+int gemm_prepare_layer(LayerW& L) {
+  L.gemm = false;
+  const int dim = L.dim, qd = g->q_dim, kvd = g->kv_dim;
+  if (dim % pl::kGmBN || qd % pl::kGmBN || kvd % pl::kGmBN) return PL_OK;
+  const size_t n_qkv = static_cast<size_t>(qd + 2 * kvd) * dim, n_o = static_cast<size_t>(dim) * qd;
+  const size_t bytes = 2 * (n_qkv + n_o) * sizeof(__half);
+  if (dev_alloc(&L.gmem, bytes) != cudaSuccess) return PL_ENOMEM;
+  __half* qkv_h = reinterpret_cast<__half*>(L.gmem);
+  __half* qkv_l = qkv_h + n_qkv;
+  __half* o_h = qkv_l + n_qkv;
+  __half* o_l = o_h + n_o;
+  int* d_over = nullptr;
+  if (dev_alloc(&d_over, sizeof(int)) != cudaSuccess) return PL_ENOMEM;
+  PL_CUDA(cudaMemsetAsync(d_over, 0, sizeof(int), g->stream));
+  const int rows[4] = {qd, kvd, kvd, dim};
+  const int row0[4] = {0, qd, qd + kvd, 0};
+  for (int i = 0; i < 4; ++i) {
+    const int n_in = i == 3 ? qd : dim;
+    const long total = static_cast<long>(rows[i]) * n_in;
+    const int blocks = static_cast<int>((total + 255) / 256 < 4096 ? (total + 255) / 256 : 4096);
+    pl::dequant_split_kernel<<<blocks, 256, 0, g->stream>>>(
+        L.w[i], L.row_bytes[i], L.type[i], rows[i], n_in, i == 3 ? o_h : qkv_h,
+        i == 3 ? o_l : qkv_l, row0[i], d_over);
+  }
+  PL_CUDA(cudaGetLastError());
+  int over = 0;
+  PL_CUDA(cudaMemcpyAsync(&over, d_over, sizeof(int), cudaMemcpyDeviceToHost, g->stream));
+  PL_CUDA(cudaStreamSynchronize(g->stream));
+  cudaFree(d_over);
+  if (over) {
+    cudaFree(L.gmem);
+    L.gmem = nullptr;
+    return PL_OK;
+  }
+  int rc = make_map_2d(&L.tm_qkv_h, qkv_h, dim, qd + 2 * kvd);
+  if (!rc) rc = make_map_2d(&L.tm_qkv_l, qkv_l, dim, qd + 2 * kvd);
+  if (!rc) rc = make_map_2d(&L.tm_o_h, o_h, qd, dim);
+  if (!rc) rc = make_map_2d(&L.tm_o_l, o_l, qd, dim);
+  if (rc) return rc;
+  L.gemm = true;
+  return PL_OK;
+}
+
+int ensure_act(size_t elems) {
+  if (elems <= g->act_cap) return PL_OK;
+  size_t cap = g->act_cap ? g->act_cap : (static_cast<size_t>(1) << 20);
+  while (cap < elems) cap *= 2;
+  if (g->d_xh) {
+    cudaStreamSynchronize(g->stream);
+    cudaFree(g->d_xh);
+    cudaFree(g->d_xl);
+  }
+  g->d_xh = g->d_xl = nullptr;
+  g->act_cap = 0;
+  if (dev_alloc(&g->d_xh, cap * sizeof(__half)) != cudaSuccess ||
+      dev_alloc(&g->d_xl, cap * sizeof(__half)) != cudaSuccess)
+    return PL_ENOMEM;
+  g->act_cap = cap;
+  return PL_OK;
+}
+
+// x [M][ldx] (RMSNorm with norm_w first, if set) -> y = x W^T over weight
+// rows [w_row0, w_row0 + N) of the layer's Q/K/V (qkv) or O matrices, routed
+// to the output segments; resid (may equal seg 0's out) added when set.
+int launch_gemm(const LayerW& L, bool qkv, const float* d_x, int ldx, int M, int K,
+                const float* norm_w, float eps, int w_row0, int N, const pl::GemmSeg* segs,
+                int n_seg, const float* resid, int ld_res, cudaStream_t st) {
+  int rc = ensure_act(static_cast<size_t>(M) * K);
+  if (rc) return rc;
+  pl::act_split_kernel<<<M, 256, 0, st>>>(d_x, ldx, K, norm_w, eps, g->d_xh, g->d_xl);
+  PL_CUDA(cudaGetLastError());
+  count_launch();
+  CUtensorMap tm_xh, tm_xl;
+  if ((rc = make_map_2d(&tm_xh, g->d_xh, K, M)) || (rc = make_map_2d(&tm_xl, g->d_xl, K, M)))
+    return rc;
+  if (!g->gemm_smem_set) {
+    PL_CUDA(cudaFuncSetAttribute(pl::gemm_hilo_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 pl::gm_smem_bytes()));
+    g->gemm_smem_set = true;
+  }
+  pl::GemmArgs a = {};
+  a.M = M;
+  a.N = N;
+  a.K = K;
+  a.w_row0 = w_row0;
+  for (int i = 0; i < n_seg; ++i) a.seg[i] = segs[i];
+  a.n_seg = n_seg;
+  a.resid = resid;
+  a.ld_res = ld_res;
+  a.err = g->d_err;
+  const dim3 grid(N / pl::kGmBN, (M + pl::kGmBM - 1) / pl::kGmBM);
+  pl::gemm_hilo_kernel<<<grid, pl::kGmThreads, pl::gm_smem_bytes(), st>>>(
+      a, tm_xh, tm_xl, qkv ? L.tm_qkv_h : L.tm_o_h, qkv ? L.tm_qkv_l : L.tm_o_l);
+  PL_CUDA(cudaGetLastError());
+  count_launch();
+  return PL_OK;
+}
+
 // rmsnorm + Q, K, V projections + biases of M rows of x [M][dim]
 int run_qkv(const LayerW& L, const float* d_x, int M, const BlkBufs& b, cudaStream_t st) {
   pl::ProjArgs a = {};
@@ -1721,7 +1855,17 @@ int run_qkv(const LayerW& L, const float* d_x, int M, const BlkBufs& b, cudaStre
   a.M = M;
   a.norm_w = L.attn_norm;
   a.eps = L.eps;
-  int rc = launch_proj(a, st, true);
+  int rc;
+  if (L.gemm && M >= pl::kGmMinRows) {
+    // many rows: the tensor-core GEMM over the concatenated Q, K, V rows
+    const pl::GemmSeg segs[3] = {{b.q, L.bias[0], 0, g->q_dim, g->q_dim},
+                                 {b.k, L.bias[1], g->q_dim, g->kv_dim, g->kv_dim},
+                                 {b.v, L.bias[2], g->q_dim + g->kv_dim, g->kv_dim, g->kv_dim}};
+    rc = launch_gemm(L, true, d_x, L.dim, M, L.dim, L.attn_norm, L.eps, 0,
+                     g->q_dim + 2 * g->kv_dim, segs, 3, nullptr, 0, st);
+  } else {
+    rc = launch_proj(a, st, true);
+  }
   if (rc || !L.q_norm) return rc;
   const dim3 grid(static_cast<unsigned>(M), (g->n_heads + g->n_kv_heads + 7) / 8);
   pl::qk_norm_kernel<<<grid, 256, 0, st>>>(b.q, b.k, g->n_heads, g->n_kv_heads, g->head_dim,
@@ -1743,6 +1887,11 @@ int run_out(const LayerW& L, const float* d_att, int M, float* d_x, cudaStream_t
   a.M = M;
   a.resid = d_x;
   a.ld_res = L.dim;
+  if (L.gemm && M >= pl::kGmMinRows) {
+    const pl::GemmSeg seg = {d_x, L.bias[3], 0, L.dim, L.dim};
+    return launch_gemm(L, false, d_att, g->q_dim, M, g->q_dim, nullptr, 0.f, 0, L.dim, &seg, 1,
+                       d_x, L.dim, st);
+  }
   return launch_proj(a, st, true);
 }
 
@@ -1832,6 +1981,7 @@ int pl_attn_set_layer(int layer, int dim, const float* attn_norm, float rms_eps,
   if (L.mem) {
     cudaStreamSynchronize(g->stream);
     cudaFree(L.mem);
+    cudaFree(L.gmem);
   }
   L = LayerW();
   L.mem = mem;
@@ -1847,7 +1997,7 @@ int pl_attn_set_layer(int layer, int dim, const float* attn_norm, float rms_eps,
   for (int i = 0; i < 4; ++i) L.bias[i] = fp(1 + i);
   L.q_norm = fp(5);
   L.k_norm = fp(6);
-  return PL_OK;
+  return gemm_prepare_layer(L);
 }
 
 int pl_attn_block_decode(int layer, int n, const int* seqs, const int* pos, float* x) {
@@ -1960,11 +2110,18 @@ int pl_attn_proj(int layer, int which, int n, const float* x, float* y) {
   a.ldx = in;
   a.n = in;
   a.M = n;
-  // the tensor-core path carries x as FP16 parts: only for inputs in range
+  // the tensor-core paths carry x as FP16 parts: only for inputs in range
   bool in_range = true;
   for (size_t i = 0; i < static_cast<size_t>(n) * in && in_range; ++i)
     in_range = std::fabs(x[i]) < 60000.f;
-  rc = launch_proj(a, g->stream, in_range);
+  if (in_range && L.gemm && n >= pl::kGmMinRows) {
+    const int w_row0 = which == 0 ? 0 : which == 1 ? g->q_dim : which == 2 ? g->q_dim + g->kv_dim : 0;
+    const pl::GemmSeg seg = {d_y, L.bias[which], 0, rows, rows};
+    rc = launch_gemm(L, which != 3, reinterpret_cast<const float*>(d), in, n, in, nullptr, 0.f,
+                     w_row0, rows, &seg, 1, nullptr, 0, g->stream);
+  } else {
+    rc = launch_proj(a, g->stream, in_range);
+  }
   if (rc) return rc;
   return read_back(d_y, y, yb, h + y_off);
 }

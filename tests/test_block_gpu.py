@@ -40,8 +40,10 @@ def _close_proj(got, want, what):
 @pytest.mark.parametrize("name", list(GGUF_TYPES))
 def test_projection_vs_oracle(name):
     # every projection of a layer whose four weights have this type, on 1, 5
-    # and 13 input rows (13 > the 8 rows a CTA stages: two row chunks), and
-    # 40 (the tensor-core path for Q4_K, Q8_0 and F16: 16-row tiles)
+    # and 13 input rows (13 > the 8 rows a CTA stages: two row chunks), 40
+    # (the mma.sync path for Q4_K, Q8_0 and F16: 16-row tiles) and 200 (the
+    # tcgen05 GEMM over the dequantised weights, from 128 rows; a ragged
+    # second 128-row tile)
     t = GGUF_TYPES[name]
     rng = np.random.default_rng(40 + t)
     H, Hk, hd, dim = 8, 2, 64, 768
@@ -51,7 +53,7 @@ def test_projection_vs_oracle(name):
     with pb.Attn(1, H, Hk, 64, head_dim=hd) as at:
         upload_layer(at, 0, L)
         for which, (rows, n) in enumerate(shapes):
-            for m in (1, 5, 13, 40):
+            for m in (1, 5, 13, 40, 200):
                 x = rng.standard_normal((m, n), dtype=np.float32)
                 got = at.proj(0, which, x, rows)
                 for i in range(m):
