@@ -166,7 +166,18 @@ int  pl_kv_upload(int seq, int layer, int pos0, int n_pos, const uint16_t *k,
                   const uint16_t *v);
 
 /* ---- Device-pointer entry points (asynchronous on `stream`, a
- *      cudaStream_t passed as void*; NULL = the CUDA default stream) ---- */
+ *      cudaStream_t passed as void*; NULL = the CUDA default stream) ----
+ *
+ * One stream at a time.  These calls use scratch that belongs to the
+ * context (the split-KV partials and segment table, the error word, the
+ * prefill's work counters and FP16 q staging), so calls that could overlap
+ * on the GPU -- on two streams with no ordering between them -- race on it.
+ * Issue them on one stream, or order the streams with events.  The current
+ * device must be the context's.  Any of them may grow that scratch with a
+ * cudaMalloc on first use (the device-wide synchronisation that implies
+ * included); pl_attn_decode_batch_dev_noalloc never does.  A device-side
+ * failure (a bounded wait that gave up, a slot or position out of range)
+ * is reported by pl_attn_status. */
 
 /* pl_attn_decode_batch with every array already in device memory.
  * max_pos must bound every d_pos[i] (it sizes the KV split).  The decode
