@@ -1070,6 +1070,94 @@ def run_decode1(local):
             "api": "pl_attn_decode through a void* ctypes binding, unregistered buffers"}
 
 
+def run_multi_device(args):
+    """One process driving every visible GPU through pl_attn_init_devices (the
+    C-ABI fan-out a C caller gets), host buffers:
+      seqs  config 4 weak-scaled, 64 sequences x 2048 rows per GPU, one
+            pl_attn_decode_batch call a step (PL_SPLIT_SEQS);
+      kv    config 5, one 32768-row sequence over 16 layers split along the
+            positions (PL_SPLIT_KV), one pl_attn_decode call per layer,
+            against the same calls on one GPU."""
+    import ctypes as C
+    import torch
+    import picolm_b200 as pb
+    D = args.gpus if args.gpus > 1 else torch.cuda.device_count()
+    res = {"devices": D}
+    devs = list(range(D))
+    # ---- sequences spread over the devices
+    n = SEQS_PER_GPU * D
+    at = pb.Attn(1, H, HK, CTX + NSTEP, n_seqs=n, devices=devs, split=pb.PL_SPLIT_SEQS)
+    rng = np.random.default_rng(3)
+    kc = make_cache_host(rng, CTX, KV_DIM)
+    for s in range(n):
+        at.kv_upload(s, 0, 0, kc, kc)
+    q = rng.standard_normal((n, Q_DIM), dtype=np.float32)
+    k = rng.standard_normal((n, KV_DIM), dtype=np.float32)
+    v = rng.standard_normal((n, KV_DIM), dtype=np.float32)
+    out = np.empty((n, Q_DIM), np.float32)
+    seqs = np.arange(n, dtype=np.int32)
+    for arr in (q, k, v, out):
+        at.host_register(arr)
+    f = at.raw().pl_attn_decode_batch
+    steps = max(args.steps, 20)
+
+    def run(j):
+        pos = np.full(n, CTX + j % NSTEP, np.int32)
+        rc = f(0, n, seqs.ctypes.data, pos.ctypes.data, q.ctypes.data, k.ctypes.data,
+               v.ctypes.data, out.ctypes.data)
+        if rc:
+            raise pb.PlAttnError(rc, "pl_attn_decode_batch")
+        return step_bytes(CTX + j % NSTEP, n)
+
+    for j in range(args.warmup):
+        run(j)
+    t0 = time.perf_counter()
+    nb = sum(run(args.warmup + j) for j in range(steps))
+    dt = time.perf_counter() - t0
+    for arr in (q, k, v, out):
+        at.host_unregister(arr)
+    at.close()
+    res["seqs"] = {"metric": "config-4 decode through pl_attn_decode_batch, host buffers, "
+                             "sequences spread over the devices of one context",
+                   "value": nb / dt / 1e9, "unit": "GB/s", "ms_per_step": dt / steps * 1e3,
+                   "sequences": n}
+    # ---- one long sequence split along the positions, against one GPU
+    L, HK5, CTX5 = 16, 8, 32768
+    kv5 = HK5 * HD
+    base = rng.standard_normal(CTX5 * kv5, dtype=np.float32)
+    from oracle import oracle as O
+    cache = O.fp32_to_fp16(base).reshape(CTX5, kv5)
+    qs = rng.standard_normal((L, Q_DIM), dtype=np.float32)
+    ks = rng.standard_normal((L, kv5), dtype=np.float32)
+    vs = rng.standard_normal((L, kv5), dtype=np.float32)
+    o5 = np.empty(Q_DIM, np.float32)
+    for label, dl, split in (("one_gpu", [0], pb.PL_SPLIT_SEQS), ("split", devs, pb.PL_SPLIT_KV)):
+        at = pb.Attn(L, H, HK5, CTX5 + 64, rope_base=500000.0, devices=dl, split=split)
+        for l in range(L):
+            at.kv_upload(0, l, 0, cache, cache)
+        d1 = at.raw().pl_attn_decode
+
+        def step5(j):
+            p = CTX5 + j
+            for l in range(L):
+                rc = d1(0, l, p, qs[l].ctypes.data, ks[l].ctypes.data, vs[l].ctypes.data,
+                        o5.ctypes.data)
+                if rc:
+                    raise pb.PlAttnError(rc, "pl_attn_decode")
+
+        step5(0)
+        ns = 16
+        t0 = time.perf_counter()
+        for j in range(1, ns + 1):
+            step5(j)
+        dt = time.perf_counter() - t0
+        nbytes = sum(L * ((CTX5 + j + 1) * kv5 * 4 + Q_DIM * 8 + kv5 * 12) for j in range(1, ns + 1))
+        res["kv_" + label] = {"value": nbytes / dt / 1e9, "unit": "GB/s",
+                              "ms_per_step_16_layers": dt / ns * 1e3, "devices": len(dl)}
+        at.close()
+    return res
+
+
 # ------------------------------------------------------------------ main
 def main():
     ap = argparse.ArgumentParser()
@@ -1078,10 +1166,12 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", choices=["all", "decode", "prefill", "long_ctx", "decode1",
-                                           "hd128", "block"],
+                                           "hd128", "block", "multi_device"],
                     default="all",
                     help="all: headline + configs 1/3/5 + CPU baseline; decode: headline only; "
-                         "prefill / long_ctx / decode1 / hd128 / block: that workload alone")
+                         "prefill / long_ctx / decode1 / hd128 / block: that workload alone; "
+                         "multi_device: every visible GPU from one process through "
+                         "pl_attn_init_devices (run without torchrun)")
     args = ap.parse_args()
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -1126,6 +1216,11 @@ def main():
             print(json.dumps(r), flush=True)
         import torch.distributed as dist
         dist.destroy_process_group()
+        return
+    if args.workload == "multi_device":
+        # one process drives every GPU itself (no torchrun)
+        if rank == 0:
+            print(json.dumps(run_multi_device(args)), flush=True)
         return
     if args.workload in ("prefill", "long_ctx", "decode1", "hd128", "block"):
         if rank == 0:
