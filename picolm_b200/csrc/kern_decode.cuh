@@ -550,8 +550,6 @@ __global__ void __launch_bounds__(288) decode_kernel(const DecodeArgs a,
   uint64_t* empty = full + NSTAGE;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int nthr = blockDim.x, n = a.n;
-  // the merge grid may start (and wait on griddepcontrol.wait) right away
-  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 
   // ---- set-up, overlapped with the end of the kernel queued before this one.
   // Launched with programmatic stream serialisation, this grid may start
@@ -593,6 +591,9 @@ __global__ void __launch_bounds__(288) decode_kernel(const DecodeArgs a,
   }
   // everything the kernel queued before this one wrote is visible from here on
   asm volatile("griddepcontrol.wait;" ::: "memory");
+  // The merge grid may launch once every CTA is here: by then the slots and
+  // positions are final, so the merge reads them before its own wait.
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   {
     const int per = (n + nthr - 1) / nthr, i0 = tid * per;
     bool any_bad = false;
@@ -694,24 +695,69 @@ __global__ void __launch_bounds__(288) decode_kernel(const DecodeArgs a,
 // memory.
 constexpr int kMergeThreads = 256;
 
+// Tile count of sequence i as the decode grid computed it (tp rows a tile;
+// 0 for a slot or position out of range).
+__device__ __forceinline__ int merge_seq_tiles(const DecodeArgs& a, int i, int tp) {
+  const int seq = a.seqs ? a.seqs[i] : a.seq1;
+  const int pos = a.pos ? a.pos[i] : a.pos1;
+  const int att_rows = a.mode == 0 ? pos + 1 : a.n_rows;
+  const int app_row = a.mode == 0 ? (a.append ? pos : -1) : (a.append ? pos - a.row0 : -1);
+  const bool bad = seq < 0 || seq >= a.n_slots || pos < 0 || pos >= a.pos_limit ||
+                   att_rows < 0 || att_rows > a.max_seq || app_row >= a.max_seq;
+  return bad ? 0 : (att_rows + tp - 1) / tp;
+}
+
 template <int HD>
-__global__ void __launch_bounds__(kMergeThreads) merge_kernel(const DecodeArgs a, int hpb) {
+__global__ void __launch_bounds__(kMergeThreads) merge_kernel(const DecodeArgs a, int hpb,
+                                                              int decode_ctas, int tp) {
   __shared__ float4 s_acc[kMergeThreads];
   __shared__ float2 s_ml[kMergeThreads];
+  __shared__ long long s_red[2][kMergeThreads / 32];
   // a merge of KV shards queued behind this grid may become resident now
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
-  asm volatile("griddepcontrol.wait;" ::: "memory");
   const int i = blockIdx.x, h0 = blockIdx.y * hpb, tid = threadIdx.x;
+  // This sequence's segments, from the same partition the decode grid used
+  // (the grid launched this one after every decode CTA had passed its own
+  // griddepcontrol.wait, so the slots and positions read here are final):
+  // tiles before sequence i and in total, then its first slot and count.
+  long long before = 0, total = 0;
+  for (int j = tid; j < a.n; j += kMergeThreads) {
+    const int t = merge_seq_tiles(a, j, tp);
+    total += t;
+    if (j < i) before += t;
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    before += __shfl_xor_sync(0xffffffffu, before, o);
+    total += __shfl_xor_sync(0xffffffffu, total, o);
+  }
+  if ((tid & 31) == 0) {
+    s_red[0][tid >> 5] = before;
+    s_red[1][tid >> 5] = total;
+  }
+  __syncthreads();
+  before = total = 0;
+  for (int w = 0; w < kMergeThreads / 32; ++w) {
+    before += s_red[0][w];
+    total += s_red[1][w];
+  }
+  const int mine = merge_seq_tiles(a, i, tp);
+  // the decode grid's partials are visible from here on
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   // every decode CTA has finished: its error bits are final
   if (a.err_host && i == 0 && blockIdx.y == 0 && tid == 0)
     *reinterpret_cast<volatile uint32_t*>(a.err_host) = atomicOr(a.err, 0u);
+  if (mine == 0 || total == 0) return;
   constexpr int PS = part_stride(HD);
   const int pairs = hpb * (HD / 4), lanes = kMergeThreads / pairs;
   const int pair = tid % pairs, lane_j = tid / pairs;
   const int hh = pair / (HD / 4), q4 = pair % (HD / 4), h = h0 + hh;
-  const int2 si = a.seg_info[i];
-  const int ns = si.y;
-  if (ns <= 1) return;  // finished by its single segment (or no rows)
+  const int G = static_cast<int>(decode_ctas < total ? decode_ctas : total);
+  const int c_first = static_cast<int>(((before + 1) * G - 1) / total);
+  const int c_last = static_cast<int>(((before + mine) * G - 1) / total);
+  const int ns = c_last - c_first + 1;
+  if (ns <= 1) return;  // finished by its single segment
+  const int2 si = make_int2(c_first + i, ns);
   const size_t slot_stride = static_cast<size_t>(a.n_heads) * PS;
   float m_loc = -INFINITY, l_loc = 0.f;
   float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);

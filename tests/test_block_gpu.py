@@ -61,6 +61,34 @@ def test_projection_vs_oracle(name):
                     _close_proj(got[i], want, f"{name} W{which} m{m} row {i}")
 
 
+@pytest.mark.parametrize("which", [0, 3])
+def test_projection_gemm_split_tiles(which):
+    # TinyLlama-shaped Q4_K weights over 1500 input rows: 12 x 16 = 192
+    # output tiles of 128 x 128, more than the 148 SMs, so the persistent
+    # GEMM splits some tiles between two CTAs and the fix-up kernel adds the
+    # parts (the last row tile is ragged too); every row against the oracle
+    import os
+    from concurrent.futures import ThreadPoolExecutor
+    rng = np.random.default_rng(77 + which)
+    H, Hk, hd, dim = 32, 4, 64, 2048
+    L = random_layer(rng, H, Hk, hd, dim, types=(GGUF_Q4_K,) * 4, bias=True)
+    rows, n = [(H * hd, dim), (Hk * hd, dim), (Hk * hd, dim), (dim, H * hd)][which]
+    bias = [L["bq"], L["bk"], L["bv"], L["bo"]][which]
+    m = 1500
+    x = rng.standard_normal((m, n), dtype=np.float32)
+    with pb.Attn(1, H, Hk, 64, head_dim=hd) as at:
+        upload_layer(at, 0, L)
+        got = at.proj(0, which, x, rows)
+
+    def one(i):
+        return O.matmul(L["w"][which], x[i], n, rows, GGUF_Q4_K) + bias
+
+    with ThreadPoolExecutor(os.cpu_count() or 4) as ex:
+        want = list(ex.map(one, range(m)))
+    for i in range(m):
+        _close_proj(got[i], want[i], f"W{which} row {i}")
+
+
 def test_projection_wide_input():
     # head_dim 128 x 32 heads: Wo takes 4096 inputs (16 KB a staged row)
     rng = np.random.default_rng(3)
