@@ -100,7 +100,8 @@ struct DecodeArgs {
   int out_stride;        // floats between the output rows of consecutive sequences
   float* part;           // [gridDim.x + n][n_heads][part_stride(HD)] segment partials
   float* part_out;       // mode 1: merged partial per sequence [n][n_heads][part_stride(HD)]
-  int2* seg_info;        // [n] (first slot, segment count), written by CTA 0
+  int2* seg_info;        // [n] (first slot, segment count), written by CTA 0 for
+                         // inspection; the merge derives the same from the positions
   // mode 0: attend rows [0, pos], append at row pos (if append; else the row
   //         is already in the cache).
   // mode 1: shard of a KV-split sequence: attend local rows [0, n_rows),

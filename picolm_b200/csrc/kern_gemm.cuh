@@ -19,13 +19,19 @@
 // quant.c:96-222); activations are split per call (act_split_kernel, with
 // the layer's RMSNorm applied on the way for the Q/K/V projections).
 //
-// Kernel: gemm_hilo_kernel below (a persistent grid, the work split evenly
-// over the SMs in 128 x 128 x 64 units), operand tiles of 16 KB (x_hi, x_lo,
-// w_hi, w_lo; 128-byte swizzle) loaded by TMA, tcgen05.mma kind::f16
-// M128 N128 into two double-buffered TMEM accumulator pairs.  Every mbarrier
-// wait is bounded; a wait that gives up sets an error bit and the CTA winds
-// down (it still waits for its own copies and MMAs, then frees its tensor
-// memory).
+// Kernel.  One CTA computes one 128 x 128 output tile over the whole K:
+//   warp 0   one lane streams the four operand tiles of each 64-wide k-step
+//            (x_hi, x_lo, w_hi, w_lo; 16 KB each, 128-byte swizzle) with 2-D
+//            TMA loads into a kGmStages-deep ring;
+//   warp 1   one lane issues the three MMAs per 16-wide k-slice
+//            (tcgen05.mma kind::f16, M128 N128) and frees each stage with a
+//            tcgen05.commit;
+//   warp 2   allocates the 256 TMEM columns (acc0, acc1) and frees them;
+//   warps 0-3 read their 32 accumulator rows back (tcgen05.ld) and write
+//            the FP32 outputs (bias, residual added).
+// Every mbarrier wait is bounded; a wait that gives up sets an error bit and
+// the CTA winds down (it still waits for its own copies and MMAs, then frees
+// its tensor memory).
 #pragma once
 #include <cstdint>
 #include <cuda.h>
@@ -66,38 +72,13 @@ struct GemmArgs {
   uint32_t* err;
 };
 
-// ---- persistent, evenly split GEMM ---------------------------------------
-// The work of one GEMM is n_tiles x kb_n units (a 128 x 128 tile times one
-// 64-wide k-step), tiles ordered row-tile major (consecutive tiles share
-// their x rows).  CTA c of the G = min(SMs, n_tiles) persistent CTAs takes
-// units [c*U/G, (c+1)*U/G), so every SM does the same MMA work whatever the
-// tile count (a fixed tiling of 320 tiles on 148 SMs leaves a third, mostly
-// idle round).  With more tiles than SMs, G is the SM count; with fewer, G
-// is a multiple of the tile count (each tile's k-steps split evenly over
-// G / n_tiles CTAs), so a few input rows still stream the weights with
-// every SM.  A tile whose units fall to more than one CTA is a split tile:
-// each part (a CTA's first or last segment) stores its partial sum to a
-// workspace, and gemm_fixup_kernel adds the parts in CTA order (earlier
-// k-steps first), then bias and residual -- the split points depend only on
-// the shape, so results repeat exactly, and no CTA waits on another.  Inside a CTA the two accumulators of a tile are double
-// buffered in tensor memory (2 x 256 of the 512 columns): the epilogue
-// warps drain one tile's while the MMA issuer fills the next one's.
-//   warp 0    one lane: TMA loads of the four operand tiles of each unit,
-//             a kGmStages-deep ring running on across tile boundaries;
-//   warp 1    one lane: the three MMAs per 16-wide k-slice, tcgen05.commit
-//             to free each stage and, at a segment's end, to hand the
-//             accumulator buffer to the epilogue;
-//   warps 2-5 epilogue (warp w reads TMEM lanes 32*(w%4)..), then release
-//             the buffer; warp 2 also allocates and frees the tensor memory.
-constexpr int kGmPThreads = 192;
-
 struct GmSmem {
   uint8_t xh[kGmStages][kGmTile];
   uint8_t xl[kGmStages][kGmTile];
   uint8_t wh[kGmStages][kGmTile];
   uint8_t wl[kGmStages][kGmTile];
   uint64_t full[kGmStages], empty[kGmStages];
-  uint64_t acc_full[2], acc_empty[2];
+  uint64_t done;
   uint32_t tmem_base;
 };
 
@@ -113,26 +94,8 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* m, uin
       : "memory");
 }
 
-struct GemmSplit {
-  int n_ntiles;        // column tiles (N / 128)
-  int kb_n;            // k-steps per tile (K / 64)
-  long long units;     // n_tiles * kb_n
-  float* ws;           // partial tiles: [G CTAs][2: first, last segment][128][128] FP32
-};
-
-// CTA of G owning unit u (the largest c with floor(units * c / G) <= u)
-__device__ __forceinline__ int gm_cta_of(const GemmSplit& sp, long long u, int G) {
-  return static_cast<int>(((u + 1) * G - 1) / sp.units);
-}
-
-// units of CTA c
-__device__ __forceinline__ long long gm_unit_begin(const GemmSplit& sp, int c) {
-  return sp.units * c / gridDim.x;
-}
-
-__global__ void __launch_bounds__(kGmPThreads, 1)
-    gemm_hilo_kernel(const GemmArgs a, const GemmSplit sp,
-                     const __grid_constant__ CUtensorMap tm_xh,
+__global__ void __launch_bounds__(kGmThreads, 1)
+    gemm_hilo_kernel(const GemmArgs a, const __grid_constant__ CUtensorMap tm_xh,
                      const __grid_constant__ CUtensorMap tm_xl,
                      const __grid_constant__ CUtensorMap tm_wh,
                      const __grid_constant__ CUtensorMap tm_wl) {
@@ -140,9 +103,8 @@ __global__ void __launch_bounds__(kGmPThreads, 1)
   GmSmem& sm = *reinterpret_cast<GmSmem*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int c = blockIdx.x;
-  const long long u0 = gm_unit_begin(sp, c), u1 = gm_unit_begin(sp, c + 1);
-  const int kb_n = sp.kb_n;
+  const int n0 = blockIdx.x * kGmBN, m0 = blockIdx.y * kGmBM;
+  const int kb_n = a.K / kGmBK;
 
   if (threadIdx.x == 0) {
     tma_prefetch_desc(&tm_xh);
@@ -153,238 +115,130 @@ __global__ void __launch_bounds__(kGmPThreads, 1)
       mbar_init(&sm.full[s], 1);
       mbar_init(&sm.empty[s], 1);
     }
-    for (int b = 0; b < 2; ++b) {
-      mbar_init(&sm.acc_full[b], 1);
-      mbar_init(&sm.acc_empty[b], 4);  // one arrival per epilogue warp
-    }
+    mbar_init(&sm.done, 1);
     fence_mbar_init();
   }
   if (warp == 2) {
-    tmem_alloc(&sm.tmem_base, 512);
+    tmem_alloc(&sm.tmem_base, 256);
     tmem_relinquish();
   }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = sm.tmem_base;
+  bool ok = true;
 
-  if (warp == 0) {
+  if (warp == 0 && lane == 0) {
     // ------------------------------------------------------------ producer
-    if (lane == 0) {
-      long long issued = 0;
-      for (long long u = u0; u < u1; ++u) {
-        const int it = static_cast<int>(u - u0), s = it % kGmStages;
-        if (it >= kGmStages && !mbar_wait_bounded(&sm.empty[s], ((it / kGmStages) - 1) & 1)) {
-          atomicOr(a.err, ERR_TIMEOUT_EMPTY);
-          break;
-        }
-        const long long t = u / kb_n;
-        const int kb = static_cast<int>(u - t * kb_n);
-        const int m0 = static_cast<int>(t / sp.n_ntiles) * kGmBM;
-        const int n0 = static_cast<int>(t % sp.n_ntiles) * kGmBN;
-        mbar_arrive_expect_tx(&sm.full[s], 4u * kGmTile);
-        const int k0 = kb * kGmBK;
-        tma_load_2d(sm.xh[s], &tm_xh, &sm.full[s], k0, m0);
-        tma_load_2d(sm.xl[s], &tm_xl, &sm.full[s], k0, m0);
-        tma_load_2d(sm.wh[s], &tm_wh, &sm.full[s], k0, a.w_row0 + n0);
-        tma_load_2d(sm.wl[s], &tm_wl, &sm.full[s], k0, a.w_row0 + n0);
-        ++issued;
+    int issued = 0;
+    for (int kb = 0; kb < kb_n; ++kb) {
+      const int s = kb % kGmStages;
+      if (kb >= kGmStages && !mbar_wait_bounded(&sm.empty[s], ((kb / kGmStages) - 1) & 1)) {
+        atomicOr(a.err, ERR_TIMEOUT_EMPTY);
+        break;
       }
-      // never leave with copies in flight: the last use of each stage must land
-      for (long long j = issued - kGmStages; j < issued; ++j)
-        if (j >= 0) mbar_wait_bounded(&sm.full[j % kGmStages], static_cast<uint32_t>((j / kGmStages) & 1));
+      mbar_arrive_expect_tx(&sm.full[s], 4u * kGmTile);
+      const int k0 = kb * kGmBK;
+      tma_load_2d(sm.xh[s], &tm_xh, &sm.full[s], k0, m0);
+      tma_load_2d(sm.xl[s], &tm_xl, &sm.full[s], k0, m0);
+      tma_load_2d(sm.wh[s], &tm_wh, &sm.full[s], k0, a.w_row0 + n0);
+      tma_load_2d(sm.wl[s], &tm_wl, &sm.full[s], k0, a.w_row0 + n0);
+      ++issued;
     }
-  } else if (warp == 1) {
+    // never leave with copies in flight: the last use of each stage must land
+    for (int j = issued - kGmStages; j < issued; ++j)
+      if (j >= 0) mbar_wait_bounded(&sm.full[j % kGmStages], (j / kGmStages) & 1);
+  } else if (warp == 1 && lane == 0) {
     // ------------------------------------------------------------ MMA issuer
-    if (lane == 0) {
-      const uint32_t idesc = idesc_f16_f32(kGmBM, kGmBN, 0);
-      bool ok = true;
-      int seg = 0;
-      for (long long u = u0; u < u1 && ok; ++seg) {
-        const long long t = u / kb_n;
-        const long long ue = (t + 1) * kb_n < u1 ? (t + 1) * kb_n : u1;  // this tile's units here
-        const int b = seg & 1;
-        // the epilogue has drained this buffer's previous tile
-        if (seg >= 2 && !mbar_wait_bounded(&sm.acc_empty[b], ((seg >> 1) - 1) & 1)) {
-          atomicOr(a.err, ERR_TIMEOUT_MMA);
-          ok = false;
-          break;
-        }
-        tc_fence_after();
-        const uint32_t acc0 = tmem + b * 2 * kGmBN, acc1 = acc0 + kGmBN;
-        for (long long v = u; v < ue; ++v) {
-          const int it = static_cast<int>(v - u0), s = it % kGmStages;
-          if (!mbar_wait_bounded(&sm.full[s], (it / kGmStages) & 1)) {
-            atomicOr(a.err, ERR_TIMEOUT_FULL);
-            ok = false;
-            break;
-          }
-          tc_fence_after();
-          const uint32_t xh = smem_u32(sm.xh[s]), xl = smem_u32(sm.xl[s]);
-          const uint32_t wh = smem_u32(sm.wh[s]), wl = smem_u32(sm.wl[s]);
-#pragma unroll
-          for (int kk = 0; kk < kGmBK / 16; ++kk) {  // 16 k per MMA, 32 bytes into the swizzle span
-            const uint32_t o = kk * 32;
-            const uint64_t dxh = smem_desc_sw128(xh + o, 16, 1024);
-            const uint64_t dxl = smem_desc_sw128(xl + o, 16, 1024);
-            const uint64_t dwh = smem_desc_sw128(wh + o, 16, 1024);
-            const uint64_t dwl = smem_desc_sw128(wl + o, 16, 1024);
-            const uint32_t accum = (v > u || kk > 0) ? 1u : 0u;
-            tc_mma_ss(acc0, dxh, dwh, idesc, accum);
-            tc_mma_ss(acc1, dxl, dwh, idesc, accum);
-            tc_mma_ss(acc1, dxh, dwl, idesc, 1u);
-          }
-          tc_commit(&sm.empty[s]);  // the stage is free once these MMAs have read it
-        }
-        tc_commit(&sm.acc_full[b]);  // the tile's sums (or partial sums) are ready
-        u = ue;
-      }
-    }
-  } else {
-    // ------------------------------------------------------------ epilogue
-    const int lg = warp & 3;  // TMEM lane group of this warp
-    bool ok = true;
-    int seg = 0;
-    for (long long u = u0; u < u1; ++seg) {
-      const long long t = u / kb_n;
-      const long long tb = t * kb_n, te = tb + kb_n;
-      const long long ue = te < u1 ? te : u1;
-      const int b = seg & 1;
-      if (ok && !mbar_wait_bounded(&sm.acc_full[b], (seg >> 1) & 1)) {
-        if (lane == 0) atomicOr(a.err, ERR_TIMEOUT_MMA);
+    const uint32_t idesc = idesc_f16_f32(kGmBM, kGmBN, 0);
+    const uint32_t acc0 = tmem, acc1 = tmem + kGmBN;
+    for (int kb = 0; kb < kb_n; ++kb) {
+      const int s = kb % kGmStages;
+      if (!mbar_wait_bounded(&sm.full[s], (kb / kGmStages) & 1)) {
+        atomicOr(a.err, ERR_TIMEOUT_FULL);
         ok = false;
+        break;
       }
-      const bool any_err = __any_sync(0xffffffffu, !ok);
-      if (any_err) break;
       tc_fence_after();
-      const int m0 = static_cast<int>(t / sp.n_ntiles) * kGmBM;
-      const int n0 = static_cast<int>(t % sp.n_ntiles) * kGmBN;
-      const int r = 32 * lg + lane;  // row of the tile
-      const int m = m0 + r;
-      // whole tile here: the outputs; else this CTA's part of a split tile,
-      // which can only be its first or its last segment
-      const bool whole = u == tb && ue == te;
-      float* part = nullptr;
-      if (!whole)
-        part = sp.ws + (static_cast<size_t>(c) * 2 + (seg == 0 ? 0 : 1)) * kGmBM * kGmBN;
-      int si = 0;
-      for (int i = 1; i < a.n_seg; ++i)
-        if (n0 >= a.seg[i].col0) si = i;
-      const GemmSeg sg = a.seg[si];
-      const int c0 = n0 - sg.col0;
-      const uint32_t lane_base = tmem + (static_cast<uint32_t>(32 * lg) << 16) + b * 2 * kGmBN;
-#pragma unroll 1
-      for (int cc = 0; cc < kGmBN; cc += 32) {
-        uint32_t r0[32], r1[32];
-        tc_ld_32x32b_x32(lane_base + cc, r0);
-        tc_ld_32x32b_x32(lane_base + kGmBN + cc, r1);
-        tc_wait_ld();
+      const uint32_t xh = smem_u32(sm.xh[s]), xl = smem_u32(sm.xl[s]);
+      const uint32_t wh = smem_u32(sm.wh[s]), wl = smem_u32(sm.wl[s]);
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          asm volatile("" : "+r"(r0[i]));
-          asm volatile("" : "+r"(r1[i]));
-        }
-        if (!whole) {
-          float* dst = part + static_cast<size_t>(r) * kGmBN + cc;
-#pragma unroll
-          for (int i = 0; i < 32; i += 4)
-            *reinterpret_cast<float4*>(dst + i) = make_float4(
-                __uint_as_float(r0[i]) + __uint_as_float(r1[i]) * kGmLoInv,
-                __uint_as_float(r0[i + 1]) + __uint_as_float(r1[i + 1]) * kGmLoInv,
-                __uint_as_float(r0[i + 2]) + __uint_as_float(r1[i + 2]) * kGmLoInv,
-                __uint_as_float(r0[i + 3]) + __uint_as_float(r1[i + 3]) * kGmLoInv);
-          continue;
-        }
-        if (m >= a.M) continue;
-        float* dst = sg.out + static_cast<size_t>(m) * sg.ld + c0 + cc;
-        const float* res = a.resid ? a.resid + static_cast<size_t>(m) * a.ld_res + c0 + cc : nullptr;
-#pragma unroll
-        for (int i = 0; i < 32; i += 4) {
-          float4 y;
-          y.x = __uint_as_float(r0[i]) + __uint_as_float(r1[i]) * kGmLoInv;
-          y.y = __uint_as_float(r0[i + 1]) + __uint_as_float(r1[i + 1]) * kGmLoInv;
-          y.z = __uint_as_float(r0[i + 2]) + __uint_as_float(r1[i + 2]) * kGmLoInv;
-          y.w = __uint_as_float(r0[i + 3]) + __uint_as_float(r1[i + 3]) * kGmLoInv;
-          if (sg.bias) {
-            const float4 bb = __ldg(reinterpret_cast<const float4*>(sg.bias + c0 + cc + i));
-            y.x += bb.x;
-            y.y += bb.y;
-            y.z += bb.z;
-            y.w += bb.w;
-          }
-          if (res) {
-            const float4 rr = *reinterpret_cast<const float4*>(res + i);
-            y.x = rr.x + y.x;
-            y.y = rr.y + y.y;
-            y.z = rr.z + y.z;
-            y.w = rr.w + y.w;
-          }
-          *reinterpret_cast<float4*>(dst + i) = y;
-        }
+      for (int kk = 0; kk < kGmBK / 16; ++kk) {  // 16 k per MMA, 32 bytes into the swizzle span
+        const uint32_t o = kk * 32;
+        const uint64_t dxh = smem_desc_sw128(xh + o, 16, 1024);
+        const uint64_t dxl = smem_desc_sw128(xl + o, 16, 1024);
+        const uint64_t dwh = smem_desc_sw128(wh + o, 16, 1024);
+        const uint64_t dwl = smem_desc_sw128(wl + o, 16, 1024);
+        const uint32_t accum = (kb > 0 || kk > 0) ? 1u : 0u;
+        tc_mma_ss(acc0, dxh, dwh, idesc, accum);
+        tc_mma_ss(acc1, dxl, dwh, idesc, accum);
+        tc_mma_ss(acc1, dxh, dwl, idesc, 1u);
       }
-      // the buffer may take the next tile's sums
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&sm.acc_empty[b]);
-      u = ue;
+      tc_commit(&sm.empty[s]);  // the stage is free once these MMAs have read it
+    }
+    tc_commit(&sm.done);  // after every MMA issued above (also on the error path)
+  }
+  __syncwarp();
+
+  // ---------------------------------------------------------------- epilogue
+  // every warp: its 32 TMEM lanes = output rows m0 + 32*warp + lane
+  if (!mbar_wait_bounded(&sm.done, 0)) {
+    if (lane == 0) atomicOr(a.err, ERR_TIMEOUT_MMA);
+    ok = false;
+  }
+  tc_fence_after();
+  // the tile's output segment (a tile never straddles two)
+  int si = 0;
+  for (int i = 1; i < a.n_seg; ++i)
+    if (n0 >= a.seg[i].col0) si = i;
+  const GemmSeg seg = a.seg[si];
+  const int c0 = n0 - seg.col0;
+  const int m = m0 + 32 * warp + lane;
+  const uint32_t lane_base = tmem + (static_cast<uint32_t>(32 * warp) << 16);
+  const bool any_err = __any_sync(0xffffffffu, !ok);
+#pragma unroll 1
+  for (int c = 0; c < kGmBN; c += 32) {
+    uint32_t r0[32], r1[32];
+    tc_ld_32x32b_x32(lane_base + c, r0);
+    tc_ld_32x32b_x32(lane_base + kGmBN + c, r1);
+    tc_wait_ld();
+#pragma unroll
+    for (int i = 0; i < 32; ++i) {
+      asm volatile("" : "+r"(r0[i]));
+      asm volatile("" : "+r"(r1[i]));
+    }
+    if (any_err || m >= a.M) continue;
+    float* dst = seg.out + static_cast<size_t>(m) * seg.ld + c0 + c;
+    const float* res = a.resid ? a.resid + static_cast<size_t>(m) * a.ld_res + c0 + c : nullptr;
+#pragma unroll
+    for (int i = 0; i < 32; i += 4) {
+      float4 y;
+      y.x = __uint_as_float(r0[i]) + __uint_as_float(r1[i]) * kGmLoInv;
+      y.y = __uint_as_float(r0[i + 1]) + __uint_as_float(r1[i + 1]) * kGmLoInv;
+      y.z = __uint_as_float(r0[i + 2]) + __uint_as_float(r1[i + 2]) * kGmLoInv;
+      y.w = __uint_as_float(r0[i + 3]) + __uint_as_float(r1[i + 3]) * kGmLoInv;
+      if (seg.bias) {
+        const float4 b = __ldg(reinterpret_cast<const float4*>(seg.bias + c0 + c + i));
+        y.x += b.x;
+        y.y += b.y;
+        y.z += b.z;
+        y.w += b.w;
+      }
+      if (res) {
+        const float4 r = *reinterpret_cast<const float4*>(res + i);
+        y.x = r.x + y.x;
+        y.y = r.y + y.y;
+        y.z = r.z + y.z;
+        y.w = r.w + y.w;
+      }
+      *reinterpret_cast<float4*>(dst + i) = y;
     }
   }
   tc_fence_before();
   __syncthreads();
   if (warp == 2) {
     tc_fence_after();
-    tmem_dealloc(tmem, 512);
-  }
-}
-
-// Split tiles: outputs = the parts of every CTA that worked on the tile,
-// added in CTA order (earlier k-steps first), + bias, + residual.
-// grid = n_tiles blocks (a tile one CTA did whole returns at once), block =
-// 256; G = the GEMM's CTA count.
-__global__ void __launch_bounds__(256) gemm_fixup_kernel(const GemmArgs a, const GemmSplit sp,
-                                                         int G) {
-  const long long t = blockIdx.x;
-  const long long tb = t * sp.kb_n, te = tb + sp.kb_n;
-  const int c_lo = gm_cta_of(sp, tb, G), c_hi = gm_cta_of(sp, te - 1, G);
-  if (c_lo == c_hi) return;  // done whole by one CTA
-  const int m0 = static_cast<int>(t / sp.n_ntiles) * kGmBM;
-  const int n0 = static_cast<int>(t % sp.n_ntiles) * kGmBN;
-  int si = 0;
-  for (int i = 1; i < a.n_seg; ++i)
-    if (n0 >= a.seg[i].col0) si = i;
-  const GemmSeg sg = a.seg[si];
-  const int c0 = n0 - sg.col0;
-  for (int idx = 4 * threadIdx.x; idx < kGmBM * kGmBN; idx += 4 * 256) {
-    const int r = idx / kGmBN, col = idx % kGmBN, m = m0 + r;
-    if (m >= a.M) continue;
-    float4 y = make_float4(0.f, 0.f, 0.f, 0.f);
-    for (int cc = c_lo; cc <= c_hi; ++cc) {
-      // the tile is CTA cc's first segment if its range starts inside it
-      const long long u0 = sp.units * cc / G;
-      const int which = u0 >= tb ? 0 : 1;
-      const float4 x = *reinterpret_cast<const float4*>(
-          sp.ws + (static_cast<size_t>(cc) * 2 + which) * kGmBM * kGmBN + idx);
-      y.x += x.x;
-      y.y += x.y;
-      y.z += x.z;
-      y.w += x.w;
-    }
-    if (sg.bias) {
-      const float4 bb = __ldg(reinterpret_cast<const float4*>(sg.bias + c0 + col));
-      y.x += bb.x;
-      y.y += bb.y;
-      y.z += bb.z;
-      y.w += bb.w;
-    }
-    if (a.resid) {
-      const float4 rr =
-          *reinterpret_cast<const float4*>(a.resid + static_cast<size_t>(m) * a.ld_res + c0 + col);
-      y.x = rr.x + y.x;
-      y.y = rr.y + y.y;
-      y.z = rr.z + y.z;
-      y.w = rr.w + y.w;
-    }
-    *reinterpret_cast<float4*>(sg.out + static_cast<size_t>(m) * sg.ld + c0 + col) = y;
+    tmem_dealloc(tmem, 256);
   }
 }
 

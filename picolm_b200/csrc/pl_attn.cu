@@ -118,8 +118,6 @@ struct Ctx {
   __half* d_xh = nullptr;            // GEMM activations: FP16 high parts, then
   __half* d_xl = nullptr;            // the 2^11-scaled residuals
   size_t act_cap = 0;                // elements of each
-  float* d_gws = nullptr;            // GEMM split-tile partials
-  size_t gws_cap = 0;                // floats
   bool gemm_smem_set = false;
   bool proj_smem_set = false;
 };
@@ -721,7 +719,6 @@ void free_ctx(Ctx* c) {
   }
   cudaFree(c->d_xh);
   cudaFree(c->d_xl);
-  cudaFree(c->d_gws);
   for (cudaEvent_t e : c->ev_pool) cudaEventDestroy(e);
   if (c->stream) cudaStreamDestroy(c->stream);
   delete c;
@@ -1836,46 +1833,11 @@ int launch_gemm(const LayerW& L, bool qkv, const float* d_x, int ldx, int M, int
   a.resid = resid;
   a.ld_res = ld_res;
   a.err = g->d_err;
-  // the tiles' units split evenly over at most one CTA per SM; tiles cut
-  // between two CTAs go through the workspace and the fix-up kernel
-  pl::GemmSplit sp = {};
-  sp.n_ntiles = N / pl::kGmBN;
-  sp.kb_n = K / pl::kGmBK;
-  const long long n_tiles = static_cast<long long>(sp.n_ntiles) * ((M + pl::kGmBM - 1) / pl::kGmBM);
-  sp.units = n_tiles * sp.kb_n;
-  // more tiles than SMs: one CTA per SM; fewer: every tile's k-steps split
-  // over the same number of CTAs, as many as the SMs allow
-  int G;
-  if (n_tiles >= g->num_sms) {
-    G = g->num_sms;
-  } else {
-    long long per = g->num_sms / n_tiles;
-    if (per > sp.kb_n) per = sp.kb_n;
-    G = static_cast<int>(n_tiles * per);
-  }
-  if (G != n_tiles) {
-    const size_t need = static_cast<size_t>(G) * 2 * pl::kGmBM * pl::kGmBN;
-    if (need > g->gws_cap) {
-      if (g->d_gws) {
-        cudaStreamSynchronize(g->stream);
-        cudaFree(g->d_gws);
-      }
-      g->d_gws = nullptr;
-      g->gws_cap = 0;
-      if (dev_alloc(&g->d_gws, need * sizeof(float)) != cudaSuccess) return PL_ENOMEM;
-      g->gws_cap = need;
-    }
-  }
-  sp.ws = g->d_gws;
-  pl::gemm_hilo_kernel<<<G, pl::kGmPThreads, pl::gm_smem_bytes(), st>>>(
-      a, sp, tm_xh, tm_xl, qkv ? L.tm_qkv_h : L.tm_o_h, qkv ? L.tm_qkv_l : L.tm_o_l);
+  const dim3 grid(N / pl::kGmBN, (M + pl::kGmBM - 1) / pl::kGmBM);
+  pl::gemm_hilo_kernel<<<grid, pl::kGmThreads, pl::gm_smem_bytes(), st>>>(
+      a, tm_xh, tm_xl, qkv ? L.tm_qkv_h : L.tm_o_h, qkv ? L.tm_qkv_l : L.tm_o_l);
   PL_CUDA(cudaGetLastError());
   count_launch();
-  if (G != n_tiles) {
-    pl::gemm_fixup_kernel<<<static_cast<unsigned>(n_tiles), 256, 0, st>>>(a, sp, G);
-    PL_CUDA(cudaGetLastError());
-    count_launch();
-  }
   return PL_OK;
 }
 
