@@ -62,11 +62,10 @@ def test_projection_vs_oracle(name):
 
 
 @pytest.mark.parametrize("which", [0, 3])
-def test_projection_gemm_split_tiles(which):
+def test_projection_gemm_many_tiles(which):
     # TinyLlama-shaped Q4_K weights over 1500 input rows: 12 x 16 = 192
-    # output tiles of 128 x 128, more than the 148 SMs, so the persistent
-    # GEMM splits some tiles between two CTAs and the fix-up kernel adds the
-    # parts (the last row tile is ragged too); every row against the oracle
+    # output tiles of 128 x 128, more CTAs than the 148 SMs (a second round),
+    # and a ragged last row tile; every row against the oracle
     import os
     from concurrent.futures import ThreadPoolExecutor
     rng = np.random.default_rng(77 + which)
