@@ -329,11 +329,38 @@ def run_batched_decode(args, rank, world, local, peaks):
         at.host_unregister(arr)
     h2d = SEQS_PER_GPU * (Q_DIM + 2 * KV_DIM) * 4 + 2 * SEQS_PER_GPU * 4
     d2h = SEQS_PER_GPU * Q_DIM * 4 + 4
+    call_us = t_e2e * 1e6 / n_e2e
+    # where a call's time goes: the copy of q to the device (a pinned-to-
+    # device copy of the same bytes, timed alone with CUDA events), the
+    # decode + merge launches as timed one by one above (the merge then
+    # writes the output over the bus instead), and the rest: the small copy
+    # of slots and positions, k/v read and the output written over the bus,
+    # launch and wake-up latency, host work
+    qpin = torch.empty(SEQS_PER_GPU * Q_DIM, dtype=torch.float32, pin_memory=True)
+    qdev = torch.empty(SEQS_PER_GPU * Q_DIM, dtype=torch.float32, device=dev)
+    for _ in range(3):
+        qdev.copy_(qpin, non_blocking=True)
+    c0, c1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    c0.record()
+    for _ in range(20):
+        qdev.copy_(qpin, non_blocking=True)
+    c1.record()
+    torch.cuda.synchronize()
+    h2d_q_us = c0.elapsed_time(c1) * 1e3 / 20
+    kern_us = kern_ms * 1e3 / n_prof
     res["e2e"] = {"value": e2e_bytes * world / t_e2e / 1e9, "unit": "GB/s",
                   "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                   "ms_per_step": t_e2e * 1e3 / n_e2e, "steps": n_e2e,
                   "api": "pl_attn_decode_batch through a void* ctypes binding (host "
                          "buffers registered with pl_attn_host_register, synchronous)",
+                  "phases_us": {"call": call_us, "h2d_q_copy": h2d_q_us,
+                                "decode_merge_launches": kern_us,
+                                "rest": call_us - h2d_q_us - kern_us},
+                  "path": "q copied to the device (one copy) with the slots and positions in a "
+                          "second; k and v read by the appending segment, and the output "
+                          "written by the merge, over the bus from / into the registered "
+                          "buffers",
                   "unregistered_ms_per_step": t_staged * 1e3 / n_e2e}
     at.close()
     return res
@@ -783,8 +810,9 @@ def run_long_ctx_split(args, rank, world, local, peaks):
     """Config 5 split along the KV axis over `world` GPUs: rank r holds a
     contiguous 1/world of the 32768 cached positions (the last rank also the
     appended ones); per layer and step each rank computes its partial
-    (m, l, o), pushes it to every rank over NVLink and merges
-    (picolm_b200/shard.py).  Timed on every rank, max over ranks."""
+    (m, l, o), pushes it to every rank over NVLink and merges, all in one
+    call (pl_attn_decode_p2p_dev through picolm_b200/shard.py).  Timed on
+    every rank, max over ranks."""
     import torch
     import picolm_b200 as pb
     from picolm_b200.shard import PART_STRIDE, KVSplitDecoder, P2PShardOps
@@ -847,9 +875,11 @@ def run_long_ctx_split(args, rank, world, local, peaks):
             "pct_peak_per_gpu": 100.0 * nbytes / (ms / 1e3) / 1e9 / world / peaks["hbm_gbs"],
             "tok_per_s": NS5 / (ms / 1e3), "ms_per_step_16_layers": ms / NS5,
             "timing": "one CUDA graph of all 32 steps, replayed",
-            "scaling": "strong", "collective": "per layer one kernel on every rank pushes its "
-                                             "32 x 68 FP32 partial into every rank's buffer over "
-                                             "NVLink (P2P stores, epoch stamps) and merges (LSE)",
+            "scaling": "strong", "collective": "per layer the merge grid of every rank's partial "
+                                             "(pl_attn_decode_p2p_dev) stores its 32 x 68 FP32 "
+                                             "partial into every rank's buffer over NVLink (P2P "
+                                             "stores); its last block stamps the epoch, waits for "
+                                             "every rank's stamp and merges (LSE)",
             "config": {"workload": "config5 16 layers, 32/8 heads, hd 64, theta 5e5, "
                                    "32768 cached + 32 steps, KV N(0,1) seed 4",
                        "shard": f"{dec.n_rows} cached positions on rank {rank}"}}

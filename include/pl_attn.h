@@ -247,6 +247,18 @@ int  pl_attn_xfer_connect(const void *handles);
  * of these calls can be replayed. */
 int  pl_attn_combine_p2p_dev(const float *d_part, float *d_out, void *stream);
 
+/* pl_attn_decode_partial_dev followed by pl_attn_combine_p2p_dev in one
+ * call, without the intermediate partial: the grid that merges this rank's
+ * segments stores the merged heads straight into every rank's buffer, and
+ * its last block stamps, waits (bounded) for every rank and writes the
+ * merged output to d_out [n_heads*head_dim].  Arguments as
+ * pl_attn_decode_partial_dev (n_rows = 0: an empty shard, which still takes
+ * part in the exchange); calling rules as pl_attn_combine_p2p_dev.  One
+ * kernel launch fewer per layer than the two calls. */
+int  pl_attn_decode_p2p_dev(int seq, int layer, int pos, int row0, int n_rows,
+                            int append, const float *d_q, const float *d_k,
+                            const float *d_v, float *d_out, void *stream);
+
 /* pl_attn_decode_batch_dev for callers that cannot allow the library to
  * allocate device memory.  No counterpart in the reference: picolm's
  * attention runs on the CPU and allocates nothing per step.
@@ -485,6 +497,15 @@ static inline int pl_attn_xfer_connect(const void *handles) {
 static inline int pl_attn_combine_p2p_dev(const float *d_part, float *d_out,
                                           void *stream) {
     (void)d_part; (void)d_out; (void)stream; return PL_ESTATE;
+}
+static inline int pl_attn_decode_p2p_dev(int seq, int layer, int pos, int row0,
+                                         int n_rows, int append,
+                                         const float *d_q, const float *d_k,
+                                         const float *d_v, float *d_out,
+                                         void *stream) {
+    (void)seq; (void)layer; (void)pos; (void)row0; (void)n_rows; (void)append;
+    (void)d_q; (void)d_k; (void)d_v; (void)d_out; (void)stream;
+    return PL_ESTATE;
 }
 static inline int pl_attn_decode_batch_dev_noalloc(int layer, int n,
                                                    const int *d_seqs,

@@ -104,6 +104,7 @@ def load(path: str = LIB_PATH) -> C.CDLL:
         "pl_attn_xfer_setup": (i, [i, i, _vp]),
         "pl_attn_xfer_connect": (i, [_vp]),
         "pl_attn_combine_p2p_dev": (i, [_vp, _vp, _vp]),
+        "pl_attn_decode_p2p_dev": (i, [i, i, i, i, i, i, _vp, _vp, _vp, _vp, _vp]),
         "pl_attn_decode_batch_dev_noalloc": (i, [i, i, _vp, _vp, i, _vp, _vp, _vp, _vp, _vp]),
         "pl_attn_set_layer": (i, [i, i, _vp, C.c_float, _vp, i, _vp, i, _vp, i, _vp, i,
                                   _vp, _vp, _vp, _vp, _vp, _vp]),
@@ -388,6 +389,12 @@ class Attn:
     def combine_p2p_dev(self, d_part, d_out, stream=None) -> None:
         _check(self.lib.pl_attn_combine_p2p_dev(d_part, d_out, stream),
                "pl_attn_combine_p2p_dev")
+
+    def decode_p2p_dev(self, seq, layer, pos, row0, n_rows, append, d_q, d_k, d_v, d_out,
+                       stream=None) -> None:
+        _check(self.lib.pl_attn_decode_p2p_dev(seq, layer, pos, row0, n_rows, int(append), d_q,
+                                               d_k, d_v, d_out, stream),
+               "pl_attn_decode_p2p_dev")
 
     def kv_ptr(self, seq: int, layer: int):
         k = _vp()

@@ -683,6 +683,168 @@ __global__ void __launch_bounds__(288) decode_kernel(const DecodeArgs a,
   }
 }
 
+// ---- exchange of a KV split over NVLink peer memory (one process per GPU)
+// Each rank owns a receive buffer, mapped into every other rank's address
+// space (CUDA IPC): a 256-byte header holding the rank's merge counter at
+// byte 128, then for each epoch parity, each source rank and each head the
+// source's partial (m, l, o) as ll_units(HD) 16-byte units
+// {a, epoch, b, epoch}: unit 0 carries (m, l), unit 1 + j carries
+// (o[2j], o[2j+1]).  A source writes each unit with one 16-byte volatile
+// store into every rank's buffer (over NVLink for the peers).  A reader
+// that finds the merge's epoch in both flag words of a unit has both
+// values, since each 8-byte half is written and read whole, so neither a
+// fence nor a separate flag is needed (the "low-latency" protocol of
+// collective libraries); the data crosses NVLink once, with its flag.  Two
+// parities alternate: a rank writes epoch e + 2 only after it has read every
+// rank's epoch e + 1 units, and a rank stores those only once its merge of
+// epoch e is complete, so no unit is overwritten while it may be read.  The
+// epoch is the rank's merge counter plus one, kept on the device, so CUDA
+// graphs of these calls replay; every rank merges equally often, so the
+// counters agree.
+constexpr int kXferMaxRanks = 8;
+constexpr int kXferHeaderBytes = 256;
+constexpr int kXferCounterOffset = 128;  // byte offset of the own merge counter
+
+__host__ __device__ constexpr int ll_units(int hd) { return 1 + hd / 2; }
+
+// Bytes of one rank's receive buffer.
+__host__ __device__ constexpr size_t xfer_buffer_bytes(int world, int n_heads, int hd) {
+  return kXferHeaderBytes + static_cast<size_t>(2) * world * n_heads * ll_units(hd) * 16;
+}
+
+struct XferPeers {
+  uint8_t* base[kXferMaxRanks];  // each rank's receive buffer, as seen from this GPU
+};
+
+// The merge grid of a KV shard's partial exchanges it itself
+// (merge_kernel<HD, true>): each block pushes its head and merges it.
+struct XferPush {
+  XferPeers peers;
+  int world, rank;
+  uint32_t* arrive;  // blocks of the merge grid that have read the counter (zero at rest)
+  float* out;        // [n_heads * HD] merged output
+};
+
+// Unit u of head h from source rank src, epoch parity `parity`, in the
+// buffer at base.
+__device__ __forceinline__ uint8_t* ll_unit(uint8_t* base, uint32_t parity, int world, int src,
+                                            int n_heads, int h, int u, int hd) {
+  return base + kXferHeaderBytes +
+         (((static_cast<size_t>(parity) * world + src) * n_heads + h) * ll_units(hd) + u) * 16;
+}
+
+__device__ __forceinline__ void st_ll(uint8_t* p, float a, float b, uint32_t e) {
+  asm volatile("st.volatile.global.v4.u32 [%0], {%1, %2, %3, %4};" ::"l"(p),
+               "r"(__float_as_uint(a)), "r"(e), "r"(__float_as_uint(b)), "r"(e)
+               : "memory");
+}
+
+__device__ __forceinline__ uint4 ld_ll(const uint8_t* p) {
+  uint4 v;
+  asm volatile("ld.volatile.global.v4.u32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(p)
+               : "memory");
+  return v;
+}
+
+// Thread (h, q4) of an exchange: this rank's partial of head h -- o[4q4 ..
+// 4q4 + 3] as units 1 + 2q4 and 2 + 2q4 and, from q4 == 0, (m, l) as unit
+// 0 -- into slot (epoch & 1, rank) of every rank's buffer.
+template <int HD>
+__device__ __forceinline__ void ll_push(const XferPeers& peers, int world, int rank,
+                                        int n_heads, uint32_t epoch, int h, int q4, float m,
+                                        float l, float4 o) {
+  for (int r = 0; r < world; ++r) {
+    uint8_t* u0 = ll_unit(peers.base[r], epoch & 1u, world, rank, n_heads, h, 0, HD);
+    st_ll(u0 + (1 + 2 * q4) * 16, o.x, o.y, epoch);
+    st_ll(u0 + (2 + 2 * q4) * 16, o.z, o.w, epoch);
+    if (q4 == 0) st_ll(u0, m, l, epoch);
+  }
+}
+
+// Thread (h, q4): wait, bounded, for every rank's units of head h in this
+// rank's buffer and write out[h * HD + 4q4 .. + 3], merged in log-sum-exp
+// form.  Two ranks at a time: their six loads are issued together, only the
+// units still missing are polled, and the pair is folded into a running
+// (max, sum, o) (few registers, however many ranks).  False (nothing
+// written) if a wait gave up.
+template <int HD>
+__device__ __forceinline__ bool ll_merge(const XferPeers& peers, int world, int rank,
+                                         int n_heads, uint32_t epoch, int h, int q4,
+                                         float* out) {
+  const uint64_t lim = wait_limit_ns();
+  uint64_t t0 = 0;
+  float M = -INFINITY, L = 0.f;
+  float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
+  for (int r0 = 0; r0 < world; r0 += 2) {
+    uint4 u[2][3];
+    const uint8_t* src[2];
+#pragma unroll
+    for (int k = 0; k < 2; ++k)
+      if (r0 + k < world) {
+        src[k] = ll_unit(peers.base[rank], epoch & 1u, world, r0 + k, n_heads, h, 0, HD);
+        u[k][0] = ld_ll(src[k]);
+        u[k][1] = ld_ll(src[k] + (1 + 2 * q4) * 16);
+        u[k][2] = ld_ll(src[k] + (2 + 2 * q4) * 16);
+      }
+#pragma unroll
+    for (int k = 0; k < 2; ++k)
+      if (r0 + k < world) {
+#pragma unroll
+        for (int j = 0; j < 3; ++j) {
+          const int off = j == 0 ? 0 : (j + 2 * q4) * 16;
+          while (u[k][j].y != epoch || u[k][j].w != epoch) {
+            const uint64_t now = globaltimer();
+            if (!t0) t0 = now;
+            else if (now - t0 > lim) return false;
+            u[k][j] = ld_ll(src[k] + off);
+          }
+        }
+        const float m = __uint_as_float(u[k][0].x);
+        if (m == -INFINITY) continue;  // an empty shard: l = 0, o = 0
+        if (m > M) {
+          const float sc = ex2(M - m);  // 0 while M is -inf
+          L *= sc;
+          o.x *= sc;
+          o.y *= sc;
+          o.z *= sc;
+          o.w *= sc;
+          M = m;
+        }
+        const float w = ex2(m - M);
+        L += w * __uint_as_float(u[k][0].z);
+        o.x += w * __uint_as_float(u[k][1].x);
+        o.y += w * __uint_as_float(u[k][1].z);
+        o.z += w * __uint_as_float(u[k][2].x);
+        o.w += w * __uint_as_float(u[k][2].z);
+      }
+  }
+  const float inv = 1.0f / L;
+  reinterpret_cast<float4*>(out + static_cast<size_t>(h) * HD)[q4] =
+      make_float4(o.x * inv, o.y * inv, o.z * inv, o.w * inv);
+  return true;
+}
+
+// End of a pushing merge block: thread (h, q4) of an active head pushes
+// and merges; the block that took the grid's last ticket (one per block,
+// taken after the block read the counter) advances the counter to `epoch`
+// and rearms the ticket count for the next merge grid.
+template <int HD>
+__device__ __forceinline__ void xfer_finish(const DecodeArgs& a, const XferPush& x,
+                                            uint32_t epoch, uint32_t ticket, bool active, int h,
+                                            int q4, float M, float L, float4 o) {
+  if (active) {
+    ll_push<HD>(x.peers, x.world, x.rank, a.n_heads, epoch, h, q4, M, L, o);
+    if (!ll_merge<HD>(x.peers, x.world, x.rank, a.n_heads, epoch, h, q4, x.out))
+      atomicOr(a.err, ERR_TIMEOUT_FULL);
+  }
+  if (threadIdx.x == blockDim.x - 1 && ticket == gridDim.x * gridDim.y - 1) {
+    *reinterpret_cast<volatile uint32_t*>(x.peers.base[x.rank] + kXferCounterOffset) = epoch;
+    *x.arrive = 0;
+  }
+}
+
 // Merge of the segment partials of one decode launch.
 // grid = (n, ceil(n_heads / hpb)), block = kMergeThreads; a block merges
 // heads [h0, h0 + hpb) of sequence i.  Thread t owns float4 column q4 of
@@ -708,9 +870,14 @@ __device__ __forceinline__ int merge_seq_tiles(const DecodeArgs& a, int i, int t
   return bad ? 0 : (att_rows + tp - 1) / tp;
 }
 
-template <int HD>
+// PUSH: the grid merges one KV shard's partial (mode 1, one sequence, one
+// head per block) and exchanges it (XferPush): each block pushes its head to
+// every rank and merges every rank's partial of that head into x.out.
+template <int HD, bool PUSH>
 __global__ void __launch_bounds__(kMergeThreads) merge_kernel(const DecodeArgs a, int hpb,
-                                                              int decode_ctas, int tp) {
+                                                              int decode_ctas, int tp,
+                                                              const XferPush x) {
+  __shared__ uint32_t s_epoch;
   __shared__ float4 s_acc[kMergeThreads];
   __shared__ float2 s_ml[kMergeThreads];
   __shared__ long long s_red[2][kMergeThreads / 32];
@@ -748,16 +915,47 @@ __global__ void __launch_bounds__(kMergeThreads) merge_kernel(const DecodeArgs a
   // every decode CTA has finished: its error bits are final
   if (a.err_host && i == 0 && blockIdx.y == 0 && tid == 0)
     *reinterpret_cast<volatile uint32_t*>(a.err_host) = atomicOr(a.err, 0u);
-  if (mine == 0 || total == 0) return;
   constexpr int PS = part_stride(HD);
   const int pairs = hpb * (HD / 4), lanes = kMergeThreads / pairs;
   const int pair = tid % pairs, lane_j = tid / pairs;
   const int hh = pair / (HD / 4), q4 = pair % (HD / 4), h = h0 + hh;
+  const bool active = lane_j == 0 && h < a.n_heads;
+  // PUSH: this merge's epoch, one past the counter that the previous merge
+  // grid (complete before the decode grid, and so this one, passed its
+  // wait) left in this rank's buffer; then one ticket per block, taken
+  // after the read
+  uint32_t epoch = 0, ticket = 0;
+  if constexpr (PUSH) {
+    if (tid == 0)
+      s_epoch = *reinterpret_cast<volatile const uint32_t*>(x.peers.base[x.rank] +
+                                                            kXferCounterOffset) + 1u;
+    __syncthreads();
+    epoch = s_epoch;
+    if (tid == kMergeThreads - 1) ticket = atomicAdd(x.arrive, 1u);
+  }
+  if (mine == 0 || total == 0) {
+    if constexpr (PUSH)  // an empty or rejected shard contributes nothing
+      xfer_finish<HD>(a, x, epoch, ticket, active, h, q4, -INFINITY, 0.f,
+                      make_float4(0.f, 0.f, 0.f, 0.f));
+    return;
+  }
   const int G = static_cast<int>(decode_ctas < total ? decode_ctas : total);
   const int c_first = static_cast<int>(((before + 1) * G - 1) / total);
   const int c_last = static_cast<int>(((before + mine) * G - 1) / total);
   const int ns = c_last - c_first + 1;
-  if (ns <= 1) return;  // finished by its single segment
+  if (ns <= 1) {  // finished by its single segment (into part_out in mode 1)
+    if constexpr (PUSH) {
+      float2 ml = make_float2(-INFINITY, 0.f);
+      float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (active) {
+        const float* src = a.part_out + static_cast<size_t>(h) * PS;
+        ml = __ldcg(reinterpret_cast<const float2*>(src));
+        o = __ldcg(reinterpret_cast<const float4*>(src + kPartO) + q4);
+      }
+      xfer_finish<HD>(a, x, epoch, ticket, active, h, q4, ml.x, ml.y, o);
+    }
+    return;
+  }
   const int2 si = make_int2(c_first + i, ns);
   const size_t slot_stride = static_cast<size_t>(a.n_heads) * PS;
   float m_loc = -INFINITY, l_loc = 0.f;
@@ -808,34 +1006,37 @@ __global__ void __launch_bounds__(kMergeThreads) merge_kernel(const DecodeArgs a
   s_acc[tid] = acc;
   s_ml[tid] = make_float2(m_loc, l_loc);
   __syncthreads();
-  if (lane_j != 0 || h >= a.n_heads) return;
-  float M = m_loc;
-  for (int l = 1; l < lanes; ++l) M = fmaxf(M, s_ml[tid + l * pairs].x);
-  float L = 0.f;
+  float M = m_loc, L = 0.f;
   float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
-  if (M != -INFINITY)
-    for (int l = 0; l < lanes; ++l) {
-      const float2 ml = s_ml[tid + l * pairs];
-      const float4 x = s_acc[tid + l * pairs];
-      const float w = ex2(ml.x - M);
-      L += w * ml.y;
-      o.x += w * x.x;
-      o.y += w * x.y;
-      o.z += w * x.z;
-      o.w += w * x.w;
-    }
-  if (a.mode == 0) {
-    const float inv = 1.0f / L;
-    reinterpret_cast<float4*>(a.out + static_cast<size_t>(i) * a.out_stride + h * HD)[q4] =
-        make_float4(o.x * inv, o.y * inv, o.z * inv, o.w * inv);
-  } else {
-    float* dst = a.part_out + (static_cast<size_t>(i) * a.n_heads + h) * PS;
-    reinterpret_cast<float4*>(dst + kPartO)[q4] = o;
-    if (q4 == 0) {
-      dst[0] = M;
-      dst[1] = L;
+  if (active) {
+    for (int l = 1; l < lanes; ++l) M = fmaxf(M, s_ml[tid + l * pairs].x);
+    if (M != -INFINITY)
+      for (int l = 0; l < lanes; ++l) {
+        const float2 ml = s_ml[tid + l * pairs];
+        const float4 xv = s_acc[tid + l * pairs];
+        const float w = ex2(ml.x - M);
+        L += w * ml.y;
+        o.x += w * xv.x;
+        o.y += w * xv.y;
+        o.z += w * xv.z;
+        o.w += w * xv.w;
+      }
+    if constexpr (PUSH) {
+      // pushed and merged below, with the rest of the block
+    } else if (a.mode == 0) {
+      const float inv = 1.0f / L;
+      reinterpret_cast<float4*>(a.out + static_cast<size_t>(i) * a.out_stride + h * HD)[q4] =
+          make_float4(o.x * inv, o.y * inv, o.z * inv, o.w * inv);
+    } else {
+      float* dst = a.part_out + (static_cast<size_t>(i) * a.n_heads + h) * PS;
+      reinterpret_cast<float4*>(dst + kPartO)[q4] = o;
+      if (q4 == 0) {
+        dst[0] = M;
+        dst[1] = L;
+      }
     }
   }
+  if constexpr (PUSH) xfer_finish<HD>(a, x, epoch, ticket, active, h, q4, M, L, o);
 }
 
 // Log-sum-exp merge of partials gathered from several devices (one

@@ -44,6 +44,10 @@ struct Xfer {
   uint8_t* local = nullptr;              // this rank's buffer (cudaMalloc)
   pl::XferPeers peers = {};              // every rank's buffer as seen from this GPU
   void* opened[pl::kXferMaxRanks] = {};  // IPC mappings to close
+  // pl_attn_decode_p2p_dev: the merge grid's arrival counter (zero at rest)
+  // and the shard's partial when one decode CTA covers it
+  uint32_t* d_arrive = nullptr;
+  float* d_part1 = nullptr;
 };
 
 // One layer's attention weights on the device (pl_attn_set_layer), all in one
@@ -86,6 +90,7 @@ struct Ctx {
   // staging for host-buffer calls
   uint8_t* d_stage = nullptr;
   uint8_t* h_stage = nullptr;
+  uint8_t* h_stage_dev = nullptr;  // h_stage as the device addresses it (mapped)
   size_t stage_cap = 0;
   // split-KV partials
   float* d_part = nullptr;
@@ -150,6 +155,8 @@ void xfer_free() {
   for (int r = 0; r < pl::kXferMaxRanks; ++r)
     if (g_xfer->opened[r]) cudaIpcCloseMemHandle(g_xfer->opened[r]);
   cudaFree(g_xfer->local);
+  cudaFree(g_xfer->d_arrive);
+  cudaFree(g_xfer->d_part1);
   delete g_xfer;
   g_xfer = nullptr;
 }
@@ -233,6 +240,10 @@ void host_rope_tables(float* c, float* s, int max_seq, int head_dim, float base)
     }
 }
 
+// A q of up to this many bytes rides in the staging area's one copy even
+// when registered: a host memcpy of 16 KB costs less than a second copy.
+constexpr size_t kStagedQBytes = 16384;
+
 int ensure_stage(size_t bytes) {
   if (bytes <= g->stage_cap) return PL_OK;
   size_t cap = g->stage_cap ? g->stage_cap : (1u << 20);
@@ -242,8 +253,12 @@ int ensure_stage(size_t bytes) {
   g->d_stage = nullptr;
   g->h_stage = nullptr;
   g->stage_cap = 0;
+  g->h_stage_dev = nullptr;
   if (dev_alloc(&g->d_stage, cap) != cudaSuccess) return PL_ENOMEM;
   if (host_alloc(&g->h_stage, cap) != cudaSuccess) return PL_ENOMEM;
+  if (cudaHostGetDevicePointer(reinterpret_cast<void**>(&g->h_stage_dev), g->h_stage, 0) !=
+      cudaSuccess)
+    return PL_ECUDA;
   g->stage_cap = cap;
   return PL_OK;
 }
@@ -253,8 +268,12 @@ int ensure_stage(size_t bytes) {
 // range directly between it and the device (no copy through the staging
 // area).  model.c allocates s->q, s->k, s->v and s->xb once and reuses them
 // for every call, so it can register them at start-up.
+// A registered range is also mapped into the device's address space:
+// kernels of a host-buffer call may read an input that is used once, or
+// write the output, straight over the bus.
 struct HostRange {
   uintptr_t lo, hi;
+  uint8_t* dev;  // device address of lo
 };
 std::vector<HostRange> g_pinned;
 
@@ -263,6 +282,19 @@ bool pinned(const void* p, size_t bytes) {
   for (const HostRange& r : g_pinned)
     if (a >= r.lo && a + bytes <= r.hi) return true;
   return false;
+}
+
+static bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// Device address of [p, p + bytes) when it lies in a registered range and p
+// is 16-byte aligned (the kernels move 8- and 16-byte vectors), else
+// nullptr.
+uint8_t* mapped(const void* p, size_t bytes) {
+  const uintptr_t a = reinterpret_cast<uintptr_t>(p);
+  if (!aligned16(p)) return nullptr;
+  for (const HostRange& r : g_pinned)
+    if (a >= r.lo && a + bytes <= r.hi) return r.dev + (a - r.lo);
+  return nullptr;
 }
 
 // ---- parallel copies between caller buffers and the pinned staging area ---
@@ -551,12 +583,15 @@ int launch_decode_tp(const pl::DecodeArgs& a, int grid, cudaStream_t st, bool pr
 // grid is resident from the start, and the next decode grid, which launches
 // once every merge block has started, can take each SM as soon as its
 // decode CTA ends (config 4: 30.2 -> 29.0 us per step).
-int launch_merge(const pl::DecodeArgs& a, int decode_grid_ctas, cudaStream_t st, bool profile) {
-  if (decode_grid_ctas <= 1) return PL_OK;  // one CTA: every sequence is one segment
+int launch_merge(const pl::DecodeArgs& a, int decode_grid_ctas, cudaStream_t st, bool profile,
+                 const pl::XferPush* push = nullptr) {
+  // one CTA: every sequence is one segment (a pushing merge still exchanges)
+  if (decode_grid_ctas <= 1 && !push) return PL_OK;
   int hpb = pl::kMergeThreads / (g->head_dim / 4);  // 16 at head_dim 64, 8 at 128
   while (hpb > 1 &&
          static_cast<long long>(a.n) * ((g->n_heads + hpb / 2 - 1) / (hpb / 2)) <= g->num_sms)
     hpb >>= 1;
+  if (push) hpb = 1;  // a pushing merge exchanges one head per block
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(a.n, (g->n_heads + hpb - 1) / hpb);
   cfg.blockDim = dim3(pl::kMergeThreads);
@@ -567,10 +602,14 @@ int launch_merge(const pl::DecodeArgs& a, int decode_grid_ctas, cudaStream_t st,
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
+  const pl::XferPush none = {};
+  const pl::XferPush& x = push ? *push : none;
   if (g->head_dim == 128)
-    PL_CUDA(cudaLaunchKernelEx(&cfg, pl::merge_kernel<128>, a, hpb, decode_grid_ctas, g->tp));
+    PL_CUDA(cudaLaunchKernelEx(&cfg, push ? pl::merge_kernel<128, true> : pl::merge_kernel<128, false>,
+                               a, hpb, decode_grid_ctas, g->tp, x));
   else
-    PL_CUDA(cudaLaunchKernelEx(&cfg, pl::merge_kernel<64>, a, hpb, decode_grid_ctas, g->tp));
+    PL_CUDA(cudaLaunchKernelEx(&cfg, push ? pl::merge_kernel<64, true> : pl::merge_kernel<64, false>,
+                               a, hpb, decode_grid_ctas, g->tp, x));
   if (profile) count_launch();
   return PL_OK;
 }
@@ -615,11 +654,12 @@ struct DecodeOccupancy {
   cudaError_t unsupported() const { return cudaErrorInvalidValue; }
 };
 
-int launch_decode_kernel(const pl::DecodeArgs& a, int grid, cudaStream_t st, bool profile) {
+int launch_decode_kernel(const pl::DecodeArgs& a, int grid, cudaStream_t st, bool profile,
+                         const pl::XferPush* push = nullptr) {
   const int rc =
       with_decode_config(g->tp, g->nstage, g->head_dim, DecodeLaunch{a, grid, st, profile});
   if (rc) return rc;
-  return launch_merge(a, grid, st, profile);
+  return launch_merge(a, grid, st, profile, push);
 }
 
 // Launch the fused decode for n sequences (chunks of kMaxLaunchSeqs).  All
@@ -996,35 +1036,51 @@ int pl_attn_decode_batch(int layer, int n, const int* seqs, const int* pos, cons
   if (rc) return rc;
   uint8_t* h = g->h_stage;
   uint8_t* d = g->d_stage;
+  // k and v are read once, by the segment that appends: from registered
+  // buffers the kernel reads them over the bus.  q is read by every segment
+  // of its sequence, so it goes to the device once: straight from a
+  // registered q when it is large, else through the staging area with the
+  // slots and positions (one copy).
+  const uint8_t* mk = mapped(k, kb);
+  const uint8_t* mv = mapped(v, kb);
+  const bool kv_mapped = mk && mv;
+  const bool q_direct = qb > kStagedQBytes && pinned(q, qb);
+  CopyPiece in[3];
+  int n_in = 0;
+  if (!q_direct) in[n_in++] = {h, reinterpret_cast<const uint8_t*>(q), qb};
+  if (!kv_mapped) {
+    in[n_in++] = {h + qb, reinterpret_cast<const uint8_t*>(k), kb};
+    in[n_in++] = {h + qb + kb, reinterpret_cast<const uint8_t*>(v), kb};
+  }
+  if (n_in) host_copy(in, n_in);
   std::memcpy(h + qb + 2 * kb, seqs, ib);
   std::memcpy(h + qb + 2 * kb + ib, pos, ib);
-  if (pinned(q, qb) && pinned(k, kb) && pinned(v, kb)) {
-    // registered inputs go straight to the device; seqs and pos are staged
+  if (q_direct) {
+    // q from the caller; then the staged rest: k and v (unless mapped),
+    // slots and positions
+    const size_t rest = kv_mapped ? qb + 2 * kb : qb;
     PL_CUDA(cudaMemcpyAsync(d, q, qb, cudaMemcpyHostToDevice, g->stream));
-    PL_CUDA(cudaMemcpyAsync(d + qb, k, kb, cudaMemcpyHostToDevice, g->stream));
-    PL_CUDA(cudaMemcpyAsync(d + qb + kb, v, kb, cudaMemcpyHostToDevice, g->stream));
-    PL_CUDA(cudaMemcpyAsync(d + qb + 2 * kb, h + qb + 2 * kb, 2 * ib, cudaMemcpyHostToDevice,
+    PL_CUDA(cudaMemcpyAsync(d + rest, h + rest, in_bytes - rest, cudaMemcpyHostToDevice,
                             g->stream));
   } else {
-    const CopyPiece in[3] = {{h, reinterpret_cast<const uint8_t*>(q), qb},
-                             {h + qb, reinterpret_cast<const uint8_t*>(k), kb},
-                             {h + qb + kb, reinterpret_cast<const uint8_t*>(v), kb}};
-    host_copy(in, 3);
     PL_CUDA(cudaMemcpyAsync(d, h, in_bytes, cudaMemcpyHostToDevice, g->stream));
   }
-  // the call's last kernel stores the device error word in mapped pinned
-  // memory, so no copy brings it back
+  // the kernels write the output straight into host memory (mapped): the
+  // caller's registered out, else the staging area; and the call's last
+  // kernel stores the device error word in mapped pinned memory.  No copy
+  // comes back.
   *reinterpret_cast<volatile uint32_t*>(g->h_err) = 0;
-  float* d_out = reinterpret_cast<float*>(d + out_off);
+  uint8_t* mo = mapped(out, qb);
+  float* d_out = reinterpret_cast<float*>(mo ? mo : g->h_stage_dev + out_off);
   rc = launch_decode(layer, n, reinterpret_cast<int*>(d + qb + 2 * kb),
                      reinterpret_cast<int*>(d + qb + 2 * kb + ib), max_pos + 1,
-                     reinterpret_cast<float*>(d), reinterpret_cast<float*>(d + qb),
-                     reinterpret_cast<float*>(d + qb + kb), d_out, 0, 0, 0, 1, nullptr,
-                     g->stream, g->h_err_dev);
+                     reinterpret_cast<float*>(d),
+                     kv_mapped ? reinterpret_cast<const float*>(mk)
+                               : reinterpret_cast<const float*>(d + qb),
+                     kv_mapped ? reinterpret_cast<const float*>(mv)
+                               : reinterpret_cast<const float*>(d + qb + kb),
+                     d_out, 0, 0, 0, 1, nullptr, g->stream, g->h_err_dev);
   if (rc) return rc;
-  const bool direct_out = pinned(out, qb);
-  PL_CUDA(cudaMemcpyAsync(direct_out ? static_cast<void*>(out) : static_cast<void*>(h + out_off),
-                          d_out, qb, cudaMemcpyDeviceToHost, g->stream));
   PL_CUDA(cudaStreamSynchronize(g->stream));
   const uint32_t w = *reinterpret_cast<volatile uint32_t*>(g->h_err);
   if (w) {
@@ -1032,7 +1088,7 @@ int pl_attn_decode_batch(int layer, int n, const int* seqs, const int* pos, cons
     cudaStreamSynchronize(g->stream);
     return check_err_word(w);
   }
-  if (!direct_out) {
+  if (!mo) {
     const CopyPiece o = {reinterpret_cast<uint8_t*>(out), h + out_off, qb};
     host_copy(&o, 1);
   }
@@ -1051,14 +1107,20 @@ int pl_attn_host_register(void* ptr, size_t bytes) {
   for (const HostRange& r : g_pinned)
     if (a < r.hi && a + bytes > r.lo) return PL_EARG;  // overlaps a registered range
   if (cudaSetDevice(g->device) != cudaSuccess) return PL_ECUDA;
-  // portable: pinned for every device of a multi-device context
-  const cudaError_t e = cudaHostRegister(ptr, bytes, cudaHostRegisterPortable);
+  // portable: pinned for every device of a multi-device context; mapped:
+  // addressable by the kernels of a host-buffer call
+  cudaError_t e = cudaHostRegister(ptr, bytes, cudaHostRegisterPortable | cudaHostRegisterMapped);
+  void* dev = nullptr;
+  if (e == cudaSuccess) {
+    e = cudaHostGetDevicePointer(&dev, ptr, 0);
+    if (e != cudaSuccess) cudaHostUnregister(ptr);
+  }
   if (e != cudaSuccess) {
     cudaGetLastError();  // the call stays usable through the staging area
     std::fprintf(stderr, "pl_attn_host_register: %s\n", cudaGetErrorString(e));
     return PL_ECUDA;
   }
-  g_pinned.push_back({a, a + bytes});
+  g_pinned.push_back({a, a + bytes, static_cast<uint8_t*>(dev)});
   return PL_OK;
 }
 
@@ -1141,18 +1203,25 @@ int pl_attn_xfer_setup(int world, int rank, void* handle_out) {
   if (world < 1 || world > pl::kXferMaxRanks || rank < 0 || rank >= world || !handle_out)
     return PL_EARG;
   if (cudaSetDevice(g->device) != cudaSuccess) return PL_ECUDA;
-  const size_t bytes = pl::kXferStampBytes +
-                       2 * static_cast<size_t>(world) * g->part_floats * sizeof(float);
+  const size_t bytes = pl::xfer_buffer_bytes(world, g->n_heads, g->head_dim);
   Xfer* x = new Xfer;
   x->world = world;
   x->rank = rank;
-  if (dev_alloc(&x->local, bytes) != cudaSuccess) {
+  if (dev_alloc(&x->local, bytes) != cudaSuccess ||
+      dev_alloc(&x->d_arrive, sizeof(uint32_t)) != cudaSuccess ||
+      dev_alloc(&x->d_part1, g->part_floats * sizeof(float)) != cudaSuccess) {
+    cudaFree(x->local);
+    cudaFree(x->d_arrive);
+    cudaFree(x->d_part1);
     delete x;
     return PL_ENOMEM;
   }
-  if (cudaMemset(x->local, 0, bytes) != cudaSuccess ||
+  if (cudaMemset(x->d_arrive, 0, sizeof(uint32_t)) != cudaSuccess ||
+      cudaMemset(x->local, 0, bytes) != cudaSuccess ||
       cudaIpcGetMemHandle(static_cast<cudaIpcMemHandle_t*>(handle_out), x->local) != cudaSuccess) {
     cudaFree(x->local);
+    cudaFree(x->d_arrive);
+    cudaFree(x->d_part1);
     delete x;
     return PL_ECUDA;
   }
@@ -1185,12 +1254,11 @@ int pl_attn_combine_p2p_dev(const float* d_part, float* d_out, void* stream) {
   for (int r = 0; r < g_xfer->world; ++r)
     if (!g_xfer->peers.base[r]) return PL_ESTATE;  // not connected yet
   cudaStream_t st = pick_stream(stream);
-  const size_t smem = static_cast<size_t>(3 * pl::kXferMaxRanks + 2) * g->n_heads * sizeof(float);
   // queued behind the partial's kernels (programmatic dependent launch)
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(1);
   cfg.blockDim = dim3(pl::kXferThreads);
-  cfg.dynamicSmemBytes = smem;
+  cfg.dynamicSmemBytes = 0;
   cfg.stream = st;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
@@ -1205,6 +1273,35 @@ int pl_attn_combine_p2p_dev(const float* d_part, float* d_out, void* stream) {
                                g_xfer->world, g_xfer->rank, g->n_heads, d_out, g->d_err));
   count_launch();
   return PL_OK;
+}
+
+int pl_attn_decode_p2p_dev(int seq, int layer, int pos, int row0, int n_rows, int append,
+                           const float* d_q, const float* d_k, const float* d_v, float* d_out,
+                           void* stream) {
+  int rc = check_seq_layer(seq, layer);
+  if (rc) return rc;
+  if (g_multi) return PL_EUNSUPPORTED;
+  if (!g_xfer) return PL_ESTATE;
+  for (int r = 0; r < g_xfer->world; ++r)
+    if (!g_xfer->peers.base[r]) return PL_ESTATE;  // not connected yet
+  if (pos < 0 || row0 < 0 || n_rows < 0 || n_rows > g->max_seq || !d_q || !d_out) return PL_EARG;
+  if (append && (pos - row0 < 0 || pos - row0 >= n_rows || !d_k || !d_v)) return PL_EARG;
+  if (pos >= g->rope_rows) return PL_EARG;
+  cudaStream_t st = pick_stream(stream);
+  const pl::XferPush push = {g_xfer->peers, g_xfer->world, g_xfer->rank, g_xfer->d_arrive, d_out};
+  const int grid = n_rows ? decode_grid(1, n_rows) : 0;
+  if (grid) {
+    rc = ensure_part(static_cast<size_t>(grid + 1) * g->part_floats);
+    if (rc) return rc;
+  }
+  pl::DecodeArgs a = decode_args(layer, 1, nullptr, nullptr, d_q, d_k ? d_k : d_q,
+                                 d_v ? d_v : d_q, nullptr, 1, row0, n_rows, append ? 1 : 0,
+                                 g_xfer->d_part1, g->d_part, g->d_seg_info);
+  a.seq1 = seq;
+  a.pos1 = pos;
+  // an empty shard runs only the merge grid, which pushes an empty partial
+  if (!grid) return launch_merge(a, 0, st, true, &push);
+  return launch_decode_kernel(a, grid, st, true, &push);
 }
 
 int pl_attn_rope(int pos0, int n_tok, float* q, float* k) {
@@ -1279,7 +1376,6 @@ int pl_attn_kv_ptr(int seq, int layer, uint16_t** d_k, uint16_t** d_v) {
 }
 
 // ---------------------------------------------------------------- prefill
-static bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
 // Prologue + tensor-core attention over the rows of one cache slab: kc_slab /
 // vc_slab are its row 0 (the prologue appends at row start_pos), tmk / tmv
@@ -2294,20 +2390,26 @@ int multi_init(int n_layers, int n_heads, int n_kv_heads, int head_dim, int max_
   return PL_OK;
 }
 
-// Wait for every device's stream; read and clear every error word.
+// Wait for every device's stream; read and clear every error word.  The
+// word's read-back is queued on each stream (into the device's pinned word)
+// before the first host wait, so the waits overlap.
 int multi_finish() {
   int rc = PL_OK;
-  for (Ctx* c : g_multi->devs) {
+  std::vector<char> queued(g_multi->devs.size(), 0);
+  for (size_t d = 0; d < g_multi->devs.size(); ++d) {
+    Ctx* c = g_multi->devs[d];
     UseCtx u(c);
-    if (cudaStreamSynchronize(c->stream) != cudaSuccess) {
+    queued[d] = cudaMemcpyAsync(c->h_err, c->d_err, sizeof(uint32_t), cudaMemcpyDeviceToHost,
+                                c->stream) == cudaSuccess;
+  }
+  for (size_t d = 0; d < g_multi->devs.size(); ++d) {
+    Ctx* c = g_multi->devs[d];
+    UseCtx u(c);
+    if (!queued[d] || cudaStreamSynchronize(c->stream) != cudaSuccess) {
       rc = PL_ECUDA;
       continue;
     }
-    uint32_t w = 0;
-    if (cudaMemcpy(&w, c->d_err, sizeof(w), cudaMemcpyDeviceToHost) != cudaSuccess) {
-      rc = PL_ECUDA;
-      continue;
-    }
+    const uint32_t w = *reinterpret_cast<volatile uint32_t*>(c->h_err);
     if (w) cudaMemset(c->d_err, 0, sizeof(uint32_t));
     const int r = check_err_word(w);
     if (r && !rc) rc = r;

@@ -131,29 +131,42 @@ class P2PShardOps(AttnShardOps):
 
     At construction every rank allocates its receive buffer, the IPC handles
     are exchanged once over `group` (any backend; they are 64-byte objects),
-    and each rank maps the others.  Per merge, pl_attn_combine_p2p_dev stores
-    this rank's partial into every rank's buffer, stamps it and, once every
-    rank's stamp has arrived, merges locally: one kernel instead of an
-    all-gather plus a merge, so `gather` has nothing left to do.  The merges
-    are numbered on the device, so the calls can be captured in a CUDA
-    graph and replayed."""
+    and each rank maps the others.  With `fused` (the default) one call per
+    layer, pl_attn_decode_p2p_dev, computes this rank's partial and the grid
+    that merges its segments stores it into every rank's buffer; the grid's
+    last block stamps it and, once every rank's stamp has arrived, merges
+    locally.  Without `fused`, pl_attn_decode_partial_dev writes the partial
+    and pl_attn_combine_p2p_dev (one kernel) pushes, stamps, waits and
+    merges.  Either way `gather` has nothing left to do, and the merges are
+    numbered on the device, so the calls can be captured in a CUDA graph and
+    replayed."""
 
     def __init__(self, attn, stream_handle: int, rank: int, world: int, group=None,
-                 seq: int = 0):
+                 seq: int = 0, fused: bool = True):
         super().__init__(attn, stream_handle, group, seq)
         import torch.distributed as dist
         handle = attn.xfer_setup(world, rank)
         handles = [None] * world
         dist.all_gather_object(handles, handle, group=group)
         attn.xfer_connect(handles)
+        self.fused = fused
         self._part = None
+        self._args = None
 
     def partial(self, layer, pos, row0, n_rows, append, q, k, v, part):
         self._part = part
-        super().partial(layer, pos, row0, n_rows, append, q, k, v, part)
+        if self.fused:
+            self._args = (layer, pos, row0, n_rows, append, q, k, v)
+        else:
+            super().partial(layer, pos, row0, n_rows, append, q, k, v, part)
 
     def gather(self, part, parts_all):
         pass
 
     def combine(self, world, parts_all, out):
-        self.attn.combine_p2p_dev(self._part.data_ptr(), out.data_ptr(), self.stream)
+        if self.fused:
+            layer, pos, row0, n_rows, append, q, k, v = self._args
+            self.attn.decode_p2p_dev(self.seq, layer, pos, row0, n_rows, append, q.data_ptr(),
+                                     k.data_ptr(), v.data_ptr(), out.data_ptr(), self.stream)
+        else:
+            self.attn.combine_p2p_dev(self._part.data_ptr(), out.data_ptr(), self.stream)

@@ -2,7 +2,8 @@
 
 * A KV-split merge whose peer never arrives: two processes on one GPU map
   each other's receive buffers (pl_attn_xfer_setup / _connect); rank 1 stays
-  alive but never calls pl_attn_combine_p2p_dev.  Rank 0's merge kernel
+  alive but never calls pl_attn_combine_p2p_dev (or pl_attn_decode_p2p_dev,
+  where the last block of the merge grid waits).  Rank 0's merge kernel
   stores its partial, stamps its epoch and waits, bounded by the limit set
   with pl_attn_set_wait_limit (50 ms here), for rank 1's stamp, which never
   comes.  pl_attn_status must report PL_ETIMEOUT, and the module must stay
@@ -48,7 +49,8 @@ def _silent_rank(conn):
     conn.send("closed")
 
 
-def test_p2p_merge_times_out_when_a_rank_never_arrives():
+@pytest.mark.parametrize("fused", [False, True], ids=["combine_p2p", "decode_p2p"])
+def test_p2p_merge_times_out_when_a_rank_never_arrives(fused):
     import torch
     ctx = mp.get_context("spawn")
     parent, child = ctx.Pipe()
@@ -67,7 +69,13 @@ def test_p2p_merge_times_out_when_a_rank_never_arrives():
             part = torch.zeros(8 * at.part_stride, device="cuda")
             out = torch.zeros(8 * 64, device="cuda")
             st = torch.cuda.current_stream().cuda_stream
-            at.combine_p2p_dev(part.data_ptr(), out.data_ptr(), st)
+            if fused:
+                # partial over 11 (zero) cache rows, pushed, then the wait
+                qd = torch.randn(8 * 64, device="cuda")
+                at.decode_p2p_dev(0, 0, 10, 0, 11, 0, qd.data_ptr(), qd.data_ptr(),
+                                  qd.data_ptr(), out.data_ptr(), st)
+            else:
+                at.combine_p2p_dev(part.data_ptr(), out.data_ptr(), st)
             assert at.status(st) == pb.PL_ETIMEOUT
             assert at.status(st) == pb.PL_OK  # the word was cleared
             at.set_wait_limit(2.0)

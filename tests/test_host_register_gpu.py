@@ -1,6 +1,7 @@
 """pl_attn_host_register: host-buffer calls whose inputs and outputs lie in
-registered (page-locked) caller memory move them directly between the caller
-and the device.  Results must equal the staged path bit for bit; the error
+registered (page-locked, mapped) caller memory move them directly between
+the caller and the device: q by one copy, k, v and the output by the
+kernels over the bus.  Results must equal the staged path bit for bit; the error
 cases return status codes and leave the module usable."""
 import numpy as np
 import pytest
@@ -31,21 +32,32 @@ def test_decode_batch_registered_equals_staged():
     q, k, v = _inputs(rng, n, H * 64, Hk * 64)
     caches = [(random_cache(rng, ms, Hk * 64), random_cache(rng, ms, Hk * 64)) for _ in range(n)]
     results = []
-    for mode in ("staged", "registered", "out only"):
+    # registered buffers: q is copied to the device, k and v are read and
+    # the output written by the kernels over the bus (mapped).  A registered
+    # range whose start is not 16-byte aligned, or a k without its v, takes
+    # the staged route for that buffer; a q copied straight from the caller
+    # with k and v staged ("q only", "misaligned") needs both copies.
+    for mode in ("staged", "registered", "out only", "misaligned", "k only", "q only"):
         with pb.Attn(1, H, Hk, ms, n_seqs=n) as at:
             for s, (kc, vc) in enumerate(caches):
                 at.kv_upload(s, 0, 0, kc, vc)
             qq, kk, vv = q.copy(), k.copy(), v.copy()
-            out = np.zeros(n * H * 64, np.float32)
-            if mode == "registered":
-                for a in (qq, kk, vv):
-                    at.host_register(a)
-            if mode != "staged":
-                at.host_register(out)
+            out_buf = np.zeros(n * H * 64 + 4, np.float32)
+            out = out_buf[1:1 + n * H * 64] if mode == "misaligned" else out_buf[:n * H * 64]
+            regs = {"registered": (qq, kk, vv, out_buf), "out only": (out_buf,),
+                    "misaligned": (qq, kk, vv, out_buf), "k only": (kk, out_buf),
+                    "q only": (qq,)}.get(mode, ())
+            if mode == "misaligned":
+                vv_buf = np.zeros(vv.size + 4, np.float32)
+                vv_buf[1:1 + vv.size] = vv.ravel()
+                vv = vv_buf[1:1 + vv.size]
+                regs = regs + (vv_buf,)
+            for a in regs:
+                at.host_register(a)
             at.decode_batch(0, seqs, pos, qq, kk, vv, out=out)
             gk, gv = at.kv_download(3, 0, 0, ms)
-            if mode != "staged":
-                at.host_unregister(out)
+            for a in regs:
+                at.host_unregister(a)
             results.append((out.copy(), gk, gv))
     for got in results[1:]:
         np.testing.assert_array_equal(got[0].view(np.uint32), results[0][0].view(np.uint32))

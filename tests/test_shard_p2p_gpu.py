@@ -2,7 +2,9 @@
 
 Two processes, one per GPU, each hold half of a sequence's cache; per
 step each computes its partial and pl_attn_combine_p2p_dev pushes it to
-the other GPU and merges.  Both ranks' outputs must equal picolm's
+the other GPU and merges (or, fused, pl_attn_decode_p2p_dev does both, the
+merge grid pushing the partial itself).  With no cached rows, rank 0's
+shard is empty and only takes part in the exchange.  Both ranks' outputs must equal picolm's
 unsplit decode chain (the oracle) within the attention tolerance.  Needs
 two GPUs (one process per GPU: the merge waits on the other rank).
 """
@@ -19,10 +21,10 @@ pytestmark = pytest.mark.gpu
 
 H, HK, HD = 32, 8, 64
 KV_DIM = HK * HD
-N_CACHED, N_NEW, WORLD = 3000, 5, 2
+N_NEW, WORLD = 5, 2
 
 
-def inputs():
+def inputs(N_CACHED):
     rng = np.random.default_rng(31)
     kc = random_cache(rng, N_CACHED, KV_DIM)
     vc = random_cache(rng, N_CACHED, KV_DIM)
@@ -32,7 +34,7 @@ def inputs():
     return kc, vc, steps
 
 
-def _rank_main(rank, world, port, out_dir):
+def _rank_main(rank, world, port, out_dir, N_CACHED, fused):
     import torch
     import torch.distributed as dist
     import picolm_b200 as pb
@@ -42,14 +44,15 @@ def _rank_main(rank, world, port, out_dir):
     torch.cuda.set_device(rank)
     dist.init_process_group("gloo", rank=rank, world_size=world)
     try:
-        kc, vc, steps = inputs()
+        kc, vc, steps = inputs(N_CACHED)
         dev = torch.device("cuda", rank)
         with pb.Attn(1, H, HK, N_CACHED + N_NEW, rope_base=500000.0, device=rank) as at:
             st = torch.cuda.current_stream(dev).cuda_stream
             dec = KVSplitDecoder(rank=rank, world=world, n_cached=N_CACHED, ops=None)
-            at.kv_upload(0, 0, 0, np.ascontiguousarray(kc[dec.row0:dec.row0 + dec.n_rows]),
-                         np.ascontiguousarray(vc[dec.row0:dec.row0 + dec.n_rows]))
-            dec.ops = P2PShardOps(at, st, rank, world)
+            if dec.n_rows:
+                at.kv_upload(0, 0, 0, np.ascontiguousarray(kc[dec.row0:dec.row0 + dec.n_rows]),
+                             np.ascontiguousarray(vc[dec.row0:dec.row0 + dec.n_rows]))
+            dec.ops = P2PShardOps(at, st, rank, world, fused=fused)
             part = torch.empty(H * PART_STRIDE, device=dev)
             out = torch.empty(H * HD, device=dev)
             outs = []
@@ -70,13 +73,16 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def test_two_gpu_p2p_split_matches_unsplit_decode(tmp_path):
+@pytest.mark.parametrize("N_CACHED", [3000, 0])
+@pytest.mark.parametrize("fused", [True, False], ids=["decode_p2p", "combine_p2p"])
+def test_two_gpu_p2p_split_matches_unsplit_decode(tmp_path, N_CACHED, fused):
     import torch
     import torch.multiprocessing as mp
     if torch.cuda.device_count() < WORLD:
         pytest.skip(f"needs {WORLD} GPUs (one process per GPU)")
-    mp.spawn(_rank_main, args=(WORLD, _free_port(), str(tmp_path)), nprocs=WORLD, join=True)
-    kc, vc, steps = inputs()
+    mp.spawn(_rank_main, args=(WORLD, _free_port(), str(tmp_path), N_CACHED, fused),
+             nprocs=WORLD, join=True)
+    kc, vc, steps = inputs(N_CACHED)
     ms = N_CACHED + N_NEW
     fk = np.zeros((ms, KV_DIM), np.uint16)
     fv = np.zeros((ms, KV_DIM), np.uint16)
