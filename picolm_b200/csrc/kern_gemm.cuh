@@ -50,7 +50,11 @@ constexpr int kGmThreads = 128;
 constexpr int kGmTile = kGmBM * kGmBK * 2;  // bytes of one operand tile (16 KB)
 constexpr float kGmLoScale = 2048.0f;       // 2^11
 constexpr float kGmLoInv = 1.0f / 2048.0f;
-constexpr int kGmMinRows = 128;             // the GEMM path from this many input rows
+// The GEMM paths from this many input rows (the skinny kernel up to
+// kSkMaxRows, gemm_hilo_kernel above).  Fewer rows stream the quantised
+// weights on CUDA cores / mma.sync (kern_proj.cuh): one row took 19.6 us
+// there against 31.7 us on the skinny GEMM, 64 rows 64.5 against 37.8 us.
+constexpr int kGmMinRows = 24;
 
 // Output columns [col0, col0 + cols) of the GEMM go to out[m * ld + n - col0]
 // with bias[n - col0] (nullptr: none).  Q, K and V are three segments of one
@@ -242,6 +246,240 @@ __global__ void __launch_bounds__(kGmThreads, 1)
   }
 }
 
+// ---- few input rows (batched decode): the weights as the A operand -------
+// With M <= kSkMaxRows input rows a 128-row tile of x would be mostly
+// padding.  Here the 128 weight rows of an output tile are the A operand
+// (M = 128 output columns on the TMEM lanes) and the input rows are B
+// (N = M rounded up to 16), so D = [output column][input row] and no lane
+// is wasted.  The producer, the ring and the three MMAs per k-slice are
+// those of gemm_hilo_kernel with A and B exchanged, with x in 64-row TMA
+// boxes (rows past M arrive as zeros, outside the tensor; only the first N
+// feed the MMA), so a stage is 48 KB and kSkStages of them fit.  The epilogue writes D transposed: thread
+// (warp w, lane l) holds output column n0 + 32w + l for every input row, so
+// for each row a warp stores 32 consecutive floats (128 contiguous bytes).
+//
+// N / 128 tiles alone leave most SMs idle (20 for the Q/K/V rows of a
+// 2048-wide layer), and one SM streams a tile's 1 MB of weight parts at
+// only about 45 GB/s, so K is split over the gridDim.y CTAs of a tile,
+// which form one thread-block cluster (rank = split).  Each CTA keeps its
+// FP32 partial tile [kSkMaxRows][128] in its own shared memory (the idle
+// operand ring); after a cluster barrier, CTA r sums rows [r M / S,
+// (r + 1) M / S) of the tile over all S partials through distributed shared
+// memory, in split order (the same order on every run, whichever CTA
+// finishes first), adds bias and residual and stores them; a second
+// cluster barrier keeps every CTA's shared memory alive until all reads are
+// done.  grid = (N / 128, S), cluster (1, S, 1) with S <= 8, block =
+// kGmThreads.
+constexpr int kSkMaxRows = 64;
+constexpr int kSkMaxSplit = 8;
+constexpr int kSkStages = 4;                  // ring depth: most of a CTA's k-steps in flight
+constexpr int kSkXTile = kSkMaxRows * kGmBK * 2;  // bytes of one 64-row x tile (8 KB)
+
+struct SkSmem {
+  uint8_t wh[kSkStages][kGmTile];
+  uint8_t wl[kSkStages][kGmTile];
+  uint8_t xh[kSkStages][kSkXTile];
+  uint8_t xl[kSkStages][kSkXTile];
+  uint64_t full[kSkStages], empty[kSkStages];
+  uint64_t done;
+  uint32_t tmem_base;
+};
+
+constexpr int sk_smem_bytes() { return static_cast<int>(sizeof(SkSmem)) + 1024; }
+static_assert(sk_smem_bytes() <= 227 * 1024, "skinny GEMM shared memory above the limit");
+static_assert(2 * kGmTile >= kSkMaxRows * kGmBM * 4, "partial tile must fit two weight tiles");
+
+__global__ void __launch_bounds__(kGmThreads, 1)
+    gemm_skinny_kernel(const GemmArgs a, const __grid_constant__ CUtensorMap tm_xh,
+                       const __grid_constant__ CUtensorMap tm_xl,
+                       const __grid_constant__ CUtensorMap tm_wh,
+                       const __grid_constant__ CUtensorMap tm_wl) {
+  extern __shared__ uint8_t smem_raw[];
+  SkSmem& sm = *reinterpret_cast<SkSmem*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int n0 = blockIdx.x * kGmBM;
+  const int n_split = gridDim.y, split = blockIdx.y;
+  const int kb_all = a.K / kGmBK;
+  const int kb_lo = split * kb_all / n_split, kb_hi = (split + 1) * kb_all / n_split;
+  const int kb_n = kb_hi - kb_lo;  // k-steps of this CTA (at least one)
+  const int nx = (a.M + 15) & ~15;  // MMA N: the input rows, rounded up to 16
+
+  if (threadIdx.x == 0) {
+    tma_prefetch_desc(&tm_xh);
+    tma_prefetch_desc(&tm_xl);
+    tma_prefetch_desc(&tm_wh);
+    tma_prefetch_desc(&tm_wl);
+    for (int s = 0; s < kSkStages; ++s) {
+      mbar_init(&sm.full[s], 1);
+      mbar_init(&sm.empty[s], 1);
+    }
+    mbar_init(&sm.done, 1);
+    fence_mbar_init();
+  }
+  if (warp == 2) {
+    tmem_alloc(&sm.tmem_base, 128);  // acc0 at columns [0, 64), acc1 at [64, 128)
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = sm.tmem_base;
+  bool ok = true;
+
+  if (warp == 0 && lane == 0) {
+    // ------------------------------------------------------------ producer
+    // Launched behind act_split_kernel with programmatic dependent launch:
+    // the weight tiles of the first stages load before griddepcontrol.wait
+    // (they do not depend on that kernel), the activations after it.
+    const int pre = kb_n < kSkStages ? kb_n : kSkStages;
+    for (int kb = 0; kb < pre; ++kb) {
+      mbar_arrive_expect_tx(&sm.full[kb], 2u * kGmTile + 2u * kSkXTile);
+      const int k0 = (kb_lo + kb) * kGmBK;
+      tma_load_2d(sm.wh[kb], &tm_wh, &sm.full[kb], k0, a.w_row0 + n0);
+      tma_load_2d(sm.wl[kb], &tm_wl, &sm.full[kb], k0, a.w_row0 + n0);
+    }
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    for (int kb = 0; kb < pre; ++kb) {
+      const int k0 = (kb_lo + kb) * kGmBK;
+      tma_load_2d(sm.xh[kb], &tm_xh, &sm.full[kb], k0, 0);
+      tma_load_2d(sm.xl[kb], &tm_xl, &sm.full[kb], k0, 0);
+    }
+    int issued = pre;
+    for (int kb = pre; kb < kb_n; ++kb) {
+      const int s = kb % kSkStages;
+      if (!mbar_wait_bounded(&sm.empty[s], ((kb / kSkStages) - 1) & 1)) {
+        atomicOr(a.err, ERR_TIMEOUT_EMPTY);
+        break;
+      }
+      mbar_arrive_expect_tx(&sm.full[s], 2u * kGmTile + 2u * kSkXTile);
+      const int k0 = (kb_lo + kb) * kGmBK;
+      tma_load_2d(sm.wh[s], &tm_wh, &sm.full[s], k0, a.w_row0 + n0);
+      tma_load_2d(sm.wl[s], &tm_wl, &sm.full[s], k0, a.w_row0 + n0);
+      tma_load_2d(sm.xh[s], &tm_xh, &sm.full[s], k0, 0);
+      tma_load_2d(sm.xl[s], &tm_xl, &sm.full[s], k0, 0);
+      ++issued;
+    }
+    for (int j = issued - kSkStages; j < issued; ++j)
+      if (j >= 0) mbar_wait_bounded(&sm.full[j % kSkStages], (j / kSkStages) & 1);
+  } else if (warp == 1 && lane == 0) {
+    // ------------------------------------------------------------ MMA issuer
+    const uint32_t idesc = idesc_f16_f32(kGmBM, nx, 0);
+    const uint32_t acc0 = tmem, acc1 = tmem + kSkMaxRows;
+    for (int kb = 0; kb < kb_n; ++kb) {
+      const int s = kb % kSkStages;
+      if (!mbar_wait_bounded(&sm.full[s], (kb / kSkStages) & 1)) {
+        atomicOr(a.err, ERR_TIMEOUT_FULL);
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      const uint32_t xh = smem_u32(sm.xh[s]), xl = smem_u32(sm.xl[s]);
+      const uint32_t wh = smem_u32(sm.wh[s]), wl = smem_u32(sm.wl[s]);
+#pragma unroll
+      for (int kk = 0; kk < kGmBK / 16; ++kk) {
+        const uint32_t o = kk * 32;
+        const uint64_t dxh = smem_desc_sw128(xh + o, 16, 1024);
+        const uint64_t dxl = smem_desc_sw128(xl + o, 16, 1024);
+        const uint64_t dwh = smem_desc_sw128(wh + o, 16, 1024);
+        const uint64_t dwl = smem_desc_sw128(wl + o, 16, 1024);
+        const uint32_t accum = (kb > 0 || kk > 0) ? 1u : 0u;
+        tc_mma_ss(acc0, dwh, dxh, idesc, accum);
+        tc_mma_ss(acc1, dwh, dxl, idesc, accum);
+        tc_mma_ss(acc1, dwl, dxh, idesc, 1u);
+      }
+      tc_commit(&sm.empty[s]);
+    }
+    tc_commit(&sm.done);
+  }
+  __syncwarp();
+
+  // ---------------------------------------------------------------- epilogue
+  if (!mbar_wait_bounded(&sm.done, 0)) {
+    if (lane == 0) atomicOr(a.err, ERR_TIMEOUT_MMA);
+    ok = false;
+  }
+  tc_fence_after();
+  asm volatile("griddepcontrol.wait;" ::: "memory");  // before any global store
+  int si = 0;
+  for (int i = 1; i < a.n_seg; ++i)
+    if (n0 >= a.seg[i].col0) si = i;
+  const GemmSeg seg = a.seg[si];
+  const int col = n0 - seg.col0 + 32 * warp + lane;  // this thread's output column in seg
+  const float bias = seg.bias ? __ldg(seg.bias + col) : 0.f;
+  const uint32_t lane_base = tmem + (static_cast<uint32_t>(32 * warp) << 16);
+  const bool any_err = __any_sync(0xffffffffu, !ok);
+  if (n_split == 1) {
+#pragma unroll 1
+    for (int c = 0; c < nx; c += 32) {
+      uint32_t r0[32], r1[32];
+      tc_ld_32x32b_x32(lane_base + c, r0);
+      tc_ld_32x32b_x32(lane_base + kSkMaxRows + c, r1);
+      tc_wait_ld();
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        asm volatile("" : "+r"(r0[i]));
+        asm volatile("" : "+r"(r1[i]));
+      }
+      if (any_err) continue;
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        const int m = c + i;
+        if (m < a.M) {
+          float y = __uint_as_float(r0[i]) + __uint_as_float(r1[i]) * kGmLoInv;
+          if (seg.bias) y += bias;
+          if (a.resid) y = a.resid[static_cast<size_t>(m) * a.ld_res + col] + y;
+          seg.out[static_cast<size_t>(m) * seg.ld + col] = y;
+        }
+      }
+    }
+  } else {
+    // every role loop has ended (the producer waited for its last copies):
+    // the ring is idle, and its first two weight tiles take this CTA's
+    // partial tile
+    __syncthreads();
+    float* P = reinterpret_cast<float*>(sm.wh[0]);  // [kSkMaxRows][kGmBM], 32 KB
+    const int fr = 32 * warp + lane;
+#pragma unroll 1
+    for (int c = 0; c < nx; c += 32) {
+      uint32_t r0[32], r1[32];
+      tc_ld_32x32b_x32(lane_base + c, r0);
+      tc_ld_32x32b_x32(lane_base + kSkMaxRows + c, r1);
+      tc_wait_ld();
+#pragma unroll
+      for (int i = 0; i < 32; ++i)
+        if (c + i < nx)
+          P[(c + i) * kGmBM + fr] = __uint_as_float(r0[i]) + __uint_as_float(r1[i]) * kGmLoInv;
+    }
+    cluster_sync_all();
+    const int m_lo = split * a.M / n_split, m_hi = (split + 1) * a.M / n_split;
+    const uint32_t p_own = smem_u32(P) + 4u * fr;
+#pragma unroll 1
+    for (int m = m_lo; m < m_hi; ++m) {
+      const uint32_t pm = p_own + static_cast<uint32_t>(m) * kGmBM * 4u;
+      float v[kSkMaxSplit];
+#pragma unroll
+      for (int r = 0; r < kSkMaxSplit; ++r)
+        v[r] = r < n_split ? ld_cluster_f32(cluster_map(pm, r)) : 0.f;
+      float y = v[0];
+#pragma unroll
+      for (int r = 1; r < kSkMaxSplit; ++r)
+        if (r < n_split) y += v[r];
+      if (any_err) continue;
+      if (seg.bias) y += bias;
+      if (a.resid) y = a.resid[static_cast<size_t>(m) * a.ld_res + col] + y;
+      seg.out[static_cast<size_t>(m) * seg.ld + col] = y;
+    }
+    cluster_sync_all();  // the others' reads of this CTA's partial are done
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 2) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 128);
+  }
+}
+
 // ---- operand preparation ------------------------------------------------
 // FP16 high part of v and the FP16 rounding of the residual scaled by 2^11.
 __device__ __forceinline__ void split_hi_lo_scaled(float v, __half& hi, __half& lo) {
@@ -257,6 +495,9 @@ __global__ void __launch_bounds__(256)
                      const float* __restrict__ norm_w, float eps, __half* __restrict__ xh,
                      __half* __restrict__ xl) {
   __shared__ float s_red[8];
+  // a skinny GEMM queued behind this grid (programmatic dependent launch)
+  // may start its set-up and weight loads now
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   const int m = blockIdx.x, t = threadIdx.x;
   const float* row = x + static_cast<size_t>(m) * ldx;
   float r = 1.0f;

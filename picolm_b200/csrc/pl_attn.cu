@@ -123,6 +123,7 @@ struct Ctx {
   __half* d_xh = nullptr;            // GEMM activations: FP16 high parts, then
   __half* d_xl = nullptr;            // the 2^11-scaled residuals
   size_t act_cap = 0;                // elements of each
+  int sk_clusters[9] = {};           // skinny GEMM: resident clusters per cluster size (lazy)
   bool gemm_smem_set = false;
   bool proj_smem_set = false;
 };
@@ -471,8 +472,13 @@ int check_err_word(uint32_t w) {
 
 // Grid of the decode kernel: one CTA per resident slot, but never more CTAs
 // than tiles (max_rows bounds every sequence's rows).
+// A single sequence of at most this many tiles is decoded by one CTA: no
+// merge grid follows (one launch fewer), and each input is read once.
+constexpr int kOneCtaTiles = 8;
+
 int decode_grid(int n, int max_rows) {
   const long long tiles = static_cast<long long>(n) * ((max_rows + g->tp - 1) / g->tp);
+  if (n == 1 && tiles <= kOneCtaTiles) return 1;
   long long G = g->decode_slots;
   if (G > tiles) G = tiles;
   return G < 1 ? 1 : static_cast<int>(G);
@@ -1011,6 +1017,70 @@ static int read_back(const float* d_out, float* out, size_t qb, uint8_t* h) {
   return PL_OK;
 }
 
+// Host-buffer decode of one sequence.  The slot and position travel as
+// kernel arguments.  When one CTA covers the sequence every input is read
+// once, so the kernel reads q, k and v over the bus (from registered
+// buffers, else from the mapped staging area after a host memcpy) and the
+// call queues no copy at all; otherwise q, k and v go to the device in one
+// copy.  The output is written over the bus either way.
+static int decode_one_host(int layer, int seq, int pos, const float* q, const float* k,
+                           const float* v, float* out) {
+  const size_t qb = static_cast<size_t>(g->q_dim) * sizeof(float);
+  const size_t kb = static_cast<size_t>(g->kv_dim) * sizeof(float);
+  const size_t in_bytes = qb + 2 * kb;
+  const size_t out_off = (in_bytes + 255) & ~static_cast<size_t>(255);
+  int rc = ensure_stage(out_off + qb + 256);
+  if (rc) return rc;
+  uint8_t* h = g->h_stage;
+  uint8_t* hd = g->h_stage_dev;
+  uint8_t* d = g->d_stage;
+  const int grid = decode_grid(1, pos + 1);
+  const float* src[3] = {q, k, v};
+  const size_t off[3] = {0, qb, qb + kb};
+  const size_t bytes[3] = {qb, kb, kb};
+  const float* dptr[3];
+  CopyPiece pc[3];
+  int n_pc = 0;
+  for (int j = 0; j < 3; ++j) {
+    const uint8_t* m = grid == 1 ? mapped(src[j], bytes[j]) : nullptr;
+    if (m) {
+      dptr[j] = reinterpret_cast<const float*>(m);
+    } else {
+      pc[n_pc++] = {h + off[j], reinterpret_cast<const uint8_t*>(src[j]), bytes[j]};
+      dptr[j] = reinterpret_cast<const float*>((grid == 1 ? hd : d) + off[j]);
+    }
+  }
+  if (n_pc) host_copy(pc, n_pc);
+  if (grid != 1) PL_CUDA(cudaMemcpyAsync(d, h, in_bytes, cudaMemcpyHostToDevice, g->stream));
+  *reinterpret_cast<volatile uint32_t*>(g->h_err) = 0;
+  uint8_t* mo = mapped(out, qb);
+  float* d_out = reinterpret_cast<float*>(mo ? mo : hd + out_off);
+  pl::DecodeArgs a = decode_args(layer, 1, nullptr, nullptr, dptr[0], dptr[1], dptr[2], d_out, 0,
+                                 0, 0, 1, nullptr, g->d_part, g->d_seg_info);
+  a.seq1 = seq;
+  a.pos1 = pos;
+  a.err_host = g->h_err_dev;
+  if (grid > 1) {
+    rc = ensure_part(static_cast<size_t>(grid + 1) * g->part_floats);
+    if (rc) return rc;
+    a.part = g->d_part;
+  }
+  rc = launch_decode_kernel(a, grid, g->stream, true);
+  if (rc) return rc;
+  PL_CUDA(cudaStreamSynchronize(g->stream));
+  const uint32_t w = *reinterpret_cast<volatile uint32_t*>(g->h_err);
+  if (w) {
+    cudaMemsetAsync(g->d_err, 0, sizeof(uint32_t), g->stream);
+    cudaStreamSynchronize(g->stream);
+    return check_err_word(w);
+  }
+  if (!mo) {
+    const CopyPiece o = {reinterpret_cast<uint8_t*>(out), h + out_off, qb};
+    host_copy(&o, 1);
+  }
+  return PL_OK;
+}
+
 int pl_attn_decode_batch(int layer, int n, const int* seqs, const int* pos, const float* q,
                          const float* k, const float* v, float* out) {
   if (!g) return PL_ESTATE;
@@ -1026,6 +1096,7 @@ int pl_attn_decode_batch(int layer, int n, const int* seqs, const int* pos, cons
     if (pos[i] > max_pos) max_pos = pos[i];
   }
   if (cudaSetDevice(g->device) != cudaSuccess) return PL_ECUDA;
+  if (n == 1) return decode_one_host(layer, seqs[0], pos[0], q, k, v, out);
   const size_t qb = static_cast<size_t>(n) * g->q_dim * sizeof(float);
   const size_t kb = static_cast<size_t>(n) * g->kv_dim * sizeof(float);
   const size_t ib = static_cast<size_t>(n) * sizeof(int);
@@ -1822,10 +1893,10 @@ pl::ProjMat proj_mat(const LayerW& L, int which, float* out, int ld_out) {
 // ---- tensor-core GEMM of many input rows (kern_gemm.cuh) -------------------
 // A row-major FP16 matrix [rows][k] as a 2-D TMA map, box 64 x 128 under the
 // 128-byte swizzle.
-int make_map_2d(CUtensorMap* m, const __half* base, int k, int rows) {
+int make_map_2d(CUtensorMap* m, const __half* base, int k, int rows, int box_rows = pl::kGmBM) {
   const cuuint64_t dims[2] = {static_cast<cuuint64_t>(k), static_cast<cuuint64_t>(rows)};
   const cuuint64_t strides[1] = {static_cast<cuuint64_t>(k) * 2};
-  const cuuint32_t box[2] = {static_cast<cuuint32_t>(pl::kGmBK), static_cast<cuuint32_t>(pl::kGmBM)};
+  const cuuint32_t box[2] = {static_cast<cuuint32_t>(pl::kGmBK), static_cast<cuuint32_t>(box_rows)};
   const cuuint32_t estr[2] = {1, 1};
   if (g->encode(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<__half*>(base), dims, strides,
                 box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
@@ -1912,11 +1983,15 @@ int launch_gemm(const LayerW& L, bool qkv, const float* d_x, int ldx, int M, int
   PL_CUDA(cudaGetLastError());
   count_launch();
   CUtensorMap tm_xh, tm_xl;
-  if ((rc = make_map_2d(&tm_xh, g->d_xh, K, M)) || (rc = make_map_2d(&tm_xl, g->d_xl, K, M)))
+  const int box_rows = M <= pl::kSkMaxRows ? pl::kSkMaxRows : pl::kGmBM;
+  if ((rc = make_map_2d(&tm_xh, g->d_xh, K, M, box_rows)) ||
+      (rc = make_map_2d(&tm_xl, g->d_xl, K, M, box_rows)))
     return rc;
   if (!g->gemm_smem_set) {
     PL_CUDA(cudaFuncSetAttribute(pl::gemm_hilo_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  pl::gm_smem_bytes()));
+    PL_CUDA(cudaFuncSetAttribute(pl::gemm_skinny_kernel,
+                                 cudaFuncAttributeMaxDynamicSharedMemorySize, pl::sk_smem_bytes()));
     g->gemm_smem_set = true;
   }
   pl::GemmArgs a = {};
@@ -1929,6 +2004,56 @@ int launch_gemm(const LayerW& L, bool qkv, const float* d_x, int ldx, int M, int
   a.resid = resid;
   a.ld_res = ld_res;
   a.err = g->d_err;
+  if (M <= pl::kSkMaxRows) {
+    // few rows: the weights are the A operand, 128 output columns per tile,
+    // K split over a cluster of S CTAs per tile: the largest S (at most 8,
+    // at least two k-steps per CTA) whose clusters all fit on the GPU at
+    // once, from the occupancy the driver reports for each cluster size
+    const int tiles = N / pl::kGmBM, kb_all = K / pl::kGmBK;
+    if (!g->sk_clusters[1]) {
+      g->sk_clusters[1] = g->num_sms;
+      for (int sz = 2; sz <= pl::kSkMaxSplit; ++sz) {
+        cudaLaunchConfig_t q = {};
+        q.gridDim = dim3(1, sz);
+        q.blockDim = dim3(pl::kGmThreads);
+        q.dynamicSmemBytes = pl::sk_smem_bytes();
+        cudaLaunchAttribute ca[1];
+        ca[0].id = cudaLaunchAttributeClusterDimension;
+        ca[0].val.clusterDim.x = 1;
+        ca[0].val.clusterDim.y = sz;
+        ca[0].val.clusterDim.z = 1;
+        q.attrs = ca;
+        q.numAttrs = 1;
+        int n_cl = 0;
+        if (cudaOccupancyMaxActiveClusters(&n_cl, pl::gemm_skinny_kernel, &q) != cudaSuccess) {
+          cudaGetLastError();
+          n_cl = 0;
+        }
+        g->sk_clusters[sz] = n_cl;
+      }
+    }
+    int split = 1;
+    for (int sz = 2; sz <= pl::kSkMaxSplit && sz <= kb_all / 2; ++sz)
+      if (tiles <= g->sk_clusters[sz]) split = sz;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(tiles, split);
+    cfg.blockDim = dim3(pl::kGmThreads);
+    cfg.dynamicSmemBytes = pl::sk_smem_bytes();
+    cfg.stream = st;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;  // behind act_split_kernel
+    attr[1].id = cudaLaunchAttributeClusterDimension;
+    attr[1].val.clusterDim.x = 1;
+    attr[1].val.clusterDim.y = split;
+    attr[1].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = split > 1 ? 2 : 1;
+    PL_CUDA(cudaLaunchKernelEx(&cfg, pl::gemm_skinny_kernel, a, tm_xh, tm_xl,
+                               qkv ? L.tm_qkv_h : L.tm_o_h, qkv ? L.tm_qkv_l : L.tm_o_l));
+    count_launch();
+    return PL_OK;
+  }
   const dim3 grid(N / pl::kGmBN, (M + pl::kGmBM - 1) / pl::kGmBM);
   pl::gemm_hilo_kernel<<<grid, pl::kGmThreads, pl::gm_smem_bytes(), st>>>(
       a, tm_xh, tm_xl, qkv ? L.tm_qkv_h : L.tm_o_h, qkv ? L.tm_qkv_l : L.tm_o_l);

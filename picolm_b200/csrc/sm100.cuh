@@ -345,6 +345,30 @@ __device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t saddr, uint32_t lbo
   return d;
 }
 
+// ---- thread-block clusters (no multicast: plain distributed shared memory)
+// Every thread of every CTA of the cluster arrives, then waits; the release /
+// acquire pair orders each CTA's shared-memory stores before the others'
+// reads.
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile(
+      "barrier.cluster.arrive.release.aligned;\n\t"
+      "barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+// The shared::cluster address of shared-memory address `saddr` (this CTA's
+// layout) in the CTA of cluster rank `rank`.
+__device__ __forceinline__ uint32_t cluster_map(uint32_t saddr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(saddr), "r"(rank));
+  return r;
+}
+
+__device__ __forceinline__ float ld_cluster_f32(uint32_t addr) {
+  float v;
+  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(addr) : "memory");
+  return v;
+}
+
 // Instruction descriptor, kind::f16: FP16 A and B, FP32 D, A K-major,
 // B K-major (b_mn_major = 0) or MN-major (1), shape M x N.
 __host__ __device__ constexpr uint32_t idesc_f16_f32(int M, int N, int b_mn_major) {

@@ -40,10 +40,12 @@ def _close_proj(got, want, what):
 @pytest.mark.parametrize("name", list(GGUF_TYPES))
 def test_projection_vs_oracle(name):
     # every projection of a layer whose four weights have this type, on 1, 5
-    # and 13 input rows (13 > the 8 rows a CTA stages: two row chunks), 40
-    # (the mma.sync path for Q4_K, Q8_0 and F16: 16-row tiles) and 200 (the
-    # tcgen05 GEMM over the dequantised weights, from 128 rows; a ragged
-    # second 128-row tile)
+    # and 13 input rows (13 > the 8 rows a CTA stages: two row chunks), 20
+    # (the mma.sync path for Q4_K, Q8_0 and F16: 16-row tiles), 24, 40 and
+    # 64 (the skinny tcgen05 GEMM over the dequantised weights, weights as
+    # the A operand, K split over CTAs and the partials summed in order), 65
+    # and 200 (gemm_hilo_kernel: one ragged 128-row tile, and a ragged
+    # second one)
     t = GGUF_TYPES[name]
     rng = np.random.default_rng(40 + t)
     H, Hk, hd, dim = 8, 2, 64, 768
@@ -53,7 +55,7 @@ def test_projection_vs_oracle(name):
     with pb.Attn(1, H, Hk, 64, head_dim=hd) as at:
         upload_layer(at, 0, L)
         for which, (rows, n) in enumerate(shapes):
-            for m in (1, 5, 13, 40, 200):
+            for m in (1, 5, 13, 20, 24, 40, 64, 65, 200):
                 x = rng.standard_normal((m, n), dtype=np.float32)
                 got = at.proj(0, which, x, rows)
                 for i in range(m):
