@@ -56,6 +56,15 @@ constexpr float kGmLoInv = 1.0f / 2048.0f;
 // there against 31.7 us on the skinny GEMM, 64 rows 64.5 against 37.8 us.
 constexpr int kGmMinRows = 24;
 
+// The weight parts are stored tiled: the 128 x 64 tile of weight rows
+// [128 t, 128 t + 128) and k-step kb (64 inputs) is one contiguous 16 KB
+// block, block t * kb_all + kb of a [blocks * 128][64] array, so each TMA
+// box is one burst of DRAM instead of 128 pieces of 128 bytes 2 K (or
+// 4 KB) apart.  First row of that block in the [blocks * 128][64] view:
+__host__ __device__ __forceinline__ int wtile_row(int row0, int kb, int kb_all) {
+  return ((row0 / kGmBN) * kb_all + kb) * kGmBN;
+}
+
 // Output columns [col0, col0 + cols) of the GEMM go to out[m * ld + n - col0]
 // with bias[n - col0] (nullptr: none).  Q, K and V are three segments of one
 // GEMM over their concatenated weight rows; each segment is a whole number
@@ -145,8 +154,8 @@ __global__ void __launch_bounds__(kGmThreads, 1)
       const int k0 = kb * kGmBK;
       tma_load_2d(sm.xh[s], &tm_xh, &sm.full[s], k0, m0);
       tma_load_2d(sm.xl[s], &tm_xl, &sm.full[s], k0, m0);
-      tma_load_2d(sm.wh[s], &tm_wh, &sm.full[s], k0, a.w_row0 + n0);
-      tma_load_2d(sm.wl[s], &tm_wl, &sm.full[s], k0, a.w_row0 + n0);
+      tma_load_2d(sm.wh[s], &tm_wh, &sm.full[s], 0, wtile_row(a.w_row0 + n0, kb, kb_n));
+      tma_load_2d(sm.wl[s], &tm_wl, &sm.full[s], 0, wtile_row(a.w_row0 + n0, kb, kb_n));
       ++issued;
     }
     // never leave with copies in flight: the last use of each stage must land
@@ -335,9 +344,9 @@ __global__ void __launch_bounds__(kGmThreads, 1)
     const int pre = kb_n < kSkStages ? kb_n : kSkStages;
     for (int kb = 0; kb < pre; ++kb) {
       mbar_arrive_expect_tx(&sm.full[kb], 2u * kGmTile + 2u * kSkXTile);
-      const int k0 = (kb_lo + kb) * kGmBK;
-      tma_load_2d(sm.wh[kb], &tm_wh, &sm.full[kb], k0, a.w_row0 + n0);
-      tma_load_2d(sm.wl[kb], &tm_wl, &sm.full[kb], k0, a.w_row0 + n0);
+      const int wr = wtile_row(a.w_row0 + n0, kb_lo + kb, kb_all);
+      tma_load_2d(sm.wh[kb], &tm_wh, &sm.full[kb], 0, wr);
+      tma_load_2d(sm.wl[kb], &tm_wl, &sm.full[kb], 0, wr);
     }
     asm volatile("griddepcontrol.wait;" ::: "memory");
     for (int kb = 0; kb < pre; ++kb) {
@@ -354,8 +363,9 @@ __global__ void __launch_bounds__(kGmThreads, 1)
       }
       mbar_arrive_expect_tx(&sm.full[s], 2u * kGmTile + 2u * kSkXTile);
       const int k0 = (kb_lo + kb) * kGmBK;
-      tma_load_2d(sm.wh[s], &tm_wh, &sm.full[s], k0, a.w_row0 + n0);
-      tma_load_2d(sm.wl[s], &tm_wl, &sm.full[s], k0, a.w_row0 + n0);
+      const int wr = wtile_row(a.w_row0 + n0, kb_lo + kb, kb_all);
+      tma_load_2d(sm.wh[s], &tm_wh, &sm.full[s], 0, wr);
+      tma_load_2d(sm.wl[s], &tm_wl, &sm.full[s], 0, wr);
       tma_load_2d(sm.xh[s], &tm_xh, &sm.full[s], k0, 0);
       tma_load_2d(sm.xl[s], &tm_xl, &sm.full[s], k0, 0);
       ++issued;
@@ -592,7 +602,10 @@ __global__ void dequant_split_kernel(const uint8_t* __restrict__ w, size_t rb, i
     if (!(fabsf(v) < 65504.f)) atomicOr(overflow, 1);
     __half h, l;
     split_hi_lo_scaled(v, h, l);
-    const size_t o = static_cast<size_t>(row0 + r) * n + i;
+    // tiled layout (wtile_row): n and the row count are multiples of 64 and 128
+    const int R = row0 + r;
+    const size_t o = (static_cast<size_t>(wtile_row(R, i / kGmBK, n / kGmBK)) + R % kGmBN) * kGmBK +
+                     i % kGmBK;
     wh[o] = h;
     wl[o] = l;
   }

@@ -1944,10 +1944,13 @@ int gemm_prepare_layer(LayerW& L) {
     L.gmem = nullptr;
     return PL_OK;
   }
-  int rc = make_map_2d(&L.tm_qkv_h, qkv_h, dim, qd + 2 * kvd);
-  if (!rc) rc = make_map_2d(&L.tm_qkv_l, qkv_l, dim, qd + 2 * kvd);
-  if (!rc) rc = make_map_2d(&L.tm_o_h, o_h, qd, dim);
-  if (!rc) rc = make_map_2d(&L.tm_o_l, o_l, qd, dim);
+  // the parts are tiled (pl::wtile_row): a [blocks * 128][64] view, one
+  // 128 x 64 tile per box
+  const int qkv_rows = static_cast<int>(n_qkv / pl::kGmBK), o_rows = static_cast<int>(n_o / pl::kGmBK);
+  int rc = make_map_2d(&L.tm_qkv_h, qkv_h, pl::kGmBK, qkv_rows);
+  if (!rc) rc = make_map_2d(&L.tm_qkv_l, qkv_l, pl::kGmBK, qkv_rows);
+  if (!rc) rc = make_map_2d(&L.tm_o_h, o_h, pl::kGmBK, o_rows);
+  if (!rc) rc = make_map_2d(&L.tm_o_l, o_l, pl::kGmBK, o_rows);
   if (rc) return rc;
   L.gemm = true;
   return PL_OK;
