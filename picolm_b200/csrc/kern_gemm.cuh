@@ -463,24 +463,57 @@ __global__ void __launch_bounds__(kGmThreads, 1)
     }
     cluster_sync_all();
     const int m_lo = split * a.M / n_split, m_hi = (split + 1) * a.M / n_split;
-    const uint32_t p_own = smem_u32(P) + 4u * fr;
+    // thread: float4 q4 of the tile's 128 columns, rows m_lo + rg, + 4, ...
+    // up to kSkRows rows at a time, all their remote loads (16 bytes each)
+    // issued before any is summed
+    const int q4 = threadIdx.x & 31, rg = threadIdx.x >> 5;
+    const int col4 = n0 - seg.col0 + 4 * q4;
+    float4 b4 = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (seg.bias) b4 = __ldg(reinterpret_cast<const float4*>(seg.bias + col4));
+    const uint32_t p_own = smem_u32(P) + 16u * q4;
+    constexpr int kSkRows = 3;
 #pragma unroll 1
-    for (int m = m_lo; m < m_hi; ++m) {
-      const uint32_t pm = p_own + static_cast<uint32_t>(m) * kGmBM * 4u;
-      float v[kSkMaxSplit];
+    for (int m0 = m_lo + rg; m0 < m_hi; m0 += 4 * kSkRows) {
+      float4 v[kSkRows][kSkMaxSplit];
 #pragma unroll
-      for (int r = 0; r < kSkMaxSplit; ++r)
-        v[r] = r < n_split ? ld_cluster_f32(cluster_map(pm, r)) : 0.f;
-      float y = v[0];
+      for (int j = 0; j < kSkRows; ++j) {
+        const int m = m0 + 4 * j;
+        const uint32_t pm = p_own + static_cast<uint32_t>(m) * kGmBM * 4u;
 #pragma unroll
-      for (int r = 1; r < kSkMaxSplit; ++r)
-        if (r < n_split) y += v[r];
-      if (any_err) continue;
-      if (seg.bias) y += bias;
-      if (a.resid) y = a.resid[static_cast<size_t>(m) * a.ld_res + col] + y;
-      seg.out[static_cast<size_t>(m) * seg.ld + col] = y;
+        for (int r = 0; r < kSkMaxSplit; ++r)
+          v[j][r] = (m < m_hi && r < n_split) ? ld_cluster_f32x4(cluster_map(pm, r))
+                                               : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+#pragma unroll
+      for (int j = 0; j < kSkRows; ++j) {
+        const int m = m0 + 4 * j;
+        if (m >= m_hi || any_err) continue;
+        float4 y = v[j][0];
+#pragma unroll
+        for (int r = 1; r < kSkMaxSplit; ++r)
+          if (r < n_split) {
+            y.x += v[j][r].x;
+            y.y += v[j][r].y;
+            y.z += v[j][r].z;
+            y.w += v[j][r].w;
+          }
+        if (seg.bias) {
+          y.x += b4.x;
+          y.y += b4.y;
+          y.z += b4.z;
+          y.w += b4.w;
+        }
+        if (a.resid) {
+          const float4 r4 =
+              *reinterpret_cast<const float4*>(a.resid + static_cast<size_t>(m) * a.ld_res + col4);
+          y = make_float4(r4.x + y.x, r4.y + y.y, r4.z + y.z, r4.w + y.w);
+        }
+        *reinterpret_cast<float4*>(seg.out + static_cast<size_t>(m) * seg.ld + col4) = y;
+      }
     }
-    cluster_sync_all();  // the others' reads of this CTA's partial are done
+    // the others' reads of this CTA's partial are done (a release here would
+    // also wait for this CTA's output stores to be acknowledged)
+    cluster_sync_relaxed();
   }
   tc_fence_before();
   __syncthreads();

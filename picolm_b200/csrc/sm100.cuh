@@ -355,12 +355,30 @@ __device__ __forceinline__ void cluster_sync_all() {
       "barrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
 
+// A cluster barrier that orders no memory: for a CTA that must not leave
+// while others still read its shared memory, where each reader consumed
+// the values it loaded (they fed its later instructions) before arriving.
+__device__ __forceinline__ void cluster_sync_relaxed() {
+  asm volatile(
+      "barrier.cluster.arrive.relaxed.aligned;\n\t"
+      "barrier.cluster.wait.aligned;" ::: "memory");
+}
+
 // The shared::cluster address of shared-memory address `saddr` (this CTA's
 // layout) in the CTA of cluster rank `rank`.
 __device__ __forceinline__ uint32_t cluster_map(uint32_t saddr, uint32_t rank) {
   uint32_t r;
   asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(saddr), "r"(rank));
   return r;
+}
+
+__device__ __forceinline__ float4 ld_cluster_f32x4(uint32_t addr) {
+  float4 v;
+  asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
+               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+               : "r"(addr)
+               : "memory");
+  return v;
 }
 
 __device__ __forceinline__ float ld_cluster_f32(uint32_t addr) {

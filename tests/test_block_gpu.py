@@ -90,6 +90,33 @@ def test_projection_gemm_many_tiles(which):
         _close_proj(got[i], want[i], f"W{which} row {i}")
 
 
+@pytest.mark.parametrize("dim", [128, 2048])
+def test_projection_skinny_split_and_unsplit(dim):
+    # the skinny GEMM (24-64 input rows, weights as the A operand): with 128
+    # inputs a tile has two k-steps and is not split (one CTA, direct
+    # epilogue); with 2048 the k-steps of a tile are split over a cluster
+    # and reduced through distributed shared memory, in split order, so two
+    # identical calls give identical bits
+    rng = np.random.default_rng(91 + dim)
+    H, Hk, hd = (2, 2, 64) if dim == 128 else (32, 4, 64)
+    t = GGUF_Q8_0 if dim == 128 else GGUF_Q4_K  # Q4_K blocks span 256 inputs
+    L = random_layer(rng, H, Hk, hd, dim, types=(t,) * 4, bias=True)
+    shapes = [(H * hd, dim), (Hk * hd, dim), (Hk * hd, dim), (dim, H * hd)]
+    biases = [L["bq"], L["bk"], L["bv"], L["bo"]]
+    with pb.Attn(1, H, Hk, 64, head_dim=hd) as at:
+        upload_layer(at, 0, L)
+        for which in (0, 3):
+            rows, n = shapes[which]
+            for m in (24, 37, 64):
+                x = rng.standard_normal((m, n), dtype=np.float32)
+                got = at.proj(0, which, x, rows)
+                again = at.proj(0, which, x, rows)
+                np.testing.assert_array_equal(got.view(np.uint32), again.view(np.uint32))
+                for i in range(m):
+                    want = O.matmul(L["w"][which], x[i], n, rows, t) + biases[which]
+                    _close_proj(got[i], want, f"dim {dim} W{which} m{m} row {i}")
+
+
 def test_projection_wide_input():
     # head_dim 128 x 32 heads: Wo takes 4096 inputs (16 KB a staged row)
     rng = np.random.default_rng(3)
