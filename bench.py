@@ -120,7 +120,9 @@ class ClockSampler:
                 self.reasons |= nv.nvmlDeviceGetCurrentClocksEventReasons(self._h)
             except Exception:
                 pass
-            time.sleep(0.005)
+            # the timed regions are short (about 0.6 ms for 20 decode steps):
+            # sample as often as NVML answers
+            time.sleep(0.0005)
 
     def __enter__(self):
         if self._h is not None:

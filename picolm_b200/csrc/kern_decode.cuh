@@ -78,6 +78,11 @@ __host__ __device__ constexpr int part_stride(int hd) { return hd + kPartO; }
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr int kMaxLaunchSeqs = 1024;    // sequences per launch (prefix scan in smem)
 constexpr int kMaxCombineParts = 16;    // device partials merged by combine_kernel
+// A launch of at most this many sequences may carry their (slot, position)
+// pairs in its arguments instead of device arrays: a host-buffer call then
+// needs no copy of them (each copy costs several microseconds of the GPU's
+// timeline, however small).
+constexpr int kInlineSeqs = 128;
 
 struct DecodeArgs {
   // cache geometry
@@ -113,6 +118,11 @@ struct DecodeArgs {
   // word here (pinned host memory mapped into the device), so the host reads
   // it without a copy.  nullptr: not wanted.
   uint32_t* err_host;
+  // n_inline > 0: (slot, position) of sequence i in sp[i], and seqs / pos
+  // are not read.  The kernels take the arguments as __grid_constant__, so
+  // sp is read in place from the parameter space.
+  int n_inline;
+  int2 sp[kInlineSeqs];
 };
 
 // RoPE of the element pair (d, d+1) of one head (d even), as picolm's
@@ -173,10 +183,10 @@ struct Partition {
 };
 
 __device__ __forceinline__ int seq_of(const DecodeArgs& a, int i) {
-  return a.seqs ? a.seqs[i] : a.seq1;
+  return a.n_inline ? a.sp[i].x : a.seqs ? a.seqs[i] : a.seq1;
 }
 __device__ __forceinline__ int pos_of(const DecodeArgs& a, int i) {
-  return a.pos ? a.pos[i] : a.pos1;
+  return a.n_inline ? a.sp[i].y : a.pos ? a.pos[i] : a.pos1;
 }
 
 // Rows attended and the append row of sequence i.
@@ -194,8 +204,9 @@ __device__ __forceinline__ void seq_rows(const DecodeArgs& a, int i, int& att_ro
 template <int TP>
 __device__ __forceinline__ int seq_tiles(const DecodeArgs& a, int i, bool hint, bool& bad,
                                          int& seq) {
-  seq = a.seqs ? (hint ? __ldcg(a.seqs + i) : a.seqs[i]) : a.seq1;
-  const int pos = a.pos ? (hint ? __ldcg(a.pos + i) : a.pos[i]) : a.pos1;
+  seq = a.n_inline ? a.sp[i].x : a.seqs ? (hint ? __ldcg(a.seqs + i) : a.seqs[i]) : a.seq1;
+  const int pos =
+      a.n_inline ? a.sp[i].y : a.pos ? (hint ? __ldcg(a.pos + i) : a.pos[i]) : a.pos1;
   const int att_rows = a.mode == 0 ? pos + 1 : a.n_rows;
   const int app_row = a.mode == 0 ? (a.append ? pos : -1) : (a.append ? pos - a.row0 : -1);
   bad = seq < 0 || seq >= a.n_slots || pos < 0 || pos >= a.pos_limit || att_rows < 0 ||
@@ -532,7 +543,7 @@ __device__ __forceinline__ void consume_segment(const DecodeArgs& a, int w, int 
 }
 
 template <int TP, int NSTAGE, int HD>
-__global__ void __launch_bounds__(288) decode_kernel(const DecodeArgs a,
+__global__ void __launch_bounds__(288) decode_kernel(const __grid_constant__ DecodeArgs a,
                                                      const __grid_constant__ CUtensorMap tmk,
                                                      const __grid_constant__ CUtensorMap tmv) {
   extern __shared__ uint8_t smem_raw[];
@@ -861,8 +872,8 @@ constexpr int kMergeThreads = 256;
 // Tile count of sequence i as the decode grid computed it (tp rows a tile;
 // 0 for a slot or position out of range).
 __device__ __forceinline__ int merge_seq_tiles(const DecodeArgs& a, int i, int tp) {
-  const int seq = a.seqs ? a.seqs[i] : a.seq1;
-  const int pos = a.pos ? a.pos[i] : a.pos1;
+  const int seq = seq_of(a, i);
+  const int pos = pos_of(a, i);
   const int att_rows = a.mode == 0 ? pos + 1 : a.n_rows;
   const int app_row = a.mode == 0 ? (a.append ? pos : -1) : (a.append ? pos - a.row0 : -1);
   const bool bad = seq < 0 || seq >= a.n_slots || pos < 0 || pos >= a.pos_limit ||
@@ -874,7 +885,8 @@ __device__ __forceinline__ int merge_seq_tiles(const DecodeArgs& a, int i, int t
 // head per block) and exchanges it (XferPush): each block pushes its head to
 // every rank and merges every rank's partial of that head into x.out.
 template <int HD, bool PUSH>
-__global__ void __launch_bounds__(kMergeThreads) merge_kernel(const DecodeArgs a, int hpb,
+__global__ void __launch_bounds__(kMergeThreads) merge_kernel(const __grid_constant__ DecodeArgs a,
+                                                              int hpb,
                                                               int decode_ctas, int tp,
                                                               const XferPush x) {
   __shared__ uint32_t s_epoch;

@@ -523,6 +523,7 @@ pl::DecodeArgs decode_args(int layer, int n, const int* d_seqs, const int* d_pos
   a.score_scale = pl::kLog2e / sqrtf(static_cast<float>(g->head_dim));
   a.err = g->d_err;
   a.err_host = nullptr;
+  a.n_inline = 0;
   return a;
 }
 
@@ -674,7 +675,8 @@ int launch_decode_kernel(const pl::DecodeArgs& a, int grid, cudaStream_t st, boo
 int launch_decode(int layer, int n, const int* d_seqs, const int* d_pos, int max_rows,
                   const float* d_q, const float* d_k, const float* d_v, float* d_out,
                   int mode, int row0, int n_rows, int append, float* part_out,
-                  cudaStream_t st, uint32_t* err_host = nullptr) {
+                  cudaStream_t st, uint32_t* err_host = nullptr,
+                  const int* h_seqs = nullptr, const int* h_pos = nullptr) {
   for (int s0 = 0; s0 < n; s0 += pl::kMaxLaunchSeqs) {
     const int m = n - s0 < pl::kMaxLaunchSeqs ? n - s0 : pl::kMaxLaunchSeqs;
     const int grid = decode_grid(m, max_rows);
@@ -689,6 +691,11 @@ int launch_decode(int layer, int n, const int* d_seqs, const int* d_pos, int max
         g->d_part, g->d_seg_info);
     pl::DecodeArgs b = a;
     b.err_host = err_host;
+    if (h_seqs && h_pos && m <= pl::kInlineSeqs) {
+      // (slot, position) pairs in the arguments: the device arrays are not read
+      b.n_inline = m;
+      for (int i = 0; i < m; ++i) b.sp[i] = make_int2(h_seqs[s0 + i], h_pos[s0 + i]);
+    }
     rc = launch_decode_kernel(b, grid, st, true);
     if (rc) return rc;
   }
@@ -1124,15 +1131,24 @@ int pl_attn_decode_batch(int layer, int n, const int* seqs, const int* pos, cons
     in[n_in++] = {h + qb + kb, reinterpret_cast<const uint8_t*>(v), kb};
   }
   if (n_in) host_copy(in, n_in);
-  std::memcpy(h + qb + 2 * kb, seqs, ib);
-  std::memcpy(h + qb + 2 * kb + ib, pos, ib);
+  // up to kInlineSeqs sequences carry their slots and positions in the
+  // kernel arguments; more are staged and copied with the rest
+  const bool sp_inline = n <= pl::kInlineSeqs;
+  if (!sp_inline) {
+    std::memcpy(h + qb + 2 * kb, seqs, ib);
+    std::memcpy(h + qb + 2 * kb + ib, pos, ib);
+  }
   if (q_direct) {
-    // q from the caller; then the staged rest: k and v (unless mapped),
-    // slots and positions
+    // q from the caller; then the staged rest, if any: k and v (unless
+    // mapped), slots and positions (unless inline).  Every copy costs
+    // several microseconds of the GPU's timeline, so none is queued for
+    // nothing.
     const size_t rest = kv_mapped ? qb + 2 * kb : qb;
+    const size_t rest_end = sp_inline ? qb + 2 * kb : in_bytes;
     PL_CUDA(cudaMemcpyAsync(d, q, qb, cudaMemcpyHostToDevice, g->stream));
-    PL_CUDA(cudaMemcpyAsync(d + rest, h + rest, in_bytes - rest, cudaMemcpyHostToDevice,
-                            g->stream));
+    if (rest_end > rest)
+      PL_CUDA(cudaMemcpyAsync(d + rest, h + rest, rest_end - rest, cudaMemcpyHostToDevice,
+                              g->stream));
   } else {
     PL_CUDA(cudaMemcpyAsync(d, h, in_bytes, cudaMemcpyHostToDevice, g->stream));
   }
@@ -1150,7 +1166,8 @@ int pl_attn_decode_batch(int layer, int n, const int* seqs, const int* pos, cons
                                : reinterpret_cast<const float*>(d + qb),
                      kv_mapped ? reinterpret_cast<const float*>(mv)
                                : reinterpret_cast<const float*>(d + qb + kb),
-                     d_out, 0, 0, 0, 1, nullptr, g->stream, g->h_err_dev);
+                     d_out, 0, 0, 0, 1, nullptr, g->stream, g->h_err_dev,
+                     sp_inline ? seqs : nullptr, sp_inline ? pos : nullptr);
   if (rc) return rc;
   PL_CUDA(cudaStreamSynchronize(g->stream));
   const uint32_t w = *reinterpret_cast<volatile uint32_t*>(g->h_err);
