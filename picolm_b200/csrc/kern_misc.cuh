@@ -232,4 +232,24 @@ inline int prologue_grid(int n_tok, int n_heads, int n_kv_heads, int head_dim, b
   return static_cast<int>(need < cap ? (need < 1 ? 1 : need) : cap);
 }
 
+// Copy of n16 16-byte words from src (host memory mapped into the device:
+// a registered caller buffer) to dst (HBM) by loads over the bus from every
+// SM.  Used in place of a cudaMemcpyAsync for the q of a host-buffer
+// decode: the decode grid is queued behind it with programmatic dependent
+// launch, so it is resident and through its set-up when the copy ends.
+// grid-stride, block 256.
+__global__ void __launch_bounds__(256)
+    bus_gather_kernel(const uint4* __restrict__ src, uint4* __restrict__ dst, long n16) {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  const long stride = static_cast<long>(gridDim.x) * blockDim.x;
+  long i = static_cast<long>(blockIdx.x) * blockDim.x + threadIdx.x;
+  // two words in flight per thread before either is stored
+  for (; i + stride < n16; i += 2 * stride) {
+    const uint4 a = src[i], b = src[i + stride];
+    dst[i] = a;
+    dst[i + stride] = b;
+  }
+  if (i < n16) dst[i] = src[i];
+}
+
 }  // namespace pl

@@ -1145,7 +1145,18 @@ int pl_attn_decode_batch(int layer, int n, const int* seqs, const int* pos, cons
     // nothing.
     const size_t rest = kv_mapped ? qb + 2 * kb : qb;
     const size_t rest_end = sp_inline ? qb + 2 * kb : in_bytes;
-    PL_CUDA(cudaMemcpyAsync(d, q, qb, cudaMemcpyHostToDevice, g->stream));
+    // q read over the bus by every SM into HBM (a kernel: the decode grid
+    // queues behind it with programmatic dependent launch), else copied
+    const uint8_t* mq = mapped(q, qb);
+    if (mq) {
+      pl::bus_gather_kernel<<<g->num_sms, 256, 0, g->stream>>>(
+          reinterpret_cast<const uint4*>(mq), reinterpret_cast<uint4*>(d),
+          static_cast<long>(qb / 16));
+      PL_CUDA(cudaGetLastError());
+      count_launch();
+    } else {
+      PL_CUDA(cudaMemcpyAsync(d, q, qb, cudaMemcpyHostToDevice, g->stream));
+    }
     if (rest_end > rest)
       PL_CUDA(cudaMemcpyAsync(d + rest, h + rest, rest_end - rest, cudaMemcpyHostToDevice,
                               g->stream));
