@@ -182,8 +182,8 @@ def test_block_decode_vs_oracle(H, Hk, hd, dim, types, bias, qk_norm, rope_type)
 
 @pytest.mark.parametrize("types", [(GGUF_Q4_K,) * 4, (GGUF_Q8_0, GGUF_F16, GGUF_Q8_0, GGUF_F16)])
 def test_block_decode_many_sequences(types):
-    """24 sequences: 16 or more input rows take the tensor-core projections
-    (proj_mma_kernel; one full and one partial 16-row tile)."""
+    """24 sequences: the projections take the skinny tcgen05 GEMM (24-64
+    input rows: weights as the A operand, K split over a cluster)."""
     rng = np.random.default_rng(sum(types))
     H, Hk, hd, dim, ms, n = 32, 4, 64, 2048, 96, 24
     kv = Hk * hd
