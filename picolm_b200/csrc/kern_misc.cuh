@@ -173,10 +173,12 @@ __device__ __forceinline__ void prologue_store(const PrologueUnit& pu, int r, ui
 // The (row, unit) pairs of the call are one flattened list, walked by a
 // persistent grid of kPrologueBlocksPerSm blocks per SM: each thread takes
 // kPrologueUnitsInFlight units per round, all their loads issued before any
-// compute, so every SM keeps ~100 KB of loads in flight (HBM latency x
-// bandwidth is ~45 KB per SM) and no block waits out one load at a time.
-constexpr int kPrologueBlocksPerSm = 3;
-constexpr int kPrologueUnitsInFlight = 2;
+// compute.  The kernel is latency-bound; resident warps hide that better
+// than units per thread (same-box A/B of the 22-layer config-3 call: one
+// unit at four blocks per SM 1.042-1.044 ms, two at three 1.057-1.059 ms,
+// three or four at two 1.15-1.27 ms).
+constexpr int kPrologueBlocksPerSm = 4;
+constexpr int kPrologueUnitsInFlight = 1;
 
 template <int HD>
 __global__ void __launch_bounds__(kPrologueThreads, kPrologueBlocksPerSm)
