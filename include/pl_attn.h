@@ -248,10 +248,10 @@ int  pl_attn_xfer_connect(const void *handles);
 int  pl_attn_combine_p2p_dev(const float *d_part, float *d_out, void *stream);
 
 /* pl_attn_decode_partial_dev followed by pl_attn_combine_p2p_dev in one
- * call, without the intermediate partial: the grid that merges this rank's
- * segments stores the merged heads straight into every rank's buffer, and
- * its last block stamps, waits (bounded) for every rank and writes the
- * merged output to d_out [n_heads*head_dim].  Arguments as
+ * call, without the intermediate partial: each block of the grid that
+ * merges this rank's segments stores its merged head straight into every
+ * rank's buffer, waits (bounded) for that head from every rank and writes
+ * the merged output of the head to d_out [n_heads*head_dim].  Arguments as
  * pl_attn_decode_partial_dev (n_rows = 0: an empty shard, which still takes
  * part in the exchange); calling rules as pl_attn_combine_p2p_dev.  One
  * kernel launch fewer per layer than the two calls. */

@@ -132,14 +132,15 @@ class P2PShardOps(AttnShardOps):
     At construction every rank allocates its receive buffer, the IPC handles
     are exchanged once over `group` (any backend; they are 64-byte objects),
     and each rank maps the others.  With `fused` (the default) one call per
-    layer, pl_attn_decode_p2p_dev, computes this rank's partial and the grid
-    that merges its segments stores it into every rank's buffer; the grid's
-    last block stamps it and, once every rank's stamp has arrived, merges
-    locally.  Without `fused`, pl_attn_decode_partial_dev writes the partial
-    and pl_attn_combine_p2p_dev (one kernel) pushes, stamps, waits and
-    merges.  Either way `gather` has nothing left to do, and the merges are
-    numbered on the device, so the calls can be captured in a CUDA graph and
-    replayed."""
+    layer, pl_attn_decode_p2p_dev, computes this rank's partial, and each
+    block of the grid that merges its segments stores its head into every
+    rank's buffer, waits for that head from every rank and merges it.
+    Without `fused`, pl_attn_decode_partial_dev writes the partial and
+    pl_attn_combine_p2p_dev (one kernel) pushes, waits and merges.  Every
+    value travels with the merge's epoch in the same 16-byte store, so no
+    fence or flag is needed.  Either way `gather` has nothing left to do,
+    and the merges are numbered on the device, so the calls can be captured
+    in a CUDA graph and replayed."""
 
     def __init__(self, attn, stream_handle: int, rank: int, world: int, group=None,
                  seq: int = 0, fused: bool = True):
