@@ -3,12 +3,13 @@
 * A KV-split merge whose peer never arrives: two processes on one GPU map
   each other's receive buffers (pl_attn_xfer_setup / _connect); rank 1 stays
   alive but never calls pl_attn_combine_p2p_dev (or pl_attn_decode_p2p_dev,
-  where the last block of the merge grid waits).  Rank 0's merge kernel
-  stores its partial, stamps its epoch and waits, bounded by the limit set
-  with pl_attn_set_wait_limit (50 ms here), for rank 1's stamp, which never
-  comes.  pl_attn_status must report PL_ETIMEOUT, and the module must stay
-  usable: a decode right after matches the oracle.  Only one kernel waits,
-  on a flag no one sets, so nothing depends on two kernels running at once;
+  where every block of the merge grid waits for its head).  Rank 0's merge
+  kernel stores its partial (each value beside the merge's epoch) and
+  waits, bounded by the limit set with pl_attn_set_wait_limit (50 ms here),
+  for rank 1's values to show that epoch, which never happens.
+  pl_attn_status must report PL_ETIMEOUT, and the module must stay usable: a
+  decode right after matches the oracle.  Only one kernel waits, on values
+  no one writes, so nothing depends on two kernels running at once;
   rank 1 leaves only after rank 0 has finished, so no mapping disappears
   under a running kernel.  This is the failure picolm's Vulkan backend
   detects with its 5 s fence timeout (picolm/gpu.c:693-698).
