@@ -69,3 +69,57 @@ def test_one_rank_exchange_matches_unsplit_decode():
                     gk, gv = at.kv_download(s, l, pos, 1)
                     np.testing.assert_array_equal(np.ravel(gk), kc[pos])
                     np.testing.assert_array_equal(np.ravel(gv), vc[pos])
+
+
+def test_one_rank_exchange_in_a_replayed_graph():
+    """Captured once and replayed: the merges are numbered on the device, so
+    every replay advances the epochs itself.  Re-running a step rewrites the
+    same appended rows with the same values, so each replay must reproduce
+    the first one bit for bit, and both must match the oracle."""
+    import torch
+    import picolm_b200 as pb
+
+    rng = np.random.default_rng(62)
+    n_cached, steps, ms = 300, 3, 320
+    kc0 = random_cache(rng, ms, KV_DIM)
+    vc0 = random_cache(rng, ms, KV_DIM)
+    tables = O.rope_tables(ms, HD, 500000.0)
+    c = O.cfg(H, HK, HD, ms)
+    dev = torch.device("cuda", 0)
+    qs = [rng.standard_normal(H * HD, dtype=np.float32) for _ in range(steps)]
+    ks = [rng.standard_normal(KV_DIM, dtype=np.float32) for _ in range(steps)]
+    vs = [rng.standard_normal(KV_DIM, dtype=np.float32) for _ in range(steps)]
+    with pb.Attn(1, H, HK, ms, rope_base=500000.0) as at:
+        at.kv_upload(0, 0, 0, kc0[:n_cached], vc0[:n_cached])
+        at.xfer_connect([at.xfer_setup(1, 0)])
+        qd = torch.from_numpy(np.stack(qs)).to(dev)
+        kd = torch.from_numpy(np.stack(ks)).to(dev)
+        vd = torch.from_numpy(np.stack(vs)).to(dev)
+        out = torch.zeros(steps, H * HD, device=dev)
+
+        def run(stream):
+            for i in range(steps):
+                pos = n_cached + i
+                at.decode_p2p_dev(0, 0, pos, 0, pos + 1, 1, qd[i].data_ptr(), kd[i].data_ptr(),
+                                  vd[i].data_ptr(), out[i].data_ptr(), stream)
+
+        run(torch.cuda.current_stream(dev).cuda_stream)  # warm-up outside the capture
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            run(torch.cuda.current_stream(dev).cuda_stream)
+        results = []
+        for _ in range(3):
+            out.zero_()
+            graph.replay()
+            torch.cuda.synchronize()
+            results.append(out.cpu().numpy().copy())
+        del graph
+        assert at.status(torch.cuda.current_stream(dev).cuda_stream) == pb.PL_OK
+    for r in results[1:]:
+        np.testing.assert_array_equal(r.view(np.uint32), results[0].view(np.uint32))
+    kc, vc = kc0.copy(), vc0.copy()
+    for i in range(steps):
+        want, _, _ = O.attn_decode(c, kc.ravel(), vc.ravel(), n_cached + i, qs[i], ks[i], vs[i],
+                                   *tables)
+        assert_attn_close(results[-1][i], want, f"replayed step {i}")
