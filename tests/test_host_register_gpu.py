@@ -136,3 +136,42 @@ def test_single_sequence_decode_paths():
             assert_attn_close(out, want, f"decode at {p}, registered={registered}")
             outs.append(out.copy())
         np.testing.assert_array_equal(outs[1].view(np.uint32), outs[0].view(np.uint32))
+
+
+@pytest.mark.parametrize("n", [128, 129])
+def test_decode_batch_inline_boundary(n):
+    """Up to 128 sequences carry their slots and positions in the kernel
+    arguments; 129 stage them and copy them after the gathered q.  Both,
+    with registered and staged buffers, against each other bit for bit and
+    against the oracle on a sample of sequences."""
+    from oracle import oracle as O
+    from tests.util import assert_attn_close
+    rng = np.random.default_rng(35 + n)
+    H, Hk, ms = 32, 4, 96
+    kv = Hk * 64
+    pos = rng.integers(0, ms, n).astype(np.int32)
+    seqs = rng.permutation(n).astype(np.int32)
+    q, k, v = _inputs(rng, n, H * 64, kv)
+    caches = [(random_cache(rng, ms, kv), random_cache(rng, ms, kv)) for _ in range(n)]
+    outs = []
+    for registered in (False, True):
+        with pb.Attn(1, H, Hk, ms, n_seqs=n) as at:
+            for s, (kc, vc) in enumerate(caches):
+                at.kv_upload(s, 0, 0, kc, vc)
+            qq, kk, vv = q.copy(), k.copy(), v.copy()
+            out = np.zeros(n * H * 64, np.float32)
+            regs = (qq, kk, vv, out) if registered else ()
+            for a in regs:
+                at.host_register(a)
+            at.decode_batch(0, seqs, pos, qq, kk, vv, out=out)
+            for a in regs:
+                at.host_unregister(a)
+            outs.append(out.reshape(n, H * 64).copy())
+    np.testing.assert_array_equal(outs[1].view(np.uint32), outs[0].view(np.uint32))
+    tables = O.rope_tables(ms, 64, 10000.0)
+    c = O.cfg(H, Hk, 64, ms)
+    for i in (0, 1, n // 2, n - 1):
+        kc, vc = (x.copy() for x in caches[seqs[i]])
+        want, _, _ = O.attn_decode(c, kc.ravel(), vc.ravel(), int(pos[i]), q[i], k[i], v[i],
+                                   *tables)
+        assert_attn_close(outs[1][i], want, f"n={n} sequence {i}")
