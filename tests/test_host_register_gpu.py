@@ -175,3 +175,42 @@ def test_decode_batch_inline_boundary(n):
         want, _, _ = O.attn_decode(c, kc.ravel(), vc.ravel(), int(pos[i]), q[i], k[i], v[i],
                                    *tables)
         assert_attn_close(outs[1][i], want, f"n={n} sequence {i}")
+
+
+def test_decode_batch_registered_hd128_qwen():
+    """head_dim 128 and Qwen pairing through the host-buffer decode: q
+    gathered over the bus (16 KB a sequence), k and v read and the output
+    written over the bus from registered buffers; against the staged call
+    bit for bit and against the oracle."""
+    from oracle import oracle as O
+    from tests.util import assert_attn_close
+    rng = np.random.default_rng(36)
+    H, Hk, hd, ms, n = 32, 8, 128, 160, 12
+    kv = Hk * hd
+    pos = rng.integers(0, ms, n).astype(np.int32)
+    seqs = np.arange(n, dtype=np.int32)
+    q, k, v = _inputs(rng, n, H * hd, kv)
+    caches = [(random_cache(rng, ms, kv), random_cache(rng, ms, kv)) for _ in range(n)]
+    outs = []
+    for registered in (False, True):
+        with pb.Attn(1, H, Hk, ms, n_seqs=n, head_dim=hd, rope_type=1,
+                     rope_base=1000000.0) as at:
+            for s, (kc, vc) in enumerate(caches):
+                at.kv_upload(s, 0, 0, kc, vc)
+            qq, kk, vv = q.copy(), k.copy(), v.copy()
+            out = np.zeros(n * H * hd, np.float32)
+            regs = (qq, kk, vv, out) if registered else ()
+            for a in regs:
+                at.host_register(a)
+            at.decode_batch(0, seqs, pos, qq, kk, vv, out=out)
+            for a in regs:
+                at.host_unregister(a)
+            outs.append(out.reshape(n, H * hd).copy())
+    np.testing.assert_array_equal(outs[1].view(np.uint32), outs[0].view(np.uint32))
+    tables = O.rope_tables(ms, hd, 1000000.0)
+    c = O.cfg(H, Hk, hd, ms, 1)
+    for i in range(n):
+        kc, vc = (x.copy() for x in caches[i])
+        want, _, _ = O.attn_decode(c, kc.ravel(), vc.ravel(), int(pos[i]), q[i], k[i], v[i],
+                                   *tables)
+        assert_attn_close(outs[1][i], want, f"hd128 qwen sequence {i}")
