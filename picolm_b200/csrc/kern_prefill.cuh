@@ -87,6 +87,7 @@ struct PrefillArgs {
   float score_scale;     // log2(e)/sqrt(HD)
   int* work;             // [2] item counter, finished-CTA counter; zero at rest
   uint32_t* err;
+  int o_tma;             // 1: the output leaves through tm_o (TMA stores, HD 64)
 };
 
 // The two shapes of the kernel: head_dim HD, KV tiles of BN cache rows,
@@ -212,7 +213,8 @@ __global__ void __launch_bounds__(kPfThreads, 1)
     prefill_attn_kernel(const PrefillArgs a, const __grid_constant__ CUtensorMap tm_q,
                         const __grid_constant__ CUtensorMap tm_ql,
                         const __grid_constant__ CUtensorMap tm_k,
-                        const __grid_constant__ CUtensorMap tm_v) {
+                        const __grid_constant__ CUtensorMap tm_v,
+                        const __grid_constant__ CUtensorMap tm_o) {
   using Sh = PfShape<HD, BN, STAGES>;
   extern __shared__ uint8_t smem_raw[];
   PfSmem<HD, BN, STAGES>& sm = *reinterpret_cast<PfSmem<HD, BN, STAGES>*>(
@@ -551,8 +553,12 @@ __global__ void __launch_bounds__(kPfThreads, 1)
       if (lane == 0) mbar_arrive(&sm.o_free[x]);
       // O / l to the output through the warp's staging buffer, 32 columns
       // at a time: a thread holds one row, so direct stores would touch 32
-      // rows per instruction; read back transposed, each store instruction
-      // covers four rows x 128 contiguous bytes.  At head_dim 128 the
+      // rows per instruction.  With an output tensor map (o_tma) one lane
+      // hands each 32 x 32 box to the TMA unit and the warp moves on to its
+      // next item (stores from the threads took about 2,500 cycles of the
+      // item switch); without one the warp reads the buffer back
+      // transposed, each store instruction covering four rows x 128
+      // contiguous bytes.  At head_dim 128 the
       // shared memory goes to a deeper K/V ring instead and the rows are
       // stored directly.
       const float inv = 1.0f / l_run;
@@ -569,15 +575,33 @@ __global__ void __launch_bounds__(kPfThreads, 1)
         }
       }
       float* stg = sm.stage[Sh::kStaged ? warp : 0];
-      float* dst = a.out + (x ? it.head1 : it.head0) * HD + (lane & 7) * 4;
+      const int o_col = (x ? it.head1 : it.head0) * HD;
+      float* dst = a.out + o_col + (lane & 7) * 4;
 #pragma unroll
       for (int hc = 0; hc < (Sh::kStaged ? HD / 32 : 0); ++hc) {
+        if (a.o_tma) {
+          // the previous TMA store from this buffer must have read it
+          if (lane == 0) bulk_wait_read_all();
+          __syncwarp();
+        }
 #pragma unroll
         for (int c = 0; c < 32; c += 4)
           *reinterpret_cast<float4*>(stg + lane * kPfStagePitch + 4 * ((c >> 2) ^ (lane & 7))) =
               make_float4(
               __uint_as_float(ov[32 * hc + c]) * inv, __uint_as_float(ov[32 * hc + c + 1]) * inv,
               __uint_as_float(ov[32 * hc + c + 2]) * inv, __uint_as_float(ov[32 * hc + c + 3]) * inv);
+        if (a.o_tma) {
+          // the staging layout is the 128-byte swizzle of a 32 x 32 FP32 box:
+          // one bulk store per round, rows past n_tok clipped by the TMA unit;
+          // the warp goes on to its next item while the store drains
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            tma_store_2d(&tm_o, stg, o_col + 32 * hc, row_base);
+            bulk_commit();
+          }
+          continue;
+        }
         __syncwarp();
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
@@ -594,6 +618,8 @@ __global__ void __launch_bounds__(kPfThreads, 1)
       ++k;
     }
     if (!ok) atomicOr(a.err, ERR_TIMEOUT_MMA);
+    // no store may still read the staging buffer (or be in flight) at exit
+    if (Sh::kStaged && a.o_tma && lane == 0) bulk_wait_all();
   }
 
   tc_fence_before();
@@ -613,8 +639,8 @@ __global__ void __launch_bounds__(kPfThreads, 1)
 template <int HD, int BN, int STAGES>
 inline int launch_prefill_shape(const PrefillArgs& a, const CUtensorMap& tm_q,
                                 const CUtensorMap& tm_ql, const CUtensorMap& tm_k,
-                                const CUtensorMap& tm_v, int num_sms, cudaStream_t st,
-                                bool overlap) {
+                                const CUtensorMap& tm_v, const CUtensorMap& tm_o, int num_sms,
+                                cudaStream_t st, bool overlap) {
   auto kern = prefill_attn_kernel<HD, BN, STAGES>;
   constexpr int smem = pf_smem_bytes<HD, BN, STAGES>();
   // kernel attributes are per device: set them the first time this kernel
@@ -651,7 +677,7 @@ inline int launch_prefill_shape(const PrefillArgs& a, const CUtensorMap& tm_q,
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = overlap ? 1 : 0;
-  if (cudaLaunchKernelEx(&cfg, kern, a, tm_q, tm_ql, tm_k, tm_v) != cudaSuccess) return -4;
+  if (cudaLaunchKernelEx(&cfg, kern, a, tm_q, tm_ql, tm_k, tm_v, tm_o) != cudaSuccess) return -4;
   return cudaGetLastError() == cudaSuccess ? 0 : -4;
 }
 
@@ -660,11 +686,13 @@ constexpr int pf_block_n(int head_dim) { return head_dim == 128 ? 64 : 128; }
 
 inline int launch_prefill_attention(int head_dim, const PrefillArgs& a, const CUtensorMap& tm_q,
                                     const CUtensorMap& tm_ql, const CUtensorMap& tm_k,
-                                    const CUtensorMap& tm_v, int num_sms, cudaStream_t st,
-                                    bool overlap) {
+                                    const CUtensorMap& tm_v, const CUtensorMap& tm_o,
+                                    int num_sms, cudaStream_t st, bool overlap) {
   if (head_dim == 128)
-    return launch_prefill_shape<128, 64, 3>(a, tm_q, tm_ql, tm_k, tm_v, num_sms, st, overlap);
-  return launch_prefill_shape<64, 128, 4>(a, tm_q, tm_ql, tm_k, tm_v, num_sms, st, overlap);
+    return launch_prefill_shape<128, 64, 3>(a, tm_q, tm_ql, tm_k, tm_v, tm_o, num_sms, st,
+                                            overlap);
+  return launch_prefill_shape<64, 128, 4>(a, tm_q, tm_ql, tm_k, tm_v, tm_o, num_sms, st,
+                                          overlap);
 }
 
 }  // namespace pl

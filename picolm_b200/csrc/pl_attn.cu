@@ -229,6 +229,24 @@ int make_map(EncodeTiledFn enc, CUtensorMap* m, uint16_t* base, int head_dim, in
   return PL_OK;
 }
 
+// The prefill output, n_tok rows of `cols` FP32 at a row stride of `stride`
+// floats, as a 2-D TMA map for the attention kernel's stores: boxes of 32
+// columns x 32 rows under the 128-byte swizzle.  False when TMA cannot
+// address the rows (base not 16-byte aligned, stride not a multiple of four
+// floats); the kernel then stores from its threads.
+bool make_out_map(EncodeTiledFn enc, CUtensorMap* m, float* out, int cols, int rows,
+                  int stride) {
+  if ((reinterpret_cast<uintptr_t>(out) & 15) || (stride & 3) || cols > stride || rows < 1)
+    return false;
+  const cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
+  const cuuint64_t strides[1] = {static_cast<cuuint64_t>(stride) * 4};
+  const cuuint32_t box[2] = {32u, 32u};
+  const cuuint32_t estr[2] = {1, 1};
+  return enc(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, out, dims, strides, box, estr,
+             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+             CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 void host_rope_tables(float* c, float* s, int max_seq, int head_dim, float base) {
   // picolm/model.c:545-556, same libm calls in FP32
   const int half = head_dim / 2;
@@ -1510,10 +1528,14 @@ static int launch_prefill_rows(uint16_t* kc_slab, uint16_t* vc_slab, const CUten
   a.score_scale = pl::kLog2e / sqrtf(static_cast<float>(g->head_dim));
   a.work = g->d_work;
   a.err = g->d_err;
+  CUtensorMap tm_o;
+  std::memset(&tm_o, 0, sizeof(tm_o));
+  a.o_tma = g->head_dim == 64 &&
+            make_out_map(g->encode, &tm_o, d_out, g->q_dim, n_tok, out_stride) ? 1 : 0;
   prof_begin(st);
   // overlap with the prologue except when events separate the two for timing
-  if (pl::launch_prefill_attention(g->head_dim, a, g->tm_q16, g->tm_q16lo, tmk, tmv, g->num_sms,
-                                   st, !g->profiling) != 0)
+  if (pl::launch_prefill_attention(g->head_dim, a, g->tm_q16, g->tm_q16lo, tmk, tmv, tm_o,
+                                   g->num_sms, st, !g->profiling) != 0)
     return PL_ECUDA;
   prof_end(st);
   count_launch();
