@@ -251,9 +251,14 @@ __global__ void __launch_bounds__(kPfThreads, 1)
   __syncthreads();
   tc_fence_after();
   // launched behind the prologue with programmatic dependent launch: the
-  // set-up above overlapped its tail; q16, the cache rows it appended and
-  // the work counters are read only after it has finished
-  asm volatile("griddepcontrol.wait;" ::: "memory");
+  // set-up above overlapped its tail; q16 and the cache rows it appended
+  // are read only after it has finished.  The scheduler lane takes its
+  // first item before its own wait: the work counter is not the
+  // prologue's (the attention grid before it, complete before the prologue
+  // started, left it at zero), so the fetch and the item's decoding
+  // overlap the prologue's tail too.
+  const bool sched_lane = warp == 8 && lane == 0;
+  if (!sched_lane) asm volatile("griddepcontrol.wait;" ::: "memory");
   const uint32_t tmem = sm.tmem_base;
   if (warp >= 8) {
     regs_dec<kPfOtherRegs>();  // warp 11 only completes the warpgroup
@@ -278,6 +283,8 @@ __global__ void __launch_bounds__(kPfThreads, 1)
           mbar_arrive(&sm.item_full[k & 1]);
           if (item < 0) break;
           const PfItem it = pf_item<BN>(a, item);
+          // the first item's loads read the prologue's output
+          if (k == 0) asm volatile("griddepcontrol.wait;" ::: "memory");
           // Q of the previous item is in use until its last S MMAs complete
           if (k >= 1 && !mbar_wait_bounded(&sm.q_empty, (k - 1) & 1)) {
             atomicOr(a.err, ERR_TIMEOUT_EMPTY);
